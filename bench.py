@@ -1,0 +1,393 @@
+#!/usr/bin/env python3
+"""Benchmark: SMat block-sparse causal softmax attention fwd+bwd on B200.
+
+Workload: B=4, H=32, T=16384, D=128, block 128, local
+window 4, stride-8 summary blocks, 2 sink blocks, bf16 inputs with fp32 LSE
+and accumulators; Q/K/V/dO i.i.d. N(0,1) (seed 2 + rank), scale 1/sqrt(D).
+A step is one forward (O, LSE) plus one backward (dQ, dK, dV) over the batch.
+
+Metric: effective TFLOP/s counting only unmasked (i, j) pairs,
+F = 3.5 * 4 * D * pairs * B * H per step (pairs per head from the layout).
+Multi-GPU (torchrun): every rank processes its own batch of the same shape
+((batch, head) partition, no collective on the data path; "weak" scaling);
+value = N * F / max-over-ranks time.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
+
+``--impl reference`` times the reference's CPU dense-masked path (the oracle
+port in ``oracle/``) on this host's cores on a bounded sample of the same
+workload and prints the same JSON line with ``"impl": "reference"``.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import re
+import statistics
+import subprocess
+import sys
+import time
+
+import torch
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+if ROOT not in sys.path:
+    sys.path.insert(0, ROOT)
+
+WORKLOAD = dict(name="c3", B=4, H=32, T=16384, D=128, block=128, window=4, stride=8, sinks=2,
+                seed=2)
+METRIC = "SMat attn fwd+bwd effective TFLOP/s (unmasked FLOPs)"
+UNIT = "TFLOP/s"
+
+
+def _layout_pairs():
+    from smat_attention_b200.mask import block_layout_stats, build_block_mask
+    w = WORKLOAD
+    spec = build_block_mask(w["T"], w["block"], w["window"], w["stride"], w["sinks"])
+    return spec, block_layout_stats(spec)["pairs"]
+
+
+def _flops(pairs):
+    w = WORKLOAD
+    fwd = 4.0 * w["D"] * pairs * w["B"] * w["H"]
+    return {"fwd": fwd, "dkdv": 2.0 * fwd, "dq": 1.5 * fwd, "step": 3.5 * fwd}
+
+
+def _peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            p = json.load(f)
+        return {"tflops": float(p["bf16_tflops_sustained"]), "hbm": float(p["hbm_gbs"]),
+                "source": "measured (MEASURED_PEAKS.json, bf16_tflops_sustained)"}
+    except (OSError, KeyError, ValueError):
+        return {"tflops": 1400.0, "hbm": 6650.0,
+                "source": "fallback (1.4 PFLOP/s sustained, 6.65 TB/s)"}
+
+
+def _traffic():
+    """Per-launch DRAM bytes of the dominant kernel from the committed ncu
+    summary (profiles/), if one is present."""
+    path = os.path.join(ROOT, "profiles", "traffic_c3.txt")
+    out = {}
+    try:
+        for line in open(path):
+            m = re.match(r"\s*(\w+)\s+dram_bytes_per_launch\s*=\s*([0-9.eE+]+)", line)
+            if m:
+                out[m.group(1)] = float(m.group(2))
+    except OSError:
+        pass
+    return out
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle samples while the timed region runs."""
+
+    FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device):
+        self.proc = None
+        try:
+            uuid = str(torch.cuda.get_device_properties(device).uuid)
+            ident = uuid if uuid.startswith("GPU-") else f"GPU-{uuid}"
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", ident, f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        time.sleep(0.25)
+        self.proc.terminate()
+        try:
+            out, _ = self.proc.communicate(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+            out, _ = self.proc.communicate()
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in out.splitlines():
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 8:
+                continue
+            try:
+                sm.append(float(parts[0]))
+                mx.append(float(parts[1]))
+            except ValueError:
+                continue
+            for name, val in zip(names, parts[4:8]):
+                if val.lower() == "active":
+                    reasons.add(name)
+        if not sm:
+            return None
+        load = [s for s in sm if s > 0.5 * max(sm)] or sm
+        return {"sm_mhz": statistics.median(load), "sm_max_mhz": max(mx),
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def _dist():
+    ws = int(os.environ.get("WORLD_SIZE", "1"))
+    if ws > 1:
+        import datetime
+        import torch.distributed as dist
+        rank = int(os.environ["RANK"])
+        local = int(os.environ.get("LOCAL_RANK", rank))
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+        return dist, rank, ws, local
+    return None, 0, 1, 0
+
+
+def _barrier(dist, device):
+    if dist is not None:
+        dist.barrier(device_ids=[device.index])
+    torch.cuda.synchronize(device)
+
+
+def _max_over_ranks(dist, value, device):
+    if dist is None:
+        return value
+    t = torch.tensor([value], dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+# ----------------------------------------------------------------------------
+# CPU baseline: the reference's dense-masked path (oracle port) on host cores
+# ----------------------------------------------------------------------------
+
+def cpu_sample(reps=1):
+    """Time the oracle's dense-masked fp32 forward + backward on one (batch,
+    head) of the workload at the full sequence length; returns the effective
+    TFLOP/s of that head and a description."""
+    from oracle import layout as OL
+    from oracle.dense_softmax import rowchunked_masked_softmax
+    w = WORKLOAD
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    spec, pairs = _layout_pairs()
+    g = torch.Generator().manual_seed(w["seed"])
+    q, k, v, do = (torch.randn(1, w["T"], w["D"], generator=g).to(torch.bfloat16).float()
+                   for _ in range(4))
+    rows = OL.block_mask_rows(w["T"], w["block"], w["window"], w["stride"], w["sinks"])
+    times = []
+    for _ in range(reps):
+        t0 = time.perf_counter()
+        rowchunked_masked_softmax(q, k, v, do, rows, 1 / math.sqrt(w["D"]), rows=2048)
+        times.append(time.perf_counter() - t0)
+    t = statistics.median(times)
+    f_head = 3.5 * 4.0 * w["D"] * pairs
+    return {"value": f_head / t / 1e12, "unit": UNIT, "cores": threads, "kind": "port",
+            "sample": f"one (b,h) head of {w['name']} (T={w['T']}, D={w['D']}) dense-masked "
+                      f"fp32 fwd+bwd, oracle port, median of {reps}: {t:.2f} s/head"}
+
+
+def run_reference(args):
+    dist, rank, ws, local = _dist()
+    if rank != 0:
+        if dist is not None:
+            dist.destroy_process_group()
+        return
+    for _ in range(max(0, args.warmup)):
+        pass   # the CPU sample needs no device warm-up; each step is a full sample
+    vals = []
+    t0 = time.perf_counter()
+    steps = max(1, args.steps)
+    base = None
+    for _ in range(steps):
+        base = cpu_sample(reps=1)
+        vals.append(base["value"])
+    elapsed = time.perf_counter() - t0
+    v = statistics.median(vals)
+    base["value"] = v
+    line = {"metric": METRIC, "value": v, "unit": UNIT, "n_gpus": args.gpus, "steps": steps,
+            "warmup": args.warmup, "ms_per_step": elapsed / steps * 1e3,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic", "impl": "reference",
+            "config": {"workload": f"{WORKLOAD['name']} sample (one head)", **WORKLOAD},
+            "cpu_baseline": base,
+            "e2e": {"value": v, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+    if dist is not None:
+        dist.destroy_process_group()
+
+
+# ----------------------------------------------------------------------------
+# GPU arm
+# ----------------------------------------------------------------------------
+
+def run_gpu(args):
+    from smat_attention_b200 import _lib
+    from smat_attention_b200.attention import (bwd, check_device_errors, fwd,
+                                               layout_device_args, smat_softmax_attention)
+    dist, rank, ws, local = _dist()
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    w = WORKLOAD
+    spec, pairs = _layout_pairs()
+    fl = _flops(pairs)
+    scale = 1.0 / math.sqrt(w["D"])
+    g = torch.Generator().manual_seed(w["seed"] + rank)
+    shape = (w["B"], w["H"], w["T"], w["D"])
+    host = [torch.randn(*shape, generator=g).to(torch.bfloat16) for _ in range(4)]
+    q, k, v, do = (x.to(device) for x in host)
+    L = _lib.lib()
+    lay = layout_device_args(spec, device)
+    o = torch.empty_like(q)
+    lse = torch.empty(w["B"], w["H"], w["T"], dtype=torch.float32, device=device)
+    delta = torch.empty_like(lse)
+    dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
+    err = torch.zeros(1, dtype=torch.int32, device=device)
+    stream = torch.cuda.current_stream(device)
+    sp = _lib.strides3
+    B, H, T, D = shape
+
+    def launch_fwd():
+        _lib.check("smat_fwd", L.smat_fwd(
+            1, q.data_ptr(), sp(q), k.data_ptr(), sp(k), v.data_ptr(), sp(v), o.data_ptr(), sp(o),
+            lse.data_ptr(), B, H, T, D, lay["indptr"].data_ptr(), lay["indices"].data_ptr(),
+            lay["kind"].data_ptr(), lay["nblocks"], lay["nnzb"], lay["block"], lay["max_row"],
+            scale, err.data_ptr(), stream.cuda_stream))
+
+    def launch_pre():
+        _lib.check("smat_bwd_preprocess", L.smat_bwd_preprocess(
+            1, o.data_ptr(), sp(o), do.data_ptr(), sp(do), delta.data_ptr(), B, H, T, D,
+            stream.cuda_stream))
+
+    def launch_dkdv():
+        _lib.check("smat_bwd_dkdv", L.smat_bwd_dkdv(
+            1, q.data_ptr(), sp(q), k.data_ptr(), sp(k), v.data_ptr(), sp(v), do.data_ptr(),
+            sp(do), lse.data_ptr(), delta.data_ptr(), dk.data_ptr(), sp(dk), dv.data_ptr(),
+            sp(dv), B, H, T, D, lay["t_indptr"].data_ptr(), lay["t_indices"].data_ptr(),
+            lay["t_kind"].data_ptr(), lay["nblocks"], lay["nnzb"], lay["block"],
+            lay["t_max_row"], scale, err.data_ptr(), stream.cuda_stream))
+
+    def launch_dq():
+        _lib.check("smat_bwd_dq", L.smat_bwd_dq(
+            1, q.data_ptr(), sp(q), k.data_ptr(), sp(k), v.data_ptr(), sp(v), do.data_ptr(),
+            sp(do), lse.data_ptr(), delta.data_ptr(), dq.data_ptr(), sp(dq), B, H, T, D,
+            lay["indptr"].data_ptr(), lay["indices"].data_ptr(), lay["kind"].data_ptr(),
+            lay["nblocks"], lay["nnzb"], lay["block"], lay["max_row"], scale, err.data_ptr(),
+            stream.cuda_stream))
+
+    kernels = [("fwd", launch_fwd), ("bwd_pre", launch_pre), ("dkdv", launch_dkdv),
+               ("dq", launch_dq)]
+    for _ in range(max(3, args.warmup)):
+        for _, fn in kernels:
+            fn()
+    _barrier(dist, device)
+
+    # ---- device-resident timed region --------------------------------------
+    K = args.steps
+    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(len(kernels) + 1)]
+          for _ in range(K)]
+    clocks = ClockSampler(device)
+    _barrier(dist, device)
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record(stream)
+    for s in range(K):
+        ev[s][0].record(stream)
+        for i, (_, fn) in enumerate(kernels):
+            fn()
+            ev[s][i + 1].record(stream)
+    stop.record(stream)
+    torch.cuda.synchronize(device)
+    clk = clocks.stop()
+    _barrier(dist, device)
+    total_ms = start.elapsed_time(stop)
+    per_kernel = {name: sum(ev[s][i].elapsed_time(ev[s][i + 1]) for s in range(K)) / K
+                  for i, (name, _) in enumerate(kernels)}
+    dev_err = int(err.item())
+    ms_step = _max_over_ranks(dist, total_ms / K, device)
+    value = ws * fl["step"] / (ms_step * 1e-3) / 1e12
+
+    # ---- end to end through the public API with host buffers ---------------
+    pinned = [x.pin_memory() for x in host]
+    outs = [torch.empty(shape, dtype=torch.bfloat16).pin_memory() for _ in range(4)]
+    E = max(1, min(K, 3))
+
+    def e2e_step():
+        qd, kd, vd, dod = (x.to(device, non_blocking=True) for x in pinned)
+        qd.requires_grad_(True)
+        kd.requires_grad_(True)
+        vd.requires_grad_(True)
+        od, _ = smat_softmax_attention(qd, kd, vd, spec, scale)
+        od.backward(dod)
+        for dst, src in zip(outs, (od.detach(), qd.grad, kd.grad, vd.grad)):
+            dst.copy_(src, non_blocking=True)
+
+    e2e_step()
+    _barrier(dist, device)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(E):
+        e2e_step()
+    e1.record(stream)
+    torch.cuda.synchronize(device)
+    e2e_ms = _max_over_ranks(dist, e0.elapsed_time(e1) / E, device)
+    dev_err |= check_device_errors(device)
+    nbytes = sum(x.numel() * x.element_size() for x in host)
+
+    if rank == 0:
+        peaks = _peaks()
+        dom = max(per_kernel, key=per_kernel.get)
+        achieved = fl[dom if dom in fl else "fwd"] / (per_kernel[dom] * 1e-3) / 1e12 \
+            if dom != "bwd_pre" else None
+        traffic = _traffic().get(dom)
+        line = {
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": ws, "steps": K,
+            "warmup": max(3, args.warmup), "ms_per_step": ms_step, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": f"{w['name']}: B={w['B']} H={w['H']} T={w['T']} D={w['D']} "
+                                   f"bs={w['block']} W={w['window']} S={w['stride']} "
+                                   f"sinks={w['sinks']} fwd+bwd per rank",
+                       "global_batch": w["B"] * ws, "seq_len": w["T"], "heads": w["H"],
+                       "head_dim": w["D"], "parallelism": f"(batch,head) partition x{ws}",
+                       "l2": "inputs larger than L2 (512 MiB per tensor); no flush"},
+            "tokens_per_s": ws * w["B"] * w["T"] / (ms_step * 1e-3),
+            "frac_of_peak": value / ws / peaks["tflops"],
+            "peak_source": peaks["source"],
+            "per_kernel_ms": per_kernel,
+            "roofline": {"bound": "tensor", "kernel": dom, "achieved": achieved,
+                         "peak": peaks["tflops"], "unit": UNIT,
+                         "frac": None if achieved is None else achieved / peaks["tflops"],
+                         "traffic": traffic},
+            "e2e": {"value": ws * fl["step"] / (e2e_ms * 1e-3) / 1e12, "unit": UNIT,
+                    "ms_per_step": e2e_ms, "h2d_bytes_per_step": nbytes,
+                    "d2h_bytes_per_step": nbytes},
+            "gpu_launches": K * len(kernels),
+            "device_errors": dev_err,
+            "clocks": clk,
+        }
+        if ws == 1 and not args.no_cpu_baseline:
+            line["cpu_baseline"] = cpu_sample(reps=1)
+        print(json.dumps(line), flush=True)
+    if dist is not None:
+        dist.destroy_process_group()
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_gpu(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,197 @@
+/*
+ * smat_b200.h -- C ABI of the B200 (sm_100a) SMat block-sparse causal softmax
+ * attention library (libsmat_b200.so).
+ *
+ * Conventions
+ *   - Tensors q, k, v, o, dO, dq, dk, dv are [B, H, T, D] with the D dimension
+ *     contiguous; each is passed as a device pointer plus a host array of three
+ *     int64 element strides {stride_b, stride_h, stride_t}.
+ *   - lse and delta are contiguous fp32 [B * H * T] device arrays.  lse is the
+ *     natural-log normaliser log(sum_j exp(scale * q_i . k_j)) over the
+ *     unmasked keys of row i (-inf for an empty row).
+ *   - The layout is an int32 CSR over blocks of `block` positions:
+ *     indptr[nblocks + 1], indices[nnzb] (key blocks per query block,
+ *     ascending) and one kind byte per entry (SMAT_TILE_FULL or
+ *     SMAT_TILE_CAUSAL).  The backward dK/dV pass takes the transposed CSR
+ *     (query blocks per key block).  All of them live in device memory.
+ *   - Every buffer is caller-allocated; no entry point allocates device
+ *     memory.  Kernels are enqueued on `stream` (a cudaStream_t, NULL for the
+ *     legacy default stream) and the calls return without synchronising.
+ *   - Return value: SMAT_OK or an smat_status code; argument errors are
+ *     detected on the host before anything is launched.  Device-side faults
+ *     of the pipeline (a bounded wait that timed out, a malformed CSR seen by
+ *     a kernel) are OR-ed into *err_word (device int32, may be NULL), which the
+ *     caller reads after synchronising.
+ *   - dtype SMAT_DTYPE_BF16 runs the tcgen05 tensor-core kernels (D in {64,
+ *     128}, block in {64, 128}); SMAT_DTYPE_F32 runs full-fp32 CUDA-core
+ *     kernels (D in {32, 64, 128}, any block size).
+ *
+ * These entry points replace, for the softmax arm, the reference's attention
+ * call sites: the dense causal SDPA of the softmax arm
+ * (src/smat/model.py:217-220) and the fused-kernel table the SMat arm looks up
+ * as module attributes (src/smat/attention.py:37-40, 183-185) with its
+ * differentiable wrappers (src/smat/kernels/triton_bwd.py:154-196, 331-346).
+ */
+#ifndef SMAT_B200_H
+#define SMAT_B200_H
+
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define SMAT_API __attribute__((visibility("default")))
+#else
+#define SMAT_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum smat_status {
+  SMAT_OK = 0,
+  SMAT_ERR_BAD_SHAPE = 1,
+  SMAT_ERR_UNSUPPORTED_D = 2,
+  SMAT_ERR_UNSUPPORTED_BLOCK = 3,
+  SMAT_ERR_UNSUPPORTED_DTYPE = 4,
+  SMAT_ERR_BAD_STRIDE = 5,
+  SMAT_ERR_BAD_ALIGNMENT = 6,
+  SMAT_ERR_CSR_INVALID = 7,
+  SMAT_ERR_NULL_POINTER = 8,
+  SMAT_ERR_LAUNCH = 9,
+  SMAT_ERR_NO_DEVICE = 10,
+  SMAT_ERR_TMA_DESCRIPTOR = 11,
+  SMAT_ERR_ROW_TOO_LONG = 12,
+  SMAT_ERR_CAPACITY = 13
+} smat_status;
+
+enum { SMAT_DTYPE_F32 = 0, SMAT_DTYPE_BF16 = 1 };
+enum { SMAT_TILE_FULL = 0, SMAT_TILE_CAUSAL = 1 };
+
+/* Bits of *err_word. */
+enum {
+  SMAT_DEVERR_WAIT_TIMEOUT = 1,
+  SMAT_DEVERR_BAD_CSR = 2,
+  SMAT_DEVERR_SCHED_OVERFLOW = 4
+};
+
+/* ABI version of this header (incremented on any signature change). */
+SMAT_API int smat_abi_version(void);
+
+/* Human-readable name of a status code (static string). */
+SMAT_API const char* smat_status_string(int status);
+
+/* SMAT_OK if `device` is an sm_100 GPU this library was built for. */
+SMAT_API int smat_device_supported(int device);
+
+/* ---------------------------------------------------------------- layouts
+ * Host-side builders and checks on host arrays (no GPU needed).
+ *
+ * smat_layout_build_block: the block layout of the module's mask builder
+ * (smat_attention_b200.mask.build_block_mask).  Tile (qb, kb) is active iff
+ * kb <= qb and (qb - window <= kb or kb < n_sink or (stride > 0 and
+ * kb % stride == stride - 1)); the diagonal tile is SMAT_TILE_CAUSAL.  With
+ * indices == NULL only *nnzb_out is computed.  indptr has nblocks + 1 =
+ * ceil(T / block) + 1 entries; indices/kind need `capacity` >= nnzb entries.
+ * Replaces, for the block kind, the reference's mask constructor
+ * (src/smat/mask.py:244-389, build_mask).
+ */
+SMAT_API int smat_layout_build_block(int T, int block, int window, int stride, int n_sink,
+                            int32_t* indptr, int32_t* indices, uint8_t* kind,
+                            int64_t capacity, int64_t* nnzb_out);
+
+/* Transposed CSR (per key block, ascending query blocks, kinds carried). */
+SMAT_API int smat_layout_transpose(int nblocks, const int32_t* indptr, const int32_t* indices,
+                          const uint8_t* kind, int32_t* t_indptr, int32_t* t_indices,
+                          uint8_t* t_kind);
+
+/* Checks a (forward or transposed) layout: indptr starts at 0, never
+ * decreases and ends at nnzb; indices are in [0, nblocks) and strictly
+ * ascending per row; every entry is causal (key block <= query block, i.e.
+ * index <= row for the forward CSR and index >= row for the transposed one);
+ * the kind is SMAT_TILE_CAUSAL exactly on the diagonal and SMAT_TILE_FULL
+ * elsewhere.  Writes the longest row to *max_row_out (may be NULL). */
+SMAT_API int smat_layout_validate(int nblocks, int64_t nnzb, const int32_t* indptr,
+                         const int32_t* indices, const uint8_t* kind, int transposed,
+                         int32_t* max_row_out);
+
+/* ---------------------------------------------------------------- forward
+ * o = softmax_M(scale q k^T) v and lse, for the layout (indptr, indices,
+ * kind).  max_row is the longest CSR row (from smat_layout_validate).
+ * Replaces the softmax arm's F.scaled_dot_product_attention call
+ * (src/smat/model.py:217-220) and, as the fused forward of the attention op,
+ * the reference's chunk_local launcher (src/smat/kernels/triton_fwd.py:118-152).
+ */
+SMAT_API int smat_fwd(int dtype,
+             const void* q, const int64_t* q_stride,
+             const void* k, const int64_t* k_stride,
+             const void* v, const int64_t* v_stride,
+             void* o, const int64_t* o_stride,
+             float* lse,
+             int B, int H, int T, int D,
+             const int32_t* indptr, const int32_t* indices, const uint8_t* kind,
+             int nblocks, int64_t nnzb, int block, int max_row,
+             float scale, int32_t* err_word, void* stream);
+
+/* ---------------------------------------------------------------- backward
+ * delta[b, h, t] = sum_d dO[b,h,t,d] * o[b,h,t,d]
+ * (the row-sum preprocess of the reference's backward,
+ * src/smat/kernels/triton_bwd.py:154-196, restated for softmax). */
+SMAT_API int smat_bwd_preprocess(int dtype,
+                        const void* o, const int64_t* o_stride,
+                        const void* dout, const int64_t* do_stride,
+                        float* delta, int B, int H, int T, int D, void* stream);
+
+/* dk, dv over the transposed CSR (t_indptr, t_indices, t_kind); t_max_row is
+ * its longest row.  Replaces the reference's column-parallel backward kernel
+ * (src/smat/kernels/triton_bwd.py:98-147). */
+SMAT_API int smat_bwd_dkdv(int dtype,
+                  const void* q, const int64_t* q_stride,
+                  const void* k, const int64_t* k_stride,
+                  const void* v, const int64_t* v_stride,
+                  const void* dout, const int64_t* do_stride,
+                  const float* lse, const float* delta,
+                  void* dk, const int64_t* dk_stride,
+                  void* dv, const int64_t* dv_stride,
+                  int B, int H, int T, int D,
+                  const int32_t* t_indptr, const int32_t* t_indices, const uint8_t* t_kind,
+                  int nblocks, int64_t nnzb, int block, int t_max_row,
+                  float scale, int32_t* err_word, void* stream);
+
+/* dq over the forward CSR.  Replaces the reference's row-parallel backward
+ * kernel (src/smat/kernels/triton_bwd.py:50-94). */
+SMAT_API int smat_bwd_dq(int dtype,
+                const void* q, const int64_t* q_stride,
+                const void* k, const int64_t* k_stride,
+                const void* v, const int64_t* v_stride,
+                const void* dout, const int64_t* do_stride,
+                const float* lse, const float* delta,
+                void* dq, const int64_t* dq_stride,
+                int B, int H, int T, int D,
+                const int32_t* indptr, const int32_t* indices, const uint8_t* kind,
+                int nblocks, int64_t nnzb, int block, int max_row,
+                float scale, int32_t* err_word, void* stream);
+
+/* The whole backward: preprocess into the caller's delta workspace
+ * (fp32 [B*H*T]), then dK/dV and dQ.  Replaces the autograd backward of the
+ * reference's fused path (src/smat/kernels/triton_bwd.py:162-196). */
+SMAT_API int smat_bwd(int dtype,
+             const void* q, const int64_t* q_stride,
+             const void* k, const int64_t* k_stride,
+             const void* v, const int64_t* v_stride,
+             const void* o, const int64_t* o_stride,
+             const void* dout, const int64_t* do_stride,
+             const float* lse, float* delta,
+             void* dq, const int64_t* dq_stride,
+             void* dk, const int64_t* dk_stride,
+             void* dv, const int64_t* dv_stride,
+             int B, int H, int T, int D,
+             const int32_t* indptr, const int32_t* indices, const uint8_t* kind,
+             const int32_t* t_indptr, const int32_t* t_indices, const uint8_t* t_kind,
+             int nblocks, int64_t nnzb, int block, int max_row, int t_max_row,
+             float scale, int32_t* err_word, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* SMAT_B200_H */

@@ -1,0 +1,254 @@
+// fp32 path: block-sparse causal softmax attention on CUDA cores.
+//
+// The fp32 contract is 1e-4 max-abs against an fp32 reference, which a
+// tensor-core tf32 product cannot meet, so fp32 inputs run here in full fp32
+// (fmaf, expf, logf).  These kernels serve the small fp32 configurations; the
+// bf16 path uses the tcgen05 kernels.
+//
+// Each query (or key) row is owned by TPR = D / 32 adjacent lanes holding 32
+// of its D components; dot products are reduced across those lanes with
+// shuffles.  The walk over the layout is the same CSR walk the tensor-core
+// kernels do, one key (or query) at a time, causal inside diagonal tiles.
+#pragma once
+
+#include "common.cuh"
+
+namespace smat {
+
+struct SimtParams {
+  const float* q;
+  const float* k;
+  const float* v;
+  const float* o;
+  const float* dout;
+  const float* lse;
+  const float* delta;
+  float* out0;  // o (fwd) / dq / dk
+  float* out1;  // lse (fwd) / dv
+  int64_t q_s[3], k_s[3], v_s[3], o_s[3], do_s[3], out0_s[3], out1_s[3];
+  const int32_t* indptr;
+  const int32_t* indices;
+  const uint8_t* kind;
+  int B, H, T, nblocks, nnzb, bs;
+  float scale;
+  int32_t* err;
+};
+
+// Sum over the TPR lanes that own one row.  Only those lanes take part (the
+// mask names them), so rows of one warp may walk different key counts.
+template <int TPR>
+__device__ __forceinline__ float group_sum(float x) {
+  if (TPR == 1) return x;
+  const unsigned lane = threadIdx.x & 31u;
+  const unsigned mask = ((1u << TPR) - 1u) << (lane & ~static_cast<unsigned>(TPR - 1));
+#pragma unroll
+  for (int o = 1; o < TPR; o <<= 1) x += __shfl_xor_sync(mask, x, o);
+  return x;
+}
+
+__device__ __forceinline__ const float* row_ptr(const float* base, const int64_t* s, int b, int h,
+                                                int t) {
+  return base + b * s[0] + h * s[1] + static_cast<int64_t>(t) * s[2];
+}
+
+// grid: (ceil(T / rows_per_cta), B * H); block 128 threads.
+template <int D>
+__global__ void __launch_bounds__(128) smat_fwd_simt_kernel(const SimtParams p) {
+  constexpr int TPR = D / 32;
+  constexpr int RPC = 128 / TPR;
+  const int bh = blockIdx.y, b = bh / p.H, h = bh % p.H;
+  const int g = threadIdx.x / TPR, part = threadIdx.x % TPR;
+  const int i = blockIdx.x * RPC + g;
+  const bool active = i < p.T;
+  const int ii = active ? i : p.T - 1;
+  float q[32], acc[32];
+  const float* qr = row_ptr(p.q, p.q_s, b, h, ii) + part * 32;
+#pragma unroll
+  for (int d = 0; d < 32; ++d) {
+    q[d] = qr[d] * p.scale;
+    acc[d] = 0.f;
+  }
+  float m = -INFINITY, l = 0.f;
+  const int qb = ii / p.bs;
+  const int e0 = p.indptr[qb], e1 = p.indptr[qb + 1];
+  for (int e = e0; e < e1; ++e) {
+    const int kb = p.indices[e];
+    const bool causal = p.kind[e] == 1;
+    const int j0 = kb * p.bs, j1 = min(p.T, j0 + p.bs);
+    for (int j = j0; j < j1; ++j) {
+      const float* kr = row_ptr(p.k, p.k_s, b, h, j) + part * 32;
+      float s = 0.f;
+#pragma unroll
+      for (int d = 0; d < 32; ++d) s = fmaf(q[d], kr[d], s);
+      s = group_sum<TPR>(s);
+      if (causal && j > ii) continue;
+      const float* vr = row_ptr(p.v, p.v_s, b, h, j) + part * 32;
+      if (s > m) {
+        const float alpha = (m == -INFINITY) ? 0.f : expf(m - s);
+        l *= alpha;
+#pragma unroll
+        for (int d = 0; d < 32; ++d) acc[d] *= alpha;
+        m = s;
+      }
+      const float pr = expf(s - m);
+      l += pr;
+#pragma unroll
+      for (int d = 0; d < 32; ++d) acc[d] = fmaf(pr, vr[d], acc[d]);
+    }
+  }
+  if (!active) return;
+  const float inv = l > 0.f ? 1.f / l : 0.f;
+  float* orow = p.out0 + b * p.out0_s[0] + h * p.out0_s[1] + static_cast<int64_t>(i) * p.out0_s[2] +
+                part * 32;
+#pragma unroll
+  for (int d = 0; d < 32; ++d) orow[d] = acc[d] * inv;
+  if (part == 0) p.out1[static_cast<int64_t>(bh) * p.T + i] = l > 0.f ? m + logf(l) : -INFINITY;
+}
+
+// dQ: per query row, walk the forward CSR.
+template <int D>
+__global__ void __launch_bounds__(128) smat_dq_simt_kernel(const SimtParams p) {
+  constexpr int TPR = D / 32;
+  constexpr int RPC = 128 / TPR;
+  const int bh = blockIdx.y, b = bh / p.H, h = bh % p.H;
+  const int g = threadIdx.x / TPR, part = threadIdx.x % TPR;
+  const int i = blockIdx.x * RPC + g;
+  const bool active = i < p.T;
+  const int ii = active ? i : p.T - 1;
+  float q[32], dor[32], dq[32];
+  const float* qr = row_ptr(p.q, p.q_s, b, h, ii) + part * 32;
+  const float* dr = row_ptr(p.dout, p.do_s, b, h, ii) + part * 32;
+#pragma unroll
+  for (int d = 0; d < 32; ++d) {
+    q[d] = qr[d] * p.scale;
+    dor[d] = dr[d];
+    dq[d] = 0.f;
+  }
+  const float lse = p.lse[static_cast<int64_t>(bh) * p.T + ii];
+  const float dl = p.delta[static_cast<int64_t>(bh) * p.T + ii];
+  const int qb = ii / p.bs;
+  for (int e = p.indptr[qb]; e < p.indptr[qb + 1]; ++e) {
+    const int kb = p.indices[e];
+    const bool causal = p.kind[e] == 1;
+    const int j0 = kb * p.bs, j1 = min(p.T, j0 + p.bs);
+    for (int j = j0; j < j1; ++j) {
+      const float* kr = row_ptr(p.k, p.k_s, b, h, j) + part * 32;
+      const float* vr = row_ptr(p.v, p.v_s, b, h, j) + part * 32;
+      float s = 0.f, dp = 0.f;
+#pragma unroll
+      for (int d = 0; d < 32; ++d) {
+        s = fmaf(q[d], kr[d], s);
+        dp = fmaf(dor[d], vr[d], dp);
+      }
+      s = group_sum<TPR>(s);
+      dp = group_sum<TPR>(dp);
+      if (causal && j > ii) continue;
+      const float pr = expf(s - lse);
+      const float ds = pr * (dp - dl);
+#pragma unroll
+      for (int d = 0; d < 32; ++d) dq[d] = fmaf(ds, kr[d], dq[d]);
+    }
+  }
+  if (!active) return;
+  float* out = p.out0 + b * p.out0_s[0] + h * p.out0_s[1] + static_cast<int64_t>(i) * p.out0_s[2] +
+               part * 32;
+#pragma unroll
+  for (int d = 0; d < 32; ++d) out[d] = dq[d] * p.scale;
+}
+
+// dK, dV: per key row, walk the transposed CSR.
+template <int D>
+__global__ void __launch_bounds__(128) smat_dkdv_simt_kernel(const SimtParams p) {
+  constexpr int TPR = D / 32;
+  constexpr int RPC = 128 / TPR;
+  const int bh = blockIdx.y, b = bh / p.H, h = bh % p.H;
+  const int g = threadIdx.x / TPR, part = threadIdx.x % TPR;
+  const int j = blockIdx.x * RPC + g;
+  const bool active = j < p.T;
+  const int jj = active ? j : p.T - 1;
+  float kr[32], vr[32], dk[32], dv[32];
+  const float* kp = row_ptr(p.k, p.k_s, b, h, jj) + part * 32;
+  const float* vp = row_ptr(p.v, p.v_s, b, h, jj) + part * 32;
+#pragma unroll
+  for (int d = 0; d < 32; ++d) {
+    kr[d] = kp[d] * p.scale;
+    vr[d] = vp[d];
+    dk[d] = 0.f;
+    dv[d] = 0.f;
+  }
+  const int kb = jj / p.bs;
+  for (int e = p.indptr[kb]; e < p.indptr[kb + 1]; ++e) {
+    const int qb = p.indices[e];
+    const bool causal = p.kind[e] == 1;
+    const int i0 = qb * p.bs, i1 = min(p.T, i0 + p.bs);
+    for (int i = i0; i < i1; ++i) {
+      const float* qp = row_ptr(p.q, p.q_s, b, h, i) + part * 32;
+      const float* dp_ = row_ptr(p.dout, p.do_s, b, h, i) + part * 32;
+      float s = 0.f, dp = 0.f;
+#pragma unroll
+      for (int d = 0; d < 32; ++d) {
+        s = fmaf(qp[d], kr[d], s);
+        dp = fmaf(dp_[d], vr[d], dp);
+      }
+      s = group_sum<TPR>(s);
+      dp = group_sum<TPR>(dp);
+      if (causal && jj > i) continue;
+      const float lse = p.lse[static_cast<int64_t>(bh) * p.T + i];
+      const float dl = p.delta[static_cast<int64_t>(bh) * p.T + i];
+      const float pr = expf(s - lse);
+      const float ds = pr * (dp - dl);
+#pragma unroll
+      for (int d = 0; d < 32; ++d) {
+        dv[d] = fmaf(pr, dp_[d], dv[d]);
+        dk[d] = fmaf(ds, qp[d], dk[d]);
+      }
+    }
+  }
+  if (!active) return;
+  float* ko = p.out0 + b * p.out0_s[0] + h * p.out0_s[1] + static_cast<int64_t>(j) * p.out0_s[2] +
+              part * 32;
+  float* vo = p.out1 + b * p.out1_s[0] + h * p.out1_s[1] + static_cast<int64_t>(j) * p.out1_s[2] +
+              part * 32;
+#pragma unroll
+  for (int d = 0; d < 32; ++d) {
+    ko[d] = dk[d] * p.scale;
+    vo[d] = dv[d];
+  }
+}
+
+// delta[bh, t] = sum_d dO[b,h,t,d] * O[b,h,t,d]; one warp per 32 / LPR rows,
+// LPR lanes per row each reading 16-byte vectors.
+template <typename T, int D>
+__global__ void __launch_bounds__(256) smat_bwd_pre_kernel(const T* __restrict__ o,
+                                                           const T* __restrict__ dout,
+                                                           float* __restrict__ delta,
+                                                           int64_t o_sb, int64_t o_sh,
+                                                           int64_t o_st, int64_t d_sb,
+                                                           int64_t d_sh, int64_t d_st, int H,
+                                                           int T_, int64_t rows) {
+  constexpr int VEC = 16 / sizeof(T);
+  constexpr int LPR = D / VEC;  // lanes per row
+  static_assert(LPR <= 32 && 32 % LPR == 0, "unsupported D");
+  const int64_t gt = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  const int64_t row = gt / LPR;
+  const int part = static_cast<int>(gt % LPR);
+  float acc = 0.f;
+  if (row < rows) {
+    const int t = static_cast<int>(row % T_);
+    const int64_t bh = row / T_;
+    const int b = static_cast<int>(bh / H), h = static_cast<int>(bh % H);
+    const T* op = o + b * o_sb + h * o_sh + t * o_st + part * VEC;
+    const T* dp = dout + b * d_sb + h * d_sh + t * d_st + part * VEC;
+    const uint4 ov = *reinterpret_cast<const uint4*>(op);
+    const uint4 dv = *reinterpret_cast<const uint4*>(dp);
+    const T* oe = reinterpret_cast<const T*>(&ov);
+    const T* de = reinterpret_cast<const T*>(&dv);
+#pragma unroll
+    for (int i = 0; i < VEC; ++i) acc = fmaf(static_cast<float>(oe[i]), static_cast<float>(de[i]), acc);
+  }
+#pragma unroll
+  for (int off = 1; off < LPR; off <<= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
+  if (row < rows && part == 0) delta[row] = acc;
+}
+
+}  // namespace smat

@@ -1,0 +1,572 @@
+// C ABI of libsmat_b200.so (declared in include/smat_b200.h): argument checks,
+// TMA descriptor construction and kernel launches.  Nothing here allocates
+// device memory and nothing synchronises; every check that can fail runs on
+// the host before the first launch.
+#include <cudaTypedefs.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstdint>
+#include <cstring>
+#include <mutex>
+#include <vector>
+
+#include "../../include/smat_b200.h"
+#include "bwd_tc.cuh"
+#include "fwd_tc.cuh"
+#include "simt_fp32.cuh"
+
+namespace {
+
+using namespace smat;
+
+struct TArg {
+  const void* p;
+  int64_t sb, sh, st;
+};
+
+TArg targ(const void* p, const int64_t* s) { return TArg{p, s[0], s[1], s[2]}; }
+
+// ---------------------------------------------------------------- checks
+int check_common(int dtype, int B, int H, int T, int D, int nblocks, int block) {
+  if (B < 1 || H < 1 || T < 1) return SMAT_ERR_BAD_SHAPE;
+  if (block < 1) return SMAT_ERR_UNSUPPORTED_BLOCK;
+  if (nblocks != (T + block - 1) / block) return SMAT_ERR_BAD_SHAPE;
+  if (dtype == SMAT_DTYPE_BF16) {
+    if (D != 64 && D != 128) return SMAT_ERR_UNSUPPORTED_D;
+    if (block != 64 && block != 128) return SMAT_ERR_UNSUPPORTED_BLOCK;
+  } else if (dtype == SMAT_DTYPE_F32) {
+    if (D != 32 && D != 64 && D != 128) return SMAT_ERR_UNSUPPORTED_D;
+  } else {
+    return SMAT_ERR_UNSUPPORTED_DTYPE;
+  }
+  if (static_cast<int64_t>(B) * H > (1LL << 30) / std::max(1, (T + 127) / 128))
+    return SMAT_ERR_BAD_SHAPE;  // linear grid index must fit an int
+  return SMAT_OK;
+}
+
+// Tensor argument: non-null, strides non-negative; for bf16 the TMA / vector
+// store rules (16-byte aligned base, strides a multiple of 8 elements).
+int check_tensor(const TArg& t, int dtype) {
+  if (!t.p) return SMAT_ERR_NULL_POINTER;
+  if (t.sb < 0 || t.sh < 0 || t.st < 0) return SMAT_ERR_BAD_STRIDE;
+  if (dtype == SMAT_DTYPE_BF16) {
+    if (reinterpret_cast<uintptr_t>(t.p) % 16) return SMAT_ERR_BAD_ALIGNMENT;
+    if (t.sb % 8 || t.sh % 8 || t.st % 8) return SMAT_ERR_BAD_ALIGNMENT;
+  } else {
+    if (reinterpret_cast<uintptr_t>(t.p) % 4) return SMAT_ERR_BAD_ALIGNMENT;
+  }
+  return SMAT_OK;
+}
+
+int check_layout_args(const int32_t* indptr, const int32_t* indices, const uint8_t* kind,
+                      int64_t nnzb, int max_row, int block) {
+  if (!indptr || !kind || (!indices && nnzb > 0)) return SMAT_ERR_NULL_POINTER;
+  if (nnzb < 0 || nnzb > (1LL << 31) - 1 || max_row < 0) return SMAT_ERR_CSR_INVALID;
+  return SMAT_OK;
+}
+
+// The tensor-core kernels keep a tile's merged chunk list in shared memory.
+int check_row_len(int dtype, int block, int max_row) {
+  if (dtype != SMAT_DTYPE_BF16) return SMAT_OK;
+  const int sub = 128 / block;
+  if (static_cast<int64_t>(max_row) * sub > FwdCfg<64, 64>::MAX_CHUNKS) return SMAT_ERR_ROW_TOO_LONG;
+  return SMAT_OK;
+}
+
+// ---------------------------------------------------------------- TMA
+PFN_cuTensorMapEncodeTiled_v12000 get_encode() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+  });
+  return fn;
+}
+
+// 4-D map over a [B, H, T, D] bf16 tensor, box {64, rows, 1, 1}, 128 B swizzle.
+int make_map(CUtensorMap* m, const TArg& t, int B, int H, int T, int D, int rows) {
+  auto enc = get_encode();
+  if (!enc) return SMAT_ERR_NO_DEVICE;
+  cuuint64_t dims[4] = {static_cast<cuuint64_t>(D), static_cast<cuuint64_t>(T),
+                        static_cast<cuuint64_t>(H), static_cast<cuuint64_t>(B)};
+  cuuint64_t strides[3] = {static_cast<cuuint64_t>(t.st) * 2, static_cast<cuuint64_t>(t.sh) * 2,
+                           static_cast<cuuint64_t>(t.sb) * 2};
+  // a size-1 dimension may carry any stride; give it a legal one
+  if (H == 1) strides[1] = std::max<cuuint64_t>(strides[1], 16);
+  if (B == 1) strides[2] = std::max<cuuint64_t>(strides[2], 16);
+  cuuint32_t box[4] = {64, static_cast<cuuint32_t>(rows), 1, 1};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(t.p), dims, strides,
+                   box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? SMAT_OK : SMAT_ERR_TMA_DESCRIPTOR;
+}
+
+template <typename K>
+int set_smem(K kernel, int bytes) {
+  return cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes) ==
+                 cudaSuccess
+             ? SMAT_OK
+             : SMAT_ERR_LAUNCH;
+}
+
+int launch_status() {
+  return cudaGetLastError() == cudaSuccess ? SMAT_OK : SMAT_ERR_LAUNCH;
+}
+
+// ---------------------------------------------------------------- forward
+template <int D, int BN>
+int fwd_tc(const TArg& q, const TArg& k, const TArg& v, const TArg& o, float* lse, int B, int H,
+           int T, const int32_t* indptr, const int32_t* indices, const uint8_t* kind,
+           int nblocks, int64_t nnzb, int block, float scale, int32_t* err, cudaStream_t s) {
+  using C = FwdCfg<D, BN>;
+  CUtensorMap mq, mk, mv;
+  int rc;
+  if ((rc = make_map(&mq, q, B, H, T, D, C::BM))) return rc;
+  if ((rc = make_map(&mk, k, B, H, T, D, BN))) return rc;
+  if ((rc = make_map(&mv, v, B, H, T, D, BN))) return rc;
+  FwdParams p{};
+  p.indptr = indptr;
+  p.indices = indices;
+  p.kind = kind;
+  p.o = static_cast<__nv_bfloat16*>(const_cast<void*>(o.p));
+  p.lse = lse;
+  p.o_sb = o.sb;
+  p.o_sh = o.sh;
+  p.o_st = o.st;
+  p.B = B;
+  p.H = H;
+  p.T = T;
+  p.nblocks = nblocks;
+  p.nnzb = static_cast<int>(nnzb);
+  p.bs = block;
+  p.n_tiles = (T + C::BM - 1) / C::BM;
+  p.scale_log2 = scale * 1.4426950408889634f;
+  p.err = err;
+  auto kern = smat_fwd_tc_kernel<D, BN>;
+  if ((rc = set_smem(kern, C::SMEM_BYTES))) return rc;
+  const int64_t grid = static_cast<int64_t>(p.n_tiles) * B * H;
+  kern<<<static_cast<unsigned>(grid), C::THREADS, C::SMEM_BYTES, s>>>(mq, mk, mv, p);
+  return launch_status();
+}
+
+SimtParams simt_params(int B, int H, int T, int block, float scale, const int32_t* indptr,
+                       const int32_t* indices, const uint8_t* kind, int nblocks, int64_t nnzb,
+                       int32_t* err) {
+  SimtParams p{};
+  p.B = B;
+  p.H = H;
+  p.T = T;
+  p.bs = block;
+  p.scale = scale;
+  p.indptr = indptr;
+  p.indices = indices;
+  p.kind = kind;
+  p.nblocks = nblocks;
+  p.nnzb = static_cast<int>(nnzb);
+  p.err = err;
+  return p;
+}
+
+void set3(int64_t* dst, const TArg& t) {
+  dst[0] = t.sb;
+  dst[1] = t.sh;
+  dst[2] = t.st;
+}
+
+template <template <int> class Launch>
+int dispatch_simt_d(int D, SimtParams& p, int T, int BH, cudaStream_t s) {
+  switch (D) {
+    case 32: return Launch<32>::run(p, T, BH, s);
+    case 64: return Launch<64>::run(p, T, BH, s);
+    case 128: return Launch<128>::run(p, T, BH, s);
+  }
+  return SMAT_ERR_UNSUPPORTED_D;
+}
+
+template <int D>
+struct FwdSimt {
+  static int run(SimtParams& p, int T, int BH, cudaStream_t s) {
+    constexpr int RPC = 128 / (D / 32);
+    dim3 grid((T + RPC - 1) / RPC, BH);
+    smat_fwd_simt_kernel<D><<<grid, 128, 0, s>>>(p);
+    return launch_status();
+  }
+};
+template <int D>
+struct DqSimt {
+  static int run(SimtParams& p, int T, int BH, cudaStream_t s) {
+    constexpr int RPC = 128 / (D / 32);
+    dim3 grid((T + RPC - 1) / RPC, BH);
+    smat_dq_simt_kernel<D><<<grid, 128, 0, s>>>(p);
+    return launch_status();
+  }
+};
+template <int D>
+struct DkdvSimt {
+  static int run(SimtParams& p, int T, int BH, cudaStream_t s) {
+    constexpr int RPC = 128 / (D / 32);
+    dim3 grid((T + RPC - 1) / RPC, BH);
+    smat_dkdv_simt_kernel<D><<<grid, 128, 0, s>>>(p);
+    return launch_status();
+  }
+};
+
+// ---------------------------------------------------------------- backward
+template <bool DKDV, int D>
+int bwd_tc(const TArg& r0, const TArg& r1, const TArg& c0, const TArg& c1, const float* lse,
+           const float* delta, const TArg& out0, const TArg* out1, int B, int H, int T,
+           const int32_t* indptr, const int32_t* indices, const uint8_t* kind, int nblocks,
+           int64_t nnzb, int block, float scale, int32_t* err, cudaStream_t s) {
+  using C = BwdCfg<D>;
+  CUtensorMap m0, m1, mc0, mc1;
+  int rc;
+  if ((rc = make_map(&m0, r0, B, H, T, D, C::BM))) return rc;
+  if ((rc = make_map(&m1, r1, B, H, T, D, C::BM))) return rc;
+  if ((rc = make_map(&mc0, c0, B, H, T, D, C::CN))) return rc;
+  if ((rc = make_map(&mc1, c1, B, H, T, D, C::CN))) return rc;
+  BwdParams p{};
+  p.indptr = indptr;
+  p.indices = indices;
+  p.kind = kind;
+  p.lse = lse;
+  p.delta = delta;
+  p.out0 = static_cast<__nv_bfloat16*>(const_cast<void*>(out0.p));
+  p.o0_sb = out0.sb;
+  p.o0_sh = out0.sh;
+  p.o0_st = out0.st;
+  if (out1) {
+    p.out1 = static_cast<__nv_bfloat16*>(const_cast<void*>(out1->p));
+    p.o1_sb = out1->sb;
+    p.o1_sh = out1->sh;
+    p.o1_st = out1->st;
+  }
+  p.B = B;
+  p.H = H;
+  p.T = T;
+  p.nblocks = nblocks;
+  p.nnzb = static_cast<int>(nnzb);
+  p.bs = block;
+  p.n_tiles = (T + C::BM - 1) / C::BM;
+  p.scale = scale;
+  p.scale_log2 = scale * 1.4426950408889634f;
+  p.err = err;
+  auto kern = smat_bwd_tc_kernel<DKDV, D>;
+  if ((rc = set_smem(kern, C::SMEM_BYTES))) return rc;
+  const int64_t grid = static_cast<int64_t>(p.n_tiles) * B * H;
+  kern<<<static_cast<unsigned>(grid), 192, C::SMEM_BYTES, s>>>(m0, m1, mc0, mc1, p);
+  return launch_status();
+}
+
+}  // namespace
+
+// ====================================================================== C ABI
+extern "C" {
+
+int smat_abi_version(void) { return 1; }
+
+const char* smat_status_string(int status) {
+  switch (status) {
+    case SMAT_OK: return "ok";
+    case SMAT_ERR_BAD_SHAPE: return "bad shape";
+    case SMAT_ERR_UNSUPPORTED_D: return "unsupported head dimension D";
+    case SMAT_ERR_UNSUPPORTED_BLOCK: return "unsupported block size";
+    case SMAT_ERR_UNSUPPORTED_DTYPE: return "unsupported dtype";
+    case SMAT_ERR_BAD_STRIDE: return "bad stride";
+    case SMAT_ERR_BAD_ALIGNMENT: return "bad alignment (bf16 needs 16-byte aligned rows)";
+    case SMAT_ERR_CSR_INVALID: return "invalid block CSR";
+    case SMAT_ERR_NULL_POINTER: return "null pointer";
+    case SMAT_ERR_LAUNCH: return "kernel launch failed";
+    case SMAT_ERR_NO_DEVICE: return "no supported device (sm_100 required)";
+    case SMAT_ERR_TMA_DESCRIPTOR: return "TMA descriptor rejected";
+    case SMAT_ERR_ROW_TOO_LONG: return "layout row longer than the kernels support";
+    case SMAT_ERR_CAPACITY: return "output capacity too small";
+  }
+  return "unknown status";
+}
+
+int smat_device_supported(int device) {
+  int major = 0, minor = 0;
+  if (cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, device) != cudaSuccess ||
+      cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, device) != cudaSuccess) {
+    cudaGetLastError();
+    return SMAT_ERR_NO_DEVICE;
+  }
+  return (major == 10 && minor == 0) ? SMAT_OK : SMAT_ERR_NO_DEVICE;
+}
+
+// ---------------------------------------------------------------- layouts
+int smat_layout_build_block(int T, int block, int window, int stride, int n_sink, int32_t* indptr,
+                            int32_t* indices, uint8_t* kind, int64_t capacity, int64_t* nnzb_out) {
+  if (T < 1 || block < 1 || window < 0 || stride < 0 || n_sink < 0) return SMAT_ERR_BAD_SHAPE;
+  if (!nnzb_out) return SMAT_ERR_NULL_POINTER;
+  const int nb = (T + block - 1) / block;
+  int64_t n = 0;
+  if (indptr) indptr[0] = 0;
+  for (int qb = 0; qb < nb; ++qb) {
+    const int lo = std::max(0, qb - window);
+    for (int kb = 0; kb <= qb; ++kb) {
+      const bool far = kb < n_sink || (stride > 0 && kb % stride == stride - 1);
+      if (kb < lo && !far) continue;
+      if (indices) {
+        if (n >= capacity || !kind) return SMAT_ERR_CAPACITY;
+        indices[n] = kb;
+        kind[n] = kb == qb ? SMAT_TILE_CAUSAL : SMAT_TILE_FULL;
+      }
+      ++n;
+    }
+    if (indptr) indptr[qb + 1] = static_cast<int32_t>(n);
+    if (n > (1LL << 31) - 1) return SMAT_ERR_CAPACITY;
+  }
+  *nnzb_out = n;
+  return SMAT_OK;
+}
+
+int smat_layout_transpose(int nblocks, const int32_t* indptr, const int32_t* indices,
+                          const uint8_t* kind, int32_t* t_indptr, int32_t* t_indices,
+                          uint8_t* t_kind) {
+  if (nblocks < 0) return SMAT_ERR_BAD_SHAPE;
+  if (!indptr || !t_indptr) return SMAT_ERR_NULL_POINTER;
+  const int64_t nnz = indptr[nblocks];
+  if (nnz > 0 && (!indices || !kind || !t_indices || !t_kind)) return SMAT_ERR_NULL_POINTER;
+  std::vector<int64_t> count(static_cast<size_t>(nblocks) + 1, 0);
+  for (int64_t e = 0; e < nnz; ++e) {
+    const int32_t c = indices[e];
+    if (c < 0 || c >= nblocks) return SMAT_ERR_CSR_INVALID;
+    ++count[c + 1];
+  }
+  for (int i = 0; i < nblocks; ++i) count[i + 1] += count[i];
+  for (int i = 0; i <= nblocks; ++i) t_indptr[i] = static_cast<int32_t>(count[i]);
+  // rows are visited in ascending order, so each column list comes out ascending
+  for (int r = 0; r < nblocks; ++r) {
+    if (indptr[r + 1] < indptr[r]) return SMAT_ERR_CSR_INVALID;
+    for (int64_t e = indptr[r]; e < indptr[r + 1]; ++e) {
+      const int64_t dst = count[indices[e]]++;
+      t_indices[dst] = r;
+      t_kind[dst] = kind[e];
+    }
+  }
+  return SMAT_OK;
+}
+
+int smat_layout_validate(int nblocks, int64_t nnzb, const int32_t* indptr, const int32_t* indices,
+                         const uint8_t* kind, int transposed, int32_t* max_row_out) {
+  if (nblocks < 0 || nnzb < 0) return SMAT_ERR_CSR_INVALID;
+  if (!indptr || (nnzb > 0 && (!indices || !kind))) return SMAT_ERR_NULL_POINTER;
+  if (indptr[0] != 0 || indptr[nblocks] != nnzb) return SMAT_ERR_CSR_INVALID;
+  int32_t longest = 0;
+  for (int r = 0; r < nblocks; ++r) {
+    const int64_t a = indptr[r], b = indptr[r + 1];
+    if (b < a || b > nnzb) return SMAT_ERR_CSR_INVALID;
+    longest = std::max<int32_t>(longest, static_cast<int32_t>(b - a));
+    int32_t prev = -1;
+    for (int64_t e = a; e < b; ++e) {
+      const int32_t c = indices[e];
+      if (c < 0 || c >= nblocks || c <= prev) return SMAT_ERR_CSR_INVALID;
+      if (transposed ? (c < r) : (c > r)) return SMAT_ERR_CSR_INVALID;
+      const uint8_t want = (c == r) ? SMAT_TILE_CAUSAL : SMAT_TILE_FULL;
+      if (kind[e] != want) return SMAT_ERR_CSR_INVALID;
+      prev = c;
+    }
+  }
+  if (max_row_out) *max_row_out = longest;
+  return SMAT_OK;
+}
+
+// ---------------------------------------------------------------- forward
+int smat_fwd(int dtype, const void* q, const int64_t* q_stride, const void* k,
+             const int64_t* k_stride, const void* v, const int64_t* v_stride, void* o,
+             const int64_t* o_stride, float* lse, int B, int H, int T, int D,
+             const int32_t* indptr, const int32_t* indices, const uint8_t* kind, int nblocks,
+             int64_t nnzb, int block, int max_row, float scale, int32_t* err_word,
+             void* stream) {
+  int rc;
+  if (!q_stride || !k_stride || !v_stride || !o_stride) return SMAT_ERR_NULL_POINTER;
+  if ((rc = check_common(dtype, B, H, T, D, nblocks, block))) return rc;
+  const TArg tq = targ(q, q_stride), tk = targ(k, k_stride), tv = targ(v, v_stride),
+             to = targ(o, o_stride);
+  for (const TArg* t : {&tq, &tk, &tv, &to})
+    if ((rc = check_tensor(*t, dtype))) return rc;
+  if (!lse) return SMAT_ERR_NULL_POINTER;
+  if ((rc = check_layout_args(indptr, indices, kind, nnzb, max_row, block))) return rc;
+  if ((rc = check_row_len(dtype, block, max_row))) return rc;
+  if (!std::isfinite(scale)) return SMAT_ERR_BAD_SHAPE;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (dtype == SMAT_DTYPE_BF16) {
+    if (D == 64 && block == 64)
+      return fwd_tc<64, 64>(tq, tk, tv, to, lse, B, H, T, indptr, indices, kind, nblocks, nnzb,
+                            block, scale, err_word, s);
+    if (D == 64 && block == 128)
+      return fwd_tc<64, 128>(tq, tk, tv, to, lse, B, H, T, indptr, indices, kind, nblocks, nnzb,
+                             block, scale, err_word, s);
+    if (D == 128 && block == 64)
+      return fwd_tc<128, 64>(tq, tk, tv, to, lse, B, H, T, indptr, indices, kind, nblocks, nnzb,
+                             block, scale, err_word, s);
+    return fwd_tc<128, 128>(tq, tk, tv, to, lse, B, H, T, indptr, indices, kind, nblocks, nnzb,
+                            block, scale, err_word, s);
+  }
+  SimtParams p = simt_params(B, H, T, block, scale, indptr, indices, kind, nblocks, nnzb, err_word);
+  p.q = static_cast<const float*>(q);
+  p.k = static_cast<const float*>(k);
+  p.v = static_cast<const float*>(v);
+  p.out0 = static_cast<float*>(o);
+  p.out1 = lse;
+  set3(p.q_s, tq);
+  set3(p.k_s, tk);
+  set3(p.v_s, tv);
+  set3(p.out0_s, to);
+  return dispatch_simt_d<FwdSimt>(D, p, T, B * H, s);
+}
+
+// ---------------------------------------------------------------- backward
+int smat_bwd_preprocess(int dtype, const void* o, const int64_t* o_stride, const void* dout,
+                        const int64_t* do_stride, float* delta, int B, int H, int T, int D,
+                        void* stream) {
+  int rc;
+  if (!o_stride || !do_stride) return SMAT_ERR_NULL_POINTER;
+  if ((rc = check_common(dtype, B, H, T, D, (T + 63) / 64, 64))) return rc;
+  const TArg to = targ(o, o_stride), td = targ(dout, do_stride);
+  for (const TArg* t : {&to, &td})
+    if ((rc = check_tensor(*t, dtype))) return rc;
+  if (!delta) return SMAT_ERR_NULL_POINTER;
+  if (dtype == SMAT_DTYPE_F32 && (to.sb % 4 || to.sh % 4 || to.st % 4 || td.sb % 4 || td.sh % 4 ||
+                                  td.st % 4 || reinterpret_cast<uintptr_t>(o) % 16 ||
+                                  reinterpret_cast<uintptr_t>(dout) % 16))
+    return SMAT_ERR_BAD_ALIGNMENT;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int64_t rows = static_cast<int64_t>(B) * H * T;
+  const int elem = dtype == SMAT_DTYPE_BF16 ? 2 : 4;
+  const int lpr = D * elem / 16;
+  const int64_t threads = rows * lpr;
+  const unsigned grid = static_cast<unsigned>((threads + 255) / 256);
+#define SMAT_PRE(TY, DD)                                                                        \
+  smat_bwd_pre_kernel<TY, DD><<<grid, 256, 0, s>>>(                                            \
+      static_cast<const TY*>(o), static_cast<const TY*>(dout), delta, to.sb, to.sh, to.st, td.sb, \
+      td.sh, td.st, H, T, rows)
+  if (dtype == SMAT_DTYPE_BF16) {
+    if (D == 64) SMAT_PRE(__nv_bfloat16, 64);
+    else SMAT_PRE(__nv_bfloat16, 128);
+  } else {
+    if (D == 32) SMAT_PRE(float, 32);
+    else if (D == 64) SMAT_PRE(float, 64);
+    else SMAT_PRE(float, 128);
+  }
+#undef SMAT_PRE
+  return launch_status();
+}
+
+int smat_bwd_dkdv(int dtype, const void* q, const int64_t* q_stride, const void* k,
+                  const int64_t* k_stride, const void* v, const int64_t* v_stride,
+                  const void* dout, const int64_t* do_stride, const float* lse,
+                  const float* delta, void* dk, const int64_t* dk_stride, void* dv,
+                  const int64_t* dv_stride, int B, int H, int T, int D, const int32_t* t_indptr,
+                  const int32_t* t_indices, const uint8_t* t_kind, int nblocks, int64_t nnzb,
+                  int block, int t_max_row, float scale, int32_t* err_word, void* stream) {
+  int rc;
+  if (!q_stride || !k_stride || !v_stride || !do_stride || !dk_stride || !dv_stride)
+    return SMAT_ERR_NULL_POINTER;
+  if ((rc = check_common(dtype, B, H, T, D, nblocks, block))) return rc;
+  const TArg tq = targ(q, q_stride), tk = targ(k, k_stride), tv = targ(v, v_stride),
+             td = targ(dout, do_stride), tdk = targ(dk, dk_stride), tdv = targ(dv, dv_stride);
+  for (const TArg* t : {&tq, &tk, &tv, &td, &tdk, &tdv})
+    if ((rc = check_tensor(*t, dtype))) return rc;
+  if (!lse || !delta) return SMAT_ERR_NULL_POINTER;
+  if ((rc = check_layout_args(t_indptr, t_indices, t_kind, nnzb, t_max_row, block))) return rc;
+  if ((rc = check_row_len(dtype, block, t_max_row))) return rc;
+  if (!std::isfinite(scale)) return SMAT_ERR_BAD_SHAPE;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (dtype == SMAT_DTYPE_BF16) {
+    if (D == 64)
+      return bwd_tc<true, 64>(tk, tv, tq, td, lse, delta, tdk, &tdv, B, H, T, t_indptr, t_indices,
+                              t_kind, nblocks, nnzb, block, scale, err_word, s);
+    return bwd_tc<true, 128>(tk, tv, tq, td, lse, delta, tdk, &tdv, B, H, T, t_indptr, t_indices,
+                             t_kind, nblocks, nnzb, block, scale, err_word, s);
+  }
+  SimtParams p =
+      simt_params(B, H, T, block, scale, t_indptr, t_indices, t_kind, nblocks, nnzb, err_word);
+  p.q = static_cast<const float*>(q);
+  p.k = static_cast<const float*>(k);
+  p.v = static_cast<const float*>(v);
+  p.dout = static_cast<const float*>(dout);
+  p.lse = lse;
+  p.delta = delta;
+  p.out0 = static_cast<float*>(dk);
+  p.out1 = static_cast<float*>(dv);
+  set3(p.q_s, tq);
+  set3(p.k_s, tk);
+  set3(p.v_s, tv);
+  set3(p.do_s, td);
+  set3(p.out0_s, tdk);
+  set3(p.out1_s, tdv);
+  return dispatch_simt_d<DkdvSimt>(D, p, T, B * H, s);
+}
+
+int smat_bwd_dq(int dtype, const void* q, const int64_t* q_stride, const void* k,
+                const int64_t* k_stride, const void* v, const int64_t* v_stride, const void* dout,
+                const int64_t* do_stride, const float* lse, const float* delta, void* dq,
+                const int64_t* dq_stride, int B, int H, int T, int D, const int32_t* indptr,
+                const int32_t* indices, const uint8_t* kind, int nblocks, int64_t nnzb,
+                int block, int max_row, float scale, int32_t* err_word, void* stream) {
+  int rc;
+  if (!q_stride || !k_stride || !v_stride || !do_stride || !dq_stride) return SMAT_ERR_NULL_POINTER;
+  if ((rc = check_common(dtype, B, H, T, D, nblocks, block))) return rc;
+  const TArg tq = targ(q, q_stride), tk = targ(k, k_stride), tv = targ(v, v_stride),
+             td = targ(dout, do_stride), tdq = targ(dq, dq_stride);
+  for (const TArg* t : {&tq, &tk, &tv, &td, &tdq})
+    if ((rc = check_tensor(*t, dtype))) return rc;
+  if (!lse || !delta) return SMAT_ERR_NULL_POINTER;
+  if ((rc = check_layout_args(indptr, indices, kind, nnzb, max_row, block))) return rc;
+  if ((rc = check_row_len(dtype, block, max_row))) return rc;
+  if (!std::isfinite(scale)) return SMAT_ERR_BAD_SHAPE;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (dtype == SMAT_DTYPE_BF16) {
+    if (D == 64)
+      return bwd_tc<false, 64>(tq, td, tk, tv, lse, delta, tdq, nullptr, B, H, T, indptr, indices,
+                               kind, nblocks, nnzb, block, scale, err_word, s);
+    return bwd_tc<false, 128>(tq, td, tk, tv, lse, delta, tdq, nullptr, B, H, T, indptr, indices,
+                              kind, nblocks, nnzb, block, scale, err_word, s);
+  }
+  SimtParams p = simt_params(B, H, T, block, scale, indptr, indices, kind, nblocks, nnzb, err_word);
+  p.q = static_cast<const float*>(q);
+  p.k = static_cast<const float*>(k);
+  p.v = static_cast<const float*>(v);
+  p.dout = static_cast<const float*>(dout);
+  p.lse = lse;
+  p.delta = delta;
+  p.out0 = static_cast<float*>(dq);
+  set3(p.q_s, tq);
+  set3(p.k_s, tk);
+  set3(p.v_s, tv);
+  set3(p.do_s, td);
+  set3(p.out0_s, tdq);
+  return dispatch_simt_d<DqSimt>(D, p, T, B * H, s);
+}
+
+int smat_bwd(int dtype, const void* q, const int64_t* q_stride, const void* k,
+             const int64_t* k_stride, const void* v, const int64_t* v_stride, const void* o,
+             const int64_t* o_stride, const void* dout, const int64_t* do_stride, const float* lse,
+             float* delta, void* dq, const int64_t* dq_stride, void* dk, const int64_t* dk_stride,
+             void* dv, const int64_t* dv_stride, int B, int H, int T, int D,
+             const int32_t* indptr, const int32_t* indices, const uint8_t* kind,
+             const int32_t* t_indptr, const int32_t* t_indices, const uint8_t* t_kind,
+             int nblocks, int64_t nnzb, int block, int max_row, int t_max_row, float scale,
+             int32_t* err_word, void* stream) {
+  int rc;
+  if ((rc = smat_bwd_preprocess(dtype, o, o_stride, dout, do_stride, delta, B, H, T, D, stream)))
+    return rc;
+  if ((rc = smat_bwd_dkdv(dtype, q, q_stride, k, k_stride, v, v_stride, dout, do_stride, lse,
+                          delta, dk, dk_stride, dv, dv_stride, B, H, T, D, t_indptr, t_indices,
+                          t_kind, nblocks, nnzb, block, t_max_row, scale, err_word, stream)))
+    return rc;
+  return smat_bwd_dq(dtype, q, q_stride, k, k_stride, v, v_stride, dout, do_stride, lse, delta,
+                     dq, dq_stride, B, H, T, D, indptr, indices, kind, nblocks, nnzb, block,
+                     max_row, scale, err_word, stream);
+}
+
+}  // extern "C"

@@ -1,0 +1,71 @@
+"""The C ABI without a GPU: the library loads, exports exactly what
+include/smat_b200.h declares, and rejects bad arguments on the host with the
+documented status codes before touching the device."""
+
+import ctypes
+import os
+import re
+
+import numpy as np
+import pytest
+
+from smat_attention_b200 import _lib
+
+HEADER = os.path.join(os.path.dirname(os.path.dirname(__file__)), "include", "smat_b200.h")
+
+
+def declared_symbols():
+    text = open(HEADER).read()
+    return sorted(set(re.findall(r"SMAT_API\s+(?:const\s+)?\w+\**\s+\**(smat_\w+)\s*\(", text)))
+
+
+def test_header_symbols_exported():
+    syms = declared_symbols()
+    assert len(syms) == 11
+    L = _lib.lib()
+    for s in syms:
+        assert hasattr(L, s), s
+    assert set(syms) == set(_lib.SIGNATURES)
+
+
+def test_version_and_status_strings():
+    L = _lib.lib()
+    assert L.smat_abi_version() == 1
+    assert L.smat_status_string(0) == b"ok"
+    assert b"CSR" in L.smat_status_string(7)
+    assert L.smat_status_string(999) == b"unknown status"
+
+
+def _fwd(**over):
+    L = _lib.lib()
+    st = (ctypes.c_int64 * 3)(4 * 1024 * 64, 1024 * 64, 64)
+    a = dict(dtype=1, q=16, k=16, v=16, o=16, lse=16, B=1, H=4, T=1024, D=64,
+             indptr=16, indices=16, kind=16, nblocks=16, nnzb=81, block=64, max_row=6,
+             scale=0.125)
+    a.update(over)
+    return L.smat_fwd(a["dtype"], a["q"], st, a["k"], st, a["v"], st, a["o"], st, a["lse"],
+                      a["B"], a["H"], a["T"], a["D"], a["indptr"], a["indices"], a["kind"],
+                      a["nblocks"], a["nnzb"], a["block"], a["max_row"], a["scale"], None, None)
+
+
+@pytest.mark.parametrize("over,code", [
+    (dict(B=0), 1), (dict(T=0), 1), (dict(nblocks=15), 1),
+    (dict(D=96), 2), (dict(dtype=0, D=48), 2),
+    (dict(block=32, nblocks=32), 3), (dict(dtype=7), 4),
+    (dict(q=8), 6), (dict(q=None), 8), (dict(lse=None), 8), (dict(indptr=None), 8),
+    (dict(max_row=300), 12), (dict(nnzb=-1), 7), (dict(scale=float("nan")), 1),
+])
+def test_fwd_rejects_on_host(over, code):
+    assert _fwd(**over) == code
+
+
+def test_bwd_rejects_on_host():
+    L = _lib.lib()
+    st = (ctypes.c_int64 * 3)(0, 0, 64)
+    bad = (ctypes.c_int64 * 3)(0, 0, 60)   # bf16 rows must be 16-byte aligned
+    args = [1, 16, st, 16, st, 16, st, 16, st, 16, 16, 16, st, 1, 1, 128, 64,
+            16, 16, 16, 2, 3, 64, 2, 0.125, None, None]
+    args_bad = list(args)
+    args_bad[12] = bad
+    assert L.smat_bwd_dq(*args_bad) == 6
+    assert L.smat_bwd_preprocess(1, 16, st, 16, st, None, 1, 1, 128, 64, None) == 8
