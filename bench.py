@@ -225,6 +225,39 @@ def run_reference(args):
 # GPU arm
 # ----------------------------------------------------------------------------
 
+def _e2e(host, shape, device, spec, scale, K, dist, stream):
+    """Same step through the public autograd API with pinned host buffers:
+    per step H2D of q, k, v, dO and D2H of o, dq, dk, dv inside the timed
+    region.  Returns (ms per step, bytes each way per step)."""
+    from smat_attention_b200.attention import smat_softmax_attention
+    pinned = [x.pin_memory() for x in host]
+    outs = [torch.empty(shape, dtype=torch.bfloat16).pin_memory() for _ in range(4)]
+    E = max(1, min(K, 3))
+
+    def e2e_step():
+        qd, kd, vd, dod = (x.to(device, non_blocking=True) for x in pinned)
+        qd.requires_grad_(True)
+        kd.requires_grad_(True)
+        vd.requires_grad_(True)
+        od, _ = smat_softmax_attention(qd, kd, vd, spec, scale)
+        od.backward(dod)
+        for dst, src in zip(outs, (od.detach(), qd.grad, kd.grad, vd.grad)):
+            dst.copy_(src, non_blocking=True)
+
+    e2e_step()
+    _barrier(dist, device)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(E):
+        e2e_step()
+    e1.record(stream)
+    torch.cuda.synchronize(device)
+    e2e_ms = _max_over_ranks(dist, e0.elapsed_time(e1) / E, device)
+    nbytes = sum(x.numel() * x.element_size() for x in host)
+
+    return e2e_ms, nbytes
+
+
 def run_gpu(args):
     from smat_attention_b200 import _lib
     from smat_attention_b200.attention import (bwd, check_device_errors, fwd,
@@ -311,31 +344,10 @@ def run_gpu(args):
     value = ws * fl["step"] / (ms_step * 1e-3) / 1e12
 
     # ---- end to end through the public API with host buffers ---------------
-    pinned = [x.pin_memory() for x in host]
-    outs = [torch.empty(shape, dtype=torch.bfloat16).pin_memory() for _ in range(4)]
-    E = max(1, min(K, 3))
-
-    def e2e_step():
-        qd, kd, vd, dod = (x.to(device, non_blocking=True) for x in pinned)
-        qd.requires_grad_(True)
-        kd.requires_grad_(True)
-        vd.requires_grad_(True)
-        od, _ = smat_softmax_attention(qd, kd, vd, spec, scale)
-        od.backward(dod)
-        for dst, src in zip(outs, (od.detach(), qd.grad, kd.grad, vd.grad)):
-            dst.copy_(src, non_blocking=True)
-
-    e2e_step()
-    _barrier(dist, device)
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record(stream)
-    for _ in range(E):
-        e2e_step()
-    e1.record(stream)
-    torch.cuda.synchronize(device)
-    e2e_ms = _max_over_ranks(dist, e0.elapsed_time(e1) / E, device)
+    e2e_ms, nbytes = None, 0
+    if not args.no_e2e:
+        e2e_ms, nbytes = _e2e(host, shape, device, spec, scale, K, dist, stream)
     dev_err |= check_device_errors(device)
-    nbytes = sum(x.numel() * x.element_size() for x in host)
 
     if rank == 0:
         peaks = _peaks()
@@ -361,9 +373,10 @@ def run_gpu(args):
                          "peak": peaks["tflops"], "unit": UNIT,
                          "frac": None if achieved is None else achieved / peaks["tflops"],
                          "traffic": traffic},
-            "e2e": {"value": ws * fl["step"] / (e2e_ms * 1e-3) / 1e12, "unit": UNIT,
-                    "ms_per_step": e2e_ms, "h2d_bytes_per_step": nbytes,
-                    "d2h_bytes_per_step": nbytes},
+            "e2e": None if e2e_ms is None else {
+                "value": ws * fl["step"] / (e2e_ms * 1e-3) / 1e12, "unit": UNIT,
+                "ms_per_step": e2e_ms, "h2d_bytes_per_step": nbytes,
+                "d2h_bytes_per_step": nbytes},
             "gpu_launches": K * len(kernels),
             "device_errors": dev_err,
             "clocks": clk,
@@ -382,7 +395,16 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true",
+                    help="skip the host-buffer end-to-end leg (profiling runs)")
+    ap.add_argument("--batch", type=int, default=None,
+                    help="override B (smaller cases for ncu captures)")
+    ap.add_argument("--heads", type=int, default=None, help="override H")
     args = ap.parse_args()
+    if args.batch:
+        WORKLOAD["B"] = args.batch
+    if args.heads:
+        WORKLOAD["H"] = args.heads
     if args.impl == "reference":
         run_reference(args)
     else:
