@@ -61,7 +61,8 @@ typedef enum smat_status {
   SMAT_ERR_NO_DEVICE = 10,
   SMAT_ERR_TMA_DESCRIPTOR = 11,
   SMAT_ERR_ROW_TOO_LONG = 12,
-  SMAT_ERR_CAPACITY = 13
+  SMAT_ERR_CAPACITY = 13,
+  SMAT_ERR_SCRATCH_LIMIT = 14
 } smat_status;
 
 enum { SMAT_DTYPE_F32 = 0, SMAT_DTYPE_BF16 = 1 };
@@ -189,6 +190,34 @@ SMAT_API int smat_bwd(int dtype,
              const int32_t* t_indptr, const int32_t* t_indices, const uint8_t* t_kind,
              int nblocks, int64_t nnzb, int block, int max_row, int t_max_row,
              float scale, int32_t* err_word, void* stream);
+
+/* smat_bwd_noalloc: smat_bwd for callers that cannot allocate device memory
+ * (their memory belongs to another allocator, or cudaMalloc's implicit
+ * synchronisation is not allowed on their path, or their budget is fixed at
+ * start-up).  Same arguments as smat_bwd minus the delta workspace: delta is
+ * kept in a fixed array compiled into the library, 16 MiB per GPU that loads
+ * it, held until the process exits.  B*H*T must be <= SMAT_NOALLOC_MAX_ROWS,
+ * else SMAT_ERR_SCRATCH_LIMIT before any launch.  All calls share the array:
+ * calls whose kernels overlap on the GPU race.  The first call on a device
+ * looks up the array's address with that device current; make it before any
+ * stream capture.  It has no counterpart in the reference. */
+#define SMAT_NOALLOC_MAX_ROWS (1 << 22)
+SMAT_API int smat_bwd_noalloc(int dtype,
+                              const void* q, const int64_t* q_stride,
+                              const void* k, const int64_t* k_stride,
+                              const void* v, const int64_t* v_stride,
+                              const void* o, const int64_t* o_stride,
+                              const void* dout, const int64_t* do_stride,
+                              const float* lse,
+                              void* dq, const int64_t* dq_stride,
+                              void* dk, const int64_t* dk_stride,
+                              void* dv, const int64_t* dv_stride,
+                              int B, int H, int T, int D,
+                              const int32_t* indptr, const int32_t* indices, const uint8_t* kind,
+                              const int32_t* t_indptr, const int32_t* t_indices,
+                              const uint8_t* t_kind,
+                              int nblocks, int64_t nnzb, int block, int max_row, int t_max_row,
+                              float scale, int32_t* err_word, void* stream);
 
 #ifdef __cplusplus
 }

@@ -47,6 +47,11 @@ SIGNATURES = {
                           _vp, _vp, _vp, _i64p, _vp, _i64p, _vp, _i64p,
                           _c_int, _c_int, _c_int, _c_int, _vp, _vp, _vp, _vp, _vp, _vp,
                           _c_int, _c_i64, _c_int, _c_int, _c_int, _c_f, _vp, _vp]),
+    # smat_bwd without the delta workspace (fixed in-library scratch)
+    "smat_bwd_noalloc": (_c_int, [_c_int, _vp, _i64p, _vp, _i64p, _vp, _i64p, _vp, _i64p, _vp,
+                                  _i64p, _vp, _vp, _i64p, _vp, _i64p, _vp, _i64p,
+                                  _c_int, _c_int, _c_int, _c_int, _vp, _vp, _vp, _vp, _vp, _vp,
+                                  _c_int, _c_i64, _c_int, _c_int, _c_int, _c_f, _vp, _vp]),
 }
 
 _lock = threading.Lock()

@@ -287,6 +287,8 @@ const char* smat_status_string(int status) {
     case SMAT_ERR_TMA_DESCRIPTOR: return "TMA descriptor rejected";
     case SMAT_ERR_ROW_TOO_LONG: return "layout row longer than the kernels support";
     case SMAT_ERR_CAPACITY: return "output capacity too small";
+    case SMAT_ERR_SCRATCH_LIMIT:
+      return "B*H*T exceeds the fixed scratch of smat_bwd_noalloc (SMAT_NOALLOC_MAX_ROWS)";
   }
   return "unknown status";
 }

@@ -21,7 +21,7 @@ def declared_symbols():
 
 def test_header_symbols_exported():
     syms = declared_symbols()
-    assert len(syms) == 11
+    assert len(syms) == 12
     L = _lib.lib()
     for s in syms:
         assert hasattr(L, s), s
