@@ -1,21 +1,25 @@
 // Block-sparse causal softmax attention, forward, bf16 on sm_100a tensor cores.
 //
-// One CTA computes one 128-row query tile of one (batch, head).  It walks the
-// tile's chunk list (the union of its CSR rows, see schedule.cuh) and for each
-// active key block of BN rows:
+// One CTA computes TWO adjacent 128-row query tiles of one (batch, head).
+// Their CSR rows overlap almost entirely (same sinks and summary blocks,
+// windows shifted by one block), so the CTA walks the union of the rows in
+// 64-key chunks, loads each K/V chunk once, and runs it against whichever of
+// the two tiles it is active for:
 //
-//   S   = Q K^T            tcgen05.mma, A = Q (smem), B = K (smem), D in TMEM
-//   P   = exp2(S*c - m)    softmax warps, online max with lazy rescale
-//   O  += P V              tcgen05.mma, A = P (smem), B = V (smem, MN-major)
+//   S_x  = Q_x K^T          tcgen05.mma, A = Q_x (smem), B = K (smem), D in TMEM
+//   P_x  = exp2(S_x c - m)  softmax warpgroup x, online max, lazy rescale
+//   O_x += P_x V            tcgen05.mma, A = P_x (smem), B = V (smem, MN-major)
 //
-// Warp roles (192 threads):
-//   warps 0-3  softmax + epilogue; thread r owns query row r = TMEM lane r
-//   warp 4     TMA producer (Q once, then K/V per chunk into a 2-stage ring)
-//   warp 5     TMEM allocator and MMA issuer (one elected lane)
-//
-// TMEM columns: S double buffer [0, 2 BN), O [2 BN, 2 BN + D).
-// Shared memory (all SWIZZLE_128B panels of 64 bf16 columns, 128 B rows):
-//   Q [128 x D], K/V ring [STAGES][BN x D] each, P [128 x BN].
+// While warpgroup 0 turns S_0 into P_0, the tensor core works on tile 1 and
+// the other way round.  Warp roles (320 threads):
+//   warps 0-3 / 4-7  softmax + epilogue of tile 0 / tile 1; thread r of a
+//                    warpgroup owns row r of its tile = TMEM lane r
+//   warp 8           TMA producer (both Q tiles once, then the K/V ring)
+//   warp 9           TMEM allocator and MMA issuer (one lane)
+// TMEM (512 columns): tile x owns [256 x, 256 x + 256): S double buffer at
+// +0 / +64, O at +128.  Shared memory (SWIZZLE_128B panels of 64 bf16
+// columns, 128-byte rows): Q [2][128 x D], K ring and V ring [STAGES][64 x D],
+// P [2][128 x 64].
 // Masked scores become -inf before the row max, so a key outside the mask
 // never enters the max or the sum.
 #pragma once
@@ -32,49 +36,73 @@ struct FwdParams {
   __nv_bfloat16* o;
   float* lse;
   int64_t o_sb, o_sh, o_st;  // element strides of O over (b, h, t); d stride is 1
-  int B, H, T, nblocks, nnzb, bs, n_tiles;
+  int B, H, T, nblocks, nnzb, bs, n_tiles, n_pairs;
   float scale_log2;          // softmax scale * log2(e)
   int32_t* err;
 };
 
-template <int D, int BN>
+template <int D>
 struct FwdCfg {
-  static constexpr int BM = 128;
-  static constexpr int STAGES = 2;
-  static constexpr int SUB = BM / BN;
+  static constexpr int BM = 128, NT = 2, BN = 64;
   static constexpr int Q_BYTES = BM * D * 2;
   static constexpr int KV_BYTES = BN * D * 2;
   static constexpr int P_BYTES = BM * BN * 2;
+  // as many K/V stages as the shared memory holds (at most 8): the ring hides
+  // the L2 -> shared latency of the loads
+  static constexpr int FIXED = NT * Q_BYTES + NT * P_BYTES + 1536;  // + barriers, alignment
+  static constexpr int STAGES_FIT = (227 * 1024 - FIXED) / (2 * KV_BYTES);
+  static constexpr int STAGES = STAGES_FIT > 8 ? 8 : STAGES_FIT;
   static constexpr int OFF_Q = 0;
-  static constexpr int OFF_K = OFF_Q + Q_BYTES;
+  static constexpr int OFF_K = OFF_Q + NT * Q_BYTES;
   static constexpr int OFF_V = OFF_K + STAGES * KV_BYTES;
   static constexpr int OFF_P = OFF_V + STAGES * KV_BYTES;
-  static constexpr int OFF_BAR = OFF_P + P_BYTES;
-  // barriers: q_full, kv_full[S], kv_empty[S], s_full[2], p_full, pv_done
+  static constexpr int OFF_BAR = OFF_P + NT * P_BYTES;
+  // barriers: q_full, kv_full[S], kv_empty[S], s_full[NT][2], p_full[NT], pv_done[NT], drain
   static constexpr int BAR_Q = 0, BAR_KVF = 1, BAR_KVE = 1 + STAGES, BAR_SF = 1 + 2 * STAGES,
-                       BAR_PF = 3 + 2 * STAGES, BAR_PV = 4 + 2 * STAGES,
-                       BAR_DRAIN = 5 + 2 * STAGES, NBAR = 6 + 2 * STAGES;
-  static constexpr int OFF_MISC = OFF_BAR + NBAR * 8;  // tmem ptr, abort flag, n_chunks
-  static constexpr int OFF_SCHED = OFF_MISC + 16;
-  static constexpr int MAX_CHUNKS = 512;
-  static constexpr int COL_S = 0, COL_O = 2 * BN;
-  static constexpr int TMEM_COLS = (2 * BN + D) <= 256 ? 256 : 512;
-  // + alignment slack; a CTA that takes all 512 TMEM columns also takes more
-  // than half the shared memory, so a second CTA never waits in tcgen05.alloc
-  static constexpr int SMEM_USED = OFF_SCHED + MAX_CHUNKS * 4 + 1024;
-  static constexpr int SMEM_BYTES =
-      (TMEM_COLS == 512 && SMEM_USED < 120 * 1024) ? 120 * 1024 : SMEM_USED;
-  static constexpr int THREADS = 192;
+                       BAR_PF = BAR_SF + 2 * NT, BAR_PV = BAR_PF + NT, BAR_DRAIN = BAR_PV + NT,
+                       NBAR = BAR_DRAIN + 1;
+  static constexpr int OFF_MISC = OFF_BAR + NBAR * 8;  // tmem ptr, abort flag
+  static constexpr int SMEM_BYTES = OFF_MISC + 16 + 1024;  // + alignment slack
+  static_assert(SMEM_BYTES <= 227 * 1024, "shared memory budget");
+  static_assert(STAGES >= 2, "at least two stages");
+  static constexpr int TMEM_COLS = 512, TILE_COLS = 256, COL_O = 128;
+  static constexpr int THREADS = 320;
   static constexpr uint32_t IDESC_S = idesc_bf16(BM, BN, false, false);
   static constexpr uint32_t IDESC_O = idesc_bf16(BM, D, false, true);
 };
 
-template <int D, int BN>
-__global__ void __launch_bounds__(192, 1)
+// Walks a merged CSR schedule in 64-row chunks (blocks of 128 rows give two
+// chunks each).
+template <int MAXROWS>
+struct ChunkIter {
+  MergeIter<MAXROWS> it;
+  uint32_t e;
+  int sub, cpb;
+  __device__ __forceinline__ void init(const int32_t* indptr, const int32_t* indices,
+                                       const uint8_t* kind, int nblocks, int nnzb, int row0,
+                                       int nrows, int cpb_, int32_t* err) {
+    it.init(indptr, indices, kind, nblocks, nnzb, row0, nrows, err);
+    cpb = cpb_;
+    sub = cpb_;
+    e = 0;
+  }
+  __device__ __forceinline__ bool next(uint32_t& entry, int& c, int32_t* err) {
+    if (sub >= cpb) {
+      if (!it.next(e, err)) return false;
+      sub = 0;
+    }
+    entry = e;
+    c = sub++;
+    return true;
+  }
+};
+
+template <int D>
+__global__ void __launch_bounds__(320, 1)
     smat_fwd_tc_kernel(const __grid_constant__ CUtensorMap tm_q,
                        const __grid_constant__ CUtensorMap tm_k,
                        const __grid_constant__ CUtensorMap tm_v, const FwdParams p) {
-  using C = FwdCfg<D, BN>;
+  using C = FwdCfg<D>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
@@ -83,14 +111,17 @@ __global__ void __launch_bounds__(192, 1)
   auto bar = [&](int i) { return bar0 + 8u * i; };
   uint32_t* misc = reinterpret_cast<uint32_t*>(smem + C::OFF_MISC);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(misc + 1);
-  uint32_t* sched = reinterpret_cast<uint32_t*>(smem + C::OFF_SCHED);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int BH = p.B * p.H;
   const int lin = blockIdx.x;
   const int bh = lin % BH;
-  const int tile = p.n_tiles - 1 - lin / BH;  // heaviest (latest) tiles first
+  const int pair = p.n_pairs - 1 - lin / BH;  // heaviest (latest) tiles first
+  const int tile0 = 2 * pair;
   const int b = bh / p.H, h = bh % p.H;
+  const int sub = C::BM / p.bs;   // CSR rows per tile: 1 (bs 128) or 2 (bs 64)
+  const int cpb = p.bs / C::BN;   // chunks per block: 2 (bs 128) or 1 (bs 64)
+  const int row0 = tile0 * sub;
 
   if (tid == 0) {
     mbar_init(bar(C::BAR_Q), 1);
@@ -98,21 +129,20 @@ __global__ void __launch_bounds__(192, 1)
       mbar_init(bar(C::BAR_KVF + s), 1);
       mbar_init(bar(C::BAR_KVE + s), 1);
     }
-    mbar_init(bar(C::BAR_SF + 0), 1);
-    mbar_init(bar(C::BAR_SF + 1), 1);
-    mbar_init(bar(C::BAR_PF), 4);
-    mbar_init(bar(C::BAR_PV), 1);
+    for (int i = 0; i < 2 * C::NT; ++i) mbar_init(bar(C::BAR_SF + i), 1);
+    for (int x = 0; x < C::NT; ++x) {
+      mbar_init(bar(C::BAR_PF + x), 4);
+      mbar_init(bar(C::BAR_PV + x), 1);
+    }
     mbar_init(bar(C::BAR_DRAIN), 1);
     fence_barrier_init();
     misc[1] = 0;
-    misc[2] = build_schedule(p.indptr, p.indices, p.kind, p.nblocks, p.nnzb, tile * C::SUB,
-                             C::SUB, sched, C::MAX_CHUNKS, p.err);
   }
-  if (warp == 5) {
+  if (warp == 9) {
     tmem_alloc(sbase + C::OFF_MISC, C::TMEM_COLS);
     tmem_relinquish();
   }
-  if (warp == 4 && lane == 0) {
+  if (warp == 8 && lane == 0) {
     prefetch_tmap(&tm_q);
     prefetch_tmap(&tm_k);
     prefetch_tmap(&tm_v);
@@ -121,82 +151,123 @@ __global__ void __launch_bounds__(192, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tbase = misc[0];
-  const int n = static_cast<int>(misc[2]);
 
-  if (warp == 4) {
+  if (warp == 8) {
     // ------------------------------------------------------------ producer
-    if (lane == 0 && n > 0) {
-      mbar_expect_tx(bar(C::BAR_Q), C::Q_BYTES);
+    if (lane == 0) {
+      ChunkIter<4> it;
+      it.init(p.indptr, p.indices, p.kind, p.nblocks, p.nnzb, row0, 2 * sub, cpb, p.err);
+      mbar_expect_tx(bar(C::BAR_Q), C::NT * C::Q_BYTES);
 #pragma unroll
-      for (int pn = 0; pn < D / 64; ++pn)
-        tma_load_4d(sbase + C::OFF_Q + pn * (C::BM * 128), &tm_q, bar(C::BAR_Q), pn * 64,
-                    tile * C::BM, h, b);
+      for (int x = 0; x < C::NT; ++x)
+#pragma unroll
+        for (int pn = 0; pn < D / 64; ++pn)
+          tma_load_4d(sbase + C::OFF_Q + x * C::Q_BYTES + pn * (C::BM * 128), &tm_q,
+                      bar(C::BAR_Q), pn * 64, (tile0 + x) * C::BM, h, b);
       int issued = 0;
-      for (int j = 0; j < n; ++j) {
+      uint32_t e;
+      int c;
+      for (int j = 0; it.next(e, c, p.err); ++j) {
         const int s = j % C::STAGES;
         if (j >= C::STAGES &&
             !mbar_wait(bar(C::BAR_KVE + s), ((j / C::STAGES) - 1) & 1, abort_flag, p.err))
           break;
-        const int kb = static_cast<int>(sched_block(sched[j]));
+        const int row = static_cast<int>(sched_block(e)) * p.bs + c * C::BN;
         mbar_expect_tx(bar(C::BAR_KVF + s), 2 * C::KV_BYTES);
 #pragma unroll
         for (int pn = 0; pn < D / 64; ++pn) {
-          tma_load_4d(sbase + C::OFF_K + s * C::KV_BYTES + pn * (BN * 128), &tm_k,
-                      bar(C::BAR_KVF + s), pn * 64, kb * p.bs, h, b);
-          tma_load_4d(sbase + C::OFF_V + s * C::KV_BYTES + pn * (BN * 128), &tm_v,
-                      bar(C::BAR_KVF + s), pn * 64, kb * p.bs, h, b);
+          tma_load_4d(sbase + C::OFF_K + s * C::KV_BYTES + pn * (C::BN * 128), &tm_k,
+                      bar(C::BAR_KVF + s), pn * 64, row, h, b);
+          tma_load_4d(sbase + C::OFF_V + s * C::KV_BYTES + pn * (C::BN * 128), &tm_v,
+                      bar(C::BAR_KVF + s), pn * 64, row, h, b);
         }
         issued = j + 1;
       }
-      // On abort, drain the loads still in flight before the CTA exits.
+      mbar_wait_drain(bar(C::BAR_Q), 0);  // Q is always loaded; never exit with it in flight
       if (*abort_flag) {
         for (int j = max(0, issued - C::STAGES); j < issued; ++j)
           mbar_wait_drain(bar(C::BAR_KVF + j % C::STAGES), (j / C::STAGES) & 1);
       }
     }
-  } else if (warp == 5) {
+  } else if (warp == 9) {
     // ------------------------------------------------------------ MMA issuer
-    if (lane == 0 && n > 0) {
-      const uint32_t tS = tbase + C::COL_S, tO = tbase + C::COL_O;
-      bool ok = mbar_wait(bar(C::BAR_Q), 0, abort_flag, p.err);
-      auto issue_s = [&](int j) {
+    if (lane == 0) {
+      ChunkIter<4> it;
+      it.init(p.indptr, p.indices, p.kind, p.nblocks, p.nnzb, row0, 2 * sub, cpb, p.err);
+      int cs[C::NT] = {0, 0}, cp[C::NT] = {0, 0};
+      auto active = [&](uint32_t e, int x) { return sched_states(e, x * sub, sub) != 0; };
+      auto issue_s = [&](int j, uint32_t e) {
         const int s = j % C::STAGES;
-        const uint32_t qa = sbase + C::OFF_Q, ka = sbase + C::OFF_K + s * C::KV_BYTES;
+        const uint32_t ka = sbase + C::OFF_K + s * C::KV_BYTES;
 #pragma unroll
-        for (int kk = 0; kk < D / 16; ++kk) {
-          const uint32_t off = (kk & 3) * 32u;
-          const uint64_t ad = sdesc_sw128(qa + (kk >> 2) * (C::BM * 128) + off, 16, 1024);
-          const uint64_t bd = sdesc_sw128(ka + (kk >> 2) * (BN * 128) + off, 16, 1024);
-          tc_mma(tS + (j & 1) * BN, ad, bd, C::IDESC_S, kk > 0 ? 1u : 0u);
+        for (int x = 0; x < C::NT; ++x) {
+          if (!active(e, x)) continue;
+          const uint32_t qa = sbase + C::OFF_Q + x * C::Q_BYTES;
+          const uint32_t dst = tbase + x * C::TILE_COLS + (cs[x] & 1) * C::BN;
+#pragma unroll
+          for (int kk = 0; kk < D / 16; ++kk) {
+            const uint32_t off = (kk & 3) * 32u;
+            tc_mma(dst, sdesc_sw128(qa + (kk >> 2) * (C::BM * 128) + off, 16, 1024),
+                   sdesc_sw128(ka + (kk >> 2) * (C::BN * 128) + off, 16, 1024), C::IDESC_S,
+                   kk > 0 ? 1u : 0u);
+          }
+          tc_commit(bar(C::BAR_SF + 2 * x + (cs[x] & 1)));
+          ++cs[x];
         }
-        tc_commit(bar(C::BAR_SF + (j & 1)));
       };
-      if (ok) ok = mbar_wait(bar(C::BAR_KVF + 0), 0, abort_flag, p.err);
-      if (ok) {
-        tc_fence_after();
-        issue_s(0);
+      bool ok = mbar_wait(bar(C::BAR_Q), 0, abort_flag, p.err);
+      uint32_t e_next = 0;
+      int c_next = 0;
+      bool has = ok && it.next(e_next, c_next, p.err);
+      if (has) {
+        ok = mbar_wait(bar(C::BAR_KVF + 0), 0, abort_flag, p.err);
+        if (ok) {
+          tc_fence_after();
+          issue_s(0, e_next);
+        }
       }
-      for (int j = 0; ok && j < n; ++j) {
-        if (j + 1 < n) {
+      for (int j = 0; ok && has; ++j) {
+        const uint32_t e = e_next;
+        has = it.next(e_next, c_next, p.err);
+        // S of the next chunk goes first if its K/V already landed; otherwise
+        // the PVs of this chunk are not held up behind that load
+        bool early = false;
+        if (has && mbar_try_wait(bar(C::BAR_KVF + (j + 1) % C::STAGES), ((j + 1) / C::STAGES) & 1)) {
+          tc_fence_after();
+          issue_s(j + 1, e_next);
+          early = true;
+        }
+        const int s = j % C::STAGES;
+        const uint32_t va = sbase + C::OFF_V + s * C::KV_BYTES;
+#pragma unroll
+        for (int x = 0; x < C::NT; ++x) {
+          if (!active(e, x)) continue;
+          if (!mbar_wait(bar(C::BAR_PF + x), cp[x] & 1, abort_flag, p.err)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t pa = sbase + C::OFF_P + x * C::P_BYTES;
+          const uint32_t dst = tbase + x * C::TILE_COLS + C::COL_O;
+#pragma unroll
+          for (int kk = 0; kk < C::BN / 16; ++kk) {
+            // V is MN-major: 64-column panels BN*128 bytes apart (LBO), 8-row
+            // groups 1024 bytes apart (SBO); 16 rows per k-step = 2048 bytes.
+            tc_mma(dst, sdesc_sw128(pa + kk * 32, 16, 1024),
+                   sdesc_sw128(va + kk * 2048, C::BN * 128, 1024), C::IDESC_O,
+                   (cp[x] > 0 || kk > 0) ? 1u : 0u);
+          }
+          tc_commit(bar(C::BAR_PV + x));
+          ++cp[x];
+        }
+        if (!ok) break;
+        tc_commit(bar(C::BAR_KVE + s));
+        if (has && !early) {
           const int s1 = (j + 1) % C::STAGES;
           if (!mbar_wait(bar(C::BAR_KVF + s1), ((j + 1) / C::STAGES) & 1, abort_flag, p.err)) break;
           tc_fence_after();
-          issue_s(j + 1);
+          issue_s(j + 1, e_next);
         }
-        if (!mbar_wait(bar(C::BAR_PF), j & 1, abort_flag, p.err)) break;
-        tc_fence_after();
-        const int s = j % C::STAGES;
-        const uint32_t pa = sbase + C::OFF_P, va = sbase + C::OFF_V + s * C::KV_BYTES;
-#pragma unroll
-        for (int kk = 0; kk < BN / 16; ++kk) {
-          const uint64_t ad = sdesc_sw128(pa + (kk >> 2) * (C::BM * 128) + (kk & 3) * 32, 16, 1024);
-          // V is MN-major: 64-column panels BN*128 bytes apart (LBO), 8-row
-          // groups 1024 bytes apart (SBO); 16 rows per k-step = 2048 bytes.
-          const uint64_t bd = sdesc_sw128(va + kk * 2048, BN * 128, 1024);
-          tc_mma(tO, ad, bd, C::IDESC_O, (j > 0 || kk > 0) ? 1u : 0u);
-        }
-        tc_commit(bar(C::BAR_PV));
-        tc_commit(bar(C::BAR_KVE + s));
       }
       if (*abort_flag) {  // let the MMAs in flight finish before TMEM is freed
         tc_commit(bar(C::BAR_DRAIN));
@@ -205,85 +276,106 @@ __global__ void __launch_bounds__(192, 1)
     }
   } else {
     // ------------------------------------------------------------ softmax
-    const int r = tid;                      // query row within the tile = TMEM lane
-    const int q_pos = tile * C::BM + r;
-    const int sub = (C::SUB == 2) ? (r >> 6) : 0;
-    const uint32_t lane_base = tbase + (static_cast<uint32_t>(warp * 32) << 16);
+    const int x = warp >> 2;                   // tile of this warpgroup
+    const int r = (warp & 3) * 32 + lane;      // row within the tile = TMEM lane
+    const int q_pos = (tile0 + x) * C::BM + r;
+    const int srow = x * sub + ((sub == 2) ? (r >> 6) : 0);   // CSR row of this query
+    const uint32_t lane_base =
+        tbase + (static_cast<uint32_t>((warp & 3) * 32) << 16) + x * C::TILE_COLS;
+    uint8_t* pbuf = smem + C::OFF_P + x * C::P_BYTES;
     float m = -INFINITY, l = 0.f;
-    uint8_t* pbuf = smem + C::OFF_P;
+    int cnt = 0;
     bool alive = true;
-    for (int j = 0; j < n && alive; ++j) {
-      const uint32_t e = sched[j];
-      const int k0 = static_cast<int>(sched_block(e)) * p.bs;
-      const uint32_t st = sched_state(e, sub);
-      if (!__all_sync(0xffffffffu,
-                      mbar_wait(bar(C::BAR_SF + (j & 1)), (j >> 1) & 1, abort_flag, p.err))) {
+    ChunkIter<4> it;
+    it.init(p.indptr, p.indices, p.kind, p.nblocks, p.nnzb, row0, 2 * sub, cpb, p.err);
+    uint32_t e;
+    int c;
+    while (alive && it.next(e, c, p.err)) {
+      if (sched_states(e, x * sub, sub) == 0) continue;
+      const uint32_t st = sched_state(e, srow);
+      const int k0 = static_cast<int>(sched_block(e)) * p.bs + c * C::BN;
+      if (!__all_sync(0xffffffffu, mbar_wait(bar(C::BAR_SF + 2 * x + (cnt & 1)), (cnt >> 1) & 1,
+                                             abort_flag, p.err))) {
         alive = false;
         break;
       }
       tc_fence_after();
-      float s[BN];
+      float s[C::BN];
+      tmem_ld64(lane_base + (cnt & 1) * C::BN, s);
+      if (st != ST_FULL) {   // uniform per warp: its 32 rows share one CSR row
 #pragma unroll
-      for (int c = 0; c < BN; c += 32) tmem_ld32(lane_base + C::COL_S + (j & 1) * BN + c, s + c);
-      float mx = -INFINITY;
-#pragma unroll
-      for (int c = 0; c < BN; ++c) {
-        const bool valid = (st == ST_FULL) || (st == ST_CAUSAL && k0 + c <= q_pos);
-        s[c] = valid ? s[c] * p.scale_log2 : -INFINITY;
-        mx = fmaxf(mx, s[c]);
+        for (int i = 0; i < C::BN; ++i)
+          if (!(st == ST_CAUSAL && k0 + i <= q_pos)) s[i] = -INFINITY;
       }
-      const float m_new = fmaxf(m, mx);
+      // row max of the raw scores (scale > 0), eight independent chains
+      float mx8[8];
+#pragma unroll
+      for (int a = 0; a < 8; ++a) mx8[a] = s[a];
+#pragma unroll
+      for (int i = 8; i < C::BN; ++i) mx8[i & 7] = fmaxf(mx8[i & 7], s[i]);
+#pragma unroll
+      for (int w = 4; w > 0; w >>= 1)
+#pragma unroll
+        for (int a = 0; a < w; ++a) mx8[a] = fmaxf(mx8[a], mx8[a + w]);
+      const float m_new = fmaxf(m, mx8[0] * p.scale_log2);
       const bool need = m_new > m + 8.0f;
-      // the P buffer and O are free once the previous chunk's PV has completed
-      if (j > 0 && !__all_sync(0xffffffffu,
-                               mbar_wait(bar(C::BAR_PV), (j - 1) & 1, abort_flag, p.err))) {
+      const bool rescale = __any_sync(0xffffffffu, need);
+      const float alpha = need ? ex2_approx(m - m_new) : 1.f;
+      if (need) {
+        l *= alpha;
+        m = m_new;
+      }
+      // exponentials first: they do not depend on the previous PV
+      const float neg_m = (m == -INFINITY) ? 0.f : -m;
+      float rs8[8];
+      uint32_t pw[C::BN / 2];
+#pragma unroll
+      for (int i = 0; i < C::BN / 2; ++i) {
+        const float a = ex2_approx(fmaf(s[2 * i], p.scale_log2, neg_m));
+        const float bb = ex2_approx(fmaf(s[2 * i + 1], p.scale_log2, neg_m));
+        if (i < 8) {
+          rs8[i] = a + bb;
+        } else {
+          rs8[i & 7] += a + bb;
+        }
+        pw[i] = pack_bf16(a, bb);
+      }
+#pragma unroll
+      for (int w = 4; w > 0; w >>= 1)
+#pragma unroll
+        for (int a = 0; a < w; ++a) rs8[a] += rs8[a + w];
+      l += rs8[0];
+      // the P buffer and O are free once this tile's previous PV has completed
+      if (cnt > 0 && !__all_sync(0xffffffffu, mbar_wait(bar(C::BAR_PV + x), (cnt - 1) & 1,
+                                                        abort_flag, p.err))) {
         alive = false;
         break;
       }
-      if (__any_sync(0xffffffffu, need)) {
-        const float alpha = need ? ex2_approx(m - m_new) : 1.f;
-        if (need) {
-          l *= alpha;
-          m = m_new;
-        }
-        if (j > 0) {
-          tc_fence_after();
+      if (rescale && cnt > 0) {
+        tc_fence_after();
 #pragma unroll
-          for (int c = 0; c < D; c += 32) {
-            float ov[32];
-            tmem_ld32(lane_base + C::COL_O + c, ov);
+        for (int cc = 0; cc < D; cc += 32) {
+          float ov[32];
+          tmem_ld32(lane_base + C::COL_O + cc, ov);
 #pragma unroll
-            for (int i = 0; i < 32; ++i) ov[i] *= alpha;
-            tmem_st32(lane_base + C::COL_O + c, ov);
-          }
-          tmem_st_wait();
+          for (int i = 0; i < 32; ++i) ov[i] *= alpha;
+          tmem_st32(lane_base + C::COL_O + cc, ov);
         }
+        tmem_st_wait();
       }
-      const float m_use = (m == -INFINITY) ? 0.f : m;
-      float rs = 0.f;
 #pragma unroll
-      for (int c16 = 0; c16 < BN / 8; ++c16) {
-        uint32_t w[4];
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const float a = ex2_approx(s[c16 * 8 + 2 * i] - m_use);
-          const float bb = ex2_approx(s[c16 * 8 + 2 * i + 1] - m_use);
-          rs += a + bb;
-          w[i] = pack_bf16(a, bb);
-        }
-        const int pn = c16 >> 3;
-        uint4* dst = reinterpret_cast<uint4*>(pbuf + pn * (C::BM * 128) + sw128_offset(r, c16 & 7));
-        *dst = make_uint4(w[0], w[1], w[2], w[3]);
-      }
-      l += rs;
+      for (int c16 = 0; c16 < C::BN / 8; ++c16)
+        *reinterpret_cast<uint4*>(pbuf + sw128_offset(r, c16)) =
+            make_uint4(pw[4 * c16], pw[4 * c16 + 1], pw[4 * c16 + 2], pw[4 * c16 + 3]);
       fence_proxy_async_smem();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(bar(C::BAR_PF));
+      if (lane == 0) mbar_arrive(bar(C::BAR_PF + x));
+      ++cnt;
     }
     // ------------------------------------------------------------ epilogue
-    if (alive && n > 0 &&
-        !__all_sync(0xffffffffu, mbar_wait(bar(C::BAR_PV), (n - 1) & 1, abort_flag, p.err)))
+    if (alive && cnt > 0 &&
+        !__all_sync(0xffffffffu, mbar_wait(bar(C::BAR_PV + x), (cnt - 1) & 1, abort_flag, p.err)))
       alive = false;
     if (alive) {
       tc_fence_after();
@@ -291,10 +383,10 @@ __global__ void __launch_bounds__(192, 1)
       __nv_bfloat16* orow = p.o + static_cast<int64_t>(b) * p.o_sb +
                             static_cast<int64_t>(h) * p.o_sh + static_cast<int64_t>(q_pos) * p.o_st;
 #pragma unroll
-      for (int c = 0; c < D; c += 32) {
+      for (int cc = 0; cc < D; cc += 32) {
         float ov[32];
-        if (n > 0) {
-          tmem_ld32(lane_base + C::COL_O + c, ov);
+        if (cnt > 0) {
+          tmem_ld32(lane_base + C::COL_O + cc, ov);
         } else {
 #pragma unroll
           for (int i = 0; i < 32; ++i) ov[i] = 0.f;
@@ -306,7 +398,7 @@ __global__ void __launch_bounds__(192, 1)
                                  pack_bf16(ov[i + 2] * inv, ov[i + 3] * inv),
                                  pack_bf16(ov[i + 4] * inv, ov[i + 5] * inv),
                                  pack_bf16(ov[i + 6] * inv, ov[i + 7] * inv));
-            *reinterpret_cast<uint4*>(orow + c + i) = w;
+            *reinterpret_cast<uint4*>(orow + cc + i) = w;
           }
         }
       }
@@ -318,7 +410,7 @@ __global__ void __launch_bounds__(192, 1)
 
   tc_fence_before();
   __syncthreads();
-  if (warp == 5) {
+  if (warp == 9) {
     __syncwarp();
     tc_fence_after();
     tmem_dealloc(tbase, C::TMEM_COLS);

@@ -1,8 +1,12 @@
-// Per-tile chunk schedule.  The tensor-core kernels work on 128-row tiles; a
-// tile covers SUB = 128 / bs consecutive blocks of the layout (SUB is 1 for
-// bs = 128 and 2 for bs = 64).  The tile's chunk list is the sorted union of
-// those SUB CSR rows, each entry carrying, per sub-block, whether the chunk is
-// absent, fully visible or causal for that sub-block's rows.
+// Chunk schedules of the tensor-core kernels.
+//
+// A CTA owns NROWS consecutive rows of a block CSR (query blocks for the
+// forward / dQ kernels, key blocks for dK/dV over the transposed CSR).  Its
+// chunk list is the sorted union of those rows; each entry carries, for every
+// owned row, whether the block is absent, fully visible or causal (diagonal)
+// for that row.  MergeIter produces the list one entry at a time straight
+// from the CSR in global memory, so rows of any length are supported; every
+// warp role runs its own iterator and all see the same sequence.
 #pragma once
 
 #include "common.cuh"
@@ -11,62 +15,94 @@ namespace smat {
 
 enum : uint32_t { ST_ABSENT = 0, ST_FULL = 1, ST_CAUSAL = 2 };
 
+// entry: bits 0..23 block index, bits 24 + 2 r .. 25 + 2 r the state of row r
 __device__ __forceinline__ uint32_t sched_block(uint32_t e) { return e & 0xFFFFFFu; }
-__device__ __forceinline__ uint32_t sched_state(uint32_t e, int sub) {
-  return (e >> (24 + 2 * sub)) & 3u;
+__device__ __forceinline__ uint32_t sched_state(uint32_t e, int r) {
+  return (e >> (24 + 2 * r)) & 3u;
+}
+// states of rows [r0, r0 + n) as one bit field (non-zero = any row active)
+__device__ __forceinline__ uint32_t sched_states(uint32_t e, int r0, int n) {
+  return (e >> (24 + 2 * r0)) & ((1u << (2 * n)) - 1u);
 }
 
-// Merge CSR rows [row0, row0 + sub) into `out` (capacity `cap`).  Invalid CSR
-// content (indptr out of range or decreasing, block index >= nblocks, rows not
-// ascending) sets DEV_ERR_BAD_CSR and yields an empty or truncated list.
-// Returns the number of entries.  Run by one thread.
-__device__ __forceinline__ int build_schedule(const int32_t* __restrict__ indptr,
-                                              const int32_t* __restrict__ indices,
-                                              const uint8_t* __restrict__ kind, int nblocks,
-                                              int nnzb, int row0, int sub, uint32_t* out, int cap,
-                                              int32_t* err) {
-  int lo[2] = {0, 0}, hi[2] = {0, 0};
-  int nrows = 0;
-  for (int s = 0; s < sub; ++s) {
-    const int r = row0 + s;
-    if (r >= nblocks) break;
-    const int a = indptr[r], b = indptr[r + 1];
-    if (a < 0 || b < a || b > nnzb) {
-      if (err) atomicOr(err, DEV_ERR_BAD_CSR);
-      return 0;
+template <int MAXROWS>
+struct MergeIter {
+  const int32_t* idx;
+  const uint8_t* kind;
+  int lo[MAXROWS], hi[MAXROWS];
+  int head[MAXROWS];     // block index at lo (prefetched), INT_MAX once a row is done
+  uint8_t hk[MAXROWS];   // its kind byte
+  int last;
+  int nb;
+  bool bad;
+
+  __device__ __forceinline__ void fetch(int s) {
+    if (lo[s] < hi[s]) {
+      head[s] = __ldg(idx + lo[s]);
+      hk[s] = __ldg(kind + lo[s]);
+    } else {
+      head[s] = 0x7FFFFFFF;
+      hk[s] = 0;
     }
-    lo[s] = a;
-    hi[s] = b;
-    nrows = s + 1;
   }
-  int n = 0;
-  int last = -1;
-  while (true) {
-    // smallest head among the rows
-    int best = 0x7FFFFFFF;
-    for (int s = 0; s < nrows; ++s)
-      if (lo[s] < hi[s]) best = min(best, indices[lo[s]]);
-    if (best == 0x7FFFFFFF) break;
-    if (best <= last || best < 0 || best >= nblocks) {
-      if (err) atomicOr(err, DEV_ERR_BAD_CSR);
-      break;
+
+  // Rows [row0, row0 + nrows) of the CSR; rows >= nblocks are empty.  Invalid
+  // CSR content sets DEV_ERR_BAD_CSR in *err and ends the sequence.
+  __device__ __forceinline__ void init(const int32_t* __restrict__ indptr,
+                                       const int32_t* __restrict__ indices,
+                                       const uint8_t* __restrict__ kinds, int nblocks, int nnzb,
+                                       int row0, int nrows, int32_t* err) {
+    idx = indices;
+    kind = kinds;
+    nb = nblocks;
+    last = -1;
+    bad = false;
+#pragma unroll
+    for (int s = 0; s < MAXROWS; ++s) {
+      lo[s] = hi[s] = 0;
+      const int r = row0 + s;
+      if (s < nrows && r < nblocks) {
+        const int a = indptr[r], b = indptr[r + 1];
+        if (a < 0 || b < a || b > nnzb) {
+          bad = true;
+        } else {
+          lo[s] = a;
+          hi[s] = b;
+        }
+      }
+      fetch(s);
     }
-    uint32_t e = static_cast<uint32_t>(best);
-    for (int s = 0; s < nrows; ++s) {
-      if (lo[s] < hi[s] && indices[lo[s]] == best) {
-        const uint32_t st = kind[lo[s]] == 1 ? ST_CAUSAL : ST_FULL;
-        e |= st << (24 + 2 * s);
+    if (bad && err) atomicOr(err, DEV_ERR_BAD_CSR);
+  }
+
+  // Next entry of the union; false at the end (or on invalid content).  The
+  // heads consumed here were loaded by the previous call, and the loads for
+  // the following call are issued before returning, so their latency hides
+  // behind the caller's work on this entry.
+  __device__ __forceinline__ bool next(uint32_t& e, int32_t* err) {
+    if (bad) return false;
+    int best = 0x7FFFFFFF;
+#pragma unroll
+    for (int s = 0; s < MAXROWS; ++s) best = min(best, head[s]);
+    if (best == 0x7FFFFFFF) return false;
+    if (best <= last || best < 0 || best >= nb || best > 0xFFFFFF) {
+      bad = true;
+      if (err) atomicOr(err, DEV_ERR_BAD_CSR);
+      return false;
+    }
+    uint32_t out = static_cast<uint32_t>(best);
+#pragma unroll
+    for (int s = 0; s < MAXROWS; ++s) {
+      if (head[s] == best) {
+        out |= (hk[s] == 1 ? ST_CAUSAL : ST_FULL) << (24 + 2 * s);
         ++lo[s];
+        fetch(s);
       }
     }
-    if (n >= cap) {
-      if (err) atomicOr(err, DEV_ERR_SCHED_OVERFLOW);
-      break;
-    }
-    out[n++] = e;
     last = best;
+    e = out;
+    return true;
   }
-  return n;
-}
+};
 
 }  // namespace smat

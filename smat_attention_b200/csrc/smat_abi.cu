@@ -66,14 +66,6 @@ int check_layout_args(const int32_t* indptr, const int32_t* indices, const uint8
   return SMAT_OK;
 }
 
-// The tensor-core kernels keep a tile's merged chunk list in shared memory.
-int check_row_len(int dtype, int block, int max_row) {
-  if (dtype != SMAT_DTYPE_BF16) return SMAT_OK;
-  const int sub = 128 / block;
-  if (static_cast<int64_t>(max_row) * sub > FwdCfg<64, 64>::MAX_CHUNKS) return SMAT_ERR_ROW_TOO_LONG;
-  return SMAT_OK;
-}
-
 // ---------------------------------------------------------------- TMA
 PFN_cuTensorMapEncodeTiled_v12000 get_encode() {
   static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
@@ -121,16 +113,16 @@ int launch_status() {
 }
 
 // ---------------------------------------------------------------- forward
-template <int D, int BN>
+template <int D>
 int fwd_tc(const TArg& q, const TArg& k, const TArg& v, const TArg& o, float* lse, int B, int H,
            int T, const int32_t* indptr, const int32_t* indices, const uint8_t* kind,
            int nblocks, int64_t nnzb, int block, float scale, int32_t* err, cudaStream_t s) {
-  using C = FwdCfg<D, BN>;
+  using C = FwdCfg<D>;
   CUtensorMap mq, mk, mv;
   int rc;
   if ((rc = make_map(&mq, q, B, H, T, D, C::BM))) return rc;
-  if ((rc = make_map(&mk, k, B, H, T, D, BN))) return rc;
-  if ((rc = make_map(&mv, v, B, H, T, D, BN))) return rc;
+  if ((rc = make_map(&mk, k, B, H, T, D, C::BN))) return rc;
+  if ((rc = make_map(&mv, v, B, H, T, D, C::BN))) return rc;
   FwdParams p{};
   p.indptr = indptr;
   p.indices = indices;
@@ -147,11 +139,12 @@ int fwd_tc(const TArg& q, const TArg& k, const TArg& v, const TArg& o, float* ls
   p.nnzb = static_cast<int>(nnzb);
   p.bs = block;
   p.n_tiles = (T + C::BM - 1) / C::BM;
+  p.n_pairs = (p.n_tiles + 1) / 2;
   p.scale_log2 = scale * 1.4426950408889634f;
   p.err = err;
-  auto kern = smat_fwd_tc_kernel<D, BN>;
+  auto kern = smat_fwd_tc_kernel<D>;
   if ((rc = set_smem(kern, C::SMEM_BYTES))) return rc;
-  const int64_t grid = static_cast<int64_t>(p.n_tiles) * B * H;
+  const int64_t grid = static_cast<int64_t>(p.n_pairs) * B * H;
   kern<<<static_cast<unsigned>(grid), C::THREADS, C::SMEM_BYTES, s>>>(mq, mk, mv, p);
   return launch_status();
 }
@@ -224,7 +217,7 @@ int bwd_tc(const TArg& r0, const TArg& r1, const TArg& c0, const TArg& c1, const
            const float* delta, const TArg& out0, const TArg* out1, int B, int H, int T,
            const int32_t* indptr, const int32_t* indices, const uint8_t* kind, int nblocks,
            int64_t nnzb, int block, float scale, int32_t* err, cudaStream_t s) {
-  using C = BwdCfg<D>;
+  using C = BwdCfg<DKDV, D>;
   CUtensorMap m0, m1, mc0, mc1;
   int rc;
   if ((rc = make_map(&m0, r0, B, H, T, D, C::BM))) return rc;
@@ -260,7 +253,7 @@ int bwd_tc(const TArg& r0, const TArg& r1, const TArg& c0, const TArg& c1, const
   auto kern = smat_bwd_tc_kernel<DKDV, D>;
   if ((rc = set_smem(kern, C::SMEM_BYTES))) return rc;
   const int64_t grid = static_cast<int64_t>(p.n_tiles) * B * H;
-  kern<<<static_cast<unsigned>(grid), 192, C::SMEM_BYTES, s>>>(m0, m1, mc0, mc1, p);
+  kern<<<static_cast<unsigned>(grid), C::THREADS, C::SMEM_BYTES, s>>>(m0, m1, mc0, mc1, p);
   return launch_status();
 }
 
@@ -397,21 +390,14 @@ int smat_fwd(int dtype, const void* q, const int64_t* q_stride, const void* k,
     if ((rc = check_tensor(*t, dtype))) return rc;
   if (!lse) return SMAT_ERR_NULL_POINTER;
   if ((rc = check_layout_args(indptr, indices, kind, nnzb, max_row, block))) return rc;
-  if ((rc = check_row_len(dtype, block, max_row))) return rc;
-  if (!std::isfinite(scale)) return SMAT_ERR_BAD_SHAPE;
+  if (!std::isfinite(scale) || scale <= 0.f) return SMAT_ERR_BAD_SHAPE;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (dtype == SMAT_DTYPE_BF16) {
-    if (D == 64 && block == 64)
-      return fwd_tc<64, 64>(tq, tk, tv, to, lse, B, H, T, indptr, indices, kind, nblocks, nnzb,
-                            block, scale, err_word, s);
-    if (D == 64 && block == 128)
-      return fwd_tc<64, 128>(tq, tk, tv, to, lse, B, H, T, indptr, indices, kind, nblocks, nnzb,
-                             block, scale, err_word, s);
-    if (D == 128 && block == 64)
-      return fwd_tc<128, 64>(tq, tk, tv, to, lse, B, H, T, indptr, indices, kind, nblocks, nnzb,
-                             block, scale, err_word, s);
-    return fwd_tc<128, 128>(tq, tk, tv, to, lse, B, H, T, indptr, indices, kind, nblocks, nnzb,
-                            block, scale, err_word, s);
+    if (D == 64)
+      return fwd_tc<64>(tq, tk, tv, to, lse, B, H, T, indptr, indices, kind, nblocks, nnzb, block,
+                        scale, err_word, s);
+    return fwd_tc<128>(tq, tk, tv, to, lse, B, H, T, indptr, indices, kind, nblocks, nnzb, block,
+                       scale, err_word, s);
   }
   SimtParams p = simt_params(B, H, T, block, scale, indptr, indices, kind, nblocks, nnzb, err_word);
   p.q = static_cast<const float*>(q);
@@ -480,8 +466,7 @@ int smat_bwd_dkdv(int dtype, const void* q, const int64_t* q_stride, const void*
     if ((rc = check_tensor(*t, dtype))) return rc;
   if (!lse || !delta) return SMAT_ERR_NULL_POINTER;
   if ((rc = check_layout_args(t_indptr, t_indices, t_kind, nnzb, t_max_row, block))) return rc;
-  if ((rc = check_row_len(dtype, block, t_max_row))) return rc;
-  if (!std::isfinite(scale)) return SMAT_ERR_BAD_SHAPE;
+  if (!std::isfinite(scale) || scale <= 0.f) return SMAT_ERR_BAD_SHAPE;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (dtype == SMAT_DTYPE_BF16) {
     if (D == 64)
@@ -524,8 +509,7 @@ int smat_bwd_dq(int dtype, const void* q, const int64_t* q_stride, const void* k
     if ((rc = check_tensor(*t, dtype))) return rc;
   if (!lse || !delta) return SMAT_ERR_NULL_POINTER;
   if ((rc = check_layout_args(indptr, indices, kind, nnzb, max_row, block))) return rc;
-  if ((rc = check_row_len(dtype, block, max_row))) return rc;
-  if (!std::isfinite(scale)) return SMAT_ERR_BAD_SHAPE;
+  if (!std::isfinite(scale) || scale <= 0.f) return SMAT_ERR_BAD_SHAPE;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (dtype == SMAT_DTYPE_BF16) {
     if (D == 64)

@@ -53,7 +53,7 @@ def _fwd(**over):
     (dict(D=96), 2), (dict(dtype=0, D=48), 2),
     (dict(block=32, nblocks=32), 3), (dict(dtype=7), 4),
     (dict(q=8), 6), (dict(q=None), 8), (dict(lse=None), 8), (dict(indptr=None), 8),
-    (dict(max_row=300), 12), (dict(nnzb=-1), 7), (dict(scale=float("nan")), 1),
+    (dict(nnzb=-1), 7), (dict(scale=float("nan")), 1),
 ])
 def test_fwd_rejects_on_host(over, code):
     assert _fwd(**over) == code
