@@ -15,9 +15,10 @@
 // Warp roles (320 threads): warps 0-7 compute -- warp w reads TMEM lanes
 // 32 (w % 4) .. +31 (its 32 tile rows) and chunk columns 32 (w / 4) .. +31;
 // warp 8 is the TMA producer; warp 9 allocates TMEM and issues the MMAs.
-// P^T / dS^T / dS go to shared memory in the SWIZZLE_128B K-major layout,
-// double-buffered, and feed the tensor core as the A operand while the
-// compute warps already work on the next chunk.
+// P^T / dS^T / dS (bf16) are written back into the TMEM columns of the S / dP
+// they came from (each warp over columns it has already read) and feed the
+// tensor core as the A operand straight from TMEM; the S/dP double buffer
+// lets the compute warps work on the next chunk meanwhile.
 #pragma once
 
 #include "common.cuh"
@@ -47,19 +48,16 @@ struct BwdCfg {
   static constexpr int CN = 64;      // chunk width (queries for dK/dV, keys for dQ)
   static constexpr int ROW_BYTES = BM * D * 2;   // one resident operand
   static constexpr int CH_BYTES = CN * D * 2;    // one streamed operand chunk
-  static constexpr int AB_BYTES = BM * CN * 2;   // one P^T / dS^T / dS tile
-  static constexpr int NA = DKDV ? 2 : 1;        // A operands per buffer
   static constexpr int LD_BYTES = DKDV ? 2 * CN * 4 : 0;   // lse + delta per stage
   // as many stages as the shared memory holds (at most 8)
-  static constexpr int FIXED = 2 * ROW_BYTES + 2 * NA * AB_BYTES + 1536;  // + barriers, alignment
+  static constexpr int FIXED = 2 * ROW_BYTES + 1536;  // + barriers, alignment
   static constexpr int STAGES_FIT = (227 * 1024 - FIXED) / (2 * CH_BYTES + LD_BYTES);
   static constexpr int STAGES = STAGES_FIT > 8 ? 8 : STAGES_FIT;
   static constexpr int OFF_R0 = 0;                              // K (dK/dV) or Q (dQ)
   static constexpr int OFF_R1 = OFF_R0 + ROW_BYTES;             // V (dK/dV) or dO (dQ)
   static constexpr int OFF_C0 = OFF_R1 + ROW_BYTES;             // Q_c (dK/dV) or K_c (dQ)
   static constexpr int OFF_C1 = OFF_C0 + STAGES * CH_BYTES;     // dO_c (dK/dV) or V_c (dQ)
-  static constexpr int OFF_A = OFF_C1 + STAGES * CH_BYTES;      // [2 buffers][NA operands]
-  static constexpr int OFF_LD = OFF_A + 2 * NA * AB_BYTES;      // per stage: lse [CN], delta [CN]
+  static constexpr int OFF_LD = OFF_C1 + STAGES * CH_BYTES;     // per stage: lse [CN], delta [CN]
   static constexpr int OFF_BAR = OFF_LD + STAGES * LD_BYTES;
   // barriers: r_full, c_full[S], c_empty[S], s_full[2], a_full[2], a_done[2], drain
   static constexpr int BAR_R = 0, BAR_CF = 1, BAR_CE = 1 + STAGES, BAR_SF = 1 + 2 * STAGES,
@@ -251,23 +249,26 @@ __global__ void __launch_bounds__(320, 1)
         const int s = j % C::STAGES;
         const uint32_t c0 = sbase + C::OFF_C0 + s * C::CH_BYTES;
         const uint32_t c1 = sbase + C::OFF_C1 + s * C::CH_BYTES;
-        const uint32_t a0 = sbase + C::OFF_A + (j & 1) * C::NA * C::AB_BYTES;
-        const uint32_t a1 = a0 + C::AB_BYTES;
+        const uint32_t tb = tbase + (j & 1) * C::BUF_COLS;
         const uint32_t acc = (j > 0) ? 1u : 0u;
 #pragma unroll
         for (int kk = 0; kk < C::CN / 16; ++kk) {
-          const uint64_t ad0 = sdesc_sw128(a0 + kk * 32, 16, 1024);
+          // A in TMEM: the 16 chunk columns of k-step kk are 8 packed columns
+          // inside the 32-column half written by warps of half kk / 2
+          const uint32_t aoff = (kk >> 1) * 32 + (kk & 1) * 8;
           if (DKDV) {
             // dV += P^T dO_c ; dK += dS^T Q_c   (B operands MN-major)
-            const uint64_t ad1 = sdesc_sw128(a1 + kk * 32, 16, 1024);
-            tc_mma(tbase + C::COL_ACC1, ad0, sdesc_sw128(c1 + kk * 2048, C::CN * 128, 1024),
-                   C::IDESC_ACC, (acc || kk > 0) ? 1u : 0u);
-            tc_mma(tbase + C::COL_ACC0, ad1, sdesc_sw128(c0 + kk * 2048, C::CN * 128, 1024),
-                   C::IDESC_ACC, (acc || kk > 0) ? 1u : 0u);
+            tc_mma_ts(tbase + C::COL_ACC1, tb + C::COL_S + aoff,
+                      sdesc_sw128(c1 + kk * 2048, C::CN * 128, 1024), C::IDESC_ACC,
+                      (acc || kk > 0) ? 1u : 0u);
+            tc_mma_ts(tbase + C::COL_ACC0, tb + C::COL_DP + aoff,
+                      sdesc_sw128(c0 + kk * 2048, C::CN * 128, 1024), C::IDESC_ACC,
+                      (acc || kk > 0) ? 1u : 0u);
           } else {
             // dQ += dS K_c
-            tc_mma(tbase + C::COL_ACC0, ad0, sdesc_sw128(c0 + kk * 2048, C::CN * 128, 1024),
-                   C::IDESC_ACC, (acc || kk > 0) ? 1u : 0u);
+            tc_mma_ts(tbase + C::COL_ACC0, tb + C::COL_DP + aoff,
+                      sdesc_sw128(c0 + kk * 2048, C::CN * 128, 1024), C::IDESC_ACC,
+                      (acc || kk > 0) ? 1u : 0u);
           }
         }
         tc_commit(bar(C::BAR_AD + (j & 1)));
@@ -374,28 +375,10 @@ __global__ void __launch_bounds__(320, 1)
         wd[i] = pack_bf16(pv[2 * i] * (dp[2 * i] - dl[2 * i]),
                           pv[2 * i + 1] * (dp[2 * i + 1] - dl[2 * i + 1]));
       }
-      // the A buffer (j & 1) is free once chunk j-2's MMAs have completed
-      if (j >= 2 && !__all_sync(0xffffffffu, mbar_wait(bar(C::BAR_AD + (j & 1)),
-                                                       ((j >> 1) - 1) & 1, abort_flag, p.err))) {
-        alive = false;
-        break;
-      }
-      uint8_t* a0 = smem + C::OFF_A + (j & 1) * C::NA * C::AB_BYTES;
-      uint8_t* a1 = a0 + C::AB_BYTES;
-#pragma unroll
-      for (int q16 = 0; q16 < 4; ++q16) {
-        const uint32_t off = sw128_offset(r, half * 4 + q16);
-        if (DKDV) {
-          *reinterpret_cast<uint4*>(a0 + off) =
-              make_uint4(wp[4 * q16], wp[4 * q16 + 1], wp[4 * q16 + 2], wp[4 * q16 + 3]);
-          *reinterpret_cast<uint4*>(a1 + off) =
-              make_uint4(wd[4 * q16], wd[4 * q16 + 1], wd[4 * q16 + 2], wd[4 * q16 + 3]);
-        } else {
-          *reinterpret_cast<uint4*>(a0 + off) =
-              make_uint4(wd[4 * q16], wd[4 * q16 + 1], wd[4 * q16 + 2], wd[4 * q16 + 3]);
-        }
-      }
-      fence_proxy_async_smem();
+      // P^T / dS^T / dS over the S / dP columns this warp has already read
+      if (DKDV) tmem_st16u(tb + C::COL_S + col0, wp);
+      tmem_st16u(tb + C::COL_DP + col0, wd);
+      tmem_st_wait();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(bar(C::BAR_AF + (j & 1)));

@@ -7,8 +7,9 @@
 // the two tiles it is active for:
 //
 //   S_x  = Q_x K^T          tcgen05.mma, A = Q_x (smem), B = K (smem), D in TMEM
-//   P_x  = exp2(S_x c - m)  softmax warpgroup x, online max, lazy rescale
-//   O_x += P_x V            tcgen05.mma, A = P_x (smem), B = V (smem, MN-major)
+//   P_x  = exp2(S_x c - m)  softmax warpgroup x, online max, lazy rescale;
+//                           P (bf16) is written back over S_x in TMEM
+//   O_x += P_x V            tcgen05.mma, A = P_x (TMEM), B = V (smem, MN-major)
 //
 // While warpgroup 0 turns S_0 into P_0, the tensor core works on tile 1 and
 // the other way round.  Warp roles (320 threads):
@@ -16,10 +17,10 @@
 //                    warpgroup owns row r of its tile = TMEM lane r
 //   warp 8           TMA producer (both Q tiles once, then the K/V ring)
 //   warp 9           TMEM allocator and MMA issuer (one lane)
-// TMEM (512 columns): tile x owns [256 x, 256 x + 256): S double buffer at
-// +0 / +64, O at +128.  Shared memory (SWIZZLE_128B panels of 64 bf16
-// columns, 128-byte rows): Q [2][128 x D], K ring and V ring [STAGES][64 x D],
-// P [2][128 x 64].
+// TMEM (512 columns): tile x owns [256 x, 256 x + 256): S / P double buffer
+// at +0 / +64 (P packs two bf16 per column into the first 32), O at +128.
+// Shared memory (SWIZZLE_128B panels of 64 bf16 columns, 128-byte rows):
+// Q [2][128 x D], K ring and V ring [STAGES][64 x D].
 // Masked scores become -inf before the row max, so a key outside the mask
 // never enters the max or the sum.
 #pragma once
@@ -46,20 +47,18 @@ struct FwdCfg {
   static constexpr int BM = 128, NT = 2, BN = 64;
   static constexpr int Q_BYTES = BM * D * 2;
   static constexpr int KV_BYTES = BN * D * 2;
-  static constexpr int P_BYTES = BM * BN * 2;
   // as many K/V stages as the shared memory holds (at most 8): the ring hides
   // the L2 -> shared latency of the loads
-  static constexpr int FIXED = NT * Q_BYTES + NT * P_BYTES + 1536;  // + barriers, alignment
+  static constexpr int FIXED = NT * Q_BYTES + 1536;  // + barriers, alignment
   static constexpr int STAGES_FIT = (227 * 1024 - FIXED) / (2 * KV_BYTES);
   static constexpr int STAGES = STAGES_FIT > 8 ? 8 : STAGES_FIT;
   static constexpr int OFF_Q = 0;
   static constexpr int OFF_K = OFF_Q + NT * Q_BYTES;
   static constexpr int OFF_V = OFF_K + STAGES * KV_BYTES;
-  static constexpr int OFF_P = OFF_V + STAGES * KV_BYTES;
-  static constexpr int OFF_BAR = OFF_P + NT * P_BYTES;
-  // barriers: q_full, kv_full[S], kv_empty[S], s_full[NT][2], p_full[NT], pv_done[NT], drain
+  static constexpr int OFF_BAR = OFF_V + STAGES * KV_BYTES;
+  // barriers: q_full, kv_full[S], kv_empty[S], s_full[NT][2], p_full[NT][2], pv_done[NT], drain
   static constexpr int BAR_Q = 0, BAR_KVF = 1, BAR_KVE = 1 + STAGES, BAR_SF = 1 + 2 * STAGES,
-                       BAR_PF = BAR_SF + 2 * NT, BAR_PV = BAR_PF + NT, BAR_DRAIN = BAR_PV + NT,
+                       BAR_PF = BAR_SF + 2 * NT, BAR_PV = BAR_PF + 2 * NT, BAR_DRAIN = BAR_PV + NT,
                        NBAR = BAR_DRAIN + 1;
   static constexpr int OFF_MISC = OFF_BAR + NBAR * 8;  // tmem ptr, abort flag
   static constexpr int SMEM_BYTES = OFF_MISC + 16 + 1024;  // + alignment slack
@@ -129,11 +128,11 @@ __global__ void __launch_bounds__(320, 1)
       mbar_init(bar(C::BAR_KVF + s), 1);
       mbar_init(bar(C::BAR_KVE + s), 1);
     }
-    for (int i = 0; i < 2 * C::NT; ++i) mbar_init(bar(C::BAR_SF + i), 1);
-    for (int x = 0; x < C::NT; ++x) {
-      mbar_init(bar(C::BAR_PF + x), 4);
-      mbar_init(bar(C::BAR_PV + x), 1);
+    for (int i = 0; i < 2 * C::NT; ++i) {
+      mbar_init(bar(C::BAR_SF + i), 1);
+      mbar_init(bar(C::BAR_PF + i), 4);
     }
+    for (int x = 0; x < C::NT; ++x) mbar_init(bar(C::BAR_PV + x), 1);
     mbar_init(bar(C::BAR_DRAIN), 1);
     fence_barrier_init();
     misc[1] = 0;
@@ -242,20 +241,21 @@ __global__ void __launch_bounds__(320, 1)
 #pragma unroll
         for (int x = 0; x < C::NT; ++x) {
           if (!active(e, x)) continue;
-          if (!mbar_wait(bar(C::BAR_PF + x), cp[x] & 1, abort_flag, p.err)) {
+          if (!mbar_wait(bar(C::BAR_PF + 2 * x + (cp[x] & 1)), (cp[x] >> 1) & 1, abort_flag,
+                         p.err)) {
             ok = false;
             break;
           }
           tc_fence_after();
-          const uint32_t pa = sbase + C::OFF_P + x * C::P_BYTES;
+          const uint32_t pa = tbase + x * C::TILE_COLS + (cp[x] & 1) * C::BN;   // P in TMEM
           const uint32_t dst = tbase + x * C::TILE_COLS + C::COL_O;
 #pragma unroll
           for (int kk = 0; kk < C::BN / 16; ++kk) {
-            // V is MN-major: 64-column panels BN*128 bytes apart (LBO), 8-row
-            // groups 1024 bytes apart (SBO); 16 rows per k-step = 2048 bytes.
-            tc_mma(dst, sdesc_sw128(pa + kk * 32, 16, 1024),
-                   sdesc_sw128(va + kk * 2048, C::BN * 128, 1024), C::IDESC_O,
-                   (cp[x] > 0 || kk > 0) ? 1u : 0u);
+            // A: 16 keys = 8 packed columns per k-step.  V is MN-major:
+            // 64-column panels BN*128 bytes apart (LBO), 8-row groups 1024
+            // bytes apart (SBO); 16 rows per k-step = 2048 bytes.
+            tc_mma_ts(dst, pa + kk * 8, sdesc_sw128(va + kk * 2048, C::BN * 128, 1024),
+                      C::IDESC_O, (cp[x] > 0 || kk > 0) ? 1u : 0u);
           }
           tc_commit(bar(C::BAR_PV + x));
           ++cp[x];
@@ -282,7 +282,6 @@ __global__ void __launch_bounds__(320, 1)
     const int srow = x * sub + ((sub == 2) ? (r >> 6) : 0);   // CSR row of this query
     const uint32_t lane_base =
         tbase + (static_cast<uint32_t>((warp & 3) * 32) << 16) + x * C::TILE_COLS;
-    uint8_t* pbuf = smem + C::OFF_P + x * C::P_BYTES;
     float m = -INFINITY, l = 0.f;
     int cnt = 0;
     bool alive = true;
@@ -345,13 +344,13 @@ __global__ void __launch_bounds__(320, 1)
 #pragma unroll
         for (int a = 0; a < w; ++a) rs8[a] += rs8[a + w];
       l += rs8[0];
-      // the P buffer and O are free once this tile's previous PV has completed
-      if (cnt > 0 && !__all_sync(0xffffffffu, mbar_wait(bar(C::BAR_PV + x), (cnt - 1) & 1,
-                                                        abort_flag, p.err))) {
-        alive = false;
-        break;
-      }
+      // O may be rescaled only once this tile's previous PV has completed
       if (rescale && cnt > 0) {
+        if (!__all_sync(0xffffffffu, mbar_wait(bar(C::BAR_PV + x), (cnt - 1) & 1, abort_flag,
+                                               p.err))) {
+          alive = false;
+          break;
+        }
         tc_fence_after();
 #pragma unroll
         for (int cc = 0; cc < D; cc += 32) {
@@ -363,14 +362,12 @@ __global__ void __launch_bounds__(320, 1)
         }
         tmem_st_wait();
       }
-#pragma unroll
-      for (int c16 = 0; c16 < C::BN / 8; ++c16)
-        *reinterpret_cast<uint4*>(pbuf + sw128_offset(r, c16)) =
-            make_uint4(pw[4 * c16], pw[4 * c16 + 1], pw[4 * c16 + 2], pw[4 * c16 + 3]);
-      fence_proxy_async_smem();
+      // P over the S columns this thread has already read
+      tmem_st32u(lane_base + (cnt & 1) * C::BN, pw);
+      tmem_st_wait();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(bar(C::BAR_PF + x));
+      if (lane == 0) mbar_arrive(bar(C::BAR_PF + 2 * x + (cnt & 1)));
       ++cnt;
     }
     // ------------------------------------------------------------ epilogue
