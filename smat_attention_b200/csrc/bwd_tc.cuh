@@ -62,7 +62,7 @@ struct BwdCfg {
   // barriers: r_full, c_full[S], c_empty[S], s_full[2], a_full[2], a_done[2], drain
   static constexpr int BAR_R = 0, BAR_CF = 1, BAR_CE = 1 + STAGES, BAR_SF = 1 + 2 * STAGES,
                        BAR_AF = BAR_SF + 2, BAR_AD = BAR_AF + 2, BAR_DRAIN = BAR_AD + 2,
-                       NBAR = BAR_DRAIN + 1;
+                       BAR_RT = BAR_DRAIN + 1, NBAR = BAR_RT + 1;
   static constexpr int OFF_MISC = OFF_BAR + NBAR * 8;
   static constexpr int SMEM_BYTES = OFF_MISC + 16 + 1024;
   static_assert(SMEM_BYTES <= 227 * 1024, "shared memory budget");
@@ -70,14 +70,22 @@ struct BwdCfg {
   // TMEM: [S 64 | dP 64] x 2 buffers, then the accumulators
   static constexpr int COL_S = 0, COL_DP = CN, BUF_COLS = 2 * CN, COL_ACC0 = 2 * BUF_COLS,
                        COL_ACC1 = COL_ACC0 + D;
+  // dQ: the resident Q and dO also go to TMEM (bf16 pairs per column), so S
+  // and dP read only the streamed chunk from shared memory
+  static constexpr bool RES_TMEM = !DKDV;
+  static constexpr int COL_RT0 = COL_ACC0 + D, COL_RT1 = COL_RT0 + D / 2;
+  static_assert(!RES_TMEM || COL_RT1 + D / 2 <= 512, "TMEM budget");
   static constexpr int TMEM_COLS = 512;
-  static constexpr int THREADS = 320, NCW = 8;   // compute warps
+  // compute warps: NCW / 4 groups of 4; group g owns chunk columns
+  // [g CW, (g + 1) CW) of all 128 tile rows
+  static constexpr int NCW = 16, CW = CN * 4 / NCW;
+  static constexpr int PRODUCER_WARP = NCW, MMA_WARP = NCW + 1, THREADS = (NCW + 2) * 32;
   static constexpr uint32_t IDESC_SC = idesc_bf16(BM, CN, false, false);  // S, dP
   static constexpr uint32_t IDESC_ACC = idesc_bf16(BM, D, false, true);   // dV, dK, dQ
 };
 
 template <bool DKDV, int D>
-__global__ void __launch_bounds__(320, 1)
+__global__ void __launch_bounds__((BwdCfg<DKDV, D>::NCW + 2) * 32, 1)
     smat_bwd_tc_kernel(const __grid_constant__ CUtensorMap tm_r0,
                        const __grid_constant__ CUtensorMap tm_r1,
                        const __grid_constant__ CUtensorMap tm_c0,
@@ -116,14 +124,15 @@ __global__ void __launch_bounds__(320, 1)
       mbar_init(bar(C::BAR_AD + i), 1);
     }
     mbar_init(bar(C::BAR_DRAIN), 1);
+    mbar_init(bar(C::BAR_RT), C::NCW);
     fence_barrier_init();
     misc[1] = 0;
   }
-  if (warp == 9) {
+  if (warp == C::MMA_WARP) {
     tmem_alloc(sbase + C::OFF_MISC, C::TMEM_COLS);
     tmem_relinquish();
   }
-  if (warp == 8 && lane == 0) {
+  if (warp == C::PRODUCER_WARP && lane == 0) {
     prefetch_tmap(&tm_r0);
     prefetch_tmap(&tm_r1);
     prefetch_tmap(&tm_c0);
@@ -134,7 +143,7 @@ __global__ void __launch_bounds__(320, 1)
   tc_fence_after();
   const uint32_t tbase = misc[0];
 
-  if (warp == 8) {
+  if (warp == C::PRODUCER_WARP) {
     // ------------------------------------------------------------ producer
     // Lane 0 issues the TMA loads; for dK/dV all 32 lanes also copy the
     // chunk's lse and delta next to it with cp.async, tracked by the same
@@ -194,7 +203,7 @@ __global__ void __launch_bounds__(320, 1)
           mbar_wait_drain(bar(C::BAR_CF + j % C::STAGES), (j / C::STAGES) & 1);
       }
     }
-  } else if (warp == 9) {
+  } else if (warp == C::MMA_WARP) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
       ChunkIter<2> it;
@@ -211,19 +220,28 @@ __global__ void __launch_bounds__(320, 1)
         for (int kk = 0; kk < D / 16; ++kk) {
           const uint32_t off = (kk >> 2) * (C::BM * 128) + (kk & 3) * 32;
           const uint32_t offc = (kk >> 2) * (C::CN * 128) + (kk & 3) * 32;
-          tc_mma(tb + C::COL_S, sdesc_sw128(r0 + off, 16, 1024), sdesc_sw128(c0 + offc, 16, 1024),
-                 C::IDESC_SC, kk > 0 ? 1u : 0u);
+          if (C::RES_TMEM)   // A = 16 d-elements = 8 packed columns per k-step
+            tc_mma_ts(tb + C::COL_S, tbase + C::COL_RT0 + kk * 8,
+                      sdesc_sw128(c0 + offc, 16, 1024), C::IDESC_SC, kk > 0 ? 1u : 0u);
+          else
+            tc_mma(tb + C::COL_S, sdesc_sw128(r0 + off, 16, 1024),
+                   sdesc_sw128(c0 + offc, 16, 1024), C::IDESC_SC, kk > 0 ? 1u : 0u);
         }
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
           const uint32_t off = (kk >> 2) * (C::BM * 128) + (kk & 3) * 32;
           const uint32_t offc = (kk >> 2) * (C::CN * 128) + (kk & 3) * 32;
-          tc_mma(tb + C::COL_DP, sdesc_sw128(r1 + off, 16, 1024), sdesc_sw128(c1 + offc, 16, 1024),
-                 C::IDESC_SC, kk > 0 ? 1u : 0u);
+          if (C::RES_TMEM)
+            tc_mma_ts(tb + C::COL_DP, tbase + C::COL_RT1 + kk * 8,
+                      sdesc_sw128(c1 + offc, 16, 1024), C::IDESC_SC, kk > 0 ? 1u : 0u);
+          else
+            tc_mma(tb + C::COL_DP, sdesc_sw128(r1 + off, 16, 1024),
+                   sdesc_sw128(c1 + offc, 16, 1024), C::IDESC_SC, kk > 0 ? 1u : 0u);
         }
         tc_commit(bar(C::BAR_SF + (j & 1)));
       };
       bool ok = mbar_wait(bar(C::BAR_R), 0, abort_flag, p.err);
+      if (C::RES_TMEM && ok) ok = mbar_wait(bar(C::BAR_RT), 0, abort_flag, p.err);
       uint32_t e;
       int c;
       bool has = ok && it.next(e, c, p.err);
@@ -254,8 +272,8 @@ __global__ void __launch_bounds__(320, 1)
 #pragma unroll
         for (int kk = 0; kk < C::CN / 16; ++kk) {
           // A in TMEM: the 16 chunk columns of k-step kk are 8 packed columns
-          // inside the 32-column half written by warps of half kk / 2
-          const uint32_t aoff = (kk >> 1) * 32 + (kk & 1) * 8;
+          // at the start of the column group of the warps that wrote them
+          const uint32_t aoff = (16 * kk / C::CW) * C::CW + (16 * kk % C::CW) / 2;
           if (DKDV) {
             // dV += P^T dO_c ; dK += dS^T Q_c   (B operands MN-major)
             tc_mma_ts(tbase + C::COL_ACC1, tb + C::COL_S + aoff,
@@ -287,11 +305,12 @@ __global__ void __launch_bounds__(320, 1)
     }
   } else {
     // ------------------------------------------------------------ compute
-    const int quad = warp & 3, half = warp >> 2;
+    constexpr int CW = C::CW;
+    const int quad = warp & 3, grp = warp >> 2;
     const int r = quad * 32 + lane;                 // tile row = TMEM lane
     const int pos = tile * C::BM + r;               // key (dK/dV) or query (dQ) position
     const int srow = (sub == 2) ? (r >> 6) : 0;     // CSR row of this tile row
-    const int col0 = half * 32;                     // this warp's 32 chunk columns
+    const int col0 = grp * CW;                      // this warp's chunk columns
     const uint32_t lane_base = tbase + (static_cast<uint32_t>(quad * 32) << 16);
     const float LOG2E = 1.4426950408889634f;
     const float* ld = reinterpret_cast<const float*>(smem + C::OFF_LD);  // [STAGES][lse | delta]
@@ -302,6 +321,36 @@ __global__ void __launch_bounds__(320, 1)
       row_delta = in ? p.delta[static_cast<int64_t>(bh) * p.T + pos] : 0.f;
     }
     bool alive = true;
+    if (C::RES_TMEM) {
+      // copy this warp's share of the resident rows (Q, dO) into TMEM: row r,
+      // 16-byte chunk q of the row = packed columns [4 q, 4 q + 4)
+      alive = __all_sync(0xffffffffu, mbar_wait(bar(C::BAR_R), 0, abort_flag, p.err));
+      if (alive) {
+        constexpr int QPG = D / 8 / (C::NCW / 4);   // 16-byte chunks per warp group
+#pragma unroll
+        for (int t = 0; t < 2; ++t) {
+          const uint8_t* src = smem + (t == 0 ? C::OFF_R0 : C::OFF_R1);
+          uint32_t w[QPG * 4];
+#pragma unroll
+          for (int u = 0; u < QPG; ++u) {
+            const int q = grp * QPG + u;
+            const uint4 v = *reinterpret_cast<const uint4*>(
+                src + (q >> 3) * (C::BM * 128) + sw128_offset(r, q & 7));
+            w[4 * u] = v.x;
+            w[4 * u + 1] = v.y;
+            w[4 * u + 2] = v.z;
+            w[4 * u + 3] = v.w;
+          }
+          const uint32_t dst = lane_base + (t == 0 ? C::COL_RT0 : C::COL_RT1) + grp * QPG * 4;
+          if (QPG * 4 == 16) tmem_st16u(dst, w);
+          else tmem_st8u(dst, w);
+        }
+        tmem_st_wait();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(bar(C::BAR_RT));
+      }
+    }
     int n = 0;
     ChunkIter<2> it;
     it.init(p.indptr, p.indices, p.kind, p.nblocks, p.nnzb, row0, sub, cpb, p.err);
@@ -318,24 +367,29 @@ __global__ void __launch_bounds__(320, 1)
         alive = false;
         break;
       }
-      if (!__all_sync(0xffffffffu, mbar_wait(bar(C::BAR_SF + (j & 1)), (j >> 1) & 1, abort_flag, p.err))) {
+      if (!__all_sync(0xffffffffu,
+                      mbar_wait(bar(C::BAR_SF + (j & 1)), (j >> 1) & 1, abort_flag, p.err))) {
         alive = false;
         break;
       }
       tc_fence_after();
       const uint32_t tb = lane_base + (j & 1) * C::BUF_COLS;
-      float sv[32], dp[32];
-      tmem_ld32x2(tb + C::COL_S + col0, tb + C::COL_DP + col0, sv, dp);
-      // warp-uniform: no element of this warp's 32 x 32 block is masked
+      float sv[CW], dp[CW];
+      if (CW == 32) {
+        tmem_ld32x2(tb + C::COL_S + col0, tb + C::COL_DP + col0, sv, dp);
+      } else {
+        tmem_ld16x2(tb + C::COL_S + col0, tb + C::COL_DP + col0, sv, dp);
+      }
+      // warp-uniform: no element of this warp's 32 x CW block is masked
       const bool all_valid = (st == ST_FULL) && (!DKDV || c0pos + C::CN <= p.T);
       // per-column terms: -lse log2(e) and delta of the chunk's queries (dK/dV),
       // or the row's own (dQ)
-      float nl2[32], dl[32];
+      float nl2[CW], dl[CW];
       if (DKDV) {
         const float4* l4 = reinterpret_cast<const float4*>(ldj + col0);
         const float4* d4 = reinterpret_cast<const float4*>(ldj + C::CN + col0);
 #pragma unroll
-        for (int q = 0; q < 8; ++q) {
+        for (int q = 0; q < CW / 4; ++q) {
           const float4 a = l4[q], dd = d4[q];
           nl2[4 * q] = a.x * -LOG2E;
           nl2[4 * q + 1] = a.y * -LOG2E;
@@ -348,18 +402,18 @@ __global__ void __launch_bounds__(320, 1)
         }
       } else {
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
+        for (int i = 0; i < CW; ++i) {
           nl2[i] = -row_lse2;
           dl[i] = row_delta;
         }
       }
-      float pv[32];
+      float pv[CW];
       if (all_valid) {
 #pragma unroll
-        for (int i = 0; i < 32; ++i) pv[i] = ex2_approx(fmaf(sv[i], p.scale_log2, nl2[i]));
+        for (int i = 0; i < CW; ++i) pv[i] = ex2_approx(fmaf(sv[i], p.scale_log2, nl2[i]));
       } else {
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
+        for (int i = 0; i < CW; ++i) {
           const int cpos = c0pos + col0 + i;
           // dK/dV: row = key `pos`, column = query `cpos`; dQ: the reverse
           const bool valid =
@@ -368,16 +422,21 @@ __global__ void __launch_bounds__(320, 1)
           pv[i] = valid ? ex2_approx(fmaf(sv[i], p.scale_log2, nl2[i])) : 0.f;
         }
       }
-      uint32_t wp[16], wd[16];
+      uint32_t wp[CW / 2], wd[CW / 2];
 #pragma unroll
-      for (int i = 0; i < 16; ++i) {
+      for (int i = 0; i < CW / 2; ++i) {
         wp[i] = pack_bf16(pv[2 * i], pv[2 * i + 1]);
         wd[i] = pack_bf16(pv[2 * i] * (dp[2 * i] - dl[2 * i]),
                           pv[2 * i + 1] * (dp[2 * i + 1] - dl[2 * i + 1]));
       }
       // P^T / dS^T / dS over the S / dP columns this warp has already read
-      if (DKDV) tmem_st16u(tb + C::COL_S + col0, wp);
-      tmem_st16u(tb + C::COL_DP + col0, wd);
+      if (CW == 32) {
+        if (DKDV) tmem_st16u(tb + C::COL_S + col0, wp);
+        tmem_st16u(tb + C::COL_DP + col0, wd);
+      } else {
+        if (DKDV) tmem_st8u(tb + C::COL_S + col0, wp);
+        tmem_st8u(tb + C::COL_DP + col0, wd);
+      }
       tmem_st_wait();
       tc_fence_before();
       __syncwarp();
@@ -397,22 +456,23 @@ __global__ void __launch_bounds__(320, 1)
                                      static_cast<int64_t>(h) * p.o1_sh +
                                      static_cast<int64_t>(pos) * p.o1_st
                                : nullptr;
+      constexpr int EW = D / (C::NCW / 4);   // accumulator columns per warp group
 #pragma unroll
       for (int acc = 0; acc < (DKDV ? 2 : 1); ++acc) {
         __nv_bfloat16* dst = acc == 0 ? o0 : o1;
         const float mul = acc == 0 ? p.scale : 1.f;  // dK and dQ carry the softmax scale
 #pragma unroll
-        for (int cc = half * (D / 2); cc < (half + 1) * (D / 2); cc += 32) {
-          float v[32];
+        for (int cc = grp * EW; cc < (grp + 1) * EW; cc += 16) {
+          float v[16];
           if (n > 0) {
-            tmem_ld32(lane_base + C::COL_ACC0 + acc * D + cc, v);
+            tmem_ld16(lane_base + C::COL_ACC0 + acc * D + cc, v);
           } else {
 #pragma unroll
-            for (int i = 0; i < 32; ++i) v[i] = 0.f;
+            for (int i = 0; i < 16; ++i) v[i] = 0.f;
           }
           if (store) {
 #pragma unroll
-            for (int i = 0; i < 32; i += 8) {
+            for (int i = 0; i < 16; i += 8) {
               uint4 w = make_uint4(pack_bf16(v[i] * mul, v[i + 1] * mul),
                                    pack_bf16(v[i + 2] * mul, v[i + 3] * mul),
                                    pack_bf16(v[i + 4] * mul, v[i + 5] * mul),
@@ -427,7 +487,7 @@ __global__ void __launch_bounds__(320, 1)
 
   tc_fence_before();
   __syncthreads();
-  if (warp == 9) {
+  if (warp == C::MMA_WARP) {
     __syncwarp();
     tc_fence_after();
     tmem_dealloc(tbase, C::TMEM_COLS);
