@@ -72,10 +72,11 @@ enum { SMAT_TILE_FULL = 0, SMAT_TILE_CAUSAL = 1 };
 enum {
   SMAT_DEVERR_WAIT_TIMEOUT = 1,
   SMAT_DEVERR_BAD_CSR = 2,
-  SMAT_DEVERR_SCHED_OVERFLOW = 4
+  SMAT_DEVERR_SCHED_OVERFLOW = 4,
+  SMAT_DEVERR_BAD_WORK = 8
 };
 
-/* ABI version of this header (incremented on any signature change). */
+/* ABI version of this header (incremented when an entry point changes or is added). */
 SMAT_API int smat_abi_version(void);
 
 /* Human-readable name of a status code (static string). */
@@ -133,6 +134,32 @@ SMAT_API int smat_fwd(int dtype,
              int nblocks, int64_t nnzb, int block, int max_row,
              float scale, int32_t* err_word, void* stream);
 
+/* ---------------------------------------------------------------- work lists
+ * The *_tiles / *_rows entry points compute a subset of the rows: a shard of
+ * the queries (forward, dQ) or of the keys (dK/dV) when one sequence is split
+ * across GPUs by query blocks.  `work` is a DEVICE array of n_work int32
+ * items, one per CTA and (b, h), run in the given order (put the heaviest
+ * first).  Item bits 0..23: a 128-row tile index t (rows [128 t, 128 t + 128)
+ * of T); bit 24, forward only: the CTA also computes tile t + 1 (two adjacent
+ * query tiles share their K/V loads).  Rows outside the listed tiles are not
+ * written.  An item naming a tile past the end, or bit 24 where it is not
+ * allowed, sets SMAT_DEVERR_BAD_WORK in *err_word and its CTA does nothing.
+ * The layout arguments are the whole layout (or a filtered copy of it, see
+ * smat_attention_b200.sharding); outputs of the listed tiles are complete
+ * sums over their CSR rows / columns.  No counterpart in the reference, which
+ * has no multi-GPU path. */
+SMAT_API int smat_fwd_tiles(int dtype,
+                   const void* q, const int64_t* q_stride,
+                   const void* k, const int64_t* k_stride,
+                   const void* v, const int64_t* v_stride,
+                   void* o, const int64_t* o_stride,
+                   float* lse,
+                   int B, int H, int T, int D,
+                   const int32_t* indptr, const int32_t* indices, const uint8_t* kind,
+                   int nblocks, int64_t nnzb, int block, int max_row,
+                   float scale, const int32_t* work, int n_work,
+                   int32_t* err_word, void* stream);
+
 /* ---------------------------------------------------------------- backward
  * delta[b, h, t] = sum_d dO[b,h,t,d] * o[b,h,t,d]
  * (the row-sum preprocess of the reference's backward,
@@ -141,6 +168,14 @@ SMAT_API int smat_bwd_preprocess(int dtype,
                         const void* o, const int64_t* o_stride,
                         const void* dout, const int64_t* do_stride,
                         float* delta, int B, int H, int T, int D, void* stream);
+
+/* smat_bwd_preprocess for rows [row_lo, row_hi) of every (b, h) only; delta
+ * keeps its [B*H, T] layout. */
+SMAT_API int smat_bwd_preprocess_rows(int dtype,
+                             const void* o, const int64_t* o_stride,
+                             const void* dout, const int64_t* do_stride,
+                             float* delta, int B, int H, int T, int D,
+                             int row_lo, int row_hi, void* stream);
 
 /* dk, dv over the transposed CSR (t_indptr, t_indices, t_kind); t_max_row is
  * its longest row.  Replaces the reference's column-parallel backward kernel
@@ -158,6 +193,21 @@ SMAT_API int smat_bwd_dkdv(int dtype,
                   int nblocks, int64_t nnzb, int block, int t_max_row,
                   float scale, int32_t* err_word, void* stream);
 
+/* smat_bwd_dkdv for the key tiles of a work list (items without bit 24). */
+SMAT_API int smat_bwd_dkdv_tiles(int dtype,
+                        const void* q, const int64_t* q_stride,
+                        const void* k, const int64_t* k_stride,
+                        const void* v, const int64_t* v_stride,
+                        const void* dout, const int64_t* do_stride,
+                        const float* lse, const float* delta,
+                        void* dk, const int64_t* dk_stride,
+                        void* dv, const int64_t* dv_stride,
+                        int B, int H, int T, int D,
+                        const int32_t* t_indptr, const int32_t* t_indices, const uint8_t* t_kind,
+                        int nblocks, int64_t nnzb, int block, int t_max_row,
+                        float scale, const int32_t* work, int n_work,
+                        int32_t* err_word, void* stream);
+
 /* dq over the forward CSR.  Replaces the reference's row-parallel backward
  * kernel (src/smat/kernels/triton_bwd.py:50-94). */
 SMAT_API int smat_bwd_dq(int dtype,
@@ -172,9 +222,24 @@ SMAT_API int smat_bwd_dq(int dtype,
                 int nblocks, int64_t nnzb, int block, int max_row,
                 float scale, int32_t* err_word, void* stream);
 
+/* smat_bwd_dq for the query tiles of a work list (items without bit 24). */
+SMAT_API int smat_bwd_dq_tiles(int dtype,
+                      const void* q, const int64_t* q_stride,
+                      const void* k, const int64_t* k_stride,
+                      const void* v, const int64_t* v_stride,
+                      const void* dout, const int64_t* do_stride,
+                      const float* lse, const float* delta,
+                      void* dq, const int64_t* dq_stride,
+                      int B, int H, int T, int D,
+                      const int32_t* indptr, const int32_t* indices, const uint8_t* kind,
+                      int nblocks, int64_t nnzb, int block, int max_row,
+                      float scale, const int32_t* work, int n_work,
+                      int32_t* err_word, void* stream);
+
 /* The whole backward: preprocess into the caller's delta workspace
  * (fp32 [B*H*T]), then dK/dV and dQ.  Replaces the autograd backward of the
- * reference's fused path (src/smat/kernels/triton_bwd.py:162-196). */
+ * reference's fused path (src/smat/kernels/triton_bwd.py:162-196).  All
+ * three passes are checked before the first launches. */
 SMAT_API int smat_bwd(int dtype,
              const void* q, const int64_t* q_stride,
              const void* k, const int64_t* k_stride,

@@ -16,6 +16,11 @@ LIB_PATH = os.path.join(_HERE, "libsmat_b200.so")
 DTYPE_F32 = 0
 DTYPE_BF16 = 1
 
+# work items of the *_tiles entry points: tile index in bits 0..23, bit 24 =
+# "also the next tile" (forward only)
+WORK_PAIR_BIT = 1 << 24
+TILE_ROWS = 128
+
 _c_int, _c_i64, _c_f = ctypes.c_int, ctypes.c_int64, ctypes.c_float
 _vp = ctypes.c_void_p
 _i64p = ctypes.POINTER(ctypes.c_int64)
@@ -33,16 +38,31 @@ SIGNATURES = {
     "smat_fwd": (_c_int, [_c_int, _vp, _i64p, _vp, _i64p, _vp, _i64p, _vp, _i64p, _vp,
                           _c_int, _c_int, _c_int, _c_int, _vp, _vp, _vp,
                           _c_int, _c_i64, _c_int, _c_int, _c_f, _vp, _vp]),
+    # smat_fwd plus (work, n_work) before err_word
+    "smat_fwd_tiles": (_c_int, [_c_int, _vp, _i64p, _vp, _i64p, _vp, _i64p, _vp, _i64p, _vp,
+                                _c_int, _c_int, _c_int, _c_int, _vp, _vp, _vp,
+                                _c_int, _c_i64, _c_int, _c_int, _c_f, _vp, _c_int, _vp, _vp]),
     "smat_bwd_preprocess": (_c_int, [_c_int, _vp, _i64p, _vp, _i64p, _vp,
                                      _c_int, _c_int, _c_int, _c_int, _vp]),
+    "smat_bwd_preprocess_rows": (_c_int, [_c_int, _vp, _i64p, _vp, _i64p, _vp,
+                                          _c_int, _c_int, _c_int, _c_int, _c_int, _c_int, _vp]),
     "smat_bwd_dkdv": (_c_int, [_c_int, _vp, _i64p, _vp, _i64p, _vp, _i64p, _vp, _i64p,
                                _vp, _vp, _vp, _i64p, _vp, _i64p,
                                _c_int, _c_int, _c_int, _c_int, _vp, _vp, _vp,
                                _c_int, _c_i64, _c_int, _c_int, _c_f, _vp, _vp]),
+    "smat_bwd_dkdv_tiles": (_c_int, [_c_int, _vp, _i64p, _vp, _i64p, _vp, _i64p, _vp, _i64p,
+                                     _vp, _vp, _vp, _i64p, _vp, _i64p,
+                                     _c_int, _c_int, _c_int, _c_int, _vp, _vp, _vp,
+                                     _c_int, _c_i64, _c_int, _c_int, _c_f, _vp, _c_int,
+                                     _vp, _vp]),
     "smat_bwd_dq": (_c_int, [_c_int, _vp, _i64p, _vp, _i64p, _vp, _i64p, _vp, _i64p,
                              _vp, _vp, _vp, _i64p,
                              _c_int, _c_int, _c_int, _c_int, _vp, _vp, _vp,
                              _c_int, _c_i64, _c_int, _c_int, _c_f, _vp, _vp]),
+    "smat_bwd_dq_tiles": (_c_int, [_c_int, _vp, _i64p, _vp, _i64p, _vp, _i64p, _vp, _i64p,
+                                   _vp, _vp, _vp, _i64p,
+                                   _c_int, _c_int, _c_int, _c_int, _vp, _vp, _vp,
+                                   _c_int, _c_i64, _c_int, _c_int, _c_f, _vp, _c_int, _vp, _vp]),
     "smat_bwd": (_c_int, [_c_int, _vp, _i64p, _vp, _i64p, _vp, _i64p, _vp, _i64p, _vp, _i64p,
                           _vp, _vp, _vp, _i64p, _vp, _i64p, _vp, _i64p,
                           _c_int, _c_int, _c_int, _c_int, _vp, _vp, _vp, _vp, _vp, _vp,

@@ -37,6 +37,7 @@ struct BwdParams {
   __nv_bfloat16* out1;     // dV (dK/dV kernel only)
   int64_t o0_sb, o0_sh, o0_st, o1_sb, o1_sh, o1_st;
   int B, H, T, nblocks, nnzb, bs, n_tiles;
+  const int32_t* work;     // optional work list (one tile per CTA and (b, h)); null = all tiles
   float scale;             // softmax scale
   float scale_log2;        // softmax scale * log2(e)
   int32_t* err;
@@ -106,7 +107,18 @@ __global__ void __launch_bounds__((BwdCfg<DKDV, D>::NCW + 2) * 32, 1)
   const int bh = lin % BH;
   // dQ: latest query tiles are the heaviest; dK/dV: earliest key tiles are
   // (sinks and summaries are read by every later query)
-  const int tile = DKDV ? lin / BH : p.n_tiles - 1 - lin / BH;
+  int tile;
+  if (p.work) {
+    // caller-chosen tiles (a shard of the rows), in the caller's order
+    const int w = __ldg(p.work + lin / BH);
+    tile = w & WORK_TILE_MASK;
+    if ((w >> 24) != 0 || tile >= p.n_tiles) {
+      if (threadIdx.x == 0 && p.err) atomicOr(p.err, DEV_ERR_BAD_WORK);
+      return;
+    }
+  } else {
+    tile = DKDV ? lin / BH : p.n_tiles - 1 - lin / BH;
+  }
   const int b = bh / p.H, h = bh % p.H;
   const int sub = C::BM / p.bs;   // CSR rows per tile: 1 or 2
   const int cpb = p.bs / C::CN;   // chunks per block: 2 or 1

@@ -17,11 +17,17 @@
 
 namespace smat {
 
+// Work items of the *_tiles entry points: bits 0..23 a 128-row tile index,
+// bit 24 (forward only) "the CTA also takes the next tile".
+constexpr int WORK_TILE_MASK = 0xFFFFFF;
+constexpr int WORK_PAIR_BIT = 1 << 24;
+
 // device error bits (OR-ed into the caller's int32 error word)
 enum : int32_t {
   DEV_ERR_WAIT_TIMEOUT = 1 << 0,
   DEV_ERR_BAD_CSR = 1 << 1,
   DEV_ERR_SCHED_OVERFLOW = 1 << 2,
+  DEV_ERR_BAD_WORK = 1 << 3,
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {

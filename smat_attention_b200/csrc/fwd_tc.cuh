@@ -38,6 +38,7 @@ struct FwdParams {
   float* lse;
   int64_t o_sb, o_sh, o_st;  // element strides of O over (b, h, t); d stride is 1
   int B, H, T, nblocks, nnzb, bs, n_tiles, n_pairs;
+  const int32_t* work;       // optional work list (one item per CTA and (b, h)); null = all tiles
   float scale_log2;          // softmax scale * log2(e)
   int32_t* err;
 };
@@ -115,8 +116,20 @@ __global__ void __launch_bounds__(320, 1)
   const int BH = p.B * p.H;
   const int lin = blockIdx.x;
   const int bh = lin % BH;
-  const int pair = p.n_pairs - 1 - lin / BH;  // heaviest (latest) tiles first
-  const int tile0 = 2 * pair;
+  int tile0, ntile;
+  if (p.work) {
+    // caller-chosen tiles (a shard of the queries), in the caller's order
+    const int w = __ldg(p.work + lin / BH);
+    tile0 = w & WORK_TILE_MASK;
+    ntile = (w & WORK_PAIR_BIT) ? 2 : 1;
+    if ((w >> 25) != 0 || tile0 + ntile > p.n_tiles) {
+      if (threadIdx.x == 0 && p.err) atomicOr(p.err, DEV_ERR_BAD_WORK);
+      return;
+    }
+  } else {
+    tile0 = 2 * (p.n_pairs - 1 - lin / BH);  // heaviest (latest) tiles first
+    ntile = min(2, p.n_tiles - tile0);
+  }
   const int b = bh / p.H, h = bh % p.H;
   const int sub = C::BM / p.bs;   // CSR rows per tile: 1 (bs 128) or 2 (bs 64)
   const int cpb = p.bs / C::BN;   // chunks per block: 2 (bs 128) or 1 (bs 64)
@@ -155,7 +168,7 @@ __global__ void __launch_bounds__(320, 1)
     // ------------------------------------------------------------ producer
     if (lane == 0) {
       ChunkIter<4> it;
-      it.init(p.indptr, p.indices, p.kind, p.nblocks, p.nnzb, row0, 2 * sub, cpb, p.err);
+      it.init(p.indptr, p.indices, p.kind, p.nblocks, p.nnzb, row0, ntile * sub, cpb, p.err);
       mbar_expect_tx(bar(C::BAR_Q), C::NT * C::Q_BYTES);
 #pragma unroll
       for (int x = 0; x < C::NT; ++x)
@@ -192,7 +205,7 @@ __global__ void __launch_bounds__(320, 1)
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
       ChunkIter<4> it;
-      it.init(p.indptr, p.indices, p.kind, p.nblocks, p.nnzb, row0, 2 * sub, cpb, p.err);
+      it.init(p.indptr, p.indices, p.kind, p.nblocks, p.nnzb, row0, ntile * sub, cpb, p.err);
       int cs[C::NT] = {0, 0}, cp[C::NT] = {0, 0};
       auto active = [&](uint32_t e, int x) { return sched_states(e, x * sub, sub) != 0; };
       auto issue_s = [&](int j, uint32_t e) {
@@ -279,6 +292,7 @@ __global__ void __launch_bounds__(320, 1)
     const int x = warp >> 2;                   // tile of this warpgroup
     const int r = (warp & 3) * 32 + lane;      // row within the tile = TMEM lane
     const int q_pos = (tile0 + x) * C::BM + r;
+    const bool store = x < ntile && q_pos < p.T;   // rows this CTA writes
     const int srow = x * sub + ((sub == 2) ? (r >> 6) : 0);   // CSR row of this query
     const uint32_t lane_base =
         tbase + (static_cast<uint32_t>((warp & 3) * 32) << 16) + x * C::TILE_COLS;
@@ -286,7 +300,7 @@ __global__ void __launch_bounds__(320, 1)
     int cnt = 0;
     bool alive = true;
     ChunkIter<4> it;
-    it.init(p.indptr, p.indices, p.kind, p.nblocks, p.nnzb, row0, 2 * sub, cpb, p.err);
+    it.init(p.indptr, p.indices, p.kind, p.nblocks, p.nnzb, row0, ntile * sub, cpb, p.err);
     uint32_t e;
     int c;
     while (alive && it.next(e, c, p.err)) {
@@ -388,7 +402,7 @@ __global__ void __launch_bounds__(320, 1)
 #pragma unroll
           for (int i = 0; i < 32; ++i) ov[i] = 0.f;
         }
-        if (q_pos < p.T) {
+        if (store) {
 #pragma unroll
           for (int i = 0; i < 32; i += 8) {
             uint4 w = make_uint4(pack_bf16(ov[i] * inv, ov[i + 1] * inv),
@@ -399,7 +413,7 @@ __global__ void __launch_bounds__(320, 1)
           }
         }
       }
-      if (q_pos < p.T)
+      if (store)
         p.lse[static_cast<int64_t>(bh) * p.T + q_pos] =
             (l > 0.f) ? (m + __log2f(l)) * 0.69314718055994531f : -INFINITY;
     }

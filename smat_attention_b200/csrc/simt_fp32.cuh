@@ -30,9 +30,39 @@ struct SimtParams {
   const int32_t* indices;
   const uint8_t* kind;
   int B, H, T, nblocks, nnzb, bs;
+  const int32_t* work;  // optional work list of 128-row tiles; null = all rows
+  int span_tiles;       // tiles one work item may span: 2 (forward) or 1
   float scale;
   int32_t* err;
 };
+
+constexpr int SIMT_TILE = 128;
+
+// Row of group g in this CTA.  Without a work list CTA x covers rows
+// [x RPC, x RPC + RPC); with one, each item owns span_tiles * 128 / RPC CTAs
+// and rows outside the item's tiles are inactive.  False for an invalid item
+// (the CTA then returns without touching memory).
+template <int RPC>
+__device__ __forceinline__ bool simt_row(const SimtParams& p, int g, int& row, bool& active) {
+  if (!p.work) {
+    row = blockIdx.x * RPC + g;
+    active = row < p.T;
+    return true;
+  }
+  const int per = p.span_tiles * SIMT_TILE / RPC;
+  const int w = __ldg(p.work + blockIdx.x / per);
+  const int tile = w & WORK_TILE_MASK;
+  const int n = (w & WORK_PAIR_BIT) ? 2 : 1;
+  const int n_tiles = (p.T + SIMT_TILE - 1) / SIMT_TILE;
+  if ((w >> 25) != 0 || n > p.span_tiles || tile + n > n_tiles) {
+    if (threadIdx.x == 0 && p.err) atomicOr(p.err, DEV_ERR_BAD_WORK);
+    return false;
+  }
+  const int off = (blockIdx.x % per) * RPC + g;
+  row = tile * SIMT_TILE + off;
+  active = off < n * SIMT_TILE && row < p.T;
+  return true;
+}
 
 // Sum over the TPR lanes that own one row.  Only those lanes take part (the
 // mask names them), so rows of one warp may walk different key counts.
@@ -51,15 +81,17 @@ __device__ __forceinline__ const float* row_ptr(const float* base, const int64_t
   return base + b * s[0] + h * s[1] + static_cast<int64_t>(t) * s[2];
 }
 
-// grid: (ceil(T / rows_per_cta), B * H); block 128 threads.
+// grid: (ceil(T / rows_per_cta) or n_work * span_tiles * 128 / rows_per_cta, B * H);
+// block 128 threads.
 template <int D>
 __global__ void __launch_bounds__(128) smat_fwd_simt_kernel(const SimtParams p) {
   constexpr int TPR = D / 32;
   constexpr int RPC = 128 / TPR;
   const int bh = blockIdx.y, b = bh / p.H, h = bh % p.H;
   const int g = threadIdx.x / TPR, part = threadIdx.x % TPR;
-  const int i = blockIdx.x * RPC + g;
-  const bool active = i < p.T;
+  int i;
+  bool active;
+  if (!simt_row<RPC>(p, g, i, active)) return;
   const int ii = active ? i : p.T - 1;
   float q[32], acc[32];
   const float* qr = row_ptr(p.q, p.q_s, b, h, ii) + part * 32;
@@ -112,8 +144,9 @@ __global__ void __launch_bounds__(128) smat_dq_simt_kernel(const SimtParams p) {
   constexpr int RPC = 128 / TPR;
   const int bh = blockIdx.y, b = bh / p.H, h = bh % p.H;
   const int g = threadIdx.x / TPR, part = threadIdx.x % TPR;
-  const int i = blockIdx.x * RPC + g;
-  const bool active = i < p.T;
+  int i;
+  bool active;
+  if (!simt_row<RPC>(p, g, i, active)) return;
   const int ii = active ? i : p.T - 1;
   float q[32], dor[32], dq[32];
   const float* qr = row_ptr(p.q, p.q_s, b, h, ii) + part * 32;
@@ -163,8 +196,9 @@ __global__ void __launch_bounds__(128) smat_dkdv_simt_kernel(const SimtParams p)
   constexpr int RPC = 128 / TPR;
   const int bh = blockIdx.y, b = bh / p.H, h = bh % p.H;
   const int g = threadIdx.x / TPR, part = threadIdx.x % TPR;
-  const int j = blockIdx.x * RPC + g;
-  const bool active = j < p.T;
+  int j;
+  bool active;
+  if (!simt_row<RPC>(p, g, j, active)) return;
   const int jj = active ? j : p.T - 1;
   float kr[32], vr[32], dk[32], dv[32];
   const float* kp = row_ptr(p.k, p.k_s, b, h, jj) + part * 32;
@@ -216,8 +250,9 @@ __global__ void __launch_bounds__(128) smat_dkdv_simt_kernel(const SimtParams p)
   }
 }
 
-// delta[bh, t] = sum_d dO[b,h,t,d] * O[b,h,t,d]; one warp per 32 / LPR rows,
-// LPR lanes per row each reading 16-byte vectors.
+// delta[bh, t] = sum_d dO[b,h,t,d] * O[b,h,t,d] for t in [row_lo, row_lo + n_rows);
+// one warp per 32 / LPR rows, LPR lanes per row each reading 16-byte vectors;
+// rows = B * H * n_rows.
 template <typename T, int D>
 __global__ void __launch_bounds__(256) smat_bwd_pre_kernel(const T* __restrict__ o,
                                                            const T* __restrict__ dout,
@@ -225,7 +260,8 @@ __global__ void __launch_bounds__(256) smat_bwd_pre_kernel(const T* __restrict__
                                                            int64_t o_sb, int64_t o_sh,
                                                            int64_t o_st, int64_t d_sb,
                                                            int64_t d_sh, int64_t d_st, int H,
-                                                           int T_, int64_t rows) {
+                                                           int T_, int row_lo, int n_rows,
+                                                           int64_t rows) {
   constexpr int VEC = 16 / sizeof(T);
   constexpr int LPR = D / VEC;  // lanes per row
   static_assert(LPR <= 32 && 32 % LPR == 0, "unsupported D");
@@ -234,8 +270,8 @@ __global__ void __launch_bounds__(256) smat_bwd_pre_kernel(const T* __restrict__
   const int part = static_cast<int>(gt % LPR);
   float acc = 0.f;
   if (row < rows) {
-    const int t = static_cast<int>(row % T_);
-    const int64_t bh = row / T_;
+    const int t = row_lo + static_cast<int>(row % n_rows);
+    const int64_t bh = row / n_rows;
     const int b = static_cast<int>(bh / H), h = static_cast<int>(bh % H);
     const T* op = o + b * o_sb + h * o_sh + t * o_st + part * VEC;
     const T* dp = dout + b * d_sb + h * d_sh + t * d_st + part * VEC;
@@ -248,7 +284,7 @@ __global__ void __launch_bounds__(256) smat_bwd_pre_kernel(const T* __restrict__
   }
 #pragma unroll
   for (int off = 1; off < LPR; off <<= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
-  if (row < rows && part == 0) delta[row] = acc;
+  if (row < rows && part == 0) delta[(row / n_rows) * T_ + row_lo + row % n_rows] = acc;
 }
 
 }  // namespace smat

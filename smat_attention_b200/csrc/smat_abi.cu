@@ -27,6 +27,20 @@ struct TArg {
 
 TArg targ(const void* p, const int64_t* s) { return TArg{p, s[0], s[1], s[2]}; }
 
+// Optional list of tiles to compute (device array); items == nullptr means
+// every tile of the sequence.
+struct Work {
+  const int32_t* items;
+  int n;
+};
+constexpr Work kAllTiles{nullptr, 0};
+
+int check_work(const Work& w) {
+  if (w.n < 0) return SMAT_ERR_BAD_SHAPE;
+  if (w.n > 0 && !w.items) return SMAT_ERR_NULL_POINTER;
+  return SMAT_OK;
+}
+
 // ---------------------------------------------------------------- checks
 int check_common(int dtype, int B, int H, int T, int D, int nblocks, int block) {
   if (B < 1 || H < 1 || T < 1) return SMAT_ERR_BAD_SHAPE;
@@ -116,7 +130,8 @@ int launch_status() {
 template <int D>
 int fwd_tc(const TArg& q, const TArg& k, const TArg& v, const TArg& o, float* lse, int B, int H,
            int T, const int32_t* indptr, const int32_t* indices, const uint8_t* kind,
-           int nblocks, int64_t nnzb, int block, float scale, int32_t* err, cudaStream_t s) {
+           int nblocks, int64_t nnzb, int block, float scale, const Work& work, int32_t* err,
+           cudaStream_t s) {
   using C = FwdCfg<D>;
   CUtensorMap mq, mk, mv;
   int rc;
@@ -140,19 +155,23 @@ int fwd_tc(const TArg& q, const TArg& k, const TArg& v, const TArg& o, float* ls
   p.bs = block;
   p.n_tiles = (T + C::BM - 1) / C::BM;
   p.n_pairs = (p.n_tiles + 1) / 2;
+  p.work = work.items;
   p.scale_log2 = scale * 1.4426950408889634f;
   p.err = err;
   auto kern = smat_fwd_tc_kernel<D>;
   if ((rc = set_smem(kern, C::SMEM_BYTES))) return rc;
-  const int64_t grid = static_cast<int64_t>(p.n_pairs) * B * H;
+  const int64_t grid = static_cast<int64_t>(work.items ? work.n : p.n_pairs) * B * H;
+  if (grid == 0) return SMAT_OK;
   kern<<<static_cast<unsigned>(grid), C::THREADS, C::SMEM_BYTES, s>>>(mq, mk, mv, p);
   return launch_status();
 }
 
 SimtParams simt_params(int B, int H, int T, int block, float scale, const int32_t* indptr,
                        const int32_t* indices, const uint8_t* kind, int nblocks, int64_t nnzb,
-                       int32_t* err) {
+                       int32_t* err, const Work& work, int span_tiles) {
   SimtParams p{};
+  p.work = work.items;
+  p.span_tiles = span_tiles;
   p.B = B;
   p.H = H;
   p.T = T;
@@ -174,38 +193,47 @@ void set3(int64_t* dst, const TArg& t) {
 }
 
 template <template <int> class Launch>
-int dispatch_simt_d(int D, SimtParams& p, int T, int BH, cudaStream_t s) {
+int dispatch_simt_d(int D, SimtParams& p, int T, int n_work, int BH, cudaStream_t s) {
   switch (D) {
-    case 32: return Launch<32>::run(p, T, BH, s);
-    case 64: return Launch<64>::run(p, T, BH, s);
-    case 128: return Launch<128>::run(p, T, BH, s);
+    case 32: return Launch<32>::run(p, T, n_work, BH, s);
+    case 64: return Launch<64>::run(p, T, n_work, BH, s);
+    case 128: return Launch<128>::run(p, T, n_work, BH, s);
   }
   return SMAT_ERR_UNSUPPORTED_D;
 }
 
 template <int D>
 struct FwdSimt {
-  static int run(SimtParams& p, int T, int BH, cudaStream_t s) {
+  static int run(SimtParams& p, int T, int n_work, int BH, cudaStream_t s) {
     constexpr int RPC = 128 / (D / 32);
-    dim3 grid((T + RPC - 1) / RPC, BH);
+    const int64_t gx = p.work ? static_cast<int64_t>(n_work) * p.span_tiles * SIMT_TILE / RPC
+                              : (T + RPC - 1) / RPC;
+    if (gx == 0) return SMAT_OK;
+    dim3 grid(static_cast<unsigned>(gx), BH);
     smat_fwd_simt_kernel<D><<<grid, 128, 0, s>>>(p);
     return launch_status();
   }
 };
 template <int D>
 struct DqSimt {
-  static int run(SimtParams& p, int T, int BH, cudaStream_t s) {
+  static int run(SimtParams& p, int T, int n_work, int BH, cudaStream_t s) {
     constexpr int RPC = 128 / (D / 32);
-    dim3 grid((T + RPC - 1) / RPC, BH);
+    const int64_t gx = p.work ? static_cast<int64_t>(n_work) * p.span_tiles * SIMT_TILE / RPC
+                              : (T + RPC - 1) / RPC;
+    if (gx == 0) return SMAT_OK;
+    dim3 grid(static_cast<unsigned>(gx), BH);
     smat_dq_simt_kernel<D><<<grid, 128, 0, s>>>(p);
     return launch_status();
   }
 };
 template <int D>
 struct DkdvSimt {
-  static int run(SimtParams& p, int T, int BH, cudaStream_t s) {
+  static int run(SimtParams& p, int T, int n_work, int BH, cudaStream_t s) {
     constexpr int RPC = 128 / (D / 32);
-    dim3 grid((T + RPC - 1) / RPC, BH);
+    const int64_t gx = p.work ? static_cast<int64_t>(n_work) * p.span_tiles * SIMT_TILE / RPC
+                              : (T + RPC - 1) / RPC;
+    if (gx == 0) return SMAT_OK;
+    dim3 grid(static_cast<unsigned>(gx), BH);
     smat_dkdv_simt_kernel<D><<<grid, 128, 0, s>>>(p);
     return launch_status();
   }
@@ -216,7 +244,8 @@ template <bool DKDV, int D>
 int bwd_tc(const TArg& r0, const TArg& r1, const TArg& c0, const TArg& c1, const float* lse,
            const float* delta, const TArg& out0, const TArg* out1, int B, int H, int T,
            const int32_t* indptr, const int32_t* indices, const uint8_t* kind, int nblocks,
-           int64_t nnzb, int block, float scale, int32_t* err, cudaStream_t s) {
+           int64_t nnzb, int block, float scale, const Work& work, int32_t* err,
+           cudaStream_t s) {
   using C = BwdCfg<DKDV, D>;
   CUtensorMap m0, m1, mc0, mc1;
   int rc;
@@ -247,12 +276,14 @@ int bwd_tc(const TArg& r0, const TArg& r1, const TArg& c0, const TArg& c1, const
   p.nnzb = static_cast<int>(nnzb);
   p.bs = block;
   p.n_tiles = (T + C::BM - 1) / C::BM;
+  p.work = work.items;
   p.scale = scale;
   p.scale_log2 = scale * 1.4426950408889634f;
   p.err = err;
   auto kern = smat_bwd_tc_kernel<DKDV, D>;
   if ((rc = set_smem(kern, C::SMEM_BYTES))) return rc;
-  const int64_t grid = static_cast<int64_t>(p.n_tiles) * B * H;
+  const int64_t grid = static_cast<int64_t>(work.items ? work.n : p.n_tiles) * B * H;
+  if (grid == 0) return SMAT_OK;
   kern<<<static_cast<unsigned>(grid), C::THREADS, C::SMEM_BYTES, s>>>(m0, m1, mc0, mc1, p);
   return launch_status();
 }
@@ -262,7 +293,7 @@ int bwd_tc(const TArg& r0, const TArg& r1, const TArg& c0, const TArg& c1, const
 // ====================================================================== C ABI
 extern "C" {
 
-int smat_abi_version(void) { return 1; }
+int smat_abi_version(void) { return 2; }
 
 const char* smat_status_string(int status) {
   switch (status) {
@@ -375,15 +406,20 @@ int smat_layout_validate(int nblocks, int64_t nnzb, const int32_t* indptr, const
 }
 
 // ---------------------------------------------------------------- forward
-int smat_fwd(int dtype, const void* q, const int64_t* q_stride, const void* k,
+}  // extern "C"
+
+namespace {
+
+int fwd_impl(int dtype, const void* q, const int64_t* q_stride, const void* k,
              const int64_t* k_stride, const void* v, const int64_t* v_stride, void* o,
              const int64_t* o_stride, float* lse, int B, int H, int T, int D,
              const int32_t* indptr, const int32_t* indices, const uint8_t* kind, int nblocks,
-             int64_t nnzb, int block, int max_row, float scale, int32_t* err_word,
-             void* stream) {
+             int64_t nnzb, int block, int max_row, float scale, const Work& work,
+             int32_t* err_word, void* stream) {
   int rc;
   if (!q_stride || !k_stride || !v_stride || !o_stride) return SMAT_ERR_NULL_POINTER;
   if ((rc = check_common(dtype, B, H, T, D, nblocks, block))) return rc;
+  if ((rc = check_work(work))) return rc;
   const TArg tq = targ(q, q_stride), tk = targ(k, k_stride), tv = targ(v, v_stride),
              to = targ(o, o_stride);
   for (const TArg* t : {&tq, &tk, &tv, &to})
@@ -395,11 +431,12 @@ int smat_fwd(int dtype, const void* q, const int64_t* q_stride, const void* k,
   if (dtype == SMAT_DTYPE_BF16) {
     if (D == 64)
       return fwd_tc<64>(tq, tk, tv, to, lse, B, H, T, indptr, indices, kind, nblocks, nnzb, block,
-                        scale, err_word, s);
+                        scale, work, err_word, s);
     return fwd_tc<128>(tq, tk, tv, to, lse, B, H, T, indptr, indices, kind, nblocks, nnzb, block,
-                       scale, err_word, s);
+                       scale, work, err_word, s);
   }
-  SimtParams p = simt_params(B, H, T, block, scale, indptr, indices, kind, nblocks, nnzb, err_word);
+  SimtParams p = simt_params(B, H, T, block, scale, indptr, indices, kind, nblocks, nnzb, err_word,
+                             work, 2);
   p.q = static_cast<const float*>(q);
   p.k = static_cast<const float*>(k);
   p.v = static_cast<const float*>(v);
@@ -409,16 +446,17 @@ int smat_fwd(int dtype, const void* q, const int64_t* q_stride, const void* k,
   set3(p.k_s, tk);
   set3(p.v_s, tv);
   set3(p.out0_s, to);
-  return dispatch_simt_d<FwdSimt>(D, p, T, B * H, s);
+  return dispatch_simt_d<FwdSimt>(D, p, T, work.n, B * H, s);
 }
 
 // ---------------------------------------------------------------- backward
-int smat_bwd_preprocess(int dtype, const void* o, const int64_t* o_stride, const void* dout,
-                        const int64_t* do_stride, float* delta, int B, int H, int T, int D,
-                        void* stream) {
+int pre_impl(int dtype, const void* o, const int64_t* o_stride, const void* dout,
+             const int64_t* do_stride, float* delta, int B, int H, int T, int D, int row_lo,
+             int row_hi, void* stream) {
   int rc;
   if (!o_stride || !do_stride) return SMAT_ERR_NULL_POINTER;
   if ((rc = check_common(dtype, B, H, T, D, (T + 63) / 64, 64))) return rc;
+  if (row_lo < 0 || row_hi < row_lo || row_hi > T) return SMAT_ERR_BAD_SHAPE;
   const TArg to = targ(o, o_stride), td = targ(dout, do_stride);
   for (const TArg* t : {&to, &td})
     if ((rc = check_tensor(*t, dtype))) return rc;
@@ -427,8 +465,10 @@ int smat_bwd_preprocess(int dtype, const void* o, const int64_t* o_stride, const
                                   td.st % 4 || reinterpret_cast<uintptr_t>(o) % 16 ||
                                   reinterpret_cast<uintptr_t>(dout) % 16))
     return SMAT_ERR_BAD_ALIGNMENT;
+  const int n_rows = row_hi - row_lo;
+  if (n_rows == 0) return SMAT_OK;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  const int64_t rows = static_cast<int64_t>(B) * H * T;
+  const int64_t rows = static_cast<int64_t>(B) * H * n_rows;
   const int elem = dtype == SMAT_DTYPE_BF16 ? 2 : 4;
   const int lpr = D * elem / 16;
   const int64_t threads = rows * lpr;
@@ -436,7 +476,7 @@ int smat_bwd_preprocess(int dtype, const void* o, const int64_t* o_stride, const
 #define SMAT_PRE(TY, DD)                                                                        \
   smat_bwd_pre_kernel<TY, DD><<<grid, 256, 0, s>>>(                                            \
       static_cast<const TY*>(o), static_cast<const TY*>(dout), delta, to.sb, to.sh, to.st, td.sb, \
-      td.sh, td.st, H, T, rows)
+      td.sh, td.st, H, T, row_lo, n_rows, rows)
   if (dtype == SMAT_DTYPE_BF16) {
     if (D == 64) SMAT_PRE(__nv_bfloat16, 64);
     else SMAT_PRE(__nv_bfloat16, 128);
@@ -449,17 +489,20 @@ int smat_bwd_preprocess(int dtype, const void* o, const int64_t* o_stride, const
   return launch_status();
 }
 
-int smat_bwd_dkdv(int dtype, const void* q, const int64_t* q_stride, const void* k,
-                  const int64_t* k_stride, const void* v, const int64_t* v_stride,
-                  const void* dout, const int64_t* do_stride, const float* lse,
-                  const float* delta, void* dk, const int64_t* dk_stride, void* dv,
-                  const int64_t* dv_stride, int B, int H, int T, int D, const int32_t* t_indptr,
-                  const int32_t* t_indices, const uint8_t* t_kind, int nblocks, int64_t nnzb,
-                  int block, int t_max_row, float scale, int32_t* err_word, void* stream) {
+// launch == false runs the host-side checks only (smat_bwd checks all three
+// passes before it launches the first)
+int dkdv_impl(int dtype, const void* q, const int64_t* q_stride, const void* k,
+              const int64_t* k_stride, const void* v, const int64_t* v_stride, const void* dout,
+              const int64_t* do_stride, const float* lse, const float* delta, void* dk,
+              const int64_t* dk_stride, void* dv, const int64_t* dv_stride, int B, int H, int T,
+              int D, const int32_t* t_indptr, const int32_t* t_indices, const uint8_t* t_kind,
+              int nblocks, int64_t nnzb, int block, int t_max_row, float scale, const Work& work,
+              int32_t* err_word, void* stream, bool launch) {
   int rc;
   if (!q_stride || !k_stride || !v_stride || !do_stride || !dk_stride || !dv_stride)
     return SMAT_ERR_NULL_POINTER;
   if ((rc = check_common(dtype, B, H, T, D, nblocks, block))) return rc;
+  if ((rc = check_work(work))) return rc;
   const TArg tq = targ(q, q_stride), tk = targ(k, k_stride), tv = targ(v, v_stride),
              td = targ(dout, do_stride), tdk = targ(dk, dk_stride), tdv = targ(dv, dv_stride);
   for (const TArg* t : {&tq, &tk, &tv, &td, &tdk, &tdv})
@@ -467,16 +510,17 @@ int smat_bwd_dkdv(int dtype, const void* q, const int64_t* q_stride, const void*
   if (!lse || !delta) return SMAT_ERR_NULL_POINTER;
   if ((rc = check_layout_args(t_indptr, t_indices, t_kind, nnzb, t_max_row, block))) return rc;
   if (!std::isfinite(scale) || scale <= 0.f) return SMAT_ERR_BAD_SHAPE;
+  if (!launch) return SMAT_OK;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (dtype == SMAT_DTYPE_BF16) {
     if (D == 64)
       return bwd_tc<true, 64>(tk, tv, tq, td, lse, delta, tdk, &tdv, B, H, T, t_indptr, t_indices,
-                              t_kind, nblocks, nnzb, block, scale, err_word, s);
+                              t_kind, nblocks, nnzb, block, scale, work, err_word, s);
     return bwd_tc<true, 128>(tk, tv, tq, td, lse, delta, tdk, &tdv, B, H, T, t_indptr, t_indices,
-                             t_kind, nblocks, nnzb, block, scale, err_word, s);
+                             t_kind, nblocks, nnzb, block, scale, work, err_word, s);
   }
-  SimtParams p =
-      simt_params(B, H, T, block, scale, t_indptr, t_indices, t_kind, nblocks, nnzb, err_word);
+  SimtParams p = simt_params(B, H, T, block, scale, t_indptr, t_indices, t_kind, nblocks, nnzb,
+                             err_word, work, 1);
   p.q = static_cast<const float*>(q);
   p.k = static_cast<const float*>(k);
   p.v = static_cast<const float*>(v);
@@ -491,18 +535,20 @@ int smat_bwd_dkdv(int dtype, const void* q, const int64_t* q_stride, const void*
   set3(p.do_s, td);
   set3(p.out0_s, tdk);
   set3(p.out1_s, tdv);
-  return dispatch_simt_d<DkdvSimt>(D, p, T, B * H, s);
+  return dispatch_simt_d<DkdvSimt>(D, p, T, work.n, B * H, s);
 }
 
-int smat_bwd_dq(int dtype, const void* q, const int64_t* q_stride, const void* k,
-                const int64_t* k_stride, const void* v, const int64_t* v_stride, const void* dout,
-                const int64_t* do_stride, const float* lse, const float* delta, void* dq,
-                const int64_t* dq_stride, int B, int H, int T, int D, const int32_t* indptr,
-                const int32_t* indices, const uint8_t* kind, int nblocks, int64_t nnzb,
-                int block, int max_row, float scale, int32_t* err_word, void* stream) {
+int dq_impl(int dtype, const void* q, const int64_t* q_stride, const void* k,
+            const int64_t* k_stride, const void* v, const int64_t* v_stride, const void* dout,
+            const int64_t* do_stride, const float* lse, const float* delta, void* dq,
+            const int64_t* dq_stride, int B, int H, int T, int D, const int32_t* indptr,
+            const int32_t* indices, const uint8_t* kind, int nblocks, int64_t nnzb, int block,
+            int max_row, float scale, const Work& work, int32_t* err_word, void* stream,
+            bool launch) {
   int rc;
   if (!q_stride || !k_stride || !v_stride || !do_stride || !dq_stride) return SMAT_ERR_NULL_POINTER;
   if ((rc = check_common(dtype, B, H, T, D, nblocks, block))) return rc;
+  if ((rc = check_work(work))) return rc;
   const TArg tq = targ(q, q_stride), tk = targ(k, k_stride), tv = targ(v, v_stride),
              td = targ(dout, do_stride), tdq = targ(dq, dq_stride);
   for (const TArg* t : {&tq, &tk, &tv, &td, &tdq})
@@ -510,15 +556,17 @@ int smat_bwd_dq(int dtype, const void* q, const int64_t* q_stride, const void* k
   if (!lse || !delta) return SMAT_ERR_NULL_POINTER;
   if ((rc = check_layout_args(indptr, indices, kind, nnzb, max_row, block))) return rc;
   if (!std::isfinite(scale) || scale <= 0.f) return SMAT_ERR_BAD_SHAPE;
+  if (!launch) return SMAT_OK;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (dtype == SMAT_DTYPE_BF16) {
     if (D == 64)
       return bwd_tc<false, 64>(tq, td, tk, tv, lse, delta, tdq, nullptr, B, H, T, indptr, indices,
-                               kind, nblocks, nnzb, block, scale, err_word, s);
+                               kind, nblocks, nnzb, block, scale, work, err_word, s);
     return bwd_tc<false, 128>(tq, td, tk, tv, lse, delta, tdq, nullptr, B, H, T, indptr, indices,
-                              kind, nblocks, nnzb, block, scale, err_word, s);
+                              kind, nblocks, nnzb, block, scale, work, err_word, s);
   }
-  SimtParams p = simt_params(B, H, T, block, scale, indptr, indices, kind, nblocks, nnzb, err_word);
+  SimtParams p = simt_params(B, H, T, block, scale, indptr, indices, kind, nblocks, nnzb, err_word,
+                             work, 1);
   p.q = static_cast<const float*>(q);
   p.k = static_cast<const float*>(k);
   p.v = static_cast<const float*>(v);
@@ -531,7 +579,99 @@ int smat_bwd_dq(int dtype, const void* q, const int64_t* q_stride, const void* k
   set3(p.v_s, tv);
   set3(p.do_s, td);
   set3(p.out0_s, tdq);
-  return dispatch_simt_d<DqSimt>(D, p, T, B * H, s);
+  return dispatch_simt_d<DqSimt>(D, p, T, work.n, B * H, s);
+}
+
+}  // namespace
+
+extern "C" {
+
+int smat_fwd(int dtype, const void* q, const int64_t* q_stride, const void* k,
+             const int64_t* k_stride, const void* v, const int64_t* v_stride, void* o,
+             const int64_t* o_stride, float* lse, int B, int H, int T, int D,
+             const int32_t* indptr, const int32_t* indices, const uint8_t* kind, int nblocks,
+             int64_t nnzb, int block, int max_row, float scale, int32_t* err_word,
+             void* stream) {
+  return fwd_impl(dtype, q, q_stride, k, k_stride, v, v_stride, o, o_stride, lse, B, H, T, D,
+                  indptr, indices, kind, nblocks, nnzb, block, max_row, scale, kAllTiles,
+                  err_word, stream);
+}
+
+int smat_fwd_tiles(int dtype, const void* q, const int64_t* q_stride, const void* k,
+                   const int64_t* k_stride, const void* v, const int64_t* v_stride, void* o,
+                   const int64_t* o_stride, float* lse, int B, int H, int T, int D,
+                   const int32_t* indptr, const int32_t* indices, const uint8_t* kind,
+                   int nblocks, int64_t nnzb, int block, int max_row, float scale,
+                   const int32_t* work, int n_work, int32_t* err_word, void* stream) {
+  if (!work && n_work == 0) return SMAT_OK;
+  if (!work) return SMAT_ERR_NULL_POINTER;
+  return fwd_impl(dtype, q, q_stride, k, k_stride, v, v_stride, o, o_stride, lse, B, H, T, D,
+                  indptr, indices, kind, nblocks, nnzb, block, max_row, scale, Work{work, n_work},
+                  err_word, stream);
+}
+
+int smat_bwd_preprocess(int dtype, const void* o, const int64_t* o_stride, const void* dout,
+                        const int64_t* do_stride, float* delta, int B, int H, int T, int D,
+                        void* stream) {
+  return pre_impl(dtype, o, o_stride, dout, do_stride, delta, B, H, T, D, 0, T, stream);
+}
+
+int smat_bwd_preprocess_rows(int dtype, const void* o, const int64_t* o_stride, const void* dout,
+                             const int64_t* do_stride, float* delta, int B, int H, int T, int D,
+                             int row_lo, int row_hi, void* stream) {
+  return pre_impl(dtype, o, o_stride, dout, do_stride, delta, B, H, T, D, row_lo, row_hi, stream);
+}
+
+int smat_bwd_dkdv(int dtype, const void* q, const int64_t* q_stride, const void* k,
+                  const int64_t* k_stride, const void* v, const int64_t* v_stride,
+                  const void* dout, const int64_t* do_stride, const float* lse,
+                  const float* delta, void* dk, const int64_t* dk_stride, void* dv,
+                  const int64_t* dv_stride, int B, int H, int T, int D, const int32_t* t_indptr,
+                  const int32_t* t_indices, const uint8_t* t_kind, int nblocks, int64_t nnzb,
+                  int block, int t_max_row, float scale, int32_t* err_word, void* stream) {
+  return dkdv_impl(dtype, q, q_stride, k, k_stride, v, v_stride, dout, do_stride, lse, delta, dk,
+                   dk_stride, dv, dv_stride, B, H, T, D, t_indptr, t_indices, t_kind, nblocks,
+                   nnzb, block, t_max_row, scale, kAllTiles, err_word, stream, true);
+}
+
+int smat_bwd_dkdv_tiles(int dtype, const void* q, const int64_t* q_stride, const void* k,
+                        const int64_t* k_stride, const void* v, const int64_t* v_stride,
+                        const void* dout, const int64_t* do_stride, const float* lse,
+                        const float* delta, void* dk, const int64_t* dk_stride, void* dv,
+                        const int64_t* dv_stride, int B, int H, int T, int D,
+                        const int32_t* t_indptr, const int32_t* t_indices, const uint8_t* t_kind,
+                        int nblocks, int64_t nnzb, int block, int t_max_row, float scale,
+                        const int32_t* work, int n_work, int32_t* err_word, void* stream) {
+  if (!work && n_work == 0) return SMAT_OK;
+  if (!work) return SMAT_ERR_NULL_POINTER;
+  return dkdv_impl(dtype, q, q_stride, k, k_stride, v, v_stride, dout, do_stride, lse, delta, dk,
+                   dk_stride, dv, dv_stride, B, H, T, D, t_indptr, t_indices, t_kind, nblocks,
+                   nnzb, block, t_max_row, scale, Work{work, n_work}, err_word, stream, true);
+}
+
+int smat_bwd_dq(int dtype, const void* q, const int64_t* q_stride, const void* k,
+                const int64_t* k_stride, const void* v, const int64_t* v_stride, const void* dout,
+                const int64_t* do_stride, const float* lse, const float* delta, void* dq,
+                const int64_t* dq_stride, int B, int H, int T, int D, const int32_t* indptr,
+                const int32_t* indices, const uint8_t* kind, int nblocks, int64_t nnzb,
+                int block, int max_row, float scale, int32_t* err_word, void* stream) {
+  return dq_impl(dtype, q, q_stride, k, k_stride, v, v_stride, dout, do_stride, lse, delta, dq,
+                 dq_stride, B, H, T, D, indptr, indices, kind, nblocks, nnzb, block, max_row,
+                 scale, kAllTiles, err_word, stream, true);
+}
+
+int smat_bwd_dq_tiles(int dtype, const void* q, const int64_t* q_stride, const void* k,
+                      const int64_t* k_stride, const void* v, const int64_t* v_stride,
+                      const void* dout, const int64_t* do_stride, const float* lse,
+                      const float* delta, void* dq, const int64_t* dq_stride, int B, int H, int T,
+                      int D, const int32_t* indptr, const int32_t* indices, const uint8_t* kind,
+                      int nblocks, int64_t nnzb, int block, int max_row, float scale,
+                      const int32_t* work, int n_work, int32_t* err_word, void* stream) {
+  if (!work && n_work == 0) return SMAT_OK;
+  if (!work) return SMAT_ERR_NULL_POINTER;
+  return dq_impl(dtype, q, q_stride, k, k_stride, v, v_stride, dout, do_stride, lse, delta, dq,
+                 dq_stride, B, H, T, D, indptr, indices, kind, nblocks, nnzb, block, max_row,
+                 scale, Work{work, n_work}, err_word, stream, true);
 }
 
 int smat_bwd(int dtype, const void* q, const int64_t* q_stride, const void* k,
@@ -544,15 +684,23 @@ int smat_bwd(int dtype, const void* q, const int64_t* q_stride, const void* k,
              int nblocks, int64_t nnzb, int block, int max_row, int t_max_row, float scale,
              int32_t* err_word, void* stream) {
   int rc;
-  if ((rc = smat_bwd_preprocess(dtype, o, o_stride, dout, do_stride, delta, B, H, T, D, stream)))
-    return rc;
-  if ((rc = smat_bwd_dkdv(dtype, q, q_stride, k, k_stride, v, v_stride, dout, do_stride, lse,
-                          delta, dk, dk_stride, dv, dv_stride, B, H, T, D, t_indptr, t_indices,
-                          t_kind, nblocks, nnzb, block, t_max_row, scale, err_word, stream)))
-    return rc;
-  return smat_bwd_dq(dtype, q, q_stride, k, k_stride, v, v_stride, dout, do_stride, lse, delta,
-                     dq, dq_stride, B, H, T, D, indptr, indices, kind, nblocks, nnzb, block,
-                     max_row, scale, err_word, stream);
+  // every pass is checked before the first one launches
+  for (int pass = 0; pass < 2; ++pass) {
+    const bool launch = pass == 1;
+    if (launch && (rc = pre_impl(dtype, o, o_stride, dout, do_stride, delta, B, H, T, D, 0, T,
+                                 stream)))
+      return rc;
+    if ((rc = dkdv_impl(dtype, q, q_stride, k, k_stride, v, v_stride, dout, do_stride, lse, delta,
+                        dk, dk_stride, dv, dv_stride, B, H, T, D, t_indptr, t_indices, t_kind,
+                        nblocks, nnzb, block, t_max_row, scale, kAllTiles, err_word, stream,
+                        launch)))
+      return rc;
+    if ((rc = dq_impl(dtype, q, q_stride, k, k_stride, v, v_stride, dout, do_stride, lse, delta,
+                      dq, dq_stride, B, H, T, D, indptr, indices, kind, nblocks, nnzb, block,
+                      max_row, scale, kAllTiles, err_word, stream, launch)))
+      return rc;
+  }
+  return SMAT_OK;
 }
 
 }  // extern "C"

@@ -21,7 +21,7 @@ def declared_symbols():
 
 def test_header_symbols_exported():
     syms = declared_symbols()
-    assert len(syms) == 12
+    assert len(syms) == 16
     L = _lib.lib()
     for s in syms:
         assert hasattr(L, s), s
@@ -30,7 +30,7 @@ def test_header_symbols_exported():
 
 def test_version_and_status_strings():
     L = _lib.lib()
-    assert L.smat_abi_version() == 1
+    assert L.smat_abi_version() == 2
     assert L.smat_status_string(0) == b"ok"
     assert b"CSR" in L.smat_status_string(7)
     assert L.smat_status_string(999) == b"unknown status"
@@ -69,3 +69,39 @@ def test_bwd_rejects_on_host():
     args_bad[12] = bad
     assert L.smat_bwd_dq(*args_bad) == 6
     assert L.smat_bwd_preprocess(1, 16, st, 16, st, None, 1, 1, 128, 64, None) == 8
+
+
+def test_work_list_entry_points_reject_on_host():
+    L = _lib.lib()
+    st = (ctypes.c_int64 * 3)(4 * 1024 * 64, 1024 * 64, 64)
+    head = [1, 16, st, 16, st, 16, st, 16, st, 16, 1, 4, 1024, 64, 16, 16, 16, 16, 81, 64, 6,
+            0.125]
+    # an empty list is a no-op; a missing list or a negative count is an error
+    assert L.smat_fwd_tiles(*head, None, 0, None, None) == 0
+    assert L.smat_fwd_tiles(*head, None, 3, None, None) == 8
+    assert L.smat_fwd_tiles(*head, 16, -1, None, None) == 1
+    assert L.smat_fwd_tiles(*(head[:13] + [96] + head[14:]), 16, 1, None, None) == 2
+    bwd = [1, 16, st, 16, st, 16, st, 16, st, 16, 16, 16, st]
+    tail = [1, 4, 1024, 64, 16, 16, 16, 16, 81, 64, 6, 0.125]
+    assert L.smat_bwd_dq_tiles(*bwd, *tail, 16, -2, None, None) == 1
+    assert L.smat_bwd_dq_tiles(*bwd, *tail, None, 0, None, None) == 0
+    assert L.smat_bwd_dkdv_tiles(*bwd, 16, st, *tail, None, 4, None, None) == 8
+    # preprocess rows must lie inside [0, T]
+    assert L.smat_bwd_preprocess_rows(1, 16, st, 16, st, 16, 1, 4, 1024, 64, 0, 1025,
+                                      None) == 1
+    assert L.smat_bwd_preprocess_rows(1, 16, st, 16, st, 16, 1, 4, 1024, 64, 512, 256,
+                                      None) == 1
+    assert L.smat_bwd_preprocess_rows(1, 16, st, 16, st, 16, 1, 4, 1024, 64, 256, 256,
+                                      None) == 0
+
+
+def test_bwd_checks_every_pass_before_launching():
+    """A bad dQ stride is reported before the preprocess would launch (on this
+    GPU-less host a launch would fail with SMAT_ERR_LAUNCH instead)."""
+    L = _lib.lib()
+    st = (ctypes.c_int64 * 3)(0, 0, 64)
+    bad = (ctypes.c_int64 * 3)(0, 0, 60)
+    args = [1, 16, st, 16, st, 16, st, 16, st, 16, st, 16, 16,
+            16, bad, 16, st, 16, st, 1, 1, 128, 64, 16, 16, 16, 16, 16, 16,
+            2, 3, 64, 2, 2, 0.125, None, None]
+    assert L.smat_bwd(*args) == 6
