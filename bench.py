@@ -13,6 +13,14 @@ Multi-GPU (torchrun): every rank processes its own batch of the same shape
 value = N * F / max-over-ranks time.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
+    python bench.py --workload c5 [--shard heads|queries] ...   (long context)
+
+``--workload c5`` runs BASELINE config 5 (B=1, H=32, T=131072) with the
+total work fixed ("strong" scaling): ``--shard heads`` gives every rank
+H / N heads (no collective); ``--shard queries`` gives every rank a zig-zag
+share of the query tiles of every head, with the K/V exchange before the
+forward and the dK/dV return after the backward inside the timed step
+(smat_attention_b200.sharding).
 
 ``--impl reference`` times the reference's CPU dense-masked path (the oracle
 port in ``oracle/``) on this host's cores on a bounded sample of the same
@@ -37,8 +45,14 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 if ROOT not in sys.path:
     sys.path.insert(0, ROOT)
 
-WORKLOAD = dict(name="c3", B=4, H=32, T=16384, D=128, block=128, window=4, stride=8, sinks=2,
-                seed=2)
+WORKLOADS = {
+    "c3": dict(name="c3", B=4, H=32, T=16384, D=128, block=128, window=4, stride=8, sinks=2,
+               seed=2),
+    # long context: B=1 leaves 32 (b, h) pairs; sharded by heads or by query blocks
+    "c5": dict(name="c5", B=1, H=32, T=131072, D=128, block=128, window=8, stride=32, sinks=4,
+               seed=4),
+}
+WORKLOAD = dict(WORKLOADS["c3"])
 METRIC = "SMat attn fwd+bwd effective TFLOP/s (unmasked FLOPs)"
 UNIT = "TFLOP/s"
 
@@ -54,6 +68,11 @@ def _flops(pairs):
     w = WORKLOAD
     fwd = 4.0 * w["D"] * pairs * w["B"] * w["H"]
     return {"fwd": fwd, "dkdv": 2.0 * fwd, "dq": 1.5 * fwd, "step": 3.5 * fwd}
+
+
+def _tensor_mib():
+    w = WORKLOAD
+    return w["B"] * w["H"] * w["T"] * w["D"] * 2 // (1 << 20)
 
 
 def _peaks():
@@ -266,6 +285,12 @@ def run_gpu(args):
     device = torch.device("cuda", local)
     torch.cuda.set_device(device)
     w = WORKLOAD
+    strong = w["name"] == "c5"
+    if strong:
+        # total work fixed: this rank's share of the heads
+        if w["H"] % ws:
+            raise SystemExit(f"H={w['H']} does not split over {ws} ranks")
+        w["H"] //= ws
     spec, pairs = _layout_pairs()
     fl = _flops(pairs)
     scale = 1.0 / math.sqrt(w["D"])
@@ -358,14 +383,18 @@ def run_gpu(args):
         line = {
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": ws, "steps": K,
             "warmup": max(3, args.warmup), "ms_per_step": ms_step, "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "scaling": "strong" if strong else "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic",
             "config": {"workload": f"{w['name']}: B={w['B']} H={w['H']} T={w['T']} D={w['D']} "
                                    f"bs={w['block']} W={w['window']} S={w['stride']} "
                                    f"sinks={w['sinks']} fwd+bwd per rank",
-                       "global_batch": w["B"] * ws, "seq_len": w["T"], "heads": w["H"],
-                       "head_dim": w["D"], "parallelism": f"(batch,head) partition x{ws}",
-                       "l2": "inputs larger than L2 (512 MiB per tensor); no flush"},
-            "tokens_per_s": ws * w["B"] * w["T"] / (ms_step * 1e-3),
+                       "global_batch": w["B"] * (1 if strong else ws), "seq_len": w["T"],
+                       "heads": w["H"] * (ws if strong else 1), "head_dim": w["D"],
+                       "parallelism": (f"head partition x{ws}" if strong
+                                       else f"(batch,head) partition x{ws}"),
+                       "l2": f"inputs larger than L2 ({_tensor_mib()} MiB per tensor); "
+                             f"no flush"},
+            "tokens_per_s": (1 if strong else ws) * w["B"] * w["T"] / (ms_step * 1e-3),
             "frac_of_peak": value / ws / peaks["tflops"],
             "peak_source": peaks["source"],
             "per_kernel_ms": per_kernel,
@@ -388,6 +417,96 @@ def run_gpu(args):
         dist.destroy_process_group()
 
 
+def run_sharded(args):
+    """c5 with query-block sharding: every rank runs its zig-zag share of the
+    query tiles of all heads; the timed step includes both exchanges."""
+    from smat_attention_b200.attention import check_device_errors
+    from smat_attention_b200.mask import block_layout_stats, build_block_mask
+    from smat_attention_b200.sharding import (gather_kv, make_plan, reduce_dkdv, sharded_bwd,
+                                              sharded_fwd)
+    dist, rank, ws, local = _dist()
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    w = WORKLOAD
+    spec = build_block_mask(w["T"], w["block"], w["window"], w["stride"], w["sinks"])
+    pairs = block_layout_stats(spec)["pairs"]
+    fl = _flops(pairs)
+    plan = make_plan(spec, ws, rank)
+    scale = 1.0 / math.sqrt(w["D"])
+    shape = (w["B"], w["H"], w["T"], w["D"])
+    # the same global inputs on every rank; rows a rank does not own are
+    # zeroed so that what it reads of them arrives through the exchange
+    g = torch.Generator(device=device).manual_seed(w["seed"])
+    q, k, v, do = (torch.randn(*shape, generator=g, device=device, dtype=torch.bfloat16)
+                   for _ in range(4))
+    own = torch.from_numpy(plan.owned_row_mask()).to(device)
+    for x in (q, k, v, do):
+        x[:, :, ~own] = 0
+    o = torch.empty_like(q)
+    lse = torch.empty(w["B"], w["H"], w["T"], dtype=torch.float32, device=device)
+    stream = torch.cuda.current_stream(device)
+
+    def step(ev=None):
+        rec = (lambda i: ev[i].record(stream)) if ev else (lambda i: None)
+        rec(0)
+        if ws > 1:
+            gather_kv(plan, k, v)
+        rec(1)
+        sharded_fwd(plan, spec, q, k, v, scale, o=o, lse=lse, gather=False)
+        rec(2)
+        dq, dk, dv = sharded_bwd(plan, spec, q, k, v, o, lse, do, scale, reduce=False)
+        rec(3)
+        if ws > 1:
+            reduce_dkdv(plan, dk, dv)
+        rec(4)
+
+    for _ in range(max(3, args.warmup)):
+        step()
+    _barrier(dist, device)
+    K = args.steps
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(5)] for _ in range(K)]
+    clocks = ClockSampler(device)
+    _barrier(dist, device)
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record(stream)
+    for s in range(K):
+        step(evs[s])
+    stop.record(stream)
+    torch.cuda.synchronize(device)
+    clk = clocks.stop()
+    _barrier(dist, device)
+    names = ["kv_exchange", "fwd", "bwd", "dkdv_exchange"]
+    phases = {n: sum(evs[s][i].elapsed_time(evs[s][i + 1]) for s in range(K)) / K
+              for i, n in enumerate(names)}
+    phases_max = {n: _max_over_ranks(dist, t, device) for n, t in phases.items()}
+    ms_step = _max_over_ranks(dist, start.elapsed_time(stop) / K, device)
+    dev_err = check_device_errors(device)
+    value = fl["step"] / (ms_step * 1e-3) / 1e12
+    if rank == 0:
+        peaks = _peaks()
+        line = {
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": ws, "steps": K,
+            "warmup": max(3, args.warmup), "ms_per_step": ms_step, "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": f"{w['name']}: B={w['B']} H={w['H']} T={w['T']} D={w['D']} "
+                                   f"bs={w['block']} W={w['window']} S={w['stride']} "
+                                   f"sinks={w['sinks']} fwd+bwd, whole job",
+                       "global_batch": w["B"], "seq_len": w["T"], "heads": w["H"],
+                       "head_dim": w["D"], "parallelism": f"query-block shards x{ws} (zig-zag)",
+                       "l2": f"inputs larger than L2 ({_tensor_mib()} MiB per tensor); "
+                             f"no flush"},
+            "tokens_per_s": w["B"] * w["T"] / (ms_step * 1e-3),
+            "frac_of_peak": value / ws / peaks["tflops"], "peak_source": peaks["source"],
+            "phase_ms_max_over_ranks": phases_max,
+            "kv_rows_received_rank0": int(sum(r.size for r in plan.recv_rows)),
+            "gpu_launches": K * (3 + len(plan.runs)),
+            "device_errors": dev_err, "clocks": clk,
+        }
+        print(json.dumps(line), flush=True)
+    if dist is not None:
+        dist.destroy_process_group()
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -400,13 +519,24 @@ def main():
     ap.add_argument("--batch", type=int, default=None,
                     help="override B (smaller cases for ncu captures)")
     ap.add_argument("--heads", type=int, default=None, help="override H")
+    ap.add_argument("--workload", default="c3", choices=sorted(WORKLOADS))
+    ap.add_argument("--shard", default="heads", choices=["heads", "queries"],
+                    help="c5 only: split the heads, or the query blocks, over the ranks")
     args = ap.parse_args()
+    WORKLOAD.clear()
+    WORKLOAD.update(WORKLOADS[args.workload])
+    if args.workload == "c5":
+        # the host-buffer leg and the CPU sample are taken on the default workload
+        args.no_e2e = True
+        args.no_cpu_baseline = True
     if args.batch:
         WORKLOAD["B"] = args.batch
     if args.heads:
         WORKLOAD["H"] = args.heads
     if args.impl == "reference":
         run_reference(args)
+    elif args.workload == "c5" and args.shard == "queries":
+        run_sharded(args)
     else:
         run_gpu(args)
 

@@ -92,7 +92,7 @@ __device__ __forceinline__ void mbar_wait_drain(uint32_t bar, uint32_t parity) {
 }
 
 // ---------------------------------------------------------------- TMA
-// Plain (non-multicast) 4-D tile load global -> this CTA's shared memory,
+// Plain 4-D tile load global -> this CTA's shared memory only,
 // completion signalled on `bar` through the transaction count.
 __device__ __forceinline__ void tma_load_4d(uint32_t dst, const CUtensorMap* map, uint32_t bar,
                                             int c0, int c1, int c2, int c3) {
