@@ -422,8 +422,7 @@ def run_sharded(args):
     query tiles of all heads; the timed step includes both exchanges."""
     from smat_attention_b200.attention import check_device_errors
     from smat_attention_b200.mask import block_layout_stats, build_block_mask
-    from smat_attention_b200.sharding import (gather_kv, make_plan, reduce_dkdv, sharded_bwd,
-                                              sharded_fwd)
+    from smat_attention_b200.sharding import make_plan, sharded_bwd, sharded_fwd
     dist, rank, ws, local = _dist()
     device = torch.device("cuda", local)
     torch.cuda.set_device(device)
@@ -446,25 +445,21 @@ def run_sharded(args):
     lse = torch.empty(w["B"], w["H"], w["T"], dtype=torch.float32, device=device)
     stream = torch.cuda.current_stream(device)
 
+    groups = args.kv_groups
+
     def step(ev=None):
         rec = (lambda i: ev[i].record(stream)) if ev else (lambda i: None)
         rec(0)
-        if ws > 1:
-            gather_kv(plan, k, v)
+        sharded_fwd(plan, spec, q, k, v, scale, o=o, lse=lse, groups=groups)
         rec(1)
-        sharded_fwd(plan, spec, q, k, v, scale, o=o, lse=lse, gather=False)
+        sharded_bwd(plan, spec, q, k, v, o, lse, do, scale, overlap=not args.no_overlap)
         rec(2)
-        dq, dk, dv = sharded_bwd(plan, spec, q, k, v, o, lse, do, scale, reduce=False)
-        rec(3)
-        if ws > 1:
-            reduce_dkdv(plan, dk, dv)
-        rec(4)
 
     for _ in range(max(3, args.warmup)):
         step()
     _barrier(dist, device)
     K = args.steps
-    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(5)] for _ in range(K)]
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(K)]
     clocks = ClockSampler(device)
     _barrier(dist, device)
     start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -475,7 +470,7 @@ def run_sharded(args):
     torch.cuda.synchronize(device)
     clk = clocks.stop()
     _barrier(dist, device)
-    names = ["kv_exchange", "fwd", "bwd", "dkdv_exchange"]
+    names = ["fwd_with_kv_exchange", "bwd_with_dkdv_return"]
     phases = {n: sum(evs[s][i].elapsed_time(evs[s][i + 1]) for s in range(K)) / K
               for i, n in enumerate(names)}
     phases_max = {n: _max_over_ranks(dist, t, device) for n, t in phases.items()}
@@ -492,14 +487,17 @@ def run_sharded(args):
                                    f"bs={w['block']} W={w['window']} S={w['stride']} "
                                    f"sinks={w['sinks']} fwd+bwd, whole job",
                        "global_batch": w["B"], "seq_len": w["T"], "heads": w["H"],
-                       "head_dim": w["D"], "parallelism": f"query-block shards x{ws} (zig-zag)",
+                       "head_dim": w["D"], "parallelism": f"query-block shards x{ws} (zig-zag"
+                                      + f", kv groups {args.kv_groups}, dK/dV return "
+                                      + ("after dQ)" if args.no_overlap else "beside dQ)"),
                        "l2": f"inputs larger than L2 ({_tensor_mib()} MiB per tensor); "
                              f"no flush"},
             "tokens_per_s": w["B"] * w["T"] / (ms_step * 1e-3),
             "frac_of_peak": value / ws / peaks["tflops"], "peak_source": peaks["source"],
             "phase_ms_max_over_ranks": phases_max,
             "kv_rows_received_rank0": int(sum(r.size for r in plan.recv_rows)),
-            "gpu_launches": K * (3 + len(plan.runs)),
+            "gpu_launches": K * ((3 + len(plan.runs)) if ws == 1 else
+                                 (groups + 2 + len(plan.runs) + 2 * groups + 2)),
             "device_errors": dev_err, "clocks": clk,
         }
         print(json.dumps(line), flush=True)
@@ -520,6 +518,10 @@ def main():
                     help="override B (smaller cases for ncu captures)")
     ap.add_argument("--heads", type=int, default=None, help="override H")
     ap.add_argument("--workload", default="c3", choices=sorted(WORKLOADS))
+    ap.add_argument("--no-overlap", action="store_true",
+                    help="c5 --shard queries: run the dK/dV return after dQ, not beside it")
+    ap.add_argument("--kv-groups", type=int, default=1,
+                    help="c5 --shard queries: head groups of the K/V exchange / forward")
     ap.add_argument("--shard", default="heads", choices=["heads", "queries"],
                     help="c5 only: split the heads, or the query blocks, over the ranks")
     args = ap.parse_args()

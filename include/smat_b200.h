@@ -160,6 +160,37 @@ SMAT_API int smat_fwd_tiles(int dtype,
                    float scale, const int32_t* work, int n_work,
                    int32_t* err_word, void* stream);
 
+/* ---------------------------------------------------------------- row exchange
+ * Copies of listed token rows between two [B, H, T, D] tensors (a: K or dK,
+ * b: V or dV, element strides as elsewhere) and a contiguous wire buffer, for
+ * the GPU-to-GPU exchanges of the query-sharded path.  Wire row r holds
+ * [2][B][H][D] elements: a[.., rows[r], :] then b[.., rows[r], :].  `rows`
+ * (int64, n_rows entries) and the contribution lists are DEVICE arrays; a row
+ * outside [0, T) or a contribution outside [0, n_wire) sets
+ * SMAT_DEVERR_BAD_WORK and is skipped.  D * element size must be a multiple
+ * of 16 bytes and bases / strides 16-byte aligned.  No reference counterpart
+ * (the reference has no multi-GPU path).
+ *
+ * smat_rows_pack:       wire[r] = (a, b)[rows[r]]
+ * smat_rows_unpack:     (a, b)[rows[r]] = wire[r]
+ * smat_rows_accumulate: (a, b)[rows[e]] += sum over c in
+ *                       [contrib_ptr[e], contrib_ptr[e+1]) of wire[contrib_wire[c]],
+ *                       in fp32, in list order, rounded once. */
+SMAT_API int smat_rows_pack(int dtype, const void* a, const int64_t* a_stride,
+                   const void* b, const int64_t* b_stride, int B, int H, int T, int D,
+                   const int64_t* rows, int64_t n_rows, void* wire,
+                   int32_t* err_word, void* stream);
+SMAT_API int smat_rows_unpack(int dtype, void* a, const int64_t* a_stride,
+                     void* b, const int64_t* b_stride, int B, int H, int T, int D,
+                     const int64_t* rows, int64_t n_rows, const void* wire,
+                     int32_t* err_word, void* stream);
+SMAT_API int smat_rows_accumulate(int dtype, void* a, const int64_t* a_stride,
+                         void* b, const int64_t* b_stride, int B, int H, int T, int D,
+                         const int64_t* rows, int64_t n_rows,
+                         const int32_t* contrib_ptr, const int64_t* contrib_wire,
+                         int64_t n_wire, const void* wire,
+                         int32_t* err_word, void* stream);
+
 /* ---------------------------------------------------------------- backward
  * delta[b, h, t] = sum_d dO[b,h,t,d] * o[b,h,t,d]
  * (the row-sum preprocess of the reference's backward,

@@ -42,6 +42,12 @@ SIGNATURES = {
     "smat_fwd_tiles": (_c_int, [_c_int, _vp, _i64p, _vp, _i64p, _vp, _i64p, _vp, _i64p, _vp,
                                 _c_int, _c_int, _c_int, _c_int, _vp, _vp, _vp,
                                 _c_int, _c_i64, _c_int, _c_int, _c_f, _vp, _c_int, _vp, _vp]),
+    "smat_rows_pack": (_c_int, [_c_int, _vp, _i64p, _vp, _i64p, _c_int, _c_int, _c_int,
+                                _c_int, _vp, _c_i64, _vp, _vp, _vp]),
+    "smat_rows_unpack": (_c_int, [_c_int, _vp, _i64p, _vp, _i64p, _c_int, _c_int, _c_int,
+                                  _c_int, _vp, _c_i64, _vp, _vp, _vp]),
+    "smat_rows_accumulate": (_c_int, [_c_int, _vp, _i64p, _vp, _i64p, _c_int, _c_int, _c_int,
+                                      _c_int, _vp, _c_i64, _vp, _vp, _c_i64, _vp, _vp, _vp]),
     "smat_bwd_preprocess": (_c_int, [_c_int, _vp, _i64p, _vp, _i64p, _vp,
                                      _c_int, _c_int, _c_int, _c_int, _vp]),
     "smat_bwd_preprocess_rows": (_c_int, [_c_int, _vp, _i64p, _vp, _i64p, _vp,

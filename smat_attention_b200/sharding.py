@@ -19,9 +19,15 @@ plan on the host without communication:
 * backward: dK / dV of a key block is a sum over the query blocks reading it.
   Each rank runs the dK/dV kernel over the transposed CSR filtered to its own
   query blocks, for every key tile that filter leaves non-empty, and so holds
-  partial sums for the blocks it imported.  The reverse all-to-all (fp32)
-  returns those partials to the owners, which add them to their own
+  partial sums for the blocks it imported.  The reverse all-to-all returns
+  those partials to the owners, which add them to their own in fp32
   (:func:`reduce_dkdv`).  dQ needs no exchange.
+
+Both exchanges are a pack kernel, one NCCL ``all_to_all_single`` and an
+unpack (or fp32 accumulate) kernel (csrc/rows.cu), run on a side stream:
+the K/V exchange can go head group by head group so that the forward of
+one group overlaps the exchange of the next, and the dK/dV return overlaps
+the dQ pass, which does not touch dK / dV.
 
 Tensors stay full length (``[B, H, T, D]``) on every rank; only the owned
 rows of q, k, v and dO need to be valid on input, and only the owned rows of
@@ -41,7 +47,7 @@ from . import _lib
 from .mask import MaskSpec
 
 __all__ = ["ShardPlan", "make_plan", "make_plans", "zigzag_tile_owner", "gather_kv",
-           "reduce_dkdv", "sharded_fwd", "sharded_bwd", "owned_rows"]
+           "reduce_dkdv", "sharded_fwd", "sharded_bwd", "owned_rows", "CudaRowOps"]
 
 TILE = _lib.TILE_ROWS
 
@@ -122,15 +128,21 @@ class ShardPlan:
             "t_indices": as_t(self.t_indices, np.int32),
             "t_kind": as_t(self.t_kind, np.uint8),
         }
-        # exchange rows, and for the backward the position of every sent row
-        # in the sorted union of sent rows (partials from several peers for
-        # one row are summed there)
-        exp = np.unique(np.concatenate([r for r in self.send_rows] + [np.zeros(0, np.int64)]))
+        # exchange lists: rows packed for the peers (peer order), rows the
+        # peers' data lands on, and for the return the union of sent rows
+        # with, per row, the received wire rows that hold its partials
+        cat = lambda xs: np.concatenate(list(xs) + [np.zeros(0, np.int64)]).astype(np.int64)
+        send_cat, recv_cat = cat(self.send_rows), cat(self.recv_rows)
+        exp = np.unique(send_cat)
+        slot = np.searchsorted(exp, send_cat)
+        order = np.argsort(slot, kind="stable")
+        ptr = np.zeros(exp.size + 1, dtype=np.int64)
+        np.cumsum(np.bincount(slot, minlength=exp.size), out=ptr[1:])
+        d["send_cat"] = as_t(send_cat, np.int64)
+        d["recv_cat"] = as_t(recv_cat, np.int64)
         d["exp_rows"] = as_t(exp, np.int64)
-        for o in range(self.world):
-            d[f"send{o}"] = as_t(self.send_rows[o], np.int64)
-            d[f"send_idx{o}"] = as_t(np.searchsorted(exp, self.send_rows[o]), np.int64)
-            d[f"recv{o}"] = as_t(self.recv_rows[o], np.int64)
+        d["contrib_ptr"] = as_t(ptr, np.int32)
+        d["contrib_wire"] = as_t(order, np.int64)
         self.dev[key] = d
         return d
 
@@ -225,60 +237,93 @@ def owned_rows(plan: ShardPlan) -> np.ndarray:
 
 # --------------------------------------------------------------------------- collectives
 
-def _exchange(send_chunks, recv_counts, like, group):
-    """All-to-all of per-peer chunks (each a tensor of ``like``'s dtype);
-    returns the received chunks as flat views, one per peer."""
-    flat = torch.cat([c.reshape(-1) for c in send_chunks]) if send_chunks else \
-        torch.zeros(0, dtype=like.dtype, device=like.device)
-    recv = torch.empty(sum(recv_counts), dtype=flat.dtype, device=flat.device)
-    torch.distributed.all_to_all_single(recv, flat, output_split_sizes=list(recv_counts),
-                                        input_split_sizes=[c.numel() for c in send_chunks],
+class CudaRowOps:
+    """The row exchange kernels of libsmat_b200 (csrc/rows.cu): pack listed
+    rows of two [B, H, T, D] tensors into a flat wire buffer, unpack, and
+    add wire rows into rows in fp32."""
+
+    @staticmethod
+    def _args(a, b, rows):
+        from .attention import _DTYPES
+        if not (a.is_cuda and b.is_cuda and rows.is_cuda):
+            raise ValueError("the row exchange runs on CUDA tensors only (no CPU path)")
+        B, H, T, D = a.shape
+        return (_DTYPES[a.dtype], a.data_ptr(), _lib.strides3(a), b.data_ptr(),
+                _lib.strides3(b), B, H, T, D, rows.data_ptr(), rows.numel())
+
+    @staticmethod
+    def _tail(a):
+        from .attention import _err_word
+        return _err_word(a.device).data_ptr(), torch.cuda.current_stream(a.device).cuda_stream
+
+    def pack(self, a, b, rows, wire):
+        _lib.check("smat_rows_pack", _lib.lib().smat_rows_pack(
+            *self._args(a, b, rows), wire.data_ptr(), *self._tail(a)))
+
+    def unpack(self, a, b, rows, wire):
+        _lib.check("smat_rows_unpack", _lib.lib().smat_rows_unpack(
+            *self._args(a, b, rows), wire.data_ptr(), *self._tail(a)))
+
+    def accumulate(self, a, b, rows, contrib_ptr, contrib_wire, wire, n_wire):
+        _lib.check("smat_rows_accumulate", _lib.lib().smat_rows_accumulate(
+            *self._args(a, b, rows), contrib_ptr.data_ptr(), contrib_wire.data_ptr(), n_wire,
+            wire.data_ptr(), *self._tail(a)))
+
+
+def _a2a(recv, send, recv_counts, send_counts, per_row, group):
+    torch.distributed.all_to_all_single(recv, send,
+                                        output_split_sizes=[c * per_row for c in recv_counts],
+                                        input_split_sizes=[c * per_row for c in send_counts],
                                         group=group)
-    return list(torch.split(recv, list(recv_counts)))
 
 
-def gather_kv(plan: ShardPlan, k: torch.Tensor, v: torch.Tensor, group=None) -> None:
-    """Fill the rows of ``k`` and ``v`` (full-length ``[B, H, T, D]``) that
-    this rank reads but does not own, from their owners: one all-to-all that
-    carries exactly the blocks each reader needs.  Every rank of ``group``
-    must call it."""
+def gather_kv(plan: ShardPlan, k: torch.Tensor, v: torch.Tensor, group=None, ops=None) -> None:
+    """Fill the rows of ``k`` and ``v`` (``[B, H, T, D]``, full length; a
+    head or batch sub-view is fine) that this rank reads but does not own,
+    from their owners: pack, one all-to-all that carries exactly the blocks
+    each reader needs, unpack.  Every rank of ``group`` must call it with the
+    same shapes, on its current stream."""
+    ops = ops or CudaRowOps()
+    if isinstance(ops, CudaRowOps) and not (k.is_cuda and v.is_cuda):
+        raise ValueError("the row exchange runs on CUDA tensors only (no CPU path)")
     B, H, T, D = k.shape
     d = plan.device(k.device)
-    chunks = [torch.stack((k.index_select(2, d[f"send{o}"]), v.index_select(2, d[f"send{o}"])))
-              for o in range(plan.world)]
     per_row = 2 * B * H * D
-    got = _exchange(chunks, [per_row * r.size for r in plan.recv_rows], k, group)
-    for o in range(plan.world):
-        n = plan.recv_rows[o].size
-        if n:
-            c = got[o].view(2, B, H, n, D)
-            k.index_copy_(2, d[f"recv{o}"], c[0])
-            v.index_copy_(2, d[f"recv{o}"], c[1])
+    sc = [r.size for r in plan.send_rows]
+    rc = [r.size for r in plan.recv_rows]
+    send = torch.empty(sum(sc) * per_row, dtype=k.dtype, device=k.device)
+    recv = torch.empty(sum(rc) * per_row, dtype=k.dtype, device=k.device)
+    if send.numel():
+        ops.pack(k, v, d["send_cat"], send)
+    _a2a(recv, send, rc, sc, per_row, group)
+    if recv.numel():
+        ops.unpack(k, v, d["recv_cat"], recv)
 
 
-def reduce_dkdv(plan: ShardPlan, dk: torch.Tensor, dv: torch.Tensor, group=None) -> None:
+def reduce_dkdv(plan: ShardPlan, dk: torch.Tensor, dv: torch.Tensor, group=None,
+                ops=None) -> None:
     """Return the partial dK / dV this rank holds for the blocks it imported
-    to their owners, and add the partials it receives for its own blocks
-    (summed in fp32, rounded once): the reverse all-to-all of
-    :func:`gather_kv`."""
+    to their owners, and add the partials it receives for its own blocks:
+    the reverse all-to-all of :func:`gather_kv`.  Partials travel in the
+    tensors' dtype (the kernels' bf16 partials are exact there) and are
+    summed in fp32 at the owner, own partial first, then the peers' in rank
+    order, and rounded once."""
+    ops = ops or CudaRowOps()
+    if isinstance(ops, CudaRowOps) and not (dk.is_cuda and dv.is_cuda):
+        raise ValueError("the row exchange runs on CUDA tensors only (no CPU path)")
     B, H, T, D = dk.shape
     d = plan.device(dk.device)
-    chunks = [torch.stack((dk.index_select(2, d[f"recv{o}"]),
-                           dv.index_select(2, d[f"recv{o}"]))).float()
-              for o in range(plan.world)]
     per_row = 2 * B * H * D
-    got = _exchange(chunks, [per_row * r.size for r in plan.send_rows],
-                    torch.empty(0, dtype=torch.float32, device=dk.device), group)
-    exp = d["exp_rows"]
-    if exp.numel() == 0:
-        return
-    acc = torch.stack((dk.index_select(2, exp), dv.index_select(2, exp))).float()
-    for o in range(plan.world):
-        n = plan.send_rows[o].size
-        if n:
-            acc.index_add_(3, d[f"send_idx{o}"], got[o].view(2, B, H, n, D))
-    dk.index_copy_(2, exp, acc[0].to(dk.dtype))
-    dv.index_copy_(2, exp, acc[1].to(dv.dtype))
+    sc = [r.size for r in plan.recv_rows]      # partials go back to the owners
+    rc = [r.size for r in plan.send_rows]
+    send = torch.empty(sum(sc) * per_row, dtype=dk.dtype, device=dk.device)
+    recv = torch.empty(sum(rc) * per_row, dtype=dk.dtype, device=dk.device)
+    if send.numel():
+        ops.pack(dk, dv, d["recv_cat"], send)
+    _a2a(recv, send, rc, sc, per_row, group)
+    if d["exp_rows"].numel():
+        ops.accumulate(dk, dv, d["exp_rows"], d["contrib_ptr"], d["contrib_wire"], recv,
+                       sum(rc))
 
 
 # --------------------------------------------------------------------------- compute
@@ -292,12 +337,53 @@ def _stream(t: torch.Tensor):
     return torch.cuda.current_stream(t.device).cuda_stream
 
 
+_SIDE: Dict[str, "torch.cuda.Stream"] = {}
+
+
+def _side_stream(device) -> "torch.cuda.Stream":
+    key = str(torch.device(device))
+    s = _SIDE.get(key)
+    if s is None:
+        s = torch.cuda.Stream(device=device)
+        _SIDE[key] = s
+    return s
+
+
+def _groups(B: int, H: int, n: int) -> List[Tuple[slice, slice]]:
+    """(batch, head) slices for ``n`` exchange groups: heads when B == 1, else
+    batches (an [B, H, T] lse / delta slice must stay one contiguous range)."""
+    if B == 1:
+        n = max(1, min(n, H))
+        cut = [H * i // n for i in range(n + 1)]
+        return [(slice(0, 1), slice(cut[i], cut[i + 1])) for i in range(n)]
+    n = max(1, min(n, B))
+    cut = [B * i // n for i in range(n + 1)]
+    return [(slice(cut[i], cut[i + 1]), slice(0, H)) for i in range(n)]
+
+
+def _fwd_launch(plan, lay, d, q, k, v, o, lse, scale):
+    from .attention import _DTYPES, _err_word
+    B, H, T, D = q.shape
+    w = d["fwd_work"]
+    _lib.check("smat_fwd_tiles", _lib.lib().smat_fwd_tiles(
+        _DTYPES[q.dtype], q.data_ptr(), _lib.strides3(q), k.data_ptr(), _lib.strides3(k),
+        v.data_ptr(), _lib.strides3(v), o.data_ptr(), _lib.strides3(o), lse.data_ptr(),
+        B, H, T, D, lay["indptr"].data_ptr(), lay["indices"].data_ptr(), lay["kind"].data_ptr(),
+        lay["nblocks"], lay["nnzb"], lay["block"], lay["max_row"], float(scale),
+        w.data_ptr(), w.numel(), _err_word(q.device).data_ptr(), _stream(q)))
+
+
 def sharded_fwd(plan: ShardPlan, spec: MaskSpec, q, k, v, scale: float, *, o=None, lse=None,
-                group=None, gather: bool = True):
-    """This rank's forward: gather the imported K/V rows (unless ``gather``
-    is False), then O and LSE of the owned query tiles.  Returns ``(o, lse)``
-    (full length; owned rows defined)."""
-    from .attention import _DTYPES, _err_word, _prep
+                group=None, gather: bool = True, groups: int = 1, ops=None):
+    """This rank's forward: bring in the imported K/V rows (unless
+    ``gather`` is False), then O and LSE of the owned query tiles.  With
+    ``groups`` > 1 the exchange runs group by group (heads, or batches when
+    B > 1) on a side stream and the forward of a group starts as soon as its
+    rows have landed (on B200 at c5 / 2 GPUs one group measured faster: the
+    split forward launches lose more to wave tails than the overlap saves).
+    Returns ``(o, lse)`` (full length; owned rows defined).  ``k`` and ``v``
+    are filled in place."""
+    from .attention import _prep
     q = _prep(q, "q")
     kp, vp = _prep(k, "k"), _prep(v, "v")
     if kp is not k or vp is not v:
@@ -306,32 +392,39 @@ def sharded_fwd(plan: ShardPlan, spec: MaskSpec, q, k, v, scale: float, *, o=Non
     B, H, T, D = q.shape
     if k.shape != q.shape or v.shape != q.shape or T != plan.T:
         raise ValueError("q, k, v must have the same [B, H, T, D] shape with T = plan.T")
-    if gather and plan.world > 1:
-        gather_kv(plan, k, v, group)
     lay = _layout(spec, q.device)
     d = plan.device(q.device)
     if o is None:
         o = torch.empty_like(q)
     if lse is None:
         lse = torch.empty(B, H, T, dtype=torch.float32, device=q.device)
-    L = _lib.lib()
-    w = d["fwd_work"]
-    _lib.check("smat_fwd_tiles", L.smat_fwd_tiles(
-        _DTYPES[q.dtype], q.data_ptr(), _lib.strides3(q), k.data_ptr(), _lib.strides3(k),
-        v.data_ptr(), _lib.strides3(v), o.data_ptr(), _lib.strides3(o), lse.data_ptr(),
-        B, H, T, D, lay["indptr"].data_ptr(), lay["indices"].data_ptr(), lay["kind"].data_ptr(),
-        lay["nblocks"], lay["nnzb"], lay["block"], lay["max_row"], float(scale),
-        w.data_ptr(), w.numel(), _err_word(q.device).data_ptr(), _stream(q)))
+    if not gather or plan.world == 1:
+        _fwd_launch(plan, lay, d, q, k, v, o, lse, scale)
+        return o, lse
+    main = torch.cuda.current_stream(q.device)
+    side = _side_stream(q.device)
+    side.wait_stream(main)                       # K / V (owned rows) are ready
+    ready = []
+    with torch.cuda.stream(side):
+        for bs, hs in _groups(B, H, groups):
+            gather_kv(plan, k[bs, hs], v[bs, hs], group, ops)
+            ev = torch.cuda.Event()
+            ev.record(side)
+            ready.append((bs, hs, ev))
+    for bs, hs, ev in ready:
+        main.wait_event(ev)
+        _fwd_launch(plan, lay, d, q[bs, hs], k[bs, hs], v[bs, hs], o[bs, hs], lse[bs, hs], scale)
     return o, lse
 
 
 def sharded_bwd(plan: ShardPlan, spec: MaskSpec, q, k, v, o, lse, do, scale: float, *,
-                group=None, reduce: bool = True):
+                group=None, reduce: bool = True, overlap: bool = True, ops=None):
     """This rank's backward: delta of the owned rows, dK/dV partials over the
-    filtered transposed CSR, dQ of the owned tiles, then (unless ``reduce``
-    is False) the dK/dV reduce-scatter.  ``k`` and ``v`` must already hold
-    the imported rows (as left by :func:`sharded_fwd`).  Returns
-    ``(dq, dk, dv)`` (full length; owned rows defined)."""
+    filtered transposed CSR, dQ of the owned tiles, and (unless ``reduce`` is
+    False) the dK/dV return, which with ``overlap`` runs on a side stream
+    while the dQ pass runs.  ``k`` and ``v`` must already hold the imported
+    rows (as left by :func:`sharded_fwd`).  Returns ``(dq, dk, dv)`` (full
+    length; owned rows defined)."""
     from .attention import _DTYPES, _err_word, _prep
     q, k, v, o, do = (_prep(x, n) for x, n in ((q, "q"), (k, "k"), (v, "v"), (o, "o"),
                                                (do, "do")))
@@ -357,6 +450,13 @@ def sharded_bwd(plan: ShardPlan, spec: MaskSpec, q, k, v, o, lse, do, scale: flo
         d["t_indptr"].data_ptr(), d["t_indices"].data_ptr(), d["t_kind"].data_ptr(),
         lay["nblocks"], int(d["t_indices"].numel()), lay["block"], plan.t_max_row,
         float(scale), wk.data_ptr(), wk.numel(), err, s))
+    exchange = reduce and plan.world > 1
+    main = torch.cuda.current_stream(q.device)
+    side = _side_stream(q.device) if exchange and overlap else None
+    if side is not None:
+        side.wait_stream(main)                   # the partials are written
+        with torch.cuda.stream(side):
+            reduce_dkdv(plan, dk, dv, group, ops)
     wq = d["dq_work"]
     _lib.check("smat_bwd_dq_tiles", L.smat_bwd_dq_tiles(
         dt, q.data_ptr(), _lib.strides3(q), k.data_ptr(), _lib.strides3(k),
@@ -365,6 +465,8 @@ def sharded_bwd(plan: ShardPlan, spec: MaskSpec, q, k, v, o, lse, do, scale: flo
         lay["indptr"].data_ptr(), lay["indices"].data_ptr(), lay["kind"].data_ptr(),
         lay["nblocks"], lay["nnzb"], lay["block"], lay["max_row"], float(scale),
         wq.data_ptr(), wq.numel(), err, s))
-    if reduce and plan.world > 1:
-        reduce_dkdv(plan, dk, dv, group)
+    if side is not None:
+        main.wait_stream(side)
+    elif exchange:
+        reduce_dkdv(plan, dk, dv, group, ops)
     return dq, dk, dv

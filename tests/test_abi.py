@@ -21,7 +21,7 @@ def declared_symbols():
 
 def test_header_symbols_exported():
     syms = declared_symbols()
-    assert len(syms) == 16
+    assert len(syms) == 19
     L = _lib.lib()
     for s in syms:
         assert hasattr(L, s), s
@@ -105,3 +105,20 @@ def test_bwd_checks_every_pass_before_launching():
             16, bad, 16, st, 16, st, 1, 1, 128, 64, 16, 16, 16, 16, 16, 16,
             2, 3, 64, 2, 2, 0.125, None, None]
     assert L.smat_bwd(*args) == 6
+
+
+def test_row_exchange_rejects_on_host():
+    L = _lib.lib()
+    st = (ctypes.c_int64 * 3)(4 * 1024 * 64, 1024 * 64, 64)
+    odd = (ctypes.c_int64 * 3)(4 * 1024 * 64, 1024 * 64, 60)
+    # an empty row list is a no-op
+    assert L.smat_rows_pack(1, 16, st, 16, st, 1, 4, 1024, 64, None, 0, None, None, None) == 0
+    assert L.smat_rows_pack(1, 16, st, 16, st, 1, 4, 1024, 64, 16, 5, None, None, None) == 8
+    assert L.smat_rows_pack(1, 16, odd, 16, st, 1, 4, 1024, 64, 16, 5, 16, None, None) == 6
+    assert L.smat_rows_pack(1, 16, st, 16, st, 1, 4, 1024, 60, 16, 5, 16, None, None) == 2
+    assert L.smat_rows_pack(3, 16, st, 16, st, 1, 4, 1024, 64, 16, 5, 16, None, None) == 4
+    assert L.smat_rows_unpack(1, 16, st, 16, st, 0, 4, 1024, 64, 16, 5, 16, None, None) == 1
+    assert L.smat_rows_accumulate(1, 16, st, 16, st, 1, 4, 1024, 64, 16, 5, None, 16, 3, 16,
+                                  None, None) == 8
+    assert L.smat_rows_accumulate(1, 16, st, 16, st, 1, 4, 1024, 64, 16, 5, 16, 16, -1, 16,
+                                  None, None) == 1

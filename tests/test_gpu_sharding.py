@@ -21,11 +21,13 @@ import torch
 
 from oracle import layout as OL
 from oracle.dense_softmax import rowchunked_masked_softmax
+from oracle.rows import TorchRowOps
 from smat_attention_b200 import _lib
 from smat_attention_b200.attention import (_DTYPES, _err_word, bwd, check_device_errors, fwd,
                                            layout_device_args)
 from smat_attention_b200.mask import build_block_mask
-from smat_attention_b200.sharding import make_plan, make_plans, sharded_bwd, sharded_fwd
+from smat_attention_b200.sharding import (CudaRowOps, make_plan, make_plans, sharded_bwd,
+                                          sharded_fwd)
 
 pytestmark = pytest.mark.gpu
 
@@ -156,6 +158,56 @@ def test_bad_work_item_sets_error_bit():
     assert torch.isfinite(o2.float()).all()
 
 
+@pytest.mark.parametrize("dtype,D", [(torch.bfloat16, 128), (torch.float32, 64)])
+def test_row_kernels_match_oracle(dtype, D):
+    """pack / unpack / accumulate of csrc/rows.cu equal the oracle's
+    restatement bit for bit, on whole tensors and on head-slice views."""
+    B, H, T = 2, 4, 700
+    g = torch.Generator().manual_seed(9)
+    a, b = (torch.randn(B, H, T, D, generator=g).to("cuda", dtype) for _ in range(2))
+    cu, ref = CudaRowOps(), TorchRowOps()
+    rows = torch.tensor([5, 699, 0, 128, 129, 5], dtype=torch.int64, device="cuda")
+    for x, y in ((a, b), (a[:, 1:3], b[:, 1:3])):
+        Bx, Hx = x.shape[:2]
+        w1 = torch.full((rows.numel() * 2 * Bx * Hx * D,), float("nan"), dtype=dtype,
+                        device="cuda")
+        w2 = w1.clone()
+        cu.pack(x, y, rows, w1)
+        ref.pack(x, y, rows, w2)
+        torch.cuda.synchronize()
+        assert torch.equal(w1, w2)
+        # unpack of distinct rows into copies
+        urows = rows[:5]
+        wire = torch.randn(urows.numel() * 2 * Bx * Hx * D, generator=g).to("cuda", dtype)
+        x1, y1, x2, y2 = x.clone(), y.clone(), x.clone(), y.clone()
+        cu.unpack(x1, y1, urows, wire)
+        ref.unpack(x2, y2, urows, wire)
+        torch.cuda.synchronize()
+        assert torch.equal(x1, x2) and torch.equal(y1, y2)
+        # accumulate: row 3 gets wire rows 1, 0; row 10 none; row 600 gets 3, 4, 2
+        exp = torch.tensor([3, 10, 600], dtype=torch.int64, device="cuda")
+        ptr = torch.tensor([0, 2, 2, 5], dtype=torch.int32, device="cuda")
+        cw = torch.tensor([1, 0, 3, 4, 2], dtype=torch.int64, device="cuda")
+        x1, y1, x2, y2 = x.clone(), y.clone(), x.clone(), y.clone()
+        cu.accumulate(x1, y1, exp, ptr, cw, wire, 5)
+        ref.accumulate(x2, y2, exp, ptr, cw, wire, 5)
+        torch.cuda.synchronize()
+        assert torch.equal(x1, x2) and torch.equal(y1, y2)
+    assert check_device_errors() == 0
+
+
+def test_row_kernels_flag_bad_rows():
+    """A row index outside [0, T) is skipped and reported (error bit 8)."""
+    a, b = (torch.zeros(1, 2, 256, 64, dtype=torch.bfloat16, device="cuda") for _ in range(2))
+    wire = torch.ones(2 * 2 * 2 * 64, dtype=torch.bfloat16, device="cuda")
+    rows = torch.tensor([3, 256], dtype=torch.int64, device="cuda")
+    check_device_errors()
+    CudaRowOps().unpack(a, b, rows, wire)
+    torch.cuda.synchronize()
+    assert check_device_errors() == 8
+    assert a[:, :, 3].float().sum().item() == 2 * 64 and a.float().sum().item() == 2 * 64
+
+
 # --------------------------------------------------------------------------- NCCL ranks
 
 def _free_port():
@@ -166,7 +218,7 @@ def _free_port():
     return port
 
 
-def _nccl_worker(rank, world, port, case):
+def _nccl_worker(rank, world, port, case, overlap):
     import torch.distributed as dist
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
@@ -186,8 +238,8 @@ def _nccl_worker(rank, world, port, case):
         qs, ks, vs, dos = (x.clone() for x in (q, k, v, do))
         for x in (qs, ks, vs, dos):
             x[:, :, ~own] = float("nan")
-        o, lse = sharded_fwd(plan, spec, qs, ks, vs, scale)
-        dq, dk, dv = sharded_bwd(plan, spec, qs, ks, vs, o, lse, dos, scale)
+        o, lse = sharded_fwd(plan, spec, qs, ks, vs, scale, groups=4 if overlap else 1)
+        dq, dk, dv = sharded_bwd(plan, spec, qs, ks, vs, o, lse, dos, scale, overlap=overlap)
         torch.cuda.synchronize()
         assert check_device_errors(dev) == 0
         ro, rlse, rdq, rdk, rdv = _oracle(q, k, v, do, lay)
@@ -204,12 +256,13 @@ def _nccl_worker(rank, world, port, case):
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
-@pytest.mark.parametrize("case", [(1, 4, 8192, 128, (128, 4, 8, 2)),
-                                  (1, 2, 4096, 64, (64, 8, 16, 1))])
-def test_two_ranks_nccl(case):
+@pytest.mark.parametrize("case,overlap", [((1, 4, 8192, 128, (128, 4, 8, 2)), True),
+                                          ((1, 4, 8192, 128, (128, 4, 8, 2)), False),
+                                          ((2, 2, 4096, 64, (64, 8, 16, 1)), True)])
+def test_two_ranks_nccl(case, overlap):
     import torch.multiprocessing as mp
-    ctx = mp.start_processes(_nccl_worker, args=(2, _free_port(), case), nprocs=2, join=False,
-                             start_method="spawn")
+    ctx = mp.start_processes(_nccl_worker, args=(2, _free_port(), case, overlap), nprocs=2,
+                             join=False, start_method="spawn")
     import time
     deadline = time.time() + 240
     while not ctx.join(timeout=5):

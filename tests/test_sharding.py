@@ -22,6 +22,7 @@ import torch.multiprocessing as mp
 
 from oracle import layout as OL
 from oracle.dense_softmax import rowchunked_masked_softmax
+from oracle.rows import TorchRowOps
 from smat_attention_b200 import _lib
 from smat_attention_b200.mask import build_block_mask
 from smat_attention_b200.sharding import (gather_kv, make_plan, make_plans, reduce_dkdv,
@@ -167,7 +168,7 @@ def _exchange_worker(rank, world, port, lay):
         kk, vv = k.clone(), v.clone()
         kk[:, :, ~own] = float("nan")
         vv[:, :, ~own] = float("nan")
-        gather_kv(plan, kk, vv)
+        gather_kv(plan, kk, vv, ops=TorchRowOps())
         imp_rows = np.concatenate([r for r in plan.recv_rows] + [np.zeros(0, np.int64)])
         readable = own.clone()
         readable[torch.from_numpy(imp_rows)] = True
@@ -183,10 +184,13 @@ def _exchange_worker(rank, world, port, lay):
         dv = torch.full_like(v, float("nan"))
         dk[:, :, readable] = pdk.reshape(B, H, T, D)[:, :, readable]
         dv[:, :, readable] = pdv.reshape(B, H, T, D)[:, :, readable]
-        reduce_dkdv(plan, dk, dv)
+        reduce_dkdv(plan, dk, dv, ops=TorchRowOps())
         err_k = (dk[:, :, own] - dk_ref.reshape(B, H, T, D)[:, :, own]).abs().max().item()
         err_v = (dv[:, :, own] - dv_ref.reshape(B, H, T, D)[:, :, own]).abs().max().item()
         assert err_k < 1e-5 and err_v < 1e-5, (err_k, err_v)
+        # the product's row kernels take CUDA tensors only (no CPU path)
+        with pytest.raises(ValueError):
+            gather_kv(plan, kk, vv)
         dist.barrier()
     finally:
         dist.destroy_process_group()
