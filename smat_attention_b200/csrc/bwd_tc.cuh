@@ -4,25 +4,34 @@
 //
 // dK/dV  one CTA per 128-row key tile of one (batch, head); it walks the
 //        union of the tile's transposed-CSR rows (the query blocks that read
-//        it) in 64-query chunks:
-//          S^T  = K Q_c^T          dP^T = V dO_c^T        (TMEM, double-buffered)
+//        it) in chunks of 128 queries:
+//          S^T  = K Q_c^T          dP^T = V dO_c^T        (TMEM, 128 x 128 each)
 //          P^T  = exp2(S^T c - lse_c log2 e)   dS^T = P^T (dP^T - delta_c)
 //          dV  += P^T dO_c         dK  += dS^T Q_c        (TMEM accumulators)
-// dQ     one CTA per 128-row query tile; it walks the forward CSR in 64-key
-//        chunks:
+// dQ     one CTA per 128-row query tile; it walks the forward CSR in chunks
+//        of 128 keys:
 //          S = Q K_c^T   dP = dO V_c^T   dS = P (dP - delta)   dQ += dS K_c
 //
-// Warp roles (320 threads): warps 0-7 compute -- warp w reads TMEM lanes
+// Every tcgen05.mma is 128 x 128 (or 128 x D): on B200 an N = 64 MMA costs
+// nearly as many cycles as an N = 128 one, so the chunk is 128 wide.  TMEM
+// (512 columns) then holds one S, one dP and the accumulators, so S and dP
+// are single-buffered and the hand-offs are split to keep the tensor core
+// fed: as soon as P (P^T) is ready the MMA warp issues dV and the next S;
+// as soon as dS is ready it issues dK (or dQ) and the next dP.  The compute
+// warps turn dP into dS while the tensor core runs dV and the next S.
+// With bs = 64 a chunk is two 64-row blocks of the merged list (TMA loads
+// each half separately; a missing second half is loaded from row T, i.e.
+// zero-filled, and masked).
+//
+// Warp roles (576 threads): warps 0-15 compute -- warp w reads TMEM lanes
 // 32 (w % 4) .. +31 (its 32 tile rows) and chunk columns 32 (w / 4) .. +31;
-// warp 8 is the TMA producer; warp 9 allocates TMEM and issues the MMAs.
+// warp 16 is the TMA producer; warp 17 allocates TMEM and issues the MMAs.
 // P^T / dS^T / dS (bf16) are written back into the TMEM columns of the S / dP
 // they came from (each warp over columns it has already read) and feed the
-// tensor core as the A operand straight from TMEM; the S/dP double buffer
-// lets the compute warps work on the next chunk meanwhile.
+// tensor core as the A operand straight from TMEM.
 #pragma once
 
 #include "common.cuh"
-#include "fwd_tc.cuh"
 #include "schedule.cuh"
 
 namespace smat {
@@ -43,15 +52,42 @@ struct BwdParams {
   int32_t* err;
 };
 
+// Chunks of 128 streamed rows: 128 / bs consecutive entries of the merged
+// CSR rows of the tile (one entry for bs = 128, two for bs = 64).  A missing
+// second entry is 0 (no row states).
+struct ChunkPair {
+  MergeIter<2> it;
+  int epc;
+  __device__ __forceinline__ void init(const int32_t* indptr, const int32_t* indices,
+                                       const uint8_t* kinds, int nblocks, int nnzb, int row0,
+                                       int nrows, int bs, int32_t* err) {
+    it.init(indptr, indices, kinds, nblocks, nnzb, row0, nrows, err);
+    epc = 128 / bs;
+  }
+  __device__ __forceinline__ bool next(uint32_t* e, int32_t* err) {
+    if (!it.next(e[0], err)) return false;
+    e[1] = 0u;
+    if (epc == 2) {
+      uint32_t t;
+      if (it.next(t, err)) e[1] = t;
+    }
+    return true;
+  }
+};
+__device__ __forceinline__ bool entry_present(uint32_t e) { return (e >> 24) != 0u; }
+
 template <bool DKDV, int D>
 struct BwdCfg {
   static constexpr int BM = 128;     // tile rows
-  static constexpr int CN = 64;      // chunk width (queries for dK/dV, keys for dQ)
+  static constexpr int CN = 128;     // chunk rows (queries for dK/dV, keys for dQ)
+  static constexpr int BOX = 64;     // TMA box rows of a chunk load
   static constexpr int ROW_BYTES = BM * D * 2;   // one resident operand
   static constexpr int CH_BYTES = CN * D * 2;    // one streamed operand chunk
+  static constexpr int PANEL_R = BM * 128;       // one 64-column SWIZZLE_128B panel
+  static constexpr int PANEL_C = CN * 128;
   static constexpr int LD_BYTES = DKDV ? 2 * CN * 4 : 0;   // lse + delta per stage
   // as many stages as the shared memory holds (at most 8)
-  static constexpr int FIXED = 2 * ROW_BYTES + 1536;  // + barriers, alignment
+  static constexpr int FIXED = 2 * ROW_BYTES + 2048;  // + barriers, alignment
   static constexpr int STAGES_FIT = (227 * 1024 - FIXED) / (2 * CH_BYTES + LD_BYTES);
   static constexpr int STAGES = STAGES_FIT > 8 ? 8 : STAGES_FIT;
   static constexpr int OFF_R0 = 0;                              // K (dK/dV) or Q (dQ)
@@ -60,33 +96,40 @@ struct BwdCfg {
   static constexpr int OFF_C1 = OFF_C0 + STAGES * CH_BYTES;     // dO_c (dK/dV) or V_c (dQ)
   static constexpr int OFF_LD = OFF_C1 + STAGES * CH_BYTES;     // per stage: lse [CN], delta [CN]
   static constexpr int OFF_BAR = OFF_LD + STAGES * LD_BYTES;
-  // barriers: r_full, c_full[S], c_empty[S], s_full[2], a_full[2], a_done[2], drain
+  // barriers: r_full, c_full[S], c_empty[S], s_full, dp_full, p_ready, ds_ready,
+  // acc_done, drain, resident-in-TMEM
   static constexpr int BAR_R = 0, BAR_CF = 1, BAR_CE = 1 + STAGES, BAR_SF = 1 + 2 * STAGES,
-                       BAR_AF = BAR_SF + 2, BAR_AD = BAR_AF + 2, BAR_DRAIN = BAR_AD + 2,
-                       BAR_RT = BAR_DRAIN + 1, NBAR = BAR_RT + 1;
+                       BAR_DPF = BAR_SF + 1, BAR_PR = BAR_DPF + 1, BAR_DSR = BAR_PR + 1,
+                       BAR_AD = BAR_DSR + 1, BAR_DRAIN = BAR_AD + 1, BAR_RT = BAR_DRAIN + 1,
+                       NBAR = BAR_RT + 1;
   static constexpr int OFF_MISC = OFF_BAR + NBAR * 8;
   static constexpr int SMEM_BYTES = OFF_MISC + 16 + 1024;
   static_assert(SMEM_BYTES <= 227 * 1024, "shared memory budget");
   static_assert(STAGES >= 2, "at least two stages");
-  // TMEM: [S 64 | dP 64] x 2 buffers, then the accumulators
-  static constexpr int COL_S = 0, COL_DP = CN, BUF_COLS = 2 * CN, COL_ACC0 = 2 * BUF_COLS,
-                       COL_ACC1 = COL_ACC0 + D;
+  // TMEM: S | dP | accumulators (| resident Q, dO for dQ)
+  static constexpr int COL_S = 0, COL_DP = CN, COL_ACC0 = 2 * CN, COL_ACC1 = COL_ACC0 + D;
   // dQ: the resident Q and dO also go to TMEM (bf16 pairs per column), so S
   // and dP read only the streamed chunk from shared memory
   static constexpr bool RES_TMEM = !DKDV;
   static constexpr int COL_RT0 = COL_ACC0 + D, COL_RT1 = COL_RT0 + D / 2;
   static_assert(!RES_TMEM || COL_RT1 + D / 2 <= 512, "TMEM budget");
+  static_assert(RES_TMEM || COL_ACC1 + D <= 512, "TMEM budget");
   static constexpr int TMEM_COLS = 512;
-  // compute warps: NCW / 4 groups of 4; group g owns chunk columns
-  // [g CW, (g + 1) CW) of all 128 tile rows
-  static constexpr int NCW = 16, CW = CN * 4 / NCW;
+  // compute warps: 4 groups of 4; group g owns chunk columns [32 g, 32 g + 32)
+  static constexpr int NCW = 16, CW = CN / 4;
+  static_assert(CW == 32, "one 32-column block per warp");
   static constexpr int PRODUCER_WARP = NCW, MMA_WARP = NCW + 1, THREADS = (NCW + 2) * 32;
   static constexpr uint32_t IDESC_SC = idesc_bf16(BM, CN, false, false);  // S, dP
   static constexpr uint32_t IDESC_ACC = idesc_bf16(BM, D, false, true);   // dV, dK, dQ
 };
 
+// TMEM column (packed bf16 pairs) of the A operand's k-step kk (16 chunk
+// columns): group kk / 2 wrote chunk columns [32 (kk / 2), +32) packed into
+// its first 16 columns
+__device__ __forceinline__ uint32_t a_col(int kk) { return 32u * (kk >> 1) + 8u * (kk & 1); }
+
 template <bool DKDV, int D>
-__global__ void __launch_bounds__((BwdCfg<DKDV, D>::NCW + 2) * 32, 1)
+__global__ void __launch_bounds__(BwdCfg<DKDV, D>::THREADS, 1)
     smat_bwd_tc_kernel(const __grid_constant__ CUtensorMap tm_r0,
                        const __grid_constant__ CUtensorMap tm_r1,
                        const __grid_constant__ CUtensorMap tm_c0,
@@ -121,7 +164,6 @@ __global__ void __launch_bounds__((BwdCfg<DKDV, D>::NCW + 2) * 32, 1)
   }
   const int b = bh / p.H, h = bh % p.H;
   const int sub = C::BM / p.bs;   // CSR rows per tile: 1 or 2
-  const int cpb = p.bs / C::CN;   // chunks per block: 2 or 1
   const int row0 = tile * sub;
 
   if (tid == 0) {
@@ -130,11 +172,11 @@ __global__ void __launch_bounds__((BwdCfg<DKDV, D>::NCW + 2) * 32, 1)
       mbar_init(bar(C::BAR_CF + s), 1);
       mbar_init(bar(C::BAR_CE + s), 1);
     }
-    for (int i = 0; i < 2; ++i) {
-      mbar_init(bar(C::BAR_SF + i), 1);
-      mbar_init(bar(C::BAR_AF + i), C::NCW);
-      mbar_init(bar(C::BAR_AD + i), 1);
-    }
+    mbar_init(bar(C::BAR_SF), 1);
+    mbar_init(bar(C::BAR_DPF), 1);
+    mbar_init(bar(C::BAR_PR), C::NCW);
+    mbar_init(bar(C::BAR_DSR), C::NCW);
+    mbar_init(bar(C::BAR_AD), 1);
     mbar_init(bar(C::BAR_DRAIN), 1);
     mbar_init(bar(C::BAR_RT), C::NCW);
     fence_barrier_init();
@@ -160,38 +202,46 @@ __global__ void __launch_bounds__((BwdCfg<DKDV, D>::NCW + 2) * 32, 1)
     // Lane 0 issues the TMA loads; for dK/dV all 32 lanes also copy the
     // chunk's lse and delta next to it with cp.async, tracked by the same
     // stage barrier, so nobody waits on a global load.
-    ChunkIter<2> it;
-    it.init(p.indptr, p.indices, p.kind, p.nblocks, p.nnzb, row0, sub, cpb, p.err);
+    ChunkPair it;
+    it.init(p.indptr, p.indices, p.kind, p.nblocks, p.nnzb, row0, sub, p.bs, p.err);
     if (lane == 0) {
       mbar_expect_tx(bar(C::BAR_R), 2 * C::ROW_BYTES);
 #pragma unroll
       for (int pn = 0; pn < D / 64; ++pn) {
-        tma_load_4d(sbase + C::OFF_R0 + pn * (C::BM * 128), &tm_r0, bar(C::BAR_R), pn * 64,
+        tma_load_4d(sbase + C::OFF_R0 + pn * C::PANEL_R, &tm_r0, bar(C::BAR_R), pn * 64,
                     tile * C::BM, h, b);
-        tma_load_4d(sbase + C::OFF_R1 + pn * (C::BM * 128), &tm_r1, bar(C::BAR_R), pn * 64,
+        tma_load_4d(sbase + C::OFF_R1 + pn * C::PANEL_R, &tm_r1, bar(C::BAR_R), pn * 64,
                     tile * C::BM, h, b);
       }
     }
     int issued = 0;
-    uint32_t e;
-    int c;
-    for (int j = 0; it.next(e, c, p.err); ++j) {
+    uint32_t e[2];
+    for (int j = 0; it.next(e, p.err); ++j) {
       const int s = j % C::STAGES;
       bool ok = true;
       if (lane == 0 && j >= C::STAGES)
         ok = mbar_wait(bar(C::BAR_CE + s), ((j / C::STAGES) - 1) & 1, abort_flag, p.err);
       if (!__shfl_sync(0xffffffffu, ok, 0)) break;
       __syncwarp();
-      const int row = static_cast<int>(sched_block(e)) * p.bs + c * C::CN;
+      // first row of each 64-row half of the chunk; a missing half reads row
+      // T onwards, which TMA fills with zeros
+      int prow[2];
+#pragma unroll
+      for (int q = 0; q < 2; ++q) {
+        const uint32_t eq = (p.bs == 64) ? e[q] : e[0];
+        prow[q] = entry_present(eq) ? static_cast<int>(sched_block(eq)) * p.bs + (q * 64) % p.bs
+                                    : p.T;
+      }
       if (DKDV) {
         const uint32_t lds = sbase + C::OFF_LD + s * C::LD_BYTES;
 #pragma unroll
         for (int u = 0; u < C::CN / 32; ++u) {
-          const int qi = row + u * 32 + lane;
+          const int col = u * 32 + lane;
+          const int qi = prow[col >> 6] + (col & 63);
           const bool in = qi < p.T;
           const int64_t gi = in ? static_cast<int64_t>(bh) * p.T + qi : 0;
-          cp_async4(lds + (u * 32 + lane) * 4, p.lse + gi, in ? 4u : 0u);
-          cp_async4(lds + (C::CN + u * 32 + lane) * 4, p.delta + gi, in ? 4u : 0u);
+          cp_async4(lds + col * 4, p.lse + gi, in ? 4u : 0u);
+          cp_async4(lds + (C::CN + col) * 4, p.delta + gi, in ? 4u : 0u);
         }
         cp_async_arrive(bar(C::BAR_CF + s));
         __syncwarp();
@@ -199,12 +249,15 @@ __global__ void __launch_bounds__((BwdCfg<DKDV, D>::NCW + 2) * 32, 1)
       if (lane == 0) {
         mbar_expect_tx(bar(C::BAR_CF + s), 2 * C::CH_BYTES);
 #pragma unroll
-        for (int pn = 0; pn < D / 64; ++pn) {
-          tma_load_4d(sbase + C::OFF_C0 + s * C::CH_BYTES + pn * (C::CN * 128), &tm_c0,
-                      bar(C::BAR_CF + s), pn * 64, row, h, b);
-          tma_load_4d(sbase + C::OFF_C1 + s * C::CH_BYTES + pn * (C::CN * 128), &tm_c1,
-                      bar(C::BAR_CF + s), pn * 64, row, h, b);
-        }
+        for (int pn = 0; pn < D / 64; ++pn)
+#pragma unroll
+          for (int q = 0; q < 2; ++q) {
+            const uint32_t off = s * C::CH_BYTES + pn * C::PANEL_C + q * (C::BOX * 128);
+            tma_load_4d(sbase + C::OFF_C0 + off, &tm_c0, bar(C::BAR_CF + s), pn * 64, prow[q], h,
+                        b);
+            tma_load_4d(sbase + C::OFF_C1 + off, &tm_c1, bar(C::BAR_CF + s), pn * 64, prow[q], h,
+                        b);
+          }
       }
       issued = j + 1;
     }
@@ -218,98 +271,81 @@ __global__ void __launch_bounds__((BwdCfg<DKDV, D>::NCW + 2) * 32, 1)
   } else if (warp == C::MMA_WARP) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
-      ChunkIter<2> it;
-      it.init(p.indptr, p.indices, p.kind, p.nblocks, p.nnzb, row0, sub, cpb, p.err);
-      // S-like products of chunk j into TMEM buffer j & 1:
-      //   buffer.S  = R0 . C0_j^T,   buffer.dP = R1 . C1_j^T
-      auto issue_sc = [&](int j) {
+      ChunkPair it;
+      it.init(p.indptr, p.indices, p.kind, p.nblocks, p.nnzb, row0, sub, p.bs, p.err);
+      // S (S^T) of chunk j:  R0 . C0_j^T;  dP (dP^T):  R1 . C1_j^T
+      auto issue_sd = [&](int j, bool dp) {
         const int s = j % C::STAGES;
-        const uint32_t tb = tbase + (j & 1) * C::BUF_COLS;
-        const uint32_t r0 = sbase + C::OFF_R0, r1 = sbase + C::OFF_R1;
-        const uint32_t c0 = sbase + C::OFF_C0 + s * C::CH_BYTES;
-        const uint32_t c1 = sbase + C::OFF_C1 + s * C::CH_BYTES;
+        const uint32_t r = sbase + (dp ? C::OFF_R1 : C::OFF_R0);
+        const uint32_t c = sbase + (dp ? C::OFF_C1 : C::OFF_C0) + s * C::CH_BYTES;
+        const uint32_t d = tbase + (dp ? C::COL_DP : C::COL_S);
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
-          const uint32_t off = (kk >> 2) * (C::BM * 128) + (kk & 3) * 32;
-          const uint32_t offc = (kk >> 2) * (C::CN * 128) + (kk & 3) * 32;
+          const uint32_t off = (kk >> 2) * C::PANEL_R + (kk & 3) * 32;
+          const uint32_t offc = (kk >> 2) * C::PANEL_C + (kk & 3) * 32;
           if (C::RES_TMEM)   // A = 16 d-elements = 8 packed columns per k-step
-            tc_mma_ts(tb + C::COL_S, tbase + C::COL_RT0 + kk * 8,
-                      sdesc_sw128(c0 + offc, 16, 1024), C::IDESC_SC, kk > 0 ? 1u : 0u);
+            tc_mma_ts(d, tbase + (dp ? C::COL_RT1 : C::COL_RT0) + kk * 8,
+                      sdesc_sw128(c + offc, 16, 1024), C::IDESC_SC, kk > 0 ? 1u : 0u);
           else
-            tc_mma(tb + C::COL_S, sdesc_sw128(r0 + off, 16, 1024),
-                   sdesc_sw128(c0 + offc, 16, 1024), C::IDESC_SC, kk > 0 ? 1u : 0u);
+            tc_mma(d, sdesc_sw128(r + off, 16, 1024), sdesc_sw128(c + offc, 16, 1024),
+                   C::IDESC_SC, kk > 0 ? 1u : 0u);
         }
+        tc_commit(bar(dp ? C::BAR_DPF : C::BAR_SF));
+      };
+      // acc (+)= A_j . C_j with A = P^T / dS^T / dS in TMEM at column `acol`,
+      // C_j the chunk operand (MN-major): 16 chunk rows per k-step
+      auto issue_acc = [&](uint32_t dcol, uint32_t acol, uint32_t cbase, bool first) {
 #pragma unroll
-        for (int kk = 0; kk < D / 16; ++kk) {
-          const uint32_t off = (kk >> 2) * (C::BM * 128) + (kk & 3) * 32;
-          const uint32_t offc = (kk >> 2) * (C::CN * 128) + (kk & 3) * 32;
-          if (C::RES_TMEM)
-            tc_mma_ts(tb + C::COL_DP, tbase + C::COL_RT1 + kk * 8,
-                      sdesc_sw128(c1 + offc, 16, 1024), C::IDESC_SC, kk > 0 ? 1u : 0u);
-          else
-            tc_mma(tb + C::COL_DP, sdesc_sw128(r1 + off, 16, 1024),
-                   sdesc_sw128(c1 + offc, 16, 1024), C::IDESC_SC, kk > 0 ? 1u : 0u);
-        }
-        tc_commit(bar(C::BAR_SF + (j & 1)));
+        for (int kk = 0; kk < C::CN / 16; ++kk)
+          tc_mma_ts(tbase + dcol, tbase + acol + a_col(kk),
+                    sdesc_sw128(cbase + kk * 2048, C::PANEL_C, 1024), C::IDESC_ACC,
+                    (!first || kk > 0) ? 1u : 0u);
       };
       bool ok = mbar_wait(bar(C::BAR_R), 0, abort_flag, p.err);
       if (C::RES_TMEM && ok) ok = mbar_wait(bar(C::BAR_RT), 0, abort_flag, p.err);
-      uint32_t e;
-      int c;
-      bool has = ok && it.next(e, c, p.err);
+      uint32_t e[2];
+      bool has = ok && it.next(e, p.err);
       if (has) {
         ok = mbar_wait(bar(C::BAR_CF + 0), 0, abort_flag, p.err);
         if (ok) {
           tc_fence_after();
-          issue_sc(0);
+          issue_sd(0, false);
+          issue_sd(0, true);
         }
       }
       for (int j = 0; ok && has; ++j) {
-        has = it.next(e, c, p.err);
-        // S/dP of the next chunk go first if its operands already landed;
-        // otherwise this chunk's accumulator MMAs are not held up behind it
-        bool early = false;
-        if (has && mbar_try_wait(bar(C::BAR_CF + (j + 1) % C::STAGES), ((j + 1) / C::STAGES) & 1)) {
-          tc_fence_after();
-          issue_sc(j + 1);
-          early = true;
-        }
-        if (!mbar_wait(bar(C::BAR_AF + (j & 1)), (j >> 1) & 1, abort_flag, p.err)) break;
-        tc_fence_after();
+        const bool nxt = it.next(e, p.err);
         const int s = j % C::STAGES;
         const uint32_t c0 = sbase + C::OFF_C0 + s * C::CH_BYTES;
         const uint32_t c1 = sbase + C::OFF_C1 + s * C::CH_BYTES;
-        const uint32_t tb = tbase + (j & 1) * C::BUF_COLS;
-        const uint32_t acc = (j > 0) ? 1u : 0u;
-#pragma unroll
-        for (int kk = 0; kk < C::CN / 16; ++kk) {
-          // A in TMEM: the 16 chunk columns of k-step kk are 8 packed columns
-          // at the start of the column group of the warps that wrote them
-          const uint32_t aoff = (16 * kk / C::CW) * C::CW + (16 * kk % C::CW) / 2;
-          if (DKDV) {
-            // dV += P^T dO_c ; dK += dS^T Q_c   (B operands MN-major)
-            tc_mma_ts(tbase + C::COL_ACC1, tb + C::COL_S + aoff,
-                      sdesc_sw128(c1 + kk * 2048, C::CN * 128, 1024), C::IDESC_ACC,
-                      (acc || kk > 0) ? 1u : 0u);
-            tc_mma_ts(tbase + C::COL_ACC0, tb + C::COL_DP + aoff,
-                      sdesc_sw128(c0 + kk * 2048, C::CN * 128, 1024), C::IDESC_ACC,
-                      (acc || kk > 0) ? 1u : 0u);
-          } else {
-            // dQ += dS K_c
-            tc_mma_ts(tbase + C::COL_ACC0, tb + C::COL_DP + aoff,
-                      sdesc_sw128(c0 + kk * 2048, C::CN * 128, 1024), C::IDESC_ACC,
-                      (acc || kk > 0) ? 1u : 0u);
-          }
-        }
-        tc_commit(bar(C::BAR_AD + (j & 1)));
-        tc_commit(bar(C::BAR_CE + s));
-        if (has && !early) {
-          const int s1 = (j + 1) % C::STAGES;
-          if (!mbar_wait(bar(C::BAR_CF + s1), ((j + 1) / C::STAGES) & 1, abort_flag, p.err)) break;
+        // P^T written (dK/dV) or S read (dQ)
+        if (!mbar_wait(bar(C::BAR_PR), j & 1, abort_flag, p.err)) break;
+        tc_fence_after();
+        if (DKDV) issue_acc(C::COL_ACC1, C::COL_S, c1, j == 0);      // dV += P^T dO_c
+        // the next S goes in behind it if its operands already landed
+        bool s_next = false;
+        if (nxt && mbar_try_wait(bar(C::BAR_CF + (j + 1) % C::STAGES), ((j + 1) / C::STAGES) & 1)) {
           tc_fence_after();
-          issue_sc(j + 1);
+          issue_sd(j + 1, false);
+          s_next = true;
         }
+        if (!mbar_wait(bar(C::BAR_DSR), j & 1, abort_flag, p.err)) break;
+        tc_fence_after();
+        issue_acc(C::COL_ACC0, C::COL_DP, c0, j == 0);   // dK += dS^T Q_c  or  dQ += dS K_c
+        tc_commit(bar(C::BAR_CE + s));                    // chunk j's operands are consumed
+        if (nxt) {
+          if (!s_next) {
+            if (!mbar_wait(bar(C::BAR_CF + (j + 1) % C::STAGES), ((j + 1) / C::STAGES) & 1,
+                           abort_flag, p.err))
+              break;
+            tc_fence_after();
+            issue_sd(j + 1, false);
+          }
+          issue_sd(j + 1, true);
+        }
+        has = nxt;
       }
+      tc_commit(bar(C::BAR_AD));
       if (*abort_flag) {  // let the MMAs in flight finish before TMEM is freed
         tc_commit(bar(C::BAR_DRAIN));
         mbar_wait_drain(bar(C::BAR_DRAIN), 0);
@@ -317,12 +353,11 @@ __global__ void __launch_bounds__((BwdCfg<DKDV, D>::NCW + 2) * 32, 1)
     }
   } else {
     // ------------------------------------------------------------ compute
-    constexpr int CW = C::CW;
     const int quad = warp & 3, grp = warp >> 2;
     const int r = quad * 32 + lane;                 // tile row = TMEM lane
     const int pos = tile * C::BM + r;               // key (dK/dV) or query (dQ) position
     const int srow = (sub == 2) ? (r >> 6) : 0;     // CSR row of this tile row
-    const int col0 = grp * CW;                      // this warp's chunk columns
+    const int col0 = grp * C::CW;                   // this warp's chunk columns
     const uint32_t lane_base = tbase + (static_cast<uint32_t>(quad * 32) << 16);
     const float LOG2E = 1.4426950408889634f;
     const float* ld = reinterpret_cast<const float*>(smem + C::OFF_LD);  // [STAGES][lse | delta]
@@ -338,7 +373,7 @@ __global__ void __launch_bounds__((BwdCfg<DKDV, D>::NCW + 2) * 32, 1)
       // 16-byte chunk q of the row = packed columns [4 q, 4 q + 4)
       alive = __all_sync(0xffffffffu, mbar_wait(bar(C::BAR_R), 0, abort_flag, p.err));
       if (alive) {
-        constexpr int QPG = D / 8 / (C::NCW / 4);   // 16-byte chunks per warp group
+        constexpr int QPG = D / 8 / 4;   // 16-byte chunks per warp group
 #pragma unroll
         for (int t = 0; t < 2; ++t) {
           const uint8_t* src = smem + (t == 0 ? C::OFF_R0 : C::OFF_R1);
@@ -347,7 +382,7 @@ __global__ void __launch_bounds__((BwdCfg<DKDV, D>::NCW + 2) * 32, 1)
           for (int u = 0; u < QPG; ++u) {
             const int q = grp * QPG + u;
             const uint4 v = *reinterpret_cast<const uint4*>(
-                src + (q >> 3) * (C::BM * 128) + sw128_offset(r, q & 7));
+                src + (q >> 3) * C::PANEL_R + sw128_offset(r, q & 7));
             w[4 * u] = v.x;
             w[4 * u + 1] = v.y;
             w[4 * u + 2] = v.z;
@@ -364,14 +399,16 @@ __global__ void __launch_bounds__((BwdCfg<DKDV, D>::NCW + 2) * 32, 1)
       }
     }
     int n = 0;
-    ChunkIter<2> it;
-    it.init(p.indptr, p.indices, p.kind, p.nblocks, p.nnzb, row0, sub, cpb, p.err);
-    uint32_t e;
-    int c;
-    for (int j = 0; alive && it.next(e, c, p.err); ++j) {
+    ChunkPair it;
+    it.init(p.indptr, p.indices, p.kind, p.nblocks, p.nnzb, row0, sub, p.bs, p.err);
+    uint32_t e[2];
+    for (int j = 0; alive && it.next(e, p.err); ++j) {
       n = j + 1;
-      const int c0pos = static_cast<int>(sched_block(e)) * p.bs + c * C::CN;
-      const uint32_t st = sched_state(e, srow);
+      // this warp's 32 columns lie in one 64-row half of the chunk
+      const uint32_t ew = (p.bs == 64 && col0 >= 64) ? e[1] : e[0];
+      const int cbase = entry_present(ew) ? static_cast<int>(sched_block(ew)) * p.bs + col0 % p.bs
+                                          : p.T;
+      const uint32_t st = entry_present(ew) ? sched_state(ew, srow) : ST_ABSENT;
       const float* ldj = ld + (j % C::STAGES) * (C::LD_BYTES / 4);
       // dK/dV reads the lse/delta the producer staged with this chunk
       if (DKDV && !__all_sync(0xffffffffu, mbar_wait(bar(C::BAR_CF + j % C::STAGES),
@@ -379,85 +416,97 @@ __global__ void __launch_bounds__((BwdCfg<DKDV, D>::NCW + 2) * 32, 1)
         alive = false;
         break;
       }
-      if (!__all_sync(0xffffffffu,
-                      mbar_wait(bar(C::BAR_SF + (j & 1)), (j >> 1) & 1, abort_flag, p.err))) {
+      if (!__all_sync(0xffffffffu, mbar_wait(bar(C::BAR_SF), j & 1, abort_flag, p.err))) {
         alive = false;
         break;
       }
       tc_fence_after();
-      const uint32_t tb = lane_base + (j & 1) * C::BUF_COLS;
-      float sv[CW], dp[CW];
-      if (CW == 32) {
-        tmem_ld32x2(tb + C::COL_S + col0, tb + C::COL_DP + col0, sv, dp);
-      } else {
-        tmem_ld16x2(tb + C::COL_S + col0, tb + C::COL_DP + col0, sv, dp);
+      // ---- P (P^T): 32 columns of S
+      float pv[C::CW];
+      tmem_ld32(lane_base + C::COL_S + col0, pv);
+      // warp-uniform: no element of this warp's 32 x 32 block is masked
+      const bool all_valid = (st == ST_FULL) && (!DKDV || cbase + C::CW <= p.T);
+      const float4* l4 = reinterpret_cast<const float4*>(ldj + col0);
+#pragma unroll
+      for (int q = 0; q < C::CW / 4; ++q) {
+        float nl[4];
+        if (DKDV) {
+          const float4 a4 = l4[q];
+          nl[0] = a4.x * -LOG2E;
+          nl[1] = a4.y * -LOG2E;
+          nl[2] = a4.z * -LOG2E;
+          nl[3] = a4.w * -LOG2E;
+        } else {
+#pragma unroll
+          for (int i = 0; i < 4; ++i) nl[i] = -row_lse2;
+        }
+        if (all_valid) {
+#pragma unroll
+          for (int i = 0; i < 4; ++i)
+            pv[4 * q + i] = ex2_approx(fmaf(pv[4 * q + i], p.scale_log2, nl[i]));
+        } else {
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const int cpos = cbase + 4 * q + i;
+            // dK/dV: row = key `pos`, column = query `cpos`; dQ: the reverse
+            const bool valid =
+                DKDV ? ((st == ST_FULL || (st == ST_CAUSAL && cpos >= pos)) && cpos < p.T)
+                     : (st == ST_FULL || (st == ST_CAUSAL && cpos <= pos));
+            pv[4 * q + i] = valid ? ex2_approx(fmaf(pv[4 * q + i], p.scale_log2, nl[i])) : 0.f;
+          }
+        }
       }
-      // warp-uniform: no element of this warp's 32 x CW block is masked
-      const bool all_valid = (st == ST_FULL) && (!DKDV || c0pos + C::CN <= p.T);
-      // per-column terms: -lse log2(e) and delta of the chunk's queries (dK/dV),
-      // or the row's own (dQ)
-      float nl2[CW], dl[CW];
       if (DKDV) {
-        const float4* l4 = reinterpret_cast<const float4*>(ldj + col0);
-        const float4* d4 = reinterpret_cast<const float4*>(ldj + C::CN + col0);
+        // P^T over the S columns this warp has read; it feeds dV
+        uint32_t wp[C::CW / 2];
 #pragma unroll
-        for (int q = 0; q < CW / 4; ++q) {
-          const float4 a = l4[q], dd = d4[q];
-          nl2[4 * q] = a.x * -LOG2E;
-          nl2[4 * q + 1] = a.y * -LOG2E;
-          nl2[4 * q + 2] = a.z * -LOG2E;
-          nl2[4 * q + 3] = a.w * -LOG2E;
-          dl[4 * q] = dd.x;
-          dl[4 * q + 1] = dd.y;
-          dl[4 * q + 2] = dd.z;
-          dl[4 * q + 3] = dd.w;
+        for (int i = 0; i < C::CW / 2; ++i) wp[i] = pack_bf16(pv[2 * i], pv[2 * i + 1]);
+        tmem_st16u(lane_base + C::COL_S + col0, wp);
+        tmem_st_wait();
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar(C::BAR_PR));
+      // ---- dS (dS^T) = P (dP - delta)
+      if (!__all_sync(0xffffffffu, mbar_wait(bar(C::BAR_DPF), j & 1, abort_flag, p.err))) {
+        alive = false;
+        break;
+      }
+      tc_fence_after();
+      const float4* d4 = reinterpret_cast<const float4*>(ldj + C::CN + col0);
+      uint32_t wd[C::CW / 2];
+#pragma unroll
+      for (int hf = 0; hf < 2; ++hf) {
+        float dp[16];
+        tmem_ld16(lane_base + C::COL_DP + col0 + 16 * hf, dp);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          float dl[4];
+          if (DKDV) {
+            const float4 dd = d4[4 * hf + q];
+            dl[0] = dd.x;
+            dl[1] = dd.y;
+            dl[2] = dd.z;
+            dl[3] = dd.w;
+          } else {
+#pragma unroll
+            for (int i = 0; i < 4; ++i) dl[i] = row_delta;
+          }
+          const int k = 16 * hf + 4 * q;
+          wd[k / 2] = pack_bf16(pv[k] * (dp[4 * q] - dl[0]), pv[k + 1] * (dp[4 * q + 1] - dl[1]));
+          wd[k / 2 + 1] =
+              pack_bf16(pv[k + 2] * (dp[4 * q + 2] - dl[2]), pv[k + 3] * (dp[4 * q + 3] - dl[3]));
         }
-      } else {
-#pragma unroll
-        for (int i = 0; i < CW; ++i) {
-          nl2[i] = -row_lse2;
-          dl[i] = row_delta;
-        }
       }
-      float pv[CW];
-      if (all_valid) {
-#pragma unroll
-        for (int i = 0; i < CW; ++i) pv[i] = ex2_approx(fmaf(sv[i], p.scale_log2, nl2[i]));
-      } else {
-#pragma unroll
-        for (int i = 0; i < CW; ++i) {
-          const int cpos = c0pos + col0 + i;
-          // dK/dV: row = key `pos`, column = query `cpos`; dQ: the reverse
-          const bool valid =
-              DKDV ? ((st == ST_FULL || (st == ST_CAUSAL && cpos >= pos)) && cpos < p.T)
-                   : (st == ST_CAUSAL && cpos <= pos);
-          pv[i] = valid ? ex2_approx(fmaf(sv[i], p.scale_log2, nl2[i])) : 0.f;
-        }
-      }
-      uint32_t wp[CW / 2], wd[CW / 2];
-#pragma unroll
-      for (int i = 0; i < CW / 2; ++i) {
-        wp[i] = pack_bf16(pv[2 * i], pv[2 * i + 1]);
-        wd[i] = pack_bf16(pv[2 * i] * (dp[2 * i] - dl[2 * i]),
-                          pv[2 * i + 1] * (dp[2 * i + 1] - dl[2 * i + 1]));
-      }
-      // P^T / dS^T / dS over the S / dP columns this warp has already read
-      if (CW == 32) {
-        if (DKDV) tmem_st16u(tb + C::COL_S + col0, wp);
-        tmem_st16u(tb + C::COL_DP + col0, wd);
-      } else {
-        if (DKDV) tmem_st8u(tb + C::COL_S + col0, wp);
-        tmem_st8u(tb + C::COL_DP + col0, wd);
-      }
+      tmem_st16u(lane_base + C::COL_DP + col0, wd);
       tmem_st_wait();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(bar(C::BAR_AF + (j & 1)));
+      if (lane == 0) mbar_arrive(bar(C::BAR_DSR));
     }
     // ------------------------------------------------------------ epilogue
     if (alive && n > 0 &&
-        !__all_sync(0xffffffffu, mbar_wait(bar(C::BAR_AD + ((n - 1) & 1)), ((n - 1) >> 1) & 1,
-                                           abort_flag, p.err)))
+        !__all_sync(0xffffffffu, mbar_wait(bar(C::BAR_AD), 0, abort_flag, p.err)))
       alive = false;
     if (alive) {
       tc_fence_after();
@@ -468,7 +517,7 @@ __global__ void __launch_bounds__((BwdCfg<DKDV, D>::NCW + 2) * 32, 1)
                                      static_cast<int64_t>(h) * p.o1_sh +
                                      static_cast<int64_t>(pos) * p.o1_st
                                : nullptr;
-      constexpr int EW = D / (C::NCW / 4);   // accumulator columns per warp group
+      constexpr int EW = D / 4;   // accumulator columns per warp group
 #pragma unroll
       for (int acc = 0; acc < (DKDV ? 2 : 1); ++acc) {
         __nv_bfloat16* dst = acc == 0 ? o0 : o1;

@@ -251,8 +251,8 @@ int bwd_tc(const TArg& r0, const TArg& r1, const TArg& c0, const TArg& c1, const
   int rc;
   if ((rc = make_map(&m0, r0, B, H, T, D, C::BM))) return rc;
   if ((rc = make_map(&m1, r1, B, H, T, D, C::BM))) return rc;
-  if ((rc = make_map(&mc0, c0, B, H, T, D, C::CN))) return rc;
-  if ((rc = make_map(&mc1, c1, B, H, T, D, C::CN))) return rc;
+  if ((rc = make_map(&mc0, c0, B, H, T, D, C::BOX))) return rc;
+  if ((rc = make_map(&mc1, c1, B, H, T, D, C::BOX))) return rc;
   BwdParams p{};
   p.indptr = indptr;
   p.indices = indices;
