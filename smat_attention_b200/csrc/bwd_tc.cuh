@@ -147,9 +147,7 @@ __global__ void __launch_bounds__(BwdCfg<DKDV, D>::THREADS, 1)
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int BH = p.B * p.H;
   const int lin = blockIdx.x;
-  const int bh = lin % BH;
-  // dQ: latest query tiles are the heaviest; dK/dV: earliest key tiles are
-  // (sinks and summaries are read by every later query)
+  int bh = lin % BH;
   int tile;
   if (p.work) {
     // caller-chosen tiles (a shard of the rows), in the caller's order
@@ -160,7 +158,13 @@ __global__ void __launch_bounds__(BwdCfg<DKDV, D>::THREADS, 1)
       return;
     }
   } else {
-    tile = DKDV ? lin / BH : p.n_tiles - 1 - lin / BH;
+    // all tiles of one (b, h) back to back, so the CTAs resident at a time
+    // share that head's streamed chunks in L2; heaviest first within a head
+    // (dQ: the latest query tiles; dK/dV: the earliest key tiles, since sinks
+    // and summaries are read by every later query)
+    bh = lin / p.n_tiles;
+    const int t = lin % p.n_tiles;
+    tile = DKDV ? t : p.n_tiles - 1 - t;
   }
   const int b = bh / p.H, h = bh % p.H;
   const int sub = C::BM / p.bs;   // CSR rows per tile: 1 or 2
