@@ -52,30 +52,6 @@ struct BwdParams {
   int32_t* err;
 };
 
-// Chunks of 128 streamed rows: 128 / bs consecutive entries of the merged
-// CSR rows of the tile (one entry for bs = 128, two for bs = 64).  A missing
-// second entry is 0 (no row states).
-struct ChunkPair {
-  MergeIter<2> it;
-  int epc;
-  __device__ __forceinline__ void init(const int32_t* indptr, const int32_t* indices,
-                                       const uint8_t* kinds, int nblocks, int nnzb, int row0,
-                                       int nrows, int bs, int32_t* err) {
-    it.init(indptr, indices, kinds, nblocks, nnzb, row0, nrows, err);
-    epc = 128 / bs;
-  }
-  __device__ __forceinline__ bool next(uint32_t* e, int32_t* err) {
-    if (!it.next(e[0], err)) return false;
-    e[1] = 0u;
-    if (epc == 2) {
-      uint32_t t;
-      if (it.next(t, err)) e[1] = t;
-    }
-    return true;
-  }
-};
-__device__ __forceinline__ bool entry_present(uint32_t e) { return (e >> 24) != 0u; }
-
 template <bool DKDV, int D>
 struct BwdCfg {
   static constexpr int BM = 128;     // tile rows
@@ -206,7 +182,7 @@ __global__ void __launch_bounds__(BwdCfg<DKDV, D>::THREADS, 1)
     // Lane 0 issues the TMA loads; for dK/dV all 32 lanes also copy the
     // chunk's lse and delta next to it with cp.async, tracked by the same
     // stage barrier, so nobody waits on a global load.
-    ChunkPair it;
+    ChunkPair<2> it;
     it.init(p.indptr, p.indices, p.kind, p.nblocks, p.nnzb, row0, sub, p.bs, p.err);
     if (lane == 0) {
       mbar_expect_tx(bar(C::BAR_R), 2 * C::ROW_BYTES);
@@ -275,7 +251,7 @@ __global__ void __launch_bounds__(BwdCfg<DKDV, D>::THREADS, 1)
   } else if (warp == C::MMA_WARP) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
-      ChunkPair it;
+      ChunkPair<2> it;
       it.init(p.indptr, p.indices, p.kind, p.nblocks, p.nnzb, row0, sub, p.bs, p.err);
       // S (S^T) of chunk j:  R0 . C0_j^T;  dP (dP^T):  R1 . C1_j^T
       auto issue_sd = [&](int j, bool dp) {
@@ -403,7 +379,7 @@ __global__ void __launch_bounds__(BwdCfg<DKDV, D>::THREADS, 1)
       }
     }
     int n = 0;
-    ChunkPair it;
+    ChunkPair<2> it;
     it.init(p.indptr, p.indices, p.kind, p.nblocks, p.nnzb, row0, sub, p.bs, p.err);
     uint32_t e[2];
     for (int j = 0; alive && it.next(e, p.err); ++j) {

@@ -3,24 +3,30 @@
 // One CTA computes TWO adjacent 128-row query tiles of one (batch, head).
 // Their CSR rows overlap almost entirely (same sinks and summary blocks,
 // windows shifted by one block), so the CTA walks the union of the rows in
-// 64-key chunks, loads each K/V chunk once, and runs it against whichever of
-// the two tiles it is active for:
+// chunks of 128 keys, loads each K/V chunk once, and runs it against
+// whichever of the two tiles it is active for:
 //
-//   S_x  = Q_x K^T          tcgen05.mma, A = Q_x (smem), B = K (smem), D in TMEM
+//   S_x  = Q_x K^T          tcgen05.mma 128 x 128, A = Q_x (smem), B = K (smem)
 //   P_x  = exp2(S_x c - m)  softmax warpgroup x, online max, lazy rescale;
 //                           P (bf16) is written back over S_x in TMEM
-//   O_x += P_x V            tcgen05.mma, A = P_x (TMEM), B = V (smem, MN-major)
+//   O_x += P_x V            tcgen05.mma 128 x D, A = P_x (TMEM), B = V (smem, MN-major)
 //
-// While warpgroup 0 turns S_0 into P_0, the tensor core works on tile 1 and
-// the other way round.  Warp roles (320 threads):
+// Every MMA has N = 128 (or D): on B200 an N = 64 MMA costs nearly as many
+// cycles as an N = 128 one.  Each tile has one S buffer (TMEM: S_x 128
+// columns + O_x D columns per tile); the MMA warp alternates the tiles --
+// PV_0(j), S_0(j+1), PV_1(j), S_1(j+1) -- so while warpgroup 0 turns S_0 into
+// P_0 the tensor core works on tile 1, and the other way round.  With
+// bs = 64 a chunk is two 64-key blocks of the merged list; a missing second
+// half is loaded from row T (zero-filled) and masked.
+//
+// Warp roles (320 threads):
 //   warps 0-3 / 4-7  softmax + epilogue of tile 0 / tile 1; thread r of a
 //                    warpgroup owns row r of its tile = TMEM lane r
 //   warp 8           TMA producer (both Q tiles once, then the K/V ring)
 //   warp 9           TMEM allocator and MMA issuer (one lane)
-// TMEM (512 columns): tile x owns [256 x, 256 x + 256): S / P double buffer
-// at +0 / +64 (P packs two bf16 per column into the first 32), O at +128.
-// Shared memory (SWIZZLE_128B panels of 64 bf16 columns, 128-byte rows):
-// Q [2][128 x D], K ring and V ring [STAGES][64 x D].
+// P of key half h (keys 64 h .. 64 h + 63) is packed into the first 32 of
+// that half's own S columns; the softmax reads S a quarter (32 keys) at a
+// time, so a thread only overwrites scores it has already read.
 // Masked scores become -inf before the row max, so a key outside the mask
 // never enters the max or the sum.
 #pragma once
@@ -45,57 +51,36 @@ struct FwdParams {
 
 template <int D>
 struct FwdCfg {
-  static constexpr int BM = 128, NT = 2, BN = 64;
+  static constexpr int BM = 128, NT = 2, BN = 128, BOX = 64;
   static constexpr int Q_BYTES = BM * D * 2;
   static constexpr int KV_BYTES = BN * D * 2;
-  // as many K/V stages as the shared memory holds (at most 8): the ring hides
-  // the L2 -> shared latency of the loads
-  static constexpr int FIXED = NT * Q_BYTES + 1536;  // + barriers, alignment
+  static constexpr int PANEL_Q = BM * 128, PANEL_KV = BN * 128;  // 64-column SW128 panels
+  // as many K/V stages as the shared memory holds (at most 8)
+  static constexpr int FIXED = NT * Q_BYTES + 2048;  // + barriers, alignment
   static constexpr int STAGES_FIT = (227 * 1024 - FIXED) / (2 * KV_BYTES);
   static constexpr int STAGES = STAGES_FIT > 8 ? 8 : STAGES_FIT;
   static constexpr int OFF_Q = 0;
   static constexpr int OFF_K = OFF_Q + NT * Q_BYTES;
   static constexpr int OFF_V = OFF_K + STAGES * KV_BYTES;
   static constexpr int OFF_BAR = OFF_V + STAGES * KV_BYTES;
-  // barriers: q_full, kv_full[S], kv_empty[S], s_full[NT][2], p_full[NT][2], pv_done[NT], drain
+  // barriers: q_full, kv_full[S], kv_empty[S], s_full[NT], p_full[NT], pv_done[NT], drain
   static constexpr int BAR_Q = 0, BAR_KVF = 1, BAR_KVE = 1 + STAGES, BAR_SF = 1 + 2 * STAGES,
-                       BAR_PF = BAR_SF + 2 * NT, BAR_PV = BAR_PF + 2 * NT, BAR_DRAIN = BAR_PV + NT,
+                       BAR_PF = BAR_SF + NT, BAR_PV = BAR_PF + NT, BAR_DRAIN = BAR_PV + NT,
                        NBAR = BAR_DRAIN + 1;
   static constexpr int OFF_MISC = OFF_BAR + NBAR * 8;  // tmem ptr, abort flag
   static constexpr int SMEM_BYTES = OFF_MISC + 16 + 1024;  // + alignment slack
   static_assert(SMEM_BYTES <= 227 * 1024, "shared memory budget");
   static_assert(STAGES >= 2, "at least two stages");
   static constexpr int TMEM_COLS = 512, TILE_COLS = 256, COL_O = 128;
+  static_assert(COL_O + D <= TILE_COLS, "TMEM budget");
   static constexpr int THREADS = 320;
   static constexpr uint32_t IDESC_S = idesc_bf16(BM, BN, false, false);
   static constexpr uint32_t IDESC_O = idesc_bf16(BM, D, false, true);
 };
 
-// Walks a merged CSR schedule in 64-row chunks (blocks of 128 rows give two
-// chunks each).
-template <int MAXROWS>
-struct ChunkIter {
-  MergeIter<MAXROWS> it;
-  uint32_t e;
-  int sub, cpb;
-  __device__ __forceinline__ void init(const int32_t* indptr, const int32_t* indices,
-                                       const uint8_t* kind, int nblocks, int nnzb, int row0,
-                                       int nrows, int cpb_, int32_t* err) {
-    it.init(indptr, indices, kind, nblocks, nnzb, row0, nrows, err);
-    cpb = cpb_;
-    sub = cpb_;
-    e = 0;
-  }
-  __device__ __forceinline__ bool next(uint32_t& entry, int& c, int32_t* err) {
-    if (sub >= cpb) {
-      if (!it.next(e, err)) return false;
-      sub = 0;
-    }
-    entry = e;
-    c = sub++;
-    return true;
-  }
-};
+// TMEM column of P's k-step kk (16 keys): key half kk / 4 packed at the start
+// of that half's S columns
+__device__ __forceinline__ uint32_t p_col(int kk) { return 64u * (kk >> 2) + 8u * (kk & 3); }
 
 template <int D>
 __global__ void __launch_bounds__(320, 1)
@@ -132,8 +117,11 @@ __global__ void __launch_bounds__(320, 1)
   }
   const int b = bh / p.H, h = bh % p.H;
   const int sub = C::BM / p.bs;   // CSR rows per tile: 1 (bs 128) or 2 (bs 64)
-  const int cpb = p.bs / C::BN;   // chunks per block: 2 (bs 128) or 1 (bs 64)
   const int row0 = tile0 * sub;
+  // is entry pair e active for tile x (any of its CSR rows)?
+  auto active = [&](const uint32_t* e, int x) {
+    return (sched_states(e[0], x * sub, sub) | sched_states(e[1], x * sub, sub)) != 0u;
+  };
 
   if (tid == 0) {
     mbar_init(bar(C::BAR_Q), 1);
@@ -141,11 +129,11 @@ __global__ void __launch_bounds__(320, 1)
       mbar_init(bar(C::BAR_KVF + s), 1);
       mbar_init(bar(C::BAR_KVE + s), 1);
     }
-    for (int i = 0; i < 2 * C::NT; ++i) {
-      mbar_init(bar(C::BAR_SF + i), 1);
-      mbar_init(bar(C::BAR_PF + i), 4);
+    for (int x = 0; x < C::NT; ++x) {
+      mbar_init(bar(C::BAR_SF + x), 1);
+      mbar_init(bar(C::BAR_PF + x), 4);
+      mbar_init(bar(C::BAR_PV + x), 1);
     }
-    for (int x = 0; x < C::NT; ++x) mbar_init(bar(C::BAR_PV + x), 1);
     mbar_init(bar(C::BAR_DRAIN), 1);
     fence_barrier_init();
     misc[1] = 0;
@@ -167,32 +155,42 @@ __global__ void __launch_bounds__(320, 1)
   if (warp == 8) {
     // ------------------------------------------------------------ producer
     if (lane == 0) {
-      ChunkIter<4> it;
-      it.init(p.indptr, p.indices, p.kind, p.nblocks, p.nnzb, row0, ntile * sub, cpb, p.err);
+      ChunkPair<4> it;
+      it.init(p.indptr, p.indices, p.kind, p.nblocks, p.nnzb, row0, ntile * sub, p.bs, p.err);
       mbar_expect_tx(bar(C::BAR_Q), C::NT * C::Q_BYTES);
 #pragma unroll
       for (int x = 0; x < C::NT; ++x)
 #pragma unroll
         for (int pn = 0; pn < D / 64; ++pn)
-          tma_load_4d(sbase + C::OFF_Q + x * C::Q_BYTES + pn * (C::BM * 128), &tm_q,
-                      bar(C::BAR_Q), pn * 64, (tile0 + x) * C::BM, h, b);
+          tma_load_4d(sbase + C::OFF_Q + x * C::Q_BYTES + pn * C::PANEL_Q, &tm_q, bar(C::BAR_Q),
+                      pn * 64, (tile0 + x) * C::BM, h, b);
       int issued = 0;
-      uint32_t e;
-      int c;
-      for (int j = 0; it.next(e, c, p.err); ++j) {
+      uint32_t e[2];
+      for (int j = 0; it.next(e, p.err); ++j) {
         const int s = j % C::STAGES;
         if (j >= C::STAGES &&
             !mbar_wait(bar(C::BAR_KVE + s), ((j / C::STAGES) - 1) & 1, abort_flag, p.err))
           break;
-        const int row = static_cast<int>(sched_block(e)) * p.bs + c * C::BN;
+        // first key of each 64-key half; a missing half reads row T onwards,
+        // which TMA fills with zeros
+        int krow[2];
+#pragma unroll
+        for (int q = 0; q < 2; ++q) {
+          const uint32_t eq = (p.bs == 64) ? e[q] : e[0];
+          krow[q] = entry_present(eq) ? static_cast<int>(sched_block(eq)) * p.bs + (q * 64) % p.bs
+                                      : p.T;
+        }
         mbar_expect_tx(bar(C::BAR_KVF + s), 2 * C::KV_BYTES);
 #pragma unroll
-        for (int pn = 0; pn < D / 64; ++pn) {
-          tma_load_4d(sbase + C::OFF_K + s * C::KV_BYTES + pn * (C::BN * 128), &tm_k,
-                      bar(C::BAR_KVF + s), pn * 64, row, h, b);
-          tma_load_4d(sbase + C::OFF_V + s * C::KV_BYTES + pn * (C::BN * 128), &tm_v,
-                      bar(C::BAR_KVF + s), pn * 64, row, h, b);
-        }
+        for (int pn = 0; pn < D / 64; ++pn)
+#pragma unroll
+          for (int q = 0; q < 2; ++q) {
+            const uint32_t off = s * C::KV_BYTES + pn * C::PANEL_KV + q * (C::BOX * 128);
+            tma_load_4d(sbase + C::OFF_K + off, &tm_k, bar(C::BAR_KVF + s), pn * 64, krow[q], h,
+                        b);
+            tma_load_4d(sbase + C::OFF_V + off, &tm_v, bar(C::BAR_KVF + s), pn * 64, krow[q], h,
+                        b);
+          }
         issued = j + 1;
       }
       mbar_wait_drain(bar(C::BAR_Q), 0);  // Q is always loaded; never exit with it in flight
@@ -204,83 +202,85 @@ __global__ void __launch_bounds__(320, 1)
   } else if (warp == 9) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
-      ChunkIter<4> it;
-      it.init(p.indptr, p.indices, p.kind, p.nblocks, p.nnzb, row0, ntile * sub, cpb, p.err);
-      int cs[C::NT] = {0, 0}, cp[C::NT] = {0, 0};
-      auto active = [&](uint32_t e, int x) { return sched_states(e, x * sub, sub) != 0; };
-      auto issue_s = [&](int j, uint32_t e) {
-        const int s = j % C::STAGES;
-        const uint32_t ka = sbase + C::OFF_K + s * C::KV_BYTES;
+      ChunkPair<4> it;
+      it.init(p.indptr, p.indices, p.kind, p.nblocks, p.nnzb, row0, ntile * sub, p.bs, p.err);
+      int cp[C::NT] = {0, 0};   // PVs issued per tile
+      // S_x of chunk j (stage j % STAGES)
+      auto issue_s = [&](int j, int x) {
+        const uint32_t ka = sbase + C::OFF_K + (j % C::STAGES) * C::KV_BYTES;
+        const uint32_t qa = sbase + C::OFF_Q + x * C::Q_BYTES;
+        const uint32_t dst = tbase + x * C::TILE_COLS;
 #pragma unroll
-        for (int x = 0; x < C::NT; ++x) {
-          if (!active(e, x)) continue;
-          const uint32_t qa = sbase + C::OFF_Q + x * C::Q_BYTES;
-          const uint32_t dst = tbase + x * C::TILE_COLS + (cs[x] & 1) * C::BN;
-#pragma unroll
-          for (int kk = 0; kk < D / 16; ++kk) {
-            const uint32_t off = (kk & 3) * 32u;
-            tc_mma(dst, sdesc_sw128(qa + (kk >> 2) * (C::BM * 128) + off, 16, 1024),
-                   sdesc_sw128(ka + (kk >> 2) * (C::BN * 128) + off, 16, 1024), C::IDESC_S,
-                   kk > 0 ? 1u : 0u);
-          }
-          tc_commit(bar(C::BAR_SF + 2 * x + (cs[x] & 1)));
-          ++cs[x];
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint32_t off = (kk & 3) * 32u;
+          tc_mma(dst, sdesc_sw128(qa + (kk >> 2) * C::PANEL_Q + off, 16, 1024),
+                 sdesc_sw128(ka + (kk >> 2) * C::PANEL_KV + off, 16, 1024), C::IDESC_S,
+                 kk > 0 ? 1u : 0u);
         }
+        tc_commit(bar(C::BAR_SF + x));
       };
       bool ok = mbar_wait(bar(C::BAR_Q), 0, abort_flag, p.err);
-      uint32_t e_next = 0;
-      int c_next = 0;
-      bool has = ok && it.next(e_next, c_next, p.err);
+      uint32_t e[2], en[2];
+      bool has = ok && it.next(e, p.err);
       if (has) {
         ok = mbar_wait(bar(C::BAR_KVF + 0), 0, abort_flag, p.err);
         if (ok) {
           tc_fence_after();
-          issue_s(0, e_next);
+#pragma unroll
+          for (int x = 0; x < C::NT; ++x)
+            if (active(e, x)) issue_s(0, x);
         }
       }
       for (int j = 0; ok && has; ++j) {
-        const uint32_t e = e_next;
-        has = it.next(e_next, c_next, p.err);
-        // S of the next chunk goes first if its K/V already landed; otherwise
-        // the PVs of this chunk are not held up behind that load
-        bool early = false;
-        if (has && mbar_try_wait(bar(C::BAR_KVF + (j + 1) % C::STAGES), ((j + 1) / C::STAGES) & 1)) {
-          tc_fence_after();
-          issue_s(j + 1, e_next);
-          early = true;
-        }
+        const bool nxt = it.next(en, p.err);
         const int s = j % C::STAGES;
+        const int s1 = (j + 1) % C::STAGES;
         const uint32_t va = sbase + C::OFF_V + s * C::KV_BYTES;
+        bool loaded = false;     // K/V of chunk j + 1 have landed
+        bool pending[C::NT] = {false, false};
 #pragma unroll
         for (int x = 0; x < C::NT; ++x) {
-          if (!active(e, x)) continue;
-          if (!mbar_wait(bar(C::BAR_PF + 2 * x + (cp[x] & 1)), (cp[x] >> 1) & 1, abort_flag,
-                         p.err)) {
-            ok = false;
-            break;
-          }
-          tc_fence_after();
-          const uint32_t pa = tbase + x * C::TILE_COLS + (cp[x] & 1) * C::BN;   // P in TMEM
-          const uint32_t dst = tbase + x * C::TILE_COLS + C::COL_O;
+          if (active(e, x)) {
+            if (!mbar_wait(bar(C::BAR_PF + x), cp[x] & 1, abort_flag, p.err)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            const uint32_t pa = tbase + x * C::TILE_COLS;   // P in TMEM
+            const uint32_t dst = pa + C::COL_O;
 #pragma unroll
-          for (int kk = 0; kk < C::BN / 16; ++kk) {
-            // A: 16 keys = 8 packed columns per k-step.  V is MN-major:
-            // 64-column panels BN*128 bytes apart (LBO), 8-row groups 1024
-            // bytes apart (SBO); 16 rows per k-step = 2048 bytes.
-            tc_mma_ts(dst, pa + kk * 8, sdesc_sw128(va + kk * 2048, C::BN * 128, 1024),
-                      C::IDESC_O, (cp[x] > 0 || kk > 0) ? 1u : 0u);
+            for (int kk = 0; kk < C::BN / 16; ++kk) {
+              // V is MN-major: 64-column panels BN*128 bytes apart (LBO),
+              // 8-row groups 1024 bytes apart (SBO); 16 rows per k-step
+              tc_mma_ts(dst, pa + p_col(kk), sdesc_sw128(va + kk * 2048, C::PANEL_KV, 1024),
+                        C::IDESC_O, (cp[x] > 0 || kk > 0) ? 1u : 0u);
+            }
+            tc_commit(bar(C::BAR_PV + x));
+            ++cp[x];
           }
-          tc_commit(bar(C::BAR_PV + x));
-          ++cp[x];
+          // the tile's next S goes in behind its PV if the K chunk has landed
+          if (nxt && active(en, x)) {
+            if (!loaded) loaded = mbar_try_wait(bar(C::BAR_KVF + s1), ((j + 1) / C::STAGES) & 1);
+            if (loaded) {
+              tc_fence_after();
+              issue_s(j + 1, x);
+            } else {
+              pending[x] = true;
+            }
+          }
         }
         if (!ok) break;
         tc_commit(bar(C::BAR_KVE + s));
-        if (has && !early) {
-          const int s1 = (j + 1) % C::STAGES;
+        if (pending[0] || pending[1]) {
           if (!mbar_wait(bar(C::BAR_KVF + s1), ((j + 1) / C::STAGES) & 1, abort_flag, p.err)) break;
           tc_fence_after();
-          issue_s(j + 1, e_next);
+#pragma unroll
+          for (int x = 0; x < C::NT; ++x)
+            if (pending[x]) issue_s(j + 1, x);
         }
+        e[0] = en[0];
+        e[1] = en[1];
+        has = nxt;
       }
       if (*abort_flag) {  // let the MMAs in flight finish before TMEM is freed
         tc_commit(bar(C::BAR_DRAIN));
@@ -299,33 +299,47 @@ __global__ void __launch_bounds__(320, 1)
     float m = -INFINITY, l = 0.f;
     int cnt = 0;
     bool alive = true;
-    ChunkIter<4> it;
-    it.init(p.indptr, p.indices, p.kind, p.nblocks, p.nnzb, row0, ntile * sub, cpb, p.err);
-    uint32_t e;
-    int c;
-    while (alive && it.next(e, c, p.err)) {
-      if (sched_states(e, x * sub, sub) == 0) continue;
-      const uint32_t st = sched_state(e, srow);
-      const int k0 = static_cast<int>(sched_block(e)) * p.bs + c * C::BN;
-      if (!__all_sync(0xffffffffu, mbar_wait(bar(C::BAR_SF + 2 * x + (cnt & 1)), (cnt >> 1) & 1,
-                                             abort_flag, p.err))) {
+    ChunkPair<4> it;
+    it.init(p.indptr, p.indices, p.kind, p.nblocks, p.nnzb, row0, ntile * sub, p.bs, p.err);
+    uint32_t e[2];
+    while (alive && it.next(e, p.err)) {
+      if (!active(e, x)) continue;
+      // per 64-key half: state of this row (warp-uniform) and first key
+      uint32_t st[2];
+      int k0[2];
+#pragma unroll
+      for (int hf = 0; hf < 2; ++hf) {
+        const uint32_t eh = (p.bs == 64) ? e[hf] : e[0];
+        st[hf] = entry_present(eh) ? sched_state(eh, srow) : ST_ABSENT;
+        k0[hf] = static_cast<int>(sched_block(eh)) * p.bs + (hf * 64) % p.bs;
+      }
+      if (!__all_sync(0xffffffffu,
+                      mbar_wait(bar(C::BAR_SF + x), cnt & 1, abort_flag, p.err))) {
         alive = false;
         break;
       }
       tc_fence_after();
-      float s[C::BN];
-      tmem_ld64(lane_base + (cnt & 1) * C::BN, s);
-      if (st != ST_FULL) {   // uniform per warp: its 32 rows share one CSR row
+      // quarter qq (32 keys, TMEM columns 32 qq ..): mask of this row
+      auto mask = [&](float* s, int qq) {
+        const uint32_t sq = (qq >> 1) ? st[1] : st[0];
+        if (sq != ST_FULL) {   // uniform per warp: its 32 rows share one CSR row
+          const int kq = ((qq >> 1) ? k0[1] : k0[0]) + 32 * (qq & 1);
 #pragma unroll
-        for (int i = 0; i < C::BN; ++i)
-          if (!(st == ST_CAUSAL && k0 + i <= q_pos)) s[i] = -INFINITY;
-      }
-      // row max of the raw scores (scale > 0), eight independent chains
+          for (int i = 0; i < 32; ++i)
+            if (!(sq == ST_CAUSAL && kq + i <= q_pos)) s[i] = -INFINITY;
+        }
+      };
+      float s[32];
       float mx8[8];
 #pragma unroll
-      for (int a = 0; a < 8; ++a) mx8[a] = s[a];
+      for (int a = 0; a < 8; ++a) mx8[a] = -INFINITY;
+#pragma unroll 1
+      for (int qq = 0; qq < 4; ++qq) {
+        tmem_ld32(lane_base + 32 * qq, s);
+        mask(s, qq);
 #pragma unroll
-      for (int i = 8; i < C::BN; ++i) mx8[i & 7] = fmaxf(mx8[i & 7], s[i]);
+        for (int i = 0; i < 32; ++i) mx8[i & 7] = fmaxf(mx8[i & 7], s[i]);
+      }
 #pragma unroll
       for (int w = 4; w > 0; w >>= 1)
 #pragma unroll
@@ -338,20 +352,25 @@ __global__ void __launch_bounds__(320, 1)
         l *= alpha;
         m = m_new;
       }
-      // exponentials first: they do not depend on the previous PV
       const float neg_m = (m == -INFINITY) ? 0.f : -m;
       float rs8[8];
-      uint32_t pw[C::BN / 2];
 #pragma unroll
-      for (int i = 0; i < C::BN / 2; ++i) {
-        const float a = ex2_approx(fmaf(s[2 * i], p.scale_log2, neg_m));
-        const float bb = ex2_approx(fmaf(s[2 * i + 1], p.scale_log2, neg_m));
-        if (i < 8) {
-          rs8[i] = a + bb;
-        } else {
+      for (int a = 0; a < 8; ++a) rs8[a] = 0.f;
+      // P of quarter qq packed into 16 columns at the start of its half's S
+      // columns (64 h + 16 (qq % 2)): only scores already read are overwritten
+#pragma unroll 1
+      for (int qq = 0; qq < 4; ++qq) {
+        tmem_ld32(lane_base + 32 * qq, s);
+        mask(s, qq);
+        uint32_t pw[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          const float a = ex2_approx(fmaf(s[2 * i], p.scale_log2, neg_m));
+          const float bb = ex2_approx(fmaf(s[2 * i + 1], p.scale_log2, neg_m));
           rs8[i & 7] += a + bb;
+          pw[i] = pack_bf16(a, bb);
         }
-        pw[i] = pack_bf16(a, bb);
+        tmem_st16u(lane_base + 64 * (qq >> 1) + 16 * (qq & 1), pw);
       }
 #pragma unroll
       for (int w = 4; w > 0; w >>= 1)
@@ -374,14 +393,11 @@ __global__ void __launch_bounds__(320, 1)
           for (int i = 0; i < 32; ++i) ov[i] *= alpha;
           tmem_st32(lane_base + C::COL_O + cc, ov);
         }
-        tmem_st_wait();
       }
-      // P over the S columns this thread has already read
-      tmem_st32u(lane_base + (cnt & 1) * C::BN, pw);
       tmem_st_wait();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(bar(C::BAR_PF + 2 * x + (cnt & 1)));
+      if (lane == 0) mbar_arrive(bar(C::BAR_PF + x));
       ++cnt;
     }
     // ------------------------------------------------------------ epilogue

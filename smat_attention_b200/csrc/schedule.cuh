@@ -105,4 +105,29 @@ struct MergeIter {
   }
 };
 
+// Chunks of 128 streamed rows: 128 / bs consecutive entries of the merged
+// list (one entry for bs = 128, two for bs = 64).  A missing second entry is
+// 0 (no row states).
+template <int MAXROWS>
+struct ChunkPair {
+  MergeIter<MAXROWS> it;
+  int epc;
+  __device__ __forceinline__ void init(const int32_t* indptr, const int32_t* indices,
+                                       const uint8_t* kinds, int nblocks, int nnzb, int row0,
+                                       int nrows, int bs, int32_t* err) {
+    it.init(indptr, indices, kinds, nblocks, nnzb, row0, nrows, err);
+    epc = 128 / bs;
+  }
+  __device__ __forceinline__ bool next(uint32_t* e, int32_t* err) {
+    if (!it.next(e[0], err)) return false;
+    e[1] = 0u;
+    if (epc == 2) {
+      uint32_t t;
+      if (it.next(t, err)) e[1] = t;
+    }
+    return true;
+  }
+};
+__device__ __forceinline__ bool entry_present(uint32_t e) { return (e >> 24) != 0u; }
+
 }  // namespace smat

@@ -136,8 +136,8 @@ int fwd_tc(const TArg& q, const TArg& k, const TArg& v, const TArg& o, float* ls
   CUtensorMap mq, mk, mv;
   int rc;
   if ((rc = make_map(&mq, q, B, H, T, D, C::BM))) return rc;
-  if ((rc = make_map(&mk, k, B, H, T, D, C::BN))) return rc;
-  if ((rc = make_map(&mv, v, B, H, T, D, C::BN))) return rc;
+  if ((rc = make_map(&mk, k, B, H, T, D, C::BOX))) return rc;
+  if ((rc = make_map(&mv, v, B, H, T, D, C::BOX))) return rc;
   FwdParams p{};
   p.indptr = indptr;
   p.indices = indices;
