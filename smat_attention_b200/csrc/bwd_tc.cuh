@@ -407,23 +407,25 @@ __global__ void __launch_bounds__(BwdCfg<DKDV, D>::THREADS, 1)
       // warp-uniform: no element of this warp's 32 x 32 block is masked
       const bool all_valid = (st == ST_FULL) && (!DKDV || cbase + C::CW <= p.T);
       const float4* l4 = reinterpret_cast<const float4*>(ldj + col0);
+      const uint64_t c2 = f2_bits(p.scale_log2, p.scale_log2);
+      const uint64_t nlog2e2 = f2_bits(-LOG2E, -LOG2E);
 #pragma unroll
       for (int q = 0; q < C::CW / 4; ++q) {
-        float nl[4];
+        // exponent arguments s c - lse log2 e, two columns per f32x2 op
+        uint64_t nl01, nl23;
         if (DKDV) {
           const float4 a4 = l4[q];
-          nl[0] = a4.x * -LOG2E;
-          nl[1] = a4.y * -LOG2E;
-          nl[2] = a4.z * -LOG2E;
-          nl[3] = a4.w * -LOG2E;
+          nl01 = fmul2(f2_bits(a4.x, a4.y), nlog2e2);
+          nl23 = fmul2(f2_bits(a4.z, a4.w), nlog2e2);
         } else {
-#pragma unroll
-          for (int i = 0; i < 4; ++i) nl[i] = -row_lse2;
+          nl01 = nl23 = f2_bits(-row_lse2, -row_lse2);
         }
+        float x[4];
+        f2_split(ffma2(f2_bits(pv[4 * q], pv[4 * q + 1]), c2, nl01), x[0], x[1]);
+        f2_split(ffma2(f2_bits(pv[4 * q + 2], pv[4 * q + 3]), c2, nl23), x[2], x[3]);
         if (all_valid) {
 #pragma unroll
-          for (int i = 0; i < 4; ++i)
-            pv[4 * q + i] = ex2_approx(fmaf(pv[4 * q + i], p.scale_log2, nl[i]));
+          for (int i = 0; i < 4; ++i) pv[4 * q + i] = ex2_approx(x[i]);
         } else {
 #pragma unroll
           for (int i = 0; i < 4; ++i) {
@@ -432,7 +434,7 @@ __global__ void __launch_bounds__(BwdCfg<DKDV, D>::THREADS, 1)
             const bool valid =
                 DKDV ? ((st == ST_FULL || (st == ST_CAUSAL && cpos >= pos)) && cpos < p.T)
                      : (st == ST_FULL || (st == ST_CAUSAL && cpos <= pos));
-            pv[4 * q + i] = valid ? ex2_approx(fmaf(pv[4 * q + i], p.scale_log2, nl[i])) : 0.f;
+            pv[4 * q + i] = valid ? ex2_approx(x[i]) : 0.f;
           }
         }
       }
@@ -473,9 +475,16 @@ __global__ void __launch_bounds__(BwdCfg<DKDV, D>::THREADS, 1)
             for (int i = 0; i < 4; ++i) dl[i] = row_delta;
           }
           const int k = 16 * hf + 4 * q;
-          wd[k / 2] = pack_bf16(pv[k] * (dp[4 * q] - dl[0]), pv[k + 1] * (dp[4 * q + 1] - dl[1]));
-          wd[k / 2 + 1] =
-              pack_bf16(pv[k + 2] * (dp[4 * q + 2] - dl[2]), pv[k + 3] * (dp[4 * q + 3] - dl[3]));
+          // dS = P (dP - delta), two columns per f32x2 op
+          float d[4];
+          f2_split(fmul2(f2_bits(pv[k], pv[k + 1]),
+                         fsub2(f2_bits(dp[4 * q], dp[4 * q + 1]), f2_bits(dl[0], dl[1]))),
+                   d[0], d[1]);
+          f2_split(fmul2(f2_bits(pv[k + 2], pv[k + 3]),
+                         fsub2(f2_bits(dp[4 * q + 2], dp[4 * q + 3]), f2_bits(dl[2], dl[3]))),
+                   d[2], d[3]);
+          wd[k / 2] = pack_bf16(d[0], d[1]);
+          wd[k / 2 + 1] = pack_bf16(d[2], d[3]);
         }
       }
       tmem_st16u(lane_base + C::COL_DP + col0, wd);

@@ -353,9 +353,10 @@ __global__ void __launch_bounds__(320, 1)
         m = m_new;
       }
       const float neg_m = (m == -INFINITY) ? 0.f : -m;
-      float rs8[8];
+      const uint64_t c2 = f2_bits(p.scale_log2, p.scale_log2), nm2 = f2_bits(neg_m, neg_m);
+      uint64_t rs2[4];   // row-sum partials, two lanes each (f32x2)
 #pragma unroll
-      for (int a = 0; a < 8; ++a) rs8[a] = 0.f;
+      for (int a = 0; a < 4; ++a) rs2[a] = 0ull;
       // P of quarter qq packed into 16 columns at the start of its half's S
       // columns (64 h + 16 (qq % 2)): only scores already read are overwritten
 #pragma unroll 1
@@ -365,18 +366,18 @@ __global__ void __launch_bounds__(320, 1)
         uint32_t pw[16];
 #pragma unroll
         for (int i = 0; i < 16; ++i) {
-          const float a = ex2_approx(fmaf(s[2 * i], p.scale_log2, neg_m));
-          const float bb = ex2_approx(fmaf(s[2 * i + 1], p.scale_log2, neg_m));
-          rs8[i & 7] += a + bb;
+          float xa, xb;
+          f2_split(ffma2(f2_bits(s[2 * i], s[2 * i + 1]), c2, nm2), xa, xb);
+          const float a = ex2_approx(xa), bb = ex2_approx(xb);
+          rs2[i & 3] = fadd2(rs2[i & 3], f2_bits(a, bb));
           pw[i] = pack_bf16(a, bb);
         }
         tmem_st16u(lane_base + 64 * (qq >> 1) + 16 * (qq & 1), pw);
       }
-#pragma unroll
-      for (int w = 4; w > 0; w >>= 1)
-#pragma unroll
-        for (int a = 0; a < w; ++a) rs8[a] += rs8[a + w];
-      l += rs8[0];
+      rs2[0] = fadd2(fadd2(rs2[0], rs2[1]), fadd2(rs2[2], rs2[3]));
+      float rlo, rhi;
+      f2_split(rs2[0], rlo, rhi);
+      l += rlo + rhi;
       // O may be rescaled only once this tile's previous PV has completed
       if (rescale && cnt > 0) {
         if (!__all_sync(0xffffffffu, mbar_wait(bar(C::BAR_PV + x), (cnt - 1) & 1, abort_flag,
