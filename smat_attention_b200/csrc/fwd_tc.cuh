@@ -22,7 +22,8 @@
 // Warp roles (320 threads):
 //   warps 0-3 / 4-7  softmax + epilogue of tile 0 / tile 1; thread r of a
 //                    warpgroup owns row r of its tile = TMEM lane r
-//   warp 8           TMA producer (both Q tiles once, then the K/V ring)
+//   warp 8           TMA producer (lane 0: both Q tiles, then the K ring;
+//                    lane 1: the V ring)
 //   warp 9           TMEM allocator and MMA issuer (one lane)
 // P of key half h (keys 64 h .. 64 h + 63) is packed into the first 32 of
 // that half's own S columns; the softmax reads S a quarter (32 keys) at a
@@ -55,22 +56,26 @@ struct FwdCfg {
   static constexpr int Q_BYTES = BM * D * 2;
   static constexpr int KV_BYTES = BN * D * 2;
   static constexpr int PANEL_Q = BM * 128, PANEL_KV = BN * 128;  // 64-column SW128 panels
-  // as many K/V stages as the shared memory holds (at most 8)
+  // K and V have separate rings: K_j is read by S(j) only and frees its slot
+  // early, V_j by PV(j) only; the shared memory left over after Q holds
+  // KS + VS chunk slots, K taking the larger share (at most 8 each)
   static constexpr int FIXED = NT * Q_BYTES + 2048;  // + barriers, alignment
-  static constexpr int STAGES_FIT = (227 * 1024 - FIXED) / (2 * KV_BYTES);
-  static constexpr int STAGES = STAGES_FIT > 8 ? 8 : STAGES_FIT;
+  static constexpr int SLOTS = (227 * 1024 - FIXED) / KV_BYTES;
+  static constexpr int VS = (SLOTS / 2) > 8 ? 8 : SLOTS / 2;
+  static constexpr int KS = (SLOTS - VS) > 8 ? 8 : SLOTS - VS;
   static constexpr int OFF_Q = 0;
   static constexpr int OFF_K = OFF_Q + NT * Q_BYTES;
-  static constexpr int OFF_V = OFF_K + STAGES * KV_BYTES;
-  static constexpr int OFF_BAR = OFF_V + STAGES * KV_BYTES;
-  // barriers: q_full, kv_full[S], kv_empty[S], s_full[NT], p_full[NT], pv_done[NT], drain
-  static constexpr int BAR_Q = 0, BAR_KVF = 1, BAR_KVE = 1 + STAGES, BAR_SF = 1 + 2 * STAGES,
-                       BAR_PF = BAR_SF + NT, BAR_PV = BAR_PF + NT, BAR_DRAIN = BAR_PV + NT,
-                       NBAR = BAR_DRAIN + 1;
+  static constexpr int OFF_V = OFF_K + KS * KV_BYTES;
+  static constexpr int OFF_BAR = OFF_V + VS * KV_BYTES;
+  // barriers: q_full, k_full[KS], k_empty[KS], v_full[VS], v_empty[VS],
+  // s_full[NT], p_full[NT], pv_done[NT], drain
+  static constexpr int BAR_Q = 0, BAR_KF = 1, BAR_KE = 1 + KS, BAR_VF = 1 + 2 * KS,
+                       BAR_VE = BAR_VF + VS, BAR_SF = BAR_VE + VS, BAR_PF = BAR_SF + NT,
+                       BAR_PV = BAR_PF + NT, BAR_DRAIN = BAR_PV + NT, NBAR = BAR_DRAIN + 1;
   static constexpr int OFF_MISC = OFF_BAR + NBAR * 8;  // tmem ptr, abort flag
   static constexpr int SMEM_BYTES = OFF_MISC + 16 + 1024;  // + alignment slack
   static_assert(SMEM_BYTES <= 227 * 1024, "shared memory budget");
-  static_assert(STAGES >= 2, "at least two stages");
+  static_assert(KS >= 2 && VS >= 2, "at least two slots per ring");
   static constexpr int TMEM_COLS = 512, TILE_COLS = 256, COL_O = 128;
   static_assert(COL_O + D <= TILE_COLS, "TMEM budget");
   static constexpr int THREADS = 320;
@@ -125,9 +130,13 @@ __global__ void __launch_bounds__(320, 1)
 
   if (tid == 0) {
     mbar_init(bar(C::BAR_Q), 1);
-    for (int s = 0; s < C::STAGES; ++s) {
-      mbar_init(bar(C::BAR_KVF + s), 1);
-      mbar_init(bar(C::BAR_KVE + s), 1);
+    for (int s = 0; s < C::KS; ++s) {
+      mbar_init(bar(C::BAR_KF + s), 1);
+      mbar_init(bar(C::BAR_KE + s), 1);
+    }
+    for (int s = 0; s < C::VS; ++s) {
+      mbar_init(bar(C::BAR_VF + s), 1);
+      mbar_init(bar(C::BAR_VE + s), 1);
     }
     for (int x = 0; x < C::NT; ++x) {
       mbar_init(bar(C::BAR_SF + x), 1);
@@ -154,23 +163,31 @@ __global__ void __launch_bounds__(320, 1)
 
   if (warp == 8) {
     // ------------------------------------------------------------ producer
-    if (lane == 0) {
+    // lane 0: both Q tiles, then the K ring; lane 1: the V ring.  Each lane
+    // walks the schedule on its own, so a V slot that frees late never holds
+    // up the next K load.
+    if (lane < 2) {
+      const bool kl = lane == 0;
+      const int NS = kl ? C::KS : C::VS;
+      const int full = kl ? C::BAR_KF : C::BAR_VF, empty = kl ? C::BAR_KE : C::BAR_VE;
+      const uint32_t ring = sbase + (kl ? C::OFF_K : C::OFF_V);
+      const CUtensorMap* tm = kl ? &tm_k : &tm_v;
       ChunkPair<4> it;
       it.init(p.indptr, p.indices, p.kind, p.nblocks, p.nnzb, row0, ntile * sub, p.bs, p.err);
-      mbar_expect_tx(bar(C::BAR_Q), C::NT * C::Q_BYTES);
+      if (kl) {
+        mbar_expect_tx(bar(C::BAR_Q), C::NT * C::Q_BYTES);
 #pragma unroll
-      for (int x = 0; x < C::NT; ++x)
+        for (int x = 0; x < C::NT; ++x)
 #pragma unroll
-        for (int pn = 0; pn < D / 64; ++pn)
-          tma_load_4d(sbase + C::OFF_Q + x * C::Q_BYTES + pn * C::PANEL_Q, &tm_q, bar(C::BAR_Q),
-                      pn * 64, (tile0 + x) * C::BM, h, b);
+          for (int pn = 0; pn < D / 64; ++pn)
+            tma_load_4d(sbase + C::OFF_Q + x * C::Q_BYTES + pn * C::PANEL_Q, &tm_q,
+                        bar(C::BAR_Q), pn * 64, (tile0 + x) * C::BM, h, b);
+      }
       int issued = 0;
       uint32_t e[2];
       for (int j = 0; it.next(e, p.err); ++j) {
-        const int s = j % C::STAGES;
-        if (j >= C::STAGES &&
-            !mbar_wait(bar(C::BAR_KVE + s), ((j / C::STAGES) - 1) & 1, abort_flag, p.err))
-          break;
+        const int s = j % NS;
+        if (j >= NS && !mbar_wait(bar(empty + s), ((j / NS) - 1) & 1, abort_flag, p.err)) break;
         // first key of each 64-key half; a missing half reads row T onwards,
         // which TMA fills with zeros
         int krow[2];
@@ -180,23 +197,19 @@ __global__ void __launch_bounds__(320, 1)
           krow[q] = entry_present(eq) ? static_cast<int>(sched_block(eq)) * p.bs + (q * 64) % p.bs
                                       : p.T;
         }
-        mbar_expect_tx(bar(C::BAR_KVF + s), 2 * C::KV_BYTES);
+        mbar_expect_tx(bar(full + s), C::KV_BYTES);
 #pragma unroll
         for (int pn = 0; pn < D / 64; ++pn)
 #pragma unroll
-          for (int q = 0; q < 2; ++q) {
-            const uint32_t off = s * C::KV_BYTES + pn * C::PANEL_KV + q * (C::BOX * 128);
-            tma_load_4d(sbase + C::OFF_K + off, &tm_k, bar(C::BAR_KVF + s), pn * 64, krow[q], h,
-                        b);
-            tma_load_4d(sbase + C::OFF_V + off, &tm_v, bar(C::BAR_KVF + s), pn * 64, krow[q], h,
-                        b);
-          }
+          for (int q = 0; q < 2; ++q)
+            tma_load_4d(ring + s * C::KV_BYTES + pn * C::PANEL_KV + q * (C::BOX * 128), tm,
+                        bar(full + s), pn * 64, krow[q], h, b);
         issued = j + 1;
       }
-      mbar_wait_drain(bar(C::BAR_Q), 0);  // Q is always loaded; never exit with it in flight
+      if (kl) mbar_wait_drain(bar(C::BAR_Q), 0);  // never exit with Q in flight
       if (*abort_flag) {
-        for (int j = max(0, issued - C::STAGES); j < issued; ++j)
-          mbar_wait_drain(bar(C::BAR_KVF + j % C::STAGES), (j / C::STAGES) & 1);
+        for (int j = max(0, issued - NS); j < issued; ++j)
+          mbar_wait_drain(bar(full + j % NS), (j / NS) & 1);
       }
     }
   } else if (warp == 9) {
@@ -205,9 +218,9 @@ __global__ void __launch_bounds__(320, 1)
       ChunkPair<4> it;
       it.init(p.indptr, p.indices, p.kind, p.nblocks, p.nnzb, row0, ntile * sub, p.bs, p.err);
       int cp[C::NT] = {0, 0};   // PVs issued per tile
-      // S_x of chunk j (stage j % STAGES)
+      // S_x of chunk j (K slot j % KS)
       auto issue_s = [&](int j, int x) {
-        const uint32_t ka = sbase + C::OFF_K + (j % C::STAGES) * C::KV_BYTES;
+        const uint32_t ka = sbase + C::OFF_K + (j % C::KS) * C::KV_BYTES;
         const uint32_t qa = sbase + C::OFF_Q + x * C::Q_BYTES;
         const uint32_t dst = tbase + x * C::TILE_COLS;
 #pragma unroll
@@ -223,20 +236,23 @@ __global__ void __launch_bounds__(320, 1)
       uint32_t e[2], en[2];
       bool has = ok && it.next(e, p.err);
       if (has) {
-        ok = mbar_wait(bar(C::BAR_KVF + 0), 0, abort_flag, p.err);
+        ok = mbar_wait(bar(C::BAR_KF + 0), 0, abort_flag, p.err);
         if (ok) {
           tc_fence_after();
 #pragma unroll
           for (int x = 0; x < C::NT; ++x)
             if (active(e, x)) issue_s(0, x);
+          tc_commit(bar(C::BAR_KE + 0));   // every S of chunk 0 is issued
         }
       }
       for (int j = 0; ok && has; ++j) {
         const bool nxt = it.next(en, p.err);
-        const int s = j % C::STAGES;
-        const int s1 = (j + 1) % C::STAGES;
-        const uint32_t va = sbase + C::OFF_V + s * C::KV_BYTES;
-        bool loaded = false;     // K/V of chunk j + 1 have landed
+        const int sv = j % C::VS;
+        const int k1 = (j + 1) % C::KS;
+        const int k1par = ((j + 1) / C::KS) & 1;
+        const uint32_t va = sbase + C::OFF_V + sv * C::KV_BYTES;
+        if (!mbar_wait(bar(C::BAR_VF + sv), (j / C::VS) & 1, abort_flag, p.err)) break;
+        bool loaded = false;     // K of chunk j + 1 has landed
         bool pending[C::NT] = {false, false};
 #pragma unroll
         for (int x = 0; x < C::NT; ++x) {
@@ -260,7 +276,7 @@ __global__ void __launch_bounds__(320, 1)
           }
           // the tile's next S goes in behind its PV if the K chunk has landed
           if (nxt && active(en, x)) {
-            if (!loaded) loaded = mbar_try_wait(bar(C::BAR_KVF + s1), ((j + 1) / C::STAGES) & 1);
+            if (!loaded) loaded = mbar_try_wait(bar(C::BAR_KF + k1), k1par);
             if (loaded) {
               tc_fence_after();
               issue_s(j + 1, x);
@@ -270,14 +286,15 @@ __global__ void __launch_bounds__(320, 1)
           }
         }
         if (!ok) break;
-        tc_commit(bar(C::BAR_KVE + s));
+        tc_commit(bar(C::BAR_VE + sv));   // V_j is read by both PVs
         if (pending[0] || pending[1]) {
-          if (!mbar_wait(bar(C::BAR_KVF + s1), ((j + 1) / C::STAGES) & 1, abort_flag, p.err)) break;
+          if (!mbar_wait(bar(C::BAR_KF + k1), k1par, abort_flag, p.err)) break;
           tc_fence_after();
 #pragma unroll
           for (int x = 0; x < C::NT; ++x)
             if (pending[x]) issue_s(j + 1, x);
         }
+        if (nxt) tc_commit(bar(C::BAR_KE + k1));   // every S of chunk j + 1 is issued
         e[0] = en[0];
         e[1] = en[1];
         has = nxt;
