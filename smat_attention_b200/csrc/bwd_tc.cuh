@@ -73,23 +73,19 @@ struct BwdCfg {
   static constexpr int OFF_LD = OFF_C1 + STAGES * CH_BYTES;     // per stage: lse [CN], delta [CN]
   static constexpr int OFF_BAR = OFF_LD + STAGES * LD_BYTES;
   // barriers: r_full, c_full[S], c_empty[S], s_full, dp_full, p_ready, ds_ready,
-  // acc_done, drain, resident-in-TMEM
+  // acc_done, drain
   static constexpr int BAR_R = 0, BAR_CF = 1, BAR_CE = 1 + STAGES, BAR_SF = 1 + 2 * STAGES,
                        BAR_DPF = BAR_SF + 1, BAR_PR = BAR_DPF + 1, BAR_DSR = BAR_PR + 1,
-                       BAR_AD = BAR_DSR + 1, BAR_DRAIN = BAR_AD + 1, BAR_RT = BAR_DRAIN + 1,
-                       NBAR = BAR_RT + 1;
+                       BAR_AD = BAR_DSR + 1, BAR_DRAIN = BAR_AD + 1, NBAR = BAR_DRAIN + 1;
   static constexpr int OFF_MISC = OFF_BAR + NBAR * 8;
   static constexpr int SMEM_BYTES = OFF_MISC + 16 + 1024;
   static_assert(SMEM_BYTES <= 227 * 1024, "shared memory budget");
   static_assert(STAGES >= 2, "at least two stages");
-  // TMEM: S | dP | accumulators (| resident Q, dO for dQ)
+  // TMEM: S | dP | accumulators.  S and dP read both operands from shared
+  // memory: with N = 128 an MMA costs the same with A in shared memory or
+  // in TMEM.
   static constexpr int COL_S = 0, COL_DP = CN, COL_ACC0 = 2 * CN, COL_ACC1 = COL_ACC0 + D;
-  // dQ: the resident Q and dO also go to TMEM (bf16 pairs per column), so S
-  // and dP read only the streamed chunk from shared memory
-  static constexpr bool RES_TMEM = !DKDV;
-  static constexpr int COL_RT0 = COL_ACC0 + D, COL_RT1 = COL_RT0 + D / 2;
-  static_assert(!RES_TMEM || COL_RT1 + D / 2 <= 512, "TMEM budget");
-  static_assert(RES_TMEM || COL_ACC1 + D <= 512, "TMEM budget");
+  static_assert(COL_ACC1 + D <= 512, "TMEM budget");
   static constexpr int TMEM_COLS = 512;
   // compute warps: 4 groups of 4; group g owns chunk columns [32 g, 32 g + 32)
   static constexpr int NCW = 16, CW = CN / 4;
@@ -158,7 +154,6 @@ __global__ void __launch_bounds__(BwdCfg<DKDV, D>::THREADS, 1)
     mbar_init(bar(C::BAR_DSR), C::NCW);
     mbar_init(bar(C::BAR_AD), 1);
     mbar_init(bar(C::BAR_DRAIN), 1);
-    mbar_init(bar(C::BAR_RT), C::NCW);
     fence_barrier_init();
     misc[1] = 0;
   }
@@ -263,12 +258,8 @@ __global__ void __launch_bounds__(BwdCfg<DKDV, D>::THREADS, 1)
         for (int kk = 0; kk < D / 16; ++kk) {
           const uint32_t off = (kk >> 2) * C::PANEL_R + (kk & 3) * 32;
           const uint32_t offc = (kk >> 2) * C::PANEL_C + (kk & 3) * 32;
-          if (C::RES_TMEM)   // A = 16 d-elements = 8 packed columns per k-step
-            tc_mma_ts(d, tbase + (dp ? C::COL_RT1 : C::COL_RT0) + kk * 8,
-                      sdesc_sw128(c + offc, 16, 1024), C::IDESC_SC, kk > 0 ? 1u : 0u);
-          else
-            tc_mma(d, sdesc_sw128(r + off, 16, 1024), sdesc_sw128(c + offc, 16, 1024),
-                   C::IDESC_SC, kk > 0 ? 1u : 0u);
+          tc_mma(d, sdesc_sw128(r + off, 16, 1024), sdesc_sw128(c + offc, 16, 1024),
+                 C::IDESC_SC, kk > 0 ? 1u : 0u);
         }
         tc_commit(bar(dp ? C::BAR_DPF : C::BAR_SF));
       };
@@ -282,7 +273,6 @@ __global__ void __launch_bounds__(BwdCfg<DKDV, D>::THREADS, 1)
                     (!first || kk > 0) ? 1u : 0u);
       };
       bool ok = mbar_wait(bar(C::BAR_R), 0, abort_flag, p.err);
-      if (C::RES_TMEM && ok) ok = mbar_wait(bar(C::BAR_RT), 0, abort_flag, p.err);
       uint32_t e[2];
       bool has = ok && it.next(e, p.err);
       if (has) {
@@ -348,36 +338,6 @@ __global__ void __launch_bounds__(BwdCfg<DKDV, D>::THREADS, 1)
       row_delta = in ? p.delta[static_cast<int64_t>(bh) * p.T + pos] : 0.f;
     }
     bool alive = true;
-    if (C::RES_TMEM) {
-      // copy this warp's share of the resident rows (Q, dO) into TMEM: row r,
-      // 16-byte chunk q of the row = packed columns [4 q, 4 q + 4)
-      alive = __all_sync(0xffffffffu, mbar_wait(bar(C::BAR_R), 0, abort_flag, p.err));
-      if (alive) {
-        constexpr int QPG = D / 8 / 4;   // 16-byte chunks per warp group
-#pragma unroll
-        for (int t = 0; t < 2; ++t) {
-          const uint8_t* src = smem + (t == 0 ? C::OFF_R0 : C::OFF_R1);
-          uint32_t w[QPG * 4];
-#pragma unroll
-          for (int u = 0; u < QPG; ++u) {
-            const int q = grp * QPG + u;
-            const uint4 v = *reinterpret_cast<const uint4*>(
-                src + (q >> 3) * C::PANEL_R + sw128_offset(r, q & 7));
-            w[4 * u] = v.x;
-            w[4 * u + 1] = v.y;
-            w[4 * u + 2] = v.z;
-            w[4 * u + 3] = v.w;
-          }
-          const uint32_t dst = lane_base + (t == 0 ? C::COL_RT0 : C::COL_RT1) + grp * QPG * 4;
-          if (QPG * 4 == 16) tmem_st16u(dst, w);
-          else tmem_st8u(dst, w);
-        }
-        tmem_st_wait();
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(bar(C::BAR_RT));
-      }
-    }
     int n = 0;
     ChunkPair<2> it;
     it.init(p.indptr, p.indices, p.kind, p.nblocks, p.nnzb, row0, sub, p.bs, p.err);
