@@ -62,11 +62,12 @@ typedef enum smat_status {
   SMAT_ERR_TMA_DESCRIPTOR = 11,
   SMAT_ERR_ROW_TOO_LONG = 12,
   SMAT_ERR_CAPACITY = 13,
-  SMAT_ERR_SCRATCH_LIMIT = 14
+  SMAT_ERR_SCRATCH_LIMIT = 14,
+  SMAT_ERR_BAD_PATTERN = 15
 } smat_status;
 
 enum { SMAT_DTYPE_F32 = 0, SMAT_DTYPE_BF16 = 1 };
-enum { SMAT_TILE_FULL = 0, SMAT_TILE_CAUSAL = 1 };
+enum { SMAT_TILE_FULL = 0, SMAT_TILE_CAUSAL = 1, SMAT_TILE_PATTERN = 2 };
 
 /* Bits of *err_word. */
 enum {
@@ -115,6 +116,75 @@ SMAT_API int smat_layout_transpose(int nblocks, const int32_t* indptr, const int
 SMAT_API int smat_layout_validate(int nblocks, int64_t nnzb, const int32_t* indptr,
                          const int32_t* indices, const uint8_t* kind, int transposed,
                          int32_t* max_row_out);
+
+/* ---------------------------------------------------------------- M^(d) masks
+ * The reference's own mask family (src/smat/mask.py:244-425, build_mask) run
+ * through the softmax kernels.  Its dense mask (mask.py:557-577, materialise)
+ * over T positions, n landmark positions and n_P global columns is
+ *
+ *   rows i <  n:  M[i,j] = (j <= i)                 family SMAT_FAMILY_GEOMETRIC
+ *                 M[i,j] = ((i & j) == j)           family SMAT_FAMILY_ENDPOINT
+ *   rows i >= n:  M[i,j] = 1 (j < n_P),  C[(i-n) mod B, (j-n_P) mod N0] (n_P <= j < n),
+ *                 (j <= i) (j >= n)
+ *
+ * with C the B x N0 0/1 incidence (CSR C_indptr / C_indices of the spec).  A
+ * layout for it has every causal tile that holds a 1; tiles that are all ones
+ * are SMAT_TILE_FULL, the diagonal tiles of the two triangles
+ * SMAT_TILE_CAUSAL, the rest SMAT_TILE_PATTERN, whose mask the kernels
+ * evaluate element-exactly from two bit tables of C with wrap-around:
+ *
+ *   row_bits[r * row_words + (t >> 5)] bit (t & 31) = C[r][t mod N0],  row_words >= (N0 + 63) / 32
+ *   col_bits[c * col_words + (t >> 5)] bit (t & 31) = C[t mod B][c],   col_words >= (B + 63) / 32
+ *
+ * The endpoint family needs N0 >= n - n_P (its profiles are the identity).
+ * Tables passed to the kernels live in device memory; the smat_pattern_mask_*
+ * checks read host copies. */
+enum { SMAT_FAMILY_GEOMETRIC = 0, SMAT_FAMILY_ENDPOINT = 1 };
+
+typedef struct smat_pattern {
+  int family;               /* SMAT_FAMILY_GEOMETRIC or SMAT_FAMILY_ENDPOINT */
+  int n;                    /* landmark positions [0, n), 0 <= n_P <= n <= T */
+  int n_P;                  /* global columns [0, n_P) */
+  int B;                    /* rows of C (row types), >= 1 */
+  int N0;                   /* columns of C (profiles), >= 1 */
+  int row_words;            /* words per row of row_bits */
+  int col_words;            /* words per row of col_bits */
+  const uint32_t* row_bits; /* [B][row_words] */
+  const uint32_t* col_bits; /* [N0][col_words] */
+} smat_pattern_t;
+
+/* Fills both bit tables from C's CSR (host arrays; C_indptr[B + 1], indices
+ * in [0, N0)). */
+SMAT_API int smat_pattern_tables(int B, int N0, const int64_t* C_indptr, const int32_t* C_indices,
+                        uint32_t* row_bits, int row_words, uint32_t* col_bits, int col_words);
+
+/* Tile layout of an M^(d) mask over T positions with square tiles of `block`
+ * rows (same CSR conventions as smat_layout_build_block).  c_all_ones != 0
+ * says every entry of C is 1 (the d = 1 mask), which makes the long-range
+ * tiles full.  Endpoint tiles of the landmark triangle are left out when
+ * they hold no 1 (block a power of two dividing n: key block kb meets query
+ * block qb iff kb & ~qb == 0). */
+SMAT_API int smat_layout_build_pattern(int T, int block, int family, int n, int n_P, int c_all_ones,
+                              int32_t* indptr, int32_t* indices, uint8_t* kind, int64_t capacity,
+                              int64_t* nnzb_out);
+
+/* smat_layout_validate for M^(d) layouts: SMAT_TILE_PATTERN may appear on
+ * any causal entry, SMAT_TILE_CAUSAL only on the diagonal, SMAT_TILE_FULL
+ * only off it. */
+SMAT_API int smat_layout_validate_pattern(int nblocks, int64_t nnzb, const int32_t* indptr,
+                                 const int32_t* indices, const uint8_t* kind, int transposed,
+                                 int32_t* max_row_out);
+
+/* Host evaluation of the kernels' mask rule (host tables): rows
+ * [row_lo, row_hi) of the dense T x T mask as 0/1 bytes, out[(i - row_lo) * T
+ * + j], through the row words the forward and dQ kernels use; the _cols form
+ * writes columns [row_lo, row_hi) as rows (out[(j - row_lo) * T + i] =
+ * M[i, j]) through the column words of the dK/dV kernel.  The native
+ * counterpart of the reference's materialise (mask.py:557-577). */
+SMAT_API int smat_pattern_mask_rows(const smat_pattern_t* pattern, int T, int row_lo, int row_hi,
+                           uint8_t* out);
+SMAT_API int smat_pattern_mask_cols(const smat_pattern_t* pattern, int T, int col_lo, int col_hi,
+                           uint8_t* out);
 
 /* ---------------------------------------------------------------- forward
  * o = softmax_M(scale q k^T) v and lse, for the layout (indptr, indices,
@@ -286,6 +356,42 @@ SMAT_API int smat_bwd(int dtype,
              const int32_t* t_indptr, const int32_t* t_indices, const uint8_t* t_kind,
              int nblocks, int64_t nnzb, int block, int max_row, int t_max_row,
              float scale, int32_t* err_word, void* stream);
+
+/* smat_fwd and smat_bwd for a layout with SMAT_TILE_PATTERN tiles (from
+ * smat_layout_build_pattern) and the device bit tables of its M^(d) mask:
+ * the reference's M^(d) masks (src/smat/mask.py:244-425) under softmax
+ * attention.  The layout arguments and outputs are those of smat_fwd /
+ * smat_bwd; `pattern` is a host struct pointing at device tables, checked
+ * (SMAT_ERR_BAD_PATTERN) before any launch.  A PATTERN tile given to the
+ * entry points without a pattern sets SMAT_DEVERR_BAD_CSR and counts as
+ * masked. */
+SMAT_API int smat_fwd_pattern(int dtype,
+                     const void* q, const int64_t* q_stride,
+                     const void* k, const int64_t* k_stride,
+                     const void* v, const int64_t* v_stride,
+                     void* o, const int64_t* o_stride,
+                     float* lse,
+                     int B, int H, int T, int D,
+                     const int32_t* indptr, const int32_t* indices, const uint8_t* kind,
+                     int nblocks, int64_t nnzb, int block, int max_row,
+                     const smat_pattern_t* pattern,
+                     float scale, int32_t* err_word, void* stream);
+SMAT_API int smat_bwd_pattern(int dtype,
+                     const void* q, const int64_t* q_stride,
+                     const void* k, const int64_t* k_stride,
+                     const void* v, const int64_t* v_stride,
+                     const void* o, const int64_t* o_stride,
+                     const void* dout, const int64_t* do_stride,
+                     const float* lse, float* delta,
+                     void* dq, const int64_t* dq_stride,
+                     void* dk, const int64_t* dk_stride,
+                     void* dv, const int64_t* dv_stride,
+                     int B, int H, int T, int D,
+                     const int32_t* indptr, const int32_t* indices, const uint8_t* kind,
+                     const int32_t* t_indptr, const int32_t* t_indices, const uint8_t* t_kind,
+                     int nblocks, int64_t nnzb, int block, int max_row, int t_max_row,
+                     const smat_pattern_t* pattern,
+                     float scale, int32_t* err_word, void* stream);
 
 /* smat_bwd_noalloc: smat_bwd for callers that cannot allocate device memory
  * (their memory belongs to another allocator, or cudaMalloc's implicit

@@ -21,6 +21,20 @@ DTYPE_BF16 = 1
 WORK_PAIR_BIT = 1 << 24
 TILE_ROWS = 128
 
+# tile kinds and M^(d) families (include/smat_b200.h)
+TILE_FULL, TILE_CAUSAL, TILE_PATTERN = 0, 1, 2
+FAMILY_GEOMETRIC, FAMILY_ENDPOINT = 0, 1
+
+
+class Pattern(ctypes.Structure):
+    """``smat_pattern_t``: the M^(d) mask of a layout's PATTERN tiles."""
+
+    _fields_ = [("family", ctypes.c_int), ("n", ctypes.c_int), ("n_P", ctypes.c_int),
+                ("B", ctypes.c_int), ("N0", ctypes.c_int), ("row_words", ctypes.c_int),
+                ("col_words", ctypes.c_int), ("row_bits", ctypes.c_void_p),
+                ("col_bits", ctypes.c_void_p)]
+
+
 _c_int, _c_i64, _c_f = ctypes.c_int, ctypes.c_int64, ctypes.c_float
 _vp = ctypes.c_void_p
 _i64p = ctypes.POINTER(ctypes.c_int64)
@@ -73,6 +87,23 @@ SIGNATURES = {
                           _vp, _vp, _vp, _i64p, _vp, _i64p, _vp, _i64p,
                           _c_int, _c_int, _c_int, _c_int, _vp, _vp, _vp, _vp, _vp, _vp,
                           _c_int, _c_i64, _c_int, _c_int, _c_int, _c_f, _vp, _vp]),
+    "smat_pattern_tables": (_c_int, [_c_int, _c_int, _vp, _vp, _vp, _c_int, _vp, _c_int]),
+    "smat_layout_build_pattern": (_c_int, [_c_int, _c_int, _c_int, _c_int, _c_int, _c_int,
+                                           _vp, _vp, _vp, _c_i64, _i64p]),
+    "smat_layout_validate_pattern": (_c_int, [_c_int, _c_i64, _vp, _vp, _vp, _c_int,
+                                              ctypes.POINTER(ctypes.c_int32)]),
+    "smat_pattern_mask_rows": (_c_int, [ctypes.POINTER(Pattern), _c_int, _c_int, _c_int, _vp]),
+    "smat_pattern_mask_cols": (_c_int, [ctypes.POINTER(Pattern), _c_int, _c_int, _c_int, _vp]),
+    # smat_fwd / smat_bwd plus the pattern before scale
+    "smat_fwd_pattern": (_c_int, [_c_int, _vp, _i64p, _vp, _i64p, _vp, _i64p, _vp, _i64p, _vp,
+                                  _c_int, _c_int, _c_int, _c_int, _vp, _vp, _vp,
+                                  _c_int, _c_i64, _c_int, _c_int, ctypes.POINTER(Pattern),
+                                  _c_f, _vp, _vp]),
+    "smat_bwd_pattern": (_c_int, [_c_int, _vp, _i64p, _vp, _i64p, _vp, _i64p, _vp, _i64p, _vp,
+                                  _i64p, _vp, _vp, _vp, _i64p, _vp, _i64p, _vp, _i64p,
+                                  _c_int, _c_int, _c_int, _c_int, _vp, _vp, _vp, _vp, _vp, _vp,
+                                  _c_int, _c_i64, _c_int, _c_int, _c_int,
+                                  ctypes.POINTER(Pattern), _c_f, _vp, _vp]),
     # smat_bwd without the delta workspace (fixed in-library scratch)
     "smat_bwd_noalloc": (_c_int, [_c_int, _vp, _i64p, _vp, _i64p, _vp, _i64p, _vp, _i64p, _vp,
                                   _i64p, _vp, _vp, _i64p, _vp, _i64p, _vp, _i64p,

@@ -1,4 +1,5 @@
-"""Block-sparse causal softmax attention under an SMat block layout.
+"""Block-sparse causal softmax attention under an SMat block layout or an
+``M^(d)`` mask.
 
 ``smat_softmax_attention(q, k, v, spec, scale=None) -> (o, lse)`` is the op.
 It runs the sm_100a kernels of ``libsmat_b200.so`` through the C ABI and is
@@ -13,6 +14,12 @@ Tensors are ``[B, H, T, D]`` on a CUDA device, bf16 (tensor-core kernels,
 D in {64, 128}, block in {64, 128}) or fp32 (full-fp32 CUDA-core kernels,
 D in {32, 64, 128}).  There is no CPU path: a CPU tensor, an unsupported
 shape or a missing library raises.
+
+The mask is a ``kind="block"`` layout, or one of the reference's own ``M^(d)``
+masks (``build_mask``, reference ``src/smat/mask.py:244-425``), which runs as
+its pattern layout: the same kernels with PATTERN tiles whose mask they
+evaluate from bit tables of the incidence (``smat_fwd_pattern`` /
+``smat_bwd_pattern``), equal element for element to ``materialise``.
 
 This is the softmax counterpart of the reference's op entry
 ``smat.attention.smat_attention`` (``src/smat/attention.py:391-455``), which
@@ -31,10 +38,10 @@ import numpy as np
 import torch
 
 from . import _lib
-from .mask import MaskSpec, to_device
+from .mask import MaskSpec, pattern_layout, to_device
 
 __all__ = ["smat_softmax_attention", "SmatSoftmaxFn", "layout_device_args",
-           "check_device_errors", "fwd", "bwd"]
+           "kernel_layout", "check_device_errors", "fwd", "bwd"]
 
 _DTYPES = {torch.bfloat16: _lib.DTYPE_BF16, torch.float32: _lib.DTYPE_F32}
 _ERR: Dict[str, torch.Tensor] = {}
@@ -61,15 +68,28 @@ def check_device_errors(device=None, reset: bool = True) -> int:
     return val
 
 
+def kernel_layout(spec: MaskSpec) -> MaskSpec:
+    """The tiled layout the kernels run: ``spec`` itself for a block or
+    pattern layout, :func:`~smat_attention_b200.mask.pattern_layout` (128-row
+    tiles) for an ``M^(d)`` spec from ``build_mask``."""
+    if spec.kind in ("block", "pattern"):
+        return spec
+    if spec.kind in ("geometric", "endpoint"):
+        return pattern_layout(spec, 128)
+    raise ValueError(f"unsupported mask kind {spec.kind!r}")
+
+
 def _validate(spec: MaskSpec) -> Tuple[int, int]:
     """Check both CSRs once on the host (C validator); cache the longest rows."""
     cached = getattr(spec, "_validated", None)
     if cached is not None:
         return cached
-    if spec.kind != "block":
-        raise ValueError(f"the softmax kernels need a block layout (kind='block'), "
+    if spec.kind not in ("block", "pattern"):
+        raise ValueError(f"the softmax kernels need a block or pattern layout, "
                          f"got kind={spec.kind!r}")
     L = _lib.lib()
+    validate = (L.smat_layout_validate_pattern if spec.kind == "pattern"
+                else L.smat_layout_validate)
     rows = []
     for ptr, idx, knd, tr in ((spec.indptr, spec.indices, spec.tile_kind, 0),
                               (spec.t_indptr, spec.t_indices, spec.t_kind, 1)):
@@ -77,7 +97,7 @@ def _validate(spec: MaskSpec) -> Tuple[int, int]:
         idx = np.ascontiguousarray(idx, dtype=np.int32)
         knd = np.ascontiguousarray(knd, dtype=np.uint8)
         mr = ctypes.c_int32(0)
-        _lib.check("smat_layout_validate", L.smat_layout_validate(
+        _lib.check("smat_layout_validate", validate(
             spec.nqb, idx.size, ptr.ctypes.data, idx.ctypes.data, knd.ctypes.data, tr,
             ctypes.byref(mr)))
         rows.append(int(mr.value))
@@ -86,12 +106,25 @@ def _validate(spec: MaskSpec) -> Tuple[int, int]:
 
 
 def layout_device_args(spec: MaskSpec, device) -> Dict[str, object]:
-    """Device CSR tensors of ``spec`` (staged once per device) plus sizes."""
+    """Device CSR tensors of ``spec`` (staged once per device) plus sizes; for
+    a pattern layout also ``pattern``, the ``smat_pattern_t`` pointing at the
+    staged bit tables."""
+    spec = kernel_layout(spec)
     max_row, t_max_row = _validate(spec)
     to_device(spec, device)
     d = spec.dev[str(torch.device(device))]
-    return dict(d, nblocks=spec.nqb, nnzb=spec.nnzb, block=spec.block,
-                max_row=max_row, t_max_row=t_max_row)
+    out = dict(d, nblocks=spec.nqb, nnzb=spec.nnzb, block=spec.block,
+               max_row=max_row, t_max_row=t_max_row, pattern=None)
+    if spec.kind == "pattern":
+        pt = d.get("pattern")
+        if pt is None:
+            pt = _lib.Pattern(
+                _lib.FAMILY_ENDPOINT if spec.source == "endpoint" else _lib.FAMILY_GEOMETRIC,
+                spec.n, spec.n_P, spec.B, spec.N0, spec.row_bits.shape[1],
+                spec.col_bits.shape[1], d["row_bits"].data_ptr(), d["col_bits"].data_ptr())
+            d["pattern"] = pt
+        out["pattern"] = ctypes.byref(pt)
+    return out
 
 
 def _prep(x: torch.Tensor, name: str) -> torch.Tensor:
@@ -122,15 +155,18 @@ def fwd(q, k, v, spec: MaskSpec, scale: float, o=None):
         o = torch.empty_like(q)
     lse = torch.empty(B, H, T, dtype=torch.float32, device=q.device)
     L = _lib.lib()
-    st = L.smat_fwd(_DTYPES[q.dtype],
-                    q.data_ptr(), _lib.strides3(q), k.data_ptr(), _lib.strides3(k),
-                    v.data_ptr(), _lib.strides3(v), o.data_ptr(), _lib.strides3(o),
-                    lse.data_ptr(), B, H, T, D,
-                    lay["indptr"].data_ptr(), lay["indices"].data_ptr(), lay["kind"].data_ptr(),
-                    lay["nblocks"], lay["nnzb"], lay["block"], lay["max_row"],
-                    float(scale), _err_word(q.device).data_ptr(),
-                    torch.cuda.current_stream(q.device).cuda_stream)
-    _lib.check("smat_fwd", st)
+    args = [_DTYPES[q.dtype],
+            q.data_ptr(), _lib.strides3(q), k.data_ptr(), _lib.strides3(k),
+            v.data_ptr(), _lib.strides3(v), o.data_ptr(), _lib.strides3(o),
+            lse.data_ptr(), B, H, T, D,
+            lay["indptr"].data_ptr(), lay["indices"].data_ptr(), lay["kind"].data_ptr(),
+            lay["nblocks"], lay["nnzb"], lay["block"], lay["max_row"]]
+    tail = [float(scale), _err_word(q.device).data_ptr(),
+            torch.cuda.current_stream(q.device).cuda_stream]
+    if lay["pattern"] is None:
+        _lib.check("smat_fwd", L.smat_fwd(*args, *tail))
+    else:
+        _lib.check("smat_fwd_pattern", L.smat_fwd_pattern(*args, lay["pattern"], *tail))
     return o, lse
 
 
@@ -144,19 +180,22 @@ def bwd(q, k, v, o, lse, do, spec: MaskSpec, scale: float):
     dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
     delta = torch.empty(B, H, T, dtype=torch.float32, device=q.device)
     L = _lib.lib()
-    st = L.smat_bwd(_DTYPES[q.dtype],
-                    q.data_ptr(), _lib.strides3(q), k.data_ptr(), _lib.strides3(k),
-                    v.data_ptr(), _lib.strides3(v), o.data_ptr(), _lib.strides3(o),
-                    do.data_ptr(), _lib.strides3(do), lse.data_ptr(), delta.data_ptr(),
-                    dq.data_ptr(), _lib.strides3(dq), dk.data_ptr(), _lib.strides3(dk),
-                    dv.data_ptr(), _lib.strides3(dv), B, H, T, D,
-                    lay["indptr"].data_ptr(), lay["indices"].data_ptr(), lay["kind"].data_ptr(),
-                    lay["t_indptr"].data_ptr(), lay["t_indices"].data_ptr(),
-                    lay["t_kind"].data_ptr(), lay["nblocks"], lay["nnzb"], lay["block"],
-                    lay["max_row"], lay["t_max_row"], float(scale),
-                    _err_word(q.device).data_ptr(),
-                    torch.cuda.current_stream(q.device).cuda_stream)
-    _lib.check("smat_bwd", st)
+    args = [_DTYPES[q.dtype],
+            q.data_ptr(), _lib.strides3(q), k.data_ptr(), _lib.strides3(k),
+            v.data_ptr(), _lib.strides3(v), o.data_ptr(), _lib.strides3(o),
+            do.data_ptr(), _lib.strides3(do), lse.data_ptr(), delta.data_ptr(),
+            dq.data_ptr(), _lib.strides3(dq), dk.data_ptr(), _lib.strides3(dk),
+            dv.data_ptr(), _lib.strides3(dv), B, H, T, D,
+            lay["indptr"].data_ptr(), lay["indices"].data_ptr(), lay["kind"].data_ptr(),
+            lay["t_indptr"].data_ptr(), lay["t_indices"].data_ptr(),
+            lay["t_kind"].data_ptr(), lay["nblocks"], lay["nnzb"], lay["block"],
+            lay["max_row"], lay["t_max_row"]]
+    tail = [float(scale), _err_word(q.device).data_ptr(),
+            torch.cuda.current_stream(q.device).cuda_stream]
+    if lay["pattern"] is None:
+        _lib.check("smat_bwd", L.smat_bwd(*args, *tail))
+    else:
+        _lib.check("smat_bwd_pattern", L.smat_bwd_pattern(*args, lay["pattern"], *tail))
     return dq, dk, dv
 
 
@@ -184,8 +223,10 @@ def smat_softmax_attention(q, k, v, spec: MaskSpec, scale=None):
 
     ``q, k, v``: ``[B, H, T, D]`` CUDA tensors, bf16 or fp32, same shape.
     ``spec``: a ``kind="block"`` layout from
-    :func:`smat_attention_b200.mask.build_block_mask` with ``spec.T == T``.
-    ``scale`` defaults to ``1 / sqrt(D)``.
+    :func:`smat_attention_b200.mask.build_block_mask`, or an ``M^(d)`` spec
+    from :func:`smat_attention_b200.mask.build_mask` (run through its pattern
+    layout, :func:`smat_attention_b200.mask.pattern_layout`), with
+    ``spec.T == T``.  ``scale`` defaults to ``1 / sqrt(D)``.
     """
     if scale is None:
         scale = 1.0 / math.sqrt(q.shape[-1])

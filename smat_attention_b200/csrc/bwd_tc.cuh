@@ -21,7 +21,9 @@
 // warps turn dP into dS while the tensor core runs dV and the next S.
 // With bs = 64 a chunk is two 64-row blocks of the merged list (TMA loads
 // each half separately; a missing second half is loaded from row T, i.e.
-// zero-filled, and masked).
+// zero-filled, and masked).  A warp's 32 x 32 block is masked by one 32-bit
+// word per row: the causal span on the diagonal, and for M^(d) PATTERN tiles
+// the row word (dQ) or column word (dK/dV) of pattern.cuh.
 //
 // Warp roles (576 threads): warps 0-15 compute -- warp w reads TMEM lanes
 // 32 (w % 4) .. +31 (its 32 tile rows) and chunk columns 32 (w / 4) .. +31;
@@ -50,6 +52,7 @@ struct BwdParams {
   float scale;             // softmax scale
   float scale_log2;        // softmax scale * log2(e)
   int32_t* err;
+  MdPattern md;            // tables of PATTERN tiles (null row_bits: the layout has none)
 };
 
 template <bool DKDV, int D>
@@ -349,6 +352,19 @@ __global__ void __launch_bounds__(BwdCfg<DKDV, D>::THREADS, 1)
       const int cbase = entry_present(ew) ? static_cast<int>(sched_block(ew)) * p.bs + col0 % p.bs
                                           : p.T;
       const uint32_t st = entry_present(ew) ? sched_state(ew, srow) : ST_ABSENT;
+      // visibility of this row's 32 columns (bit c: column cbase + c); for
+      // PATTERN tiles the table loads overlap the waits below
+      uint32_t vw = 0u;
+      if (st == ST_FULL) {
+        vw = DKDV ? span_word(cbase, 0, p.T) : 0xffffffffu;
+      } else if (st == ST_CAUSAL) {
+        vw = DKDV ? span_word(cbase, pos, p.T) : span_word(cbase, 0, pos + 1);
+      } else if (st == ST_PATTERN) {
+        if (p.md.row_bits)
+          vw = DKDV ? md_col_word(p.md, p.T, pos, cbase) : md_row_word(p.md, p.T, pos, cbase);
+        else if (p.err)
+          atomicOr(p.err, DEV_ERR_BAD_CSR);
+      }
       const float* ldj = ld + (j % C::STAGES) * (C::LD_BYTES / 4);
       // dK/dV reads the lse/delta the producer staged with this chunk
       if (DKDV && !__all_sync(0xffffffffu, mbar_wait(bar(C::BAR_CF + j % C::STAGES),
@@ -388,14 +404,8 @@ __global__ void __launch_bounds__(BwdCfg<DKDV, D>::THREADS, 1)
           for (int i = 0; i < 4; ++i) pv[4 * q + i] = ex2_approx(x[i]);
         } else {
 #pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            const int cpos = cbase + 4 * q + i;
-            // dK/dV: row = key `pos`, column = query `cpos`; dQ: the reverse
-            const bool valid =
-                DKDV ? ((st == ST_FULL || (st == ST_CAUSAL && cpos >= pos)) && cpos < p.T)
-                     : (st == ST_FULL || (st == ST_CAUSAL && cpos <= pos));
-            pv[4 * q + i] = valid ? ex2_approx(x[i]) : 0.f;
-          }
+          for (int i = 0; i < 4; ++i)
+            pv[4 * q + i] = ((vw >> (4 * q + i)) & 1u) ? ex2_approx(x[i]) : 0.f;
         }
       }
       if (DKDV) {

@@ -29,7 +29,10 @@
 // that half's own S columns; the softmax reads S a quarter (32 keys) at a
 // time, so a thread only overwrites scores it has already read.
 // Masked scores become -inf before the row max, so a key outside the mask
-// never enters the max or the sum.
+// never enters the max or the sum.  Each quarter's mask is one 32-bit word per
+// row: all ones for a full block, a span for the causal diagonal, and for an
+// M^(d) PATTERN tile the word pattern.cuh evaluates from the C bit tables.  A
+// row may see no visible key in a tile (its max stays -inf, its P is 0).
 #pragma once
 
 #include "common.cuh"
@@ -48,6 +51,7 @@ struct FwdParams {
   const int32_t* work;       // optional work list (one item per CTA and (b, h)); null = all tiles
   float scale_log2;          // softmax scale * log2(e)
   int32_t* err;
+  MdPattern md;              // tables of PATTERN tiles (null row_bits: the layout has none)
 };
 
 template <int D>
@@ -330,6 +334,18 @@ __global__ void __launch_bounds__(320, 1)
         st[hf] = entry_present(eh) ? sched_state(eh, srow) : ST_ABSENT;
         k0[hf] = static_cast<int>(sched_block(eh)) * p.bs + (hf * 64) % p.bs;
       }
+      // visibility words of the four quarters (bit i: key 32 qq + i of the
+      // chunk); computed before the wait so pattern-table loads overlap it
+      auto qword = [&](int qq) -> uint32_t {
+        const uint32_t sq = (qq >> 1) ? st[1] : st[0];
+        const int kq = ((qq >> 1) ? k0[1] : k0[0]) + 32 * (qq & 1);
+        if (sq == ST_FULL) return 0xffffffffu;
+        if (sq == ST_CAUSAL) return span_word(kq, 0, q_pos + 1);
+        if (sq == ST_PATTERN && p.md.row_bits) return md_row_word(p.md, p.T, q_pos, kq);
+        if (sq == ST_PATTERN && p.err) atomicOr(p.err, DEV_ERR_BAD_CSR);
+        return 0u;
+      };
+      const uint32_t mw0 = qword(0), mw1 = qword(1), mw2 = qword(2), mw3 = qword(3);
       if (!__all_sync(0xffffffffu,
                       mbar_wait(bar(C::BAR_SF + x), cnt & 1, abort_flag, p.err))) {
         alive = false;
@@ -340,10 +356,10 @@ __global__ void __launch_bounds__(320, 1)
       auto mask = [&](float* s, int qq) {
         const uint32_t sq = (qq >> 1) ? st[1] : st[0];
         if (sq != ST_FULL) {   // uniform per warp: its 32 rows share one CSR row
-          const int kq = ((qq >> 1) ? k0[1] : k0[0]) + 32 * (qq & 1);
+          const uint32_t w = qq == 0 ? mw0 : (qq == 1 ? mw1 : (qq == 2 ? mw2 : mw3));
 #pragma unroll
           for (int i = 0; i < 32; ++i)
-            if (!(sq == ST_CAUSAL && kq + i <= q_pos)) s[i] = -INFINITY;
+            if (!((w >> i) & 1u)) s[i] = -INFINITY;
         }
       };
       float s[32];

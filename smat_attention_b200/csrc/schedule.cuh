@@ -3,17 +3,24 @@
 // A CTA owns NROWS consecutive rows of a block CSR (query blocks for the
 // forward / dQ kernels, key blocks for dK/dV over the transposed CSR).  Its
 // chunk list is the sorted union of those rows; each entry carries, for every
-// owned row, whether the block is absent, fully visible or causal (diagonal)
-// for that row.  MergeIter produces the list one entry at a time straight
+// owned row, whether the block is absent, fully visible, causal (diagonal) or
+// patterned (an M^(d) tile, masked by the rule in pattern.cuh) for that row.
+// MergeIter produces the list one entry at a time straight
 // from the CSR in global memory, so rows of any length are supported; every
 // warp role runs its own iterator and all see the same sequence.
 #pragma once
 
 #include "common.cuh"
+#include "pattern.cuh"
 
 namespace smat {
 
-enum : uint32_t { ST_ABSENT = 0, ST_FULL = 1, ST_CAUSAL = 2 };
+enum : uint32_t { ST_ABSENT = 0, ST_FULL = 1, ST_CAUSAL = 2, ST_PATTERN = 3 };
+
+// row state of a CSR kind byte: 1 causal, 2 pattern, anything else full
+__device__ __forceinline__ uint32_t kind_state(uint8_t k) {
+  return k == 1 ? ST_CAUSAL : (k == 2 ? ST_PATTERN : ST_FULL);
+}
 
 // entry: bits 0..23 block index, bits 24 + 2 r .. 25 + 2 r the state of row r
 __device__ __forceinline__ uint32_t sched_block(uint32_t e) { return e & 0xFFFFFFu; }
@@ -94,7 +101,7 @@ struct MergeIter {
 #pragma unroll
     for (int s = 0; s < MAXROWS; ++s) {
       if (head[s] == best) {
-        out |= (hk[s] == 1 ? ST_CAUSAL : ST_FULL) << (24 + 2 * s);
+        out |= kind_state(hk[s]) << (24 + 2 * s);
         ++lo[s];
         fetch(s);
       }

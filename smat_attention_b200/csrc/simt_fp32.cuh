@@ -8,10 +8,12 @@
 // Each query (or key) row is owned by TPR = D / 32 adjacent lanes holding 32
 // of its D components; dot products are reduced across those lanes with
 // shuffles.  The walk over the layout is the same CSR walk the tensor-core
-// kernels do, one key (or query) at a time, causal inside diagonal tiles.
+// kernels do, one key (or query) at a time, causal inside diagonal tiles and
+// masked by the pattern.cuh rule inside M^(d) PATTERN tiles.
 #pragma once
 
 #include "common.cuh"
+#include "pattern.cuh"
 
 namespace smat {
 
@@ -34,6 +36,7 @@ struct SimtParams {
   int span_tiles;       // tiles one work item may span: 2 (forward) or 1
   float scale;
   int32_t* err;
+  MdPattern md;         // tables of PATTERN tiles (null row_bits: the layout has none)
 };
 
 constexpr int SIMT_TILE = 128;
@@ -76,6 +79,24 @@ __device__ __forceinline__ float group_sum(float x) {
   return x;
 }
 
+// Is (query i, key j) visible in a tile of kind `kd` (0 full, 1 causal diagonal,
+// 2 M^(d) pattern)?  For pattern tiles `w` caches the mask word of the 32-aligned
+// group holding the varying index (j for a row walk, i for a column walk);
+// `fresh` asks for it to be reloaded.
+__device__ __forceinline__ bool simt_visible(const SimtParams& p, uint8_t kd, int i, int j,
+                                             bool col_walk, bool fresh, uint32_t& w) {
+  if (kd == 1) return j <= i;
+  if (kd != 2) return true;
+  if (!p.md.row_bits) {
+    if (p.err) atomicOr(p.err, DEV_ERR_BAD_CSR);
+    return false;
+  }
+  const int v = col_walk ? i : j;
+  if (fresh || (v & 31) == 0)
+    w = col_walk ? md_col_word(p.md, p.T, j, v & ~31) : md_row_word(p.md, p.T, i, v & ~31);
+  return (w >> (v & 31)) & 1u;
+}
+
 __device__ __forceinline__ const float* row_ptr(const float* base, const int64_t* s, int b, int h,
                                                 int t) {
   return base + b * s[0] + h * s[1] + static_cast<int64_t>(t) * s[2];
@@ -105,15 +126,16 @@ __global__ void __launch_bounds__(128) smat_fwd_simt_kernel(const SimtParams p) 
   const int e0 = p.indptr[qb], e1 = p.indptr[qb + 1];
   for (int e = e0; e < e1; ++e) {
     const int kb = p.indices[e];
-    const bool causal = p.kind[e] == 1;
+    const uint8_t kd = p.kind[e];
     const int j0 = kb * p.bs, j1 = min(p.T, j0 + p.bs);
+    uint32_t w = 0u;
     for (int j = j0; j < j1; ++j) {
       const float* kr = row_ptr(p.k, p.k_s, b, h, j) + part * 32;
       float s = 0.f;
 #pragma unroll
       for (int d = 0; d < 32; ++d) s = fmaf(q[d], kr[d], s);
       s = group_sum<TPR>(s);
-      if (causal && j > ii) continue;
+      if (!simt_visible(p, kd, ii, j, false, j == j0, w)) continue;
       const float* vr = row_ptr(p.v, p.v_s, b, h, j) + part * 32;
       if (s > m) {
         const float alpha = (m == -INFINITY) ? 0.f : expf(m - s);
@@ -162,8 +184,9 @@ __global__ void __launch_bounds__(128) smat_dq_simt_kernel(const SimtParams p) {
   const int qb = ii / p.bs;
   for (int e = p.indptr[qb]; e < p.indptr[qb + 1]; ++e) {
     const int kb = p.indices[e];
-    const bool causal = p.kind[e] == 1;
+    const uint8_t kd = p.kind[e];
     const int j0 = kb * p.bs, j1 = min(p.T, j0 + p.bs);
+    uint32_t w = 0u;
     for (int j = j0; j < j1; ++j) {
       const float* kr = row_ptr(p.k, p.k_s, b, h, j) + part * 32;
       const float* vr = row_ptr(p.v, p.v_s, b, h, j) + part * 32;
@@ -175,7 +198,7 @@ __global__ void __launch_bounds__(128) smat_dq_simt_kernel(const SimtParams p) {
       }
       s = group_sum<TPR>(s);
       dp = group_sum<TPR>(dp);
-      if (causal && j > ii) continue;
+      if (!simt_visible(p, kd, ii, j, false, j == j0, w)) continue;
       const float pr = expf(s - lse);
       const float ds = pr * (dp - dl);
 #pragma unroll
@@ -213,8 +236,9 @@ __global__ void __launch_bounds__(128) smat_dkdv_simt_kernel(const SimtParams p)
   const int kb = jj / p.bs;
   for (int e = p.indptr[kb]; e < p.indptr[kb + 1]; ++e) {
     const int qb = p.indices[e];
-    const bool causal = p.kind[e] == 1;
+    const uint8_t kd = p.kind[e];
     const int i0 = qb * p.bs, i1 = min(p.T, i0 + p.bs);
+    uint32_t w = 0u;
     for (int i = i0; i < i1; ++i) {
       const float* qp = row_ptr(p.q, p.q_s, b, h, i) + part * 32;
       const float* dp_ = row_ptr(p.dout, p.do_s, b, h, i) + part * 32;
@@ -226,7 +250,7 @@ __global__ void __launch_bounds__(128) smat_dkdv_simt_kernel(const SimtParams p)
       }
       s = group_sum<TPR>(s);
       dp = group_sum<TPR>(dp);
-      if (causal && jj > i) continue;
+      if (!simt_visible(p, kd, i, jj, true, i == i0, w)) continue;
       const float lse = p.lse[static_cast<int64_t>(bh) * p.T + i];
       const float dl = p.delta[static_cast<int64_t>(bh) * p.T + i];
       const float pr = expf(s - lse);

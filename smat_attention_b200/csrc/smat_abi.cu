@@ -34,6 +34,7 @@ struct Work {
   int n;
 };
 constexpr Work kAllTiles{nullptr, 0};
+constexpr MdPattern kNoPattern{nullptr, nullptr, 0, 0, 0, 1, 1, 0, 0};
 
 int check_work(const Work& w) {
   if (w.n < 0) return SMAT_ERR_BAD_SHAPE;
@@ -77,6 +78,51 @@ int check_layout_args(const int32_t* indptr, const int32_t* indices, const uint8
                       int64_t nnzb, int max_row, int block) {
   if (!indptr || !kind || (!indices && nnzb > 0)) return SMAT_ERR_NULL_POINTER;
   if (nnzb < 0 || nnzb > (1LL << 31) - 1 || max_row < 0) return SMAT_ERR_CSR_INVALID;
+  return SMAT_OK;
+}
+
+// M^(d) pattern of a layout's PATTERN tiles: field ranges (the device rule
+// indexes the tables only within them) and, for launches, the tables.
+int check_pattern(const smat_pattern_t* pt, int T, bool need_tables, MdPattern* out) {
+  if (!pt) return SMAT_ERR_NULL_POINTER;
+  if (pt->family != SMAT_FAMILY_GEOMETRIC && pt->family != SMAT_FAMILY_ENDPOINT)
+    return SMAT_ERR_BAD_PATTERN;
+  if (pt->n_P < 0 || pt->n < pt->n_P || pt->n > T || pt->B < 1 || pt->N0 < 1)
+    return SMAT_ERR_BAD_PATTERN;
+  if (static_cast<int64_t>(pt->row_words) < (static_cast<int64_t>(pt->N0) + 63) / 32 ||
+      static_cast<int64_t>(pt->col_words) < (static_cast<int64_t>(pt->B) + 63) / 32)
+    return SMAT_ERR_BAD_PATTERN;
+  if (pt->family == SMAT_FAMILY_ENDPOINT && pt->N0 < pt->n - pt->n_P) return SMAT_ERR_BAD_PATTERN;
+  if (need_tables && (!pt->row_bits || !pt->col_bits)) return SMAT_ERR_NULL_POINTER;
+  *out = MdPattern{pt->row_bits, pt->col_bits, pt->family, pt->n,        pt->n_P,
+                   pt->B,        pt->N0,       pt->row_words, pt->col_words};
+  return SMAT_OK;
+}
+
+// Layout checks shared by smat_layout_validate (FULL / CAUSAL kinds) and
+// smat_layout_validate_pattern (PATTERN allowed anywhere).
+int validate_layout(int nblocks, int64_t nnzb, const int32_t* indptr, const int32_t* indices,
+                    const uint8_t* kind, int transposed, bool allow_pattern, int32_t* max_row_out) {
+  if (nblocks < 0 || nnzb < 0) return SMAT_ERR_CSR_INVALID;
+  if (!indptr || (nnzb > 0 && (!indices || !kind))) return SMAT_ERR_NULL_POINTER;
+  if (indptr[0] != 0 || indptr[nblocks] != nnzb) return SMAT_ERR_CSR_INVALID;
+  int32_t longest = 0;
+  for (int r = 0; r < nblocks; ++r) {
+    const int64_t a = indptr[r], b = indptr[r + 1];
+    if (b < a || b > nnzb) return SMAT_ERR_CSR_INVALID;
+    longest = std::max<int32_t>(longest, static_cast<int32_t>(b - a));
+    int32_t prev = -1;
+    for (int64_t e = a; e < b; ++e) {
+      const int32_t c = indices[e];
+      if (c < 0 || c >= nblocks || c <= prev) return SMAT_ERR_CSR_INVALID;
+      if (transposed ? (c < r) : (c > r)) return SMAT_ERR_CSR_INVALID;
+      const uint8_t want = (c == r) ? SMAT_TILE_CAUSAL : SMAT_TILE_FULL;
+      if (kind[e] != want && !(allow_pattern && kind[e] == SMAT_TILE_PATTERN))
+        return SMAT_ERR_CSR_INVALID;
+      prev = c;
+    }
+  }
+  if (max_row_out) *max_row_out = longest;
   return SMAT_OK;
 }
 
@@ -130,8 +176,8 @@ int launch_status() {
 template <int D>
 int fwd_tc(const TArg& q, const TArg& k, const TArg& v, const TArg& o, float* lse, int B, int H,
            int T, const int32_t* indptr, const int32_t* indices, const uint8_t* kind,
-           int nblocks, int64_t nnzb, int block, float scale, const Work& work, int32_t* err,
-           cudaStream_t s) {
+           int nblocks, int64_t nnzb, int block, float scale, const Work& work,
+           const MdPattern& md, int32_t* err, cudaStream_t s) {
   using C = FwdCfg<D>;
   CUtensorMap mq, mk, mv;
   int rc;
@@ -158,6 +204,7 @@ int fwd_tc(const TArg& q, const TArg& k, const TArg& v, const TArg& o, float* ls
   p.work = work.items;
   p.scale_log2 = scale * 1.4426950408889634f;
   p.err = err;
+  p.md = md;
   auto kern = smat_fwd_tc_kernel<D>;
   if ((rc = set_smem(kern, C::SMEM_BYTES))) return rc;
   const int64_t grid = static_cast<int64_t>(work.items ? work.n : p.n_pairs) * B * H;
@@ -168,8 +215,9 @@ int fwd_tc(const TArg& q, const TArg& k, const TArg& v, const TArg& o, float* ls
 
 SimtParams simt_params(int B, int H, int T, int block, float scale, const int32_t* indptr,
                        const int32_t* indices, const uint8_t* kind, int nblocks, int64_t nnzb,
-                       int32_t* err, const Work& work, int span_tiles) {
+                       int32_t* err, const Work& work, int span_tiles, const MdPattern& md) {
   SimtParams p{};
+  p.md = md;
   p.work = work.items;
   p.span_tiles = span_tiles;
   p.B = B;
@@ -244,8 +292,8 @@ template <bool DKDV, int D>
 int bwd_tc(const TArg& r0, const TArg& r1, const TArg& c0, const TArg& c1, const float* lse,
            const float* delta, const TArg& out0, const TArg* out1, int B, int H, int T,
            const int32_t* indptr, const int32_t* indices, const uint8_t* kind, int nblocks,
-           int64_t nnzb, int block, float scale, const Work& work, int32_t* err,
-           cudaStream_t s) {
+           int64_t nnzb, int block, float scale, const Work& work, const MdPattern& md,
+           int32_t* err, cudaStream_t s) {
   using C = BwdCfg<DKDV, D>;
   CUtensorMap m0, m1, mc0, mc1;
   int rc;
@@ -280,6 +328,7 @@ int bwd_tc(const TArg& r0, const TArg& r1, const TArg& c0, const TArg& c1, const
   p.scale = scale;
   p.scale_log2 = scale * 1.4426950408889634f;
   p.err = err;
+  p.md = md;
   auto kern = smat_bwd_tc_kernel<DKDV, D>;
   if ((rc = set_smem(kern, C::SMEM_BYTES))) return rc;
   const int64_t grid = static_cast<int64_t>(work.items ? work.n : p.n_tiles) * B * H;
@@ -293,7 +342,7 @@ int bwd_tc(const TArg& r0, const TArg& r1, const TArg& c0, const TArg& c1, const
 // ====================================================================== C ABI
 extern "C" {
 
-int smat_abi_version(void) { return 2; }
+int smat_abi_version(void) { return 3; }
 
 const char* smat_status_string(int status) {
   switch (status) {
@@ -313,6 +362,7 @@ const char* smat_status_string(int status) {
     case SMAT_ERR_CAPACITY: return "output capacity too small";
     case SMAT_ERR_SCRATCH_LIMIT:
       return "B*H*T exceeds the fixed scratch of smat_bwd_noalloc (SMAT_NOALLOC_MAX_ROWS)";
+    case SMAT_ERR_BAD_PATTERN: return "invalid M^(d) pattern (fields, table sizes or C)";
   }
   return "unknown status";
 }
@@ -383,25 +433,125 @@ int smat_layout_transpose(int nblocks, const int32_t* indptr, const int32_t* ind
 
 int smat_layout_validate(int nblocks, int64_t nnzb, const int32_t* indptr, const int32_t* indices,
                          const uint8_t* kind, int transposed, int32_t* max_row_out) {
-  if (nblocks < 0 || nnzb < 0) return SMAT_ERR_CSR_INVALID;
-  if (!indptr || (nnzb > 0 && (!indices || !kind))) return SMAT_ERR_NULL_POINTER;
-  if (indptr[0] != 0 || indptr[nblocks] != nnzb) return SMAT_ERR_CSR_INVALID;
-  int32_t longest = 0;
-  for (int r = 0; r < nblocks; ++r) {
-    const int64_t a = indptr[r], b = indptr[r + 1];
-    if (b < a || b > nnzb) return SMAT_ERR_CSR_INVALID;
-    longest = std::max<int32_t>(longest, static_cast<int32_t>(b - a));
-    int32_t prev = -1;
-    for (int64_t e = a; e < b; ++e) {
-      const int32_t c = indices[e];
-      if (c < 0 || c >= nblocks || c <= prev) return SMAT_ERR_CSR_INVALID;
-      if (transposed ? (c < r) : (c > r)) return SMAT_ERR_CSR_INVALID;
-      const uint8_t want = (c == r) ? SMAT_TILE_CAUSAL : SMAT_TILE_FULL;
-      if (kind[e] != want) return SMAT_ERR_CSR_INVALID;
-      prev = c;
+  return validate_layout(nblocks, nnzb, indptr, indices, kind, transposed, false, max_row_out);
+}
+
+int smat_layout_validate_pattern(int nblocks, int64_t nnzb, const int32_t* indptr,
+                                 const int32_t* indices, const uint8_t* kind, int transposed,
+                                 int32_t* max_row_out) {
+  return validate_layout(nblocks, nnzb, indptr, indices, kind, transposed, true, max_row_out);
+}
+
+// ---------------------------------------------------------------- M^(d) masks
+int smat_pattern_tables(int B, int N0, const int64_t* C_indptr, const int32_t* C_indices,
+                        uint32_t* row_bits, int row_words, uint32_t* col_bits, int col_words) {
+  if (B < 1 || N0 < 1) return SMAT_ERR_BAD_PATTERN;
+  if (static_cast<int64_t>(row_words) < (static_cast<int64_t>(N0) + 63) / 32 ||
+      static_cast<int64_t>(col_words) < (static_cast<int64_t>(B) + 63) / 32)
+    return SMAT_ERR_BAD_PATTERN;
+  if (!C_indptr || !row_bits || !col_bits) return SMAT_ERR_NULL_POINTER;
+  if (C_indptr[0] != 0) return SMAT_ERR_BAD_PATTERN;
+  for (int r = 0; r < B; ++r)
+    if (C_indptr[r + 1] < C_indptr[r]) return SMAT_ERR_BAD_PATTERN;
+  if (C_indptr[B] > 0 && !C_indices) return SMAT_ERR_NULL_POINTER;
+  const int64_t rbits = 32LL * row_words, cbits = 32LL * col_words;
+  std::memset(row_bits, 0, sizeof(uint32_t) * static_cast<size_t>(B) * row_words);
+  std::memset(col_bits, 0, sizeof(uint32_t) * static_cast<size_t>(N0) * col_words);
+  for (int r = 0; r < B; ++r) {
+    for (int64_t e = C_indptr[r]; e < C_indptr[r + 1]; ++e) {
+      const int32_t c = C_indices[e];
+      if (c < 0 || c >= N0) return SMAT_ERR_BAD_PATTERN;
+      uint32_t* rw = row_bits + static_cast<int64_t>(r) * row_words;
+      for (int64_t t = c; t < rbits; t += N0) rw[t >> 5] |= 1u << (t & 31);
+      uint32_t* cw = col_bits + static_cast<int64_t>(c) * col_words;
+      for (int64_t t = r; t < cbits; t += B) cw[t >> 5] |= 1u << (t & 31);
     }
   }
-  if (max_row_out) *max_row_out = longest;
+  return SMAT_OK;
+}
+
+int smat_layout_build_pattern(int T, int block, int family, int n, int n_P, int c_all_ones,
+                              int32_t* indptr, int32_t* indices, uint8_t* kind, int64_t capacity,
+                              int64_t* nnzb_out) {
+  if (T < 1 || block < 1) return SMAT_ERR_BAD_SHAPE;
+  if ((family != SMAT_FAMILY_GEOMETRIC && family != SMAT_FAMILY_ENDPOINT) || n_P < 0 || n < n_P ||
+      n > T)
+    return SMAT_ERR_BAD_PATTERN;
+  if (!nnzb_out) return SMAT_ERR_NULL_POINTER;
+  const int nb = (T + block - 1) / block;
+  const bool pow2 = (block & (block - 1)) == 0;
+  int64_t cnt = 0;
+  if (indptr) indptr[0] = 0;
+  for (int qb = 0; qb < nb; ++qb) {
+    const int r0 = qb * block, r1 = std::min(T, r0 + block);
+    for (int kb = 0; kb <= qb; ++kb) {
+      const int c0 = kb * block, c1 = std::min(T, c0 + block);
+      uint8_t k;
+      if (r1 <= n) {          // landmark rows: the lower triangle or the subset relation
+        if (family == SMAT_FAMILY_GEOMETRIC) {
+          k = kb == qb ? SMAT_TILE_CAUSAL : SMAT_TILE_FULL;
+        } else {
+          // i = qb block + a, j = kb block + b: j within i iff kb within qb and b within a
+          if (pow2 && (kb & ~qb) != 0) continue;
+          k = SMAT_TILE_PATTERN;
+        }
+      } else if (r0 >= n) {   // recent rows: global, long-range and recent columns
+        if (kb == qb) {
+          k = SMAT_TILE_CAUSAL;
+        } else {
+          const int g0 = std::max(c0, n_P), g1 = std::min(c1, n);
+          k = (g0 >= g1 || c_all_ones) ? SMAT_TILE_FULL : SMAT_TILE_PATTERN;
+        }
+      } else {                // rows straddle n
+        k = SMAT_TILE_PATTERN;
+      }
+      if (indices) {
+        if (cnt >= capacity || !kind) return SMAT_ERR_CAPACITY;
+        indices[cnt] = kb;
+        kind[cnt] = k;
+      }
+      ++cnt;
+    }
+    if (cnt > (1LL << 31) - 1) return SMAT_ERR_CAPACITY;
+    if (indptr) indptr[qb + 1] = static_cast<int32_t>(cnt);
+  }
+  *nnzb_out = cnt;
+  return SMAT_OK;
+}
+
+int smat_pattern_mask_rows(const smat_pattern_t* pattern, int T, int row_lo, int row_hi,
+                           uint8_t* out) {
+  MdPattern md;
+  int rc;
+  if (T < 1) return SMAT_ERR_BAD_SHAPE;
+  if ((rc = check_pattern(pattern, T, true, &md))) return rc;
+  if (row_lo < 0 || row_hi < row_lo || row_hi > T) return SMAT_ERR_BAD_SHAPE;
+  if (!out && row_hi > row_lo) return SMAT_ERR_NULL_POINTER;
+  for (int i = row_lo; i < row_hi; ++i) {
+    uint8_t* o = out + static_cast<int64_t>(i - row_lo) * T;
+    for (int j0 = 0; j0 < T; j0 += 32) {
+      const uint32_t w = md_row_word(md, T, i, j0);
+      for (int c = 0; c < 32 && j0 + c < T; ++c) o[j0 + c] = (w >> c) & 1u;
+    }
+  }
+  return SMAT_OK;
+}
+
+int smat_pattern_mask_cols(const smat_pattern_t* pattern, int T, int col_lo, int col_hi,
+                           uint8_t* out) {
+  MdPattern md;
+  int rc;
+  if (T < 1) return SMAT_ERR_BAD_SHAPE;
+  if ((rc = check_pattern(pattern, T, true, &md))) return rc;
+  if (col_lo < 0 || col_hi < col_lo || col_hi > T) return SMAT_ERR_BAD_SHAPE;
+  if (!out && col_hi > col_lo) return SMAT_ERR_NULL_POINTER;
+  for (int j = col_lo; j < col_hi; ++j) {
+    uint8_t* o = out + static_cast<int64_t>(j - col_lo) * T;
+    for (int i0 = 0; i0 < T; i0 += 32) {
+      const uint32_t w = md_col_word(md, T, j, i0);
+      for (int c = 0; c < 32 && i0 + c < T; ++c) o[i0 + c] = (w >> c) & 1u;
+    }
+  }
   return SMAT_OK;
 }
 
@@ -415,7 +565,7 @@ int fwd_impl(int dtype, const void* q, const int64_t* q_stride, const void* k,
              const int64_t* o_stride, float* lse, int B, int H, int T, int D,
              const int32_t* indptr, const int32_t* indices, const uint8_t* kind, int nblocks,
              int64_t nnzb, int block, int max_row, float scale, const Work& work,
-             int32_t* err_word, void* stream) {
+             const MdPattern& md, int32_t* err_word, void* stream) {
   int rc;
   if (!q_stride || !k_stride || !v_stride || !o_stride) return SMAT_ERR_NULL_POINTER;
   if ((rc = check_common(dtype, B, H, T, D, nblocks, block))) return rc;
@@ -431,12 +581,12 @@ int fwd_impl(int dtype, const void* q, const int64_t* q_stride, const void* k,
   if (dtype == SMAT_DTYPE_BF16) {
     if (D == 64)
       return fwd_tc<64>(tq, tk, tv, to, lse, B, H, T, indptr, indices, kind, nblocks, nnzb, block,
-                        scale, work, err_word, s);
+                        scale, work, md, err_word, s);
     return fwd_tc<128>(tq, tk, tv, to, lse, B, H, T, indptr, indices, kind, nblocks, nnzb, block,
-                       scale, work, err_word, s);
+                       scale, work, md, err_word, s);
   }
   SimtParams p = simt_params(B, H, T, block, scale, indptr, indices, kind, nblocks, nnzb, err_word,
-                             work, 2);
+                             work, 2, md);
   p.q = static_cast<const float*>(q);
   p.k = static_cast<const float*>(k);
   p.v = static_cast<const float*>(v);
@@ -497,7 +647,7 @@ int dkdv_impl(int dtype, const void* q, const int64_t* q_stride, const void* k,
               const int64_t* dk_stride, void* dv, const int64_t* dv_stride, int B, int H, int T,
               int D, const int32_t* t_indptr, const int32_t* t_indices, const uint8_t* t_kind,
               int nblocks, int64_t nnzb, int block, int t_max_row, float scale, const Work& work,
-              int32_t* err_word, void* stream, bool launch) {
+              const MdPattern& md, int32_t* err_word, void* stream, bool launch) {
   int rc;
   if (!q_stride || !k_stride || !v_stride || !do_stride || !dk_stride || !dv_stride)
     return SMAT_ERR_NULL_POINTER;
@@ -515,12 +665,12 @@ int dkdv_impl(int dtype, const void* q, const int64_t* q_stride, const void* k,
   if (dtype == SMAT_DTYPE_BF16) {
     if (D == 64)
       return bwd_tc<true, 64>(tk, tv, tq, td, lse, delta, tdk, &tdv, B, H, T, t_indptr, t_indices,
-                              t_kind, nblocks, nnzb, block, scale, work, err_word, s);
+                              t_kind, nblocks, nnzb, block, scale, work, md, err_word, s);
     return bwd_tc<true, 128>(tk, tv, tq, td, lse, delta, tdk, &tdv, B, H, T, t_indptr, t_indices,
-                             t_kind, nblocks, nnzb, block, scale, work, err_word, s);
+                             t_kind, nblocks, nnzb, block, scale, work, md, err_word, s);
   }
   SimtParams p = simt_params(B, H, T, block, scale, t_indptr, t_indices, t_kind, nblocks, nnzb,
-                             err_word, work, 1);
+                             err_word, work, 1, md);
   p.q = static_cast<const float*>(q);
   p.k = static_cast<const float*>(k);
   p.v = static_cast<const float*>(v);
@@ -543,8 +693,8 @@ int dq_impl(int dtype, const void* q, const int64_t* q_stride, const void* k,
             const int64_t* do_stride, const float* lse, const float* delta, void* dq,
             const int64_t* dq_stride, int B, int H, int T, int D, const int32_t* indptr,
             const int32_t* indices, const uint8_t* kind, int nblocks, int64_t nnzb, int block,
-            int max_row, float scale, const Work& work, int32_t* err_word, void* stream,
-            bool launch) {
+            int max_row, float scale, const Work& work, const MdPattern& md, int32_t* err_word,
+            void* stream, bool launch) {
   int rc;
   if (!q_stride || !k_stride || !v_stride || !do_stride || !dq_stride) return SMAT_ERR_NULL_POINTER;
   if ((rc = check_common(dtype, B, H, T, D, nblocks, block))) return rc;
@@ -561,12 +711,12 @@ int dq_impl(int dtype, const void* q, const int64_t* q_stride, const void* k,
   if (dtype == SMAT_DTYPE_BF16) {
     if (D == 64)
       return bwd_tc<false, 64>(tq, td, tk, tv, lse, delta, tdq, nullptr, B, H, T, indptr, indices,
-                               kind, nblocks, nnzb, block, scale, work, err_word, s);
+                               kind, nblocks, nnzb, block, scale, work, md, err_word, s);
     return bwd_tc<false, 128>(tq, td, tk, tv, lse, delta, tdq, nullptr, B, H, T, indptr, indices,
-                              kind, nblocks, nnzb, block, scale, work, err_word, s);
+                              kind, nblocks, nnzb, block, scale, work, md, err_word, s);
   }
   SimtParams p = simt_params(B, H, T, block, scale, indptr, indices, kind, nblocks, nnzb, err_word,
-                             work, 1);
+                             work, 1, md);
   p.q = static_cast<const float*>(q);
   p.k = static_cast<const float*>(k);
   p.v = static_cast<const float*>(v);
@@ -582,6 +732,35 @@ int dq_impl(int dtype, const void* q, const int64_t* q_stride, const void* k,
   return dispatch_simt_d<DqSimt>(D, p, T, work.n, B * H, s);
 }
 
+// preprocess, dK/dV and dQ; every pass is checked before the first launches
+int bwd_all(int dtype, const void* q, const int64_t* q_stride, const void* k,
+            const int64_t* k_stride, const void* v, const int64_t* v_stride, const void* o,
+            const int64_t* o_stride, const void* dout, const int64_t* do_stride, const float* lse,
+            float* delta, void* dq, const int64_t* dq_stride, void* dk, const int64_t* dk_stride,
+            void* dv, const int64_t* dv_stride, int B, int H, int T, int D,
+            const int32_t* indptr, const int32_t* indices, const uint8_t* kind,
+            const int32_t* t_indptr, const int32_t* t_indices, const uint8_t* t_kind, int nblocks,
+            int64_t nnzb, int block, int max_row, int t_max_row, float scale,
+            const MdPattern& md, int32_t* err_word, void* stream) {
+  int rc;
+  for (int pass = 0; pass < 2; ++pass) {
+    const bool launch = pass == 1;
+    if (launch && (rc = pre_impl(dtype, o, o_stride, dout, do_stride, delta, B, H, T, D, 0, T,
+                                 stream)))
+      return rc;
+    if ((rc = dkdv_impl(dtype, q, q_stride, k, k_stride, v, v_stride, dout, do_stride, lse, delta,
+                        dk, dk_stride, dv, dv_stride, B, H, T, D, t_indptr, t_indices, t_kind,
+                        nblocks, nnzb, block, t_max_row, scale, kAllTiles, md, err_word, stream,
+                        launch)))
+      return rc;
+    if ((rc = dq_impl(dtype, q, q_stride, k, k_stride, v, v_stride, dout, do_stride, lse, delta,
+                      dq, dq_stride, B, H, T, D, indptr, indices, kind, nblocks, nnzb, block,
+                      max_row, scale, kAllTiles, md, err_word, stream, launch)))
+      return rc;
+  }
+  return SMAT_OK;
+}
+
 }  // namespace
 
 extern "C" {
@@ -593,7 +772,7 @@ int smat_fwd(int dtype, const void* q, const int64_t* q_stride, const void* k,
              int64_t nnzb, int block, int max_row, float scale, int32_t* err_word,
              void* stream) {
   return fwd_impl(dtype, q, q_stride, k, k_stride, v, v_stride, o, o_stride, lse, B, H, T, D,
-                  indptr, indices, kind, nblocks, nnzb, block, max_row, scale, kAllTiles,
+                  indptr, indices, kind, nblocks, nnzb, block, max_row, scale, kAllTiles, kNoPattern,
                   err_word, stream);
 }
 
@@ -606,7 +785,7 @@ int smat_fwd_tiles(int dtype, const void* q, const int64_t* q_stride, const void
   if (!work && n_work == 0) return SMAT_OK;
   if (!work) return SMAT_ERR_NULL_POINTER;
   return fwd_impl(dtype, q, q_stride, k, k_stride, v, v_stride, o, o_stride, lse, B, H, T, D,
-                  indptr, indices, kind, nblocks, nnzb, block, max_row, scale, Work{work, n_work},
+                  indptr, indices, kind, nblocks, nnzb, block, max_row, scale, Work{work, n_work}, kNoPattern,
                   err_word, stream);
 }
 
@@ -631,7 +810,7 @@ int smat_bwd_dkdv(int dtype, const void* q, const int64_t* q_stride, const void*
                   int block, int t_max_row, float scale, int32_t* err_word, void* stream) {
   return dkdv_impl(dtype, q, q_stride, k, k_stride, v, v_stride, dout, do_stride, lse, delta, dk,
                    dk_stride, dv, dv_stride, B, H, T, D, t_indptr, t_indices, t_kind, nblocks,
-                   nnzb, block, t_max_row, scale, kAllTiles, err_word, stream, true);
+                   nnzb, block, t_max_row, scale, kAllTiles, kNoPattern, err_word, stream, true);
 }
 
 int smat_bwd_dkdv_tiles(int dtype, const void* q, const int64_t* q_stride, const void* k,
@@ -646,7 +825,7 @@ int smat_bwd_dkdv_tiles(int dtype, const void* q, const int64_t* q_stride, const
   if (!work) return SMAT_ERR_NULL_POINTER;
   return dkdv_impl(dtype, q, q_stride, k, k_stride, v, v_stride, dout, do_stride, lse, delta, dk,
                    dk_stride, dv, dv_stride, B, H, T, D, t_indptr, t_indices, t_kind, nblocks,
-                   nnzb, block, t_max_row, scale, Work{work, n_work}, err_word, stream, true);
+                   nnzb, block, t_max_row, scale, Work{work, n_work}, kNoPattern, err_word, stream, true);
 }
 
 int smat_bwd_dq(int dtype, const void* q, const int64_t* q_stride, const void* k,
@@ -657,7 +836,7 @@ int smat_bwd_dq(int dtype, const void* q, const int64_t* q_stride, const void* k
                 int block, int max_row, float scale, int32_t* err_word, void* stream) {
   return dq_impl(dtype, q, q_stride, k, k_stride, v, v_stride, dout, do_stride, lse, delta, dq,
                  dq_stride, B, H, T, D, indptr, indices, kind, nblocks, nnzb, block, max_row,
-                 scale, kAllTiles, err_word, stream, true);
+                 scale, kAllTiles, kNoPattern, err_word, stream, true);
 }
 
 int smat_bwd_dq_tiles(int dtype, const void* q, const int64_t* q_stride, const void* k,
@@ -671,7 +850,7 @@ int smat_bwd_dq_tiles(int dtype, const void* q, const int64_t* q_stride, const v
   if (!work) return SMAT_ERR_NULL_POINTER;
   return dq_impl(dtype, q, q_stride, k, k_stride, v, v_stride, dout, do_stride, lse, delta, dq,
                  dq_stride, B, H, T, D, indptr, indices, kind, nblocks, nnzb, block, max_row,
-                 scale, Work{work, n_work}, err_word, stream, true);
+                 scale, Work{work, n_work}, kNoPattern, err_word, stream, true);
 }
 
 int smat_bwd(int dtype, const void* q, const int64_t* q_stride, const void* k,
@@ -683,24 +862,45 @@ int smat_bwd(int dtype, const void* q, const int64_t* q_stride, const void* k,
              const int32_t* t_indptr, const int32_t* t_indices, const uint8_t* t_kind,
              int nblocks, int64_t nnzb, int block, int max_row, int t_max_row, float scale,
              int32_t* err_word, void* stream) {
-  int rc;
-  // every pass is checked before the first one launches
-  for (int pass = 0; pass < 2; ++pass) {
-    const bool launch = pass == 1;
-    if (launch && (rc = pre_impl(dtype, o, o_stride, dout, do_stride, delta, B, H, T, D, 0, T,
-                                 stream)))
-      return rc;
-    if ((rc = dkdv_impl(dtype, q, q_stride, k, k_stride, v, v_stride, dout, do_stride, lse, delta,
-                        dk, dk_stride, dv, dv_stride, B, H, T, D, t_indptr, t_indices, t_kind,
-                        nblocks, nnzb, block, t_max_row, scale, kAllTiles, err_word, stream,
-                        launch)))
-      return rc;
-    if ((rc = dq_impl(dtype, q, q_stride, k, k_stride, v, v_stride, dout, do_stride, lse, delta,
-                      dq, dq_stride, B, H, T, D, indptr, indices, kind, nblocks, nnzb, block,
-                      max_row, scale, kAllTiles, err_word, stream, launch)))
-      return rc;
-  }
-  return SMAT_OK;
+  return bwd_all(dtype, q, q_stride, k, k_stride, v, v_stride, o, o_stride, dout, do_stride, lse,
+                 delta, dq, dq_stride, dk, dk_stride, dv, dv_stride, B, H, T, D, indptr, indices,
+                 kind, t_indptr, t_indices, t_kind, nblocks, nnzb, block, max_row, t_max_row,
+                 scale, kNoPattern, err_word, stream);
+}
+
+int smat_fwd_pattern(int dtype, const void* q, const int64_t* q_stride, const void* k,
+                     const int64_t* k_stride, const void* v, const int64_t* v_stride, void* o,
+                     const int64_t* o_stride, float* lse, int B, int H, int T, int D,
+                     const int32_t* indptr, const int32_t* indices, const uint8_t* kind,
+                     int nblocks, int64_t nnzb, int block, int max_row,
+                     const smat_pattern_t* pattern, float scale, int32_t* err_word,
+                     void* stream) {
+  MdPattern md;
+  const int rc = check_pattern(pattern, T, true, &md);
+  if (rc) return rc;
+  return fwd_impl(dtype, q, q_stride, k, k_stride, v, v_stride, o, o_stride, lse, B, H, T, D,
+                  indptr, indices, kind, nblocks, nnzb, block, max_row, scale, kAllTiles, md,
+                  err_word, stream);
+}
+
+int smat_bwd_pattern(int dtype, const void* q, const int64_t* q_stride, const void* k,
+                     const int64_t* k_stride, const void* v, const int64_t* v_stride,
+                     const void* o, const int64_t* o_stride, const void* dout,
+                     const int64_t* do_stride, const float* lse, float* delta, void* dq,
+                     const int64_t* dq_stride, void* dk, const int64_t* dk_stride, void* dv,
+                     const int64_t* dv_stride, int B, int H, int T, int D,
+                     const int32_t* indptr, const int32_t* indices, const uint8_t* kind,
+                     const int32_t* t_indptr, const int32_t* t_indices, const uint8_t* t_kind,
+                     int nblocks, int64_t nnzb, int block, int max_row, int t_max_row,
+                     const smat_pattern_t* pattern, float scale, int32_t* err_word,
+                     void* stream) {
+  MdPattern md;
+  const int rc = check_pattern(pattern, T, true, &md);
+  if (rc) return rc;
+  return bwd_all(dtype, q, q_stride, k, k_stride, v, v_stride, o, o_stride, dout, do_stride, lse,
+                 delta, dq, dq_stride, dk, dk_stride, dv, dv_stride, B, H, T, D, indptr, indices,
+                 kind, t_indptr, t_indices, t_kind, nblocks, nnzb, block, max_row, t_max_row,
+                 scale, md, err_word, stream);
 }
 
 }  // extern "C"

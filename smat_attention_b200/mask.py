@@ -25,6 +25,15 @@ Two mask families share one container, :class:`MaskSpec`:
     backward dK/dV pass walks.  The reference has no block layout; this
     definition is the one the parity tests hold the kernels to.
 
+``kind="pattern"``
+    An ``M^(d)`` mask tiled for the same kernels (:func:`pattern_layout`).
+    Every causal tile that holds a 1 is active; tiles that are all ones are
+    ``KIND_FULL``, the diagonal tiles of the landmark and recent triangles
+    ``KIND_CAUSAL``, and the rest ``KIND_PATTERN``: the kernels evaluate their
+    mask element by element from two bit tables of the incidence ``C`` (its
+    rows and its columns, each extended by wrap-around so that any 32
+    consecutive profiles or row types are one shift of two words).
+
 Everything here is host-side numpy; :func:`to_device` stages the int32 arrays
 as torch tensors for the CUDA kernels.
 """
@@ -51,10 +60,13 @@ __all__ = [
     "to_device",
     "KIND_FULL",
     "KIND_CAUSAL",
+    "KIND_PATTERN",
+    "pattern_layout",
 ]
 
 KIND_FULL = 0      # tile fully unmasked
 KIND_CAUSAL = 1    # diagonal tile: key position <= query position
+KIND_PATTERN = 2   # M^(d) tile: mask evaluated from the bit tables of C
 
 
 # ---------------------------------------------------------------------------
@@ -198,6 +210,12 @@ class MaskSpec:
     t_kind: Optional[np.ndarray] = None         # (nnzb,) uint8
     dev: Dict[str, object] = field(default_factory=dict)   # device -> staged tensors
 
+    # --- pattern layout (kind="pattern") ----------------------------------
+    source: str = ""                            # "geometric" | "endpoint"
+    row_bits: Optional[np.ndarray] = None       # (B, row_words) uint32, C rows wrapped
+    col_bits: Optional[np.ndarray] = None       # (N0, col_words) uint32, C columns wrapped
+    layouts: Dict[int, object] = field(default_factory=dict)   # block -> pattern layout
+
     # -- derived -----------------------------------------------------------
     @property
     def n_X(self) -> int:
@@ -227,8 +245,13 @@ class MaskSpec:
             return 0
         return int(np.diff(self.indptr).max())
 
+    @property
+    def family(self) -> str:
+        """The M^(d) family of the mask: "geometric" or "endpoint"."""
+        return self.source if self.kind == "pattern" else self.kind
+
     def prof_of_column(self) -> np.ndarray:
-        if self.kind == "endpoint":
+        if self.family == "endpoint":
             return np.arange(self.n_X, dtype=np.int64)
         return np.arange(self.n_X, dtype=np.int64) % self.N0
 
@@ -242,6 +265,11 @@ class MaskSpec:
         return C
 
     def summary(self) -> str:
+        if self.kind == "pattern":
+            kinds = np.bincount(self.tile_kind, minlength=3)
+            return (f"M^({self.d}) {self.source} T={self.T} tiled by {self.block}: "
+                    f"{self.nnzb} tiles ({kinds[KIND_FULL]} full, {kinds[KIND_CAUSAL]} "
+                    f"causal, {kinds[KIND_PATTERN]} pattern), C {self.B}x{self.N0}")
         if self.kind == "block":
             return (f"block layout T={self.T} bs={self.block} W={self.window} "
                     f"S={self.stride} sinks={self.n_sink}: {self.nqb} query "
@@ -470,14 +498,131 @@ def build_block_mask(T: int, block: int, window: int, stride: int = 0,
     return spec
 
 
+def _csr_transpose(nqb: int, indptr: np.ndarray, indices: np.ndarray, kind: np.ndarray):
+    """Per key block, the query blocks reading it (ascending) and their kinds."""
+    lens = np.diff(indptr)
+    row_of = np.repeat(np.arange(nqb, dtype=np.int64), lens)
+    order = np.lexsort((row_of, indices))
+    t_lens = np.bincount(indices, minlength=nqb)
+    t_indptr = np.zeros(nqb + 1, dtype=np.int64)
+    np.cumsum(t_lens, out=t_indptr[1:])
+    return t_indptr.astype(np.int32), row_of[order].astype(np.int32), kind[order]
+
+
+def _wrapped_bits(rows: np.ndarray, period: int, words: int) -> np.ndarray:
+    """Bit table: bit t of row r is ``rows[r, t mod period]`` for ``t < 32 words``."""
+    ext = rows[:, np.arange(32 * words, dtype=np.int64) % period].astype(np.uint8)
+    packed = np.packbits(ext, axis=1, bitorder="little")          # (R, 4 words) bytes
+    return np.ascontiguousarray(packed).view("<u4").astype(np.uint32)
+
+
+def pattern_layout(spec: MaskSpec, block: int = 128) -> MaskSpec:
+    """Tile layout (``kind="pattern"``) of an ``M^(d)`` spec for the softmax kernels.
+
+    The dense mask it stands for is :func:`materialise` of ``spec`` (reference
+    ``mask.py:557-577``), tile by tile: with query tile rows ``[r0, r1)``, key
+    tile columns ``[c0, c1)`` and ``kb <= qb``,
+
+    * landmark rows (``r1 <= n``): geometric tiles are full below the diagonal
+      and causal on it; endpoint tiles follow ``(i & j) == j`` and are PATTERN
+      (left out when empty, which for a power-of-two block is ``kb & ~qb != 0``);
+    * recent rows (``r0 >= n``): the diagonal tile is causal; an off-diagonal
+      tile is full unless it meets the long-range columns ``[n_P, n)`` and
+      ``C`` has a 0, in which case it is PATTERN;
+    * tiles whose rows straddle ``n`` are PATTERN.
+
+    The result is cached on ``spec`` per block size.  ``spec`` keeps its own
+    meaning; the layout carries copies of the fields the kernels need plus the
+    two bit tables of ``C`` (``row_bits``, ``col_bits``).
+    """
+    if spec.kind not in ("geometric", "endpoint"):
+        raise ValueError(f"pattern_layout needs an M^(d) spec, got kind={spec.kind!r}")
+    block = int(block)
+    if block < 1:
+        raise ValueError(f"block must be >= 1, got {block}")
+    cached = spec.layouts.get(block)
+    if cached is not None:
+        return cached
+    t0 = time.perf_counter()
+    T, n, n_P = spec.T, spec.n, spec.n_P
+    endpoint = spec.kind == "endpoint"
+    C = spec.dense_C()
+    c_all = bool(C.all())
+    pow2 = (block & (block - 1)) == 0
+    nqb = -(-T // block)
+    rows, kinds = [], []
+    for qb in range(nqb):
+        r0, r1 = qb * block, min(T, (qb + 1) * block)
+        kb = np.arange(qb + 1, dtype=np.int64)
+        if r1 <= n:
+            if endpoint:
+                if pow2:
+                    kb = kb[(kb & ~qb) == 0]
+                k = np.full(kb.size, KIND_PATTERN, np.uint8)
+            else:
+                k = np.where(kb == qb, KIND_CAUSAL, KIND_FULL).astype(np.uint8)
+        elif r0 >= n:
+            c0 = kb * block
+            c1 = np.minimum(T, c0 + block)
+            plain = (np.maximum(c0, n_P) >= np.minimum(c1, n)) | c_all
+            k = np.where(kb == qb, KIND_CAUSAL,
+                         np.where(plain, KIND_FULL, KIND_PATTERN)).astype(np.uint8)
+        else:
+            k = np.full(kb.size, KIND_PATTERN, np.uint8)
+        rows.append(kb)
+        kinds.append(k)
+    lens = np.fromiter((r.size for r in rows), dtype=np.int64, count=nqb)
+    indptr = np.zeros(nqb + 1, dtype=np.int64)
+    np.cumsum(lens, out=indptr[1:])
+    indices = np.concatenate(rows)
+    kind = np.concatenate(kinds)
+    t_indptr, t_indices, t_kind = _csr_transpose(nqb, indptr, indices, kind)
+    row_words, col_words = (spec.N0 + 63) // 32, (spec.B + 63) // 32
+    lay = MaskSpec(T=T, d=spec.d, kind="pattern", n=n, T_R=spec.T_R,
+                   chunk_align=spec.chunk_align, q=spec.q, dim=spec.dim, N0=spec.N0,
+                   n_dirs=spec.n_dirs, B=spec.B, n_planted=spec.n_planted,
+                   planted_cols=spec.planted_cols, k=spec.k, n_P=n_P,
+                   C_indptr=spec.C_indptr, C_indices=spec.C_indices,
+                   uniform_deg=spec.uniform_deg,
+                   block=block, nqb=nqb, indptr=indptr.astype(np.int32),
+                   indices=indices.astype(np.int32), tile_kind=kind,
+                   t_indptr=t_indptr, t_indices=t_indices, t_kind=t_kind,
+                   source=spec.kind,
+                   row_bits=_wrapped_bits(C, spec.N0, row_words),
+                   col_bits=_wrapped_bits(np.ascontiguousarray(C.T), spec.B, col_words))
+    lay.build_times["total"] = time.perf_counter() - t0
+    spec.layouts[block] = lay
+    return lay
+
+
+def _md_pairs(spec: MaskSpec) -> int:
+    """Ones of the dense ``M^(d)`` mask, counted without building it."""
+    n, T_R, n_P = spec.n, spec.T_R, spec.n_P
+    if spec.family == "endpoint":
+        top = int((np.int64(1) << np.bitwise_count(np.arange(n, dtype=np.int64)).astype(np.int64)).sum())
+    else:
+        top = n * (n + 1) // 2
+    mult = np.bincount(np.arange(T_R, dtype=np.int64) % spec.B, minlength=spec.B)
+    pmult = np.bincount(spec.prof_of_column(), minlength=spec.N0)
+    long_range = int(mult @ spec.dense_C().astype(np.int64) @ pmult)
+    return top + T_R * (T_R + 1) // 2 + T_R * n_P + long_range
+
+
 def block_layout_stats(spec: MaskSpec) -> Dict[str, int]:
-    """Unmasked ``(i, j)`` pairs per head and tile counts of a block layout.
+    """Unmasked ``(i, j)`` pairs per head and tile counts of a block layout
+    (for an ``M^(d)`` spec or its pattern layout: the ones of the dense mask
+    and the tiles of :func:`pattern_layout`).
 
     A full tile contributes ``rows * cols`` (both clipped to ``T``); a causal
     diagonal tile of ``r`` rows contributes ``r (r + 1) / 2``.  The effective
     FLOP count of one head is ``4 D * pairs`` forward and ``3.5x`` that for
     forward plus backward.
     """
+    if spec.kind in ("geometric", "endpoint", "pattern"):
+        lay = pattern_layout(spec) if spec.kind != "pattern" else spec
+        return {"pairs": _md_pairs(lay), "tiles": lay.nnzb, "nqb": lay.nqb,
+                "max_row": lay.max_row, "causal_pairs": lay.T * (lay.T + 1) // 2,
+                "pattern_tiles": int((lay.tile_kind == KIND_PATTERN).sum())}
     if spec.kind != "block":
         raise ValueError("block_layout_stats needs a block layout")
     bs, T = spec.block, spec.T
@@ -566,8 +711,33 @@ def materialise(spec: MaskSpec, dtype=np.float64) -> np.ndarray:
                     M[r0:r1, c0:c1] = 1
         return M
 
+    if spec.kind == "pattern":
+        # the tiles of the layout only: full / causal by kind, pattern tiles
+        # copied from the source mask; everything outside them stays 0
+        src = _materialise_md(spec, dtype)
+        bs = spec.block
+        for qb in range(spec.nqb):
+            r0, r1 = qb * bs, min(T, (qb + 1) * bs)
+            for e in range(spec.indptr[qb], spec.indptr[qb + 1]):
+                kb = int(spec.indices[e])
+                c0, c1 = kb * bs, min(T, (kb + 1) * bs)
+                if spec.tile_kind[e] == KIND_FULL:
+                    M[r0:r1, c0:c1] = 1
+                elif spec.tile_kind[e] == KIND_CAUSAL:
+                    ii = np.arange(r0, r1)[:, None]
+                    jj = np.arange(c0, c1)[None, :]
+                    M[r0:r1, c0:c1] = (jj <= ii).astype(dtype)
+                else:
+                    M[r0:r1, c0:c1] = src[r0:r1, c0:c1]
+        return M
+    return _materialise_md(spec, dtype)
+
+
+def _materialise_md(spec: MaskSpec, dtype) -> np.ndarray:
+    T = spec.T
+    M = np.zeros((T, T), dtype=dtype)
     n, T_R = spec.n, spec.T_R
-    if spec.kind == "endpoint":
+    if spec.family == "endpoint":
         a = np.arange(n, dtype=np.int64)
         M[:n, :n] = ((a[:, None] & a[None, :]) == a[None, :]).astype(dtype)
     else:
@@ -616,21 +786,26 @@ def to_device(spec: MaskSpec, device, *, want_direct: bool = False) -> MaskSpec:
     """Stage the spec's index arrays on ``device`` as torch tensors.
 
     ``M^(d)`` kinds get the reference's views (``attention.py:542-555``):
-    ``C_indptr_t`` / ``C_indices_t`` (int64) and ``plane_pts_t``.  A block
-    layout gets its int32 CSR, kinds and transposed CSR in ``spec.dev[device]``
-    (the arrays the CUDA kernels read), cached per device.
+    ``C_indptr_t`` / ``C_indices_t`` (int64) and ``plane_pts_t``.  A block or
+    pattern layout gets its int32 CSR, kinds and transposed CSR (and, for a
+    pattern layout, the two bit tables of ``C``) in ``spec.dev[device]`` (the
+    arrays the CUDA kernels read), cached per device.
     """
     import torch
 
-    if spec.kind == "block":
+    if spec.kind in ("block", "pattern"):
         key = str(torch.device(device))
         if key not in spec.dev:
             as_t = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(device)
-            spec.dev[key] = {
+            d = {
                 "indptr": as_t(spec.indptr), "indices": as_t(spec.indices),
                 "kind": as_t(spec.tile_kind), "t_indptr": as_t(spec.t_indptr),
                 "t_indices": as_t(spec.t_indices), "t_kind": as_t(spec.t_kind),
             }
+            if spec.kind == "pattern":
+                d["row_bits"] = as_t(spec.row_bits.view(np.int32))
+                d["col_bits"] = as_t(spec.col_bits.view(np.int32))
+            spec.dev[key] = d
         return spec
 
     spec.C_indptr_t = torch.from_numpy(spec.C_indptr).to(device)

@@ -8,9 +8,9 @@ QK-norm, the attention op, and a bias-free ``out`` projection.  Arms:
 
 ``"softmax"``       dense causal softmax through torch SDPA, exactly the
                     reference's baseline arm (``model.py:217-220``);
-``"smat_softmax"``  block-sparse causal softmax under ``spec`` (a
-                    ``kind="block"`` :class:`~smat_attention_b200.mask.MaskSpec`)
-                    on the sm_100a kernels.
+``"smat_softmax"``  causal softmax under ``spec`` on the sm_100a kernels:
+                    a ``kind="block"`` layout, or an ``M^(d)`` mask from
+                    ``build_mask`` (run through its pattern layout).
 
 The reference's kernelised ``"smat"`` arm and its variants (decay, gates,
 content hashing, Mamba mixers) are not part of this package.
@@ -55,8 +55,9 @@ class Attention(nn.Module):
         if d_model % n_heads:
             raise ValueError("d_model must be a multiple of n_heads")
         if arm == "smat_softmax":
-            if spec is None or spec.kind != "block":
-                raise ValueError("arm 'smat_softmax' needs spec=build_block_mask(...)")
+            if spec is None or spec.kind not in ("block", "pattern", "geometric", "endpoint"):
+                raise ValueError("arm 'smat_softmax' needs spec=build_block_mask(...) or "
+                                 "spec=build_mask(...)")
         self.h, self.dh = n_heads, d_model // n_heads
         self.arm, self.spec = arm, spec
         self.qn = nn.LayerNorm(self.dh) if qk_norm else nn.Identity()

@@ -1,0 +1,191 @@
+"""GPU parity of the reference's M^(d) masks through the softmax kernels.
+
+An M^(d) spec from build_mask runs as its pattern layout: the tensor-core
+(bf16) and CUDA-core (fp32) kernels with PATTERN tiles masked element by
+element from bit tables of the incidence C.  Every case compares the kernels
+with the oracle's dense-masked softmax (oracle.dense_softmax) under the
+reference's own dense mask (materialise, src/smat/mask.py:557-577) on the same
+rounded inputs.  Tolerances (max-abs) as for block layouts: bf16 2e-2 for O,
+dQ, dK, dV and 1e-3 for the fp32 LSE; fp32 1e-4.
+"""
+
+import ctypes
+import math
+import os
+
+import numpy as np
+import pytest
+import torch
+
+from oracle.dense_softmax import rowchunked_masked_softmax
+from smat_attention_b200 import _lib
+from smat_attention_b200.attention import (bwd, check_device_errors, fwd, layout_device_args,
+                                           smat_softmax_attention)
+from smat_attention_b200.mask import build_mask, materialise, pattern_layout
+from smat_attention_b200.model import Attention
+
+pytestmark = pytest.mark.gpu
+
+TOL_BF16, TOL_BF16_LSE, TOL_F32 = 2e-2, 1e-3, 1e-4
+GOLD = os.path.join(os.path.dirname(__file__), "golden")
+
+
+def _inputs(B, H, T, D, dtype, seed, device):
+    g = torch.Generator().manual_seed(seed)
+    return [torch.randn(B, H, T, D, generator=g).to(device=device, dtype=dtype)
+            for _ in range(4)]
+
+
+def _mask_rows(M, device):
+    Mt = torch.from_numpy(M).to(device)
+    return lambda r0, r1: Mt[r0:r1]
+
+
+def _run(spec, layout, B, H, D, dtype, seed, device, rows=512):
+    T = spec.T
+    q, k, v, do = _inputs(B, H, T, D, dtype, seed, device)
+    scale = 1.0 / math.sqrt(D)
+    o, lse = fwd(q, k, v, layout, scale)
+    dq, dk, dv = bwd(q, k, v, o, lse, do, layout, scale)
+    torch.cuda.synchronize()
+    assert check_device_errors() == 0
+    f = lambda x: x.float().reshape(B * H, T, D)
+    ref = rowchunked_masked_softmax(f(q), f(k), f(v), f(do),
+                                    _mask_rows(materialise(spec, np.uint8), device), scale,
+                                    rows=rows)
+    shape = lambda x: x.reshape(B, H, T, -1).squeeze(-1)
+    tol = TOL_F32 if dtype == torch.float32 else TOL_BF16
+    tol_lse = TOL_F32 if dtype == torch.float32 else TOL_BF16_LSE
+    errs = {}
+    for name, got, want in zip(("o", "lse", "dq", "dk", "dv"), (o, lse, dq, dk, dv), ref):
+        errs[name] = (got.float() - shape(want).float()).abs().max().item()
+        assert torch.isfinite(got).all(), name
+    print(f"{spec.kind} T={T} d={spec.d} n={spec.n} n_P={spec.n_P} B={spec.B} N0={spec.N0} "
+          f"bs={layout.block if layout.kind == 'pattern' else 128} D={D} {dtype}: " +
+          " ".join(f"{k}={v:.2e}" for k, v in errs.items()))
+    for name, e in errs.items():
+        assert e <= (tol_lse if name == "lse" else tol), (name, e, errs)
+
+
+# (T, d, chunk, n_P): the reference fixture grid of tests/golden/mask_md.npz
+SPECS = [
+    (256, 1, 64, 0),      # d = 1: the plain causal mask (C all ones, no PATTERN tiles)
+    (512, 2, 64, 0),
+    (1024, 3, 64, 0),
+    (2048, 3, 64, 16),    # global columns; PATTERN tiles straddle n_P
+    (1024, 10, 64, 0),    # endpoint family (subset relation on the landmarks)
+    (1000, 3, 32, 0),     # n = 480: tiles straddle n, ragged last tile
+    (300, 8, 8, 0),       # endpoint, T not a multiple of the tile
+    (256, 7, 16, 0),
+    (512, 3, 1, 0),
+]
+
+
+@pytest.mark.parametrize("args", SPECS)
+@pytest.mark.parametrize("D", [64, 128])
+@pytest.mark.parametrize("bs", [128, 64])
+def test_bf16_md(cuda_device, args, D, bs):
+    T, d, chunk, nP = args
+    spec = build_mask(T, d, chunk=chunk, n_P=nP)
+    _run(spec, pattern_layout(spec, bs), 2, 2, D, torch.bfloat16, seed=T + d + D, device=cuda_device)
+
+
+@pytest.mark.parametrize("args", SPECS)
+@pytest.mark.parametrize("bs", [64, 48])
+def test_fp32_md(cuda_device, args, bs):
+    T, d, chunk, nP = args
+    spec = build_mask(T, d, chunk=chunk, n_P=nP)
+    _run(spec, pattern_layout(spec, bs), 1, 2, 64, torch.float32, seed=T + d, device=cuda_device)
+
+
+def test_c3_shape_md3(cuda_device):
+    """The c3 sequence (T = 16384, D = 128, bf16) under the reference's M^(3)
+    mask at chunk 128 (n = 8192, B = 552, N0 = 529), 2 heads; the spec itself is
+    passed (the op tiles it by 128)."""
+    spec = build_mask(16384, 3, chunk=128)
+    _run(spec, spec, 1, 2, 128, torch.bfloat16, seed=2, device=cuda_device)
+
+
+def test_endpoint_t4096(cuda_device):
+    """The endpoint family at T = 4096 (d = 12, B = N0 = 2048), bf16 D = 64."""
+    spec = build_mask(4096, 12, chunk=64)
+    assert spec.kind == "endpoint"
+    _run(spec, spec, 1, 2, 64, torch.bfloat16, seed=12, device=cuda_device)
+
+
+def test_reference_fixture_md3(cuda_device):
+    """The reference's dense-masked outputs (tests/golden/softmax_md3_t256.npz:
+    M^(3), T = 256, chunk 16, D = 16, fp64) through the fp32 kernels, with the
+    head dimension zero-padded to 32 (scores unchanged, padded outputs 0)."""
+    f = np.load(os.path.join(GOLD, "softmax_md3_t256.npz"))
+    args = [str(a) for a in f["mask_args"]]
+    assert args[0] == "md"
+    T = f["q"].shape[1]
+    spec = build_mask(T, int(args[1]), chunk=int(args[2]))
+    pad = lambda x: torch.nn.functional.pad(torch.from_numpy(f[x]).float(), (0, 16))
+    q, k, v, do = (pad(x).unsqueeze(0).to(cuda_device) for x in ("q", "k", "v", "do"))
+    scale = float(f["scale"])
+    o, lse = fwd(q, k, v, spec, scale)
+    dq, dk, dv = bwd(q, k, v, o, lse, do, spec, scale)
+    torch.cuda.synchronize()
+    assert check_device_errors() == 0
+    for got, key in ((o, "o"), (dq, "dq"), (dk, "dk"), (dv, "dv")):
+        g = got[0, :, :, :16].double().cpu().numpy()
+        assert np.abs(g - f[key]).max() < TOL_F32, key
+        assert got[0, :, :, 16:].abs().max().item() == 0.0
+
+
+def test_module_and_autograd(cuda_device):
+    """Attention(arm="smat_softmax", spec=build_mask(...)) forward + backward,
+    against the same module's weights through the oracle."""
+    T, d_model, heads = 1024, 256, 4
+    spec = build_mask(T, 3, chunk=64)
+    torch.manual_seed(0)
+    att = Attention(d_model, heads, "smat_softmax", spec=spec, device=cuda_device)
+    att = att.to(torch.bfloat16)
+    x = torch.randn(2, T, d_model, device=cuda_device, dtype=torch.bfloat16, requires_grad=True)
+    y = att(x)
+    y.float().square().mean().backward()
+    assert torch.isfinite(y).all() and torch.isfinite(x.grad).all()
+    # the op on the module's q, k, v against the oracle
+    q, k, v = att.qkv(x.detach()).view(2, T, 3, heads, 64).unbind(2)
+    q, k, v = (t.transpose(1, 2).contiguous() for t in (q, k, v))
+    o, _ = smat_softmax_attention(q, k, v, spec)
+    ref = rowchunked_masked_softmax(q.float().reshape(-1, T, 64), k.float().reshape(-1, T, 64),
+                                    v.float().reshape(-1, T, 64), v.float().reshape(-1, T, 64),
+                                    _mask_rows(materialise(spec, np.uint8), cuda_device),
+                                    1 / 8, backward=False)[0]
+    assert (o.float().reshape(-1, T, 64) - ref).abs().max().item() < TOL_BF16
+
+
+def test_pattern_tiles_need_the_pattern(cuda_device):
+    """A layout with PATTERN tiles passed to the plain entry point (no tables):
+    the kernels record SMAT_DEVERR_BAD_CSR and treat those tiles as masked."""
+    spec = build_mask(1024, 3, chunk=64)
+    lay = pattern_layout(spec, 128)
+    args = layout_device_args(lay, cuda_device)
+    q, k, v, _ = _inputs(1, 1, 1024, 64, torch.bfloat16, 0, cuda_device)
+    o = torch.empty_like(q)
+    lse = torch.empty(1, 1, 1024, device=cuda_device)
+    err = torch.zeros(1, dtype=torch.int32, device=cuda_device)
+    L = _lib.lib()
+    st = L.smat_fwd(_lib.DTYPE_BF16, q.data_ptr(), _lib.strides3(q), k.data_ptr(),
+                    _lib.strides3(k), v.data_ptr(), _lib.strides3(v), o.data_ptr(),
+                    _lib.strides3(o), lse.data_ptr(), 1, 1, 1024, 64,
+                    args["indptr"].data_ptr(), args["indices"].data_ptr(),
+                    args["kind"].data_ptr(), args["nblocks"], args["nnzb"], 128,
+                    args["max_row"], 0.125, err.data_ptr(),
+                    torch.cuda.current_stream().cuda_stream)
+    assert st == 0
+    torch.cuda.synchronize()
+    assert int(err.item()) & 2
+    # the pattern entry point rejects a bad pattern before launching
+    bad = _lib.Pattern(5, spec.n, 0, spec.B, spec.N0, 1, 1, 0, 0)
+    st = L.smat_fwd_pattern(_lib.DTYPE_BF16, q.data_ptr(), _lib.strides3(q), k.data_ptr(),
+                            _lib.strides3(k), v.data_ptr(), _lib.strides3(v), o.data_ptr(),
+                            _lib.strides3(o), lse.data_ptr(), 1, 1, 1024, 64,
+                            args["indptr"].data_ptr(), args["indices"].data_ptr(),
+                            args["kind"].data_ptr(), args["nblocks"], args["nnzb"], 128,
+                            args["max_row"], ctypes.byref(bad), 0.125, err.data_ptr(),
+                            torch.cuda.current_stream().cuda_stream)
+    assert st == 15
