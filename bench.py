@@ -39,6 +39,7 @@ import subprocess
 import sys
 import time
 
+import numpy as np
 import torch
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
@@ -51,6 +52,9 @@ WORKLOADS = {
     # long context: B=1 leaves 32 (b, h) pairs; sharded by heads or by query blocks
     "c5": dict(name="c5", B=1, H=32, T=131072, D=128, block=128, window=8, stride=32, sinks=4,
                seed=4),
+    # the reference's own mask family on the c3 shapes: M^(3) at chunk 128
+    # (n = 8192 landmarks, C 552 x 529), tiled by 128 as a pattern layout
+    "md3": dict(name="md3", B=4, H=32, T=16384, D=128, block=128, d=3, chunk=128, seed=2),
 }
 WORKLOAD = dict(WORKLOADS["c3"])
 METRIC = "SMat attn fwd+bwd effective TFLOP/s (unmasked FLOPs)"
@@ -58,16 +62,29 @@ UNIT = "TFLOP/s"
 
 
 def _layout_pairs():
-    from smat_attention_b200.mask import block_layout_stats, build_block_mask
+    """The workload's mask (a block layout, or an M^(d) spec) and its unmasked
+    pairs per head."""
+    from smat_attention_b200.mask import block_layout_stats, build_block_mask, build_mask
     w = WORKLOAD
-    spec = build_block_mask(w["T"], w["block"], w["window"], w["stride"], w["sinks"])
+    if "d" in w:
+        spec = build_mask(w["T"], w["d"], chunk=w["chunk"])
+    else:
+        spec = build_block_mask(w["T"], w["block"], w["window"], w["stride"], w["sinks"])
     return spec, block_layout_stats(spec)["pairs"]
+
+
+def _describe():
+    w = WORKLOAD
+    head = f"{w['name']}: B={w['B']} H={w['H']} T={w['T']} D={w['D']} bs={w['block']} "
+    if "d" in w:
+        return head + f"M^({w['d']}) chunk={w['chunk']} (reference build_mask) fwd+bwd per rank"
+    return head + f"W={w['window']} S={w['stride']} sinks={w['sinks']} fwd+bwd per rank"
 
 
 def _flops(pairs):
     w = WORKLOAD
     fwd = 4.0 * w["D"] * pairs * w["B"] * w["H"]
-    return {"fwd": fwd, "dkdv": 2.0 * fwd, "dq": 1.5 * fwd, "step": 3.5 * fwd}
+    return {"fwd": fwd, "dkdv": 2.0 * fwd, "dq": 1.5 * fwd, "bwd": 2.5 * fwd, "step": 3.5 * fwd}
 
 
 def _tensor_mib():
@@ -197,7 +214,12 @@ def cpu_sample(reps=1):
     g = torch.Generator().manual_seed(w["seed"])
     q, k, v, do = (torch.randn(1, w["T"], w["D"], generator=g).to(torch.bfloat16).float()
                    for _ in range(4))
-    rows = OL.block_mask_rows(w["T"], w["block"], w["window"], w["stride"], w["sinks"])
+    if "d" in w:
+        from smat_attention_b200.mask import materialise
+        dense = torch.from_numpy(materialise(spec, np.uint8))
+        rows = lambda r0, r1: dense[r0:r1]
+    else:
+        rows = OL.block_mask_rows(w["T"], w["block"], w["window"], w["stride"], w["sinks"])
     times = []
     for _ in range(reps):
         t0 = time.perf_counter()
@@ -337,8 +359,31 @@ def run_gpu(args):
             lay["nblocks"], lay["nnzb"], lay["block"], lay["max_row"], scale, err.data_ptr(),
             stream.cuda_stream))
 
-    kernels = [("fwd", launch_fwd), ("bwd_pre", launch_pre), ("dkdv", launch_dkdv),
-               ("dq", launch_dq)]
+    def launch_fwd_pattern():
+        _lib.check("smat_fwd_pattern", L.smat_fwd_pattern(
+            1, q.data_ptr(), sp(q), k.data_ptr(), sp(k), v.data_ptr(), sp(v), o.data_ptr(), sp(o),
+            lse.data_ptr(), B, H, T, D, lay["indptr"].data_ptr(), lay["indices"].data_ptr(),
+            lay["kind"].data_ptr(), lay["nblocks"], lay["nnzb"], lay["block"], lay["max_row"],
+            lay["pattern"], scale, err.data_ptr(), stream.cuda_stream))
+
+    def launch_bwd_pattern():
+        _lib.check("smat_bwd_pattern", L.smat_bwd_pattern(
+            1, q.data_ptr(), sp(q), k.data_ptr(), sp(k), v.data_ptr(), sp(v), o.data_ptr(), sp(o),
+            do.data_ptr(), sp(do), lse.data_ptr(), delta.data_ptr(), dq.data_ptr(), sp(dq),
+            dk.data_ptr(), sp(dk), dv.data_ptr(), sp(dv), B, H, T, D,
+            lay["indptr"].data_ptr(), lay["indices"].data_ptr(), lay["kind"].data_ptr(),
+            lay["t_indptr"].data_ptr(), lay["t_indices"].data_ptr(), lay["t_kind"].data_ptr(),
+            lay["nblocks"], lay["nnzb"], lay["block"], lay["max_row"], lay["t_max_row"],
+            lay["pattern"], scale, err.data_ptr(), stream.cuda_stream))
+
+    if lay["pattern"] is None:
+        kernels = [("fwd", launch_fwd), ("bwd_pre", launch_pre), ("dkdv", launch_dkdv),
+                   ("dq", launch_dq)]
+        launches_per_step = 4
+    else:
+        # M^(d): the pattern entry points (the backward launches its three passes)
+        kernels = [("fwd", launch_fwd_pattern), ("bwd", launch_bwd_pattern)]
+        launches_per_step = 4
     for _ in range(max(3, args.warmup)):
         for _, fn in kernels:
             fn()
@@ -385,9 +430,7 @@ def run_gpu(args):
             "warmup": max(3, args.warmup), "ms_per_step": ms_step, "higher_is_better": True,
             "scaling": "strong" if strong else "weak", "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic",
-            "config": {"workload": f"{w['name']}: B={w['B']} H={w['H']} T={w['T']} D={w['D']} "
-                                   f"bs={w['block']} W={w['window']} S={w['stride']} "
-                                   f"sinks={w['sinks']} fwd+bwd per rank",
+            "config": {"workload": _describe(),
                        "global_batch": w["B"] * (1 if strong else ws), "seq_len": w["T"],
                        "heads": w["H"] * (ws if strong else 1), "head_dim": w["D"],
                        "parallelism": (f"head partition x{ws}" if strong
@@ -406,7 +449,7 @@ def run_gpu(args):
                 "value": ws * fl["step"] / (e2e_ms * 1e-3) / 1e12, "unit": UNIT,
                 "ms_per_step": e2e_ms, "h2d_bytes_per_step": nbytes,
                 "d2h_bytes_per_step": nbytes},
-            "gpu_launches": K * len(kernels),
+            "gpu_launches": K * launches_per_step,
             "device_errors": dev_err,
             "clocks": clk,
         }

@@ -7,6 +7,18 @@ with the oracle's dense-masked softmax (oracle.dense_softmax) under the
 reference's own dense mask (materialise, src/smat/mask.py:557-577) on the same
 rounded inputs.  Tolerances (max-abs) as for block layouts: bf16 2e-2 for O,
 dQ, dK, dV and 1e-3 for the fp32 LSE; fp32 1e-4.
+
+The 2e-2 bf16 bound is an absolute one, set for block layouts whose outputs
+and gradients stay below about 4 in magnitude at N(0,1) inputs.  M^(d) masks
+concentrate attention (a landmark row of the endpoint family sees
+2^popcount(i) keys, and key 0 is visible to every row), so dK / dV of the
+endpoint family reach about 10, and the rounding of the bf16 tensor-core
+operands (P, dS) grows with them: the relative error stays that of the block
+layouts (relative norm 2-3e-3 in both families).  A bf16 tensor is therefore
+held to 2e-2 * max(1, max|ref| / 4) max-abs -- the plain 2e-2 wherever its
+largest entry is at most 4, as for every geometric case here -- and to 1e-2 in
+relative norm (the reference's own backward test allows 2e-2,
+tests/test_triton_bwd.py:46).
 """
 
 import ctypes
@@ -56,15 +68,24 @@ def _run(spec, layout, B, H, D, dtype, seed, device, rows=512):
     shape = lambda x: x.reshape(B, H, T, -1).squeeze(-1)
     tol = TOL_F32 if dtype == torch.float32 else TOL_BF16
     tol_lse = TOL_F32 if dtype == torch.float32 else TOL_BF16_LSE
-    errs = {}
+    errs, bounds, rel = {}, {}, {}
     for name, got, want in zip(("o", "lse", "dq", "dk", "dv"), (o, lse, dq, dk, dv), ref):
-        errs[name] = (got.float() - shape(want).float()).abs().max().item()
+        want = shape(want).float()
+        diff = got.float() - want
+        errs[name] = diff.abs().max().item()
+        rel[name] = (diff.norm() / want.norm().clamp_min(1e-30)).item()
+        bounds[name] = tol_lse if name == "lse" else tol
+        if dtype == torch.bfloat16 and name != "lse":
+            bounds[name] *= max(1.0, want.abs().max().item() / 4.0)
         assert torch.isfinite(got).all(), name
     print(f"{spec.kind} T={T} d={spec.d} n={spec.n} n_P={spec.n_P} B={spec.B} N0={spec.N0} "
           f"bs={layout.block if layout.kind == 'pattern' else 128} D={D} {dtype}: " +
-          " ".join(f"{k}={v:.2e}" for k, v in errs.items()))
+          " ".join(f"{k}={v:.2e}(<{bounds[k]:.1e})" for k, v in errs.items()) +
+          " rel " + " ".join(f"{k}={v:.1e}" for k, v in rel.items()))
     for name, e in errs.items():
-        assert e <= (tol_lse if name == "lse" else tol), (name, e, errs)
+        assert e <= bounds[name], (name, e, errs, bounds)
+        if dtype == torch.bfloat16 and name != "lse":
+            assert rel[name] <= 1e-2, (name, rel)
 
 
 # (T, d, chunk, n_P): the reference fixture grid of tests/golden/mask_md.npz
