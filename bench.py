@@ -52,6 +52,8 @@ WORKLOADS = {
     # long context: B=1 leaves 32 (b, h) pairs; sharded by heads or by query blocks
     "c5": dict(name="c5", B=1, H=32, T=131072, D=128, block=128, window=8, stride=32, sinks=4,
                seed=4),
+    # LM training step, batch 8 x 8192 per rank
+    "c4": dict(name="c4", B=8, seed=3),
     # the reference's own mask family on the c3 shapes: M^(3) at chunk 128
     # (n = 8192 landmarks, C 552 x 529), tiled by 128 as a pattern layout
     "md3": dict(name="md3", B=4, H=32, T=16384, D=128, block=128, d=3, chunk=128, seed=2),
@@ -460,6 +462,95 @@ def run_gpu(args):
         dist.destroy_process_group()
 
 
+def run_lm(args):
+    """training steps (forward, backward, AdamW on fp32
+    masters) of the 12-layer LM with the block-sparse arm in every layer, on
+    uniform synthetic token IDs.  Data parallel over the ranks: every rank
+    runs the full per-rank batch and the bf16 gradients are all-reduced
+    (one NCCL call over a flat buffer) before the optimizer step."""
+    from smat_attention_b200.attention import check_device_errors
+    from smat_attention_b200.lm import C4, LM, MasterAdamW, allreduce_grads, train_step
+    dist, rank, ws, local = _dist()
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    w = WORKLOAD
+    cfg = C4
+    B, T = w["B"], cfg.seq_len
+    model = LM(cfg, device=device, seed=w["seed"])
+    opt = MasterAdamW(model.parameters(), lr=6e-4)
+    g = torch.Generator().manual_seed(w["seed"] + rank)
+    host = torch.randint(0, cfg.vocab, (B, T + 1), generator=g).pin_memory()
+    tokens = host.to(device)
+    hook = (lambda: allreduce_grads(model, dist)) if dist is not None else None
+
+    def step(tok):
+        return train_step(model, opt, tok, before_step=hook)
+
+    for _ in range(max(3, args.warmup)):
+        step(tokens)
+    _barrier(dist, device)
+    K = args.steps
+    clocks = ClockSampler(device)
+    stream = torch.cuda.current_stream(device)
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(K + 1)]
+    ev[0].record(stream)
+    for i in range(K):
+        loss = step(tokens)
+        ev[i + 1].record(stream)
+    torch.cuda.synchronize(device)
+    clk = clocks.stop()
+    ms = [ev[i].elapsed_time(ev[i + 1]) for i in range(K)]
+    ms_step = _max_over_ranks(dist, sum(ms) / K, device)
+    # end to end: token IDs from pinned host memory, the loss read back, per step
+    E = max(1, min(K, 3))
+    _barrier(dist, device)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    losses = []
+    for _ in range(E):
+        loss_e = step(host.to(device, non_blocking=True))
+        losses.append(loss_e.to("cpu", non_blocking=True))
+    e1.record(stream)
+    torch.cuda.synchronize(device)
+    e2e_ms = _max_over_ranks(dist, e0.elapsed_time(e1) / E, device)
+    dev_err = check_device_errors(device)
+    if rank == 0:
+        tok_step = ws * B * T
+        attn = cfg.n_layers * 3.5 * 4.0 * cfg.head_dim * _lm_pairs(cfg) * B * cfg.n_heads
+        dense = 6.0 * cfg.n_params() * B * T
+        line = {
+            "metric": "LM training tokens/s (fwd+bwd+AdamW)", "value": tok_step / (ms_step * 1e-3),
+            "unit": "tokens/s", "n_gpus": ws, "steps": K, "warmup": max(3, args.warmup),
+            "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": f"c4: {cfg.n_layers} layers d_model {cfg.d_model} "
+                                   f"{cfg.n_heads}x{cfg.head_dim} heads SwiGLU {cfg.mlp_hidden} "
+                                   f"vocab {cfg.vocab}, batch {B} x {T} per rank, bs "
+                                   f"{cfg.block} W={cfg.window} S={cfg.stride} "
+                                   f"sinks={cfg.n_sink}, bf16 + fp32 master AdamW",
+                       "global_batch": B * ws, "seq_len": T,
+                       "parallelism": f"data parallel x{ws} (NCCL gradient all-reduce)",
+                       "params": cfg.n_params(),
+                       "l2": "activations far larger than L2; no flush"},
+            "model_tflops": (dense + attn) * ws / (ms_step * 1e-3) / 1e12,
+            "attention_tflops_per_step": attn / 1e12,
+            "loss": float(losses[-1].item()),
+            "e2e": {"value": tok_step / (e2e_ms * 1e-3), "unit": "tokens/s",
+                    "ms_per_step": e2e_ms, "h2d_bytes_per_step": host.numel() * 8,
+                    "d2h_bytes_per_step": 4},
+            "device_errors": dev_err,
+            "clocks": clk,
+        }
+        print(json.dumps(line), flush=True)
+    if dist is not None:
+        dist.destroy_process_group()
+
+
+def _lm_pairs(cfg):
+    from smat_attention_b200.mask import block_layout_stats
+    return block_layout_stats(cfg.mask())["pairs"]
+
+
 def run_sharded(args):
     """c5 with query-block sharding: every rank runs its zig-zag share of the
     query tiles of all heads; the timed step includes both exchanges."""
@@ -578,8 +669,15 @@ def main():
         WORKLOAD["B"] = args.batch
     if args.heads:
         WORKLOAD["H"] = args.heads
-    if args.impl == "reference":
+    if args.workload == "c4":
+        args.no_cpu_baseline = True
+    if args.impl == "reference" and args.workload != "c4":
         run_reference(args)
+    elif args.impl == "reference":
+        print(json.dumps({"impl": "reference", "unavailable": "the reference arm times the "
+                          "dense-masked attention on host cores; c4 is a GPU training step"}))
+    elif args.workload == "c4":
+        run_lm(args)
     elif args.workload == "c5" and args.shard == "queries":
         run_sharded(args)
     else:

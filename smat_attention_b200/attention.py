@@ -204,8 +204,13 @@ class SmatSoftmaxFn(torch.autograd.Function):
     ``lse`` not)."""
 
     @staticmethod
-    def forward(ctx, q, k, v, spec, scale):
-        o, lse = fwd(q, k, v, spec, scale)
+    def forward(ctx, q, k, v, spec, scale, tokens_major=False):
+        o = None
+        if tokens_major:
+            # O in [B, T, H, D] memory, handed out as its [B, H, T, D] view
+            B, H, T, D = q.shape
+            o = torch.empty(B, T, H, D, dtype=q.dtype, device=q.device).transpose(1, 2)
+        o, lse = fwd(q, k, v, spec, scale, o=o)
         ctx.save_for_backward(q, k, v, o, lse)
         ctx.spec, ctx.scale = spec, scale
         ctx.mark_non_differentiable(lse)
@@ -215,10 +220,10 @@ class SmatSoftmaxFn(torch.autograd.Function):
     def backward(ctx, do, _dlse):
         q, k, v, o, lse = ctx.saved_tensors
         dq, dk, dv = bwd(q, k, v, o, lse, do, ctx.spec, ctx.scale)
-        return dq, dk, dv, None, None
+        return dq, dk, dv, None, None, None
 
 
-def smat_softmax_attention(q, k, v, spec: MaskSpec, scale=None):
+def smat_softmax_attention(q, k, v, spec: MaskSpec, scale=None, tokens_major=False):
     """``(o, lse)`` of block-sparse causal softmax attention under ``spec``.
 
     ``q, k, v``: ``[B, H, T, D]`` CUDA tensors, bf16 or fp32, same shape.
@@ -227,7 +232,10 @@ def smat_softmax_attention(q, k, v, spec: MaskSpec, scale=None):
     from :func:`smat_attention_b200.mask.build_mask` (run through its pattern
     layout, :func:`smat_attention_b200.mask.pattern_layout`), with
     ``spec.T == T``.  ``scale`` defaults to ``1 / sqrt(D)``.
+    ``tokens_major=True`` stores ``o`` in ``[B, T, H, D]`` memory (returned as
+    its ``[B, H, T, D]`` view), so ``o.transpose(1, 2).reshape(B, T, H * D)``
+    is free for the output projection.
     """
     if scale is None:
         scale = 1.0 / math.sqrt(q.shape[-1])
-    return SmatSoftmaxFn.apply(q, k, v, spec, float(scale))
+    return SmatSoftmaxFn.apply(q, k, v, spec, float(scale), bool(tokens_major))

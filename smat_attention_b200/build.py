@@ -18,7 +18,7 @@ PKG = os.path.dirname(os.path.abspath(__file__))
 ROOT = os.path.dirname(PKG)
 CSRC = os.path.join(PKG, "csrc")
 LIB = os.path.join(PKG, "libsmat_b200.so")
-SOURCES = ["smat_abi.cu", "noalloc.cu", "rows.cu"]
+SOURCES = ["smat_abi.cu", "noalloc.cu", "rows.cu", "lm_ops.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 
@@ -33,6 +33,7 @@ def _inputs():
     files = [os.path.join(CSRC, f) for f in os.listdir(CSRC)
              if f.endswith((".cu", ".cuh", ".h"))]
     files.append(os.path.join(ROOT, "include", "smat_b200.h"))
+    files.append(os.path.join(ROOT, "include", "smat_lm.h"))
     files.append(os.path.abspath(__file__))
     return files
 

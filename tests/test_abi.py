@@ -123,3 +123,34 @@ def test_row_exchange_rejects_on_host():
                                   None, None) == 8
     assert L.smat_rows_accumulate(1, 16, st, 16, st, 1, 4, 1024, 64, 16, 5, 16, 16, -1, 16,
                                   None, None) == 1
+
+
+LM_HEADER = os.path.join(os.path.dirname(HEADER), "smat_lm.h")
+
+
+def test_lm_header_symbols_exported():
+    from smat_attention_b200 import lm_ops
+    text = open(LM_HEADER).read()
+    syms = sorted(set(re.findall(r"SMAT_API\s+\w+\**\s+\**(smat_\w+)\s*\(", text)))
+    assert len(syms) == 7 and set(syms) == set(lm_ops.SIGNATURES)
+    L = lm_ops._L()
+    for s in syms:
+        assert hasattr(L, s), s
+
+
+def test_lm_ops_reject_on_host():
+    from smat_attention_b200 import lm_ops
+    L = lm_ops._L()
+    assert L.smat_lm_rmsnorm_fwd(None, None, 16, None, 16, 16, 4, 768, 1e-5, None) == 8
+    assert L.smat_lm_rmsnorm_fwd(16, 16, 16, None, 16, 16, 4, 768, 1e-5, None) == 8
+    assert L.smat_lm_rmsnorm_fwd(16, None, 16, None, 16, 16, 4, 700, 1e-5, None) == 1
+    assert L.smat_lm_rmsnorm_fwd(16, None, 16, None, 16, 16, 4, 1280, 1e-5, None) == 1
+    assert L.smat_lm_rmsnorm_fwd(8, None, 16, None, 16, 16, 4, 768, 1e-5, None) == 6
+    assert L.smat_lm_rmsnorm_bwd(16, 16, 16, 16, None, 16, 16, 0, 4, 768, None) == 1
+    assert L.smat_lm_rmsnorm_bwd(16, 16, 16, 16, 24, 16, 16, 4, 4, 768, None) == 6
+    assert L.smat_lm_rope_split_fwd(16, 16, 16, 16, 16, 16, 1, 8, 2, 12, None) == 1
+    assert L.smat_lm_rope_split_bwd(16, 16, None, 16, 16, 16, 1, 8, 2, 64, None) == 8
+    assert L.smat_lm_swiglu_fwd(16, 16, 4, 12, None) == 1
+    assert L.smat_lm_swiglu_bwd(16, 16, 8, 4, 16, None) == 6
+    assert L.smat_lm_cross_entropy(16, 16, 16, 4, 1001, 1.0, None, None) == 1
+    assert L.smat_lm_cross_entropy(16, None, 16, 4, 1000, 1.0, None, None) == 8
