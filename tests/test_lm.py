@@ -63,3 +63,37 @@ def test_master_adamw_cpu():
         assert torch.allclose(opt.master[0], rp, atol=1e-6)
         assert torch.allclose(opt.master[1], rs, atol=1e-6)
         assert torch.equal(p.detach(), rp.detach().to(torch.bfloat16))
+
+
+def _dp_worker(rank, world, port):
+    import datetime
+    import os
+
+    import torch.distributed as dist
+
+    from smat_attention_b200.lm import allreduce_grads
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=60))
+    try:
+        m = torch.nn.Sequential(torch.nn.Linear(4, 3), torch.nn.Linear(3, 2, bias=False))
+        for i, p in enumerate(m.parameters()):
+            p.grad = torch.full_like(p, float(rank + 1) * (i + 1))
+        allreduce_grads(m, dist)
+        for i, p in enumerate(m.parameters()):
+            want = (i + 1) * sum(r + 1 for r in range(world)) / world
+            assert torch.allclose(p.grad, torch.full_like(p, want)), (i, p.grad)
+    finally:
+        dist.destroy_process_group()
+
+
+def test_allreduce_grads_gloo():
+    import socket
+
+    import torch.multiprocessing as mp
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    mp.spawn(_dp_worker, args=(3, port), nprocs=3, join=True)
