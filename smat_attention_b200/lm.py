@@ -282,7 +282,8 @@ def allreduce_grads(model: nn.Module, dist, group=None) -> None:
     flat = torch.cat([g.reshape(-1) for g in grads])
     dist.all_reduce(flat, group=group)
     flat.div_(dist.get_world_size(group))
-    torch._foreach_copy_(grads, list(flat.split([g.numel() for g in grads])))
+    parts = flat.split([g.numel() for g in grads])
+    torch._foreach_copy_(grads, [c.view_as(g) for c, g in zip(parts, grads)])
 
 
 def train_step(model: LM, opt: MasterAdamW, tokens: torch.Tensor,
