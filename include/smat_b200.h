@@ -393,6 +393,34 @@ SMAT_API int smat_bwd_pattern(int dtype,
                      const smat_pattern_t* pattern,
                      float scale, int32_t* err_word, void* stream);
 
+/* ---------------------------------------------------------------- decode
+ * One new query per (batch, head) against its KV cache: for b, h,
+ *   o[b,h] = softmax_j(scale q[b,h] . k[b,h,j]) v[b,h,j] over the keys j the
+ *   layout shows to query position t = pos[b] (its CSR row t / block; FULL
+ *   entries all keys, CAUSAL entries j <= t, PATTERN entries the M^(d) rule
+ *   of `pattern`, which may be NULL for layouts without PATTERN tiles),
+ * and lse[b*H + h] (natural log, may be NULL).  q, o: [B, H, D] with (b, h)
+ * element strides q_stride[2] / o_stride[2]; k_cache, v_cache: [B, H, T, D]
+ * with (b, h, t) strides; pos: DEVICE int32 [B], each in [0, T) (else
+ * SMAT_DEVERR_BAD_WORK and that row's output is 0).  bf16 only, D in {64,
+ * 128}.  `workspace` holds the per-split partial results: at least
+ * smat_decode_workspace(B, H, D, max_row) floats of device memory.
+ * The softmax counterpart of the reference's streaming decoder
+ * (src/smat/attention.py:496-535, SmatDecoder.step). */
+SMAT_API int smat_decode_workspace(int B, int H, int D, int max_row, int64_t* floats_out);
+SMAT_API int smat_decode(int dtype,
+                const void* q, const int64_t* q_stride,
+                const void* k_cache, const int64_t* k_stride,
+                const void* v_cache, const int64_t* v_stride,
+                void* o, const int64_t* o_stride,
+                float* lse, const int32_t* pos,
+                int B, int H, int T, int D,
+                const int32_t* indptr, const int32_t* indices, const uint8_t* kind,
+                int nblocks, int64_t nnzb, int block, int max_row,
+                const smat_pattern_t* pattern,
+                float scale, float* workspace, int64_t workspace_floats,
+                int32_t* err_word, void* stream);
+
 /* smat_bwd_noalloc: smat_bwd for callers that cannot allocate device memory
  * (their memory belongs to another allocator, or cudaMalloc's implicit
  * synchronisation is not allowed on their path, or their budget is fixed at

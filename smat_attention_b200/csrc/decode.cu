@@ -1,0 +1,324 @@
+// Decode: one new query per (batch, head) attending over its KV cache under a
+// block layout or an M^(d) pattern layout (smat_decode in include/smat_b200.h).
+//
+// One query row reads every visible key and value once, so decode is
+// HBM-bound (2 D bytes per key and value at bf16) and runs on CUDA cores:
+//
+//   partial  grid (B H, n_split), 128 threads.  Split s walks entries
+//            [s bps, (s + 1) bps) of the query's CSR row.  A key is owned by
+//            a group of D / 8 lanes (16-byte vectors, a 256-byte row read by
+//            16 lanes at D = 128), each warp handling 32 / (D / 8) keys per
+//            step; the dot product is reduced inside the group and each
+//            group keeps an online softmax (max, sum, D / 8 x 8 outputs).
+//            Groups and warps are merged at the end into one partial
+//            (m, l, o[D]) per split, in base-2 exponent units.
+//   combine  grid B H, D threads: rescales the partials to their common max
+//            and writes o (bf16) and the natural-log LSE.
+//
+// Visibility of key j for query position t: FULL entries all keys, CAUSAL
+// entries j <= t, PATTERN entries the row word of pattern.cuh.
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+
+#include <cmath>
+#include <cstdint>
+
+#include "../../include/smat_b200.h"
+#include "common.cuh"
+#include "pattern.cuh"
+
+namespace {
+
+using namespace smat;
+
+struct DecodeParams {
+  const __nv_bfloat16* q;
+  const __nv_bfloat16* k;
+  const __nv_bfloat16* v;
+  __nv_bfloat16* o;
+  float* lse;
+  const int32_t* pos;
+  const int32_t* indptr;
+  const int32_t* indices;
+  const uint8_t* kind;
+  float* part;               // [B H][n_split][D + 2]: m, l, o[D]
+  int64_t q_sb, q_sh, k_sb, k_sh, k_st, v_sb, v_sh, v_st, o_sb, o_sh;
+  int B, H, T, nblocks, nnzb, bs, n_split, bps;
+  float scale_log2;
+  int32_t* err;
+  MdPattern md;
+};
+
+struct alignas(16) V8 {
+  __nv_bfloat162 h[4];
+};
+
+__device__ __forceinline__ void unpack8(const V8& v, float* f) {
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 t = __bfloat1622float2(v.h[i]);
+    f[2 * i] = t.x;
+    f[2 * i + 1] = t.y;
+  }
+}
+
+// merge (m2, l2, o2) into (m, l, o): all in base-2 exponent units
+template <int N>
+__device__ __forceinline__ void merge_state(float& m, float& l, float* o, float m2, float l2,
+                                            const float* o2) {
+  const float mm = fmaxf(m, m2);
+  if (mm == -INFINITY) return;
+  const float a = exp2f(m - mm), b = exp2f(m2 - mm);
+  l = l * a + l2 * b;
+#pragma unroll
+  for (int i = 0; i < N; ++i) o[i] = o[i] * a + o2[i] * b;
+  m = mm;
+}
+
+template <int D>
+__global__ void __launch_bounds__(128) decode_partial_kernel(const DecodeParams p) {
+  constexpr int G = D / 8;        // lanes per key
+  constexpr int KPW = 32 / G;     // keys per warp step
+  __shared__ float red_m[4][KPW], red_l[4][KPW];
+  __shared__ float red_o[4][D];
+  const int bh = blockIdx.x, split = blockIdx.y;
+  const int b = bh / p.H, h = bh % p.H;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int slot = lane / G, part = lane % G;
+  float* out = p.part + (static_cast<int64_t>(bh) * p.n_split + split) * (D + 2);
+
+  const int t = __ldg(p.pos + b);
+  int e0 = 0, e1 = 0;
+  if (t < 0 || t >= p.T) {
+    if (threadIdx.x == 0 && p.err) atomicOr(p.err, DEV_ERR_BAD_WORK);
+  } else {
+    const int qb = t / p.bs;
+    const int a = __ldg(p.indptr + qb), z = __ldg(p.indptr + qb + 1);
+    if (a < 0 || z < a || z > p.nnzb) {
+      if (threadIdx.x == 0 && p.err) atomicOr(p.err, DEV_ERR_BAD_CSR);
+    } else {
+      e0 = a + split * p.bps;
+      e1 = min(z, e0 + p.bps);
+    }
+  }
+
+  float qv[8];
+  {
+    const V8 raw = *reinterpret_cast<const V8*>(p.q + b * p.q_sb + h * p.q_sh + part * 8);
+    unpack8(raw, qv);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) qv[i] *= p.scale_log2;
+  }
+  float m = -INFINITY, l = 0.f, o[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) o[i] = 0.f;
+  const __nv_bfloat16* kbase = p.k + b * p.k_sb + h * p.k_sh + part * 8;
+  const __nv_bfloat16* vbase = p.v + b * p.v_sb + h * p.v_sh + part * 8;
+
+  for (int e = e0; e < e1; ++e) {
+    const int kb = __ldg(p.indices + e);
+    const uint8_t kd = __ldg(p.kind + e);
+    if (kb < 0 || kb >= p.nblocks || kb * p.bs > t) {
+      if (threadIdx.x == 0 && p.err) atomicOr(p.err, DEV_ERR_BAD_CSR);
+      continue;
+    }
+    const int j0 = kb * p.bs;
+    const int jn = min(p.bs, p.T - j0);
+    // warp-uniform trip count: every lane of a group takes part in its shuffles
+    for (int base = warp * KPW; base < jn; base += 4 * KPW) {
+      const int jj = base + slot;
+      const bool in = jj < jn;
+      const int j = j0 + (in ? jj : 0);
+      float kv[8];
+      unpack8(*reinterpret_cast<const V8*>(kbase + static_cast<int64_t>(j) * p.k_st), kv);
+      float s = 0.f;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) s = fmaf(qv[i], kv[i], s);
+#pragma unroll
+      for (int off = G / 2; off > 0; off >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
+      bool vis = in;
+      if (kd == 1) {
+        vis = vis && j <= t;
+      } else if (kd == 2) {
+        if (p.md.row_bits) {
+          vis = vis && ((md_row_word(p.md, p.T, t, j & ~31) >> (j & 31)) & 1u);
+        } else {
+          vis = false;
+          if (part == 0 && p.err) atomicOr(p.err, DEV_ERR_BAD_CSR);
+        }
+      }
+      if (!vis) continue;
+      float vv[8];
+      unpack8(*reinterpret_cast<const V8*>(vbase + static_cast<int64_t>(j) * p.v_st), vv);
+      if (s > m) {
+        const float a = exp2f(m - s);   // 0 when m is still -inf
+        l *= a;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) o[i] *= a;
+        m = s;
+      }
+      const float pr = exp2f(s - m);
+      l += pr;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) o[i] = fmaf(pr, vv[i], o[i]);
+    }
+  }
+
+  // merge the KPW groups of the warp: lanes with the same part, xor over slot bits
+#pragma unroll
+  for (int off = G; off < 32; off <<= 1) {
+    const float m2 = __shfl_xor_sync(0xffffffffu, m, off);
+    const float l2 = __shfl_xor_sync(0xffffffffu, l, off);
+    float o2[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) o2[i] = __shfl_xor_sync(0xffffffffu, o[i], off);
+    merge_state<8>(m, l, o, m2, l2, o2);
+  }
+  // merge the four warps
+  if (slot == 0) {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) red_o[warp][part * 8 + i] = o[i];
+    if (part == 0) {
+      red_m[warp][0] = m;
+      red_l[warp][0] = l;
+    }
+  }
+  __syncthreads();
+  for (int d = threadIdx.x; d < D; d += blockDim.x) {
+    float M = red_m[0][0], L = red_l[0][0], O = red_o[0][d];
+#pragma unroll
+    for (int w = 1; w < 4; ++w) merge_state<1>(M, L, &O, red_m[w][0], red_l[w][0], &red_o[w][d]);
+    out[2 + d] = O;
+    if (d == 0) {
+      out[0] = M;
+      out[1] = L;
+    }
+  }
+}
+
+template <int D>
+__global__ void __launch_bounds__(D) decode_combine_kernel(const DecodeParams p) {
+  const int bh = blockIdx.x, d = threadIdx.x;
+  const int b = bh / p.H, h = bh % p.H;
+  const float* in = p.part + static_cast<int64_t>(bh) * p.n_split * (D + 2);
+  float M = -INFINITY, L = 0.f, O = 0.f;
+  for (int s = 0; s < p.n_split; ++s) {
+    const float* ps = in + s * (D + 2);
+    merge_state<1>(M, L, &O, ps[0], ps[1], &ps[2 + d]);
+  }
+  const float r = L > 0.f ? O / L : 0.f;
+  p.o[b * p.o_sb + h * p.o_sh + d] = __float2bfloat16_rn(r);
+  if (d == 0 && p.lse)
+    p.lse[bh] = L > 0.f ? (M + log2f(L)) * 0.69314718055994531f : -INFINITY;
+}
+
+int status() { return cudaGetLastError() == cudaSuccess ? SMAT_OK : SMAT_ERR_LAUNCH; }
+
+// splits per (b, h): enough CTAs for about four per SM, at most one entry each
+int n_splits(int B, int H, int max_row) {
+  const int64_t bh = static_cast<int64_t>(B) * H;
+  int64_t s = (592 + bh - 1) / bh;
+  if (s > max_row) s = max_row;
+  return static_cast<int>(s < 1 ? 1 : s);
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+}  // namespace
+
+extern "C" {
+
+int smat_decode_workspace(int B, int H, int D, int max_row, int64_t* floats_out) {
+  if (B < 1 || H < 1 || max_row < 0 || (D != 64 && D != 128)) return SMAT_ERR_BAD_SHAPE;
+  if (!floats_out) return SMAT_ERR_NULL_POINTER;
+  *floats_out = static_cast<int64_t>(B) * H * n_splits(B, H, max_row) * (D + 2);
+  return SMAT_OK;
+}
+
+int smat_decode(int dtype, const void* q, const int64_t* q_stride, const void* k_cache,
+                const int64_t* k_stride, const void* v_cache, const int64_t* v_stride, void* o,
+                const int64_t* o_stride, float* lse, const int32_t* pos, int B, int H, int T,
+                int D, const int32_t* indptr, const int32_t* indices, const uint8_t* kind,
+                int nblocks, int64_t nnzb, int block, int max_row, const smat_pattern_t* pattern,
+                float scale, float* workspace, int64_t workspace_floats, int32_t* err_word,
+                void* stream) {
+  if (dtype != SMAT_DTYPE_BF16) return SMAT_ERR_UNSUPPORTED_DTYPE;
+  if (D != 64 && D != 128) return SMAT_ERR_UNSUPPORTED_D;
+  if (B < 1 || H < 1 || T < 1 || block < 1 || nblocks != (T + block - 1) / block)
+    return SMAT_ERR_BAD_SHAPE;
+  if (!q || !k_cache || !v_cache || !o || !pos || !indptr || !kind || !workspace ||
+      !q_stride || !k_stride || !v_stride || !o_stride || (!indices && nnzb > 0))
+    return SMAT_ERR_NULL_POINTER;
+  if (nnzb < 0 || nnzb > 0x7FFFFFFF || max_row < 1) return SMAT_ERR_CSR_INVALID;
+  if (!std::isfinite(scale) || scale <= 0.f) return SMAT_ERR_BAD_SHAPE;
+  const int64_t* strides[4] = {q_stride, k_stride, v_stride, o_stride};
+  const void* ptrs[4] = {q, k_cache, v_cache, o};
+  for (int i = 0; i < 4; ++i) {
+    const int ns = (i == 0 || i == 3) ? 2 : 3;
+    for (int j = 0; j < ns; ++j)
+      if (strides[i][j] < 0) return SMAT_ERR_BAD_STRIDE;
+    if (i != 3) {
+      for (int j = 0; j < ns; ++j)
+        if (strides[i][j] % 8) return SMAT_ERR_BAD_ALIGNMENT;
+      if (!aligned16(ptrs[i])) return SMAT_ERR_BAD_ALIGNMENT;
+    }
+  }
+  DecodeParams p{};
+  if (pattern) {
+    const smat_pattern_t* pt = pattern;
+    if (pt->family != SMAT_FAMILY_GEOMETRIC && pt->family != SMAT_FAMILY_ENDPOINT)
+      return SMAT_ERR_BAD_PATTERN;
+    if (pt->n_P < 0 || pt->n < pt->n_P || pt->n > T || pt->B < 1 || pt->N0 < 1 ||
+        static_cast<int64_t>(pt->row_words) < (static_cast<int64_t>(pt->N0) + 63) / 32 ||
+        static_cast<int64_t>(pt->col_words) < (static_cast<int64_t>(pt->B) + 63) / 32 ||
+        (pt->family == SMAT_FAMILY_ENDPOINT && pt->N0 < pt->n - pt->n_P))
+      return SMAT_ERR_BAD_PATTERN;
+    if (!pt->row_bits || !pt->col_bits) return SMAT_ERR_NULL_POINTER;
+    p.md = MdPattern{pt->row_bits, pt->col_bits, pt->family, pt->n,        pt->n_P,
+                     pt->B,        pt->N0,       pt->row_words, pt->col_words};
+  }
+  const int ns = n_splits(B, H, max_row);
+  if (workspace_floats < static_cast<int64_t>(B) * H * ns * (D + 2)) return SMAT_ERR_CAPACITY;
+  p.q = static_cast<const __nv_bfloat16*>(q);
+  p.k = static_cast<const __nv_bfloat16*>(k_cache);
+  p.v = static_cast<const __nv_bfloat16*>(v_cache);
+  p.o = static_cast<__nv_bfloat16*>(o);
+  p.lse = lse;
+  p.pos = pos;
+  p.indptr = indptr;
+  p.indices = indices;
+  p.kind = kind;
+  p.part = workspace;
+  p.q_sb = q_stride[0];
+  p.q_sh = q_stride[1];
+  p.k_sb = k_stride[0];
+  p.k_sh = k_stride[1];
+  p.k_st = k_stride[2];
+  p.v_sb = v_stride[0];
+  p.v_sh = v_stride[1];
+  p.v_st = v_stride[2];
+  p.o_sb = o_stride[0];
+  p.o_sh = o_stride[1];
+  p.B = B;
+  p.H = H;
+  p.T = T;
+  p.nblocks = nblocks;
+  p.nnzb = static_cast<int>(nnzb);
+  p.bs = block;
+  p.n_split = ns;
+  p.bps = (max_row + ns - 1) / ns;
+  p.scale_log2 = scale * 1.4426950408889634f;
+  p.err = err_word;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const dim3 grid(static_cast<unsigned>(B * H), static_cast<unsigned>(ns));
+  if (D == 64) {
+    decode_partial_kernel<64><<<grid, 128, 0, s>>>(p);
+    decode_combine_kernel<64><<<B * H, 64, 0, s>>>(p);
+  } else {
+    decode_partial_kernel<128><<<grid, 128, 0, s>>>(p);
+    decode_combine_kernel<128><<<B * H, 128, 0, s>>>(p);
+  }
+  return status();
+}
+
+}  // extern "C"

@@ -342,7 +342,7 @@ int bwd_tc(const TArg& r0, const TArg& r1, const TArg& c0, const TArg& c1, const
 // ====================================================================== C ABI
 extern "C" {
 
-int smat_abi_version(void) { return 3; }
+int smat_abi_version(void) { return 4; }
 
 const char* smat_status_string(int status) {
   switch (status) {
