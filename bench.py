@@ -54,6 +54,8 @@ WORKLOADS = {
                seed=4),
     # LM training step, batch 8 x 8192 per rank
     "c4": dict(name="c4", B=8, seed=3),
+    # decode over a c3-shaped KV cache
+    "decode": dict(name="decode", seed=2),
     # the reference's own mask family on the c3 shapes: M^(3) at chunk 128
     # (n = 8192 landmarks, C 552 x 529), tiled by 128 as a pattern layout
     "md3": dict(name="md3", B=4, H=32, T=16384, D=128, block=128, d=3, chunk=128, seed=2),
@@ -546,6 +548,89 @@ def run_lm(args):
         dist.destroy_process_group()
 
 
+def run_decode(args):
+    """Decode on the c3 shapes: every (batch, head) row attends from the last
+    position (t = T - 1, the longest CSR row) over a KV cache of the whole
+    sequence; L2 is flushed (a 256 MiB read) between timed steps.  Algorithmic
+    bytes per step: the visible keys and values (2 D bytes each, bf16) plus q
+    and o."""
+    from smat_attention_b200.attention import check_device_errors
+    from smat_attention_b200.decode import decode_attention
+    from smat_attention_b200.mask import build_block_mask
+    dist, rank, ws, local = _dist()
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    w = WORKLOADS["c3"]
+    B, H, T, D = w["B"], w["H"], w["T"], w["D"]
+    spec = build_block_mask(T, w["block"], w["window"], w["stride"], w["sinks"])
+    g = torch.Generator().manual_seed(w["seed"] + rank)
+    k = torch.randn(B, H, T, D, generator=g).to(device, torch.bfloat16)
+    v = torch.randn(B, H, T, D, generator=g).to(device, torch.bfloat16)
+    q = torch.randn(B, H, D, generator=g).to(device, torch.bfloat16)
+    pos = torch.full((B,), T - 1, dtype=torch.int32, device=device)
+    qb = (T - 1) // w["block"]
+    row = spec.indices[spec.indptr[qb]:spec.indptr[qb + 1]]
+    keys = sum(min(w["block"], T - int(kb) * w["block"]) for kb in row)
+    nbytes = B * H * (keys * 2 * D * 2 + 2 * D * 2)
+    # read-only flush: a 256 MiB read evicts the cache's contents without
+    # leaving dirty lines whose write-back would land inside the timed step
+    flush = torch.ones(64 << 20, dtype=torch.float32, device=device)
+    sink = torch.empty((), dtype=torch.float32, device=device)
+    stream = torch.cuda.current_stream(device)
+    for _ in range(max(3, args.warmup)):
+        decode_attention(q, k, v, pos, spec)
+    _barrier(dist, device)
+    K = max(args.steps, 10)
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+          for _ in range(K)]
+    clocks = ClockSampler(device)
+    for i in range(K):
+        torch.sum(flush, 0, out=sink)
+        ev[i][0].record(stream)
+        o, _ = decode_attention(q, k, v, pos, spec)
+        ev[i][1].record(stream)
+    torch.cuda.synchronize(device)
+    clk = clocks.stop()
+    ms = sorted(a.elapsed_time(b) for a, b in ev)
+    ms_step = _max_over_ranks(dist, statistics.median(ms), device)
+    # end to end: q from pinned host memory in, o out, every step
+    qh = q.cpu().pin_memory()
+    oh = torch.empty(B, H, D, dtype=torch.bfloat16).pin_memory()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(K):
+        o, _ = decode_attention(qh.to(device, non_blocking=True), k, v, pos, spec)
+        oh.copy_(o, non_blocking=True)
+    e1.record(stream)
+    torch.cuda.synchronize(device)
+    e2e_ms = _max_over_ranks(dist, e0.elapsed_time(e1) / K, device)
+    dev_err = check_device_errors(device)
+    if rank == 0:
+        peaks = _peaks()
+        gbs = nbytes / (ms_step * 1e-3) / 1e9
+        line = {
+            "metric": "decode tokens/s (one query per sequence, c3 shapes)",
+            "value": ws * B / (ms_step * 1e-3), "unit": "tokens/s", "n_gpus": ws, "steps": K,
+            "warmup": max(3, args.warmup), "ms_per_step": ms_step, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": f"decode at t = T - 1 over a KV cache: B={B} H={H} T={T} "
+                                   f"D={D} bs={w['block']} W={w['window']} S={w['stride']} "
+                                   f"sinks={w['sinks']} ({len(row)} blocks, {keys} keys)",
+                       "global_batch": B * ws, "seq_len": T,
+                       "parallelism": f"(batch) partition x{ws}",
+                       "l2": "flushed (256 MiB read) between timed steps"},
+            "roofline": {"bound": "hbm", "kernel": "decode_partial", "achieved": gbs,
+                         "peak": peaks["hbm"], "unit": "GB/s", "frac": gbs / peaks["hbm"],
+                         "traffic": None, "algorithmic_bytes": nbytes},
+            "e2e": {"value": ws * B / (e2e_ms * 1e-3), "unit": "tokens/s", "ms_per_step": e2e_ms,
+                    "h2d_bytes_per_step": B * H * D * 2, "d2h_bytes_per_step": B * H * D * 2},
+            "gpu_launches": 2 * K, "device_errors": dev_err, "clocks": clk,
+        }
+        print(json.dumps(line), flush=True)
+    if dist is not None:
+        dist.destroy_process_group()
+
+
 def _lm_pairs(cfg):
     from smat_attention_b200.mask import block_layout_stats
     return block_layout_stats(cfg.mask())["pairs"]
@@ -669,15 +754,18 @@ def main():
         WORKLOAD["B"] = args.batch
     if args.heads:
         WORKLOAD["H"] = args.heads
-    if args.workload == "c4":
+    if args.workload in ("c4", "decode"):
         args.no_cpu_baseline = True
-    if args.impl == "reference" and args.workload != "c4":
+    if args.impl == "reference" and args.workload not in ("c4", "decode"):
         run_reference(args)
     elif args.impl == "reference":
         print(json.dumps({"impl": "reference", "unavailable": "the reference arm times the "
-                          "dense-masked attention on host cores; c4 is a GPU training step"}))
+                          "dense-masked attention step on host cores; this workload has no "
+                          "CPU counterpart there"}))
     elif args.workload == "c4":
         run_lm(args)
+    elif args.workload == "decode":
+        run_decode(args)
     elif args.workload == "c5" and args.shard == "queries":
         run_sharded(args)
     else:

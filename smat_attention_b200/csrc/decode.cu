@@ -7,8 +7,9 @@
 //   partial  grid (B H, n_split), 128 threads.  Split s walks entries
 //            [s bps, (s + 1) bps) of the query's CSR row.  A key is owned by
 //            a group of D / 8 lanes (16-byte vectors, a 256-byte row read by
-//            16 lanes at D = 128), each warp handling 32 / (D / 8) keys per
-//            step; the dot product is reduced inside the group and each
+//            16 lanes at D = 128), each warp handling 4 x 32 / (D / 8) keys
+//            per step with all their loads issued first (values only for
+//            visible keys); the dot product is reduced inside the group and each
 //            group keeps an online softmax (max, sum, D / 8 x 8 outputs).
 //            Groups and warps are merged at the end into one partial
 //            (m, l, o[D]) per split, in base-2 exponent units.
@@ -78,7 +79,8 @@ __device__ __forceinline__ void merge_state(float& m, float& l, float* o, float 
 template <int D>
 __global__ void __launch_bounds__(128) decode_partial_kernel(const DecodeParams p) {
   constexpr int G = D / 8;        // lanes per key
-  constexpr int KPW = 32 / G;     // keys per warp step
+  constexpr int KPW = 32 / G;     // keys per warp and unrolled step
+  constexpr int U = 4;            // unrolled steps
   __shared__ float red_m[4][KPW], red_l[4][KPW];
   __shared__ float red_o[4][D];
   const int bh = blockIdx.x, split = blockIdx.y;
@@ -115,41 +117,58 @@ __global__ void __launch_bounds__(128) decode_partial_kernel(const DecodeParams 
   const __nv_bfloat16* kbase = p.k + b * p.k_sb + h * p.k_sh + part * 8;
   const __nv_bfloat16* vbase = p.v + b * p.v_sb + h * p.v_sh + part * 8;
 
-  for (int e = e0; e < e1; ++e) {
+  // The row's keys as one sequence of steps: step k covers entry
+  // e0 + k / SPB, keys (k % SPB) STEP + warp KPW U + u KPW + slot of it.  The
+  // loads of step k + 1 are issued before the arithmetic of step k (two
+  // register buffers), so every warp keeps loads in flight while it computes.
+  constexpr int STEP = 4 * KPW * U;             // keys per CTA step
+  const int spb = (p.bs + STEP - 1) / STEP;     // steps per block
+  const int nsteps = (e1 - e0) * spb;
+  V8 kr[2][U], vr[2][U];
+  bool vis[2][U];
+  auto issue = [&](int k, int buf) {
+    const int e = e0 + k / spb;
     const int kb = __ldg(p.indices + e);
     const uint8_t kd = __ldg(p.kind + e);
-    if (kb < 0 || kb >= p.nblocks || kb * p.bs > t) {
-      if (threadIdx.x == 0 && p.err) atomicOr(p.err, DEV_ERR_BAD_CSR);
-      continue;
-    }
-    const int j0 = kb * p.bs;
-    const int jn = min(p.bs, p.T - j0);
-    // warp-uniform trip count: every lane of a group takes part in its shuffles
-    for (int base = warp * KPW; base < jn; base += 4 * KPW) {
-      const int jj = base + slot;
+    const bool ok = kb >= 0 && kb < p.nblocks && kb * p.bs <= t;
+    if (!ok && threadIdx.x == 0 && p.err) atomicOr(p.err, DEV_ERR_BAD_CSR);
+    const int j0 = ok ? kb * p.bs : 0;
+    const int jn = ok ? min(p.bs, p.T - j0) : 0;
+    const int base = (k % spb) * STEP + warp * KPW * U;
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int jj = base + u * KPW + slot;
       const bool in = jj < jn;
       const int j = j0 + (in ? jj : 0);
+      bool vs = in;
+      if (kd == 1) {
+        vs = vs && j <= t;
+      } else if (kd == 2) {
+        if (p.md.row_bits) {
+          vs = vs && ((md_row_word(p.md, p.T, t, j & ~31) >> (j & 31)) & 1u);
+        } else {
+          vs = false;
+          if (part == 0 && p.err) atomicOr(p.err, DEV_ERR_BAD_CSR);
+        }
+      }
+      vis[buf][u] = vs;
+      kr[buf][u] = *reinterpret_cast<const V8*>(kbase + static_cast<int64_t>(j) * p.k_st);
+      if (vs) vr[buf][u] = *reinterpret_cast<const V8*>(vbase + static_cast<int64_t>(j) * p.v_st);
+    }
+  };
+  auto consume = [&](int buf) {
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
       float kv[8];
-      unpack8(*reinterpret_cast<const V8*>(kbase + static_cast<int64_t>(j) * p.k_st), kv);
+      unpack8(kr[buf][u], kv);
       float s = 0.f;
 #pragma unroll
       for (int i = 0; i < 8; ++i) s = fmaf(qv[i], kv[i], s);
 #pragma unroll
       for (int off = G / 2; off > 0; off >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
-      bool vis = in;
-      if (kd == 1) {
-        vis = vis && j <= t;
-      } else if (kd == 2) {
-        if (p.md.row_bits) {
-          vis = vis && ((md_row_word(p.md, p.T, t, j & ~31) >> (j & 31)) & 1u);
-        } else {
-          vis = false;
-          if (part == 0 && p.err) atomicOr(p.err, DEV_ERR_BAD_CSR);
-        }
-      }
-      if (!vis) continue;
+      if (!vis[buf][u]) continue;
       float vv[8];
-      unpack8(*reinterpret_cast<const V8*>(vbase + static_cast<int64_t>(j) * p.v_st), vv);
+      unpack8(vr[buf][u], vv);
       if (s > m) {
         const float a = exp2f(m - s);   // 0 when m is still -inf
         l *= a;
@@ -161,6 +180,16 @@ __global__ void __launch_bounds__(128) decode_partial_kernel(const DecodeParams 
       l += pr;
 #pragma unroll
       for (int i = 0; i < 8; ++i) o[i] = fmaf(pr, vv[i], o[i]);
+    }
+  };
+  // buffers are named by constants (a runtime index would move them to the stack)
+  if (nsteps > 0) issue(0, 0);
+  for (int k = 0; k < nsteps; k += 2) {
+    if (k + 1 < nsteps) issue(k + 1, 1);
+    consume(0);
+    if (k + 1 < nsteps) {
+      if (k + 2 < nsteps) issue(k + 2, 0);
+      consume(1);
     }
   }
 
@@ -201,10 +230,20 @@ __global__ void __launch_bounds__(D) decode_combine_kernel(const DecodeParams p)
   const int bh = blockIdx.x, d = threadIdx.x;
   const int b = bh / p.H, h = bh % p.H;
   const float* in = p.part + static_cast<int64_t>(bh) * p.n_split * (D + 2);
-  float M = -INFINITY, L = 0.f, O = 0.f;
-  for (int s = 0; s < p.n_split; ++s) {
-    const float* ps = in + s * (D + 2);
-    merge_state<1>(M, L, &O, ps[0], ps[1], &ps[2 + d]);
+  // two passes with independent loads (the maxima, then the rescaled sums), so
+  // the loads of all splits are in flight together
+  float M = -INFINITY;
+#pragma unroll 8
+  for (int s = 0; s < p.n_split; ++s) M = fmaxf(M, in[s * (D + 2)]);
+  float L = 0.f, O = 0.f;
+  if (M != -INFINITY) {
+#pragma unroll 8
+    for (int s = 0; s < p.n_split; ++s) {
+      const float* ps = in + s * (D + 2);
+      const float w = exp2f(ps[0] - M);   // 0 for an empty split (m = -inf)
+      L = fmaf(ps[1], w, L);
+      O = fmaf(ps[2 + d], w, O);
+    }
   }
   const float r = L > 0.f ? O / L : 0.f;
   p.o[b * p.o_sb + h * p.o_sh + d] = __float2bfloat16_rn(r);
@@ -214,12 +253,19 @@ __global__ void __launch_bounds__(D) decode_combine_kernel(const DecodeParams p)
 
 int status() { return cudaGetLastError() == cudaSuccess ? SMAT_OK : SMAT_ERR_LAUNCH; }
 
-// splits per (b, h): enough CTAs for about four per SM, at most one entry each
-int n_splits(int B, int H, int max_row) {
+// splits per (b, h) and entries per split: about four waves of CTAs (four
+// resident per SM at 128 registers), so the last wave's tail is short; the
+// split count is then trimmed so that no split is empty
+int entries_per_split(int B, int H, int max_row) {
   const int64_t bh = static_cast<int64_t>(B) * H;
-  int64_t s = (592 + bh - 1) / bh;
+  int64_t s = (4 * 592 + bh - 1) / bh;
   if (s > max_row) s = max_row;
-  return static_cast<int>(s < 1 ? 1 : s);
+  if (s < 1) s = 1;
+  return static_cast<int>((max_row + s - 1) / s);
+}
+int n_splits(int B, int H, int max_row) {
+  const int bps = entries_per_split(B, H, max_row);
+  return max_row < 1 ? 1 : (max_row + bps - 1) / bps;
 }
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
@@ -306,7 +352,7 @@ int smat_decode(int dtype, const void* q, const int64_t* q_stride, const void* k
   p.nnzb = static_cast<int>(nnzb);
   p.bs = block;
   p.n_split = ns;
-  p.bps = (max_row + ns - 1) / ns;
+  p.bps = entries_per_split(B, H, max_row);
   p.scale_log2 = scale * 1.4426950408889634f;
   p.err = err_word;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
