@@ -21,6 +21,11 @@ It imports the reference's ``smat`` package (``src/smat``) and records
     attention.  Gradients come from torch autograd through that call.  Inputs
     are fp32-representable values; outputs are fp64.
 
+``kattn_<case>.npz``
+    The reference's kernelised op ``smat_attention`` on its torch path (fp64)
+    for ``M^(d)`` masks: inputs, output, autograd gradients and the pooled
+    intermediates ``F`` (profiles) and ``U`` (per row type), the latter two as fp32.
+
 Nothing at test time imports the reference: the tests read only these files.
 """
 
@@ -112,6 +117,44 @@ def make_softmax(A, R, name, T, BH, D, mask, seed):
         dv=vg.grad.numpy())
 
 
+# (name, T, d, chunk, n_P, nb, r, d_v)
+KATTN_CASES = [
+    ("geo3_t512_c64", 512, 3, 64, 0, 2, 16, 8),
+    ("geo3_t1024_c128_np16", 1024, 3, 128, 16, 2, 32, 16),
+    ("geo2_t512_c64", 512, 2, 64, 0, 1, 16, 8),
+    ("endpoint_t1024_c64", 1024, 10, 64, 0, 1, 16, 8),
+]
+
+
+def make_kattn(A, R, name, T, d, chunk, n_P, nb, r, dv, seed):
+    """The reference's kernelised op ``smat_attention`` (``src/smat/attention.py:391-455``)
+    on its torch path in fp64, with autograd gradients, plus its pooled
+    intermediates ``F = pool_profiles`` and ``U = apply_incidence``.  Features
+    are ``elu(x) + 1`` of fp32 normals (strictly positive, as the op assumes)."""
+    g = torch.Generator().manual_seed(seed)
+    xq, xk = (torch.randn(nb, T, r, generator=g, dtype=torch.float32) for _ in range(2))
+    v = torch.randn(nb, T, dv, generator=g, dtype=torch.float32)
+    dout = torch.randn(nb, T, dv, generator=g, dtype=torch.float32)
+    Phi = (torch.nn.functional.elu(xq.double()) + 1).float().double()
+    Psi = (torch.nn.functional.elu(xk.double()) + 1).float().double()
+    spec = R.build_mask(T, d, chunk=chunk, n_P=n_P)
+    A.to_device(spec, "cpu")
+    Pg, Sg, Vg = (x.clone().requires_grad_(True) for x in (Phi, Psi, v.double()))
+    Vb = torch.cat([Vg, torch.ones(nb, T, 1, dtype=torch.float64)], dim=-1)
+    out = A.smat_attention(Pg, Sg, Vb, spec, chunk=chunk, scan_backend="torch",
+                           incidence_backend="torch")
+    (out * dout.double()).sum().backward()
+    with torch.no_grad():
+        Vb0 = torch.cat([v.double(), torch.ones(nb, T, 1, dtype=torch.float64)], dim=-1)
+        F = A.pool_profiles(Psi, Vb0, spec, backend="torch")
+        U = A.apply_incidence(F, spec, backend="torch")
+    np.savez_compressed(
+        os.path.join(HERE, f"kattn_{name}.npz"),
+        args=np.array([T, d, chunk, n_P]), phi=Phi.float().numpy(), psi=Psi.float().numpy(),
+        v=v.numpy(), dout=dout.numpy(), out=out.detach().numpy(), dphi=Pg.grad.numpy(),
+        dpsi=Sg.grad.numpy(), dv=Vg.grad.numpy(), F=F.float().numpy(), U=U.float().numpy())
+
+
 def main():
     ref = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("SMAT_REFERENCE")
     if not ref:
@@ -122,6 +165,8 @@ def main():
     make_mask_md(R)
     for i, (name, T, BH, D, mask) in enumerate(SOFTMAX_CASES):
         make_softmax(A, R, name, T, BH, D, mask, seed=100 + i)
+    for i, case in enumerate(KATTN_CASES):
+        make_kattn(A, R, *case, seed=200 + i)
     print("fixtures written to", HERE)
 
 

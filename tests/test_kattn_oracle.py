@@ -1,0 +1,51 @@
+"""The kernelised-attention oracle (oracle/kernel_attention.py) against the
+reference's own torch path (tests/golden/kattn_*.npz, written by
+tests/golden/make_golden.py from src/smat/attention.py:391-455 in fp64):
+output, gradients (torch autograd through the oracle), and the pooled
+intermediates F and U."""
+
+import glob
+import os
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import kernel_attention as OK
+from smat_attention_b200.mask import build_mask
+
+CASES = sorted(glob.glob(os.path.join(os.path.dirname(__file__), "golden", "kattn_*.npz")))
+
+
+@pytest.mark.parametrize("path", CASES, ids=[os.path.basename(c)[6:-4] for c in CASES])
+def test_oracle_matches_reference(path):
+    f = np.load(path)
+    T, d, chunk, n_P = (int(x) for x in f["args"])
+    spec = build_mask(T, d, chunk=chunk, n_P=n_P)
+    phi, psi, v = (torch.from_numpy(f[k]).double().requires_grad_(True)
+                   for k in ("phi", "psi", "v"))
+    Vb = torch.cat([v, torch.ones(*v.shape[:-1], 1, dtype=torch.float64)], dim=-1)
+    out = OK.smat_attention(phi, psi, Vb, spec, chunk=chunk)
+    assert np.abs(out.detach().numpy() - f["out"]).max() < 1e-11
+    (out * torch.from_numpy(f["dout"]).double()).sum().backward()
+    for g, k in ((phi.grad, "dphi"), (psi.grad, "dpsi"), (v.grad, "dv")):
+        ref = f[k]
+        assert np.abs(g.numpy() - ref).max() <= 1e-10 * (1 + np.abs(ref).max()), k
+    with torch.no_grad():
+        Vb0 = torch.cat([v.detach(), torch.ones(*v.shape[:-1], 1, dtype=torch.float64)], -1)
+        F = OK.pool_profiles(psi.detach(), Vb0, spec)
+        U = OK.apply_incidence(F, spec)
+    assert np.abs(F.numpy() - f["F"]).max() <= 1e-5 * (1 + np.abs(f["F"]).max())
+    assert np.abs(U.numpy() - f["U"]).max() <= 1e-5 * (1 + np.abs(f["U"]).max())
+
+
+def test_chunk_local_definition():
+    g = torch.Generator().manual_seed(0)
+    Phi, Psi = (torch.rand(1, 2, 8, 3, generator=g, dtype=torch.float64) for _ in range(2))
+    Vb = torch.rand(1, 2, 8, 4, generator=g, dtype=torch.float64)
+    Sin = torch.rand(1, 2, 3, 4, generator=g, dtype=torch.float64)
+    out = OK.chunk_local(Phi, Psi, Vb, Sin)
+    i, c = 5, 1
+    want = Phi[0, c, i] @ Sin[0, c] + sum((Phi[0, c, i] @ Psi[0, c, j]) * Vb[0, c, j]
+                                          for j in range(i + 1))
+    assert torch.allclose(out[0, c, i], want)
