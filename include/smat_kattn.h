@@ -1,0 +1,58 @@
+/*
+ * smat_kattn.h -- the reference's kernelised-attention schedule on B200
+ * (libsmat_b200.so, beside the softmax ABI of smat_b200.h).
+ *
+ * The reference computes smat_attention(Phi, Psi, Vb, spec) (src/smat/
+ * attention.py:391-455) from three fused passes that its Triton module exports
+ * (src/smat/kernels/triton_fwd.py:49-311, triton_bwd.py:50-312); these entry
+ * points are their counterparts.  All tensors are fp32, contiguous, device
+ * memory; statuses are those of smat_b200.h; kernels are enqueued on
+ * `stream`.
+ */
+#ifndef SMAT_KATTN_H_
+#define SMAT_KATTN_H_
+
+#include <stdint.h>
+
+#include "smat_b200.h"
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* out[b] = phi[b] sin[b] + tril(phi[b] psi[b]^T) vb[b] for every chunk b
+ * (chunk_local, triton_fwd.py:49-152): phi, psi [n_chunks, C, R], vb, out
+ * [n_chunks, C, P], sin [n_chunks, R, P].  tcgen05 kind::tf32 (TF32 inputs,
+ * fp32 accumulation, the reference's allow_tf32 dots).  C = 128, R in {32, 64,
+ * 128}, 1 <= P <= 128 (<= 96 when R = 128); phi and psi 16-byte aligned. */
+SMAT_API int smat_kattn_chunk_local_fwd(const float* phi, const float* psi, const float* vb,
+                               const float* sin_, float* out, int64_t n_chunks, int C,
+                               int R, int P, int32_t* err_word, void* stream);
+
+/* F[b, x] = sum_{j in [n_P, n), (j - n_P) mod N0 = x} psi[b, j] vb[b, j]^T
+ * (pool, triton_fwd.py:225-311): psi [nb, T, R], vb [nb, T, P], F [nb, N0, R, P];
+ * R * P <= 16384, 32 (R + P) floats of staging <= 96 KB.  Exact fp32 FMAs. */
+SMAT_API int smat_kattn_pool_fwd(const float* psi, const float* vb, float* F, int nb, int T,
+                        int R, int P, int n_P, int n, int N0, void* stream);
+
+/* Its backward (triton_bwd.py:203-278): for every column j of profile x,
+ * dpsi[b, j] = dF[b, x] vb[b, j], dvb[b, j] = dF[b, x]^T psi[b, j]; rows outside
+ * [n_P, n) are not written (the caller zeroes them). */
+SMAT_API int smat_kattn_pool_bwd(const float* psi, const float* vb, const float* dF,
+                        float* dpsi, float* dvb, int nb, int T, int R, int P, int n_P,
+                        int n, int N0, void* stream);
+
+/* U[b, h] = sum_{e in [ptr[h], ptr[h+1])} F[b, idx[e]] over rows of RP floats
+ * (incidence, triton_fwd.py:161-222): F [nb, N_in, RP], U [nb, N_out, RP],
+ * ptr (int64, N_out + 1) and idx (int32) a CSR in device memory.  With the
+ * transposed CSR it is its own backward (triton_bwd.py:281-316).  An index
+ * outside [0, N_in) sets SMAT_DEVERR_BAD_CSR and is skipped. */
+SMAT_API int smat_kattn_incidence(const float* F, const int64_t* ptr, const int32_t* idx,
+                         float* U, int nb, int N_in, int N_out, int RP,
+                         int32_t* err_word, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* SMAT_KATTN_H_ */

@@ -18,7 +18,7 @@ PKG = os.path.dirname(os.path.abspath(__file__))
 ROOT = os.path.dirname(PKG)
 CSRC = os.path.join(PKG, "csrc")
 LIB = os.path.join(PKG, "libsmat_b200.so")
-SOURCES = ["smat_abi.cu", "noalloc.cu", "rows.cu", "lm_ops.cu", "decode.cu"]
+SOURCES = ["smat_abi.cu", "noalloc.cu", "rows.cu", "lm_ops.cu", "decode.cu", "kattn.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 
@@ -34,6 +34,7 @@ def _inputs():
              if f.endswith((".cu", ".cuh", ".h"))]
     files.append(os.path.join(ROOT, "include", "smat_b200.h"))
     files.append(os.path.join(ROOT, "include", "smat_lm.h"))
+    files.append(os.path.join(ROOT, "include", "smat_kattn.h"))
     files.append(os.path.abspath(__file__))
     return files
 

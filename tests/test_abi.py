@@ -154,3 +154,18 @@ def test_lm_ops_reject_on_host():
     assert L.smat_lm_swiglu_bwd(16, 16, 8, 4, 16, None) == 6
     assert L.smat_lm_cross_entropy(16, 16, 16, 4, 1001, 1.0, None, None) == 1
     assert L.smat_lm_cross_entropy(16, None, 16, 4, 1000, 1.0, None, None) == 8
+
+
+def test_kattn_header_symbols_exported():
+    from smat_attention_b200 import kernel_attention as KA
+    text = open(os.path.join(os.path.dirname(HEADER), "smat_kattn.h")).read()
+    syms = sorted(set(re.findall(r"SMAT_API\s+\w+\**\s+\**(smat_\w+)\s*\(", text)))
+    assert len(syms) == 4 and set(syms) == set(KA.SIGNATURES)
+    L = KA._L()
+    assert L.smat_kattn_chunk_local_fwd(16, 16, 16, 16, 16, 1, 64, 64, 65, None, None) == 1
+    assert L.smat_kattn_chunk_local_fwd(16, 16, 16, 16, 16, 1, 128, 48, 65, None, None) == 1
+    assert L.smat_kattn_chunk_local_fwd(16, 16, 16, 16, 16, 1, 128, 128, 128, None, None) == 1
+    assert L.smat_kattn_chunk_local_fwd(8, 16, 16, 16, 16, 1, 128, 64, 65, None, None) == 6
+    assert L.smat_kattn_chunk_local_fwd(None, 16, 16, 16, 16, 1, 128, 64, 65, None, None) == 8
+    assert L.smat_kattn_pool_fwd(16, 16, 16, 1, 100, 64, 65, 0, 200, 7, None) == 1
+    assert L.smat_kattn_incidence(16, 16, 16, 16, 0, 4, 4, 8, None, None) == 1

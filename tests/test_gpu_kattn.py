@@ -1,0 +1,139 @@
+"""GPU parity of the kernelised-attention kernels (include/smat_kattn.h)
+against the oracle (oracle/kernel_attention.py, itself pinned to the
+reference's torch path by tests/test_kattn_oracle.py).
+
+Tolerances: the chunk-local forward runs TF32 tensor cores, as the reference's
+Triton kernel does (allow_tf32), and is held to 2e-3 of each tensor's largest
+entry -- the reference's own fp32 kernel-vs-torch bound
+(tests/test_smat.py:390); everything else is fp32 arithmetic, held to 1e-5
+relative (pool, incidence) or 1e-4 (the library-GEMM backward of the chunk
+pass, whose inputs come from the TF32 forward only through dout)."""
+
+import glob
+import os
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import kernel_attention as OK
+from smat_attention_b200 import kernel_attention as KA
+from smat_attention_b200.attention import check_device_errors
+from smat_attention_b200.mask import build_mask
+
+pytestmark = pytest.mark.gpu
+
+
+def _close(got, ref, rel, name):
+    scale = ref.abs().max().item() + 1e-30
+    err = (got.double().cpu() - ref.double().cpu()).abs().max().item()
+    print(f"{name}: max err {err:.3e} (scale {scale:.3e})")
+    assert err <= rel * scale, (name, err, scale)
+
+
+def _feat(*shape, g):
+    return torch.nn.functional.elu(torch.randn(*shape, generator=g, dtype=torch.float64)) + 1
+
+
+@pytest.mark.parametrize("R,P", [(32, 9), (64, 65), (64, 17), (128, 96), (32, 128)])
+def test_chunk_local(cuda_device, R, P):
+    g = torch.Generator().manual_seed(R + P)
+    nb, nc, C = 2, 3, 128
+    Phi, Psi = _feat(nb, nc, C, R, g=g), _feat(nb, nc, C, R, g=g)
+    Vb = torch.randn(nb, nc, C, P, generator=g, dtype=torch.float64)
+    Sin = torch.rand(nb, nc, R, P, generator=g, dtype=torch.float64) * 10
+    dout = torch.randn(nb, nc, C, P, generator=g, dtype=torch.float64)
+    ins = [x.float().to(cuda_device).requires_grad_(True) for x in (Phi, Psi, Vb, Sin)]
+    out = KA.chunk_local(*ins)
+    (out * dout.float().to(cuda_device)).sum().backward()
+    torch.cuda.synchronize()
+    assert check_device_errors() == 0
+    ref_in = [x.float().double().requires_grad_(True) for x in (Phi, Psi, Vb, Sin)]
+    ref = OK.chunk_local(*ref_in)
+    (ref * dout.float().double()).sum().backward()
+    _close(out, ref.detach(), 2e-3, "out")
+    for a, b, n in zip(ins, ref_in, ("dphi", "dpsi", "dvb", "dsin")):
+        _close(a.grad, b.grad, 1e-4, n)
+
+
+@pytest.mark.parametrize("T,d,n_P,R,P", [(1024, 3, 0, 64, 65), (2048, 3, 16, 32, 17),
+                                          (512, 2, 0, 16, 9), (1000, 3, 0, 64, 65)])
+def test_pool_and_incidence(cuda_device, T, d, n_P, R, P):
+    spec = build_mask(T, d, chunk=8, n_P=n_P)
+    g = torch.Generator().manual_seed(T + d)
+    nb = 2
+    Psi = _feat(nb, T, R, g=g).float().double()
+    Vb = torch.randn(nb, T, P, generator=g, dtype=torch.float32).double()
+    dF = torch.randn(nb, spec.N0, R, P, generator=g, dtype=torch.float32).double()
+    dU = torch.randn(nb, spec.B, R, P, generator=g, dtype=torch.float32).double()
+    k = Psi.float().to(cuda_device).requires_grad_(True)
+    v = Vb.float().to(cuda_device).requires_grad_(True)
+    F = KA.pool_profiles(k, v, spec)
+    (F * dF.float().to(cuda_device)).sum().backward()
+    rk, rv = Psi.clone().requires_grad_(True), Vb.clone().requires_grad_(True)
+    rF = OK.pool_profiles(rk, rv, spec)
+    (rF * dF).sum().backward()
+    _close(F, rF.detach(), 1e-5, "F")
+    _close(k.grad, rk.grad, 1e-5, "dpsi")
+    _close(v.grad, rv.grad, 1e-5, "dvb")
+    Fg = rF.detach().float().to(cuda_device).requires_grad_(True)
+    U = KA.apply_incidence(Fg, spec)
+    (U * dU.float().to(cuda_device)).sum().backward()
+    rFg = rF.detach().float().double().requires_grad_(True)
+    rU = OK.apply_incidence(rFg, spec)
+    (rU * dU).sum().backward()
+    _close(U, rU.detach(), 1e-5, "U")
+    _close(Fg.grad, rFg.grad, 1e-5, "dF")
+    torch.cuda.synchronize()
+    assert check_device_errors() == 0
+
+
+def _run_op(spec, Phi, Psi, v, dout, device, chunk=128):
+    ins = [x.float().to(device).requires_grad_(True) for x in (Phi, Psi, v)]
+    Vb = torch.cat([ins[2], torch.ones(*v.shape[:-1], 1, device=device)], dim=-1)
+    out = KA.smat_attention(ins[0], ins[1], Vb, spec, chunk=chunk)
+    (out * dout.float().to(device)).sum().backward()
+    torch.cuda.synchronize()
+    assert check_device_errors() == 0
+    return out, [x.grad for x in ins]
+
+
+def test_op_matches_reference_fixture(cuda_device):
+    """The whole op against the reference's own fp64 outputs and gradients
+    (tests/golden/kattn_geo3_t1024_c128_np16.npz: M^(3), chunk 128, n_P 16)."""
+    path = os.path.join(os.path.dirname(__file__), "golden", "kattn_geo3_t1024_c128_np16.npz")
+    f = np.load(path)
+    T, d, chunk, n_P = (int(x) for x in f["args"])
+    spec = build_mask(T, d, chunk=chunk, n_P=n_P)
+    out, grads = _run_op(spec, *(torch.from_numpy(f[k]) for k in ("phi", "psi", "v", "dout")),
+                         cuda_device, chunk)
+    _close(out, torch.from_numpy(f["out"]), 2e-3, "out")
+    for gr, k in zip(grads, ("dphi", "dpsi", "dv")):
+        _close(gr, torch.from_numpy(f[k]), 2e-3, k)
+
+
+@pytest.mark.parametrize("T,d,r,dv", [(4096, 3, 64, 64), (1024, 10, 64, 64), (2048, 2, 32, 32)])
+def test_op_matches_oracle(cuda_device, T, d, r, dv):
+    spec = build_mask(T, d, chunk=128)
+    g = torch.Generator().manual_seed(T + d)
+    nb = 2
+    Phi, Psi = _feat(nb, T, r, g=g).float().double(), _feat(nb, T, r, g=g).float().double()
+    v = torch.randn(nb, T, dv, generator=g, dtype=torch.float32).double()
+    dout = torch.randn(nb, T, dv, generator=g, dtype=torch.float32).double()
+    out, grads = _run_op(spec, Phi, Psi, v, dout, cuda_device)
+    ref_in = [x.clone().requires_grad_(True) for x in (Phi, Psi, v)]
+    Vb = torch.cat([ref_in[2], torch.ones(nb, T, 1, dtype=torch.float64)], dim=-1)
+    ref = OK.smat_attention(ref_in[0], ref_in[1], Vb, spec, chunk=128)
+    (ref * dout).sum().backward()
+    _close(out, ref.detach(), 2e-3, "out")
+    for gr, rr, k in zip(grads, ref_in, ("dphi", "dpsi", "dv")):
+        _close(gr, rr.grad, 2e-3, k)
+
+
+def test_rejects(cuda_device):
+    x = torch.zeros(1, 1, 64, 32, device=cuda_device)
+    with pytest.raises(Exception):
+        KA.chunk_local(x, x, torch.zeros(1, 1, 64, 9, device=cuda_device),
+                       torch.zeros(1, 1, 32, 9, device=cuda_device))     # C = 64
+    with pytest.raises(ValueError):
+        KA.chunk_local(*(t.cpu() for t in (x, x, x, x)))

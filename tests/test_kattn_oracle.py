@@ -49,3 +49,28 @@ def test_chunk_local_definition():
     want = Phi[0, c, i] @ Sin[0, c] + sum((Phi[0, c, i] @ Psi[0, c, j]) * Vb[0, c, j]
                                           for j in range(i + 1))
     assert torch.allclose(out[0, c, i], want)
+
+
+def test_torch_parts_match_oracle():
+    """The product module's torch-side parts (Walsh incidence for the endpoint
+    family, the zeta butterfly, the per-type query) against the oracle, on CPU."""
+    from smat_attention_b200 import kernel_attention as KA
+    g = torch.Generator().manual_seed(3)
+    spec = build_mask(1024, 10, chunk=64)                  # endpoint, B = N0 = 512
+    F = torch.randn(2, spec.N0, 3, 4, generator=g, dtype=torch.float64)
+    assert torch.allclose(KA.walsh_incidence(F), OK.apply_incidence(F, spec), atol=1e-10)
+    Fz = torch.randn(1, 64, 2, 3, generator=g, dtype=torch.float64)
+    assert torch.allclose(KA.zeta_transform(Fz), OK.zeta_transform(Fz), atol=1e-12)
+    spec3 = build_mask(1000, 3, chunk=8)
+    Phi_rec = torch.randn(2, spec3.T_R, 5, generator=g, dtype=torch.float64)
+    U = torch.randn(2, spec3.B, 5, 6, generator=g, dtype=torch.float64)
+    assert torch.allclose(KA.query_by_type(Phi_rec, U, spec3).double(),
+                          OK.query_by_type(Phi_rec, U, spec3), atol=1e-5)
+    # the transposed CSR used by the incidence backward
+    ptr = torch.from_numpy(spec3.C_indptr)
+    idx = torch.from_numpy(spec3.C_indices)
+    t_ptr, t_idx = KA._transpose_csr(ptr, idx, spec3.N0)
+    Cd = spec3.dense_C()
+    for x in range(0, spec3.N0, 7):
+        rows = t_idx[t_ptr[x]:t_ptr[x + 1]].tolist()
+        assert rows == np.flatnonzero(Cd[:, x]).tolist()
