@@ -56,6 +56,8 @@ WORKLOADS = {
     "c4": dict(name="c4", B=8, seed=3),
     # decode over a c3-shaped KV cache
     "decode": dict(name="decode", seed=2),
+    # the reference's kernelised op (pooled schedule) on B200 kernels
+    "kattn": dict(name="kattn", seed=5),
     # the reference's own mask family on the c3 shapes: M^(3) at chunk 128
     # (n = 8192 landmarks, C 552 x 529), tiled by 128 as a pattern layout
     "md3": dict(name="md3", B=4, H=32, T=16384, D=128, block=128, d=3, chunk=128, seed=2),
@@ -631,6 +633,128 @@ def run_decode(args):
         dist.destroy_process_group()
 
 
+def _import_reference():
+    """The reference package installed under baseline/_ref (its own code,
+    unmodified), or None when it is absent."""
+    ref = os.path.join(ROOT, "baseline", "_ref")
+    if not os.path.isdir(os.path.join(ref, "smat")):
+        return None
+    if ref not in sys.path:
+        sys.path.insert(0, ref)
+    try:
+        import smat.attention as RA
+        import smat.kernels.triton_bwd as RB
+        import smat.mask as RM
+        return RA, RB, RM
+    except Exception:
+        return None
+
+
+def run_kattn(args):
+    """The reference's kernelised op (smat_attention, pooled schedule, M^(3) at
+    chunk 128) forward + backward on nb = 32 sequences of T = 16384 with r = 64
+    features and d_v = 64: ours (kernel_attention, tcgen05 TF32 chunk pass)
+    against the reference's own Triton kernels (baseline/_ref, scan and
+    incidence backends "triton", triton_bwd.patch() for the backward) on the
+    same inputs and GPU."""
+    from smat_attention_b200 import kernel_attention as KA
+    from smat_attention_b200.attention import check_device_errors
+    from smat_attention_b200.mask import build_mask
+    dist, rank, ws, local = _dist()
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    nb, T, r, dv, d = 32, 16384, 64, 64, 3
+    g = torch.Generator().manual_seed(5 + rank)
+    Phi = (torch.nn.functional.elu(torch.randn(nb, T, r, generator=g)) + 1).to(device)
+    Psi = (torch.nn.functional.elu(torch.randn(nb, T, r, generator=g)) + 1).to(device)
+    V = torch.randn(nb, T, dv, generator=g).to(device)
+    dout = torch.randn(nb, T, dv, generator=g).to(device)
+    spec = build_mask(T, d, chunk=128)
+    stream = torch.cuda.current_stream(device)
+
+    def timed(fn, K):
+        for _ in range(max(3, args.warmup)):
+            fn()
+        torch.cuda.synchronize(device)
+        ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+              for _ in range(K)]
+        for a, b in ev:
+            a.record(stream)
+            fn()
+            b.record(stream)
+        torch.cuda.synchronize(device)
+        return statistics.median(a.elapsed_time(b) for a, b in ev)
+
+    def ours(backward):
+        def fn():
+            ins = [x.requires_grad_(backward) for x in (Phi.detach(), Psi.detach(), V.detach())]
+            Vb = torch.cat([ins[2], torch.ones(nb, T, 1, device=device)], dim=-1)
+            out = KA.smat_attention(ins[0], ins[1], Vb, spec, chunk=128)
+            if backward:
+                out.backward(dout)
+        return fn
+
+    K = max(args.steps, 5)
+    t_fwd = timed(ours(False), K)
+    t_step = timed(ours(True), K)
+    # one forward's chunk pass alone (the fused kernel), as the roofline line
+    C = 128
+    nc = T // C
+    Phi_c, Psi_c = Phi.reshape(nb, nc, C, r), Psi.reshape(nb, nc, C, r)
+    Vb_c = torch.cat([V, torch.ones(nb, T, 1, device=device)], -1).reshape(nb, nc, C, dv + 1)
+    Sin = torch.rand(nb, nc, r, dv + 1, device=device)
+    t_chunk = timed(lambda: KA.chunk_local(Phi_c, Psi_c, Vb_c, Sin), K)
+    chunk_bytes = nb * T * (2 * r + 2 * (dv + 1)) * 4 + nb * nc * r * (dv + 1) * 4
+    ref_line = None
+    R = _import_reference()
+    if R is not None:
+        RA, RB, RM = R
+        try:
+            rspec = RM.build_mask(T, d, chunk=128)
+            RA.to_device(rspec, device)
+            RB.patch()
+
+            def theirs(backward):
+                def fn():
+                    ins = [x.requires_grad_(backward)
+                           for x in (Phi.detach(), Psi.detach(), V.detach())]
+                    Vb = torch.cat([ins[2], torch.ones(nb, T, 1, device=device)], dim=-1)
+                    out = RA.smat_attention(ins[0], ins[1], Vb, rspec, chunk=128,
+                                            scan_backend="triton", incidence_backend="triton")
+                    if backward:
+                        out.backward(dout)
+                return fn
+            ref_line = {"fwd_ms": timed(theirs(False), K), "step_ms": timed(theirs(True), K),
+                        "source": "reference smat (baseline/_ref), Triton backends, patched "
+                                  "differentiable kernels"}
+        except Exception as e:   # noqa: BLE001 -- reported, not fatal
+            ref_line = {"unavailable": f"{type(e).__name__}: {str(e)[:200]}"}
+    dev_err = check_device_errors(device)
+    if rank == 0:
+        peaks = _peaks()
+        line = {
+            "metric": "kernelised SMat attention fwd+bwd tokens/s (reference op, M^(3))",
+            "value": ws * nb * T / (t_step * 1e-3), "unit": "tokens/s", "n_gpus": ws,
+            "steps": K, "warmup": max(3, args.warmup), "ms_per_step": t_step,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic",
+            "config": {"workload": f"kattn: nb={nb} T={T} r={r} d_v={dv} M^({d}) chunk 128, "
+                                   f"fp32 features elu+1", "global_batch": nb * ws,
+                       "seq_len": T, "parallelism": f"(sequence) partition x{ws}",
+                       "l2": "inputs larger than L2; no flush"},
+            "fwd_ms": t_fwd,
+            "roofline": {"bound": "hbm", "kernel": "kattn_chunk_fwd", "achieved":
+                         chunk_bytes / (t_chunk * 1e-3) / 1e9, "peak": peaks["hbm"],
+                         "unit": "GB/s", "frac": chunk_bytes / (t_chunk * 1e-3) / 1e9 /
+                         peaks["hbm"], "traffic": None, "kernel_ms": t_chunk},
+            "reference_triton": ref_line,
+            "device_errors": dev_err,
+        }
+        print(json.dumps(line), flush=True)
+    if dist is not None:
+        dist.destroy_process_group()
+
+
 def _lm_pairs(cfg):
     from smat_attention_b200.mask import block_layout_stats
     return block_layout_stats(cfg.mask())["pairs"]
@@ -754,9 +878,9 @@ def main():
         WORKLOAD["B"] = args.batch
     if args.heads:
         WORKLOAD["H"] = args.heads
-    if args.workload in ("c4", "decode"):
+    if args.workload in ("c4", "decode", "kattn"):
         args.no_cpu_baseline = True
-    if args.impl == "reference" and args.workload not in ("c4", "decode"):
+    if args.impl == "reference" and args.workload not in ("c4", "decode", "kattn"):
         run_reference(args)
     elif args.impl == "reference":
         print(json.dumps({"impl": "reference", "unavailable": "the reference arm times the "
@@ -766,6 +890,8 @@ def main():
         run_lm(args)
     elif args.workload == "decode":
         run_decode(args)
+    elif args.workload == "kattn":
+        run_kattn(args)
     elif args.workload == "c5" and args.shard == "queries":
         run_sharded(args)
     else:
