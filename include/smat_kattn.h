@@ -29,15 +29,27 @@ SMAT_API int smat_kattn_chunk_local_fwd(const float* phi, const float* psi, cons
                                const float* sin_, float* out, int64_t n_chunks, int C,
                                int R, int P, int32_t* err_word, void* stream);
 
+/* The backward of chunk_local (triton_bwd.py:50-196) except dsin (= phi^T dout
+ * per chunk, a plain GEMM left to the caller): dphi = dout sin^T +
+ * tril(dout vb^T) psi, dpsi = tril(dout vb^T)^T phi, dvb = tril(phi psi^T)^T
+ * dout, written to dphi, dpsi [n_chunks, C, R] and dvb [n_chunks, C, P].
+ * Three launches of the same tcgen05 kind::tf32 tile kernel; shapes as for
+ * smat_kattn_chunk_local_fwd. */
+SMAT_API int smat_kattn_chunk_local_bwd(const float* phi, const float* psi, const float* vb,
+                               const float* sin_, const float* dout, float* dphi,
+                               float* dpsi, float* dvb, int64_t n_chunks, int C, int R, int P,
+                               int32_t* err_word, void* stream);
+
 /* F[b, x] = sum_{j in [n_P, n), (j - n_P) mod N0 = x} psi[b, j] vb[b, j]^T
  * (pool, triton_fwd.py:225-311): psi [nb, T, R], vb [nb, T, P], F [nb, N0, R, P];
- * R * P <= 16384, 32 (R + P) floats of staging <= 96 KB.  Exact fp32 FMAs. */
+ * 64 (R + P) floats of staging <= 96 KB.  Exact fp32 FMAs. */
 SMAT_API int smat_kattn_pool_fwd(const float* psi, const float* vb, float* F, int nb, int T,
                         int R, int P, int n_P, int n, int N0, void* stream);
 
 /* Its backward (triton_bwd.py:203-278): for every column j of profile x,
  * dpsi[b, j] = dF[b, x] vb[b, j], dvb[b, j] = dF[b, x]^T psi[b, j]; rows outside
- * [n_P, n) are not written (the caller zeroes them). */
+ * [n_P, n) are not written (the caller zeroes them).  (R P + 64 (R + P)) floats
+ * of staging <= 96 KB. */
 SMAT_API int smat_kattn_pool_bwd(const float* psi, const float* vb, const float* dF,
                         float* dpsi, float* dvb, int nb, int T, int R, int P, int n_P,
                         int n, int N0, void* stream);

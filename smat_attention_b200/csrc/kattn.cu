@@ -3,11 +3,12 @@
 // the reference's TF32 Triton dots) and the long-range pooling / incidence
 // passes on CUDA cores (they move far more bytes than they compute).
 //
-// chunk_local, one CTA per 128-row chunk b:
+// chunk_local, one CTA per 128-row chunk b (kattn_tile_kernel, mode FWD):
 //   S    = Phi_b Psi_b^T            tcgen05.mma 128 x 128, K = R, both K-major (TMA)
 //   S   := tril(S)                  4 warps, thread = row = TMEM lane
 //   O    = S Vb_b + Phi_b Sin_b     A = S from TMEM (TS) / Phi from smem (SS),
 //                                   B = Vb_b / Sin_b MN-major, N = P rounded to 32
+// and its backward in three more modes of the same kernel (dPhi, dVb, dPsi).
 // Vb and Sin rows are P floats (P = d_v + 1 is odd in the reference), which
 // TMA cannot describe, so the compute warps copy them with 4-byte cp.async
 // (zero-filling the padding) into the MN-major layout tcgen05 takes for tf32:
@@ -86,45 +87,83 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map
       : "memory");
 }
 
-struct ChunkParams {
+// One 128-row chunk tile, four modes sharing one pipeline:
+//   G   = A1 B1^T                     128 x 128, K = K1, both K-major
+//   G  := mask(G)                     lower (j <= i) or upper (j >= i) triangle
+//   OUT = [A1 EX] + G B2              B2 MN-major (32-byte atoms), N = NO
+//
+//   mode  A1        B1        mask   EX (SS term)      B2    OUT
+//   FWD   Phi (T)   Psi (T)   lower  Phi Sin (MN)      Vb    out  = Phi Sin + tril(Phi Psi^T) Vb
+//   DPHI  dO (c)    Vb (c)    lower  dO Sin^T (K)      Psi   dPhi = dO Sin^T + tril(dO Vb^T) Psi
+//   DV    Psi (T)   Phi (T)   upper  -                 dO    dVb  = tril(Phi Psi^T)^T dO
+//   DPSI  Vb (c)    dO (c)    upper  -                 Phi   dPsi = tril(dO Vb^T)^T Phi
+// (T: TMA from [rows, R]; c: 4-byte cp.async from rows of P floats, zero-padded
+// to PN.)  Phi / Psi as B2 come by TMA in the 32-byte-atom swizzle.
+enum : int { TM_FWD = 0, TM_DPHI = 1, TM_DV = 2, TM_DPSI = 3 };
+
+struct TileParams {
   const float* vb;     // [n_chunks, KC, P]
   const float* sin;    // [n_chunks, R, P]
-  float* out;          // [n_chunks, KC, P]
-  int P;
+  const float* dout;   // [n_chunks, KC, P]
+  float* out;          // [n_chunks, KC, n_store]
+  int P, n_store;
   int32_t* err;
 };
 
-// R: feature width (K of S and of Phi Sin); PN: P rounded up to 32.
-template <int R, int PN>
-struct ChunkCfg {
-  static constexpr int PANEL = KC * 128;                 // 32 fp32 columns x 128 rows
-  static constexpr int KR = R / 32;                      // K-major panels of Phi / Psi
-  static constexpr int OFF_PHI = 0;
-  static constexpr int OFF_PSI = OFF_PHI + KR * PANEL;
-  static constexpr int VB_PANEL = KC * 128;              // Vb: 128 K-rows x 32 columns
-  static constexpr int SIN_PANEL = R * 128;              // Sin: R K-rows x 32 columns
-  static constexpr int OFF_VB = OFF_PSI + KR * PANEL;
-  static constexpr int OFF_SIN = OFF_VB + (PN / 32) * VB_PANEL;
-  static constexpr int OFF_BAR = OFF_SIN + (PN / 32) * SIN_PANEL;
-  // barriers: phi/psi full, vb/sin full (128 arrivals), s full, s masked (4), o full
-  static constexpr int BAR_QK = 0, BAR_VS = 1, BAR_SF = 2, BAR_SM = 3, BAR_OF = 4, NBAR = 5;
+template <int MODE, int R, int PN>
+struct TileCfg {
+  static constexpr bool KR_G1 = MODE == TM_FWD || MODE == TM_DV;     // G contracts over R
+  static constexpr int K1 = KR_G1 ? R : PN;
+  static constexpr int NO = KR_G1 ? PN : R;                           // OUT columns (padded)
+  static constexpr bool EXTRA = MODE == TM_FWD || MODE == TM_DPHI;
+  static constexpr bool LOWER = MODE == TM_FWD || MODE == TM_DPHI;
+  static constexpr int PANEL = KC * 128;                 // 128 rows x 32 fp32
+  static constexpr int EX_PANEL = R * 128;               // R rows x 32 fp32
+  static constexpr int OFF_A1 = 0;
+  static constexpr int OFF_B1 = OFF_A1 + (K1 / 32) * PANEL;
+  static constexpr int OFF_B2 = OFF_B1 + (K1 / 32) * PANEL;
+  static constexpr int OFF_EX = OFF_B2 + (NO / 32) * PANEL;
+  static constexpr int OFF_BAR = OFF_EX + (EXTRA ? (PN / 32) * EX_PANEL : 0);
+  // barriers: TMA full, copies full (128 arrivals), G full, G masked (4), OUT full
+  static constexpr int BAR_TMA = 0, BAR_CP = 1, BAR_SF = 2, BAR_SM = 3, BAR_OF = 4, NBAR = 5;
   static constexpr int OFF_MISC = OFF_BAR + NBAR * 8;
   static constexpr int SMEM_BYTES = OFF_MISC + 16 + 1024;
   static_assert(SMEM_BYTES <= 227 * 1024, "shared memory budget");
-  static constexpr int COL_S = 0, COL_O = 128;
-  static constexpr int TMEM_COLS = 256;
-  static_assert(COL_O + PN <= TMEM_COLS, "TMEM budget");
-  static constexpr uint32_t IDESC_S = idesc_tf32(128, 128, false, false);
-  static constexpr uint32_t IDESC_O = idesc_tf32(128, PN, false, true);
+  static constexpr int COL_G = 0, COL_O = 128, TMEM_COLS = 256;
+  static_assert(COL_O + NO <= TMEM_COLS, "TMEM budget");
+  // bytes the producer's TMA loads bring
+  static constexpr int TMA_BYTES = KR_G1 ? 2 * (K1 / 32) * PANEL : (NO / 32) * PANEL;
+  static constexpr uint32_t IDESC_G = idesc_tf32(128, 128, false, false);
+  static constexpr uint32_t IDESC_O = idesc_tf32(128, NO, false, true);
+  static constexpr uint32_t IDESC_EX = idesc_tf32(128, NO, false, MODE == TM_FWD);
 };
 
-// 192 threads: warps 0-3 copy Vb / Sin, mask S and store O (thread = row);
-// warp 4 issues the TMA loads; warp 5 allocates TMEM and issues the MMAs.
-template <int R, int PN>
+// rows [0, nrows) x PN fp32 columns of `src` (row stride P) into a K-major
+// SWIZZLE_128B tile (panels of nrows x 32), row r by thread r
+__device__ __forceinline__ void cp_kmajor(uint32_t dst, const float* src, int row, int nrows,
+                                          int P, int PN) {
+  if (row >= nrows) return;
+  for (int k = 0; k < PN; ++k)
+    cp_async4(dst + (k >> 5) * (nrows * 128) + sw128_offset(row, (k & 31) >> 2) + (k & 3) * 4,
+              src + static_cast<int64_t>(row) * P + (k < P ? k : 0), k < P ? 4u : 0u);
+}
+// the same rows into an MN-major tile with 32-byte swizzle atoms (rows = K)
+__device__ __forceinline__ void cp_mn32(uint32_t dst, const float* src, int row, int nrows, int P,
+                                        int PN) {
+  if (row >= nrows) return;
+  for (int c = 0; c < PN; ++c)
+    cp_async4(dst + (c >> 5) * (nrows * 128) + mn32_offset(row, c & 31),
+              src + static_cast<int64_t>(row) * P + (c < P ? c : 0), c < P ? 4u : 0u);
+}
+
+// 192 threads: warps 0-3 copy the cp.async operands, mask G and store OUT
+// (thread = row = TMEM lane); warp 4 issues the TMA loads; warp 5 allocates
+// TMEM and issues the MMAs.
+template <int MODE, int R, int PN>
 __global__ void __launch_bounds__(192, 1)
-    kattn_chunk_fwd_kernel(const __grid_constant__ CUtensorMap tm_phi,
-                           const __grid_constant__ CUtensorMap tm_psi, const ChunkParams p) {
-  using C = ChunkCfg<R, PN>;
+    kattn_tile_kernel(const __grid_constant__ CUtensorMap tm0,
+                      const __grid_constant__ CUtensorMap tm1, const TileParams p) {
+  using C = TileCfg<MODE, R, PN>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
@@ -137,8 +176,8 @@ __global__ void __launch_bounds__(192, 1)
   const int64_t chunk = blockIdx.x;
 
   if (tid == 0) {
-    mbar_init(bar(C::BAR_QK), 1);
-    mbar_init(bar(C::BAR_VS), 128);
+    mbar_init(bar(C::BAR_TMA), 1);
+    mbar_init(bar(C::BAR_CP), 128);
     mbar_init(bar(C::BAR_SF), 1);
     mbar_init(bar(C::BAR_SM), 4);
     mbar_init(bar(C::BAR_OF), 1);
@@ -156,48 +195,57 @@ __global__ void __launch_bounds__(192, 1)
 
   if (warp == 4) {
     if (lane == 0) {
-      mbar_expect_tx(bar(C::BAR_QK), 2 * C::KR * C::PANEL);
+      mbar_expect_tx(bar(C::BAR_TMA), C::TMA_BYTES);
       const int row0 = static_cast<int>(chunk * KC);
+      if (C::KR_G1) {          // A1, B1 from the two K-major maps
 #pragma unroll
-      for (int k = 0; k < C::KR; ++k) {
-        tma_load_2d(sbase + C::OFF_PHI + k * C::PANEL, &tm_phi, bar(C::BAR_QK), 32 * k, row0);
-        tma_load_2d(sbase + C::OFF_PSI + k * C::PANEL, &tm_psi, bar(C::BAR_QK), 32 * k, row0);
+        for (int k = 0; k < C::K1 / 32; ++k) {
+          tma_load_2d(sbase + C::OFF_A1 + k * C::PANEL, &tm0, bar(C::BAR_TMA), 32 * k, row0);
+          tma_load_2d(sbase + C::OFF_B1 + k * C::PANEL, &tm1, bar(C::BAR_TMA), 32 * k, row0);
+        }
+      } else {                 // B2 from the 32-byte-atom map
+#pragma unroll
+        for (int k = 0; k < C::NO / 32; ++k)
+          tma_load_2d(sbase + C::OFF_B2 + k * C::PANEL, &tm0, bar(C::BAR_TMA), 32 * k, row0);
       }
     }
   } else if (warp == 5) {
     if (lane == 0) {
-      bool ok = mbar_wait(bar(C::BAR_QK), 0, abort_flag, p.err);
+      bool ok = mbar_wait(bar(C::BAR_TMA), 0, abort_flag, p.err) &&
+                mbar_wait(bar(C::BAR_CP), 0, abort_flag, p.err);
       if (ok) {
         tc_fence_after();
-        // S = Phi Psi^T: K = R in steps of 8 (32 bytes of a 128-byte row)
 #pragma unroll
-        for (int kk = 0; kk < R / 8; ++kk) {
+        for (int kk = 0; kk < C::K1 / 8; ++kk) {
           const uint32_t off = (kk >> 2) * C::PANEL + (kk & 3) * 32;
-          mma_tf32(tbase + C::COL_S, sdesc_sw128(sbase + C::OFF_PHI + off, 16, 1024),
-                   sdesc_sw128(sbase + C::OFF_PSI + off, 16, 1024), C::IDESC_S, kk > 0);
+          mma_tf32(tbase + C::COL_G, sdesc_sw128(sbase + C::OFF_A1 + off, 16, 1024),
+                   sdesc_sw128(sbase + C::OFF_B1 + off, 16, 1024), C::IDESC_G, kk > 0);
         }
         tc_commit(bar(C::BAR_SF));
-        ok = mbar_wait(bar(C::BAR_VS), 0, abort_flag, p.err);
-      }
-      if (ok) {
-        tc_fence_after();
-        // O = Phi Sin (SS): B = Sin, MN-major, 8 K-rows (one 1024-byte atom) per step
+        if (C::EXTRA) {
+          // FWD: Phi (A1, K = R) x Sin (MN-major); DPHI: dO (A1, K = PN) x Sin^T (K-major)
 #pragma unroll
-        for (int kk = 0; kk < R / 8; ++kk) {
-          const uint32_t off = (kk >> 2) * C::PANEL + (kk & 3) * 32;
-          mma_tf32(tbase + C::COL_O, sdesc_sw128(sbase + C::OFF_PHI + off, 16, 1024),
-                   sdesc_mn32(sbase + C::OFF_SIN + kk * 1024, C::SIN_PANEL), C::IDESC_O,
-                   kk > 0);
+          for (int kk = 0; kk < C::K1 / 8; ++kk) {
+            const uint32_t off = (kk >> 2) * C::PANEL + (kk & 3) * 32;
+            const uint64_t bd =
+                MODE == TM_FWD
+                    ? sdesc_mn32(sbase + C::OFF_EX + kk * 1024, C::EX_PANEL)
+                    : sdesc_sw128(sbase + C::OFF_EX + (kk >> 2) * C::EX_PANEL + (kk & 3) * 32, 16,
+                                  1024);
+            mma_tf32(tbase + C::COL_O, sdesc_sw128(sbase + C::OFF_A1 + off, 16, 1024), bd,
+                     C::IDESC_EX, kk > 0);
+          }
         }
         ok = mbar_wait(bar(C::BAR_SM), 0, abort_flag, p.err);
       }
       if (ok) {
         tc_fence_after();
-        // O += tril(S) Vb (TS): A = S from TMEM, 8 columns per step
+        // OUT += mask(G) B2 (TS): A = G from TMEM, 8 columns per step
 #pragma unroll 4
         for (int kk = 0; kk < KC / 8; ++kk)
-          mma_tf32_ts(tbase + C::COL_O, tbase + C::COL_S + 8 * kk,
-                      sdesc_mn32(sbase + C::OFF_VB + kk * 1024, C::VB_PANEL), C::IDESC_O, 1u);
+          mma_tf32_ts(tbase + C::COL_O, tbase + C::COL_G + 8 * kk,
+                      sdesc_mn32(sbase + C::OFF_B2 + kk * 1024, C::PANEL), C::IDESC_O,
+                      (C::EXTRA || kk > 0) ? 1u : 0u);
         tc_commit(bar(C::BAR_OF));
       }
       if (*abort_flag) {   // let issued MMAs finish before TMEM is freed
@@ -207,42 +255,47 @@ __global__ void __launch_bounds__(192, 1)
     }
   } else {
     // ---------------------------------------------------------------- warps 0-3
-    const int r = warp * 32 + lane;      // chunk row = TMEM lane
-    // Vb [KC x P] and Sin [R x P] into MN-major SW128 panels of 32 columns
-    const float* vb = p.vb + chunk * KC * p.P;
+    const int r = warp * 32 + lane;      // tile row = TMEM lane
+    const int64_t rows_off = chunk * KC * p.P;
+    const float* vb = p.vb + rows_off;
+    const float* dO = p.dout + rows_off;
     const float* sn = p.sin + chunk * R * p.P;
-    for (int c = 0; c < PN; ++c) {
-      const uint32_t dst = sbase + C::OFF_VB + (c >> 5) * C::VB_PANEL + mn32_offset(r, c & 31);
-      cp_async4(dst, vb + static_cast<int64_t>(r) * p.P + (c < p.P ? c : 0), c < p.P ? 4u : 0u);
+    if (MODE == TM_FWD) {
+      cp_mn32(sbase + C::OFF_B2, vb, r, KC, p.P, PN);
+      cp_mn32(sbase + C::OFF_EX, sn, r, R, p.P, PN);
+    } else if (MODE == TM_DPHI) {
+      cp_kmajor(sbase + C::OFF_A1, dO, r, KC, p.P, PN);
+      cp_kmajor(sbase + C::OFF_B1, vb, r, KC, p.P, PN);
+      cp_kmajor(sbase + C::OFF_EX, sn, r, R, p.P, PN);
+    } else if (MODE == TM_DV) {
+      cp_mn32(sbase + C::OFF_B2, dO, r, KC, p.P, PN);
+    } else {
+      cp_kmajor(sbase + C::OFF_A1, vb, r, KC, p.P, PN);
+      cp_kmajor(sbase + C::OFF_B1, dO, r, KC, p.P, PN);
     }
-    for (int kr = r; kr < R; kr += 128)
-      for (int c = 0; c < PN; ++c) {
-        const uint32_t dst = sbase + C::OFF_SIN + (c >> 5) * C::SIN_PANEL + mn32_offset(kr, c & 31);
-        cp_async4(dst, sn + static_cast<int64_t>(kr) * p.P + (c < p.P ? c : 0),
-                  c < p.P ? 4u : 0u);
-      }
     asm volatile("cp.async.wait_all;" ::: "memory");
     fence_proxy_async_smem();
-    mbar_arrive(bar(C::BAR_VS));
+    mbar_arrive(bar(C::BAR_CP));
     const uint32_t lane_base = tbase + (static_cast<uint32_t>(warp * 32) << 16);
     bool alive = __all_sync(0xffffffffu, mbar_wait(bar(C::BAR_SF), 0, abort_flag, p.err));
     if (alive) {
       tc_fence_after();
-      // keep S[r, j] for j <= r: 32-column blocks past the diagonal become 0
+      // lower: keep G[r, j] for j <= r; upper: keep j >= r
 #pragma unroll 1
       for (int q = 0; q < 4; ++q) {
-        if (32 * q > warp * 32 + 31) {
+        const bool all_out = C::LOWER ? q > warp : q < warp;
+        if (all_out) {
           float z[32];
 #pragma unroll
           for (int i = 0; i < 32; ++i) z[i] = 0.f;
-          tmem_st32(lane_base + C::COL_S + 32 * q, z);
+          tmem_st32(lane_base + C::COL_G + 32 * q, z);
         } else if (q == warp) {
-          float s[32];
-          tmem_ld32(lane_base + C::COL_S + 32 * q, s);
+          float g[32];
+          tmem_ld32(lane_base + C::COL_G + 32 * q, g);
 #pragma unroll
           for (int i = 0; i < 32; ++i)
-            if (32 * q + i > r) s[i] = 0.f;
-          tmem_st32(lane_base + C::COL_S + 32 * q, s);
+            if (C::LOWER ? (32 * q + i > r) : (32 * q + i < r)) g[i] = 0.f;
+          tmem_st32(lane_base + C::COL_G + 32 * q, g);
         }
       }
       tmem_st_wait();
@@ -253,14 +306,14 @@ __global__ void __launch_bounds__(192, 1)
     }
     if (alive) {
       tc_fence_after();
-      float* orow = p.out + (chunk * KC + r) * p.P;
+      float* orow = p.out + (chunk * KC + r) * p.n_store;
 #pragma unroll 1
-      for (int c0 = 0; c0 < PN; c0 += 32) {
+      for (int c0 = 0; c0 < C::NO; c0 += 32) {
         float o[32];
         tmem_ld32(lane_base + C::COL_O + c0, o);
 #pragma unroll
         for (int i = 0; i < 32; ++i)
-          if (c0 + i < p.P) orow[c0 + i] = o[i];
+          if (c0 + i < p.n_store) orow[c0 + i] = o[i];
       }
     }
   }
@@ -274,83 +327,102 @@ __global__ void __launch_bounds__(192, 1)
 }
 
 // ---------------------------------------------------------------- pool
-// One CTA per (profile x, b); 256 threads, each accumulating R P / 256 outputs
-// (16 for R = 64, P = 65) over the profile's columns, staged 32 at a time.
+// One CTA per (profile x, b).  The profile's columns (about n_X / N0, 16 at
+// c3 sizes) are staged in shared memory; each thread then owns 4
+// consecutive outputs of F_x per pass over the R P outputs.
+constexpr int POOL_MAXG = 64;   // columns staged per round
+
 __global__ void __launch_bounds__(256) kattn_pool_kernel(const float* __restrict__ psi,
                                                          const float* __restrict__ vb,
                                                          float* __restrict__ F, int T, int R,
                                                          int P, int n_P, int n, int N0) {
-  extern __shared__ float stage[];   // [32][R] psi rows, then [32][P] vb rows
+  extern __shared__ float stage[];   // [POOL_MAXG][R] psi rows, then [POOL_MAXG][P] vb rows
   const int x = blockIdx.x, b = blockIdx.y;
   float* sp = stage;
-  float* sv = stage + 32 * R;
+  float* sv = stage + POOL_MAXG * R;
   const int RP = R * P;
-  constexpr int MAXO = 64;            // outputs per thread (R P <= 16384)
-  float acc[MAXO];
-#pragma unroll
-  for (int i = 0; i < MAXO; ++i) acc[i] = 0.f;
   const int n_X = n - n_P;
-  const int g = (n_X - x + N0 - 1) / N0;   // columns of this profile
+  const int g = x < n_X ? (n_X - x + N0 - 1) / N0 : 0;   // columns of this profile
   const float* pb = psi + static_cast<int64_t>(b) * T * R;
   const float* vbb = vb + static_cast<int64_t>(b) * T * P;
-  for (int s0 = 0; s0 < g; s0 += 32) {
-    const int ns = min(32, g - s0);
-    __syncthreads();
-    for (int e = threadIdx.x; e < ns * R; e += blockDim.x) {
-      const int s = e / R, c = e % R;
-      sp[s * R + c] = pb[static_cast<int64_t>(n_P + x + (s0 + s) * N0) * R + c];
-    }
-    for (int e = threadIdx.x; e < ns * P; e += blockDim.x) {
-      const int s = e / P, c = e % P;
-      sv[s * P + c] = vbb[static_cast<int64_t>(n_P + x + (s0 + s) * N0) * P + c];
-    }
-    __syncthreads();
+  float* fo = F + (static_cast<int64_t>(b) * N0 + x) * RP;
+  // passes over the outputs; the trip count is the same for every thread
+  // (the staging below synchronises the CTA)
+  for (int base = 0; base < RP; base += 1024) {
+    const int o0 = base + threadIdx.x * 4;
+    float acc[4] = {0.f, 0.f, 0.f, 0.f};
+    int rr[4], pp[4];
 #pragma unroll
-    for (int i = 0; i < MAXO; ++i) {
-      const int o = threadIdx.x + i * 256;
-      if (o < RP) {
-        const int rr = o / P, pp = o % P;
-        float a = acc[i];
-        for (int s = 0; s < ns; ++s) a = fmaf(sp[s * R + rr], sv[s * P + pp], a);
-        acc[i] = a;
+    for (int u = 0; u < 4; ++u) {
+      const int o = min(o0 + u, RP - 1);
+      rr[u] = o / P;
+      pp[u] = o % P;
+    }
+    for (int s0 = 0; s0 < g; s0 += POOL_MAXG) {
+      const int ns = min(POOL_MAXG, g - s0);
+      __syncthreads();
+      for (int e = threadIdx.x; e < ns * R; e += blockDim.x) {
+        const int si = e / R, c = e % R;
+        sp[si * R + c] = pb[static_cast<int64_t>(n_P + x + (s0 + si) * N0) * R + c];
+      }
+      for (int e = threadIdx.x; e < ns * P; e += blockDim.x) {
+        const int si = e / P, c = e % P;
+        sv[si * P + c] = vbb[static_cast<int64_t>(n_P + x + (s0 + si) * N0) * P + c];
+      }
+      __syncthreads();
+      for (int si = 0; si < ns; ++si) {
+#pragma unroll
+        for (int u = 0; u < 4; ++u) acc[u] = fmaf(sp[si * R + rr[u]], sv[si * P + pp[u]], acc[u]);
       }
     }
-  }
-  float* fo = F + (static_cast<int64_t>(b) * N0 + x) * RP;
 #pragma unroll
-  for (int i = 0; i < MAXO; ++i) {
-    const int o = threadIdx.x + i * 256;
-    if (o < RP) fo[o] = acc[i];
+    for (int u = 0; u < 4; ++u)
+      if (o0 + u < RP) fo[o0 + u] = acc[u];
   }
 }
 
 // For every column j of profile x: dpsi_j = dF_x vb_j, dvb_j = dF_x^T psi_j.
-// One CTA per (x, b), dF_x staged in shared memory.
+// One CTA per (x, b); dF_x and the profile's columns are staged in shared
+// memory, and the (column, row) pairs of both products are spread over the
+// threads.
 __global__ void __launch_bounds__(256) kattn_pool_bwd_kernel(
     const float* __restrict__ psi, const float* __restrict__ vb, const float* __restrict__ dF,
     float* __restrict__ dpsi, float* __restrict__ dvb, int T, int R, int P, int n_P, int n,
     int N0) {
-  extern __shared__ float sdf[];   // [R][P]
+  extern __shared__ float sm[];   // dF [R][P], then psi [POOL_MAXG][R], vb [POOL_MAXG][P]
   const int x = blockIdx.x, b = blockIdx.y;
   const int RP = R * P;
+  float* sdf = sm;
+  float* sp = sm + RP;
+  float* sv = sp + POOL_MAXG * R;
   const float* df = dF + (static_cast<int64_t>(b) * N0 + x) * RP;
   for (int e = threadIdx.x; e < RP; e += blockDim.x) sdf[e] = df[e];
-  __syncthreads();
   const int n_X = n - n_P;
-  const int g = (n_X - x + N0 - 1) / N0;
-  for (int s = 0; s < g; ++s) {
-    const int64_t j = static_cast<int64_t>(b) * T + n_P + x + s * N0;
-    const float* pr = psi + j * R;
-    const float* vr = vb + j * P;
-    for (int rr = threadIdx.x; rr < R; rr += blockDim.x) {
-      float a = 0.f;
-      for (int pp = 0; pp < P; ++pp) a = fmaf(sdf[rr * P + pp], vr[pp], a);
-      dpsi[j * R + rr] = a;
+  const int g = x < n_X ? (n_X - x + N0 - 1) / N0 : 0;
+  const int64_t row0 = static_cast<int64_t>(b) * T + n_P + x;
+  for (int s0 = 0; s0 < g; s0 += POOL_MAXG) {
+    const int ns = min(POOL_MAXG, g - s0);
+    __syncthreads();
+    for (int e = threadIdx.x; e < ns * R; e += blockDim.x) {
+      const int si = e / R, c = e % R;
+      sp[si * R + c] = psi[(row0 + static_cast<int64_t>(s0 + si) * N0) * R + c];
     }
-    for (int pp = threadIdx.x; pp < P; pp += blockDim.x) {
+    for (int e = threadIdx.x; e < ns * P; e += blockDim.x) {
+      const int si = e / P, c = e % P;
+      sv[si * P + c] = vb[(row0 + static_cast<int64_t>(s0 + si) * N0) * P + c];
+    }
+    __syncthreads();
+    for (int e = threadIdx.x; e < ns * R; e += blockDim.x) {   // dpsi[j, rr]
+      const int si = e / R, rr = e % R;
       float a = 0.f;
-      for (int rr = 0; rr < R; ++rr) a = fmaf(sdf[rr * P + pp], pr[rr], a);
-      dvb[j * P + pp] = a;
+      for (int pp = 0; pp < P; ++pp) a = fmaf(sdf[rr * P + pp], sv[si * P + pp], a);
+      dpsi[(row0 + static_cast<int64_t>(s0 + si) * N0) * R + rr] = a;
+    }
+    for (int e = threadIdx.x; e < ns * P; e += blockDim.x) {   // dvb[j, pp]
+      const int si = e / P, pp = e % P;
+      float a = 0.f;
+      for (int rr = 0; rr < R; ++rr) a = fmaf(sdf[rr * P + pp], sp[si * R + rr], a);
+      dvb[(row0 + static_cast<int64_t>(s0 + si) * N0) * P + pp] = a;
     }
   }
 }
@@ -414,8 +486,11 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   return fn;
 }
 
-// 2-D fp32 map over [rows, R], box {32, 128}, 128-byte swizzle
-int map_rows(CUtensorMap* m, const float* base, int64_t rows, int R) {
+bool al16(const void* p);
+
+// 2-D fp32 map over [rows, R], box {32, 128}: 128-byte swizzle (K-major
+// operand tiles) or its 32-byte-atom form (MN-major operand tiles)
+int map_rows(CUtensorMap* m, const float* base, int64_t rows, int R, bool atom32 = false) {
   auto enc = encode_fn();
   if (!enc) return SMAT_ERR_NO_DEVICE;
   cuuint64_t dims[2] = {static_cast<cuuint64_t>(R), static_cast<cuuint64_t>(rows)};
@@ -423,37 +498,57 @@ int map_rows(CUtensorMap* m, const float* base, int64_t rows, int R) {
   cuuint32_t box[2] = {32, 128};
   cuuint32_t estr[2] = {1, 1};
   CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(base), dims, strides,
-                   box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                   box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                   atom32 ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B : CU_TENSOR_MAP_SWIZZLE_128B,
                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS ? SMAT_OK : SMAT_ERR_TMA_DESCRIPTOR;
 }
 
-template <int R, int PN>
-int chunk_fwd_launch(const CUtensorMap& mphi, const CUtensorMap& mpsi, const ChunkParams& p,
-                     int64_t n_chunks, cudaStream_t s) {
-  using C = ChunkCfg<R, PN>;
-  auto kern = kattn_chunk_fwd_kernel<R, PN>;
+template <int MODE, int R, int PN>
+int tile_launch(const CUtensorMap& m0, const CUtensorMap& m1, const TileParams& p,
+                int64_t n_chunks, cudaStream_t s) {
+  using C = TileCfg<MODE, R, PN>;
+  auto kern = kattn_tile_kernel<MODE, R, PN>;
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES) !=
       cudaSuccess)
     return SMAT_ERR_LAUNCH;
-  kern<<<static_cast<unsigned>(n_chunks), 192, C::SMEM_BYTES, s>>>(mphi, mpsi, p);
+  kern<<<static_cast<unsigned>(n_chunks), 192, C::SMEM_BYTES, s>>>(m0, m1, p);
   return cudaGetLastError() == cudaSuccess ? SMAT_OK : SMAT_ERR_LAUNCH;
 }
 
-template <int R>
-int chunk_fwd_p(const CUtensorMap& a, const CUtensorMap& b, const ChunkParams& p, int64_t nc,
-                cudaStream_t s) {
-  const int pn = (p.P + 31) / 32 * 32;
-  switch (pn) {
-    case 32: return chunk_fwd_launch<R, 32>(a, b, p, nc, s);
-    case 64: return chunk_fwd_launch<R, 64>(a, b, p, nc, s);
-    case 96: return chunk_fwd_launch<R, 96>(a, b, p, nc, s);
+template <int MODE, int R>
+int tile_p(const CUtensorMap& a, const CUtensorMap& b, const TileParams& p, int64_t nc,
+           cudaStream_t s) {
+  switch ((p.P + 31) / 32 * 32) {
+    case 32: return tile_launch<MODE, R, 32>(a, b, p, nc, s);
+    case 64: return tile_launch<MODE, R, 64>(a, b, p, nc, s);
+    case 96: return tile_launch<MODE, R, 96>(a, b, p, nc, s);
     case 128:
       // R = 128 with P > 96 exceeds the shared memory (four 64 KB operands)
-      if constexpr (R < 128) return chunk_fwd_launch<R, 128>(a, b, p, nc, s);
+      if constexpr (R < 128) return tile_launch<MODE, R, 128>(a, b, p, nc, s);
       break;
   }
   return SMAT_ERR_BAD_SHAPE;
+}
+
+template <int MODE>
+int tile_r(const CUtensorMap& a, const CUtensorMap& b, const TileParams& p, int R, int64_t nc,
+           cudaStream_t s) {
+  switch (R) {
+    case 32: return tile_p<MODE, 32>(a, b, p, nc, s);
+    case 64: return tile_p<MODE, 64>(a, b, p, nc, s);
+    case 128: return tile_p<MODE, 128>(a, b, p, nc, s);
+  }
+  return SMAT_ERR_BAD_SHAPE;
+}
+
+int check_chunk(const float* phi, const float* psi, int64_t n_chunks, int C, int R, int P) {
+  if (!phi || !psi) return SMAT_ERR_NULL_POINTER;
+  if (C != KC || (R != 32 && R != 64 && R != 128) || P < 1 || P > (R == 128 ? 96 : 128) ||
+      n_chunks < 0 || n_chunks > 0x7FFFFFFF / KC)
+    return SMAT_ERR_BAD_SHAPE;
+  if (!al16(phi) || !al16(psi)) return SMAT_ERR_BAD_ALIGNMENT;
+  return SMAT_OK;
 }
 
 bool al16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
@@ -465,32 +560,47 @@ extern "C" {
 int smat_kattn_chunk_local_fwd(const float* phi, const float* psi, const float* vb,
                                const float* sin_, float* out, int64_t n_chunks, int C, int R,
                                int P, int32_t* err_word, void* stream) {
-  if (!phi || !psi || !vb || !sin_ || !out) return SMAT_ERR_NULL_POINTER;
-  if (C != KC || (R != 32 && R != 64 && R != 128) || P < 1 || P > (R == 128 ? 96 : 128) ||
-      n_chunks < 0 || n_chunks > 0x7FFFFFFF / KC)
-    return SMAT_ERR_BAD_SHAPE;
-  if (!al16(phi) || !al16(psi)) return SMAT_ERR_BAD_ALIGNMENT;
+  int rc = check_chunk(phi, psi, n_chunks, C, R, P);
+  if (rc) return rc;
+  if (!vb || !sin_ || !out) return SMAT_ERR_NULL_POINTER;
   if (n_chunks == 0) return SMAT_OK;
   CUtensorMap mphi, mpsi;
-  int rc;
   if ((rc = map_rows(&mphi, phi, n_chunks * KC, R))) return rc;
   if ((rc = map_rows(&mpsi, psi, n_chunks * KC, R))) return rc;
-  ChunkParams p{vb, sin_, out, P, err_word};
+  TileParams p{vb, sin_, nullptr, out, P, P, err_word};
+  return tile_r<TM_FWD>(mphi, mpsi, p, R, n_chunks, static_cast<cudaStream_t>(stream));
+}
+
+int smat_kattn_chunk_local_bwd(const float* phi, const float* psi, const float* vb,
+                               const float* sin_, const float* dout, float* dphi, float* dpsi,
+                               float* dvb, int64_t n_chunks, int C, int R, int P,
+                               int32_t* err_word, void* stream) {
+  int rc = check_chunk(phi, psi, n_chunks, C, R, P);
+  if (rc) return rc;
+  if (!vb || !sin_ || !dout || !dphi || !dpsi || !dvb) return SMAT_ERR_NULL_POINTER;
+  if (n_chunks == 0) return SMAT_OK;
+  CUtensorMap kphi, kpsi, mphi, mpsi;
+  if ((rc = map_rows(&kphi, phi, n_chunks * KC, R))) return rc;
+  if ((rc = map_rows(&kpsi, psi, n_chunks * KC, R))) return rc;
+  if ((rc = map_rows(&mphi, phi, n_chunks * KC, R, true))) return rc;
+  if ((rc = map_rows(&mpsi, psi, n_chunks * KC, R, true))) return rc;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  switch (R) {
-    case 32: return chunk_fwd_p<32>(mphi, mpsi, p, n_chunks, s);
-    case 64: return chunk_fwd_p<64>(mphi, mpsi, p, n_chunks, s);
-    default: return chunk_fwd_p<128>(mphi, mpsi, p, n_chunks, s);
-  }
+  TileParams p{vb, sin_, dout, dphi, P, R, err_word};
+  if ((rc = tile_r<TM_DPHI>(mpsi, mpsi, p, R, n_chunks, s))) return rc;
+  p.out = dvb;
+  p.n_store = P;
+  if ((rc = tile_r<TM_DV>(kpsi, kphi, p, R, n_chunks, s))) return rc;
+  p.out = dpsi;
+  p.n_store = R;
+  return tile_r<TM_DPSI>(mphi, mphi, p, R, n_chunks, s);
 }
 
 int smat_kattn_pool_fwd(const float* psi, const float* vb, float* F, int nb, int T, int R, int P,
                         int n_P, int n, int N0, void* stream) {
   if (!psi || !vb || !F) return SMAT_ERR_NULL_POINTER;
-  if (nb < 1 || T < 1 || R < 1 || P < 1 || R * P > 64 * 256 || N0 < 1 || n_P < 0 ||
-      n < n_P || n > T)
+  if (nb < 1 || T < 1 || R < 1 || P < 1 || N0 < 1 || n_P < 0 || n < n_P || n > T)
     return SMAT_ERR_BAD_SHAPE;
-  const int bytes = 32 * (R + P) * 4;
+  const int bytes = POOL_MAXG * (R + P) * 4;
   if (bytes > 96 * 1024) return SMAT_ERR_BAD_SHAPE;
   if (cudaFuncSetAttribute(kattn_pool_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                            96 * 1024) != cudaSuccess)
@@ -506,7 +616,7 @@ int smat_kattn_pool_bwd(const float* psi, const float* vb, const float* dF, floa
   if (!psi || !vb || !dF || !dpsi || !dvb) return SMAT_ERR_NULL_POINTER;
   if (nb < 1 || T < 1 || R < 1 || P < 1 || N0 < 1 || n_P < 0 || n < n_P || n > T)
     return SMAT_ERR_BAD_SHAPE;
-  const int bytes = R * P * 4;
+  const int bytes = (R * P + POOL_MAXG * (R + P)) * 4;
   if (bytes > 96 * 1024) return SMAT_ERR_BAD_SHAPE;
   if (cudaFuncSetAttribute(kattn_pool_bwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                            96 * 1024) != cudaSuccess)

@@ -10,8 +10,9 @@ with the three passes its Triton module fuses replaced by kernels of
     ``Phi_b Sin_b + tril(Phi_b Psi_b^T) Vb_b`` per 128-row chunk on tcgen05
     tensor cores (TF32 inputs, fp32 accumulation: the reference's
     ``allow_tf32`` dots, ``kernels/triton_fwd.py:49-152``).  Backward: the
-    same contractions as the reference's two backward kernels
-    (``kernels/triton_bwd.py:50-196``), as fp32 library GEMMs.
+    contractions of the reference's two backward kernels
+    (``kernels/triton_bwd.py:50-196``) as three more modes of the same tile
+    kernel (dPhi, dVb, dPsi); ``dSin = Phi^T dOut`` is a batched GEMM.
 ``pool(Psi, Vb, n_P, n, N0)``
     ``F_x = sum_{prof(j) = x} Psi_j Vb_j^T`` (``triton_fwd.py:225-311``) and its
     backward (``triton_bwd.py:203-278``), fp32 on CUDA cores.
@@ -42,6 +43,8 @@ __all__ = ["chunk_local", "pool", "incidence", "segmented_causal_scan", "pool_pr
 _vp, _ci, _cl = ctypes.c_void_p, ctypes.c_int, ctypes.c_int64
 SIGNATURES = {
     "smat_kattn_chunk_local_fwd": (_ci, [_vp, _vp, _vp, _vp, _vp, _cl, _ci, _ci, _ci, _vp, _vp]),
+    "smat_kattn_chunk_local_bwd": (_ci, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _cl, _ci, _ci,
+                                         _ci, _vp, _vp]),
     "smat_kattn_pool_fwd": (_ci, [_vp, _vp, _vp, _ci, _ci, _ci, _ci, _ci, _ci, _ci, _vp]),
     "smat_kattn_pool_bwd": (_ci, [_vp, _vp, _vp, _vp, _vp, _ci, _ci, _ci, _ci, _ci, _ci, _ci,
                                   _vp]),
@@ -95,13 +98,16 @@ class _ChunkLocal(torch.autograd.Function):
     @staticmethod
     def backward(ctx, dout):
         q, k, v, s = ctx.saved_tensors
-        do = dout.float()
-        A = (q @ k.transpose(-1, -2)).tril()
-        dA = (do @ v.transpose(-1, -2)).tril()
-        dq = do @ s.transpose(-1, -2) + dA @ k
-        dk = dA.transpose(-1, -2) @ q
-        dv = A.transpose(-1, -2) @ do
-        ds = q.transpose(-1, -2) @ do
+        nb, nc, C, R = q.shape
+        P = v.shape[-1]
+        do = dout.float().contiguous()
+        dq, dk = torch.empty_like(q), torch.empty_like(k)
+        dv = torch.empty_like(v)
+        _lib.check("smat_kattn_chunk_local_bwd", _L().smat_kattn_chunk_local_bwd(
+            q.data_ptr(), k.data_ptr(), v.data_ptr(), s.data_ptr(), do.data_ptr(),
+            dq.data_ptr(), dk.data_ptr(), dv.data_ptr(), nb * nc, C, R, P, _err(q.device),
+            _stream(q)))
+        ds = q.transpose(-1, -2) @ do          # (nb, nc, r, p), a plain batched GEMM
         return tuple(g.to(t) for g, t in zip((dq, dk, dv, ds), ctx.dtypes))
 
 

@@ -2,12 +2,11 @@
 against the oracle (oracle/kernel_attention.py, itself pinned to the
 reference's torch path by tests/test_kattn_oracle.py).
 
-Tolerances: the chunk-local forward runs TF32 tensor cores, as the reference's
-Triton kernel does (allow_tf32), and is held to 2e-3 of each tensor's largest
-entry -- the reference's own fp32 kernel-vs-torch bound
-(tests/test_smat.py:390); everything else is fp32 arithmetic, held to 1e-5
-relative (pool, incidence) or 1e-4 (the library-GEMM backward of the chunk
-pass, whose inputs come from the TF32 forward only through dout)."""
+Tolerances: the chunk-local pass (forward and backward) runs TF32 tensor
+cores, as the reference's Triton kernels do (allow_tf32), and is held to 2e-3
+of each tensor's largest entry -- the reference's own fp32 kernel-vs-torch
+bound (tests/test_smat.py:390); pool and incidence are fp32 arithmetic, held
+to 1e-5 relative."""
 
 import glob
 import os
@@ -53,7 +52,7 @@ def test_chunk_local(cuda_device, R, P):
     (ref * dout.float().double()).sum().backward()
     _close(out, ref.detach(), 2e-3, "out")
     for a, b, n in zip(ins, ref_in, ("dphi", "dpsi", "dvb", "dsin")):
-        _close(a.grad, b.grad, 1e-4, n)
+        _close(a.grad, b.grad, 2e-3 if n != "dsin" else 1e-4, n)
 
 
 @pytest.mark.parametrize("T,d,n_P,R,P", [(1024, 3, 0, 64, 65), (2048, 3, 16, 32, 17),
