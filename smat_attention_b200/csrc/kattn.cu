@@ -346,38 +346,38 @@ __global__ void __launch_bounds__(256) kattn_pool_kernel(const float* __restrict
   const float* pb = psi + static_cast<int64_t>(b) * T * R;
   const float* vbb = vb + static_cast<int64_t>(b) * T * P;
   float* fo = F + (static_cast<int64_t>(b) * N0 + x) * RP;
-  // passes over the outputs; the trip count is the same for every thread
-  // (the staging below synchronises the CTA)
-  for (int base = 0; base < RP; base += 1024) {
-    const int o0 = base + threadIdx.x * 4;
-    float acc[4] = {0.f, 0.f, 0.f, 0.f};
-    int rr[4], pp[4];
-#pragma unroll
-    for (int u = 0; u < 4; ++u) {
-      const int o = min(o0 + u, RP - 1);
-      rr[u] = o / P;
-      pp[u] = o % P;
+  // rounds of up to POOL_MAXG staged columns (one round at the usual sizes);
+  // every pass over the outputs then reads the staged columns only
+  for (int s0 = 0; s0 == 0 || s0 < g; s0 += POOL_MAXG) {
+    const int ns = max(0, min(POOL_MAXG, g - s0));
+    __syncthreads();
+    for (int e = threadIdx.x; e < ns * R; e += blockDim.x) {
+      const int si = e / R, c = e % R;
+      sp[si * R + c] = pb[static_cast<int64_t>(n_P + x + (s0 + si) * N0) * R + c];
     }
-    for (int s0 = 0; s0 < g; s0 += POOL_MAXG) {
-      const int ns = min(POOL_MAXG, g - s0);
-      __syncthreads();
-      for (int e = threadIdx.x; e < ns * R; e += blockDim.x) {
-        const int si = e / R, c = e % R;
-        sp[si * R + c] = pb[static_cast<int64_t>(n_P + x + (s0 + si) * N0) * R + c];
+    for (int e = threadIdx.x; e < ns * P; e += blockDim.x) {
+      const int si = e / P, c = e % P;
+      sv[si * P + c] = vbb[static_cast<int64_t>(n_P + x + (s0 + si) * N0) * P + c];
+    }
+    __syncthreads();
+    for (int o0 = threadIdx.x * 4; o0 < RP; o0 += 1024) {
+      float acc[4];
+      int rr[4], pp[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int o = min(o0 + u, RP - 1);
+        rr[u] = o / P;
+        pp[u] = o % P;
+        acc[u] = (s0 > 0 && o0 + u < RP) ? fo[o0 + u] : 0.f;
       }
-      for (int e = threadIdx.x; e < ns * P; e += blockDim.x) {
-        const int si = e / P, c = e % P;
-        sv[si * P + c] = vbb[static_cast<int64_t>(n_P + x + (s0 + si) * N0) * P + c];
-      }
-      __syncthreads();
       for (int si = 0; si < ns; ++si) {
 #pragma unroll
         for (int u = 0; u < 4; ++u) acc[u] = fmaf(sp[si * R + rr[u]], sv[si * P + pp[u]], acc[u]);
       }
-    }
 #pragma unroll
-    for (int u = 0; u < 4; ++u)
-      if (o0 + u < RP) fo[o0 + u] = acc[u];
+      for (int u = 0; u < 4; ++u)
+        if (o0 + u < RP) fo[o0 + u] = acc[u];
+    }
   }
 }
 
@@ -412,17 +412,28 @@ __global__ void __launch_bounds__(256) kattn_pool_bwd_kernel(
       sv[si * P + c] = vb[(row0 + static_cast<int64_t>(s0 + si) * N0) * P + c];
     }
     __syncthreads();
+    // dot products with four independent partial sums (the chains are long
+    // and the CTA holds few warps)
     for (int e = threadIdx.x; e < ns * R; e += blockDim.x) {   // dpsi[j, rr]
       const int si = e / R, rr = e % R;
-      float a = 0.f;
-      for (int pp = 0; pp < P; ++pp) a = fmaf(sdf[rr * P + pp], sv[si * P + pp], a);
-      dpsi[(row0 + static_cast<int64_t>(s0 + si) * N0) * R + rr] = a;
+      float a[4] = {0.f, 0.f, 0.f, 0.f};
+      int pp = 0;
+      for (; pp + 4 <= P; pp += 4)
+#pragma unroll
+        for (int u = 0; u < 4; ++u) a[u] = fmaf(sdf[rr * P + pp + u], sv[si * P + pp + u], a[u]);
+      for (; pp < P; ++pp) a[0] = fmaf(sdf[rr * P + pp], sv[si * P + pp], a[0]);
+      dpsi[(row0 + static_cast<int64_t>(s0 + si) * N0) * R + rr] = (a[0] + a[1]) + (a[2] + a[3]);
     }
     for (int e = threadIdx.x; e < ns * P; e += blockDim.x) {   // dvb[j, pp]
       const int si = e / P, pp = e % P;
-      float a = 0.f;
-      for (int rr = 0; rr < R; ++rr) a = fmaf(sdf[rr * P + pp], sp[si * R + rr], a);
-      dvb[(row0 + static_cast<int64_t>(s0 + si) * N0) * P + pp] = a;
+      float a[4] = {0.f, 0.f, 0.f, 0.f};
+      int rr = 0;
+      for (; rr + 4 <= R; rr += 4)
+#pragma unroll
+        for (int u = 0; u < 4; ++u)
+          a[u] = fmaf(sdf[(rr + u) * P + pp], sp[si * R + rr + u], a[u]);
+      for (; rr < R; ++rr) a[0] = fmaf(sdf[rr * P + pp], sp[si * R + rr], a[0]);
+      dvb[(row0 + static_cast<int64_t>(s0 + si) * N0) * P + pp] = (a[0] + a[1]) + (a[2] + a[3]);
     }
   }
 }
