@@ -63,6 +63,16 @@ SMAT_API int smat_kattn_incidence(const float* F, const int64_t* ptr, const int3
                          float* U, int nb, int N_in, int N_out, int RP,
                          int32_t* err_word, void* stream);
 
+/* One streaming-decode token of the kernelised op for nb sequences
+ * (SmatDecoder.step, attention.py:521-527): S[b] += psi[b] vb[b]^T, then
+ * o = phi[b]^T (S[b] + U[b, h]) and out[b, c] = o[c] / o[P - 1] for c < P - 1.
+ * phi, psi [nb, R]; vb [nb, P]; S [nb, R, P] (updated in place);
+ * U [nb, nU, R, P] (the prefill's type table); out [nb, P - 1]; h the
+ * token's type (its step index mod nU).  R, P <= 1024. */
+SMAT_API int smat_kattn_decode_step(const float* phi, const float* psi, const float* vb,
+                           float* S, const float* U, float* out, int nb, int R, int P,
+                           int nU, int h, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -17,7 +17,10 @@ pooled schedule of ``smat.attention.smat_attention``
   ``:310-330``);
 * the endpoint family's landmark block by the subset-sum (zeta) transform
   (``:364-381``, ``:432-441``);
-* one division by the last column.
+* one division by the last column;
+* the streaming decoder (``SmatDecoder``, ``attention.py:496-535``): the type
+  table ``U`` from the prefix, then per token ``S += Psi_t Vb_t^T`` and
+  ``Phi_t^T (S + U_{i mod B})``, divided by its last column.
 
 Only the tests import this module; the product path is
 ``smat_attention_b200.kernel_attention``.
@@ -28,7 +31,7 @@ from __future__ import annotations
 import torch
 
 __all__ = ["chunk_local", "segmented_causal_scan", "pool_profiles", "apply_incidence",
-           "query_by_type", "zeta_transform", "smat_attention"]
+           "query_by_type", "zeta_transform", "smat_attention", "SmatDecoder"]
 
 
 def chunk_local(Phi_c, Psi_c, Vb_c, Sin):
@@ -116,3 +119,28 @@ def smat_attention(Phi, Psi, Vb, spec, chunk: int = 128):
         H = segmented_causal_scan(Phi, Psi, Vb, n, chunk)
         H = torch.cat([H[:, :n], H[:, n:] + Y_lr], dim=1)
     return H[..., :-1] / H[..., -1:]
+
+
+class SmatDecoder:
+    """Streaming decode over a pooled prefix (``attention.py:496-535``), in the
+    dtype of its inputs."""
+
+    def __init__(self, Psi_prefix, Vb_prefix, spec):
+        self.spec = spec
+        U = apply_incidence(pool_profiles(Psi_prefix, Vb_prefix, spec), spec)
+        if spec.n_P:
+            U = U + (Psi_prefix[:, :spec.n_P].transpose(-1, -2)
+                     @ Vb_prefix[:, :spec.n_P]).unsqueeze(1)
+        self.U = U
+        nb, _, r = Psi_prefix.shape
+        self.S = torch.zeros(nb, r, Vb_prefix.shape[-1], dtype=Psi_prefix.dtype)
+        self.i = 0
+
+    def step(self, Phi_t, Psi_t, Vb_t):
+        self.S = self.S + Psi_t.unsqueeze(-1) * Vb_t.unsqueeze(-2)
+        o = (Phi_t.unsqueeze(-2) @ (self.S + self.U[:, self.i % self.spec.B])).squeeze(-2)
+        self.i += 1
+        return o[..., :-1] / o[..., -1:]
+
+    def cache_words(self) -> int:
+        return int(self.S.numel() + self.U.numel())

@@ -482,6 +482,50 @@ __global__ void __launch_bounds__(256) kattn_incidence_kernel(
   }
 }
 
+// ---------------------------------------------------------------- streaming decode
+// One token for every sequence b (SmatDecoder.step, attention.py:521-527):
+// S_b += psi_b vb_b^T, o_b = phi_b^T (S_b + U_b[h]), out_b = o_b[:P-1] / o_b[P-1].
+// One CTA per b; thread (rg, c) walks rows rg, rg + 4, ... of column c, so
+// every S / U access is a coalesced 256-byte row segment read once.
+constexpr int DEC_THREADS = 256, DEC_MAX_RP = 1024;
+__global__ void __launch_bounds__(DEC_THREADS)
+    kattn_decode_kernel(const float* __restrict__ phi, const float* __restrict__ psi,
+                        const float* __restrict__ vb, float* __restrict__ S,
+                        const float* __restrict__ U, float* __restrict__ out, int R, int P,
+                        int nU, int h) {
+  extern __shared__ float dsm[];  // phi[R] | psi[R] | part[4][P]
+  float* sphi = dsm;
+  float* spsi = dsm + R;
+  float* part = dsm + 2 * R;
+  const int64_t b = blockIdx.x;
+  const int tid = threadIdx.x;
+  for (int a = tid; a < R; a += DEC_THREADS) {
+    sphi[a] = phi[b * R + a];
+    spsi[a] = psi[b * R + a];
+  }
+  __syncthreads();
+  const int rg = tid >> 6, cl = tid & 63;
+  float* Sb = S + b * R * P;
+  const float* Ub = U + (b * nU + h) * R * P;
+  for (int c = cl; c < P; c += 64) {
+    const float v = vb[b * P + c];
+    float acc = 0.f;
+    for (int a = rg; a < R; a += 4) {
+      const int64_t o = static_cast<int64_t>(a) * P + c;
+      const float sv = Sb[o] + spsi[a] * v;
+      Sb[o] = sv;
+      acc = fmaf(sphi[a], sv + Ub[o], acc);
+    }
+    part[rg * P + c] = acc;
+  }
+  __syncthreads();
+  for (int c = tid; c < P; c += DEC_THREADS)
+    part[c] = (part[c] + part[P + c]) + (part[2 * P + c] + part[3 * P + c]);
+  __syncthreads();
+  const float den = part[P - 1];
+  for (int c = tid; c < P - 1; c += DEC_THREADS) out[b * (P - 1) + c] = part[c] / den;
+}
+
 // ---------------------------------------------------------------- host
 PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
@@ -645,6 +689,19 @@ int smat_kattn_incidence(const float* F, const int64_t* ptr, const int32_t* idx,
   const dim3 grid(N_out, nb, (RP + 1023) / 1024);
   kattn_incidence_kernel<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(
       F, ptr, idx, U, N_in, N_out, RP, err_word);
+  return cudaGetLastError() == cudaSuccess ? SMAT_OK : SMAT_ERR_LAUNCH;
+}
+
+int smat_kattn_decode_step(const float* phi, const float* psi, const float* vb, float* S,
+                           const float* U, float* out, int nb, int R, int P, int nU, int h,
+                           void* stream) {
+  if (!phi || !psi || !vb || !S || !U || !out) return SMAT_ERR_NULL_POINTER;
+  if (nb < 1 || R < 1 || R > DEC_MAX_RP || P < 2 || P > DEC_MAX_RP || nU < 1 || h < 0 ||
+      h >= nU)
+    return SMAT_ERR_BAD_SHAPE;
+  const size_t smem = (2 * static_cast<size_t>(R) + 4 * static_cast<size_t>(P)) * sizeof(float);
+  kattn_decode_kernel<<<nb, DEC_THREADS, smem, static_cast<cudaStream_t>(stream)>>>(
+      phi, psi, vb, S, U, out, R, P, nU, h);
   return cudaGetLastError() == cudaSuccess ? SMAT_OK : SMAT_ERR_LAUNCH;
 }
 

@@ -19,6 +19,10 @@ with the three passes its Triton module fuses replaced by kernels of
 ``incidence(F, plane_pts, B)``
     ``U_h = sum_{x in H_h} F_x`` (``triton_fwd.py:161-222``) with the transposed
     table as its backward (``triton_bwd.py:281-316``), fp32 on CUDA cores.
+``SmatDecoder``
+    the streaming decoder (``attention.py:496-535``): the prefill builds the
+    type table ``U`` with ``pool`` and ``incidence``; each token is one launch
+    that updates the running sum ``S``, queries ``S + U_h`` and normalises.
 
 The scan summaries, the segmented prefix sums, the per-type query
 (``query_by_type``) and the endpoint's butterflies are batched library GEMMs
@@ -38,7 +42,7 @@ from .mask import MaskSpec
 
 __all__ = ["chunk_local", "pool", "incidence", "segmented_causal_scan", "pool_profiles",
            "apply_incidence", "query_by_type", "walsh_incidence", "zeta_transform",
-           "smat_attention"]
+           "smat_attention", "SmatDecoder"]
 
 _vp, _ci, _cl = ctypes.c_void_p, ctypes.c_int, ctypes.c_int64
 SIGNATURES = {
@@ -49,6 +53,8 @@ SIGNATURES = {
     "smat_kattn_pool_bwd": (_ci, [_vp, _vp, _vp, _vp, _vp, _ci, _ci, _ci, _ci, _ci, _ci, _ci,
                                   _vp]),
     "smat_kattn_incidence": (_ci, [_vp, _vp, _vp, _vp, _ci, _ci, _ci, _ci, _vp, _vp]),
+    "smat_kattn_decode_step": (_ci, [_vp, _vp, _vp, _vp, _vp, _vp, _ci, _ci, _ci, _ci, _ci,
+                                     _vp]),
 }
 CHUNK = 128
 _bound = None
@@ -327,3 +333,60 @@ def smat_attention(Phi, Psi, Vb, spec: MaskSpec, *, chunk: int = CHUNK, g=None):
     if g is not None:
         out = out * g.unsqueeze(-1).to(out.dtype)
     return out
+
+
+# ---------------------------------------------------------------- streaming decode
+class SmatDecoder:
+    """Exact autoregressive decoding at ``O(r p)`` per token (reference
+    ``SmatDecoder``, ``attention.py:496-535``).
+
+    Every landmark key precedes every recent query, so the type table
+    ``U_h`` is fixed once the prefix is pooled; token ``n + i`` is
+    ``Phi^T (U_{i mod B} + sum_{n < u <= n + i} Psi_u Vb_u^T)``.  The prefill
+    runs the ``pool`` and ``incidence`` kernels (plus the rank-one global term
+    for ``n_P > 0``); each :meth:`step` is one ``smat_kattn_decode_step``
+    launch over all ``nb`` sequences.  State and arithmetic are fp32;
+    ``acc_dtype`` other than fp32 is rejected (there is no CPU path)."""
+
+    def __init__(self, Psi_prefix, Vb_prefix, spec: MaskSpec, *, acc_dtype=None,
+                 incidence_backend: str = "auto"):
+        if acc_dtype not in (None, torch.float32):
+            raise ValueError("the decode kernel accumulates in fp32")
+        if spec.kind not in ("geometric", "endpoint"):
+            raise ValueError("SmatDecoder needs an M^(d) spec from build_mask")
+        self.spec = spec
+        self.acc = torch.float32
+        nb, _, r = Psi_prefix.shape
+        p = Vb_prefix.shape[-1]
+        self.nb, self.r, self.p = nb, r, p
+        F = pool_profiles(Psi_prefix, Vb_prefix, spec)
+        U = apply_incidence(F, spec)
+        if spec.n_P:
+            b = (Psi_prefix[:, :spec.n_P].float().transpose(-1, -2)
+                 @ Vb_prefix[:, :spec.n_P].float())
+            U = U + b.unsqueeze(1)
+        self.U = U.float().contiguous()
+        self.S = torch.zeros(nb, r, p, device=Psi_prefix.device, dtype=torch.float32)
+        self.i = 0
+
+    def step(self, Phi_t, Psi_t, Vb_t):
+        """One token: ``Phi_t, Psi_t (nb, r)``, ``Vb_t (nb, p)`` -> ``(nb, p - 1)`` fp32."""
+        phi, psi, vb = (_f32(x) for x in (Phi_t, Psi_t, Vb_t))
+        if phi.shape != (self.nb, self.r) or psi.shape != (self.nb, self.r) \
+                or vb.shape != (self.nb, self.p):
+            raise ValueError("step expects Phi_t, Psi_t (nb, r) and Vb_t (nb, p)")
+        out = torch.empty(self.nb, self.p - 1, dtype=torch.float32, device=phi.device)
+        nU = self.U.shape[1]
+        _lib.check("smat_kattn_decode_step", _L().smat_kattn_decode_step(
+            phi.data_ptr(), psi.data_ptr(), vb.data_ptr(), self.S.data_ptr(),
+            self.U.data_ptr(), out.data_ptr(), self.nb, self.r, self.p, nU,
+            self.i % self.spec.B, _stream(phi)))
+        self.i += 1
+        return out
+
+    def cache_words(self) -> int:
+        return int(self.S.numel() + self.U.numel())
+
+    @staticmethod
+    def kv_cache_words(nb: int, T: int, d_v: int) -> int:
+        return int(nb * 2 * T * d_v)

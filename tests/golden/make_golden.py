@@ -24,7 +24,10 @@ It imports the reference's ``smat`` package (``src/smat``) and records
 ``kattn_<case>.npz``
     The reference's kernelised op ``smat_attention`` on its torch path (fp64)
     for ``M^(d)`` masks: inputs, output, autograd gradients and the pooled
-    intermediates ``F`` (profiles) and ``U`` (per row type), the latter two as fp32.
+    intermediates ``F`` (profiles) and ``U`` (per row type), the latter two as fp32,
+    and the outputs of its streaming decoder ``SmatDecoder``
+    (``src/smat/attention.py:496-535``) prefilled with the first ``n`` columns
+    and stepped through rows ``n .. T-1`` (fp64; ``dec``).
 
 Nothing at test time imports the reference: the tests read only these files.
 """
@@ -148,11 +151,16 @@ def make_kattn(A, R, name, T, d, chunk, n_P, nb, r, dv, seed):
         Vb0 = torch.cat([v.double(), torch.ones(nb, T, 1, dtype=torch.float64)], dim=-1)
         F = A.pool_profiles(Psi, Vb0, spec, backend="torch")
         U = A.apply_incidence(F, spec, backend="torch")
+        n = spec.n
+        dec = A.SmatDecoder(Psi[:, :n], Vb0[:, :n], spec, incidence_backend="torch")
+        dec_out = torch.stack([dec.step(Phi[:, i], Psi[:, i], Vb0[:, i]) for i in range(n, T)],
+                              dim=1)
     np.savez_compressed(
         os.path.join(HERE, f"kattn_{name}.npz"),
         args=np.array([T, d, chunk, n_P]), phi=Phi.float().numpy(), psi=Psi.float().numpy(),
         v=v.numpy(), dout=dout.numpy(), out=out.detach().numpy(), dphi=Pg.grad.numpy(),
-        dpsi=Sg.grad.numpy(), dv=Vg.grad.numpy(), F=F.float().numpy(), U=U.float().numpy())
+        dpsi=Sg.grad.numpy(), dv=Vg.grad.numpy(), F=F.float().numpy(), U=U.float().numpy(),
+        dec=dec_out.numpy(), dec_words=np.array([dec.cache_words()]))
 
 
 def main():

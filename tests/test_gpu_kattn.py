@@ -136,3 +136,44 @@ def test_rejects(cuda_device):
                        torch.zeros(1, 1, 32, 9, device=cuda_device))     # C = 64
     with pytest.raises(ValueError):
         KA.chunk_local(*(t.cpu() for t in (x, x, x, x)))
+
+
+@pytest.mark.parametrize("path", sorted(glob.glob(os.path.join(os.path.dirname(__file__),
+                                                                 "golden", "kattn_*.npz"))),
+                         ids=lambda p: os.path.basename(p)[6:-4])
+def test_decoder_matches_reference_fixture(cuda_device, path):
+    """``SmatDecoder`` on the decode kernel against the reference's own
+    ``SmatDecoder`` outputs (fp64) for rows n .. T-1, stepping one token per
+    launch; fp32 state and arithmetic, held to 1e-4 of the largest output."""
+    f = np.load(path)
+    T, d, chunk, n_P = (int(x) for x in f["args"])
+    spec = build_mask(T, d, chunk=chunk, n_P=n_P)
+    phi, psi, v = (torch.from_numpy(f[k]).to(cuda_device) for k in ("phi", "psi", "v"))
+    Vb = torch.cat([v, torch.ones(*v.shape[:-1], 1, device=cuda_device)], dim=-1)
+    n = spec.n
+    dec = KA.SmatDecoder(psi[:, :n], Vb[:, :n], spec)
+    got = torch.stack([dec.step(phi[:, i], psi[:, i], Vb[:, i]) for i in range(n, T)], dim=1)
+    torch.cuda.synchronize()
+    assert check_device_errors() == 0
+    _close(got, torch.from_numpy(f["dec"]), 1e-4, "dec")
+    assert dec.cache_words() == int(f["dec_words"][0])
+
+
+def test_decoder_matches_oracle_wide(cuda_device):
+    """A wider state (r = 128, p = 129) than the fixtures, against the oracle."""
+    T, d, r, dv = 2048, 3, 128, 128
+    spec = build_mask(T, d, chunk=64)
+    g = torch.Generator().manual_seed(17)
+    nb = 3
+    Phi, Psi = _feat(nb, T, r, g=g).float(), _feat(nb, T, r, g=g).float()
+    Vb = torch.cat([torch.randn(nb, T, dv, generator=g), torch.ones(nb, T, 1)], dim=-1)
+    n = spec.n
+    ref = OK.SmatDecoder(Psi[:, :n].double(), Vb[:, :n].double(), spec)
+    dec = KA.SmatDecoder(Psi[:, :n].to(cuda_device), Vb[:, :n].to(cuda_device), spec)
+    for i in range(n, min(T, n + 300)):
+        got = dec.step(*(x[:, i].to(cuda_device) for x in (Phi, Psi, Vb)))
+        want = ref.step(Phi[:, i].double(), Psi[:, i].double(), Vb[:, i].double())
+        _close(got, want, 1e-4, f"row {i}")
+    with pytest.raises(ValueError):
+        dec.step(Phi[:, 0].to(cuda_device), Psi[:, 0].to(cuda_device),
+                 Vb[:, 0, :5].to(cuda_device))

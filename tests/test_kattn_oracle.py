@@ -39,6 +39,25 @@ def test_oracle_matches_reference(path):
     assert np.abs(U.numpy() - f["U"]).max() <= 1e-5 * (1 + np.abs(f["U"]).max())
 
 
+@pytest.mark.parametrize("path", CASES, ids=[os.path.basename(c)[6:-4] for c in CASES])
+def test_oracle_decoder_matches_reference(path):
+    """The oracle's streaming decoder against the reference's ``SmatDecoder``
+    outputs (rows n .. T-1) and cache size; for the geometric family it also
+    reproduces the prefill rows, as the reference's test_smat.py:327-342 checks."""
+    f = np.load(path)
+    T, d, chunk, n_P = (int(x) for x in f["args"])
+    spec = build_mask(T, d, chunk=chunk, n_P=n_P)
+    phi, psi, v = (torch.from_numpy(f[k]).double() for k in ("phi", "psi", "v"))
+    Vb = torch.cat([v, torch.ones(*v.shape[:-1], 1, dtype=torch.float64)], dim=-1)
+    n = spec.n
+    dec = OK.SmatDecoder(psi[:, :n], Vb[:, :n], spec)
+    got = torch.stack([dec.step(phi[:, i], psi[:, i], Vb[:, i]) for i in range(n, T)], dim=1)
+    assert np.abs(got.numpy() - f["dec"]).max() < 1e-11
+    assert dec.cache_words() == int(f["dec_words"][0])
+    if spec.kind == "geometric":
+        assert np.abs(f["dec"] - f["out"][:, n:]).max() < 1e-11
+
+
 def test_chunk_local_definition():
     g = torch.Generator().manual_seed(0)
     Phi, Psi = (torch.rand(1, 2, 8, 3, generator=g, dtype=torch.float64) for _ in range(2))
