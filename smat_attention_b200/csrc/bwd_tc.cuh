@@ -84,6 +84,8 @@ struct BwdCfg {
   static constexpr int SMEM_BYTES = OFF_MISC + 16 + 1024;
   static_assert(SMEM_BYTES <= 227 * 1024, "shared memory budget");
   static_assert(STAGES >= 2, "at least two stages");
+  // the epilogue stages the output tile(s) in the chunk buffers of C0
+  static_assert((DKDV ? 2 : 1) * ROW_BYTES <= STAGES * CH_BYTES, "epilogue staging");
   // TMEM: S | dP | accumulators.  S and dP read both operands from shared
   // memory: with N = 128 an MMA costs the same with A in shared memory or
   // in TMEM.
@@ -108,7 +110,9 @@ __global__ void __launch_bounds__(BwdCfg<DKDV, D>::THREADS, 1)
     smat_bwd_tc_kernel(const __grid_constant__ CUtensorMap tm_r0,
                        const __grid_constant__ CUtensorMap tm_r1,
                        const __grid_constant__ CUtensorMap tm_c0,
-                       const __grid_constant__ CUtensorMap tm_c1, const BwdParams p) {
+                       const __grid_constant__ CUtensorMap tm_c1,
+                       const __grid_constant__ CUtensorMap tm_o0,
+                       const __grid_constant__ CUtensorMap tm_o1, const BwdParams p) {
   using C = BwdCfg<DKDV, D>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
@@ -464,23 +468,21 @@ __global__ void __launch_bounds__(BwdCfg<DKDV, D>::THREADS, 1)
       if (lane == 0) mbar_arrive(bar(C::BAR_DSR));
     }
     // ------------------------------------------------------------ epilogue
+    // The accumulators leave through shared memory: each thread writes its
+    // row's bf16 values into the SW128 layout of the output tensor maps (the
+    // chunk stages are free once the last MMA has completed), then one thread
+    // stores the tiles with TMA.  Stored row by row from registers, every warp
+    // instruction would touch 32 rows, i.e. 32 cache lines.
     if (alive && n > 0 &&
         !__all_sync(0xffffffffu, mbar_wait(bar(C::BAR_AD), 0, abort_flag, p.err)))
       alive = false;
     if (alive) {
       tc_fence_after();
-      const bool store = pos < p.T;
-      __nv_bfloat16* o0 = p.out0 + static_cast<int64_t>(b) * p.o0_sb +
-                          static_cast<int64_t>(h) * p.o0_sh + static_cast<int64_t>(pos) * p.o0_st;
-      __nv_bfloat16* o1 = DKDV ? p.out1 + static_cast<int64_t>(b) * p.o1_sb +
-                                     static_cast<int64_t>(h) * p.o1_sh +
-                                     static_cast<int64_t>(pos) * p.o1_st
-                               : nullptr;
       constexpr int EW = D / 4;   // accumulator columns per warp group
 #pragma unroll
       for (int acc = 0; acc < (DKDV ? 2 : 1); ++acc) {
-        __nv_bfloat16* dst = acc == 0 ? o0 : o1;
         const float mul = acc == 0 ? p.scale : 1.f;  // dK and dQ carry the softmax scale
+        const uint32_t stage = sbase + C::OFF_C0 + acc * C::ROW_BYTES;
 #pragma unroll
         for (int cc = grp * EW; cc < (grp + 1) * EW; cc += 16) {
           float v[16];
@@ -490,18 +492,31 @@ __global__ void __launch_bounds__(BwdCfg<DKDV, D>::THREADS, 1)
 #pragma unroll
             for (int i = 0; i < 16; ++i) v[i] = 0.f;
           }
-          if (store) {
 #pragma unroll
-            for (int i = 0; i < 16; i += 8) {
-              uint4 w = make_uint4(pack_bf16(v[i] * mul, v[i + 1] * mul),
-                                   pack_bf16(v[i + 2] * mul, v[i + 3] * mul),
-                                   pack_bf16(v[i + 4] * mul, v[i + 5] * mul),
-                                   pack_bf16(v[i + 6] * mul, v[i + 7] * mul));
-              *reinterpret_cast<uint4*>(dst + cc + i) = w;
-            }
+          for (int i = 0; i < 16; i += 8) {
+            const int col = cc + i;   // 8 columns = one 16-byte unit of the 128-byte row
+            const uint32_t addr = stage + (col >> 6) * C::PANEL_R + r * 128 +
+                                  ((((col & 63) >> 3) ^ (r & 7)) << 4);
+            st_shared_v4(addr, make_uint4(pack_bf16(v[i] * mul, v[i + 1] * mul),
+                                          pack_bf16(v[i + 2] * mul, v[i + 3] * mul),
+                                          pack_bf16(v[i + 4] * mul, v[i + 5] * mul),
+                                          pack_bf16(v[i + 6] * mul, v[i + 7] * mul)));
           }
         }
       }
+      fence_proxy_async_smem();
+    }
+    named_barrier_sync(1, C::NCW * 32);
+    if (tid == 0 && !*abort_flag) {
+#pragma unroll
+      for (int acc = 0; acc < (DKDV ? 2 : 1); ++acc)
+#pragma unroll
+        for (int pn = 0; pn < D / 64; ++pn)
+          tma_store_4d(acc == 0 ? &tm_o0 : &tm_o1,
+                       sbase + C::OFF_C0 + acc * C::ROW_BYTES + pn * C::PANEL_R, pn * 64,
+                       tile * C::BM, h, b);
+      bulk_commit_group();
+      bulk_wait_read_all();   // the source must stay valid until it has been read
     }
   }
 

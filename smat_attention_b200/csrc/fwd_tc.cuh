@@ -95,7 +95,8 @@ template <int D>
 __global__ void __launch_bounds__(320, 1)
     smat_fwd_tc_kernel(const __grid_constant__ CUtensorMap tm_q,
                        const __grid_constant__ CUtensorMap tm_k,
-                       const __grid_constant__ CUtensorMap tm_v, const FwdParams p) {
+                       const __grid_constant__ CUtensorMap tm_v,
+                       const __grid_constant__ CUtensorMap tm_o, const FwdParams p) {
   using C = FwdCfg<D>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
@@ -438,11 +439,17 @@ __global__ void __launch_bounds__(320, 1)
     if (alive && cnt > 0 &&
         !__all_sync(0xffffffffu, mbar_wait(bar(C::BAR_PV + x), (cnt - 1) & 1, abort_flag, p.err)))
       alive = false;
+    // O leaves through shared memory: each thread writes its row in the SW128
+    // layout of the output tensor map into its tile's Q buffer (free once the
+    // tile's last MMA has completed; a tile without chunks first lets its Q
+    // load land), then one thread per warpgroup stores the tile with TMA.
+    if (alive && cnt == 0 &&
+        !__all_sync(0xffffffffu, mbar_wait(bar(C::BAR_Q), 0, abort_flag, p.err)))
+      alive = false;
+    const uint32_t stage = sbase + C::OFF_Q + x * C::Q_BYTES;
     if (alive) {
       tc_fence_after();
       const float inv = (l > 0.f) ? 1.f / l : 0.f;
-      __nv_bfloat16* orow = p.o + static_cast<int64_t>(b) * p.o_sb +
-                            static_cast<int64_t>(h) * p.o_sh + static_cast<int64_t>(q_pos) * p.o_st;
 #pragma unroll
       for (int cc = 0; cc < D; cc += 32) {
         float ov[32];
@@ -452,20 +459,29 @@ __global__ void __launch_bounds__(320, 1)
 #pragma unroll
           for (int i = 0; i < 32; ++i) ov[i] = 0.f;
         }
-        if (store) {
 #pragma unroll
-          for (int i = 0; i < 32; i += 8) {
-            uint4 w = make_uint4(pack_bf16(ov[i] * inv, ov[i + 1] * inv),
-                                 pack_bf16(ov[i + 2] * inv, ov[i + 3] * inv),
-                                 pack_bf16(ov[i + 4] * inv, ov[i + 5] * inv),
-                                 pack_bf16(ov[i + 6] * inv, ov[i + 7] * inv));
-            *reinterpret_cast<uint4*>(orow + cc + i) = w;
-          }
+        for (int i = 0; i < 32; i += 8) {
+          const int col = cc + i;   // 8 columns = one 16-byte unit of the 128-byte row
+          const uint32_t addr = stage + (col >> 6) * C::PANEL_Q + r * 128 +
+                                ((((col & 63) >> 3) ^ (r & 7)) << 4);
+          st_shared_v4(addr, make_uint4(pack_bf16(ov[i] * inv, ov[i + 1] * inv),
+                                        pack_bf16(ov[i + 2] * inv, ov[i + 3] * inv),
+                                        pack_bf16(ov[i + 4] * inv, ov[i + 5] * inv),
+                                        pack_bf16(ov[i + 6] * inv, ov[i + 7] * inv)));
         }
       }
+      fence_proxy_async_smem();
       if (store)
         p.lse[static_cast<int64_t>(bh) * p.T + q_pos] =
             (l > 0.f) ? (m + __log2f(l)) * 0.69314718055994531f : -INFINITY;
+    }
+    named_barrier_sync(1 + x, 128);
+    if ((warp & 3) == 0 && lane == 0 && x < ntile && !*abort_flag) {
+#pragma unroll
+      for (int pn = 0; pn < D / 64; ++pn)
+        tma_store_4d(&tm_o, stage + pn * C::PANEL_Q, pn * 64, (tile0 + x) * C::BM, h, b);
+      bulk_commit_group();
+      bulk_wait_read_all();   // the source must stay valid until it has been read
     }
   }
 

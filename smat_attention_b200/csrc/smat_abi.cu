@@ -179,9 +179,10 @@ int fwd_tc(const TArg& q, const TArg& k, const TArg& v, const TArg& o, float* ls
            int nblocks, int64_t nnzb, int block, float scale, const Work& work,
            const MdPattern& md, int32_t* err, cudaStream_t s) {
   using C = FwdCfg<D>;
-  CUtensorMap mq, mk, mv;
+  CUtensorMap mq, mk, mv, mo;
   int rc;
   if ((rc = make_map(&mq, q, B, H, T, D, C::BM))) return rc;
+  if ((rc = make_map(&mo, o, B, H, T, D, C::BM))) return rc;   // O is stored by TMA
   if ((rc = make_map(&mk, k, B, H, T, D, C::BOX))) return rc;
   if ((rc = make_map(&mv, v, B, H, T, D, C::BOX))) return rc;
   FwdParams p{};
@@ -209,7 +210,7 @@ int fwd_tc(const TArg& q, const TArg& k, const TArg& v, const TArg& o, float* ls
   if ((rc = set_smem(kern, C::SMEM_BYTES))) return rc;
   const int64_t grid = static_cast<int64_t>(work.items ? work.n : p.n_pairs) * B * H;
   if (grid == 0) return SMAT_OK;
-  kern<<<static_cast<unsigned>(grid), C::THREADS, C::SMEM_BYTES, s>>>(mq, mk, mv, p);
+  kern<<<static_cast<unsigned>(grid), C::THREADS, C::SMEM_BYTES, s>>>(mq, mk, mv, mo, p);
   return launch_status();
 }
 
@@ -295,12 +296,15 @@ int bwd_tc(const TArg& r0, const TArg& r1, const TArg& c0, const TArg& c1, const
            int64_t nnzb, int block, float scale, const Work& work, const MdPattern& md,
            int32_t* err, cudaStream_t s) {
   using C = BwdCfg<DKDV, D>;
-  CUtensorMap m0, m1, mc0, mc1;
+  CUtensorMap m0, m1, mc0, mc1, mo0, mo1;
   int rc;
   if ((rc = make_map(&m0, r0, B, H, T, D, C::BM))) return rc;
   if ((rc = make_map(&m1, r1, B, H, T, D, C::BM))) return rc;
   if ((rc = make_map(&mc0, c0, B, H, T, D, C::BOX))) return rc;
   if ((rc = make_map(&mc1, c1, B, H, T, D, C::BOX))) return rc;
+  // the outputs are stored by TMA from the SW128 tile layout
+  if ((rc = make_map(&mo0, out0, B, H, T, D, C::BM))) return rc;
+  if ((rc = make_map(&mo1, out1 ? *out1 : out0, B, H, T, D, C::BM))) return rc;
   BwdParams p{};
   p.indptr = indptr;
   p.indices = indices;
@@ -333,7 +337,8 @@ int bwd_tc(const TArg& r0, const TArg& r1, const TArg& c0, const TArg& c1, const
   if ((rc = set_smem(kern, C::SMEM_BYTES))) return rc;
   const int64_t grid = static_cast<int64_t>(work.items ? work.n : p.n_tiles) * B * H;
   if (grid == 0) return SMAT_OK;
-  kern<<<static_cast<unsigned>(grid), C::THREADS, C::SMEM_BYTES, s>>>(m0, m1, mc0, mc1, p);
+  kern<<<static_cast<unsigned>(grid), C::THREADS, C::SMEM_BYTES, s>>>(m0, m1, mc0, mc1, mo0, mo1,
+                                                                       p);
   return launch_status();
 }
 
