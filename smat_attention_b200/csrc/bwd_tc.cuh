@@ -184,8 +184,7 @@ __global__ void __launch_bounds__(BwdCfg<DKDV, D>::THREADS, 1)
     // Lane 0 issues the TMA loads; for dK/dV all 32 lanes also copy the
     // chunk's lse and delta next to it with cp.async, tracked by the same
     // stage barrier, so nobody waits on a global load.
-    ChunkPair<2> it;
-    it.init(p.indptr, p.indices, p.kind, p.nblocks, p.nnzb, row0, sub, p.bs, p.err);
+    // the resident tiles first: they do not depend on the schedule reads
     if (lane == 0) {
       mbar_expect_tx(bar(C::BAR_R), 2 * C::ROW_BYTES);
 #pragma unroll
@@ -196,6 +195,8 @@ __global__ void __launch_bounds__(BwdCfg<DKDV, D>::THREADS, 1)
                     tile * C::BM, h, b);
       }
     }
+    ChunkPair<2> it;
+    it.init(p.indptr, p.indices, p.kind, p.nblocks, p.nnzb, row0, sub, p.bs, p.err);
     int issued = 0;
     uint32_t e[2];
     for (int j = 0; it.next(e, p.err); ++j) {

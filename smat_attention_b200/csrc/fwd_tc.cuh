@@ -177,8 +177,7 @@ __global__ void __launch_bounds__(320, 1)
       const int full = kl ? C::BAR_KF : C::BAR_VF, empty = kl ? C::BAR_KE : C::BAR_VE;
       const uint32_t ring = sbase + (kl ? C::OFF_K : C::OFF_V);
       const CUtensorMap* tm = kl ? &tm_k : &tm_v;
-      ChunkPair<4> it;
-      it.init(p.indptr, p.indices, p.kind, p.nblocks, p.nnzb, row0, ntile * sub, p.bs, p.err);
+      // the Q tiles first: they do not depend on the schedule reads
       if (kl) {
         mbar_expect_tx(bar(C::BAR_Q), C::NT * C::Q_BYTES);
 #pragma unroll
@@ -188,6 +187,8 @@ __global__ void __launch_bounds__(320, 1)
             tma_load_4d(sbase + C::OFF_Q + x * C::Q_BYTES + pn * C::PANEL_Q, &tm_q,
                         bar(C::BAR_Q), pn * 64, (tile0 + x) * C::BM, h, b);
       }
+      ChunkPair<4> it;
+      it.init(p.indptr, p.indices, p.kind, p.nblocks, p.nnzb, row0, ntile * sub, p.bs, p.err);
       int issued = 0;
       uint32_t e[2];
       for (int j = 0; it.next(e, p.err); ++j) {
