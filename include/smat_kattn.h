@@ -42,14 +42,16 @@ SMAT_API int smat_kattn_chunk_local_bwd(const float* phi, const float* psi, cons
 
 /* F[b, x] = sum_{j in [n_P, n), (j - n_P) mod N0 = x} psi[b, j] vb[b, j]^T
  * (pool, triton_fwd.py:225-311): psi [nb, T, R], vb [nb, T, P], F [nb, N0, R, P];
- * 64 (R + P) floats of staging <= 96 KB.  Exact fp32 FMAs. */
+ * shared staging of 64 (R4 + S) + R4 S floats <= 200 KB (R4 = R rounded up to
+ * 4, S = P rounded up to 4 with an odd count of 4-float units).  fp32 FMAs,
+ * columns in order. */
 SMAT_API int smat_kattn_pool_fwd(const float* psi, const float* vb, float* F, int nb, int T,
                         int R, int P, int n_P, int n, int N0, void* stream);
 
 /* Its backward (triton_bwd.py:203-278): for every column j of profile x,
  * dpsi[b, j] = dF[b, x] vb[b, j], dvb[b, j] = dF[b, x]^T psi[b, j]; rows outside
- * [n_P, n) are not written (the caller zeroes them).  (R P + 64 (R + P)) floats
- * of staging <= 96 KB. */
+ * [n_P, n) are not written (the caller zeroes them).  (R S + 64 (R + S)) floats
+ * of staging <= 200 KB, S as above. */
 SMAT_API int smat_kattn_pool_bwd(const float* psi, const float* vb, const float* dF,
                         float* dpsi, float* dvb, int nb, int T, int R, int P, int n_P,
                         int n, int N0, void* stream);

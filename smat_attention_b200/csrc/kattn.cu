@@ -328,112 +328,188 @@ __global__ void __launch_bounds__(192, 1)
 
 // ---------------------------------------------------------------- pool
 // One CTA per (profile x, b).  The profile's columns (about n_X / N0, 16 at
-// c3 sizes) are staged in shared memory; each thread then owns 4
-// consecutive outputs of F_x per pass over the R P outputs.
+// c3 sizes) are staged in shared memory -- psi rows [POOL_MAXG][RR] and vb
+// rows [POOL_MAXG][SP], zero-padded to multiples of 4 -- and each thread
+// accumulates 4 x 4 tiles of the R x P outer-product sum in registers (two
+// 16-byte shared loads per 16 FMAs, columns in order, so the sum is the same
+// sequence of fmaf as a scalar loop).  The tile goes back to global memory
+// through shared memory as one contiguous run of R P floats.
 constexpr int POOL_MAXG = 64;   // columns staged per round
+constexpr int POOL_SMEM_MAX = 200 * 1024;
+
+// Row stride of a zero-padded shared row of P floats: a multiple of 4 whose
+// count of 16-byte units is odd, so 8 consecutive rows hit 8 distinct bank
+// groups.
+__host__ __device__ inline int pool_stride(int P) {
+  int sp = (P + 3) & ~3;
+  if (((sp >> 2) & 1) == 0) sp += 4;
+  return sp;
+}
 
 __global__ void __launch_bounds__(256) kattn_pool_kernel(const float* __restrict__ psi,
                                                          const float* __restrict__ vb,
                                                          float* __restrict__ F, int T, int R,
                                                          int P, int n_P, int n, int N0) {
-  extern __shared__ float stage[];   // [POOL_MAXG][R] psi rows, then [POOL_MAXG][P] vb rows
+  extern __shared__ float4 stage4[];   // psi [MAXG][RR] | vb [MAXG][SP] | F_x [RR][SP]
+  float* stage = reinterpret_cast<float*>(stage4);
   const int x = blockIdx.x, b = blockIdx.y;
+  const int RR = (R + 3) & ~3, SP = pool_stride(P);
   float* sp = stage;
-  float* sv = stage + POOL_MAXG * R;
+  float* sv = sp + POOL_MAXG * RR;
+  float* so = sv + POOL_MAXG * SP;
   const int RP = R * P;
   const int n_X = n - n_P;
   const int g = x < n_X ? (n_X - x + N0 - 1) / N0 : 0;   // columns of this profile
   const float* pb = psi + static_cast<int64_t>(b) * T * R;
   const float* vbb = vb + static_cast<int64_t>(b) * T * P;
   float* fo = F + (static_cast<int64_t>(b) * N0 + x) * RP;
-  // rounds of up to POOL_MAXG staged columns (one round at the usual sizes);
-  // every pass over the outputs then reads the staged columns only
-  for (int s0 = 0; s0 == 0 || s0 < g; s0 += POOL_MAXG) {
-    const int ns = max(0, min(POOL_MAXG, g - s0));
+  const int cg = SP >> 2;                 // 4-column groups per row
+  const int ntile = (RR >> 2) * cg;
+  for (int e = threadIdx.x; e < RR * SP; e += blockDim.x) so[e] = 0.f;
+  // rounds of up to POOL_MAXG staged columns (one round at the usual sizes)
+  for (int s0 = 0; s0 < g; s0 += POOL_MAXG) {
+    const int ns = min(POOL_MAXG, g - s0);
     __syncthreads();
-    for (int e = threadIdx.x; e < ns * R; e += blockDim.x) {
-      const int si = e / R, c = e % R;
-      sp[si * R + c] = pb[static_cast<int64_t>(n_P + x + (s0 + si) * N0) * R + c];
+    // asynchronous 4-byte copies (zero-filled padding), all in flight at once
+    for (int e = threadIdx.x; e < ns * RR; e += blockDim.x) {
+      const int si = e / RR, c = e % RR;
+      const bool in = c < R;
+      cp_async4(smem_u32(sp + e),
+                in ? pb + static_cast<int64_t>(n_P + x + (s0 + si) * N0) * R + c : pb, in ? 4u : 0u);
     }
-    for (int e = threadIdx.x; e < ns * P; e += blockDim.x) {
-      const int si = e / P, c = e % P;
-      sv[si * P + c] = vbb[static_cast<int64_t>(n_P + x + (s0 + si) * N0) * P + c];
+    for (int e = threadIdx.x; e < ns * SP; e += blockDim.x) {
+      const int si = e / SP, c = e % SP;
+      const bool in = c < P;
+      cp_async4(smem_u32(sv + e),
+                in ? vbb + static_cast<int64_t>(n_P + x + (s0 + si) * N0) * P + c : vbb,
+                in ? 4u : 0u);
     }
+    asm volatile("cp.async.wait_all;" ::: "memory");
     __syncthreads();
-    for (int o0 = threadIdx.x * 4; o0 < RP; o0 += 1024) {
-      float acc[4];
-      int rr[4], pp[4];
+    for (int t = threadIdx.x; t < ntile; t += blockDim.x) {
+      const int r0 = (t / cg) * 4, c0 = (t % cg) * 4;
+      float acc[4][4];
 #pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        const int o = min(o0 + u, RP - 1);
-        rr[u] = o / P;
-        pp[u] = o % P;
-        acc[u] = (s0 > 0 && o0 + u < RP) ? fo[o0 + u] : 0.f;
+      for (int i = 0; i < 4; ++i) {
+        const float4 o = *reinterpret_cast<const float4*>(so + (r0 + i) * SP + c0);
+        acc[i][0] = o.x;
+        acc[i][1] = o.y;
+        acc[i][2] = o.z;
+        acc[i][3] = o.w;
       }
       for (int si = 0; si < ns; ++si) {
+        const float4 a = *reinterpret_cast<const float4*>(sp + si * RR + r0);
+        const float4 v = *reinterpret_cast<const float4*>(sv + si * SP + c0);
+        const float av[4] = {a.x, a.y, a.z, a.w}, vv[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
-        for (int u = 0; u < 4; ++u) acc[u] = fmaf(sp[si * R + rr[u]], sv[si * P + pp[u]], acc[u]);
+        for (int i = 0; i < 4; ++i)
+#pragma unroll
+          for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(av[i], vv[j], acc[i][j]);
       }
 #pragma unroll
-      for (int u = 0; u < 4; ++u)
-        if (o0 + u < RP) fo[o0 + u] = acc[u];
+      for (int i = 0; i < 4; ++i)
+        *reinterpret_cast<float4*>(so + (r0 + i) * SP + c0) =
+            make_float4(acc[i][0], acc[i][1], acc[i][2], acc[i][3]);
     }
   }
+  __syncthreads();
+  for (int o = threadIdx.x; o < RP; o += blockDim.x) fo[o] = so[(o / P) * SP + o % P];
 }
 
 // For every column j of profile x: dpsi_j = dF_x vb_j, dvb_j = dF_x^T psi_j.
-// One CTA per (x, b); dF_x and the profile's columns are staged in shared
-// memory, and the (column, row) pairs of both products are spread over the
-// threads.
+// One CTA per (x, b); dF_x [R][SP] and the profile's columns are staged in
+// shared memory (zero-padded as in the forward).  dpsi: a thread owns one row
+// rr of dF_x and four columns j, 16-byte loads along p; dvb: a thread owns four
+// p of one column j, one 16-byte dF load and one broadcast psi load per four
+// FMAs.  Staging is by asynchronous 4-byte copies.
 __global__ void __launch_bounds__(256) kattn_pool_bwd_kernel(
     const float* __restrict__ psi, const float* __restrict__ vb, const float* __restrict__ dF,
     float* __restrict__ dpsi, float* __restrict__ dvb, int T, int R, int P, int n_P, int n,
     int N0) {
-  extern __shared__ float sm[];   // dF [R][P], then psi [POOL_MAXG][R], vb [POOL_MAXG][P]
+  extern __shared__ float4 sm4[];   // dF [R][SP] | psi [MAXG][R] | vb [MAXG][SP]
+  float* sm = reinterpret_cast<float*>(sm4);
   const int x = blockIdx.x, b = blockIdx.y;
-  const int RP = R * P;
+  const int RP = R * P, SP = pool_stride(P), cg = SP >> 2;
   float* sdf = sm;
-  float* sp = sm + RP;
+  float* sp = sm + R * SP;
   float* sv = sp + POOL_MAXG * R;
   const float* df = dF + (static_cast<int64_t>(b) * N0 + x) * RP;
-  for (int e = threadIdx.x; e < RP; e += blockDim.x) sdf[e] = df[e];
   const int n_X = n - n_P;
   const int g = x < n_X ? (n_X - x + N0 - 1) / N0 : 0;
+  if (g == 0) return;   // a profile without columns has nothing to write
+  for (int e = threadIdx.x; e < R * SP; e += blockDim.x) {
+    const int rr = e / SP, c = e % SP;
+    const bool in = c < P;
+    cp_async4(smem_u32(sdf + e), in ? df + rr * P + c : df, in ? 4u : 0u);
+  }
   const int64_t row0 = static_cast<int64_t>(b) * T + n_P + x;
   for (int s0 = 0; s0 < g; s0 += POOL_MAXG) {
     const int ns = min(POOL_MAXG, g - s0);
+    const int nsb = (ns + 3) >> 2;   // blocks of four columns
     __syncthreads();
-    for (int e = threadIdx.x; e < ns * R; e += blockDim.x) {
+    for (int e = threadIdx.x; e < nsb * 4 * R; e += blockDim.x) {
       const int si = e / R, c = e % R;
-      sp[si * R + c] = psi[(row0 + static_cast<int64_t>(s0 + si) * N0) * R + c];
+      const bool in = si < ns;
+      cp_async4(smem_u32(sp + e),
+                in ? psi + (row0 + static_cast<int64_t>(s0 + si) * N0) * R + c : psi,
+                in ? 4u : 0u);
     }
-    for (int e = threadIdx.x; e < ns * P; e += blockDim.x) {
-      const int si = e / P, c = e % P;
-      sv[si * P + c] = vb[(row0 + static_cast<int64_t>(s0 + si) * N0) * P + c];
+    for (int e = threadIdx.x; e < nsb * 4 * SP; e += blockDim.x) {
+      const int si = e / SP, c = e % SP;
+      const bool in = si < ns && c < P;
+      cp_async4(smem_u32(sv + e),
+                in ? vb + (row0 + static_cast<int64_t>(s0 + si) * N0) * P + c : vb,
+                in ? 4u : 0u);
     }
+    asm volatile("cp.async.wait_all;" ::: "memory");
     __syncthreads();
-    // dot products with four independent partial sums (the chains are long
-    // and the CTA holds few warps)
-    for (int e = threadIdx.x; e < ns * R; e += blockDim.x) {   // dpsi[j, rr]
-      const int si = e / R, rr = e % R;
+    for (int e = threadIdx.x; e < nsb * R; e += blockDim.x) {   // dpsi[j, rr]
+      const int rr = e % R, sb = e / R;
       float a[4] = {0.f, 0.f, 0.f, 0.f};
-      int pp = 0;
-      for (; pp + 4 <= P; pp += 4)
+      for (int q = 0; q < cg; ++q) {
+        const float4 d = *reinterpret_cast<const float4*>(sdf + rr * SP + 4 * q);
 #pragma unroll
-        for (int u = 0; u < 4; ++u) a[u] = fmaf(sdf[rr * P + pp + u], sv[si * P + pp + u], a[u]);
-      for (; pp < P; ++pp) a[0] = fmaf(sdf[rr * P + pp], sv[si * P + pp], a[0]);
-      dpsi[(row0 + static_cast<int64_t>(s0 + si) * N0) * R + rr] = (a[0] + a[1]) + (a[2] + a[3]);
+        for (int i = 0; i < 4; ++i) {
+          const float4 v = *reinterpret_cast<const float4*>(sv + (4 * sb + i) * SP + 4 * q);
+          a[i] = fmaf(d.x, v.x, a[i]);
+          a[i] = fmaf(d.y, v.y, a[i]);
+          a[i] = fmaf(d.z, v.z, a[i]);
+          a[i] = fmaf(d.w, v.w, a[i]);
+        }
+      }
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+        if (4 * sb + i < ns)
+          dpsi[(row0 + static_cast<int64_t>(s0 + 4 * sb + i) * N0) * R + rr] = a[i];
     }
-    for (int e = threadIdx.x; e < ns * P; e += blockDim.x) {   // dvb[j, pp]
-      const int si = e / P, pp = e % P;
-      float a[4] = {0.f, 0.f, 0.f, 0.f};
+    for (int e = threadIdx.x; e < ns * cg; e += blockDim.x) {   // dvb[j, pp]
+      const int q = e % cg, si = e / cg;
+      float a[2][4] = {};   // even / odd rows: two independent chains
+      const float* pr = sp + si * R;
       int rr = 0;
-      for (; rr + 4 <= R; rr += 4)
+      for (; rr + 2 <= R; rr += 2) {
 #pragma unroll
-        for (int u = 0; u < 4; ++u)
-          a[u] = fmaf(sdf[(rr + u) * P + pp], sp[si * R + rr + u], a[u]);
-      for (; rr < R; ++rr) a[0] = fmaf(sdf[rr * P + pp], sp[si * R + rr], a[0]);
-      dvb[(row0 + static_cast<int64_t>(s0 + si) * N0) * P + pp] = (a[0] + a[1]) + (a[2] + a[3]);
+        for (int k = 0; k < 2; ++k) {
+          const float4 d = *reinterpret_cast<const float4*>(sdf + (rr + k) * SP + 4 * q);
+          const float pv = pr[rr + k];
+          a[k][0] = fmaf(pv, d.x, a[k][0]);
+          a[k][1] = fmaf(pv, d.y, a[k][1]);
+          a[k][2] = fmaf(pv, d.z, a[k][2]);
+          a[k][3] = fmaf(pv, d.w, a[k][3]);
+        }
+      }
+      if (rr < R) {
+        const float4 d = *reinterpret_cast<const float4*>(sdf + rr * SP + 4 * q);
+        const float pv = pr[rr];
+        a[0][0] = fmaf(pv, d.x, a[0][0]);
+        a[0][1] = fmaf(pv, d.y, a[0][1]);
+        a[0][2] = fmaf(pv, d.z, a[0][2]);
+        a[0][3] = fmaf(pv, d.w, a[0][3]);
+      }
+      float* dst = dvb + (row0 + static_cast<int64_t>(s0 + si) * N0) * P;
+#pragma unroll
+      for (int c = 0; c < 4; ++c)
+        if (4 * q + c < P) dst[4 * q + c] = a[0][c] + a[1][c];
     }
   }
 }
@@ -655,10 +731,11 @@ int smat_kattn_pool_fwd(const float* psi, const float* vb, float* F, int nb, int
   if (!psi || !vb || !F) return SMAT_ERR_NULL_POINTER;
   if (nb < 1 || T < 1 || R < 1 || P < 1 || N0 < 1 || n_P < 0 || n < n_P || n > T)
     return SMAT_ERR_BAD_SHAPE;
-  const int bytes = POOL_MAXG * (R + P) * 4;
-  if (bytes > 96 * 1024) return SMAT_ERR_BAD_SHAPE;
+  const int RR = (R + 3) & ~3, SP = pool_stride(P);
+  const int64_t bytes = (static_cast<int64_t>(POOL_MAXG) * (RR + SP) + RR * SP) * 4;
+  if (bytes > POOL_SMEM_MAX) return SMAT_ERR_BAD_SHAPE;
   if (cudaFuncSetAttribute(kattn_pool_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                           96 * 1024) != cudaSuccess)
+                           POOL_SMEM_MAX) != cudaSuccess)
     return SMAT_ERR_LAUNCH;
   kattn_pool_kernel<<<dim3(N0, nb), 256, bytes, static_cast<cudaStream_t>(stream)>>>(
       psi, vb, F, T, R, P, n_P, n, N0);
@@ -671,10 +748,11 @@ int smat_kattn_pool_bwd(const float* psi, const float* vb, const float* dF, floa
   if (!psi || !vb || !dF || !dpsi || !dvb) return SMAT_ERR_NULL_POINTER;
   if (nb < 1 || T < 1 || R < 1 || P < 1 || N0 < 1 || n_P < 0 || n < n_P || n > T)
     return SMAT_ERR_BAD_SHAPE;
-  const int bytes = (R * P + POOL_MAXG * (R + P)) * 4;
-  if (bytes > 96 * 1024) return SMAT_ERR_BAD_SHAPE;
+  const int SP = pool_stride(P);
+  const int64_t bytes = (static_cast<int64_t>(R) * SP + POOL_MAXG * (R + SP)) * 4;
+  if (bytes > POOL_SMEM_MAX) return SMAT_ERR_BAD_SHAPE;
   if (cudaFuncSetAttribute(kattn_pool_bwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                           96 * 1024) != cudaSuccess)
+                           POOL_SMEM_MAX) != cudaSuccess)
     return SMAT_ERR_LAUNCH;
   kattn_pool_bwd_kernel<<<dim3(N0, nb), 256, bytes, static_cast<cudaStream_t>(stream)>>>(
       psi, vb, dF, dpsi, dvb, T, R, P, n_P, n, N0);
