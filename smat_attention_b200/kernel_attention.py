@@ -242,11 +242,12 @@ def segmented_causal_scan(Phi, Psi, Vb, n: int, chunk: int = CHUNK):
     Phi_c, Psi_c = Phi.reshape(nb, nc, C, r), Psi.reshape(nb, nc, C, r)
     Vb_c = Vb.reshape(nb, nc, C, p)
     D = Psi_c.transpose(-1, -2) @ Vb_c                                  # (nb, nc, r, p)
-    parts = []
-    for lo, hi in ([(0, nc0), (nc0, nc)] if 0 < nc0 < nc else [(0, nc)]):
-        seg = torch.cumsum(D[:, lo:hi], dim=1)
-        parts.append(torch.cat([torch.zeros_like(seg[:, :1]), seg[:, :-1]], dim=1))
-    Sin = torch.cat(parts, dim=1)
+    # exclusive prefix sums inside each segment: inclusive cumsum minus D
+    if 0 < nc0 < nc:
+        Sin = torch.cat([torch.cumsum(D[:, :nc0], dim=1), torch.cumsum(D[:, nc0:], dim=1)],
+                        dim=1) - D
+    else:
+        Sin = torch.cumsum(D, dim=1) - D
     out = chunk_local(Phi_c, Psi_c, Vb_c, Sin)
     return out.reshape(nb, T + pad, p)[:, :T]
 
@@ -295,6 +296,21 @@ def query_by_type(Phi_rec, U, spec: MaskSpec):
     return torch.cat(pieces, dim=1)
 
 
+def _add_query_by_type(H_rec, Phi_rec, U, spec: MaskSpec):
+    """``H_rec += query_by_type(Phi_rec, U, spec)`` in place, with no
+    intermediate copy of the ``(nb, T_R, p)`` result."""
+    nb, T_R, r = Phi_rec.shape
+    B, p = spec.B, U.shape[-1]
+    U = U.float()
+    c, rem = divmod(T_R, B)
+    if c:
+        head = Phi_rec[:, :c * B].float().reshape(nb, c, B, r).transpose(1, 2)   # (nb,B,c,r)
+        H_rec[:, :c * B].view(nb, c, B, p).add_((head @ U).transpose(1, 2))
+    if rem:
+        tail = Phi_rec[:, c * B:].float().unsqueeze(-2)
+        H_rec[:, c * B:].add_((tail @ U[:, :rem]).squeeze(-2))
+
+
 def zeta_transform(F):
     """``(Z F)_a = sum_{x subset of a} F_x`` by a butterfly (reference
     ``attention.py:364-381``)."""
@@ -320,15 +336,15 @@ def smat_attention(Phi, Psi, Vb, spec: MaskSpec, *, chunk: int = CHUNK, g=None):
     if spec.n_P:
         b = Psi[:, :spec.n_P].float().transpose(-1, -2) @ Vb[:, :spec.n_P].float()
         U = U + b.unsqueeze(1)
-    Y_lr = query_by_type(Phi[:, n:], U, spec)
     if spec.kind == "endpoint":
+        Y_lr = query_by_type(Phi[:, n:], U, spec)
         Fz = Psi[:, :n].float().unsqueeze(-1) * Vb[:, :n].float().unsqueeze(-2)
         top = (Phi[:, :n].float().unsqueeze(-2) @ zeta_transform(Fz)).squeeze(-2)
         loc = segmented_causal_scan(Phi[:, n:], Psi[:, n:], Vb[:, n:], 0, chunk)
         H = torch.cat([top, loc + Y_lr], dim=1)
     else:
         H = segmented_causal_scan(Phi, Psi, Vb, n, chunk)
-        H = torch.cat([H[:, :n], H[:, n:] + Y_lr], dim=1)
+        _add_query_by_type(H[:, n:], Phi[:, n:], U, spec)
     out = H[..., :-1] / H[..., -1:]
     if g is not None:
         out = out * g.unsqueeze(-1).to(out.dtype)

@@ -85,6 +85,12 @@ def test_torch_parts_match_oracle():
     U = torch.randn(2, spec3.B, 5, 6, generator=g, dtype=torch.float64)
     assert torch.allclose(KA.query_by_type(Phi_rec, U, spec3).double(),
                           OK.query_by_type(Phi_rec, U, spec3), atol=1e-5)
+    # the in-place form the op uses on its chunk-pass output
+    H0 = torch.randn(2, spec3.T_R, 6, generator=g, dtype=torch.float64).float()
+    H1 = H0.clone()
+    KA._add_query_by_type(H1, Phi_rec.float(), U.float(), spec3)
+    assert torch.allclose(H1.double(), H0.double() + OK.query_by_type(Phi_rec, U, spec3),
+                          atol=1e-4)
     # the transposed CSR used by the incidence backward
     ptr = torch.from_numpy(spec3.C_indptr)
     idx = torch.from_numpy(spec3.C_indices)
