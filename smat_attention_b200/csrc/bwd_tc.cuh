@@ -262,22 +262,23 @@ __global__ void __launch_bounds__(BwdCfg<DKDV, D>::THREADS, 1)
         const uint32_t r = sbase + (dp ? C::OFF_R1 : C::OFF_R0);
         const uint32_t c = sbase + (dp ? C::OFF_C1 : C::OFF_C0) + s * C::CH_BYTES;
         const uint32_t d = tbase + (dp ? C::COL_DP : C::COL_S);
+        const uint64_t rd = sdesc_sw128(r, 16, 1024), cd = sdesc_sw128(c, 16, 1024);
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
           const uint32_t off = (kk >> 2) * C::PANEL_R + (kk & 3) * 32;
           const uint32_t offc = (kk >> 2) * C::PANEL_C + (kk & 3) * 32;
-          tc_mma(d, sdesc_sw128(r + off, 16, 1024), sdesc_sw128(c + offc, 16, 1024),
-                 C::IDESC_SC, kk > 0 ? 1u : 0u);
+          tc_mma(d, sdesc_add(rd, off), sdesc_add(cd, offc), C::IDESC_SC, kk > 0 ? 1u : 0u);
         }
         tc_commit(bar(dp ? C::BAR_DPF : C::BAR_SF));
       };
       // acc (+)= A_j . C_j with A = P^T / dS^T / dS in TMEM at column `acol`,
       // C_j the chunk operand (MN-major): 16 chunk rows per k-step
       auto issue_acc = [&](uint32_t dcol, uint32_t acol, uint32_t cbase, bool first) {
+        const uint64_t cd = sdesc_sw128(cbase, C::PANEL_C, 1024);
+        const uint32_t dt = tbase + dcol, at = tbase + acol;
 #pragma unroll
         for (int kk = 0; kk < C::CN / 16; ++kk)
-          tc_mma_ts(tbase + dcol, tbase + acol + a_col(kk),
-                    sdesc_sw128(cbase + kk * 2048, C::PANEL_C, 1024), C::IDESC_ACC,
+          tc_mma_ts(dt, at + a_col(kk), sdesc_add(cd, kk * 2048), C::IDESC_ACC,
                     (!first || kk > 0) ? 1u : 0u);
       };
       bool ok = mbar_wait(bar(C::BAR_R), 0, abort_flag, p.err);

@@ -372,6 +372,15 @@ __device__ __forceinline__ uint64_t sdesc_sw128(uint32_t saddr, uint32_t lbo, ui
   return d;
 }
 
+// The descriptor of an address `bytes` (a multiple of 16) past the one `d`
+// describes: the start field holds the address in 16-byte units in its low
+// 14 bits, and shared-memory addresses stay below 2^18 bytes, so a plain
+// add never carries into the other fields.  Lets an MMA loop build each
+// descriptor with one add instead of recomputing all fields.
+__device__ __forceinline__ uint64_t sdesc_add(uint64_t d, uint32_t bytes) {
+  return d + (bytes >> 4);
+}
+
 // Instruction descriptor for kind::f16 with bf16 A/B, fp32 accumulate.
 // a_mn / b_mn select MN-major operands (otherwise K-major).
 __host__ __device__ constexpr uint32_t idesc_bf16(int M, int N, bool a_mn, bool b_mn) {

@@ -229,12 +229,12 @@ __global__ void __launch_bounds__(320, 1)
         const uint32_t ka = sbase + C::OFF_K + (j % C::KS) * C::KV_BYTES;
         const uint32_t qa = sbase + C::OFF_Q + x * C::Q_BYTES;
         const uint32_t dst = tbase + x * C::TILE_COLS;
+        const uint64_t qd = sdesc_sw128(qa, 16, 1024), kd = sdesc_sw128(ka, 16, 1024);
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
           const uint32_t off = (kk & 3) * 32u;
-          tc_mma(dst, sdesc_sw128(qa + (kk >> 2) * C::PANEL_Q + off, 16, 1024),
-                 sdesc_sw128(ka + (kk >> 2) * C::PANEL_KV + off, 16, 1024), C::IDESC_S,
-                 kk > 0 ? 1u : 0u);
+          tc_mma(dst, sdesc_add(qd, (kk >> 2) * C::PANEL_Q + off),
+                 sdesc_add(kd, (kk >> 2) * C::PANEL_KV + off), C::IDESC_S, kk > 0 ? 1u : 0u);
         }
         tc_commit(bar(C::BAR_SF + x));
       };
@@ -270,13 +270,13 @@ __global__ void __launch_bounds__(320, 1)
             tc_fence_after();
             const uint32_t pa = tbase + x * C::TILE_COLS;   // P in TMEM
             const uint32_t dst = pa + C::COL_O;
+            // V is MN-major: 64-column panels BN*128 bytes apart (LBO),
+            // 8-row groups 1024 bytes apart (SBO); 16 rows per k-step
+            const uint64_t vd = sdesc_sw128(va, C::PANEL_KV, 1024);
 #pragma unroll
-            for (int kk = 0; kk < C::BN / 16; ++kk) {
-              // V is MN-major: 64-column panels BN*128 bytes apart (LBO),
-              // 8-row groups 1024 bytes apart (SBO); 16 rows per k-step
-              tc_mma_ts(dst, pa + p_col(kk), sdesc_sw128(va + kk * 2048, C::PANEL_KV, 1024),
-                        C::IDESC_O, (cp[x] > 0 || kk > 0) ? 1u : 0u);
-            }
+            for (int kk = 0; kk < C::BN / 16; ++kk)
+              tc_mma_ts(dst, pa + p_col(kk), sdesc_add(vd, kk * 2048), C::IDESC_O,
+                        (cp[x] > 0 || kk > 0) ? 1u : 0u);
             tc_commit(bar(C::BAR_PV + x));
             ++cp[x];
           }
