@@ -56,7 +56,8 @@ def test_chunk_local(cuda_device, R, P):
 
 
 @pytest.mark.parametrize("T,d,n_P,R,P", [(1024, 3, 0, 64, 65), (2048, 3, 16, 32, 17),
-                                          (512, 2, 0, 16, 9), (1000, 3, 0, 64, 65)])
+                                          (512, 2, 0, 16, 9), (1000, 3, 0, 64, 65),
+                                          (1024, 3, 0, 128, 129), (512, 2, 8, 20, 33)])
 def test_pool_and_incidence(cuda_device, T, d, n_P, R, P):
     spec = build_mask(T, d, chunk=8, n_P=n_P)
     g = torch.Generator().manual_seed(T + d)
