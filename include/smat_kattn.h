@@ -65,6 +65,18 @@ SMAT_API int smat_kattn_incidence(const float* F, const int64_t* ptr, const int3
                          float* U, int nb, int N_in, int N_out, int RP,
                          int32_t* err_word, void* stream);
 
+/* The op's final division (attention.py:450-451) over rows of P floats:
+ * out[r, c] = H[r, c] / H[r, P - 1], c < P - 1 (H [rows, P], out [rows, P - 1],
+ * both contiguous fp32). */
+SMAT_API int smat_kattn_normalise_fwd(const float* H, float* out, int64_t rows, int P,
+                             void* stream);
+
+/* Its backward: dH[r, c] = dout[r, c] / H[r, P - 1] for c < P - 1 and
+ * dH[r, P - 1] = -sum_c dout[r, c] H[r, c] / H[r, P - 1]^2 (dout [rows, P - 1],
+ * dH [rows, P]). */
+SMAT_API int smat_kattn_normalise_bwd(const float* H, const float* dout, float* dH,
+                             int64_t rows, int P, void* stream);
+
 /* One streaming-decode token of the kernelised op for nb sequences
  * (SmatDecoder.step, attention.py:521-527): S[b] += psi[b] vb[b]^T, then
  * o = phi[b]^T (S[b] + U[b, h]) and out[b, c] = o[c] / o[P - 1] for c < P - 1.

@@ -558,6 +558,44 @@ __global__ void __launch_bounds__(256) kattn_incidence_kernel(
   }
 }
 
+// ---------------------------------------------------------------- normalisation
+// The op's last step (attention.py:450-451): out[row, c] = H[row, c] / H[row, P-1]
+// for c < P - 1, and its backward dH[row, c] = dout[row, c] / den for c < P - 1,
+// dH[row, P - 1] = -sum_c dout[row, c] out[row, c] / den.  One warp per row.
+__global__ void __launch_bounds__(256) kattn_norm_fwd_kernel(const float* __restrict__ H,
+                                                             float* __restrict__ out,
+                                                             int64_t rows, int P) {
+  const int64_t row = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (row >= rows) return;
+  const float* h = H + row * P;
+  float* o = out + row * (P - 1);
+  const float inv = 1.f / h[P - 1];
+  for (int c = lane; c < P - 1; c += 32) o[c] = h[c] * inv;
+}
+
+__global__ void __launch_bounds__(256) kattn_norm_bwd_kernel(const float* __restrict__ H,
+                                                             const float* __restrict__ dout,
+                                                             float* __restrict__ dH,
+                                                             int64_t rows, int P) {
+  const int64_t row = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (row >= rows) return;   // whole warps: rows are warp-uniform
+  const float* h = H + row * P;
+  const float* g = dout + row * (P - 1);
+  float* d = dH + row * P;
+  const float inv = 1.f / h[P - 1];
+  float acc = 0.f;
+  for (int c = lane; c < P - 1; c += 32) {
+    const float gc = g[c] * inv;
+    d[c] = gc;
+    acc = fmaf(gc, h[c], acc);
+  }
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
+  if (lane == 0) d[P - 1] = -acc * inv;
+}
+
 // ---------------------------------------------------------------- streaming decode
 // One token for every sequence b (SmatDecoder.step, attention.py:521-527):
 // S_b += psi_b vb_b^T, o_b = phi_b^T (S_b + U_b[h]), out_b = o_b[:P-1] / o_b[P-1].
@@ -780,6 +818,27 @@ int smat_kattn_decode_step(const float* phi, const float* psi, const float* vb, 
   const size_t smem = (2 * static_cast<size_t>(R) + 4 * static_cast<size_t>(P)) * sizeof(float);
   kattn_decode_kernel<<<nb, DEC_THREADS, smem, static_cast<cudaStream_t>(stream)>>>(
       phi, psi, vb, S, U, out, R, P, nU, h);
+  return cudaGetLastError() == cudaSuccess ? SMAT_OK : SMAT_ERR_LAUNCH;
+}
+
+int smat_kattn_normalise_fwd(const float* H, float* out, int64_t rows, int P, void* stream) {
+  if (!H || !out) return SMAT_ERR_NULL_POINTER;
+  if (rows < 0 || P < 2 || rows > (static_cast<int64_t>(1) << 36)) return SMAT_ERR_BAD_SHAPE;
+  if (rows == 0) return SMAT_OK;
+  const int64_t blocks = (rows + 7) / 8;
+  kattn_norm_fwd_kernel<<<static_cast<unsigned>(blocks), 256, 0,
+                          static_cast<cudaStream_t>(stream)>>>(H, out, rows, P);
+  return cudaGetLastError() == cudaSuccess ? SMAT_OK : SMAT_ERR_LAUNCH;
+}
+
+int smat_kattn_normalise_bwd(const float* H, const float* dout, float* dH, int64_t rows, int P,
+                             void* stream) {
+  if (!H || !dout || !dH) return SMAT_ERR_NULL_POINTER;
+  if (rows < 0 || P < 2 || rows > (static_cast<int64_t>(1) << 36)) return SMAT_ERR_BAD_SHAPE;
+  if (rows == 0) return SMAT_OK;
+  const int64_t blocks = (rows + 7) / 8;
+  kattn_norm_bwd_kernel<<<static_cast<unsigned>(blocks), 256, 0,
+                          static_cast<cudaStream_t>(stream)>>>(H, dout, dH, rows, P);
   return cudaGetLastError() == cudaSuccess ? SMAT_OK : SMAT_ERR_LAUNCH;
 }
 

@@ -42,7 +42,7 @@ from .mask import MaskSpec
 
 __all__ = ["chunk_local", "pool", "incidence", "segmented_causal_scan", "pool_profiles",
            "apply_incidence", "query_by_type", "walsh_incidence", "zeta_transform",
-           "smat_attention", "SmatDecoder"]
+           "smat_attention", "SmatDecoder", "normalise"]
 
 _vp, _ci, _cl = ctypes.c_void_p, ctypes.c_int, ctypes.c_int64
 SIGNATURES = {
@@ -55,6 +55,8 @@ SIGNATURES = {
     "smat_kattn_incidence": (_ci, [_vp, _vp, _vp, _vp, _ci, _ci, _ci, _ci, _vp, _vp]),
     "smat_kattn_decode_step": (_ci, [_vp, _vp, _vp, _vp, _vp, _vp, _ci, _ci, _ci, _ci, _ci,
                                      _vp]),
+    "smat_kattn_normalise_fwd": (_ci, [_vp, _vp, _cl, _ci, _vp]),
+    "smat_kattn_normalise_bwd": (_ci, [_vp, _vp, _vp, _cl, _ci, _vp]),
 }
 CHUNK = 128
 _bound = None
@@ -221,6 +223,37 @@ def _incidence_csr(F, spec: MaskSpec):
     return _Incidence.apply(F, ptr, idx, int(spec.B))
 
 
+# ---------------------------------------------------------------- normalisation
+class _Normalise(torch.autograd.Function):
+    """``H[..., :-1] / H[..., -1:]`` (reference ``attention.py:450-451``) and its
+    backward, one kernel each."""
+
+    @staticmethod
+    def forward(ctx, H):
+        h = _f32(H)
+        p = h.shape[-1]
+        out = torch.empty(*h.shape[:-1], p - 1, dtype=torch.float32, device=h.device)
+        _lib.check("smat_kattn_normalise_fwd", _L().smat_kattn_normalise_fwd(
+            h.data_ptr(), out.data_ptr(), h.numel() // p, p, _stream(h)))
+        ctx.save_for_backward(h)
+        return out
+
+    @staticmethod
+    def backward(ctx, dout):
+        (h,) = ctx.saved_tensors
+        p = h.shape[-1]
+        g = dout.float().contiguous()
+        dH = torch.empty_like(h)
+        _lib.check("smat_kattn_normalise_bwd", _L().smat_kattn_normalise_bwd(
+            h.data_ptr(), g.data_ptr(), dH.data_ptr(), h.numel() // p, p, _stream(h)))
+        return dH
+
+
+def normalise(H):
+    """``H[..., :-1] / H[..., -1:]`` for fp32 CUDA ``H`` (the op's last step)."""
+    return _Normalise.apply(H)
+
+
 # ---------------------------------------------------------------- the schedule
 def segmented_causal_scan(Phi, Psi, Vb, n: int, chunk: int = CHUNK):
     """``[[L_n, 0], [0, L_{T_R}]] Phi Psi^T Vb`` by chunks with one reset at ``n``
@@ -345,7 +378,7 @@ def smat_attention(Phi, Psi, Vb, spec: MaskSpec, *, chunk: int = CHUNK, g=None):
     else:
         H = segmented_causal_scan(Phi, Psi, Vb, n, chunk)
         _add_query_by_type(H[:, n:], Phi[:, n:], U, spec)
-    out = H[..., :-1] / H[..., -1:]
+    out = normalise(H)
     if g is not None:
         out = out * g.unsqueeze(-1).to(out.dtype)
     return out

@@ -178,3 +178,22 @@ def test_decoder_matches_oracle_wide(cuda_device):
     with pytest.raises(ValueError):
         dec.step(Phi[:, 0].to(cuda_device), Psi[:, 0].to(cuda_device),
                  Vb[:, 0, :5].to(cuda_device))
+
+
+@pytest.mark.parametrize("P", [2, 9, 65, 129])
+def test_normalise(cuda_device, P):
+    """The fused final division and its backward against torch autograd of
+    ``H[..., :-1] / H[..., -1:]`` (fp64), within 1e-5 of scale."""
+    g = torch.Generator().manual_seed(P)
+    H = torch.randn(3, 257, P, generator=g, dtype=torch.float64)
+    H[..., -1] = H[..., -1].abs() + 0.5
+    dout = torch.randn(3, 257, P - 1, generator=g, dtype=torch.float64)
+    x = H.float().to(cuda_device).requires_grad_(True)
+    out = KA.normalise(x)
+    out.backward(dout.float().to(cuda_device))
+    torch.cuda.synchronize()
+    r = H.float().double().requires_grad_(True)
+    ref = r[..., :-1] / r[..., -1:]
+    ref.backward(dout.float().double())
+    _close(out, ref.detach(), 1e-5, "out")
+    _close(x.grad, r.grad, 1e-5, "dH")
