@@ -275,23 +275,40 @@ def run_reference(args):
 def _e2e(host, shape, device, spec, scale, K, dist, stream):
     """Same step through the public autograd API with pinned host buffers:
     per step H2D of q, k, v, dO and D2H of o, dq, dk, dv inside the timed
-    region.  Returns (ms per step, bytes each way per step)."""
+    region.  The batch goes through in slices of one sequence, pipelined the
+    way a caller streaming from host memory would: the H2D of slice b + 1 (a
+    copy stream) and the D2H of slice b - 1 (another) overlap the attention
+    of slice b (slices of 8 heads measured slower: the smaller launches do
+    not fill the GPU).  Returns (ms per step, bytes each way per step)."""
     from smat_attention_b200.attention import smat_softmax_attention
     pinned = [x.pin_memory() for x in host]
     outs = [torch.empty(shape, dtype=torch.bfloat16).pin_memory() for _ in range(4)]
     E = max(1, min(K, 3))
+    h2d, d2h = torch.cuda.Stream(device), torch.cuda.Stream(device)
 
     def e2e_step():
-        qd, kd, vd, dod = (x.to(device, non_blocking=True) for x in pinned)
-        qd.requires_grad_(True)
-        kd.requires_grad_(True)
-        vd.requires_grad_(True)
-        od, _ = smat_softmax_attention(qd, kd, vd, spec, scale)
-        od.backward(dod)
-        for dst, src in zip(outs, (od.detach(), qd.grad, kd.grad, vd.grad)):
-            dst.copy_(src, non_blocking=True)
+        for b in range(shape[0]):
+            sl = slice(b, b + 1)
+            with torch.cuda.stream(h2d):
+                ins = [x[sl].to(device, non_blocking=True) for x in pinned]
+            stream.wait_stream(h2d)
+            for t in ins:
+                t.record_stream(stream)
+            qd, kd, vd, dod = ins
+            qd.requires_grad_(True)
+            kd.requires_grad_(True)
+            vd.requires_grad_(True)
+            od, _ = smat_softmax_attention(qd, kd, vd, spec, scale)
+            od.backward(dod)
+            d2h.wait_stream(stream)
+            with torch.cuda.stream(d2h):
+                for dst, src in zip(outs, (od.detach(), qd.grad, kd.grad, vd.grad)):
+                    dst[sl].copy_(src, non_blocking=True)
+                    src.record_stream(d2h)
+        stream.wait_stream(d2h)   # the step ends when its last result is on the host
 
     e2e_step()
+    torch.cuda.synchronize(device)
     _barrier(dist, device)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(stream)
