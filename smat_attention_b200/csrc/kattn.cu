@@ -138,22 +138,28 @@ struct TileCfg {
   static constexpr uint32_t IDESC_EX = idesc_tf32(128, NO, false, MODE == TM_FWD);
 };
 
-// rows [0, nrows) x PN fp32 columns of `src` (row stride P) into a K-major
-// SWIZZLE_128B tile (panels of nrows x 32), row r by thread r
-__device__ __forceinline__ void cp_kmajor(uint32_t dst, const float* src, int row, int nrows,
-                                          int P, int PN) {
-  if (row >= nrows) return;
-  for (int k = 0; k < PN; ++k)
+// rows [0, nrows) x PN fp32 columns of `src` (row stride P, the rows
+// contiguous) into a K-major SWIZZLE_128B tile (panels of nrows x 32).  Thread
+// t of nt copies elements t, t + nt, ... of the run, so a warp's 32 copies
+// read 32 consecutive floats (columns past P are zero-filled).
+template <int PN>
+__device__ __forceinline__ void cp_kmajor(uint32_t dst, const float* src, int t, int nt,
+                                          int nrows, int P) {
+  for (int e = t; e < nrows * PN; e += nt) {
+    const int row = e / PN, k = e % PN;
     cp_async4(dst + (k >> 5) * (nrows * 128) + sw128_offset(row, (k & 31) >> 2) + (k & 3) * 4,
               src + static_cast<int64_t>(row) * P + (k < P ? k : 0), k < P ? 4u : 0u);
+  }
 }
 // the same rows into an MN-major tile with 32-byte swizzle atoms (rows = K)
-__device__ __forceinline__ void cp_mn32(uint32_t dst, const float* src, int row, int nrows, int P,
-                                        int PN) {
-  if (row >= nrows) return;
-  for (int c = 0; c < PN; ++c)
+template <int PN>
+__device__ __forceinline__ void cp_mn32(uint32_t dst, const float* src, int t, int nt, int nrows,
+                                        int P) {
+  for (int e = t; e < nrows * PN; e += nt) {
+    const int row = e / PN, c = e % PN;
     cp_async4(dst + (c >> 5) * (nrows * 128) + mn32_offset(row, c & 31),
               src + static_cast<int64_t>(row) * P + (c < P ? c : 0), c < P ? 4u : 0u);
+  }
 }
 
 // 192 threads: warps 0-3 copy the cp.async operands, mask G and store OUT
@@ -261,17 +267,17 @@ __global__ void __launch_bounds__(192, 1)
     const float* dO = p.dout + rows_off;
     const float* sn = p.sin + chunk * R * p.P;
     if (MODE == TM_FWD) {
-      cp_mn32(sbase + C::OFF_B2, vb, r, KC, p.P, PN);
-      cp_mn32(sbase + C::OFF_EX, sn, r, R, p.P, PN);
+      cp_mn32<PN>(sbase + C::OFF_B2, vb, r, 128, KC, p.P);
+      cp_mn32<PN>(sbase + C::OFF_EX, sn, r, 128, R, p.P);
     } else if (MODE == TM_DPHI) {
-      cp_kmajor(sbase + C::OFF_A1, dO, r, KC, p.P, PN);
-      cp_kmajor(sbase + C::OFF_B1, vb, r, KC, p.P, PN);
-      cp_kmajor(sbase + C::OFF_EX, sn, r, R, p.P, PN);
+      cp_kmajor<PN>(sbase + C::OFF_A1, dO, r, 128, KC, p.P);
+      cp_kmajor<PN>(sbase + C::OFF_B1, vb, r, 128, KC, p.P);
+      cp_kmajor<PN>(sbase + C::OFF_EX, sn, r, 128, R, p.P);
     } else if (MODE == TM_DV) {
-      cp_mn32(sbase + C::OFF_B2, dO, r, KC, p.P, PN);
+      cp_mn32<PN>(sbase + C::OFF_B2, dO, r, 128, KC, p.P);
     } else {
-      cp_kmajor(sbase + C::OFF_A1, vb, r, KC, p.P, PN);
-      cp_kmajor(sbase + C::OFF_B1, dO, r, KC, p.P, PN);
+      cp_kmajor<PN>(sbase + C::OFF_A1, vb, r, 128, KC, p.P);
+      cp_kmajor<PN>(sbase + C::OFF_B1, dO, r, 128, KC, p.P);
     }
     asm volatile("cp.async.wait_all;" ::: "memory");
     fence_proxy_async_smem();
