@@ -722,6 +722,29 @@ def run_kattn(args):
     Sin = torch.rand(nb, nc, r, dv + 1, device=device)
     t_chunk = timed(lambda: KA.chunk_local(Phi_c, Psi_c, Vb_c, Sin), K)
     chunk_bytes = nb * T * (2 * r + 2 * (dv + 1)) * 4 + nb * nc * r * (dv + 1) * 4
+    # streaming decode (SmatDecoder): prefill with the first n columns, then
+    # 64 tokens n, n + 1, ... (nb sequences per step), each step's inputs
+    # contiguous as a model would produce them; 64 steps back to back between
+    # two events, per step
+    Vb_all = torch.cat([V, torch.ones(nb, T, 1, device=device)], -1)
+    n0 = spec.n
+    ND = 64
+    step_in = [x[:, n0:n0 + ND].transpose(0, 1).contiguous() for x in (Phi, Psi, Vb_all)]
+
+    def timed_decode(make):
+        d = make()
+        for i in range(ND):            # warm-up pass over the tokens
+            d.step(*(x[i] for x in step_in))
+        d = make()
+        torch.cuda.synchronize(device)
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        for i in range(ND):
+            d.step(*(x[i] for x in step_in))
+        b.record(stream)
+        torch.cuda.synchronize(device)
+        return a.elapsed_time(b) / ND
+    t_dec = timed_decode(lambda: KA.SmatDecoder(Psi[:, :n0], Vb_all[:, :n0], spec))
     ref_line = None
     R = _import_reference()
     if R is not None:
@@ -744,6 +767,8 @@ def run_kattn(args):
             ref_line = {"fwd_ms": timed(theirs(False), K), "step_ms": timed(theirs(True), K),
                         "source": "reference smat (baseline/_ref), Triton backends, patched "
                                   "differentiable kernels"}
+            ref_line["decode_step_us"] = timed_decode(
+                lambda: RA.SmatDecoder(Psi[:, :n0], Vb_all[:, :n0], rspec)) * 1e3
         except Exception as e:   # noqa: BLE001 -- reported, not fatal
             ref_line = {"unavailable": f"{type(e).__name__}: {str(e)[:200]}"}
     dev_err = check_device_errors(device)
@@ -760,6 +785,7 @@ def run_kattn(args):
                        "seq_len": T, "parallelism": f"(sequence) partition x{ws}",
                        "l2": "inputs larger than L2; no flush"},
             "fwd_ms": t_fwd,
+            "decode_step_us": t_dec * 1e3,
             "roofline": {"bound": "hbm", "kernel": "kattn_chunk_fwd", "achieved":
                          chunk_bytes / (t_chunk * 1e-3) / 1e9, "peak": peaks["hbm"],
                          "unit": "GB/s", "frac": chunk_bytes / (t_chunk * 1e-3) / 1e9 /
