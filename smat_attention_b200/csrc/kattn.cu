@@ -829,7 +829,7 @@ int smat_kattn_decode_step(const float* phi, const float* psi, const float* vb, 
 
 int smat_kattn_normalise_fwd(const float* H, float* out, int64_t rows, int P, void* stream) {
   if (!H || !out) return SMAT_ERR_NULL_POINTER;
-  if (rows < 0 || P < 2 || rows > (static_cast<int64_t>(1) << 36)) return SMAT_ERR_BAD_SHAPE;
+  if (rows < 0 || P < 2 || rows > 8 * static_cast<int64_t>(0x7FFFFFFF)) return SMAT_ERR_BAD_SHAPE;
   if (rows == 0) return SMAT_OK;
   const int64_t blocks = (rows + 7) / 8;
   kattn_norm_fwd_kernel<<<static_cast<unsigned>(blocks), 256, 0,
@@ -840,7 +840,7 @@ int smat_kattn_normalise_fwd(const float* H, float* out, int64_t rows, int P, vo
 int smat_kattn_normalise_bwd(const float* H, const float* dout, float* dH, int64_t rows, int P,
                              void* stream) {
   if (!H || !dout || !dH) return SMAT_ERR_NULL_POINTER;
-  if (rows < 0 || P < 2 || rows > (static_cast<int64_t>(1) << 36)) return SMAT_ERR_BAD_SHAPE;
+  if (rows < 0 || P < 2 || rows > 8 * static_cast<int64_t>(0x7FFFFFFF)) return SMAT_ERR_BAD_SHAPE;
   if (rows == 0) return SMAT_OK;
   const int64_t blocks = (rows + 7) / 8;
   kattn_norm_bwd_kernel<<<static_cast<unsigned>(blocks), 256, 0,

@@ -395,7 +395,10 @@ class SmatDecoder:
     runs the ``pool`` and ``incidence`` kernels (plus the rank-one global term
     for ``n_P > 0``); each :meth:`step` is one ``smat_kattn_decode_step``
     launch over all ``nb`` sequences.  State and arithmetic are fp32;
-    ``acc_dtype`` other than fp32 is rejected (there is no CPU path)."""
+    ``acc_dtype`` other than fp32 is rejected (there is no CPU path).
+    ``incidence_backend`` is accepted for the reference's signature; the
+    incidence always runs the CSR kernel (the Walsh butterfly for the
+    endpoint family)."""
 
     def __init__(self, Psi_prefix, Vb_prefix, spec: MaskSpec, *, acc_dtype=None,
                  incidence_backend: str = "auto"):
