@@ -79,9 +79,10 @@ def _layout_pairs():
     return spec, block_layout_stats(spec)["pairs"]
 
 
-def _describe():
+def _describe(H=None):
     w = WORKLOAD
-    head = f"{w['name']}: B={w['B']} H={w['H']} T={w['T']} D={w['D']} bs={w['block']} "
+    H = w["H"] if H is None else H
+    head = f"{w['name']}: B={w['B']} H={H} T={w['T']} D={w['D']} bs={w['block']} "
     if "d" in w:
         return head + f"M^({w['d']}) chunk={w['chunk']} (reference build_mask) fwd+bwd per rank"
     return head + f"W={w['window']} S={w['stride']} sinks={w['sinks']} fwd+bwd per rank"
@@ -238,6 +239,19 @@ def cpu_sample(reps=1):
                       f"fp32 fwd+bwd, oracle port, median of {reps}: {t:.2f} s/head"}
 
 
+def _config(ws, strong, H_rank):
+    """The `config` of the attention workloads' JSON line (both arms):
+    H_rank is the heads each rank runs."""
+    w = WORKLOAD
+    return {"workload": _describe(H_rank),
+            "global_batch": w["B"] * (1 if strong else ws), "seq_len": w["T"],
+            "heads": H_rank * (ws if strong else 1), "head_dim": w["D"],
+            "parallelism": (f"head partition x{ws}" if strong
+                            else f"(batch,head) partition x{ws}"),
+            "l2": f"inputs larger than L2 ({w['B'] * H_rank * w['T'] * w['D'] * 2 >> 20} MiB "
+                  f"per tensor); no flush"}
+
+
 def run_reference(args):
     dist, rank, ws, local = _dist()
     if rank != 0:
@@ -260,7 +274,9 @@ def run_reference(args):
             "warmup": args.warmup, "ms_per_step": elapsed / steps * 1e3,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
             "data": "synthetic", "impl": "reference",
-            "config": {"workload": f"{WORKLOAD['name']} sample (one head)", **WORKLOAD},
+            "config": _config(args.gpus, WORKLOAD["name"] == "c5",
+                              WORKLOAD["H"] // args.gpus if WORKLOAD["name"] == "c5"
+                              else WORKLOAD["H"]),
             "cpu_baseline": base,
             "e2e": {"value": v, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
@@ -453,13 +469,7 @@ def run_gpu(args):
             "warmup": max(3, args.warmup), "ms_per_step": ms_step, "higher_is_better": True,
             "scaling": "strong" if strong else "weak", "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic",
-            "config": {"workload": _describe(),
-                       "global_batch": w["B"] * (1 if strong else ws), "seq_len": w["T"],
-                       "heads": w["H"] * (ws if strong else 1), "head_dim": w["D"],
-                       "parallelism": (f"head partition x{ws}" if strong
-                                       else f"(batch,head) partition x{ws}"),
-                       "l2": f"inputs larger than L2 ({_tensor_mib()} MiB per tensor); "
-                             f"no flush"},
+            "config": _config(ws, strong, w["H"]),
             "tokens_per_s": (1 if strong else ws) * w["B"] * w["T"] / (ms_step * 1e-3),
             "frac_of_peak": value / ws / peaks["tflops"],
             "peak_source": peaks["source"],
