@@ -420,19 +420,30 @@ class SmatDecoder:
         self.U = U.float().contiguous()
         self.S = torch.zeros(nb, r, p, device=Psi_prefix.device, dtype=torch.float32)
         self.i = 0
+        self._fn = None
+        self._S_ptr, self._U_ptr, self._nU = self.S.data_ptr(), self.U.data_ptr(), self.U.shape[1]
 
     def step(self, Phi_t, Psi_t, Vb_t):
         """One token: ``Phi_t, Psi_t (nb, r)``, ``Vb_t (nb, p)`` -> ``(nb, p - 1)`` fp32."""
-        phi, psi, vb = (_f32(x) for x in (Phi_t, Psi_t, Vb_t))
+        dev = self.S.device
+        ins = []
+        for x in (Phi_t, Psi_t, Vb_t):
+            # tokens usually arrive fp32 and contiguous on the device: no copies
+            if not (x.dtype is torch.float32 and x.device == dev and x.is_contiguous()):
+                x = _f32(x)
+            ins.append(x)
+        phi, psi, vb = ins
         if phi.shape != (self.nb, self.r) or psi.shape != (self.nb, self.r) \
                 or vb.shape != (self.nb, self.p):
             raise ValueError("step expects Phi_t, Psi_t (nb, r) and Vb_t (nb, p)")
-        out = torch.empty(self.nb, self.p - 1, dtype=torch.float32, device=phi.device)
-        nU = self.U.shape[1]
-        _lib.check("smat_kattn_decode_step", _L().smat_kattn_decode_step(
-            phi.data_ptr(), psi.data_ptr(), vb.data_ptr(), self.S.data_ptr(),
-            self.U.data_ptr(), out.data_ptr(), self.nb, self.r, self.p, nU,
-            self.i % self.spec.B, _stream(phi)))
+        out = torch.empty(self.nb, self.p - 1, dtype=torch.float32, device=dev)
+        if self._fn is None:
+            self._fn = _L().smat_kattn_decode_step
+        rc = self._fn(phi.data_ptr(), psi.data_ptr(), vb.data_ptr(), self._S_ptr, self._U_ptr,
+                      out.data_ptr(), self.nb, self.r, self.p, self._nU, self.i % self.spec.B,
+                      torch.cuda.current_stream(dev).cuda_stream)
+        if rc:
+            _lib.check("smat_kattn_decode_step", rc)
         self.i += 1
         return out
 
