@@ -63,7 +63,8 @@ typedef enum smat_status {
   SMAT_ERR_ROW_TOO_LONG = 12,
   SMAT_ERR_CAPACITY = 13,
   SMAT_ERR_SCRATCH_LIMIT = 14,
-  SMAT_ERR_BAD_PATTERN = 15
+  SMAT_ERR_BAD_PATTERN = 15,
+  SMAT_ERR_CAPTURE = 16
 } smat_status;
 
 enum { SMAT_DTYPE_F32 = 0, SMAT_DTYPE_BF16 = 1 };
@@ -77,7 +78,7 @@ enum {
   SMAT_DEVERR_BAD_WORK = 8
 };
 
-/* ABI version of this header (incremented when an entry point changes or is added). */
+/* ABI version of this header (incremented when an entry point changes or is added): 5. */
 SMAT_API int smat_abi_version(void);
 
 /* Human-readable name of a status code (static string). */
@@ -429,8 +430,11 @@ SMAT_API int smat_decode(int dtype,
  * it, held until the process exits.  B*H*T must be <= SMAT_NOALLOC_MAX_ROWS,
  * else SMAT_ERR_SCRATCH_LIMIT before any launch.  All calls share the array:
  * calls whose kernels overlap on the GPU race.  The first call on a device
- * looks up the array's address with that device current; make it before any
- * stream capture.  It has no counterpart in the reference. */
+ * looks up the array's address with that device current and caches it with
+ * the identity of the device's context (a call under a new context, e.g.
+ * after cudaDeviceReset, looks it up again); make that first call before any
+ * stream capture (during a capture the lookup returns SMAT_ERR_CAPTURE).  It
+ * has no counterpart in the reference. */
 #define SMAT_NOALLOC_MAX_ROWS (1 << 22)
 SMAT_API int smat_bwd_noalloc(int dtype,
                               const void* q, const int64_t* q_stride,
@@ -448,6 +452,22 @@ SMAT_API int smat_bwd_noalloc(int dtype,
                               const uint8_t* t_kind,
                               int nblocks, int64_t nnzb, int block, int max_row, int t_max_row,
                               float scale, int32_t* err_word, void* stream);
+
+/* ---------------------------------------------------------------- self-test
+ * smat_selftest_wait_timeout: runs the kernels' bounded-wait failure path on
+ * the device.  One CTA waits on an mbarrier nothing arrives on with the same
+ * wait code the kernels use, but with a limit of `limit_cycles` SM cycles
+ * (1000 .. SMAT_SELFTEST_MAX_LIMIT, about 0.5 ms at 1e6): the wait gives up,
+ * ORs SMAT_DEVERR_WAIT_TIMEOUT into *err_word and raises the CTA's abort flag;
+ * a second warp waiting elsewhere leaves through that flag; both run the
+ * bounded drain wait; the CTA frees its TMEM and returns, leaving the context
+ * usable.  report: device int32[4], written by the kernel: {first wait gave up,
+ * second wait gave up, second wait left through the abort flag, both drains
+ * gave up}, each 1 when the path behaved.  Counterpart of the reference's
+ * per-kernel retire-with-warning fallback (src/smat/attention.py:58-75). */
+#define SMAT_SELFTEST_MAX_LIMIT (100000000LL)
+SMAT_API int smat_selftest_wait_timeout(int64_t limit_cycles, int32_t* err_word, int32_t* report,
+                                        void* stream);
 
 #ifdef __cplusplus
 }

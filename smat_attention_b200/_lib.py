@@ -109,6 +109,7 @@ SIGNATURES = {
                              _c_int, _c_int, _c_int, _c_int, _vp, _vp, _vp,
                              _c_int, _c_i64, _c_int, _c_int, ctypes.POINTER(Pattern),
                              _c_f, _vp, _c_i64, _vp, _vp]),
+    "smat_selftest_wait_timeout": (_c_int, [_c_i64, _vp, _vp, _vp]),
     # smat_bwd without the delta workspace (fixed in-library scratch)
     "smat_bwd_noalloc": (_c_int, [_c_int, _vp, _i64p, _vp, _i64p, _vp, _i64p, _vp, _i64p, _vp,
                                   _i64p, _vp, _vp, _i64p, _vp, _i64p, _vp, _i64p,

@@ -18,7 +18,8 @@ PKG = os.path.dirname(os.path.abspath(__file__))
 ROOT = os.path.dirname(PKG)
 CSRC = os.path.join(PKG, "csrc")
 LIB = os.path.join(PKG, "libsmat_b200.so")
-SOURCES = ["smat_abi.cu", "noalloc.cu", "rows.cu", "lm_ops.cu", "decode.cu", "kattn.cu"]
+SOURCES = ["smat_abi.cu", "noalloc.cu", "selftest.cu", "rows.cu", "lm_ops.cu", "decode.cu",
+           "kattn.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 

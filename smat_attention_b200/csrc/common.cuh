@@ -65,8 +65,11 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
 // The abort flag and the clock are checked once every 32 polls so that a
 // waiting warp takes few issue slots from the working warps of its SM
 // sub-partition (try_wait itself suspends the thread for a short while).
-__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag,
-                                          int32_t* err) {
+// `limit` is the give-up time in SM cycles (SMAT_WAIT_LIMIT in the kernels; the
+// self-test entry point passes a short one).
+__device__ __forceinline__ bool mbar_wait_for(uint32_t bar, uint32_t parity,
+                                              volatile int* abort_flag, int32_t* err,
+                                              long long limit) {
   if (mbar_try_wait(bar, parity)) return true;
   const long long t0 = clock64();
   while (true) {
@@ -74,21 +77,31 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatil
     for (int i = 0; i < 32; ++i)
       if (mbar_try_wait(bar, parity)) return true;
     if (*abort_flag) return false;
-    if (clock64() - t0 > SMAT_WAIT_LIMIT) {
+    if (clock64() - t0 > limit) {
       *abort_flag = 1;
       if (err) atomicOr(err, DEV_ERR_WAIT_TIMEOUT);
       return false;
     }
   }
 }
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag,
+                                          int32_t* err) {
+  return mbar_wait_for(bar, parity, abort_flag, err, SMAT_WAIT_LIMIT);
+}
 
 // Bounded wait that ignores the abort flag: used on the abort path to let this
 // CTA's own copies / MMAs in flight finish before it frees TMEM and exits.
-__device__ __forceinline__ void mbar_wait_drain(uint32_t bar, uint32_t parity) {
+// Returns whether the phase completed.
+__device__ __forceinline__ bool mbar_wait_drain_for(uint32_t bar, uint32_t parity,
+                                                    long long limit) {
   const long long t0 = clock64();
   while (!mbar_try_wait(bar, parity)) {
-    if (clock64() - t0 > SMAT_WAIT_LIMIT) return;
+    if (clock64() - t0 > limit) return false;
   }
+  return true;
+}
+__device__ __forceinline__ void mbar_wait_drain(uint32_t bar, uint32_t parity) {
+  mbar_wait_drain_for(bar, parity, SMAT_WAIT_LIMIT);
 }
 
 // ---------------------------------------------------------------- TMA

@@ -20,8 +20,12 @@
 //     but two calls whose kernels overlap on the GPU (different streams, no
 //     ordering between them) race on it.
 //   * The first call on a device looks up the array's device address
-//     (cudaGetSymbolAddress, with that device current) and caches it; make
-//     that first call before any stream capture.
+//     (cudaGetSymbolAddress, with that device current) and caches it together
+//     with the identity of the device's current context; make that first call
+//     before any stream capture (during a capture the lookup is refused with
+//     SMAT_ERR_CAPTURE).  A later call made under another context (after
+//     cudaDeviceReset, which reloads the module) looks the address up again.
+#include <cuda.h>
 #include <cuda_runtime.h>
 
 #include <cstdint>
@@ -36,26 +40,83 @@ namespace {
 __device__ __align__(256) float g_delta_scratch[SMAT_NOALLOC_MAX_ROWS];
 
 constexpr int kMaxDevices = 128;
-float* g_scratch_addr[kMaxDevices] = {};
+struct ScratchSlot {
+  float* addr = nullptr;
+  unsigned long long ctx_id = 0;   // context the address belongs to (0: none yet)
+};
+ScratchSlot g_slots[kMaxDevices];
 std::mutex g_scratch_mu;
 
-// Device address of this device's copy of the array, looked up once.
+using PFN_ctx_get_current = CUresult (*)(CUcontext*);
+using PFN_ctx_get_id = CUresult (*)(CUcontext, unsigned long long*);
+
+// Unique id of the calling thread's current context (cuCtxGetId, CUDA >= 12.0),
+// reached through the runtime's driver entry points; 0 when unavailable.
+unsigned long long current_ctx_id() {
+  static PFN_ctx_get_current get_current = nullptr;
+  static PFN_ctx_get_id get_id = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      get_current = reinterpret_cast<PFN_ctx_get_current>(p);
+    p = nullptr;
+    if (cudaGetDriverEntryPoint("cuCtxGetId", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      get_id = reinterpret_cast<PFN_ctx_get_id>(p);
+  });
+  if (!get_current || !get_id) return 0;
+  CUcontext ctx = nullptr;
+  unsigned long long id = 0;
+  if (get_current(&ctx) != CUDA_SUCCESS || !ctx) return 0;
+  if (get_id(ctx, &id) != CUDA_SUCCESS) return 0;
+  return id;
+}
+
+// The cause of a failed lookup, as a status the caller can act on.
+int lookup_status(cudaError_t e) {
+  switch (e) {
+    case cudaErrorStreamCaptureUnsupported:
+    case cudaErrorStreamCaptureInvalidated:
+    case cudaErrorStreamCaptureImplicit:
+    case cudaErrorStreamCaptureWrongThread:
+      return SMAT_ERR_CAPTURE;
+    case cudaErrorNoDevice:
+    case cudaErrorInvalidDevice:
+    case cudaErrorNoKernelImageForDevice:
+    case cudaErrorInsufficientDriver:
+      return SMAT_ERR_NO_DEVICE;
+    default:
+      return SMAT_ERR_LAUNCH;
+  }
+}
+
+// Device address of this device's copy of the array, looked up once per
+// device and context.
 int scratch_for_current_device(float** out) {
   int dev = -1;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) {
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess || dev < 0 || dev >= kMaxDevices) {
     cudaGetLastError();
-    return SMAT_ERR_NO_DEVICE;
+    return e == cudaSuccess ? SMAT_ERR_NO_DEVICE : lookup_status(e);
   }
   std::lock_guard<std::mutex> lock(g_scratch_mu);
-  if (!g_scratch_addr[dev]) {
+  ScratchSlot& slot = g_slots[dev];
+  const unsigned long long ctx = slot.addr ? current_ctx_id() : 0;
+  if (!slot.addr || ctx == 0 || ctx != slot.ctx_id) {
     void* p = nullptr;
-    if (cudaGetSymbolAddress(&p, g_delta_scratch) != cudaSuccess || !p) {
+    e = cudaGetSymbolAddress(&p, g_delta_scratch);
+    if (e != cudaSuccess || !p) {
       cudaGetLastError();
-      return SMAT_ERR_NO_DEVICE;
+      slot.addr = nullptr;
+      return e == cudaSuccess ? SMAT_ERR_LAUNCH : lookup_status(e);
     }
-    g_scratch_addr[dev] = static_cast<float*>(p);
+    slot.addr = static_cast<float*>(p);
+    slot.ctx_id = current_ctx_id();   // the lookup made the device's context current
   }
-  *out = g_scratch_addr[dev];
+  *out = slot.addr;
   return SMAT_OK;
 }
 

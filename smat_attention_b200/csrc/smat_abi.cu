@@ -347,7 +347,7 @@ int bwd_tc(const TArg& r0, const TArg& r1, const TArg& c0, const TArg& c1, const
 // ====================================================================== C ABI
 extern "C" {
 
-int smat_abi_version(void) { return 4; }
+int smat_abi_version(void) { return 5; }
 
 const char* smat_status_string(int status) {
   switch (status) {
@@ -368,6 +368,8 @@ const char* smat_status_string(int status) {
     case SMAT_ERR_SCRATCH_LIMIT:
       return "B*H*T exceeds the fixed scratch of smat_bwd_noalloc (SMAT_NOALLOC_MAX_ROWS)";
     case SMAT_ERR_BAD_PATTERN: return "invalid M^(d) pattern (fields, table sizes or C)";
+    case SMAT_ERR_CAPTURE:
+      return "one-time set-up refused during stream capture (make the first call outside it)";
   }
   return "unknown status";
 }

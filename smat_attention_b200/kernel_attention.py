@@ -430,7 +430,9 @@ class SmatDecoder:
         for x in (Phi_t, Psi_t, Vb_t):
             # tokens usually arrive fp32 and contiguous on the device: no copies
             if not (x.dtype is torch.float32 and x.device == dev and x.is_contiguous()):
-                x = _f32(x)
+                if x.device.type != "cuda":
+                    raise ValueError("SmatDecoder.step takes CUDA tensors (there is no CPU path)")
+                x = x.to(dev, torch.float32).contiguous()
             ins.append(x)
         phi, psi, vb = ins
         if phi.shape != (self.nb, self.r) or psi.shape != (self.nb, self.r) \
@@ -439,9 +441,14 @@ class SmatDecoder:
         out = torch.empty(self.nb, self.p - 1, dtype=torch.float32, device=dev)
         if self._fn is None:
             self._fn = _L().smat_kattn_decode_step
-        rc = self._fn(phi.data_ptr(), psi.data_ptr(), vb.data_ptr(), self._S_ptr, self._U_ptr,
-                      out.data_ptr(), self.nb, self.r, self.p, self._nU, self.i % self.spec.B,
-                      torch.cuda.current_stream(dev).cuda_stream)
+        args = (phi.data_ptr(), psi.data_ptr(), vb.data_ptr(), self._S_ptr, self._U_ptr,
+                out.data_ptr(), self.nb, self.r, self.p, self._nU, self.i % self.spec.B,
+                torch.cuda.current_stream(dev).cuda_stream)
+        if torch.cuda.current_device() == dev.index:
+            rc = self._fn(*args)
+        else:   # the launch goes to dev's stream, so dev must be current
+            with torch.cuda.device(dev):
+                rc = self._fn(*args)
         if rc:
             _lib.check("smat_kattn_decode_step", rc)
         self.i += 1

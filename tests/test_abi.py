@@ -21,7 +21,7 @@ def declared_symbols():
 
 def test_header_symbols_exported():
     syms = declared_symbols()
-    assert len(syms) == 28
+    assert len(syms) == 29
     L = _lib.lib()
     for s in syms:
         assert hasattr(L, s), s
@@ -30,11 +30,12 @@ def test_header_symbols_exported():
 
 def test_version_and_status_strings():
     L = _lib.lib()
-    assert L.smat_abi_version() == 4
+    assert L.smat_abi_version() == 5
     assert L.smat_status_string(0) == b"ok"
     assert b"CSR" in L.smat_status_string(7)
     assert L.smat_status_string(999) == b"unknown status"
     assert b"pattern" in L.smat_status_string(15)
+    assert b"capture" in L.smat_status_string(16)
 
 
 def _fwd(**over):

@@ -31,4 +31,4 @@ def test_reference_arm_line():
     import bench
     assert line["metric"] == bench.METRIC and line["unit"] == bench.UNIT
     assert line["higher_is_better"] is True
-    assert line["config"] == bench._config(1, False, bench.WORKLOAD["H"])
+    assert line["config"] == bench._config(1)
