@@ -228,36 +228,41 @@ def _events(n):
 # ----------------------------------------------------------------------------
 
 def _gpu_numa_cpus(device):
-    """CPUs of the NUMA node the GPU's PCIe root sits on, or None."""
+    """(CPUs of the NUMA node the GPU's PCIe function sits on, or None; a note
+    saying what was found)."""
     try:
         p = torch.cuda.get_device_properties(device)
         bus = f"{p.pci_domain_id:04x}:{p.pci_bus_id:02x}:{p.pci_device_id:02x}.0"
         with open(f"/sys/bus/pci/devices/{bus}/numa_node") as f:
             node = int(f.read().strip())
         if node < 0:
-            return None
+            return None, f"{bus}: no NUMA node reported"
         with open(f"/sys/devices/system/node/node{node}/cpulist") as f:
             spec = f.read().strip()
         cpus = set()
         for part in spec.split(","):
             lo, _, hi = part.partition("-")
             cpus.update(range(int(lo), int(hi or lo) + 1))
-        return cpus & os.sched_getaffinity(0) or None
-    except (OSError, ValueError, AttributeError):
-        return None
+        cpus &= os.sched_getaffinity(0)
+        if not cpus:
+            return None, f"{bus}: node {node} has none of this process's CPUs"
+        return cpus, f"{bus}: node {node}, {len(cpus)} CPUs"
+    except (OSError, ValueError, AttributeError) as e:
+        return None, f"no placement ({type(e).__name__})"
 
 
 @contextlib.contextmanager
 def _near_gpu(device):
     """Run the body on the CPUs of the GPU's NUMA node, so that pinned host
     buffers allocated inside it are placed in that node's memory (the driver
-    allocates and touches the pages from the calling thread)."""
-    cpus = _gpu_numa_cpus(device)
+    allocates and touches the pages from the calling thread).  Yields a note
+    on the placement."""
+    cpus, note = _gpu_numa_cpus(device)
     old = os.sched_getaffinity(0)
     if cpus:
         os.sched_setaffinity(0, cpus)
     try:
-        yield cpus
+        yield note
     finally:
         if cpus:
             os.sched_setaffinity(0, old)
@@ -531,26 +536,30 @@ class AttnCase:
 def _e2e(case, K, dist):
     """The step through the public autograd API with pinned host buffers:
     per step H2D of q, k, v, dO and D2H of o, dq, dk, dv inside the timed
-    region.  The batch goes through in slices of one sequence, pipelined the
-    way a caller streaming from host memory would: the H2D of slice b + 1 (a
-    copy stream) and the D2H of slice b - 1 (another) overlap the attention
-    of slice b.  The pinned buffers are allocated from the CPUs of the GPU's
-    NUMA node.  Also times the copy floor: the same copies on the same
-    streams with no kernels (all H2D on one stream, all D2H on the other).
-    Returns (e2e ms per step, floor ms per step, bytes each way per step,
-    NUMA-bound?)."""
+    region.  The batch goes through in slices of one sequence and `hs` heads,
+    pipelined the way a caller streaming from host memory would: the H2D of
+    slice s + 1 (a copy stream) and the D2H of slice s - 1 (another) overlap
+    the attention of slice s, so the step costs the transfers plus one slice's
+    H2D at the start and one slice's D2H at the end.  The pinned buffers are
+    allocated from the CPUs of the GPU's NUMA node.  Also times the copy
+    floor: the same copies on the same streams with no kernels (all H2D on one
+    stream, all D2H on the other).  Returns (e2e ms per step, floor ms per
+    step, bytes each way per step, placement note, heads per slice)."""
     from smat_attention_b200.attention import smat_softmax_attention
     device, stream, shape, spec, scale = case.device, case.stream, case.shape, case.spec, \
         case.scale
-    with _near_gpu(device) as cpus:
+    with _near_gpu(device) as note:
         pinned = [x.pin_memory() for x in case.host]
         outs = [torch.empty(shape, dtype=case.dtype).pin_memory() for _ in range(4)]
     E = max(1, min(K, 3))
     h2d, d2h = torch.cuda.Stream(device), torch.cuda.Stream(device)
+    B, H = shape[0], shape[1]
+    hs = max(1, min(H, 8))
+    slices = [(slice(b, b + 1), slice(h, min(H, h + hs))) for b in range(B)
+              for h in range(0, H, hs)]
 
     def e2e_step():
-        for b in range(shape[0]):
-            sl = slice(b, b + 1)
+        for sl in slices:
             with torch.cuda.stream(h2d):
                 ins = [x[sl].to(device, non_blocking=True) for x in pinned]
             stream.wait_stream(h2d)
@@ -574,8 +583,7 @@ def _e2e(case, K, dist):
     def floor_step():
         h2d.wait_stream(stream)
         d2h.wait_stream(stream)
-        for b in range(shape[0]):
-            sl = slice(b, b + 1)
+        for sl in slices:
             with torch.cuda.stream(h2d):
                 for src, dst in zip(pinned, dev_bufs):
                     dst[sl].copy_(src[sl], non_blocking=True)
@@ -601,7 +609,7 @@ def _e2e(case, K, dist):
     floor_ms = timed(floor_step)
     nbytes = sum(x.numel() * x.element_size() for x in case.host)
     del dev_bufs, pinned, outs
-    return e2e_ms, floor_ms, nbytes, bool(cpus)
+    return e2e_ms, floor_ms, nbytes, note, hs
 
 
 # ----------------------------------------------------------------------------
@@ -1116,14 +1124,15 @@ def run_gpu(args):
     # ---- end to end through the public API with host buffers ---------------
     e2e = None
     if not args.no_e2e and not w.get("fwd_only") and case.dtype == torch.bfloat16:
-        e2e_ms, floor_ms, nbytes, numa = _e2e(case, K, dist)
+        e2e_ms, floor_ms, nbytes, numa, hs = _e2e(case, K, dist)
         e2e = {"value": total_fl / (e2e_ms * 1e-3) / 1e12, "unit": UNIT,
                "ms_per_step": e2e_ms, "h2d_bytes_per_step": nbytes,
                "d2h_bytes_per_step": nbytes,
                "floor_ms_per_step": floor_ms, "e2e_over_floor": e2e_ms / floor_ms,
                "host_gbs_floor": 2 * nbytes * ws / (floor_ms * 1e-3) / 1e9,
-               "pinned_on_gpu_numa_node": numa}
+               "host_placement": numa, "slice": f"1 sequence x {hs} heads"}
     dev_err |= check_device_errors(device)
+    launches = K * case.launches_per_step
     case.free()
     torch.cuda.empty_cache()
 
@@ -1160,7 +1169,7 @@ def run_gpu(args):
                      "frac_sustained": achieved / peaks["tflops_sustained"],
                      "traffic": traffic, "sm_mhz": sm_mhz},
         "e2e": e2e,
-        "gpu_launches": K * case.launches_per_step,
+        "gpu_launches": launches,
         "device_errors": dev_err,
         "clocks": clk,
     }
