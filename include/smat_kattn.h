@@ -87,6 +87,45 @@ SMAT_API int smat_kattn_decode_step(const float* phi, const float* psi, const fl
                            float* S, const float* U, float* out, int nb, int R, int P,
                            int nU, int h, void* stream);
 
+/* The causal scan's chunk prefix (segmented_causal_scan, attention.py:134-192):
+ * for every sequence s and chunk c of C rows (nc = ceil(T / C), rows past T
+ * count as zero),
+ *   out[s, c] = sum over chunks c' of c's segment with c' < c of a_c'^T b_c'
+ * (reverse != 0: c' > c), where a_c' = rows [c' C, c' C + C) of a[s] ([T, R]) and
+ * b_c' likewise of b[s] ([T, P]); the segments are chunks [0, nc0) and
+ * [nc0, nc).  A shifted scan: a chunk's own product never enters its output,
+ * and nothing crosses the segment boundary.  Forward: (psi, vb) -> Sin; backward:
+ * (phi, dout), reverse -> the summaries' gradient.  a [nb, T, R], b [nb, T, P],
+ * out [nb, nc, R, P], all contiguous fp32.  C (RA + PB) * 4 <= 200 KB (RA = R
+ * rounded up to 8, PB = P rounded up to 4). */
+SMAT_API int smat_kattn_chunk_prefix(const float* a, const float* b, float* out, int nb, int T,
+                                     int C, int R, int P, int nc0, int reverse, void* stream);
+
+/* The summaries' backward: for every chunk c, da_c += b_c dD_c^T and
+ * db_c += a_c dD_c (the gradient of D_c = a_c^T b_c; rows past T untouched).
+ * a, da [nb, T, R]; b, db [nb, T, P]; dD [nb, nc, R, P]. */
+SMAT_API int smat_kattn_chunk_expand(const float* a, const float* b, const float* dD, float* da,
+                                     float* db, int nb, int T, int C, int R, int P,
+                                     void* stream);
+
+/* query_by_type (attention.py:310-330): out[s, i] (+)= phi[s, i] U[s, i mod nU] for
+ * the T_R recent rows i (accumulate != 0 adds into out).  phi rows of R floats,
+ * out rows of P floats, both contiguous within a sequence, sequence strides
+ * given in floats (so phi may be Phi[:, n:] and out H[:, n:] of the whole
+ * tensors); U [nb, nU, R, P] contiguous. */
+SMAT_API int smat_kattn_query_by_type(const float* phi, int64_t phi_seq_stride, const float* U,
+                                      float* out, int64_t out_seq_stride, int nb, int T_R, int R,
+                                      int P, int nU, int accumulate, void* stream);
+
+/* Its backward: dphi[s, i] = dout[s, i] U[s, i mod nU]^T (written) and
+ * dU[s, h] = sum over the rows i of type h of phi[s, i]^T dout[s, i] (written,
+ * zero for a type without rows); strides as above. */
+SMAT_API int smat_kattn_query_by_type_bwd(const float* phi, int64_t phi_seq_stride,
+                                          const float* U, const float* dout,
+                                          int64_t dout_seq_stride, float* dphi,
+                                          int64_t dphi_seq_stride, float* dU, int nb, int T_R,
+                                          int R, int P, int nU, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

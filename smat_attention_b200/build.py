@@ -19,7 +19,7 @@ ROOT = os.path.dirname(PKG)
 CSRC = os.path.join(PKG, "csrc")
 LIB = os.path.join(PKG, "libsmat_b200.so")
 SOURCES = ["smat_abi.cu", "noalloc.cu", "selftest.cu", "rows.cu", "lm_ops.cu", "decode.cu",
-           "kattn.cu"]
+           "kattn.cu", "kattn_glue.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 

@@ -1,0 +1,448 @@
+// The kernelised op's glue between its fused passes (include/smat_kattn.h):
+// the chunk summaries and their segmented prefix sums of the causal scan, the
+// backward's expansion of the summary gradient, and the per-type long-range
+// query, with its backward.  All fp32 FMA on CUDA cores (the reference runs
+// them as fp32 torch GEMMs and cumsums, src/smat/attention.py:134-192 and
+// :310-330); each moves more bytes than it computes per element.
+//
+// chunk prefix (forward Sin, backward dD):
+//   D_c      = a_c^T b_c                      one CTA per (chunk, sequence), 8 x 4
+//                                             register tiles over shared memory
+//   out_c    = sum of D_c' over the chunks c' before c (or after c, reverse)
+//              in c's segment [0, nc0) or [nc0, nc)   one thread per element,
+//                                             sequential over the chunks (a
+//                                             shifted scan: D_c never enters
+//                                             out_c, and the segments never mix)
+// chunk expand:  db_c += a_c dD_c and da_c += b_c dD_c^T (8 x 4 register tiles)
+// query by type: out_i (+)= phi_i U_{i mod nU}; its backward dphi_i =
+//                dout_i U^T, dU_h = sum over the rows of type h of phi_i^T dout_i
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cstdint>
+
+#include "../../include/smat_b200.h"
+#include "../../include/smat_kattn.h"
+#include "common.cuh"
+
+namespace {
+
+using namespace smat;
+
+constexpr int GLUE_SMEM_MAX = 200 * 1024;
+constexpr int QT_ROWS = 16;   // rows of one type handled per pass of the query kernels
+
+__host__ __device__ inline int round_up(int x, int m) { return (x + m - 1) / m * m; }
+
+// rows [row0, row0 + nrows) of a row-major [T, W] matrix into shared [nrows][WS]
+// (zero-filled past T and past W), by asynchronous 4-byte copies
+__device__ __forceinline__ void stage_rows(float* dst, const float* src, int row0, int nrows,
+                                           int T, int W, int WS) {
+  for (int e = threadIdx.x; e < nrows * WS; e += blockDim.x) {
+    const int i = e / WS, c = e % WS;
+    const bool in = c < W && row0 + i < T;
+    cp_async4(smem_u32(dst + e), in ? src + static_cast<int64_t>(row0 + i) * W + c : src,
+              in ? 4u : 0u);
+  }
+}
+// the same rows transposed: shared [WS][NS] (row i of the source in column i);
+// consecutive threads take consecutive rows, so the shared writes do not
+// collide on a bank (the strided global reads are served from L1)
+__device__ __forceinline__ void stage_rows_t(float* dst, const float* src, int row0, int nrows,
+                                             int T, int W, int WS, int NS) {
+  for (int e = threadIdx.x; e < nrows * WS; e += blockDim.x) {
+    const int i = e % nrows, c = e / nrows;
+    const bool in = c < W && row0 + i < T;
+    cp_async4(smem_u32(dst + c * NS + i),
+              in ? src + static_cast<int64_t>(row0 + i) * W + c : src, in ? 4u : 0u);
+  }
+}
+__device__ __forceinline__ void cp_async_wait_all() {
+  asm volatile("cp.async.wait_all;" ::: "memory");
+}
+
+// ---------------------------------------------------------------- chunk sums
+// D[s, c] = a_c^T b_c over the C rows of chunk c (rows past T count as zero).
+// Shared: a rows [C][RA], b rows [C][PB]; a thread owns an 8 (r) x 4 (p) tile
+// and walks the chunk's rows in order.
+__global__ void __launch_bounds__(256) kattn_chunk_sum_kernel(const float* __restrict__ a,
+                                                              const float* __restrict__ b,
+                                                              float* __restrict__ D, int T,
+                                                              int C, int R, int P) {
+  extern __shared__ float4 sm4[];
+  float* sm = reinterpret_cast<float*>(sm4);
+  const int c = blockIdx.x, s = blockIdx.y, nc = gridDim.x;
+  const int RA = round_up(R, 8), PB = round_up(P, 4);
+  float* sa = sm;
+  float* sb = sm + C * RA;
+  const float* as = a + static_cast<int64_t>(s) * T * R;
+  const float* bs = b + static_cast<int64_t>(s) * T * P;
+  stage_rows(sa, as, c * C, C, T, R, RA);
+  stage_rows(sb, bs, c * C, C, T, P, PB);
+  cp_async_wait_all();
+  __syncthreads();
+  const int PG = PB / 4, tiles = (RA / 8) * PG;
+  float* out = D + (static_cast<int64_t>(s) * nc + c) * R * P;
+  for (int t = threadIdx.x; t < tiles; t += blockDim.x) {
+    const int r0 = (t / PG) * 8, p0 = (t % PG) * 4;
+    float acc[8][4];
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+#pragma unroll
+      for (int j = 0; j < 4; ++j) acc[i][j] = 0.f;
+#pragma unroll 4
+    for (int k = 0; k < C; ++k) {
+      const float4 x0 = *reinterpret_cast<const float4*>(sa + k * RA + r0);
+      const float4 x1 = *reinterpret_cast<const float4*>(sa + k * RA + r0 + 4);
+      const float4 y = *reinterpret_cast<const float4*>(sb + k * PB + p0);
+      const float xv[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+      const float yv[4] = {y.x, y.y, y.z, y.w};
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(xv[i], yv[j], acc[i][j]);
+    }
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+        if (r0 + i < R && p0 + j < P) out[(r0 + i) * P + p0 + j] = acc[i][j];
+  }
+}
+
+// In place over D [nb, nc, RP]: element e of chunk c becomes the sum of the
+// elements of the chunks before c (reverse: after c) in c's segment.  The
+// chunk values are loaded eight at a time ahead of the dependent adds.
+__global__ void __launch_bounds__(256) kattn_seg_scan_kernel(float* __restrict__ D, int nc,
+                                                             int64_t RP, int nc0, int reverse) {
+  const int64_t e = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (e >= RP) return;
+  float* base = D + static_cast<int64_t>(blockIdx.y) * nc * RP + e;
+  float run = 0.f;
+  for (int i0 = 0; i0 < nc; i0 += 8) {
+    float v[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int i = i0 + j;
+      const int c = reverse ? nc - 1 - i : i;
+      v[j] = i < nc ? base[static_cast<int64_t>(c) * RP] : 0.f;
+    }
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int i = i0 + j;
+      if (i >= nc) break;
+      const int c = reverse ? nc - 1 - i : i;
+      // a segment starts here: nothing before it (after it, reverse) reaches it
+      if ((!reverse && c == nc0) || (reverse && c == nc0 - 1)) run = 0.f;
+      base[static_cast<int64_t>(c) * RP] = run;
+      run += v[j];
+    }
+  }
+}
+
+// ---------------------------------------------------------------- chunk expand
+// For every chunk c: db_c += a_c dD_c ([C, R] x [R, P]) and
+// da_c += b_c dD_c^T ([C, P] x [P, R]).  Shared: a_c^T [RA][CS], b_c^T
+// [PB][CS], dD [R][PB], dD^T [P][RA] (zero-padded), so every 8 x 4 tile
+// reads two 16-byte words of rows and one of dD per 32 FMAs.
+__global__ void __launch_bounds__(256) kattn_chunk_expand_kernel(
+    const float* __restrict__ a, const float* __restrict__ b, const float* __restrict__ dD,
+    float* __restrict__ da, float* __restrict__ db, int T, int C, int R, int P) {
+  extern __shared__ float4 sm4[];
+  float* sm = reinterpret_cast<float*>(sm4);
+  const int c = blockIdx.x, s = blockIdx.y, nc = gridDim.x;
+  const int RA = round_up(R, 8), PB = round_up(P, 8), CS = round_up(C, 8);
+  float* saT = sm;                 // [RA][CS]
+  float* sbT = saT + RA * CS;      // [PB][CS]
+  float* sd = sbT + PB * CS;       // [RA][PB]  dD
+  float* sdT = sd + RA * PB;       // [PB][RA]  dD^T
+  const int64_t row0 = static_cast<int64_t>(c) * C;
+  stage_rows_t(saT, a + static_cast<int64_t>(s) * T * R, c * C, C, T, R, RA, CS);
+  stage_rows_t(sbT, b + static_cast<int64_t>(s) * T * P, c * C, C, T, P, PB, CS);
+  const float* dd = dD + (static_cast<int64_t>(s) * nc + c) * R * P;
+  for (int e = threadIdx.x; e < RA * PB; e += blockDim.x) {
+    const int r = e / PB, p = e % PB;
+    const float v = (r < R && p < P) ? dd[r * P + p] : 0.f;
+    sd[e] = v;
+    sdT[p * RA + r] = v;
+  }
+  for (int e = threadIdx.x; e < (CS - C) * (RA + PB); e += blockDim.x) {
+    // rows past the chunk in the transposed tiles stay zero
+    const int w = e / (CS - C), i = C + e % (CS - C);
+    if (w < RA) saT[w * CS + i] = 0.f;
+    else sbT[(w - RA) * CS + i] = 0.f;
+  }
+  cp_async_wait_all();
+  __syncthreads();
+  const int rows = static_cast<int>(T - row0 < C ? T - row0 : C);
+  // db tiles: 8 rows x 4 p, K = R; then da tiles: 8 rows x 4 r, K = P
+  const int tb = (CS / 8) * (PB / 4), ta = (CS / 8) * (RA / 4);
+  for (int t = threadIdx.x; t < tb + ta; t += blockDim.x) {
+    const bool is_b = t < tb;
+    const int u = is_b ? t : t - tb;
+    const int W = is_b ? PB : RA;          // output width (padded)
+    const int K = is_b ? RA : PB;          // contraction length (padded)
+    const float* X = is_b ? saT : sbT;     // [K][CS]
+    const float* Y = is_b ? sd : sdT;      // [K][W]
+    const int i0 = (u / (W / 4)) * 8, j0 = (u % (W / 4)) * 4;
+    float acc[8][4];
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+#pragma unroll
+      for (int j = 0; j < 4; ++j) acc[i][j] = 0.f;
+#pragma unroll 4
+    for (int k = 0; k < K; ++k) {
+      const float4 x0 = *reinterpret_cast<const float4*>(X + k * CS + i0);
+      const float4 x1 = *reinterpret_cast<const float4*>(X + k * CS + i0 + 4);
+      const float4 y = *reinterpret_cast<const float4*>(Y + k * W + j0);
+      const float xv[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+      const float yv[4] = {y.x, y.y, y.z, y.w};
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(xv[i], yv[j], acc[i][j]);
+    }
+    const int Wo = is_b ? P : R;
+    float* dst = (is_b ? db + static_cast<int64_t>(s) * T * P : da + static_cast<int64_t>(s) * T * R) +
+                 row0 * Wo;
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+        if (i0 + i < rows && j0 + j < Wo) dst[(i0 + i) * Wo + j0 + j] += acc[i][j];
+  }
+}
+
+// ---------------------------------------------------------------- query by type
+// out[s, i] (+)= phi[s, i] U[s, i mod nU] for i < T_R.  One CTA per (type h,
+// sequence); thread = output column p (one or more); the rows of type h
+// (h, h + nU, ...) go QT_ROWS at a time through shared memory, U_h is read
+// once per pass straight from global memory (a warp reads consecutive p).
+__global__ void __launch_bounds__(128) kattn_query_kernel(
+    const float* __restrict__ phi, int64_t phi_sb, const float* __restrict__ U,
+    float* __restrict__ out, int64_t out_sb, int T_R, int R, int P, int nU, int accumulate) {
+  extern __shared__ float4 sm4[];
+  float* sph = reinterpret_cast<float*>(sm4);   // [QT_ROWS][RA]
+  const int h = blockIdx.x, s = blockIdx.y;
+  const int RA = round_up(R, 4);
+  const float* Uh = U + (static_cast<int64_t>(s) * nU + h) * R * P;
+  const float* ph = phi + s * phi_sb;
+  float* os = out + s * out_sb;
+  const int n_rows = h < T_R ? (T_R - h + nU - 1) / nU : 0;
+  for (int g0 = 0; g0 < n_rows; g0 += QT_ROWS) {
+    const int ng = min(QT_ROWS, n_rows - g0);
+    __syncthreads();
+    for (int e = threadIdx.x; e < QT_ROWS * RA; e += blockDim.x) {
+      const int i = e / RA, r = e % RA;
+      sph[e] = (i < ng && r < R)
+                   ? ph[static_cast<int64_t>(h + (g0 + i) * static_cast<int64_t>(nU)) * R + r]
+                   : 0.f;
+    }
+    __syncthreads();
+    for (int p = threadIdx.x; p < P; p += blockDim.x) {
+      float acc[QT_ROWS];
+#pragma unroll
+      for (int i = 0; i < QT_ROWS; ++i) acc[i] = 0.f;
+      for (int r0 = 0; r0 < RA; r0 += 4) {
+        float u[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) u[j] = (r0 + j < R) ? __ldg(Uh + (r0 + j) * P + p) : 0.f;
+#pragma unroll
+        for (int i = 0; i < QT_ROWS; ++i) {
+          const float4 x = *reinterpret_cast<const float4*>(sph + i * RA + r0);
+          acc[i] = fmaf(x.x, u[0], acc[i]);
+          acc[i] = fmaf(x.y, u[1], acc[i]);
+          acc[i] = fmaf(x.z, u[2], acc[i]);
+          acc[i] = fmaf(x.w, u[3], acc[i]);
+        }
+      }
+#pragma unroll
+      for (int i = 0; i < QT_ROWS; ++i) {
+        if (i < ng) {
+          float* o = os + static_cast<int64_t>(h + (g0 + i) * static_cast<int64_t>(nU)) * P + p;
+          *o = accumulate ? *o + acc[i] : acc[i];
+        }
+      }
+    }
+  }
+}
+
+// dphi[s, i] = dout[s, i] U_h^T and dU[s, h] = sum over rows i of type h of
+// phi[s, i]^T dout[s, i].  One CTA per (h, sequence); rows go QT_ROWS at a
+// time through shared memory (phi rows [QT_ROWS][RA], dout rows [QT_ROWS][PA]).
+// dU: thread = column p, 16 r at a time in registers, accumulated over the
+// row passes in shared memory [R][PA]; dphi: thread = r, walking U_h's row r.
+__global__ void __launch_bounds__(128) kattn_query_bwd_kernel(
+    const float* __restrict__ phi, int64_t phi_sb, const float* __restrict__ U,
+    const float* __restrict__ dout, int64_t dout_sb, float* __restrict__ dphi, int64_t dphi_sb,
+    float* __restrict__ dU, int T_R, int R, int P, int nU) {
+  extern __shared__ float4 sm4[];
+  const int RA = round_up(R, 4), PA = round_up(P, 4);
+  float* sph = reinterpret_cast<float*>(sm4);   // [QT_ROWS][RA]
+  float* sdo = sph + QT_ROWS * RA;              // [QT_ROWS][PA]
+  float* sdu = sdo + QT_ROWS * PA;              // [R][PA]
+  const int h = blockIdx.x, s = blockIdx.y;
+  const float* Uh = U + (static_cast<int64_t>(s) * nU + h) * R * P;
+  float* dUh = dU + (static_cast<int64_t>(s) * nU + h) * R * P;
+  const int n_rows = h < T_R ? (T_R - h + nU - 1) / nU : 0;
+  for (int e = threadIdx.x; e < R * PA; e += blockDim.x) sdu[e] = 0.f;
+  for (int g0 = 0; g0 < n_rows; g0 += QT_ROWS) {
+    const int ng = min(QT_ROWS, n_rows - g0);
+    __syncthreads();
+    for (int e = threadIdx.x; e < QT_ROWS * RA; e += blockDim.x) {
+      const int i = e / RA, r = e % RA;
+      const int64_t row = h + (g0 + i) * static_cast<int64_t>(nU);
+      sph[e] = (i < ng && r < R) ? phi[s * phi_sb + row * R + r] : 0.f;
+    }
+    for (int e = threadIdx.x; e < QT_ROWS * PA; e += blockDim.x) {
+      const int i = e / PA, p = e % PA;
+      const int64_t row = h + (g0 + i) * static_cast<int64_t>(nU);
+      sdo[e] = (i < ng && p < P) ? dout[s * dout_sb + row * P + p] : 0.f;
+    }
+    __syncthreads();
+    // dU: column p, 16 r per round
+    for (int p = threadIdx.x; p < P; p += blockDim.x) {
+      for (int r0 = 0; r0 < R; r0 += 16) {
+        float acc[16];
+#pragma unroll
+        for (int j = 0; j < 16; ++j) acc[j] = 0.f;
+        for (int i = 0; i < ng; ++i) {
+          const float d = sdo[i * PA + p];
+#pragma unroll
+          for (int j = 0; j < 16; j += 4) {
+            if (r0 + j < RA) {
+              const float4 x = *reinterpret_cast<const float4*>(sph + i * RA + r0 + j);
+              acc[j] = fmaf(x.x, d, acc[j]);
+              acc[j + 1] = fmaf(x.y, d, acc[j + 1]);
+              acc[j + 2] = fmaf(x.z, d, acc[j + 2]);
+              acc[j + 3] = fmaf(x.w, d, acc[j + 3]);
+            }
+          }
+        }
+#pragma unroll
+        for (int j = 0; j < 16; ++j)
+          if (r0 + j < R) sdu[(r0 + j) * PA + p] += acc[j];
+      }
+    }
+    // dphi: row r of U_h against each dout row
+    for (int r = threadIdx.x; r < R; r += blockDim.x) {
+      float acc[QT_ROWS];
+#pragma unroll
+      for (int i = 0; i < QT_ROWS; ++i) acc[i] = 0.f;
+      const float* ur = Uh + static_cast<int64_t>(r) * P;
+      for (int p0 = 0; p0 < PA; p0 += 4) {
+        float u[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) u[j] = (p0 + j < P) ? __ldg(ur + p0 + j) : 0.f;
+#pragma unroll
+        for (int i = 0; i < QT_ROWS; ++i) {
+          const float4 d = *reinterpret_cast<const float4*>(sdo + i * PA + p0);
+          acc[i] = fmaf(d.x, u[0], acc[i]);
+          acc[i] = fmaf(d.y, u[1], acc[i]);
+          acc[i] = fmaf(d.z, u[2], acc[i]);
+          acc[i] = fmaf(d.w, u[3], acc[i]);
+        }
+      }
+#pragma unroll
+      for (int i = 0; i < QT_ROWS; ++i)
+        if (i < ng)
+          dphi[s * dphi_sb + (h + (g0 + i) * static_cast<int64_t>(nU)) * R + r] = acc[i];
+    }
+  }
+  __syncthreads();
+  for (int e = threadIdx.x; e < R * P; e += blockDim.x) dUh[e] = sdu[(e / P) * PA + e % P];
+}
+
+cudaStream_t st(void* s) { return static_cast<cudaStream_t>(s); }
+
+int launch_ok() { return cudaGetLastError() == cudaSuccess ? SMAT_OK : SMAT_ERR_LAUNCH; }
+
+template <typename K>
+int allow_smem(K kernel, int bytes) {
+  return cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes) ==
+                 cudaSuccess
+             ? SMAT_OK
+             : SMAT_ERR_LAUNCH;
+}
+
+int sum_smem(int C, int R, int P) { return C * (round_up(R, 8) + round_up(P, 4)) * 4; }
+int expand_smem(int C, int R, int P) {
+  const int RA = round_up(R, 8), PB = round_up(P, 8), CS = round_up(C, 8);
+  return (RA * CS + PB * CS + 2 * RA * PB) * 4;
+}
+
+}  // namespace
+
+extern "C" {
+
+int smat_kattn_chunk_prefix(const float* a, const float* b, float* out, int nb, int T, int C,
+                            int R, int P, int nc0, int reverse, void* stream) {
+  if (!a || !b || !out) return SMAT_ERR_NULL_POINTER;
+  if (nb < 1 || nb > 65535 || T < 1 || C < 1 || R < 1 || P < 1) return SMAT_ERR_BAD_SHAPE;
+  const int nc = (T + C - 1) / C;
+  if (nc0 < 0 || nc0 > nc || sum_smem(C, R, P) > GLUE_SMEM_MAX) return SMAT_ERR_BAD_SHAPE;
+  const int smem = sum_smem(C, R, P);
+  int rc = allow_smem(kattn_chunk_sum_kernel, smem);
+  if (rc) return rc;
+  const int tiles = (round_up(R, 8) / 8) * (round_up(P, 4) / 4);
+  const int threads = std::min(256, round_up(tiles, 32));
+  kattn_chunk_sum_kernel<<<dim3(nc, nb), threads, smem, st(stream)>>>(a, b, out, T, C, R, P);
+  if ((rc = launch_ok())) return rc;
+  const int64_t RP = static_cast<int64_t>(R) * P;
+  kattn_seg_scan_kernel<<<dim3(static_cast<unsigned>((RP + 255) / 256), nb), 256, 0,
+                          st(stream)>>>(out, nc, RP, nc0, reverse ? 1 : 0);
+  return launch_ok();
+}
+
+int smat_kattn_chunk_expand(const float* a, const float* b, const float* dD, float* da,
+                            float* db, int nb, int T, int C, int R, int P, void* stream) {
+  if (!a || !b || !dD || !da || !db) return SMAT_ERR_NULL_POINTER;
+  if (nb < 1 || nb > 65535 || T < 1 || C < 1 || R < 1 || P < 1) return SMAT_ERR_BAD_SHAPE;
+  const int smem = expand_smem(C, R, P);
+  if (smem > GLUE_SMEM_MAX) return SMAT_ERR_BAD_SHAPE;
+  int rc = allow_smem(kattn_chunk_expand_kernel, smem);
+  if (rc) return rc;
+  const int nc = (T + C - 1) / C;
+  kattn_chunk_expand_kernel<<<dim3(nc, nb), 256, smem, st(stream)>>>(a, b, dD, da, db, T, C, R,
+                                                                    P);
+  return launch_ok();
+}
+
+int smat_kattn_query_by_type(const float* phi, int64_t phi_seq_stride, const float* U,
+                             float* out, int64_t out_seq_stride, int nb, int T_R, int R, int P,
+                             int nU, int accumulate, void* stream) {
+  if (!phi || !U || !out) return SMAT_ERR_NULL_POINTER;
+  if (nb < 1 || nb > 65535 || T_R < 0 || R < 1 || P < 1 || nU < 1 || phi_seq_stride < 0 ||
+      out_seq_stride < 0)
+    return SMAT_ERR_BAD_SHAPE;
+  if (T_R == 0) return SMAT_OK;
+  const int smem = QT_ROWS * round_up(R, 4) * 4;
+  if (smem > GLUE_SMEM_MAX) return SMAT_ERR_BAD_SHAPE;
+  int rc = allow_smem(kattn_query_kernel, smem);
+  if (rc) return rc;
+  const int threads = std::min(128, round_up(P, 32));
+  kattn_query_kernel<<<dim3(std::min(nU, T_R), nb), threads, smem, st(stream)>>>(
+      phi, phi_seq_stride, U, out, out_seq_stride, T_R, R, P, nU, accumulate ? 1 : 0);
+  return launch_ok();
+}
+
+int smat_kattn_query_by_type_bwd(const float* phi, int64_t phi_seq_stride, const float* U,
+                                 const float* dout, int64_t dout_seq_stride, float* dphi,
+                                 int64_t dphi_seq_stride, float* dU, int nb, int T_R, int R,
+                                 int P, int nU, void* stream) {
+  if (!phi || !U || !dout || !dphi || !dU) return SMAT_ERR_NULL_POINTER;
+  if (nb < 1 || nb > 65535 || T_R < 0 || R < 1 || P < 1 || nU < 1 || phi_seq_stride < 0 ||
+      dout_seq_stride < 0 || dphi_seq_stride < 0)
+    return SMAT_ERR_BAD_SHAPE;
+  const int RA = round_up(R, 4), PA = round_up(P, 4);
+  const int smem = (QT_ROWS * (RA + PA) + R * PA) * 4;
+  if (smem > GLUE_SMEM_MAX) return SMAT_ERR_BAD_SHAPE;
+  int rc = allow_smem(kattn_query_bwd_kernel, smem);
+  if (rc) return rc;
+  // every type gets a CTA: types without rows write dU_h = 0
+  kattn_query_bwd_kernel<<<dim3(nU, nb), 128, smem, st(stream)>>>(
+      phi, phi_seq_stride, U, dout, dout_seq_stride, dphi, dphi_seq_stride, dU, T_R, R, P, nU);
+  return launch_ok();
+}
+
+}  // extern "C"

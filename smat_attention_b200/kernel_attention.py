@@ -32,6 +32,7 @@ lower precision are promoted); there is no CPU path.
 
 from __future__ import annotations
 
+import contextlib
 import ctypes
 
 import numpy as np
@@ -42,7 +43,8 @@ from .mask import MaskSpec
 
 __all__ = ["chunk_local", "pool", "incidence", "segmented_causal_scan", "pool_profiles",
            "apply_incidence", "query_by_type", "walsh_incidence", "zeta_transform",
-           "smat_attention", "SmatDecoder", "normalise"]
+           "direct_long_range", "smat_attention", "SmatDecoder", "normalise", "make_phi",
+           "featurise", "PhaseTimer"]
 
 _vp, _ci, _cl = ctypes.c_void_p, ctypes.c_int, ctypes.c_int64
 SIGNATURES = {
@@ -57,6 +59,12 @@ SIGNATURES = {
                                      _vp]),
     "smat_kattn_normalise_fwd": (_ci, [_vp, _vp, _cl, _ci, _vp]),
     "smat_kattn_normalise_bwd": (_ci, [_vp, _vp, _vp, _cl, _ci, _vp]),
+    "smat_kattn_chunk_prefix": (_ci, [_vp, _vp, _vp, _ci, _ci, _ci, _ci, _ci, _ci, _ci, _vp]),
+    "smat_kattn_chunk_expand": (_ci, [_vp, _vp, _vp, _vp, _vp, _ci, _ci, _ci, _ci, _ci, _vp]),
+    "smat_kattn_query_by_type": (_ci, [_vp, _cl, _vp, _vp, _cl, _ci, _ci, _ci, _ci, _ci, _ci,
+                                       _vp]),
+    "smat_kattn_query_by_type_bwd": (_ci, [_vp, _cl, _vp, _vp, _cl, _vp, _cl, _vp, _ci, _ci,
+                                           _ci, _ci, _ci, _vp]),
 }
 CHUNK = 128
 _bound = None
@@ -255,38 +263,96 @@ def normalise(H):
 
 
 # ---------------------------------------------------------------- the schedule
-def segmented_causal_scan(Phi, Psi, Vb, n: int, chunk: int = CHUNK):
+_BACKENDS = ("auto", "triton", "torch", "walsh")
+
+
+def _check_acc(acc_dtype):
+    if acc_dtype not in (None, torch.float32):
+        raise ValueError("the B200 kernels accumulate in fp32 (acc_dtype None or torch.float32); "
+                         "fp64 belongs to the oracle")
+
+
+def _check_backend(name, value):
+    if value not in _BACKENDS:
+        raise ValueError(f"{name}={value!r}: expected one of {_BACKENDS}")
+
+
+class _CausalScan(torch.autograd.Function):
+    """``[[L_n, 0], [0, L_{T_R}]] Phi Psi^T Vb`` on whole chunks: the chunk
+    prefix kernel (summaries ``Psi_c^T Vb_c`` and their shifted, segmented scan,
+    ``Sin``), then the tcgen05 chunk pass.  Backward: the chunk pass's three
+    gradients, ``dD`` = the reverse segmented scan of ``Phi_c^T dOut_c`` (the
+    same prefix kernel), and its expansion into ``dPsi`` and ``dVb``."""
+
+    @staticmethod
+    def forward(ctx, Phi, Psi, Vb, nc0):
+        nb, T, r = Phi.shape
+        p = Vb.shape[-1]
+        nc = T // CHUNK
+        q, k, v = _f32(Phi), _f32(Psi), _f32(Vb)
+        L = _L()
+        Sin = torch.empty(nb, nc, r, p, dtype=torch.float32, device=q.device)
+        _lib.check("smat_kattn_chunk_prefix", L.smat_kattn_chunk_prefix(
+            k.data_ptr(), v.data_ptr(), Sin.data_ptr(), nb, T, CHUNK, r, p, nc0, 0, _stream(k)))
+        out = torch.empty(nb, T, p, dtype=torch.float32, device=q.device)
+        _lib.check("smat_kattn_chunk_local_fwd", L.smat_kattn_chunk_local_fwd(
+            q.data_ptr(), k.data_ptr(), v.data_ptr(), Sin.data_ptr(), out.data_ptr(), nb * nc,
+            CHUNK, r, p, _err(q.device), _stream(q)))
+        ctx.save_for_backward(q, k, v, Sin)
+        ctx.nc0 = nc0
+        ctx.dtypes = (Phi.dtype, Psi.dtype, Vb.dtype)
+        return out
+
+    @staticmethod
+    def backward(ctx, dout):
+        q, k, v, Sin = ctx.saved_tensors
+        nb, T, r = q.shape
+        p = v.shape[-1]
+        nc = T // CHUNK
+        do = dout.float().contiguous()
+        dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
+        L = _L()
+        s = _stream(q)
+        _lib.check("smat_kattn_chunk_local_bwd", L.smat_kattn_chunk_local_bwd(
+            q.data_ptr(), k.data_ptr(), v.data_ptr(), Sin.data_ptr(), do.data_ptr(),
+            dq.data_ptr(), dk.data_ptr(), dv.data_ptr(), nb * nc, CHUNK, r, p, _err(q.device), s))
+        dD = torch.empty_like(Sin)
+        _lib.check("smat_kattn_chunk_prefix", L.smat_kattn_chunk_prefix(
+            q.data_ptr(), do.data_ptr(), dD.data_ptr(), nb, T, CHUNK, r, p, ctx.nc0, 1, s))
+        _lib.check("smat_kattn_chunk_expand", L.smat_kattn_chunk_expand(
+            k.data_ptr(), v.data_ptr(), dD.data_ptr(), dk.data_ptr(), dv.data_ptr(), nb, T, CHUNK,
+            r, p, s))
+        return tuple(g.to(t) for g, t in zip((dq, dk, dv), ctx.dtypes)) + (None,)
+
+
+def segmented_causal_scan(Phi, Psi, Vb, n: int, chunk: int = CHUNK, acc_dtype=None,
+                          backend: str = "auto"):
     """``[[L_n, 0], [0, L_{T_R}]] Phi Psi^T Vb`` by chunks with one reset at ``n``
-    (reference ``attention.py:134-192``): chunk summaries ``Psi_c^T Vb_c``, an
-    exclusive prefix sum inside each segment, then :func:`chunk_local`."""
+    (reference ``attention.py:134-192``): chunk summaries ``Psi_c^T Vb_c``, a
+    shifted prefix sum inside each segment (a chunk's own summary never enters
+    its prefix, and the landmark segment never reaches the recent one), then
+    the chunk pass; all in ``libsmat_b200.so`` kernels, fp32.  ``backend`` takes
+    the reference's names; every one runs these kernels."""
+    _check_acc(acc_dtype)
+    _check_backend("backend", backend)
     if chunk != CHUNK:
         raise ValueError(f"the chunk-local kernel runs chunks of {CHUNK} rows")
     nb, T, r = Phi.shape
-    p = Vb.shape[-1]
     C = CHUNK
     if n % C:
         raise ValueError(f"segment boundary n={n} is not a multiple of chunk={C}")
     pad = (-T) % C
-    Phi, Psi, Vb = (x.float() for x in (Phi, Psi, Vb))
-    if pad:
-        Phi, Psi, Vb = (torch.nn.functional.pad(x, (0, 0, 0, pad)) for x in (Phi, Psi, Vb))
-    nc = (T + pad) // C
-    nc0 = n // C
-    Phi_c, Psi_c = Phi.reshape(nb, nc, C, r), Psi.reshape(nb, nc, C, r)
-    Vb_c = Vb.reshape(nb, nc, C, p)
-    D = Psi_c.transpose(-1, -2) @ Vb_c                                  # (nb, nc, r, p)
-    # exclusive prefix sums inside each segment: inclusive cumsum minus D
-    if 0 < nc0 < nc:
-        Sin = torch.cat([torch.cumsum(D[:, :nc0], dim=1), torch.cumsum(D[:, nc0:], dim=1)],
-                        dim=1) - D
-    else:
-        Sin = torch.cumsum(D, dim=1) - D
-    out = chunk_local(Phi_c, Psi_c, Vb_c, Sin)
-    return out.reshape(nb, T + pad, p)[:, :T]
+    if pad:                                   # the tail lives in the recent segment
+        Phi, Psi, Vb = (torch.nn.functional.pad(x.float(), (0, 0, 0, pad))
+                        for x in (Phi, Psi, Vb))
+    out = _CausalScan.apply(Phi, Psi, Vb, n // C)
+    return out[:, :T] if pad else out
 
 
-def pool_profiles(Psi, Vb, spec: MaskSpec):
+def pool_profiles(Psi, Vb, spec: MaskSpec, acc_dtype=None, backend: str = "auto"):
     """``F`` over the landmark columns ``[n_P, n)`` (reference ``attention.py:199-236``)."""
+    _check_acc(acc_dtype)
+    _check_backend("backend", backend)
     return pool(Psi, Vb, spec.n_P, spec.n, spec.N0)
 
 
@@ -304,44 +370,92 @@ def walsh_incidence(F):
     return 0.5 * (tot + H.reshape(nb, N, r, p))
 
 
-def apply_incidence(F, spec: MaskSpec):
-    """``U_h = sum_{x in H_h} F_x`` (reference ``attention.py:239-285``): the CSR
-    gather-sum kernel, or the Walsh butterfly for the endpoint family."""
-    if spec.kind == "endpoint":
+def apply_incidence(F, spec: MaskSpec, *, backend: str = "auto", gather_chunk: int = 0):
+    """``U_h = sum_{x in H_h} F_x`` (reference ``attention.py:239-285``): the Walsh
+    butterfly for the endpoint family under ``"auto"`` / ``"walsh"`` (as in the
+    reference), else the CSR gather-sum kernel (any row degree).
+    ``gather_chunk`` is the reference's torch-path knob and has no effect."""
+    _check_backend("backend", backend)
+    if spec.kind == "endpoint" and backend in ("auto", "walsh"):
         return walsh_incidence(F)
     return _incidence_csr(F, spec)
 
 
+class _Query(torch.autograd.Function):
+    """``Y_i = Phi_i U_{i mod B}`` for the rows of ``Phi_rec`` (``query_by_type``
+    kernel; backward: ``query_by_type_bwd``)."""
+
+    @staticmethod
+    def forward(ctx, Phi_rec, U):
+        nb, T_R, r = Phi_rec.shape
+        B, p = U.shape[1], U.shape[-1]
+        ph, u = _f32(Phi_rec), _f32(U)
+        Y = torch.empty(nb, T_R, p, dtype=torch.float32, device=ph.device)
+        _lib.check("smat_kattn_query_by_type", _L().smat_kattn_query_by_type(
+            ph.data_ptr(), T_R * r, u.data_ptr(), Y.data_ptr(), T_R * p, nb, T_R, r, p, B, 0,
+            _stream(ph)))
+        ctx.save_for_backward(ph, u)
+        ctx.dtypes = (Phi_rec.dtype, U.dtype)
+        return Y
+
+    @staticmethod
+    def backward(ctx, dY):
+        ph, u = ctx.saved_tensors
+        nb, T_R, r = ph.shape
+        B, p = u.shape[1], u.shape[-1]
+        d = dY.float().contiguous()
+        dph, du = torch.empty_like(ph), torch.empty_like(u)
+        _lib.check("smat_kattn_query_by_type_bwd", _L().smat_kattn_query_by_type_bwd(
+            ph.data_ptr(), T_R * r, u.data_ptr(), d.data_ptr(), T_R * p, dph.data_ptr(), T_R * r,
+            du.data_ptr(), nb, T_R, r, p, B, _stream(ph)))
+        return dph.to(ctx.dtypes[0]), du.to(ctx.dtypes[1])
+
+
+class _QueryAdd(torch.autograd.Function):
+    """``H[:, n:] += query_by_type(Phi[:, n:], U)`` in place on ``H`` (no
+    ``(nb, T_R, p)`` intermediate); ``Phi`` is the whole ``(nb, T, r)``."""
+
+    @staticmethod
+    def forward(ctx, H, Phi, U, n):
+        nb, T, p = H.shape
+        r, B = Phi.shape[-1], U.shape[1]
+        ph, u = _f32(Phi), _f32(U)
+        if H.dtype != torch.float32 or not H.is_contiguous():
+            raise ValueError("H must be a contiguous fp32 tensor")
+        T_R = T - n
+        _lib.check("smat_kattn_query_by_type", _L().smat_kattn_query_by_type(
+            ph.data_ptr() + 4 * n * r, T * r, u.data_ptr(), H.data_ptr() + 4 * n * p, T * p, nb,
+            T_R, r, p, B, 1, _stream(ph)))
+        ctx.mark_dirty(H)
+        ctx.save_for_backward(ph, u)
+        ctx.n = n
+        ctx.dtypes = (Phi.dtype, U.dtype)
+        return H
+
+    @staticmethod
+    def backward(ctx, dH):
+        ph, u = ctx.saved_tensors
+        n = ctx.n
+        nb, T, r = ph.shape
+        B, p = u.shape[1], u.shape[-1]
+        d = dH.float().contiguous()
+        dph = torch.empty_like(ph)
+        if n:
+            dph[:, :n].zero_()
+        du = torch.empty_like(u)
+        _lib.check("smat_kattn_query_by_type_bwd", _L().smat_kattn_query_by_type_bwd(
+            ph.data_ptr() + 4 * n * r, T * r, u.data_ptr(), d.data_ptr() + 4 * n * p, T * p,
+            dph.data_ptr() + 4 * n * r, T * r, du.data_ptr(), nb, T - n, r, p, B, _stream(ph)))
+        return dH, dph.to(ctx.dtypes[0]), du.to(ctx.dtypes[1]), None
+
+
 def query_by_type(Phi_rec, U, spec: MaskSpec):
     """``Ybar_i = Phi_i U_{(i - n) mod B}`` for the recent rows (reference
-    ``attention.py:310-330``): one batched GEMM over the stride-B slices."""
-    nb, T_R, r = Phi_rec.shape
-    B, p = spec.B, U.shape[-1]
-    U = U.float()
-    c, rem = divmod(T_R, B)
-    pieces = []
-    if c:
-        head = Phi_rec[:, :c * B].float().reshape(nb, c, B, r).transpose(1, 2)   # (nb,B,c,r)
-        pieces.append((head @ U).transpose(1, 2).reshape(nb, c * B, p))
-    if rem:
-        tail = Phi_rec[:, c * B:].float().unsqueeze(-2)
-        pieces.append((tail @ U[:, :rem]).squeeze(-2))
-    return torch.cat(pieces, dim=1)
-
-
-def _add_query_by_type(H_rec, Phi_rec, U, spec: MaskSpec):
-    """``H_rec += query_by_type(Phi_rec, U, spec)`` in place, with no
-    intermediate copy of the ``(nb, T_R, p)`` result."""
-    nb, T_R, r = Phi_rec.shape
-    B, p = spec.B, U.shape[-1]
-    U = U.float()
-    c, rem = divmod(T_R, B)
-    if c:
-        head = Phi_rec[:, :c * B].float().reshape(nb, c, B, r).transpose(1, 2)   # (nb,B,c,r)
-        H_rec[:, :c * B].view(nb, c, B, p).add_((head @ U).transpose(1, 2))
-    if rem:
-        tail = Phi_rec[:, c * B:].float().unsqueeze(-2)
-        H_rec[:, c * B:].add_((tail @ U[:, :rem]).squeeze(-2))
+    ``attention.py:310-330``): the ``query_by_type`` kernel, one CTA per row
+    type and sequence."""
+    if U.shape[1] != spec.B:
+        raise ValueError(f"U has {U.shape[1]} types, the spec {spec.B}")
+    return _Query.apply(Phi_rec, U)
 
 
 def zeta_transform(F):
@@ -357,31 +471,179 @@ def zeta_transform(F):
     return H.reshape(nb, N, r, p)
 
 
-def smat_attention(Phi, Psi, Vb, spec: MaskSpec, *, chunk: int = CHUNK, g=None):
-    """The pooled schedule of the reference's ``smat_attention``
-    (``attention.py:391-455``) on these kernels; returns ``(nb, T, p - 1)``
-    fp32 (the last column of ``Vb`` is the normaliser's)."""
+def direct_long_range(Psi, Vb, spec: MaskSpec, acc_dtype=None, type_chunk: int = 64):
+    """The unpooled comparison backend (reference ``attention.py:333-362``):
+    every landmark column scattered to its row types, ``U_h = sum over the
+    columns of type h of Psi_j Vb_j^T`` -- a factor ``~T^{1/d}`` more work than
+    the pooled route; batched library GEMMs over the reference's padded column
+    table ``spec.type_cols_t`` (``to_device(spec, device, want_direct=True)``)."""
+    _check_acc(acc_dtype)
+    cols = spec.type_cols_t
+    if cols is None:
+        raise ValueError("the direct backend needs to_device(..., want_direct=True)")
+    nb, _, r = Psi.shape
+    p = Vb.shape[-1]
+    B, kap = cols.shape
+    Ps = torch.cat([Psi[:, spec.n_P:spec.n].float(), Psi.new_zeros(nb, 1, r, dtype=torch.float32)],
+                   dim=1)
+    Vs = torch.cat([Vb[:, spec.n_P:spec.n].float(), Vb.new_zeros(nb, 1, p, dtype=torch.float32)],
+                   dim=1)
+    U = torch.empty(nb, B, r, p, device=Psi.device, dtype=torch.float32)
+    for lo in range(0, B, type_chunk):
+        hi = min(lo + type_chunk, B)
+        c = cols[lo:hi].reshape(-1).long()
+        U[:, lo:hi] = (Ps[:, c].reshape(nb, hi - lo, kap, r).transpose(-1, -2)
+                       @ Vs[:, c].reshape(nb, hi - lo, kap, p))
+    return U
+
+
+def _nullcontext_timer(name):
+    return contextlib.nullcontext()
+
+
+def smat_attention(Phi, Psi, Vb, spec: MaskSpec, *, chunk: int = CHUNK, g=None, acc_dtype=None,
+                   timer=None, long_range: str = "pooled", scan_backend: str = "auto",
+                   incidence_backend: str = "auto", return_parts: bool = False):
+    """The reference's op ``smat_attention`` (``attention.py:391-455``) on these
+    kernels: the long-range pass (pool, incidence, the rank-one ``n_P`` term,
+    the per-type query) and the segmented causal scan, summed before one
+    division.  Returns ``(nb, T, p - 1)`` fp32, or ``(out, parts)`` with
+    ``return_parts`` (``U``, ``Y_lr``, ``H``; ``zeta`` for the endpoint family;
+    ``H``, ``Y_ex`` for ``"subtractive"``).
+
+    * ``long_range``: ``"pooled"`` (the schedule), ``"direct"`` (the unpooled
+      comparison, needs ``to_device(spec, dev, want_direct=True)``), or
+      ``"subtractive"`` (one unbroken scan minus the excluded mass, the form
+      the reference computes only to measure its cancellation);
+    * ``timer``: a callable ``timer(name)`` returning a context manager around
+      each phase (``lr_pool``, ``lr_incidence``, ``lr_query``, ``zeta``,
+      ``scan``, ``normalise``), e.g. :class:`PhaseTimer`;
+    * ``acc_dtype``: ``None`` or ``torch.float32`` (the kernels accumulate in
+      fp32; the fp64 path is the oracle's);
+    * ``scan_backend`` / ``incidence_backend``: the reference's names, all
+      running these kernels (``"walsh"`` / ``"auto"`` pick the Walsh butterfly
+      for the endpoint family, as there)."""
+    _check_acc(acc_dtype)
+    _check_backend("scan_backend", scan_backend)
+    _check_backend("incidence_backend", incidence_backend)
     if spec.kind not in ("geometric", "endpoint"):
         raise ValueError("smat_attention needs an M^(d) spec from build_mask")
+    if long_range not in ("pooled", "direct", "subtractive"):
+        raise ValueError(f"unknown long_range {long_range!r}")
+    tm = timer or _nullcontext_timer
     n = spec.n
-    F = pool_profiles(Psi, Vb, spec)
-    U = apply_incidence(F, spec)
-    if spec.n_P:
-        b = Psi[:, :spec.n_P].float().transpose(-1, -2) @ Vb[:, :spec.n_P].float()
-        U = U + b.unsqueeze(1)
+    parts = {}
+    if long_range == "subtractive":
+        if spec.kind != "geometric":
+            raise ValueError("the subtractive form is defined for the geometric family")
+        with tm("lr_pool"):
+            F = pool_profiles(Psi, Vb, spec)
+        with tm("lr_incidence"):
+            U = apply_incidence(F, spec, backend=incidence_backend)
+            Ubar = F.sum(1, keepdim=True) - U
+        with tm("lr_query"):
+            Y_ex = query_by_type(Phi[:, n:], Ubar, spec)
+        with tm("scan"):
+            H = segmented_causal_scan(Phi, Psi, Vb, 0, chunk)
+        H = torch.cat([H[:, :n], H[:, n:] - Y_ex], dim=1)
+        with tm("normalise"):
+            out = normalise(H)
+            if g is not None:
+                out = out * g.unsqueeze(-1).to(out.dtype)
+        return (out, {"H": H, "Y_ex": Y_ex}) if return_parts else out
+
+    with tm("lr_pool"):
+        F = pool_profiles(Psi, Vb, spec)
+    with tm("lr_incidence"):
+        if long_range == "direct":
+            U = direct_long_range(Psi, Vb, spec)
+        else:
+            U = apply_incidence(F, spec, backend=incidence_backend)
+        if spec.n_P:                                   # the rank-one global term
+            b = Psi[:, :spec.n_P].float().transpose(-1, -2) @ Vb[:, :spec.n_P].float()
+            U = U + b.unsqueeze(1)
+    Y_lr = None
+    if spec.kind == "endpoint" or return_parts:
+        with tm("lr_query"):
+            Y_lr = query_by_type(Phi[:, n:], U, spec)
     if spec.kind == "endpoint":
-        Y_lr = query_by_type(Phi[:, n:], U, spec)
-        Fz = Psi[:, :n].float().unsqueeze(-1) * Vb[:, :n].float().unsqueeze(-2)
-        top = (Phi[:, :n].float().unsqueeze(-2) @ zeta_transform(Fz)).squeeze(-2)
-        loc = segmented_causal_scan(Phi[:, n:], Psi[:, n:], Vb[:, n:], 0, chunk)
+        with tm("zeta"):
+            Fz = Psi[:, :n].float().unsqueeze(-1) * Vb[:, :n].float().unsqueeze(-2)
+            top = (Phi[:, :n].float().unsqueeze(-2) @ zeta_transform(Fz)).squeeze(-2)
+        with tm("scan"):
+            loc = segmented_causal_scan(Phi[:, n:], Psi[:, n:], Vb[:, n:], 0, chunk)
         H = torch.cat([top, loc + Y_lr], dim=1)
+        parts["zeta"] = top
     else:
-        H = segmented_causal_scan(Phi, Psi, Vb, n, chunk)
-        _add_query_by_type(H[:, n:], Phi[:, n:], U, spec)
-    out = normalise(H)
-    if g is not None:
-        out = out * g.unsqueeze(-1).to(out.dtype)
-    return out
+        with tm("scan"):
+            H = segmented_causal_scan(Phi, Psi, Vb, n, chunk)
+        if Y_lr is None and not H.is_contiguous():   # a padded tail leaves a strided view
+            with tm("lr_query"):
+                Y_lr = query_by_type(Phi[:, n:], U, spec)
+        if Y_lr is not None:
+            H = torch.cat([H[:, :n], H[:, n:] + Y_lr], dim=1)
+        else:
+            with tm("lr_query"):   # added into the recent rows in place
+                H = _QueryAdd.apply(H, Phi, U, n)
+    parts.update(U=U, Y_lr=Y_lr, H=H)
+    with tm("normalise"):
+        out = normalise(H)
+        if g is not None:
+            out = out * g.unsqueeze(-1).to(out.dtype)
+    return (out, parts) if return_parts else out
+
+
+class PhaseTimer:
+    """``with timer("name"):`` attribution with CUDA events, accumulated per
+    name (the reference's ``PhaseTimer``, ``analysis/bench_prefill.py:51-75``);
+    pass it as ``smat_attention(..., timer=PhaseTimer(device))``."""
+
+    def __init__(self, device):
+        self.device = torch.device(device)
+        self.spans = []
+
+    @contextlib.contextmanager
+    def __call__(self, name):
+        a, b = (torch.cuda.Event(enable_timing=True) for _ in range(2))
+        a.record(torch.cuda.current_stream(self.device))
+        yield
+        b.record(torch.cuda.current_stream(self.device))
+        self.spans.append((name, a, b))
+
+    def results(self):
+        torch.cuda.synchronize(self.device)
+        out = {}
+        for name, a, b in self.spans:
+            out[name] = out.get(name, 0.0) + a.elapsed_time(b)
+        return out
+
+
+# ---------------------------------------------------------------- feature maps
+def make_phi(d_qk: int, r: int, *, kind: str = "elu1", device="cpu", dtype=torch.float32,
+             seed: int = 0):
+    """A strictly positive feature map ``R^{d_qk} -> R^r`` (reference
+    ``attention.py:82-97``): the same random projection for the same seed
+    (``N(0, 1) / sqrt(d_qk)`` drawn in fp64 from a CPU generator), then
+    ``elu + 1`` or ``relu + 1e-3``."""
+    gen = torch.Generator(device="cpu").manual_seed(seed)
+    W = (torch.randn(r, d_qk, generator=gen, dtype=torch.float64)
+         / np.sqrt(d_qk)).to(device=device, dtype=dtype)
+    if kind == "elu1":
+        return lambda x: torch.nn.functional.elu(x @ W.T) + 1.0
+    if kind == "relu":
+        return lambda x: torch.nn.functional.relu(x @ W.T) + 1e-3
+    raise ValueError(f"unknown feature map {kind!r}")
+
+
+def featurise(Q, K, V, phi, *, g=None, h=None):
+    """``(Q, K, V) -> (Phi, Psi, Vb)`` with the key gate ``h`` folded into
+    ``Psi`` and ``Vb = [V, 1]`` (reference ``attention.py:100-106``)."""
+    Phi = phi(Q)
+    Psi = phi(K)
+    if h is not None:
+        Psi = Psi * h.unsqueeze(-1)
+    ones = torch.ones(*V.shape[:-1], 1, device=V.device, dtype=V.dtype)
+    return Phi, Psi, torch.cat([V, ones], dim=-1)
 
 
 # ---------------------------------------------------------------- streaming decode

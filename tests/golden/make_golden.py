@@ -29,6 +29,14 @@ It imports the reference's ``smat`` package (``src/smat``) and records
     (``src/smat/attention.py:496-535``) prefilled with the first ``n`` columns
     and stepped through rows ``n .. T-1`` (fp64; ``dec``).
 
+``smat_module.npz``
+    The reference's ``Attention`` module in its plain ``"smat"`` arm
+    (``src/smat/model.py:112-343``; ``make_phi`` feature map, ``featurise``,
+    ``smat_attention`` on its torch path) for an ``M^(3)`` mask at chunk 128:
+    its weights, an input, the output and the input's gradient for a given
+    output gradient; and ``make_phi`` (``src/smat/attention.py:82-97``) applied
+    to a fixed input for both kinds.
+
 Nothing at test time imports the reference: the tests read only these files.
 """
 
@@ -163,6 +171,30 @@ def make_kattn(A, R, name, T, d, chunk, n_P, nb, r, dv, seed):
         dec=dec_out.numpy(), dec_words=np.array([dec.cache_words()]))
 
 
+def make_module(A, R, M, seed=300):
+    """The reference's ``Attention(arm="smat")`` forward and input gradient
+    (fp32, torch path on the CPU), plus ``make_phi`` outputs."""
+    torch.manual_seed(seed)
+    T, d_model, heads, nb = 512, 32, 2, 2
+    spec = R.build_mask(T, 3, chunk=128)
+    A.to_device(spec, "cpu")
+    mod = M.Attention(d_model, heads, "smat", spec=spec, r=32, chunk=128, seed=7)
+    g = torch.Generator().manual_seed(seed)
+    x = torch.randn(nb, T, d_model, generator=g)
+    dy = torch.randn(nb, T, d_model, generator=g)
+    xg = x.clone().requires_grad_(True)
+    y = mod(xg)
+    (y * dy).sum().backward()
+    xp = torch.randn(5, 16, generator=g)
+    phi_elu = A.make_phi(16, 8, seed=3)(xp)
+    phi_relu = A.make_phi(16, 8, kind="relu", seed=3)(xp)
+    np.savez_compressed(
+        os.path.join(HERE, "smat_module.npz"), args=np.array([T, d_model, heads, 32, 7]),
+        qkv=mod.qkv.weight.detach().numpy(), out_w=mod.out.weight.detach().numpy(),
+        x=x.numpy(), dy=dy.numpy(), y=y.detach().numpy(), dx=xg.grad.numpy(), xp=xp.numpy(),
+        phi_elu=phi_elu.numpy(), phi_relu=phi_relu.numpy())
+
+
 def main():
     ref = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("SMAT_REFERENCE")
     if not ref:
@@ -175,6 +207,8 @@ def main():
         make_softmax(A, R, name, T, BH, D, mask, seed=100 + i)
     for i, case in enumerate(KATTN_CASES):
         make_kattn(A, R, *case, seed=200 + i)
+    from smat import model as M
+    make_module(A, R, M)
     print("fixtures written to", HERE)
 
 

@@ -161,7 +161,7 @@ def test_kattn_header_symbols_exported():
     from smat_attention_b200 import kernel_attention as KA
     text = open(os.path.join(os.path.dirname(HEADER), "smat_kattn.h")).read()
     syms = sorted(set(re.findall(r"SMAT_API\s+\w+\**\s+\**(smat_\w+)\s*\(", text)))
-    assert len(syms) == 8 and set(syms) == set(KA.SIGNATURES)
+    assert len(syms) == 12 and set(syms) == set(KA.SIGNATURES)
     L = KA._L()
     assert L.smat_kattn_chunk_local_fwd(16, 16, 16, 16, 16, 1, 64, 64, 65, None, None) == 1
     assert L.smat_kattn_chunk_local_fwd(16, 16, 16, 16, 16, 1, 128, 48, 65, None, None) == 1

@@ -197,3 +197,184 @@ def test_normalise(cuda_device, P):
     ref.backward(dout.float().double())
     _close(out, ref.detach(), 1e-5, "out")
     _close(x.grad, r.grad, 1e-5, "dH")
+
+
+# ---------------------------------------------------------------- glue kernels
+def _chunk_prefix_ref(a, b, C, nc0, reverse):
+    """fp64 loops: the shifted, segmented prefix of the chunk products."""
+    nb, T, R = a.shape
+    P = b.shape[-1]
+    nc = -(-T // C)
+    pad = nc * C - T
+    a = torch.nn.functional.pad(a, (0, 0, 0, pad))
+    b = torch.nn.functional.pad(b, (0, 0, 0, pad))
+    D = a.reshape(nb, nc, C, R).transpose(-1, -2) @ b.reshape(nb, nc, C, P)
+    out = torch.zeros_like(D)
+    order = range(nc - 1, -1, -1) if reverse else range(nc)
+    run = torch.zeros_like(D[:, 0])
+    for c in order:
+        if (not reverse and c == nc0) or (reverse and c == nc0 - 1):
+            run = torch.zeros_like(run)
+        out[:, c] = run
+        run = run + D[:, c]
+    return out
+
+
+@pytest.mark.parametrize("T,R,P,nc0", [(1024, 64, 65, 4), (1000, 32, 17, 3), (512, 128, 129, 0),
+                                       (700, 20, 9, 6)])
+def test_chunk_prefix(cuda_device, T, R, P, nc0):
+    g = torch.Generator().manual_seed(T + R)
+    nb, C = 2, 128
+    a = _feat(nb, T, R, g=g).float()
+    b = torch.randn(nb, T, P, generator=g)
+    L = KA._L()
+    nc = -(-T // C)
+    for reverse in (0, 1):
+        out = torch.empty(nb, nc, R, P, device=cuda_device)
+        ad, bd = a.to(cuda_device), b.to(cuda_device)
+        assert L.smat_kattn_chunk_prefix(ad.data_ptr(), bd.data_ptr(), out.data_ptr(), nb, T, C,
+                                         R, P, nc0, reverse, None) == 0
+        torch.cuda.synchronize()
+        _close(out, _chunk_prefix_ref(a.double(), b.double(), C, nc0, reverse), 1e-5,
+               f"prefix reverse={reverse}")
+    # the segments never mix: the recent segment's prefixes are bitwise
+    # independent of the landmark chunks (and the other way round, reversed)
+    if 0 < nc0 < nc:
+        a2, b2 = a.clone(), b.clone()
+        a2[:, :nc0 * C] *= 3.0
+        b2[:, :nc0 * C] += 1.0
+        for x, y in ((a, b), (a2, b2)):
+            o = torch.empty(nb, nc, R, P, device=cuda_device)
+            xd, yd = x.to(cuda_device), y.to(cuda_device)
+            L.smat_kattn_chunk_prefix(xd.data_ptr(), yd.data_ptr(), o.data_ptr(), nb, T, C, R,
+                                      P, nc0, 0, None)
+            torch.cuda.synchronize()
+            if x is a:
+                first = o[:, nc0:].clone()
+            else:
+                assert torch.equal(first, o[:, nc0:])
+
+
+def test_chunk_expand(cuda_device):
+    g = torch.Generator().manual_seed(11)
+    nb, T, C, R, P = 2, 900, 128, 64, 65
+    nc = -(-T // C)
+    a, b = torch.randn(nb, T, R, generator=g), torch.randn(nb, T, P, generator=g)
+    dD = torch.randn(nb, nc, R, P, generator=g)
+    da0, db0 = torch.randn(nb, T, R, generator=g), torch.randn(nb, T, P, generator=g)
+    ad, bd, dDd = (x.to(cuda_device) for x in (a, b, dD))
+    da, db = da0.clone().to(cuda_device), db0.clone().to(cuda_device)
+    assert KA._L().smat_kattn_chunk_expand(ad.data_ptr(), bd.data_ptr(), dDd.data_ptr(),
+                                           da.data_ptr(), db.data_ptr(), nb, T, C, R, P,
+                                           None) == 0
+    torch.cuda.synchronize()
+    pad = nc * C - T
+    ap = torch.nn.functional.pad(a.double(), (0, 0, 0, pad)).reshape(nb, nc, C, R)
+    bp = torch.nn.functional.pad(b.double(), (0, 0, 0, pad)).reshape(nb, nc, C, P)
+    want_da = da0.double() + (bp @ dD.double().transpose(-1, -2)).reshape(nb, -1, R)[:, :T]
+    want_db = db0.double() + (ap @ dD.double()).reshape(nb, -1, P)[:, :T]
+    _close(da, want_da, 1e-5, "da")
+    _close(db, want_db, 1e-5, "db")
+
+
+@pytest.mark.parametrize("T,d,r,p", [(1024, 3, 64, 65), (2048, 3, 32, 33), (1000, 2, 20, 9)])
+def test_query_by_type(cuda_device, T, d, r, p):
+    spec = build_mask(T, d, chunk=8)
+    g = torch.Generator().manual_seed(T + r)
+    nb = 2
+    Phi_rec = torch.randn(nb, spec.T_R, r, generator=g, dtype=torch.float32).double()
+    U = torch.randn(nb, spec.B, r, p, generator=g, dtype=torch.float32).double()
+    dY = torch.randn(nb, spec.T_R, p, generator=g, dtype=torch.float32).double()
+    x, u = (t.float().to(cuda_device).requires_grad_(True) for t in (Phi_rec, U))
+    Y = KA.query_by_type(x, u, spec)
+    (Y * dY.float().to(cuda_device)).sum().backward()
+    torch.cuda.synchronize()
+    rx, ru = Phi_rec.clone().requires_grad_(True), U.clone().requires_grad_(True)
+    rY = OK.query_by_type(rx, ru, spec)
+    (rY * dY).sum().backward()
+    _close(Y, rY.detach(), 1e-5, "Y")
+    _close(x.grad, rx.grad, 1e-5, "dphi")
+    _close(u.grad, ru.grad, 1e-5, "dU")
+
+
+# ---------------------------------------------------------------- the op's arguments
+def test_op_arguments(cuda_device):
+    """return_parts, the phase timer, and the direct / subtractive long-range
+    forms against the pooled schedule and the oracle."""
+    T, d, r, dv = 2048, 3, 64, 64
+    spec = build_mask(T, d, chunk=128)
+    g = torch.Generator().manual_seed(5)
+    nb = 2
+    Phi, Psi = _feat(nb, T, r, g=g).float(), _feat(nb, T, r, g=g).float()
+    v = torch.randn(nb, T, dv, generator=g)
+    dev = lambda t: t.to(cuda_device)
+    Vb = torch.cat([dev(v), torch.ones(nb, T, 1, device=cuda_device)], -1)
+    tm = KA.PhaseTimer(cuda_device)
+    out, parts = KA.smat_attention(dev(Phi), dev(Psi), Vb, spec, timer=tm, return_parts=True,
+                                   acc_dtype=torch.float32, scan_backend="torch",
+                                   incidence_backend="triton")
+    phases = tm.results()
+    assert set(phases) >= {"lr_pool", "lr_incidence", "lr_query", "scan", "normalise"}
+    assert set(parts) == {"U", "Y_lr", "H"}
+    ref = OK.smat_attention(Phi.double(), Psi.double(),
+                            torch.cat([v.double(), torch.ones(nb, T, 1, dtype=torch.float64)],
+                                      -1), spec, chunk=128)
+    _close(out, ref, 2e-3, "pooled")
+    plain = KA.smat_attention(dev(Phi), dev(Psi), Vb, spec)
+    assert torch.equal(plain, out)      # the fused in-place query equals the split one
+    from smat_attention_b200.mask import to_device
+    to_device(spec, cuda_device, want_direct=True)
+    direct = KA.smat_attention(dev(Phi), dev(Psi), Vb, spec, long_range="direct")
+    _close(direct, ref, 2e-3, "direct")
+    sub, sparts = KA.smat_attention(dev(Phi), dev(Psi), Vb, spec, long_range="subtractive",
+                                    return_parts=True)
+    _close(sub, ref, 2e-3, "subtractive")
+    assert set(sparts) == {"H", "Y_ex"}
+    torch.cuda.synchronize()
+    assert check_device_errors() == 0
+
+
+def test_op_landmark_rows_do_not_see_recent_rows(cuda_device):
+    """Bitwise non-influence (the reference's property, tests/test_smat.py:292-324):
+    the landmark rows' outputs do not change when the recent rows' keys and
+    values do, since the scan's segments never mix and the long-range query
+    writes only recent rows."""
+    T, d, r, dv = 4096, 3, 64, 64
+    spec = build_mask(T, d, chunk=128)
+    n = spec.n
+    g = torch.Generator().manual_seed(9)
+    nb = 2
+    Phi, Psi = (_feat(nb, T, r, g=g).float().to(cuda_device) for _ in range(2))
+    v = torch.randn(nb, T, dv, generator=g).to(cuda_device)
+    outs = []
+    for bump in (0.0, 5.0):
+        Psi2, v2 = Psi.clone(), v.clone()
+        Psi2[:, n:] += bump
+        v2[:, n:] -= bump
+        Vb = torch.cat([v2, torch.ones(nb, T, 1, device=cuda_device)], -1)
+        outs.append(KA.smat_attention(Phi, Psi2, Vb, spec))
+    torch.cuda.synchronize()
+    assert torch.equal(outs[0][:, :n], outs[1][:, :n])
+    assert not torch.equal(outs[0][:, n:], outs[1][:, n:])
+
+
+def test_module_smat_arm_matches_reference_fixture(cuda_device):
+    """Attention(arm="smat") (featurise with make_phi of the same seed, then the
+    op on the B200 kernels) against the reference module's own output and input
+    gradient (tests/golden/smat_module.npz), within the op's 2e-3 TF32 bound."""
+    from smat_attention_b200.model import Attention
+    f = np.load(os.path.join(os.path.dirname(__file__), "golden", "smat_module.npz"))
+    T, d_model, heads, r, seed = (int(x) for x in f["args"])
+    spec = build_mask(T, 3, chunk=128)
+    m = Attention(d_model, heads, "smat", spec=spec, r=r, chunk=128, seed=seed,
+                  device=cuda_device)
+    with torch.no_grad():
+        m.qkv.weight.copy_(torch.from_numpy(f["qkv"]))
+        m.out.weight.copy_(torch.from_numpy(f["out_w"]))
+    x = torch.from_numpy(f["x"]).to(cuda_device).requires_grad_(True)
+    y = m(x)
+    (y * torch.from_numpy(f["dy"]).to(cuda_device)).sum().backward()
+    torch.cuda.synchronize()
+    assert check_device_errors() == 0
+    _close(y, torch.from_numpy(f["y"]), 2e-3, "y")
+    _close(x.grad, torch.from_numpy(f["dx"]), 2e-3, "dx")

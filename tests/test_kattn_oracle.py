@@ -72,7 +72,8 @@ def test_chunk_local_definition():
 
 def test_torch_parts_match_oracle():
     """The product module's torch-side parts (Walsh incidence for the endpoint
-    family, the zeta butterfly, the per-type query) against the oracle, on CPU."""
+    family, the zeta butterfly, the incidence's transposed CSR) against the
+    oracle, on CPU."""
     from smat_attention_b200 import kernel_attention as KA
     g = torch.Generator().manual_seed(3)
     spec = build_mask(1024, 10, chunk=64)                  # endpoint, B = N0 = 512
@@ -81,16 +82,6 @@ def test_torch_parts_match_oracle():
     Fz = torch.randn(1, 64, 2, 3, generator=g, dtype=torch.float64)
     assert torch.allclose(KA.zeta_transform(Fz), OK.zeta_transform(Fz), atol=1e-12)
     spec3 = build_mask(1000, 3, chunk=8)
-    Phi_rec = torch.randn(2, spec3.T_R, 5, generator=g, dtype=torch.float64)
-    U = torch.randn(2, spec3.B, 5, 6, generator=g, dtype=torch.float64)
-    assert torch.allclose(KA.query_by_type(Phi_rec, U, spec3).double(),
-                          OK.query_by_type(Phi_rec, U, spec3), atol=1e-5)
-    # the in-place form the op uses on its chunk-pass output
-    H0 = torch.randn(2, spec3.T_R, 6, generator=g, dtype=torch.float64).float()
-    H1 = H0.clone()
-    KA._add_query_by_type(H1, Phi_rec.float(), U.float(), spec3)
-    assert torch.allclose(H1.double(), H0.double() + OK.query_by_type(Phi_rec, U, spec3),
-                          atol=1e-4)
     # the transposed CSR used by the incidence backward
     ptr = torch.from_numpy(spec3.C_indptr)
     idx = torch.from_numpy(spec3.C_indices)
@@ -99,3 +90,42 @@ def test_torch_parts_match_oracle():
     for x in range(0, spec3.N0, 7):
         rows = t_idx[t_ptr[x]:t_ptr[x + 1]].tolist()
         assert rows == np.flatnonzero(Cd[:, x]).tolist()
+
+
+def test_make_phi_matches_reference_fixture():
+    """make_phi draws the reference's projection for the same seed: outputs
+    equal the reference's make_phi bit for bit (tests/golden/smat_module.npz)."""
+    import os
+    from smat_attention_b200 import kernel_attention as KA
+    f = np.load(os.path.join(os.path.dirname(__file__), "golden", "smat_module.npz"))
+    x = torch.from_numpy(f["xp"])
+    assert np.array_equal(KA.make_phi(16, 8, seed=3)(x).numpy(), f["phi_elu"])
+    assert np.array_equal(KA.make_phi(16, 8, kind="relu", seed=3)(x).numpy(), f["phi_relu"])
+    Phi, Psi, Vb = KA.featurise(x, x, x[:, :4], KA.make_phi(16, 8, seed=3),
+                                h=torch.full((5,), 0.5))
+    assert torch.equal(Psi, Phi * 0.5) and Vb.shape == (5, 5) and torch.all(Vb[:, -1] == 1)
+
+
+def test_op_and_module_reject_on_the_host():
+    """Argument errors of the op and of the module's smat arm are raised before
+    anything reaches a kernel."""
+    import pytest
+    from smat_attention_b200 import kernel_attention as KA
+    from smat_attention_b200.model import Attention
+    spec = build_mask(512, 3, chunk=128)
+    x = torch.zeros(1, 512, 32)
+    vb = torch.zeros(1, 512, 33)
+    with pytest.raises(ValueError):
+        KA.smat_attention(x, x, vb, spec, acc_dtype=torch.float64)
+    with pytest.raises(ValueError):
+        KA.smat_attention(x, x, vb, spec, scan_backend="cuda")
+    with pytest.raises(ValueError):
+        KA.smat_attention(x, x, vb, spec, long_range="dense")
+    with pytest.raises(ValueError):
+        Attention(32, 2, "smat", spec=spec, decay=True)
+    with pytest.raises(ValueError):
+        Attention(32, 2, "smat", spec=None)
+    with pytest.raises(TypeError):
+        Attention(32, 2, "smat", spec=spec, not_an_option=1)
+    m = Attention(32, 2, "smat", spec=spec, r=32, phi_kind="taylor", taylor_dim=4)
+    assert m.phi(torch.zeros(3, 16)).shape == (3, 1 + 4 + 16)
