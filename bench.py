@@ -533,10 +533,11 @@ class AttnCase:
         self.kernels = []
 
 
-def _e2e(case, K, dist):
+def _e2e(case, K, dist, heads_per_slice=None):
     """The step through the public autograd API with pinned host buffers:
     per step H2D of q, k, v, dO and D2H of o, dq, dk, dv inside the timed
-    region.  The batch goes through in slices of one sequence and `hs` heads,
+    region.  The batch goes through in slices of one sequence (and, if asked,
+    `heads_per_slice` heads),
     pipelined the way a caller streaming from host memory would: the H2D of
     slice s + 1 (a copy stream) and the D2H of slice s - 1 (another) overlap
     the attention of slice s, so the step costs the transfers plus one slice's
@@ -554,7 +555,7 @@ def _e2e(case, K, dist):
     E = max(1, min(K, 3))
     h2d, d2h = torch.cuda.Stream(device), torch.cuda.Stream(device)
     B, H = shape[0], shape[1]
-    hs = max(1, min(H, 8))
+    hs = H if not heads_per_slice else max(1, min(H, heads_per_slice))
     slices = [(slice(b, b + 1), slice(h, min(H, h + hs))) for b in range(B)
               for h in range(0, H, hs)]
 
@@ -856,6 +857,12 @@ def measure_kattn(args, device, dist=None, rank=0, ws=1, K=None, with_reference=
     K = max(args.steps, 5) if K is None else K
     t_fwd = timed(ours(False), K)
     t_step = timed(ours(True), K)
+    # the forward's phases (the reference's timer hook), mean of K forwards
+    Vb_ph = torch.cat([V, torch.ones(nb, T, 1, device=device)], dim=-1)
+    tm = KA.PhaseTimer(device)
+    for _ in range(K):
+        KA.smat_attention(Phi, Psi, Vb_ph, spec, chunk=128, timer=tm)
+    phases = {k: v / K for k, v in tm.results().items()}
     # one forward's chunk pass alone (the fused kernel), as the roofline line
     C = 128
     nc = T // C
@@ -921,7 +928,7 @@ def measure_kattn(args, device, dist=None, rank=0, ws=1, K=None, with_reference=
     peaks = _peaks()
     return {
         "value": ws * nb * T / (t_step * 1e-3), "unit": "tokens/s", "ms_per_step": t_step,
-        "steps": K, "fwd_ms": t_fwd, "decode_step_us": t_dec * 1e3,
+        "steps": K, "fwd_ms": t_fwd, "fwd_phase_ms": phases, "decode_step_us": t_dec * 1e3,
         "config": {"workload": f"kattn: nb={nb} T={T} r={r} d_v={dv} M^({d}) chunk 128, "
                                f"fp32 features elu+1", "global_batch": nb * ws,
                    "seq_len": T, "parallelism": f"(sequence) partition x{ws}",
@@ -1124,7 +1131,7 @@ def run_gpu(args):
     # ---- end to end through the public API with host buffers ---------------
     e2e = None
     if not args.no_e2e and not w.get("fwd_only") and case.dtype == torch.bfloat16:
-        e2e_ms, floor_ms, nbytes, numa, hs = _e2e(case, K, dist)
+        e2e_ms, floor_ms, nbytes, numa, hs = _e2e(case, K, dist, args.e2e_heads)
         e2e = {"value": total_fl / (e2e_ms * 1e-3) / 1e12, "unit": UNIT,
                "ms_per_step": e2e_ms, "h2d_bytes_per_step": nbytes,
                "d2h_bytes_per_step": nbytes,
@@ -1274,6 +1281,8 @@ def main():
                     help="the c3 numbers only (= --no-e2e --no-c5 --no-extras "
                          "--no-cpu-baseline; profiling runs)")
     ap.add_argument("--c5-steps", type=int, default=5)
+    ap.add_argument("--e2e-heads", type=int, default=None,
+                    help="heads per slice of the host-buffer leg (default: whole sequences)")
     ap.add_argument("--batch", type=int, default=None,
                     help="override B (smaller cases for ncu captures)")
     ap.add_argument("--heads", type=int, default=None, help="override H")

@@ -60,6 +60,13 @@ __device__ __forceinline__ void stage_rows_t(float* dst, const float* src, int r
 __device__ __forceinline__ void cp_async_wait_all() {
   asm volatile("cp.async.wait_all;" ::: "memory");
 }
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
+}
+__device__ __forceinline__ bool al16d(const void* p) {
+  return (reinterpret_cast<uintptr_t>(p) & 15u) == 0;
+}
+
 
 // ---------------------------------------------------------------- chunk sums
 // D[s, c] = a_c^T b_c over the C rows of chunk c (rows past T count as zero).
@@ -75,12 +82,41 @@ __global__ void __launch_bounds__(256) kattn_chunk_sum_kernel(const float* __res
   const int RA = round_up(R, 8), PB = round_up(P, 4);
   float* sa = sm;
   float* sb = sm + C * RA;
+  float* flat = sb + C * PB;    // [C * P] staging of the b chunk as one run
   const float* as = a + static_cast<int64_t>(s) * T * R;
   const float* bs = b + static_cast<int64_t>(s) * T * P;
-  stage_rows(sa, as, c * C, C, T, R, RA);
-  stage_rows(sb, bs, c * C, C, T, P, PB);
+  const int rows = min(C, T - c * C);
+  if ((R & 7) == 0 && al16d(as)) {
+    // whole rows of 16-byte units; rows past T zero
+    const int u = R / 4;
+    for (int e = threadIdx.x; e < C * u; e += blockDim.x) {
+      const int i = e / u, k = (e % u) * 4;
+      if (i < rows)
+        cp_async16(smem_u32(sa + i * RA + k), as + static_cast<int64_t>(c * C + i) * R + k);
+      else
+        *reinterpret_cast<float4*>(sa + i * RA + k) = make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+  } else {
+    stage_rows(sa, as, c * C, C, T, R, RA);
+  }
+  const float* bc = bs + static_cast<int64_t>(c) * C * P;
+  const int nflat = rows * P;
+  const bool flat16 = al16d(bc) && (nflat & 3) == 0;
+  if (flat16) {
+    for (int e = threadIdx.x * 4; e < nflat; e += blockDim.x * 4)
+      cp_async16(smem_u32(flat + e), bc + e);
+  } else {
+    stage_rows(sb, bs, c * C, C, T, P, PB);
+  }
   cp_async_wait_all();
   __syncthreads();
+  if (flat16) {   // [rows * P] -> [C][PB], zero padding
+    for (int e = threadIdx.x; e < C * PB; e += blockDim.x) {
+      const int i = e / PB, p = e % PB;
+      sb[e] = (i < rows && p < P) ? flat[i * P + p] : 0.f;
+    }
+    __syncthreads();
+  }
   const int PG = PB / 4, tiles = (RA / 8) * PG;
   float* out = D + (static_cast<int64_t>(s) * nc + c) * R * P;
   for (int t = threadIdx.x; t < tiles; t += blockDim.x) {
@@ -215,29 +251,55 @@ __global__ void __launch_bounds__(256) kattn_chunk_expand_kernel(
 
 // ---------------------------------------------------------------- query by type
 // out[s, i] (+)= phi[s, i] U[s, i mod nU] for i < T_R.  One CTA per (type h,
-// sequence); thread = output column p (one or more); the rows of type h
-// (h, h + nU, ...) go QT_ROWS at a time through shared memory, U_h is read
-// once per pass straight from global memory (a warp reads consecutive p).
+// sequence): U_h (R x P, contiguous) and the rows of type h (h, h + nU, ...,
+// QT_ROWS per pass) are staged in shared memory by asynchronous copies issued
+// all at once (16 bytes each where the layout allows), then thread = output
+// column p sums over r from shared memory (U_h rows conflict-free, phi
+// broadcast).
+
 __global__ void __launch_bounds__(128) kattn_query_kernel(
     const float* __restrict__ phi, int64_t phi_sb, const float* __restrict__ U,
     float* __restrict__ out, int64_t out_sb, int T_R, int R, int P, int nU, int accumulate) {
   extern __shared__ float4 sm4[];
-  float* sph = reinterpret_cast<float*>(sm4);   // [QT_ROWS][RA]
-  const int h = blockIdx.x, s = blockIdx.y;
   const int RA = round_up(R, 4);
+  float* su = reinterpret_cast<float*>(sm4);    // [R][P] = U_h
+  float* sph = su + round_up(R * P, 4);         // [QT_ROWS][RA]
+  const int h = blockIdx.x, s = blockIdx.y;
   const float* Uh = U + (static_cast<int64_t>(s) * nU + h) * R * P;
   const float* ph = phi + s * phi_sb;
   float* os = out + s * out_sb;
+  const int RP = R * P;
+  if ((RP & 3) == 0 && al16d(Uh)) {
+    for (int e = threadIdx.x * 4; e < RP; e += blockDim.x * 4) cp_async16(smem_u32(su + e), Uh + e);
+  } else {
+    for (int e = threadIdx.x; e < RP; e += blockDim.x) cp_async4(smem_u32(su + e), Uh + e, 4u);
+  }
+  const bool vec_phi = (R & 3) == 0 && al16d(ph) && ((nU * static_cast<int64_t>(R)) & 3) == 0;
   const int n_rows = h < T_R ? (T_R - h + nU - 1) / nU : 0;
   for (int g0 = 0; g0 < n_rows; g0 += QT_ROWS) {
     const int ng = min(QT_ROWS, n_rows - g0);
-    __syncthreads();
-    for (int e = threadIdx.x; e < QT_ROWS * RA; e += blockDim.x) {
-      const int i = e / RA, r = e % RA;
-      sph[e] = (i < ng && r < R)
-                   ? ph[static_cast<int64_t>(h + (g0 + i) * static_cast<int64_t>(nU)) * R + r]
-                   : 0.f;
+    if (g0 > 0) __syncthreads();   // the previous pass has finished reading sph
+    if (vec_phi) {
+      for (int e = threadIdx.x * 4; e < QT_ROWS * RA; e += blockDim.x * 4) {
+        const int i = e / RA, r = e % RA;
+        if (i < ng) {
+          cp_async16(smem_u32(sph + e),
+                     ph + static_cast<int64_t>(h + (g0 + i) * static_cast<int64_t>(nU)) * R + r);
+        } else {
+          *reinterpret_cast<float4*>(sph + e) = make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+      }
+    } else {
+      for (int e = threadIdx.x; e < QT_ROWS * RA; e += blockDim.x) {
+        const int i = e / RA, r = e % RA;
+        const bool in = i < ng && r < R;
+        cp_async4(smem_u32(sph + e),
+                  in ? ph + static_cast<int64_t>(h + (g0 + i) * static_cast<int64_t>(nU)) * R + r
+                     : ph,
+                  in ? 4u : 0u);
+      }
     }
+    cp_async_wait_all();
     __syncthreads();
     for (int p = threadIdx.x; p < P; p += blockDim.x) {
       float acc[QT_ROWS];
@@ -246,7 +308,7 @@ __global__ void __launch_bounds__(128) kattn_query_kernel(
       for (int r0 = 0; r0 < RA; r0 += 4) {
         float u[4];
 #pragma unroll
-        for (int j = 0; j < 4; ++j) u[j] = (r0 + j < R) ? __ldg(Uh + (r0 + j) * P + p) : 0.f;
+        for (int j = 0; j < 4; ++j) u[j] = (r0 + j < R) ? su[(r0 + j) * P + p] : 0.f;
 #pragma unroll
         for (int i = 0; i < QT_ROWS; ++i) {
           const float4 x = *reinterpret_cast<const float4*>(sph + i * RA + r0);
@@ -265,6 +327,7 @@ __global__ void __launch_bounds__(128) kattn_query_kernel(
       }
     }
   }
+  cp_async_wait_all();   // a type without rows still drains its U copy
 }
 
 // dphi[s, i] = dout[s, i] U_h^T and dU[s, h] = sum over rows i of type h of
@@ -365,7 +428,7 @@ int allow_smem(K kernel, int bytes) {
              : SMAT_ERR_LAUNCH;
 }
 
-int sum_smem(int C, int R, int P) { return C * (round_up(R, 8) + round_up(P, 4)) * 4; }
+int sum_smem(int C, int R, int P) { return C * (round_up(R, 8) + round_up(P, 4) + P) * 4; }
 int expand_smem(int C, int R, int P) {
   const int RA = round_up(R, 8), PB = round_up(P, 8), CS = round_up(C, 8);
   return (RA * CS + PB * CS + 2 * RA * PB) * 4;
@@ -416,7 +479,7 @@ int smat_kattn_query_by_type(const float* phi, int64_t phi_seq_stride, const flo
       out_seq_stride < 0)
     return SMAT_ERR_BAD_SHAPE;
   if (T_R == 0) return SMAT_OK;
-  const int smem = QT_ROWS * round_up(R, 4) * 4;
+  const int smem = (round_up(R * P, 4) + QT_ROWS * round_up(R, 4)) * 4;
   if (smem > GLUE_SMEM_MAX) return SMAT_ERR_BAD_SHAPE;
   int rc = allow_smem(kattn_query_kernel, smem);
   if (rc) return rc;
