@@ -1051,8 +1051,12 @@ def measure_c5_parity(dist, rank, ws, device, H=4):
     config 5 (its first H heads at the full T): every rank runs the sharded
     forward + backward with NaN in every row it does not own (so a row read
     without the exchange poisons the result) and the unsharded kernels on the
-    full inputs; O, LSE and dQ of its owned rows must be equal bit for bit,
-    dK and dV within 2e-2 (their partial sums are added in another order)."""
+    full inputs; O, LSE and dQ of its owned rows must be equal bit for bit.
+    dK and dV of an imported key block are sums of bf16 partials from several
+    ranks (each rounded once before the owner adds them in fp32), so they may
+    differ from the single-GPU value by a rounding or two: the bound is 2e-2
+    or two bf16 units in the last place of the single-GPU value, whichever is
+    larger."""
     from smat_attention_b200.attention import bwd, check_device_errors, fwd
     from smat_attention_b200.mask import build_block_mask
     from smat_attention_b200.sharding import make_plan, sharded_bwd, sharded_fwd
@@ -1076,16 +1080,27 @@ def measure_c5_parity(dist, rank, ws, device, H=4):
     errs = int(check_device_errors(device))
     exact = {name: bool(torch.equal(a[:, :, own], b[:, :, own]))
              for name, a, b in (("o", o, o1), ("lse", lse, lse1), ("dq", dq, dq1))}
-    dmax = {name: float((a[:, :, own].float() - b[:, :, own].float()).abs().max().item())
-            for name, a, b in (("dk", dk, dk1), ("dv", dv, dv1))}
-    ok = all(exact.values()) and all(x <= 2e-2 for x in dmax.values()) and errs == 0
+    dmax, ulps = {}, {}
+    for name, a, b in (("dk", dk, dk1), ("dv", dv, dv1)):
+        diff = (a[:, :, own].float() - b[:, :, own].float()).abs()
+        ref = b[:, :, own].float().abs()
+        # one bf16 unit in the last place of |ref| (8 significant bits)
+        ulp = torch.exp2(torch.floor(torch.log2(ref.clamp_min(2.0 ** -126))) - 7)
+        dmax[name] = float(diff.max().item())
+        # worst element against its own bound max(2e-2, 2 ulp): <= 1 passes
+        ulps[name] = float((diff / torch.clamp(2.0 * ulp, min=2e-2)).max().item())
+        del diff, ref, ulp
+    ok = all(exact.values()) and errs == 0 and all(u <= 1.0 for u in ulps.values())
     ok_all = _reduce(dist, 1.0 if ok else 0.0, device, "min") == 1.0
     exact_all = {n: _reduce(dist, 1.0 if e else 0.0, device, "min") == 1.0
                  for n, e in exact.items()}
     dmax_all = {n: _max_over_ranks(dist, x, device) for n, x in dmax.items()}
+    ulps_all = {n: _max_over_ranks(dist, x, device) for n, x in ulps.items()}
     errs_all = int(_max_over_ranks(dist, errs, device))
     return {"pass": ok_all, "bit_exact_owned_rows": exact_all, "dkdv_max_abs": dmax_all,
-            "tolerance_dkdv": 2e-2, "device_errors": errs_all,
+            "dkdv_worst_over_bound": ulps_all,
+            "tolerance_dkdv": "per element max(2e-2, 2 bf16 ulps of the single-GPU value)",
+            "device_errors": errs_all,
             "slice": f"c5 first {H} heads (B=1, T={w['T']}), {ws} rank(s), non-owned rows NaN"}
 
 
