@@ -365,21 +365,17 @@ __global__ void __launch_bounds__(320, 1)
         }
       };
       float s[32];
-      float mx8[8];
+      float mx[4];   // three-input max: 16 instructions per 32 scores
 #pragma unroll
-      for (int a = 0; a < 8; ++a) mx8[a] = -INFINITY;
+      for (int a = 0; a < 4; ++a) mx[a] = -INFINITY;
 #pragma unroll 1
       for (int qq = 0; qq < 4; ++qq) {
         tmem_ld32(lane_base + 32 * qq, s);
         mask(s, qq);
 #pragma unroll
-        for (int i = 0; i < 32; ++i) mx8[i & 7] = fmaxf(mx8[i & 7], s[i]);
+        for (int i = 0; i < 32; i += 2) mx[(i >> 1) & 3] = fmax3(mx[(i >> 1) & 3], s[i], s[i + 1]);
       }
-#pragma unroll
-      for (int w = 4; w > 0; w >>= 1)
-#pragma unroll
-        for (int a = 0; a < w; ++a) mx8[a] = fmaxf(mx8[a], mx8[a + w]);
-      const float m_new = fmaxf(m, mx8[0] * p.scale_log2);
+      const float m_new = fmaxf(m, fmax3(fmaxf(mx[0], mx[1]), mx[2], mx[3]) * p.scale_log2);
       const bool need = m_new > m + 8.0f;
       const bool rescale = __any_sync(0xffffffffu, need);
       const float alpha = need ? ex2_approx(m - m_new) : 1.f;
