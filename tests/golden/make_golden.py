@@ -63,6 +63,10 @@ SOFTMAX_CASES = [
     ("block_ragged_t200", 200, 2, 16, ("block", 32, 1, 2, 1)),
     ("md3_t256", 256, 1, 16, ("md", 3, 16)),
 ]
+# one head of config 1 at full size (T = 1024, D = 64, bs 64, W 4, one sink):
+# inputs are regenerated from the seed by the test (a digest guards against a
+# change of the generator), outputs stored as fp32
+C1_CASE = ("c1_t1024", 1024, 1, 64, ("block", 64, 4, 0, 1))
 
 
 def _sha(a: np.ndarray) -> str:
@@ -103,6 +107,37 @@ def _dense_mask(R, T, mask):
         return (act & (j <= i)).astype(np.float64)
     _, d, chunk = mask
     return R.materialise(R.build_mask(T, d, chunk=chunk))
+
+
+def c1_inputs(seed):
+    """Config 1's inputs for the fixture: N(0, 1) fp32 from a CPU generator."""
+    g = torch.Generator().manual_seed(seed)
+    T, BH, D = C1_CASE[1], C1_CASE[2], C1_CASE[3]
+    return [torch.randn(BH, T, D, generator=g, dtype=torch.float32) for _ in range(4)]
+
+
+def make_softmax_c1(A, R, seed=0):
+    """The reference's dense-masked path on one head of config 1 (fp64), outputs
+    and gradients stored as fp32, inputs as a seed plus their SHA-256."""
+    name, T, BH, D, mask = C1_CASE
+    q, k, v, do = (x.double() for x in c1_inputs(seed))
+    M = torch.from_numpy(_dense_mask(R, T, mask))
+    scale = 1.0 / math.sqrt(D)
+    qg, kg, vg = (x.clone().requires_grad_(True) for x in (q, k, v))
+    s = torch.einsum("nta,nsa->nts", qg, kg) * scale
+    m = s.masked_fill(M == 0, float("-inf")).amax(-1, keepdim=True).detach()
+    Phi = torch.exp(s - m)
+    Psi = torch.eye(T, dtype=torch.float64).expand(BH, T, T)
+    Vb = torch.cat([vg, torch.ones(BH, T, 1, dtype=torch.float64)], dim=-1)
+    o = A.dense_masked_kernel_attention(Phi, Psi, Vb, M)
+    (o * do).sum().backward()
+    digest = _sha(np.concatenate([x.float().numpy().ravel() for x in (q, k, v, do)]))
+    np.savez_compressed(
+        os.path.join(HERE, f"softmax_{name}.npz"), seed=np.array(seed),
+        inputs_sha256=np.array(digest), mask_sha256=np.array(_sha(M.numpy().astype(np.uint8))),
+        mask_args=np.array([str(x) for x in mask]), scale=np.array(scale),
+        o=o.detach().float().numpy(), dq=qg.grad.float().numpy(), dk=kg.grad.float().numpy(),
+        dv=vg.grad.float().numpy())
 
 
 def make_softmax(A, R, name, T, BH, D, mask, seed):
@@ -205,6 +240,7 @@ def main():
     make_mask_md(R)
     for i, (name, T, BH, D, mask) in enumerate(SOFTMAX_CASES):
         make_softmax(A, R, name, T, BH, D, mask, seed=100 + i)
+    make_softmax_c1(A, R)
     for i, case in enumerate(KATTN_CASES):
         make_kattn(A, R, *case, seed=200 + i)
     from smat import model as M

@@ -180,3 +180,21 @@ def test_rejects_unsupported(cuda_device):
     with pytest.raises(ValueError):
         fwd(qb[..., :64].contiguous()[:, :, :128], qb[..., :64].contiguous()[:, :, :128],
             qb[..., :64].contiguous()[:, :, :128], spec, 0.125)   # T mismatch
+
+
+def test_fp32_matches_reference_c1_head(cuda_device):
+    """Config 1 in full size on the fp32 path against the reference's own
+    dense-masked attention (tests/golden/softmax_c1_t1024.npz, one head,
+    T = 1024, D = 64, bs 64, W 4, one sink): O, dQ, dK, dV within 1e-4."""
+    import numpy as np
+    from test_oracle import c1_fixture
+    f, (q, k, v, do), _ = c1_fixture()
+    spec = build_block_mask(1024, 64, 4, 0, 1)
+    dev = [x.reshape(1, 1, 1024, 64).to(cuda_device) for x in (q, k, v, do)]
+    o, lse = fwd(dev[0], dev[1], dev[2], spec, float(f["scale"]))
+    dq, dk, dv = bwd(dev[0], dev[1], dev[2], o, lse, dev[3], spec, float(f["scale"]))
+    torch.cuda.synchronize()
+    assert check_device_errors() == 0
+    for got, key in ((o, "o"), (dq, "dq"), (dk, "dk"), (dv, "dv")):
+        err = np.abs(got.reshape(1, 1024, 64).cpu().double().numpy() - f[key]).max()
+        assert err <= TOL_F32, (key, err)
