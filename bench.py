@@ -137,26 +137,71 @@ def _traffic():
 
 
 class ClockSampler:
-    """nvidia-smi clock / throttle samples while the timed region runs."""
+    """SM clock and clock-event reasons sampled every ~2 ms while the timed
+    region runs (NVML read-only queries from a background thread; nothing is
+    set).  Falls back to an `nvidia-smi` poll when NVML is unavailable."""
 
+    REASONS = (("hw_slowdown", "nvmlClocksEventReasonHwSlowdown"),
+               ("hw_thermal_slowdown", "nvmlClocksEventReasonHwThermalSlowdown"),
+               ("sw_thermal_slowdown", "nvmlClocksEventReasonSwThermalSlowdown"),
+               ("sw_power_cap", "nvmlClocksEventReasonSwPowerCap"))
     FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
     def __init__(self, device):
-        self.proc = None
+        import threading
+        self.samples, self.proc, self.thread = [], None, None
+        self.stop_flag = threading.Event()
+        uuid = str(torch.cuda.get_device_properties(device).uuid)
+        ident = uuid if uuid.startswith("GPU-") else f"GPU-{uuid}"
         try:
-            uuid = str(torch.cuda.get_device_properties(device).uuid)
-            ident = uuid if uuid.startswith("GPU-") else f"GPU-{uuid}"
+            import pynvml
+            pynvml.nvmlInit()
+            self.nv = pynvml
+            self.handle = pynvml.nvmlDeviceGetHandleByUUID(ident)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.handle, pynvml.NVML_CLOCK_SM)
+            self.thread = threading.Thread(target=self._poll, daemon=True)
+            self.thread.start()
+            time.sleep(0.01)
+            return
+        except Exception:
+            self.nv = None
+        try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", "-i", ident, f"--query-gpu={self.FIELDS}",
                  "--format=csv,noheader,nounits", "-lms", "100"],
                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-            time.sleep(0.3)   # let the first sample land before the timed region
+            time.sleep(0.3)
         except Exception:
             self.proc = None
 
+    def _poll(self):
+        nv, h = self.nv, self.handle
+        while not self.stop_flag.is_set():
+            try:
+                mhz = nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)
+                bits = nv.nvmlDeviceGetCurrentClocksEventReasons(h)
+                self.samples.append((float(mhz), int(bits)))
+            except Exception:
+                return
+            time.sleep(0.002)
+
     def stop(self):
+        if self.thread is not None:
+            self.stop_flag.set()
+            self.thread.join(timeout=2)
+            if not self.samples:
+                return None
+            sm = [m for m, _ in self.samples]
+            reasons = set()
+            for name, attr in self.REASONS:
+                bit = getattr(self.nv, attr, 0)
+                if any(b & bit for _, b in self.samples):
+                    reasons.add(name)
+            load = [x for x in sm if x > 0.5 * max(sm)] or sm
+            return {"sm_mhz": statistics.median(load), "sm_max_mhz": float(self.max_mhz),
+                    "reasons": sorted(reasons), "samples": len(sm), "source": "nvml 2 ms"}
         if self.proc is None:
             return None
         time.sleep(0.25)
@@ -167,7 +212,7 @@ class ClockSampler:
             self.proc.kill()
             out, _ = self.proc.communicate()
         sm, mx, reasons = [], [], set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        names = [n for n, _ in self.REASONS]
         for line in out.splitlines():
             parts = [p.strip() for p in line.split(",")]
             if len(parts) < 8:
@@ -184,7 +229,7 @@ class ClockSampler:
             return None
         load = [s for s in sm if s > 0.5 * max(sm)] or sm
         return {"sm_mhz": statistics.median(load), "sm_max_mhz": max(mx),
-                "reasons": sorted(reasons), "samples": len(sm)}
+                "reasons": sorted(reasons), "samples": len(sm), "source": "nvidia-smi 100 ms"}
 
 
 def _dist():
