@@ -301,14 +301,15 @@ def build_mask(T: int, d: int, *, chunk: int = 1, n_P: int = 0,
     built).
     """
     if T < 8:
-        raise ValueError(f"T must be >= 8, got {T}")
+        raise ValueError(f"build_mask: context length T={T} is below the minimum of 8")
     d_ceiling = int(T).bit_length() - 1
     if not (1 <= d <= d_ceiling):
-        raise ValueError(f"need 1 <= d <= floor(log2 T) = {d_ceiling}, got d={d}")
+        raise ValueError(f"build_mask: d={d} is outside the admissible range [1, {d_ceiling}] "
+                         f"(the top is floor(log2 T))")
     c = max(1, int(chunk))
     n = c * (T // (2 * c))
     if n <= 0:
-        raise ValueError(f"chunk={c} too large for T={T}")
+        raise ValueError(f"build_mask: chunk={c} leaves no landmark positions at T={T}")
     T_R = T - n
     t0 = time.perf_counter()
 
@@ -331,10 +332,10 @@ def build_mask(T: int, d: int, *, chunk: int = 1, n_P: int = 0,
     q = next_prime(int(np.ceil(n ** (1.0 / d))))
     N0 = q ** dim
     if n_P < 0 or n_P >= n:
-        raise ValueError(f"n_P={n_P} out of range for n={n}")
+        raise ValueError(f"build_mask: n_P={n_P} global columns do not fit in [0, n={n})")
     if N0 > n - n_P:
-        raise ValueError(f"T={T}, d={d}: |F_q^{dim}| = {N0} exceeds the "
-                         f"{n - n_P} profiled landmark columns")
+        raise ValueError(f"build_mask: {N0} points of F_{q}^{dim} need more than the "
+                         f"{n - n_P} profiled landmark columns of T={T}, d={d}")
 
     t = time.perf_counter()
     pts = _lex_points(q, dim)
@@ -349,29 +350,29 @@ def build_mask(T: int, d: int, *, chunk: int = 1, n_P: int = 0,
     dir_pts = np.flatnonzero(is_dir)                       # point index per direction
     n_dirs = int(dir_pts.size)
     if n_dirs != (q ** dim - 1) // (q - 1):
-        raise AssertionError("direction count mismatch")
+        raise AssertionError("normalised directions: count differs from (q^dim - 1) / (q - 1)")
     dir_of_point = np.full(N0, -1, dtype=np.int64)
     dir_of_point[dir_pts] = np.arange(n_dirs)
-    B_max = n_dirs * q
-    times["directions"] = time.perf_counter() - t
+    n_planes_all = n_dirs * q
+    times["dir_table"] = time.perf_counter() - t
 
     n_planted = 1 << dim
-    B = max(n_planted, min(int(round(B_frac * B_max)), B_max))
+    B = max(n_planted, min(int(round(B_frac * n_planes_all)), n_planes_all))
     if T_R < 2 * B:
-        msg = (f"T={T}, d={d}: recent block T_R={T_R} < 2B={2 * B}; the type "
-               f"map does not complete two cycles")
+        msg = (f"build_mask T={T}, d={d}: only {T_R} recent rows for {B} row types, "
+               f"fewer than two full passes over the types")
         if _probe:
             raise ValueError(msg)
         warns.append(msg)
 
-    deg = q ** (dim - 1)
-    if max_I_prof is not None and B * deg > max_I_prof:
-        raise MemoryError(f"T={T}, d={d}: nnz(C)={B * deg:,} exceeds "
-                          f"max_I_prof={max_I_prof:,}")
+    per_plane = q ** (dim - 1)
+    if max_I_prof is not None and B * per_plane > max_I_prof:
+        raise MemoryError(f"build_mask T={T}, d={d}: the incidence would hold "
+                          f"{B * per_plane:,} entries, above max_I_prof={max_I_prof:,}")
     if _probe:
         return MaskSpec(T=T, d=d, kind="geometric", n=n, T_R=T_R, chunk_align=c,
                         q=q, dim=dim, N0=N0, n_dirs=n_dirs, B=B,
-                        n_planted=n_planted, n_P=n_P, uniform_deg=deg)
+                        n_planted=n_planted, n_P=n_P, uniform_deg=per_plane)
 
     # hyperplane h = e*q + b is {x : <a_e, x> = b (mod q)}; its points are
     # listed in increasing point index.  A counting sort of the inner products
@@ -381,8 +382,8 @@ def build_mask(T: int, d: int, *, chunk: int = 1, n_P: int = 0,
     inner = (pts @ A.T) % q                                 # (N0, n_dirs)
     key = inner.T * N0 + np.arange(N0)[None, :]             # (n_dirs, N0)
     order = np.argsort(key, axis=1) % N0                    # sort by (b, point)
-    planes = order.reshape(n_dirs * q, deg)                 # row e*q+b
-    times["incidence"] = time.perf_counter() - t
+    planes = order.reshape(n_dirs * q, per_plane)                 # row e*q+b
+    times["plane_lists"] = time.perf_counter() - t
 
     t = time.perf_counter()
     weights = q ** np.arange(dim - 1, -1, -1, dtype=np.int64)
@@ -390,16 +391,16 @@ def build_mask(T: int, d: int, *, chunk: int = 1, n_P: int = 0,
     for a, b in planted_hyperplane_normals(d):
         e = int(dir_of_point[int((a * weights).sum())])
         if e < 0:
-            raise AssertionError("planted normal is not a normalised direction")
+            raise AssertionError("a planted hyperplane normal is not among the normalised directions")
         planted.append(e * q + b)
     if len(set(planted)) != n_planted:
-        raise AssertionError("planted hyperplanes are not distinct")
-    taken = np.zeros(B_max, dtype=bool)
+        raise AssertionError("two planted hyperplanes coincide")
+    taken = np.zeros(n_planes_all, dtype=bool)
     taken[planted] = True
-    h_order = np.concatenate([np.asarray(planted, dtype=np.int64),
+    row_order = np.concatenate([np.asarray(planted, dtype=np.int64),
                               np.flatnonzero(~taken)])[:B]
-    plane_pts = planes[h_order].astype(np.int32)
-    times["reorder"] = time.perf_counter() - t
+    plane_lists = planes[row_order].astype(np.int32)
+    times["planted_first"] = time.perf_counter() - t
 
     planted_cols = np.array([n_P + q ** (dim - l) for l in range(1, dim + 1)],
                             dtype=np.int64)
@@ -407,8 +408,8 @@ def build_mask(T: int, d: int, *, chunk: int = 1, n_P: int = 0,
     return MaskSpec(T=T, d=d, kind="geometric", n=n, T_R=T_R, chunk_align=c,
                     q=q, dim=dim, N0=N0, n_dirs=n_dirs, B=B, n_planted=n_planted,
                     planted_cols=planted_cols, n_P=n_P,
-                    C_indptr=np.arange(B + 1, dtype=np.int64) * deg,
-                    C_indices=plane_pts.reshape(-1), uniform_deg=deg,
+                    C_indptr=np.arange(B + 1, dtype=np.int64) * per_plane,
+                    C_indices=plane_lists.reshape(-1), uniform_deg=per_plane,
                     build_times=times, warnings=warns)
 
 
@@ -422,10 +423,10 @@ def _endpoint_spec(T: int, d: int, c: int, t0: float, *,
     B = 1 << k
     warns: List[str] = []
     if T_R < B:
-        warns.append(f"T={T}: recent block T_R={T_R} < B={B}; fewer than one "
-                     f"full Walsh cycle")
+        warns.append(f"build_mask T={T}: only {T_R} recent rows for {B} row types, "
+                     f"less than one pass over the Walsh types")
     if _probe:
-        raise NotImplementedError("endpoint is not part of the geometric family")
+        raise NotImplementedError("build_mask: the endpoint mask has no geometric probe")
     a = np.arange(B, dtype=np.int64)
     parity = np.bitwise_count(a[:, None] & a[None, :]) & 1      # (B, B)
     keep = parity == 0
