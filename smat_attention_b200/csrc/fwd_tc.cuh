@@ -19,15 +19,17 @@
 // bs = 64 a chunk is two 64-key blocks of the merged list; a missing second
 // half is loaded from row T (zero-filled) and masked.
 //
-// Warp roles (320 threads):
+// Warp roles (384 threads):
 //   warps 0-3 / 4-7  softmax + epilogue of tile 0 / tile 1; thread r of a
 //                    warpgroup owns row r of its tile = TMEM lane r
 //   warp 8           TMA producer (lane 0: both Q tiles, then the K ring;
 //                    lane 1: the V ring)
 //   warp 9           TMEM allocator and MMA issuer (one lane)
+//   warps 10-11      idle (they complete warpgroup 2)
+// The softmax warpgroups take registers from warpgroup 2 (setmaxnreg) so a
+// thread holds its whole 128-score row: S is read from TMEM once per chunk.
 // P of key half h (keys 64 h .. 64 h + 63) is packed into the first 32 of
-// that half's own S columns; the softmax reads S a quarter (32 keys) at a
-// time, so a thread only overwrites scores it has already read.
+// that half's own S columns.
 // Masked scores become -inf before the row max, so a key outside the mask
 // never enters the max or the sum.  Each quarter's mask is one 32-bit word per
 // row: all ones for a full block, a span for the causal diagonal, and for an
@@ -82,7 +84,13 @@ struct FwdCfg {
   static_assert(KS >= 2 && VS >= 2, "at least two slots per ring");
   static constexpr int TMEM_COLS = 512, TILE_COLS = 256, COL_O = 128;
   static_assert(COL_O + D <= TILE_COLS, "TMEM budget");
-  static constexpr int THREADS = 320;
+  // warpgroups 0 / 1 softmax, warpgroup 2 the producer and MMA warps (and two
+  // idle ones, so that every warpgroup is whole for the register split)
+  static constexpr int THREADS = 384;
+  static constexpr int REGS_LAUNCH = (65536 / THREADS) & ~7;   // 168
+  static constexpr int REGS_SOFTMAX = 192, REGS_OTHER = 112;
+  static_assert(128 * (2 * REGS_SOFTMAX + REGS_OTHER) <= THREADS * REGS_LAUNCH,
+                "register split exceeds the launch allocation");
   static constexpr uint32_t IDESC_S = idesc_bf16(BM, BN, false, false);
   static constexpr uint32_t IDESC_O = idesc_bf16(BM, D, false, true);
 };
@@ -92,7 +100,7 @@ struct FwdCfg {
 __device__ __forceinline__ uint32_t p_col(int kk) { return 64u * (kk >> 2) + 8u * (kk & 3); }
 
 template <int D>
-__global__ void __launch_bounds__(320, 1)
+__global__ void __launch_bounds__(384, 1)
     smat_fwd_tc_kernel(const __grid_constant__ CUtensorMap tm_q,
                        const __grid_constant__ CUtensorMap tm_k,
                        const __grid_constant__ CUtensorMap tm_v,
@@ -166,151 +174,157 @@ __global__ void __launch_bounds__(320, 1)
   tc_fence_after();
   const uint32_t tbase = misc[0];
 
-  if (warp == 8) {
-    // ------------------------------------------------------------ producer
-    // lane 0: both Q tiles, then the K ring; lane 1: the V ring.  Each lane
-    // walks the schedule on its own, so a V slot that frees late never holds
-    // up the next K load.
-    if (lane < 2) {
-      const bool kl = lane == 0;
-      const int NS = kl ? C::KS : C::VS;
-      const int full = kl ? C::BAR_KF : C::BAR_VF, empty = kl ? C::BAR_KE : C::BAR_VE;
-      const uint32_t ring = sbase + (kl ? C::OFF_K : C::OFF_V);
-      const CUtensorMap* tm = kl ? &tm_k : &tm_v;
-      // the Q tiles first: they do not depend on the schedule reads
-      if (kl) {
-        mbar_expect_tx(bar(C::BAR_Q), C::NT * C::Q_BYTES);
-#pragma unroll
-        for (int x = 0; x < C::NT; ++x)
-#pragma unroll
+  // Each warpgroup changes its register count at the top of its own branch, so
+  // that no code path joins between the change and the role's code.
+  if (warp >= 8) {
+    regs_dec<C::REGS_OTHER>();
+    if (warp == 8) {
+      // ------------------------------------------------------------ producer
+      // lane 0: both Q tiles, then the K ring; lane 1: the V ring.  Each lane
+      // walks the schedule on its own, so a V slot that frees late never holds
+      // up the next K load.
+      if (lane < 2) {
+        const bool kl = lane == 0;
+        const int NS = kl ? C::KS : C::VS;
+        const int full = kl ? C::BAR_KF : C::BAR_VF, empty = kl ? C::BAR_KE : C::BAR_VE;
+        const uint32_t ring = sbase + (kl ? C::OFF_K : C::OFF_V);
+        const CUtensorMap* tm = kl ? &tm_k : &tm_v;
+        // the Q tiles first: they do not depend on the schedule reads
+        if (kl) {
+          mbar_expect_tx(bar(C::BAR_Q), C::NT * C::Q_BYTES);
+  #pragma unroll
+          for (int x = 0; x < C::NT; ++x)
+  #pragma unroll
+            for (int pn = 0; pn < D / 64; ++pn)
+              tma_load_4d(sbase + C::OFF_Q + x * C::Q_BYTES + pn * C::PANEL_Q, &tm_q,
+                          bar(C::BAR_Q), pn * 64, (tile0 + x) * C::BM, h, b);
+        }
+        ChunkPair<4> it;
+        it.init(p.indptr, p.indices, p.kind, p.nblocks, p.nnzb, row0, ntile * sub, p.bs, p.err);
+        int issued = 0;
+        uint32_t e[2];
+        for (int j = 0; it.next(e, p.err); ++j) {
+          const int s = j % NS;
+          if (j >= NS && !mbar_wait(bar(empty + s), ((j / NS) - 1) & 1, abort_flag, p.err)) break;
+          // first key of each 64-key half; a missing half reads row T onwards,
+          // which TMA fills with zeros
+          int krow[2];
+  #pragma unroll
+          for (int q = 0; q < 2; ++q) {
+            const uint32_t eq = (p.bs == 64) ? e[q] : e[0];
+            krow[q] = entry_present(eq) ? static_cast<int>(sched_block(eq)) * p.bs + (q * 64) % p.bs
+                                        : p.T;
+          }
+          mbar_expect_tx(bar(full + s), C::KV_BYTES);
+  #pragma unroll
           for (int pn = 0; pn < D / 64; ++pn)
-            tma_load_4d(sbase + C::OFF_Q + x * C::Q_BYTES + pn * C::PANEL_Q, &tm_q,
-                        bar(C::BAR_Q), pn * 64, (tile0 + x) * C::BM, h, b);
-      }
-      ChunkPair<4> it;
-      it.init(p.indptr, p.indices, p.kind, p.nblocks, p.nnzb, row0, ntile * sub, p.bs, p.err);
-      int issued = 0;
-      uint32_t e[2];
-      for (int j = 0; it.next(e, p.err); ++j) {
-        const int s = j % NS;
-        if (j >= NS && !mbar_wait(bar(empty + s), ((j / NS) - 1) & 1, abort_flag, p.err)) break;
-        // first key of each 64-key half; a missing half reads row T onwards,
-        // which TMA fills with zeros
-        int krow[2];
-#pragma unroll
-        for (int q = 0; q < 2; ++q) {
-          const uint32_t eq = (p.bs == 64) ? e[q] : e[0];
-          krow[q] = entry_present(eq) ? static_cast<int>(sched_block(eq)) * p.bs + (q * 64) % p.bs
-                                      : p.T;
+  #pragma unroll
+            for (int q = 0; q < 2; ++q)
+              tma_load_4d(ring + s * C::KV_BYTES + pn * C::PANEL_KV + q * (C::BOX * 128), tm,
+                          bar(full + s), pn * 64, krow[q], h, b);
+          issued = j + 1;
         }
-        mbar_expect_tx(bar(full + s), C::KV_BYTES);
-#pragma unroll
-        for (int pn = 0; pn < D / 64; ++pn)
-#pragma unroll
-          for (int q = 0; q < 2; ++q)
-            tma_load_4d(ring + s * C::KV_BYTES + pn * C::PANEL_KV + q * (C::BOX * 128), tm,
-                        bar(full + s), pn * 64, krow[q], h, b);
-        issued = j + 1;
-      }
-      if (kl) mbar_wait_drain(bar(C::BAR_Q), 0);  // never exit with Q in flight
-      if (*abort_flag) {
-        for (int j = max(0, issued - NS); j < issued; ++j)
-          mbar_wait_drain(bar(full + j % NS), (j / NS) & 1);
-      }
-    }
-  } else if (warp == 9) {
-    // ------------------------------------------------------------ MMA issuer
-    if (lane == 0) {
-      ChunkPair<4> it;
-      it.init(p.indptr, p.indices, p.kind, p.nblocks, p.nnzb, row0, ntile * sub, p.bs, p.err);
-      int cp[C::NT] = {0, 0};   // PVs issued per tile
-      // S_x of chunk j (K slot j % KS)
-      auto issue_s = [&](int j, int x) {
-        const uint32_t ka = sbase + C::OFF_K + (j % C::KS) * C::KV_BYTES;
-        const uint32_t qa = sbase + C::OFF_Q + x * C::Q_BYTES;
-        const uint32_t dst = tbase + x * C::TILE_COLS;
-        const uint64_t qd = sdesc_sw128(qa, 16, 1024), kd = sdesc_sw128(ka, 16, 1024);
-#pragma unroll
-        for (int kk = 0; kk < D / 16; ++kk) {
-          const uint32_t off = (kk & 3) * 32u;
-          tc_mma(dst, sdesc_add(qd, (kk >> 2) * C::PANEL_Q + off),
-                 sdesc_add(kd, (kk >> 2) * C::PANEL_KV + off), C::IDESC_S, kk > 0 ? 1u : 0u);
-        }
-        tc_commit(bar(C::BAR_SF + x));
-      };
-      bool ok = mbar_wait(bar(C::BAR_Q), 0, abort_flag, p.err);
-      uint32_t e[2], en[2];
-      bool has = ok && it.next(e, p.err);
-      if (has) {
-        ok = mbar_wait(bar(C::BAR_KF + 0), 0, abort_flag, p.err);
-        if (ok) {
-          tc_fence_after();
-#pragma unroll
-          for (int x = 0; x < C::NT; ++x)
-            if (active(e, x)) issue_s(0, x);
-          tc_commit(bar(C::BAR_KE + 0));   // every S of chunk 0 is issued
+        if (kl) mbar_wait_drain(bar(C::BAR_Q), 0);  // never exit with Q in flight
+        if (*abort_flag) {
+          for (int j = max(0, issued - NS); j < issued; ++j)
+            mbar_wait_drain(bar(full + j % NS), (j / NS) & 1);
         }
       }
-      for (int j = 0; ok && has; ++j) {
-        const bool nxt = it.next(en, p.err);
-        const int sv = j % C::VS;
-        const int k1 = (j + 1) % C::KS;
-        const int k1par = ((j + 1) / C::KS) & 1;
-        const uint32_t va = sbase + C::OFF_V + sv * C::KV_BYTES;
-        if (!mbar_wait(bar(C::BAR_VF + sv), (j / C::VS) & 1, abort_flag, p.err)) break;
-        bool loaded = false;     // K of chunk j + 1 has landed
-        bool pending[C::NT] = {false, false};
-#pragma unroll
-        for (int x = 0; x < C::NT; ++x) {
-          if (active(e, x)) {
-            if (!mbar_wait(bar(C::BAR_PF + x), cp[x] & 1, abort_flag, p.err)) {
-              ok = false;
-              break;
-            }
+    } else if (warp == 9) {
+      // ------------------------------------------------------------ MMA issuer
+      if (lane == 0) {
+        ChunkPair<4> it;
+        it.init(p.indptr, p.indices, p.kind, p.nblocks, p.nnzb, row0, ntile * sub, p.bs, p.err);
+        int cp[C::NT] = {0, 0};   // PVs issued per tile
+        // S_x of chunk j (K slot j % KS)
+        auto issue_s = [&](int j, int x) {
+          const uint32_t ka = sbase + C::OFF_K + (j % C::KS) * C::KV_BYTES;
+          const uint32_t qa = sbase + C::OFF_Q + x * C::Q_BYTES;
+          const uint32_t dst = tbase + x * C::TILE_COLS;
+          const uint64_t qd = sdesc_sw128(qa, 16, 1024), kd = sdesc_sw128(ka, 16, 1024);
+  #pragma unroll
+          for (int kk = 0; kk < D / 16; ++kk) {
+            const uint32_t off = (kk & 3) * 32u;
+            tc_mma(dst, sdesc_add(qd, (kk >> 2) * C::PANEL_Q + off),
+                   sdesc_add(kd, (kk >> 2) * C::PANEL_KV + off), C::IDESC_S, kk > 0 ? 1u : 0u);
+          }
+          tc_commit(bar(C::BAR_SF + x));
+        };
+        bool ok = mbar_wait(bar(C::BAR_Q), 0, abort_flag, p.err);
+        uint32_t e[2], en[2];
+        bool has = ok && it.next(e, p.err);
+        if (has) {
+          ok = mbar_wait(bar(C::BAR_KF + 0), 0, abort_flag, p.err);
+          if (ok) {
             tc_fence_after();
-            const uint32_t pa = tbase + x * C::TILE_COLS;   // P in TMEM
-            const uint32_t dst = pa + C::COL_O;
-            // V is MN-major: 64-column panels BN*128 bytes apart (LBO),
-            // 8-row groups 1024 bytes apart (SBO); 16 rows per k-step
-            const uint64_t vd = sdesc_sw128(va, C::PANEL_KV, 1024);
-#pragma unroll
-            for (int kk = 0; kk < C::BN / 16; ++kk)
-              tc_mma_ts(dst, pa + p_col(kk), sdesc_add(vd, kk * 2048), C::IDESC_O,
-                        (cp[x] > 0 || kk > 0) ? 1u : 0u);
-            tc_commit(bar(C::BAR_PV + x));
-            ++cp[x];
+  #pragma unroll
+            for (int x = 0; x < C::NT; ++x)
+              if (active(e, x)) issue_s(0, x);
+            tc_commit(bar(C::BAR_KE + 0));   // every S of chunk 0 is issued
           }
-          // the tile's next S goes in behind its PV if the K chunk has landed
-          if (nxt && active(en, x)) {
-            if (!loaded) loaded = mbar_try_wait(bar(C::BAR_KF + k1), k1par);
-            if (loaded) {
+        }
+        for (int j = 0; ok && has; ++j) {
+          const bool nxt = it.next(en, p.err);
+          const int sv = j % C::VS;
+          const int k1 = (j + 1) % C::KS;
+          const int k1par = ((j + 1) / C::KS) & 1;
+          const uint32_t va = sbase + C::OFF_V + sv * C::KV_BYTES;
+          if (!mbar_wait(bar(C::BAR_VF + sv), (j / C::VS) & 1, abort_flag, p.err)) break;
+          bool loaded = false;     // K of chunk j + 1 has landed
+          bool pending[C::NT] = {false, false};
+  #pragma unroll
+          for (int x = 0; x < C::NT; ++x) {
+            if (active(e, x)) {
+              if (!mbar_wait(bar(C::BAR_PF + x), cp[x] & 1, abort_flag, p.err)) {
+                ok = false;
+                break;
+              }
               tc_fence_after();
-              issue_s(j + 1, x);
-            } else {
-              pending[x] = true;
+              const uint32_t pa = tbase + x * C::TILE_COLS;   // P in TMEM
+              const uint32_t dst = pa + C::COL_O;
+              // V is MN-major: 64-column panels BN*128 bytes apart (LBO),
+              // 8-row groups 1024 bytes apart (SBO); 16 rows per k-step
+              const uint64_t vd = sdesc_sw128(va, C::PANEL_KV, 1024);
+  #pragma unroll
+              for (int kk = 0; kk < C::BN / 16; ++kk)
+                tc_mma_ts(dst, pa + p_col(kk), sdesc_add(vd, kk * 2048), C::IDESC_O,
+                          (cp[x] > 0 || kk > 0) ? 1u : 0u);
+              tc_commit(bar(C::BAR_PV + x));
+              ++cp[x];
+            }
+            // the tile's next S goes in behind its PV if the K chunk has landed
+            if (nxt && active(en, x)) {
+              if (!loaded) loaded = mbar_try_wait(bar(C::BAR_KF + k1), k1par);
+              if (loaded) {
+                tc_fence_after();
+                issue_s(j + 1, x);
+              } else {
+                pending[x] = true;
+              }
             }
           }
+          if (!ok) break;
+          tc_commit(bar(C::BAR_VE + sv));   // V_j is read by both PVs
+          if (pending[0] || pending[1]) {
+            if (!mbar_wait(bar(C::BAR_KF + k1), k1par, abort_flag, p.err)) break;
+            tc_fence_after();
+  #pragma unroll
+            for (int x = 0; x < C::NT; ++x)
+              if (pending[x]) issue_s(j + 1, x);
+          }
+          if (nxt) tc_commit(bar(C::BAR_KE + k1));   // every S of chunk j + 1 is issued
+          e[0] = en[0];
+          e[1] = en[1];
+          has = nxt;
         }
-        if (!ok) break;
-        tc_commit(bar(C::BAR_VE + sv));   // V_j is read by both PVs
-        if (pending[0] || pending[1]) {
-          if (!mbar_wait(bar(C::BAR_KF + k1), k1par, abort_flag, p.err)) break;
-          tc_fence_after();
-#pragma unroll
-          for (int x = 0; x < C::NT; ++x)
-            if (pending[x]) issue_s(j + 1, x);
+        if (*abort_flag) {  // let the MMAs in flight finish before TMEM is freed
+          tc_commit(bar(C::BAR_DRAIN));
+          mbar_wait_drain(bar(C::BAR_DRAIN), 0);
         }
-        if (nxt) tc_commit(bar(C::BAR_KE + k1));   // every S of chunk j + 1 is issued
-        e[0] = en[0];
-        e[1] = en[1];
-        has = nxt;
-      }
-      if (*abort_flag) {  // let the MMAs in flight finish before TMEM is freed
-        tc_commit(bar(C::BAR_DRAIN));
-        mbar_wait_drain(bar(C::BAR_DRAIN), 0);
       }
     }
   } else {
+    regs_inc<C::REGS_SOFTMAX>();
     // ------------------------------------------------------------ softmax
     const int x = warp >> 2;                   // tile of this warpgroup
     const int r = (warp & 3) * 32 + lane;      // row within the tile = TMEM lane
@@ -354,28 +368,28 @@ __global__ void __launch_bounds__(320, 1)
         break;
       }
       tc_fence_after();
+      // the whole row of scores in one TMEM read
+      float s[128];
+      tmem_ld128(lane_base, s);
       // quarter qq (32 keys, TMEM columns 32 qq ..): mask of this row
-      auto mask = [&](float* s, int qq) {
+#pragma unroll
+      for (int qq = 0; qq < 4; ++qq) {
         const uint32_t sq = (qq >> 1) ? st[1] : st[0];
         if (sq != ST_FULL) {   // uniform per warp: its 32 rows share one CSR row
           const uint32_t w = qq == 0 ? mw0 : (qq == 1 ? mw1 : (qq == 2 ? mw2 : mw3));
 #pragma unroll
           for (int i = 0; i < 32; ++i)
-            if (!((w >> i) & 1u)) s[i] = -INFINITY;
+            if (!((w >> i) & 1u)) s[32 * qq + i] = -INFINITY;
         }
-      };
-      float s[32];
-      float mx[4];   // three-input max: 16 instructions per 32 scores
-#pragma unroll
-      for (int a = 0; a < 4; ++a) mx[a] = -INFINITY;
-#pragma unroll 1
-      for (int qq = 0; qq < 4; ++qq) {
-        tmem_ld32(lane_base + 32 * qq, s);
-        mask(s, qq);
-#pragma unroll
-        for (int i = 0; i < 32; i += 2) mx[(i >> 1) & 3] = fmax3(mx[(i >> 1) & 3], s[i], s[i + 1]);
       }
-      const float m_new = fmaxf(m, fmax3(fmaxf(mx[0], mx[1]), mx[2], mx[3]) * p.scale_log2);
+      float mx[8];   // three-input max: 64 instructions per 128 scores
+#pragma unroll
+      for (int a = 0; a < 8; ++a) mx[a] = s[a];
+#pragma unroll
+      for (int i = 8; i < 128; i += 2) mx[(i >> 1) & 7] = fmax3(mx[(i >> 1) & 7], s[i], s[i + 1]);
+      const float m_new = fmaxf(
+          m, fmax3(fmax3(mx[0], mx[1], mx[2]), fmax3(mx[3], mx[4], mx[5]), fmaxf(mx[6], mx[7])) *
+                 p.scale_log2);
       const bool need = m_new > m + 8.0f;
       const bool rescale = __any_sync(0xffffffffu, need);
       const float alpha = need ? ex2_approx(m - m_new) : 1.f;
@@ -389,16 +403,14 @@ __global__ void __launch_bounds__(320, 1)
 #pragma unroll
       for (int a = 0; a < 4; ++a) rs2[a] = 0ull;
       // P of quarter qq packed into 16 columns at the start of its half's S
-      // columns (64 h + 16 (qq % 2)): only scores already read are overwritten
-#pragma unroll 1
+      // columns (64 h + 16 (qq % 2))
+#pragma unroll
       for (int qq = 0; qq < 4; ++qq) {
-        tmem_ld32(lane_base + 32 * qq, s);
-        mask(s, qq);
         uint32_t pw[16];
 #pragma unroll
         for (int i = 0; i < 16; ++i) {
           float xa, xb;
-          f2_split(ffma2(f2_bits(s[2 * i], s[2 * i + 1]), c2, nm2), xa, xb);
+          f2_split(ffma2(f2_bits(s[32 * qq + 2 * i], s[32 * qq + 2 * i + 1]), c2, nm2), xa, xb);
           const float a = ex2_approx(xa), bb = ex2_approx(xb);
           rs2[i & 3] = fadd2(rs2[i & 3], f2_bits(a, bb));
           pw[i] = pack_bf16(a, bb);
