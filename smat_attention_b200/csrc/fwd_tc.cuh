@@ -19,13 +19,13 @@
 // bs = 64 a chunk is two 64-key blocks of the merged list; a missing second
 // half is loaded from row T (zero-filled) and masked.
 //
-// Warp roles (384 threads):
+// Warp roles (384 threads; 256 with one tile per CTA, see FwdCfg):
 //   warps 0-3 / 4-7  softmax + epilogue of tile 0 / tile 1; thread r of a
 //                    warpgroup owns row r of its tile = TMEM lane r
 //   warp 8           TMA producer (lane 0: both Q tiles, then the K ring;
 //                    lane 1: the V ring)
 //   warp 9           TMEM allocator and MMA issuer (one lane)
-//   warps 10-11      idle (they complete warpgroup 2)
+//   warps 10-11      idle (they complete the last warpgroup)
 // The softmax warpgroups take registers from warpgroup 2 (setmaxnreg) so a
 // thread holds its whole 128-score row: S is read from TMEM once per chunk.
 // P of key half h (keys 64 h .. 64 h + 63) is packed into the first 32 of
@@ -56,9 +56,16 @@ struct FwdParams {
   MdPattern md;              // tables of PATTERN tiles (null row_bits: the layout has none)
 };
 
-template <int D>
+// NT_ query tiles per CTA: 2 (one CTA per SM; its two softmax warpgroups
+// alternate on the tensor core) or 1 (D = 64 only: two CTAs per SM alternate,
+// and one CTA's set-up and epilogue overlap the other's chunks).
+template <int D, int NT_>
 struct FwdCfg {
-  static constexpr int BM = 128, NT = 2, BN = 128, BOX = 64;
+  static constexpr int BM = 128, NT = NT_, BN = 128, BOX = 64;
+  static_assert(NT == 2 || (NT == 1 && D == 64), "tiles per CTA");
+  static constexpr int MIN_BLOCKS = 3 - NT;   // CTAs per SM
+  // per-CTA shared memory: 227 KB alone, 113 KB with two CTAs per SM
+  static constexpr int SMEM_CAP = (NT == 2 ? 227 : 113) * 1024;
   static constexpr int Q_BYTES = BM * D * 2;
   static constexpr int KV_BYTES = BN * D * 2;
   static constexpr int PANEL_Q = BM * 128, PANEL_KV = BN * 128;  // 64-column SW128 panels
@@ -66,7 +73,7 @@ struct FwdCfg {
   // early, V_j by PV(j) only; the shared memory left over after Q holds
   // KS + VS chunk slots, K taking the larger share (at most 8 each)
   static constexpr int FIXED = NT * Q_BYTES + 2048;  // + barriers, alignment
-  static constexpr int SLOTS = (227 * 1024 - FIXED) / KV_BYTES;
+  static constexpr int SLOTS = (SMEM_CAP - FIXED) / KV_BYTES;
   static constexpr int VS = (SLOTS / 2) > 8 ? 8 : SLOTS / 2;
   static constexpr int KS = (SLOTS - VS) > 8 ? 8 : SLOTS - VS;
   static constexpr int OFF_Q = 0;
@@ -80,16 +87,18 @@ struct FwdCfg {
                        BAR_PV = BAR_PF + NT, BAR_DRAIN = BAR_PV + NT, NBAR = BAR_DRAIN + 1;
   static constexpr int OFF_MISC = OFF_BAR + NBAR * 8;  // tmem ptr, abort flag
   static constexpr int SMEM_BYTES = OFF_MISC + 16 + 1024;  // + alignment slack
-  static_assert(SMEM_BYTES <= 227 * 1024, "shared memory budget");
+  static_assert(SMEM_BYTES <= SMEM_CAP, "shared memory budget");
   static_assert(KS >= 2 && VS >= 2, "at least two slots per ring");
-  static constexpr int TMEM_COLS = 512, TILE_COLS = 256, COL_O = 128;
+  static constexpr int TILE_COLS = 256, COL_O = 128, TMEM_COLS = NT * TILE_COLS;
   static_assert(COL_O + D <= TILE_COLS, "TMEM budget");
-  // warpgroups 0 / 1 softmax, warpgroup 2 the producer and MMA warps (and two
-  // idle ones, so that every warpgroup is whole for the register split)
-  static constexpr int THREADS = 384;
-  static constexpr int REGS_LAUNCH = (65536 / THREADS) & ~7;   // 168
-  static constexpr int REGS_SOFTMAX = 192, REGS_OTHER = 112;
-  static_assert(128 * (2 * REGS_SOFTMAX + REGS_OTHER) <= THREADS * REGS_LAUNCH,
+  // warpgroups 0 (and 1) softmax, the last warpgroup the producer and MMA
+  // warps (and two idle ones, so that every warpgroup is whole for the
+  // register split)
+  static constexpr int PRODUCER_WARP = 4 * NT, MMA_WARP = 4 * NT + 1;
+  static constexpr int THREADS = 128 * (NT + 1);
+  static constexpr int REGS_LAUNCH = (65536 / (THREADS * MIN_BLOCKS)) & ~7;   // 168 / 128
+  static constexpr int REGS_SOFTMAX = NT == 2 ? 192 : 176, REGS_OTHER = NT == 2 ? 112 : 80;
+  static_assert(128 * (NT * REGS_SOFTMAX + REGS_OTHER) <= THREADS * REGS_LAUNCH,
                 "register split exceeds the launch allocation");
   static constexpr uint32_t IDESC_S = idesc_bf16(BM, BN, false, false);
   static constexpr uint32_t IDESC_O = idesc_bf16(BM, D, false, true);
@@ -99,13 +108,13 @@ struct FwdCfg {
 // of that half's S columns
 __device__ __forceinline__ uint32_t p_col(int kk) { return 64u * (kk >> 2) + 8u * (kk & 3); }
 
-template <int D>
-__global__ void __launch_bounds__(384, 1)
+template <int D, int NT>
+__global__ void __launch_bounds__(FwdCfg<D, NT>::THREADS, FwdCfg<D, NT>::MIN_BLOCKS)
     smat_fwd_tc_kernel(const __grid_constant__ CUtensorMap tm_q,
                        const __grid_constant__ CUtensorMap tm_k,
                        const __grid_constant__ CUtensorMap tm_v,
                        const __grid_constant__ CUtensorMap tm_o, const FwdParams p) {
-  using C = FwdCfg<D>;
+  using C = FwdCfg<D, NT>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
@@ -125,13 +134,14 @@ __global__ void __launch_bounds__(384, 1)
     const int w = __ldg(p.work + lin / BH);
     tile0 = w & WORK_TILE_MASK;
     ntile = (w & WORK_PAIR_BIT) ? 2 : 1;
-    if ((w >> 25) != 0 || tile0 + ntile > p.n_tiles) {
+    if ((w >> 25) != 0 || ntile > NT || tile0 + ntile > p.n_tiles) {
       if (threadIdx.x == 0 && p.err) atomicOr(p.err, DEV_ERR_BAD_WORK);
       return;
     }
   } else {
-    tile0 = 2 * (p.n_pairs - 1 - lin / BH);  // heaviest (latest) tiles first
-    ntile = min(2, p.n_tiles - tile0);
+    // heaviest (latest) tiles first
+    tile0 = NT * ((p.n_tiles + NT - 1) / NT - 1 - lin / BH);
+    ntile = min(NT, p.n_tiles - tile0);
   }
   const int b = bh / p.H, h = bh % p.H;
   const int sub = C::BM / p.bs;   // CSR rows per tile: 1 (bs 128) or 2 (bs 64)
@@ -160,11 +170,11 @@ __global__ void __launch_bounds__(384, 1)
     fence_barrier_init();
     misc[1] = 0;
   }
-  if (warp == 9) {
+  if (warp == C::MMA_WARP) {
     tmem_alloc(sbase + C::OFF_MISC, C::TMEM_COLS);
     tmem_relinquish();
   }
-  if (warp == 8 && lane == 0) {
+  if (warp == C::PRODUCER_WARP && lane == 0) {
     prefetch_tmap(&tm_q);
     prefetch_tmap(&tm_k);
     prefetch_tmap(&tm_v);
@@ -176,9 +186,9 @@ __global__ void __launch_bounds__(384, 1)
 
   // Each warpgroup changes its register count at the top of its own branch, so
   // that no code path joins between the change and the role's code.
-  if (warp >= 8) {
+  if (warp >= C::PRODUCER_WARP) {
     regs_dec<C::REGS_OTHER>();
-    if (warp == 8) {
+    if (warp == C::PRODUCER_WARP) {
       // ------------------------------------------------------------ producer
       // lane 0: both Q tiles, then the K ring; lane 1: the V ring.  Each lane
       // walks the schedule on its own, so a V slot that frees late never holds
@@ -230,12 +240,12 @@ __global__ void __launch_bounds__(384, 1)
             mbar_wait_drain(bar(full + j % NS), (j / NS) & 1);
         }
       }
-    } else if (warp == 9) {
+    } else if (warp == C::MMA_WARP) {
       // ------------------------------------------------------------ MMA issuer
       if (lane == 0) {
         ChunkPair<4> it;
         it.init(p.indptr, p.indices, p.kind, p.nblocks, p.nnzb, row0, ntile * sub, p.bs, p.err);
-        int cp[C::NT] = {0, 0};   // PVs issued per tile
+        int cp[C::NT] = {};   // PVs issued per tile
         // S_x of chunk j (K slot j % KS)
         auto issue_s = [&](int j, int x) {
           const uint32_t ka = sbase + C::OFF_K + (j % C::KS) * C::KV_BYTES;
@@ -271,7 +281,7 @@ __global__ void __launch_bounds__(384, 1)
           const uint32_t va = sbase + C::OFF_V + sv * C::KV_BYTES;
           if (!mbar_wait(bar(C::BAR_VF + sv), (j / C::VS) & 1, abort_flag, p.err)) break;
           bool loaded = false;     // K of chunk j + 1 has landed
-          bool pending[C::NT] = {false, false};
+          bool pending[C::NT] = {};
   #pragma unroll
           for (int x = 0; x < C::NT; ++x) {
             if (active(e, x)) {
@@ -305,7 +315,10 @@ __global__ void __launch_bounds__(384, 1)
           }
           if (!ok) break;
           tc_commit(bar(C::BAR_VE + sv));   // V_j is read by both PVs
-          if (pending[0] || pending[1]) {
+          bool any_pending = false;
+  #pragma unroll
+          for (int x = 0; x < C::NT; ++x) any_pending |= pending[x];
+          if (any_pending) {
             if (!mbar_wait(bar(C::BAR_KF + k1), k1par, abort_flag, p.err)) break;
             tc_fence_after();
   #pragma unroll
@@ -496,7 +509,7 @@ __global__ void __launch_bounds__(384, 1)
 
   tc_fence_before();
   __syncthreads();
-  if (warp == 9) {
+  if (warp == C::MMA_WARP) {
     __syncwarp();
     tc_fence_after();
     tmem_dealloc(tbase, C::TMEM_COLS);

@@ -173,12 +173,12 @@ int launch_status() {
 }
 
 // ---------------------------------------------------------------- forward
-template <int D>
+template <int D, int NT>
 int fwd_tc(const TArg& q, const TArg& k, const TArg& v, const TArg& o, float* lse, int B, int H,
            int T, const int32_t* indptr, const int32_t* indices, const uint8_t* kind,
            int nblocks, int64_t nnzb, int block, float scale, const Work& work,
            const MdPattern& md, int32_t* err, cudaStream_t s) {
-  using C = FwdCfg<D>;
+  using C = FwdCfg<D, NT>;
   CUtensorMap mq, mk, mv, mo;
   int rc;
   if ((rc = make_map(&mq, q, B, H, T, D, C::BM))) return rc;
@@ -206,9 +206,10 @@ int fwd_tc(const TArg& q, const TArg& k, const TArg& v, const TArg& o, float* ls
   p.scale_log2 = scale * 1.4426950408889634f;
   p.err = err;
   p.md = md;
-  auto kern = smat_fwd_tc_kernel<D>;
+  auto kern = smat_fwd_tc_kernel<D, NT>;
   if ((rc = set_smem(kern, C::SMEM_BYTES))) return rc;
-  const int64_t grid = static_cast<int64_t>(work.items ? work.n : p.n_pairs) * B * H;
+  const int64_t grid =
+      static_cast<int64_t>(work.items ? work.n : (p.n_tiles + NT - 1) / NT) * B * H;
   if (grid == 0) return SMAT_OK;
   kern<<<static_cast<unsigned>(grid), C::THREADS, C::SMEM_BYTES, s>>>(mq, mk, mv, mo, p);
   return launch_status();
@@ -586,11 +587,16 @@ int fwd_impl(int dtype, const void* q, const int64_t* q_stride, const void* k,
   if (!std::isfinite(scale) || scale <= 0.f) return SMAT_ERR_BAD_SHAPE;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (dtype == SMAT_DTYPE_BF16) {
+    // D = 64: one tile per CTA, two CTAs per SM (work lists name tile pairs,
+    // which take the two-tile kernel)
+    if (D == 64 && !work.items)
+      return fwd_tc<64, 1>(tq, tk, tv, to, lse, B, H, T, indptr, indices, kind, nblocks, nnzb,
+                           block, scale, work, md, err_word, s);
     if (D == 64)
-      return fwd_tc<64>(tq, tk, tv, to, lse, B, H, T, indptr, indices, kind, nblocks, nnzb, block,
-                        scale, work, md, err_word, s);
-    return fwd_tc<128>(tq, tk, tv, to, lse, B, H, T, indptr, indices, kind, nblocks, nnzb, block,
-                       scale, work, md, err_word, s);
+      return fwd_tc<64, 2>(tq, tk, tv, to, lse, B, H, T, indptr, indices, kind, nblocks, nnzb,
+                           block, scale, work, md, err_word, s);
+    return fwd_tc<128, 2>(tq, tk, tv, to, lse, B, H, T, indptr, indices, kind, nblocks, nnzb,
+                          block, scale, work, md, err_word, s);
   }
   SimtParams p = simt_params(B, H, T, block, scale, indptr, indices, kind, nblocks, nnzb, err_word,
                              work, 2, md);
