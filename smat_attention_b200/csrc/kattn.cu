@@ -119,16 +119,33 @@ struct TileCfg {
   static constexpr bool LOWER = MODE == TM_FWD || MODE == TM_DPHI;
   static constexpr int PANEL = KC * 128;                 // 128 rows x 32 fp32
   static constexpr int EX_PANEL = R * 128;               // R rows x 32 fp32
+  static constexpr int SZ_A1 = (K1 / 32) * PANEL, SZ_B1 = SZ_A1, SZ_B2 = (NO / 32) * PANEL;
+  static constexpr int SZ_EX = EXTRA ? (PN / 32) * EX_PANEL : 0;
+  // barriers: TMA full, copies full (128 arrivals), G full, G masked (4), OUT
+  // full, B2 full (the late B2 of the aliased layout)
+  static constexpr int BAR_TMA = 0, BAR_CP = 1, BAR_SF = 2, BAR_SM = 3, BAR_OF = 4, BAR_B2 = 5,
+                       NBAR = 6;
+  static constexpr int TAIL = NBAR * 8 + 16 + 1024;   // barriers, misc, alignment slack
+  // Two CTAs per SM need <= 113 KB each.  B2 is read only by the last MMA
+  // group, B1 only by the first: where that brings the layout under the
+  // limit, B2 is loaded over B1 once G has been computed (the other CTA on
+  // the SM covers the load).
+  static constexpr int CAP2 = 113 * 1024;
+  static constexpr int PLAIN = SZ_A1 + SZ_B1 + SZ_B2 + SZ_EX + TAIL;
+  static constexpr int SZ_B12 = SZ_B1 > SZ_B2 ? SZ_B1 : SZ_B2;
+  static constexpr bool ALIAS = PLAIN > CAP2 && SZ_A1 + SZ_B12 + SZ_EX + TAIL <= CAP2;
   static constexpr int OFF_A1 = 0;
-  static constexpr int OFF_B1 = OFF_A1 + (K1 / 32) * PANEL;
-  static constexpr int OFF_B2 = OFF_B1 + (K1 / 32) * PANEL;
-  static constexpr int OFF_EX = OFF_B2 + (NO / 32) * PANEL;
-  static constexpr int OFF_BAR = OFF_EX + (EXTRA ? (PN / 32) * EX_PANEL : 0);
-  // barriers: TMA full, copies full (128 arrivals), G full, G masked (4), OUT full
-  static constexpr int BAR_TMA = 0, BAR_CP = 1, BAR_SF = 2, BAR_SM = 3, BAR_OF = 4, NBAR = 5;
+  static constexpr int OFF_B1 = OFF_A1 + SZ_A1;
+  static constexpr int OFF_B2 = ALIAS ? OFF_B1 : OFF_B1 + SZ_B1;
+  static constexpr int OFF_EX = OFF_B1 + (ALIAS ? SZ_B12 : SZ_B1 + SZ_B2);
+  static constexpr int OFF_BAR = OFF_EX + SZ_EX;
   static constexpr int OFF_MISC = OFF_BAR + NBAR * 8;
   static constexpr int SMEM_BYTES = OFF_MISC + 16 + 1024;
   static_assert(SMEM_BYTES <= 227 * 1024, "shared memory budget");
+  static constexpr int MIN_BLOCKS = SMEM_BYTES <= CAP2 ? 2 : 1;
+  // OUT is staged in the operand tiles: KC rows at a stride of NO + 1 words
+  static constexpr int STAGE_LD = NO + 1;
+  static_assert(KC * STAGE_LD * 4 <= OFF_BAR, "OUT staging");
   static constexpr int COL_G = 0, COL_O = 128, TMEM_COLS = 256;
   static_assert(COL_O + NO <= TMEM_COLS, "TMEM budget");
   // bytes the producer's TMA loads bring
@@ -166,7 +183,7 @@ __device__ __forceinline__ void cp_mn32(uint32_t dst, const float* src, int t, i
 // (thread = row = TMEM lane); warp 4 issues the TMA loads; warp 5 allocates
 // TMEM and issues the MMAs.
 template <int MODE, int R, int PN>
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(192, (TileCfg<MODE, R, PN>::MIN_BLOCKS))
     kattn_tile_kernel(const __grid_constant__ CUtensorMap tm0,
                       const __grid_constant__ CUtensorMap tm1, const TileParams p) {
   using C = TileCfg<MODE, R, PN>;
@@ -187,6 +204,7 @@ __global__ void __launch_bounds__(192, 1)
     mbar_init(bar(C::BAR_SF), 1);
     mbar_init(bar(C::BAR_SM), 4);
     mbar_init(bar(C::BAR_OF), 1);
+    mbar_init(bar(C::BAR_B2), C::KR_G1 ? 128 : 1);   // compute warps' copies, or TMA
     fence_barrier_init();
     misc[1] = 0;
   }
@@ -209,15 +227,24 @@ __global__ void __launch_bounds__(192, 1)
           tma_load_2d(sbase + C::OFF_A1 + k * C::PANEL, &tm0, bar(C::BAR_TMA), 32 * k, row0);
           tma_load_2d(sbase + C::OFF_B1 + k * C::PANEL, &tm1, bar(C::BAR_TMA), 32 * k, row0);
         }
-      } else {                 // B2 from the 32-byte-atom map
+      } else if (!C::ALIAS) {  // B2 from the 32-byte-atom map
 #pragma unroll
         for (int k = 0; k < C::NO / 32; ++k)
           tma_load_2d(sbase + C::OFF_B2 + k * C::PANEL, &tm0, bar(C::BAR_TMA), 32 * k, row0);
+      } else if (mbar_wait(bar(C::BAR_SF), 0, abort_flag, p.err)) {
+        // aliased: B2 over B1 once G (the only reader of B1) has completed
+        tc_fence_after();
+        mbar_expect_tx(bar(C::BAR_B2), C::SZ_B2);
+#pragma unroll
+        for (int k = 0; k < C::NO / 32; ++k)
+          tma_load_2d(sbase + C::OFF_B2 + k * C::PANEL, &tm0, bar(C::BAR_B2), 32 * k, row0);
+        mbar_wait_drain(bar(C::BAR_B2), 0);   // never exit with the load in flight
       }
     }
   } else if (warp == 5) {
     if (lane == 0) {
-      bool ok = mbar_wait(bar(C::BAR_TMA), 0, abort_flag, p.err) &&
+      // (the aliased layouts without TMA operands before G load nothing there)
+      bool ok = ((!C::KR_G1 && C::ALIAS) || mbar_wait(bar(C::BAR_TMA), 0, abort_flag, p.err)) &&
                 mbar_wait(bar(C::BAR_CP), 0, abort_flag, p.err);
       if (ok) {
         tc_fence_after();
@@ -242,7 +269,8 @@ __global__ void __launch_bounds__(192, 1)
                      C::IDESC_EX, kk > 0);
           }
         }
-        ok = mbar_wait(bar(C::BAR_SM), 0, abort_flag, p.err);
+        ok = mbar_wait(bar(C::BAR_SM), 0, abort_flag, p.err) &&
+             (!C::ALIAS || mbar_wait(bar(C::BAR_B2), 0, abort_flag, p.err));
       }
       if (ok) {
         tc_fence_after();
@@ -267,14 +295,14 @@ __global__ void __launch_bounds__(192, 1)
     const float* dO = p.dout + rows_off;
     const float* sn = p.sin + chunk * R * p.P;
     if (MODE == TM_FWD) {
-      cp_mn32<PN>(sbase + C::OFF_B2, vb, r, 128, KC, p.P);
+      if (!C::ALIAS) cp_mn32<PN>(sbase + C::OFF_B2, vb, r, 128, KC, p.P);
       cp_mn32<PN>(sbase + C::OFF_EX, sn, r, 128, R, p.P);
     } else if (MODE == TM_DPHI) {
       cp_kmajor<PN>(sbase + C::OFF_A1, dO, r, 128, KC, p.P);
       cp_kmajor<PN>(sbase + C::OFF_B1, vb, r, 128, KC, p.P);
       cp_kmajor<PN>(sbase + C::OFF_EX, sn, r, 128, R, p.P);
     } else if (MODE == TM_DV) {
-      cp_mn32<PN>(sbase + C::OFF_B2, dO, r, 128, KC, p.P);
+      if (!C::ALIAS) cp_mn32<PN>(sbase + C::OFF_B2, dO, r, 128, KC, p.P);
     } else {
       cp_kmajor<PN>(sbase + C::OFF_A1, vb, r, 128, KC, p.P);
       cp_kmajor<PN>(sbase + C::OFF_B1, dO, r, 128, KC, p.P);
@@ -286,6 +314,10 @@ __global__ void __launch_bounds__(192, 1)
     bool alive = __all_sync(0xffffffffu, mbar_wait(bar(C::BAR_SF), 0, abort_flag, p.err));
     if (alive) {
       tc_fence_after();
+      // aliased FWD / DV: B2 over B1, which G has read; the copies overlap
+      // the masking below
+      if (C::ALIAS && C::KR_G1) cp_mn32<PN>(sbase + C::OFF_B2, MODE == TM_FWD ? vb : dO, r, 128,
+                                            KC, p.P);
       // lower: keep G[r, j] for j <= r; upper: keep j >= r
 #pragma unroll 1
       for (int q = 0; q < 4; ++q) {
@@ -308,18 +340,42 @@ __global__ void __launch_bounds__(192, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(bar(C::BAR_SM));
+      if (C::ALIAS && C::KR_G1) {
+        asm volatile("cp.async.wait_all;" ::: "memory");
+        fence_proxy_async_smem();
+        mbar_arrive(bar(C::BAR_B2));
+      }
       alive = __all_sync(0xffffffffu, mbar_wait(bar(C::BAR_OF), 0, abort_flag, p.err));
     }
+    // OUT leaves through shared memory (every operand tile is free once the
+    // last MMA has completed): each thread writes its row at a stride of
+    // NO + 1 words (no bank conflicts), then the four warps copy the chunk's
+    // contiguous [KC, n_store] block to global memory in coalesced stores.
+    float* stg = reinterpret_cast<float*>(smem + C::OFF_A1);
     if (alive) {
       tc_fence_after();
-      float* orow = p.out + (chunk * KC + r) * p.n_store;
 #pragma unroll 1
       for (int c0 = 0; c0 < C::NO; c0 += 32) {
         float o[32];
         tmem_ld32(lane_base + C::COL_O + c0, o);
 #pragma unroll
         for (int i = 0; i < 32; ++i)
-          if (c0 + i < p.n_store) orow[c0 + i] = o[i];
+          if (c0 + i < p.n_store) stg[r * C::STAGE_LD + c0 + i] = o[i];
+      }
+    }
+    named_barrier_sync(1, 128);
+    if (alive) {
+      float* dst = p.out + chunk * KC * p.n_store;
+      int row = r / p.n_store, col = r % p.n_store;
+      const int step_rows = 128 / p.n_store, step_cols = 128 % p.n_store;
+      for (int e = r; e < KC * p.n_store; e += 128) {
+        dst[e] = stg[row * C::STAGE_LD + col];
+        row += step_rows;
+        col += step_cols;
+        if (col >= p.n_store) {
+          col -= p.n_store;
+          ++row;
+        }
       }
     }
   }

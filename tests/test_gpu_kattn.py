@@ -34,7 +34,8 @@ def _feat(*shape, g):
     return torch.nn.functional.elu(torch.randn(*shape, generator=g, dtype=torch.float64)) + 1
 
 
-@pytest.mark.parametrize("R,P", [(32, 9), (64, 65), (64, 17), (128, 96), (32, 128)])
+@pytest.mark.parametrize("R,P", [(32, 9), (64, 65), (64, 17), (128, 96), (32, 128), (64, 60),
+                                 (32, 70), (128, 20)])
 def test_chunk_local(cuda_device, R, P):
     g = torch.Generator().manual_seed(R + P)
     nb, nc, C = 2, 3, 128
