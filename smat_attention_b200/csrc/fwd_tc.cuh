@@ -130,13 +130,23 @@ __global__ void __launch_bounds__(FwdCfg<D, NT>::THREADS, FwdCfg<D, NT>::MIN_BLO
   const int bh = lin % BH;
   int tile0, ntile;
   if (p.work) {
-    // caller-chosen tiles (a shard of the queries), in the caller's order
-    const int w = __ldg(p.work + lin / BH);
-    tile0 = w & WORK_TILE_MASK;
+    // caller-chosen tiles (a shard of the queries), in the caller's order.
+    // With one tile per CTA an item takes two CTAs (the second returns at
+    // once for a single-tile item), so every tile walks its own chunk list
+    // exactly as in the launch without a work list -- the per-row results
+    // are bitwise the same.
+    constexpr int PER = 3 - NT;   // CTAs per item
+    const int w = __ldg(p.work + lin / (BH * PER));
+    const int half = (lin / BH) % PER;
+    tile0 = (w & WORK_TILE_MASK) + half;
     ntile = (w & WORK_PAIR_BIT) ? 2 : 1;
-    if ((w >> 25) != 0 || ntile > NT || tile0 + ntile > p.n_tiles) {
+    if ((w >> 25) != 0 || (w & WORK_TILE_MASK) + ntile > p.n_tiles) {
       if (threadIdx.x == 0 && p.err) atomicOr(p.err, DEV_ERR_BAD_WORK);
       return;
+    }
+    if (NT == 1) {
+      if (half >= ntile) return;
+      ntile = 1;
     }
   } else {
     // heaviest (latest) tiles first

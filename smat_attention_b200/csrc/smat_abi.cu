@@ -209,7 +209,7 @@ int fwd_tc(const TArg& q, const TArg& k, const TArg& v, const TArg& o, float* ls
   auto kern = smat_fwd_tc_kernel<D, NT>;
   if ((rc = set_smem(kern, C::SMEM_BYTES))) return rc;
   const int64_t grid =
-      static_cast<int64_t>(work.items ? work.n : (p.n_tiles + NT - 1) / NT) * B * H;
+      static_cast<int64_t>(work.items ? work.n * (3 - NT) : (p.n_tiles + NT - 1) / NT) * B * H;
   if (grid == 0) return SMAT_OK;
   kern<<<static_cast<unsigned>(grid), C::THREADS, C::SMEM_BYTES, s>>>(mq, mk, mv, mo, p);
   return launch_status();
@@ -587,13 +587,10 @@ int fwd_impl(int dtype, const void* q, const int64_t* q_stride, const void* k,
   if (!std::isfinite(scale) || scale <= 0.f) return SMAT_ERR_BAD_SHAPE;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (dtype == SMAT_DTYPE_BF16) {
-    // D = 64: one tile per CTA, two CTAs per SM (work lists name tile pairs,
-    // which take the two-tile kernel)
-    if (D == 64 && !work.items)
-      return fwd_tc<64, 1>(tq, tk, tv, to, lse, B, H, T, indptr, indices, kind, nblocks, nnzb,
-                           block, scale, work, md, err_word, s);
+    // D = 64: one tile per CTA, two CTAs per SM (with or without a work list,
+    // so that both launches group a tile's keys into the same chunks)
     if (D == 64)
-      return fwd_tc<64, 2>(tq, tk, tv, to, lse, B, H, T, indptr, indices, kind, nblocks, nnzb,
+      return fwd_tc<64, 1>(tq, tk, tv, to, lse, B, H, T, indptr, indices, kind, nblocks, nnzb,
                            block, scale, work, md, err_word, s);
     return fwd_tc<128, 2>(tq, tk, tv, to, lse, B, H, T, indptr, indices, kind, nblocks, nnzb,
                           block, scale, work, md, err_word, s);
