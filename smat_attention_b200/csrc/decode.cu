@@ -4,8 +4,10 @@
 // One query row reads every visible key and value once, so decode is
 // HBM-bound (2 D bytes per key and value at bf16) and runs on CUDA cores:
 //
-//   partial  grid (B H, n_split), 128 threads.  Split s walks entries
-//            [s bps, (s + 1) bps) of the query's CSR row.  A key is owned by
+//   partial  grid (B H, n_split), 128 threads.  The query's CSR row is a
+//            sequence of steps (STEP keys of one entry each); split s walks
+//            steps [s sps, (s + 1) sps), sps chosen so that the grid fills
+//            whole waves of resident CTAs.  A key is owned by
 //            a group of D / 8 lanes (16-byte vectors, a 256-byte row read by
 //            16 lanes at D = 128), each warp handling 4 x 32 / (D / 8) keys
 //            per step with all their loads issued first (values only for
@@ -21,6 +23,7 @@
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <cmath>
 #include <cstdint>
 
@@ -44,7 +47,7 @@ struct DecodeParams {
   const uint8_t* kind;
   float* part;               // [B H][n_split][D + 2]: m, l, o[D]
   int64_t q_sb, q_sh, k_sb, k_sh, k_st, v_sb, v_sh, v_st, o_sb, o_sh;
-  int B, H, T, nblocks, nnzb, bs, n_split, bps;
+  int B, H, T, nblocks, nnzb, bs, n_split, sps;
   float scale_log2;
   int32_t* err;
   MdPattern md;
@@ -89,8 +92,14 @@ __global__ void __launch_bounds__(128) decode_partial_kernel(const DecodeParams 
   const int slot = lane / G, part = lane % G;
   float* out = p.part + (static_cast<int64_t>(bh) * p.n_split + split) * (D + 2);
 
+  // The row's keys as one sequence of steps: step g covers entry e0 + g / spb,
+  // keys (g % spb) STEP + warp KPW U + u KPW + slot of it.  The loads of step
+  // k + 1 are issued before the arithmetic of step k (two register buffers),
+  // so every warp keeps loads in flight while it computes.
+  constexpr int STEP = 4 * KPW * U;             // keys per CTA step
+  const int spb = (p.bs + STEP - 1) / STEP;     // steps per block
   const int t = __ldg(p.pos + b);
-  int e0 = 0, e1 = 0;
+  int e0 = 0, s0 = 0, nsteps = 0;
   if (t < 0 || t >= p.T) {
     if (threadIdx.x == 0 && p.err) atomicOr(p.err, DEV_ERR_BAD_WORK);
   } else {
@@ -99,8 +108,9 @@ __global__ void __launch_bounds__(128) decode_partial_kernel(const DecodeParams 
     if (a < 0 || z < a || z > p.nnzb) {
       if (threadIdx.x == 0 && p.err) atomicOr(p.err, DEV_ERR_BAD_CSR);
     } else {
-      e0 = a + split * p.bps;
-      e1 = min(z, e0 + p.bps);
+      e0 = a;
+      s0 = split * p.sps;
+      nsteps = max(0, min((z - a) * spb - s0, p.sps));
     }
   }
 
@@ -117,24 +127,18 @@ __global__ void __launch_bounds__(128) decode_partial_kernel(const DecodeParams 
   const __nv_bfloat16* kbase = p.k + b * p.k_sb + h * p.k_sh + part * 8;
   const __nv_bfloat16* vbase = p.v + b * p.v_sb + h * p.v_sh + part * 8;
 
-  // The row's keys as one sequence of steps: step k covers entry
-  // e0 + k / SPB, keys (k % SPB) STEP + warp KPW U + u KPW + slot of it.  The
-  // loads of step k + 1 are issued before the arithmetic of step k (two
-  // register buffers), so every warp keeps loads in flight while it computes.
-  constexpr int STEP = 4 * KPW * U;             // keys per CTA step
-  const int spb = (p.bs + STEP - 1) / STEP;     // steps per block
-  const int nsteps = (e1 - e0) * spb;
   V8 kr[2][U], vr[2][U];
   bool vis[2][U];
   auto issue = [&](int k, int buf) {
-    const int e = e0 + k / spb;
+    const int g = s0 + k;
+    const int e = e0 + g / spb;
     const int kb = __ldg(p.indices + e);
     const uint8_t kd = __ldg(p.kind + e);
     const bool ok = kb >= 0 && kb < p.nblocks && kb * p.bs <= t;
     if (!ok && threadIdx.x == 0 && p.err) atomicOr(p.err, DEV_ERR_BAD_CSR);
     const int j0 = ok ? kb * p.bs : 0;
     const int jn = ok ? min(p.bs, p.T - j0) : 0;
-    const int base = (k % spb) * STEP + warp * KPW * U;
+    const int base = (g % spb) * STEP + warp * KPW * U;
 #pragma unroll
     for (int u = 0; u < U; ++u) {
       const int jj = base + u * KPW + slot;
@@ -156,27 +160,44 @@ __global__ void __launch_bounds__(128) decode_partial_kernel(const DecodeParams 
       if (vs) vr[buf][u] = *reinterpret_cast<const V8*>(vbase + static_cast<int64_t>(j) * p.v_st);
     }
   };
+  // A step's U keys are independent until the softmax update: their dot
+  // products and group reductions interleave, then one max, at most one
+  // rescale, and the U accumulations.
   auto consume = [&](int buf) {
+    float sc[U];
 #pragma unroll
     for (int u = 0; u < U; ++u) {
       float kv[8];
       unpack8(kr[buf][u], kv);
-      float s = 0.f;
+      float s0 = qv[0] * kv[0], s1 = qv[1] * kv[1];
 #pragma unroll
-      for (int i = 0; i < 8; ++i) s = fmaf(qv[i], kv[i], s);
+      for (int i = 2; i < 8; i += 2) {
+        s0 = fmaf(qv[i], kv[i], s0);
+        s1 = fmaf(qv[i + 1], kv[i + 1], s1);
+      }
+      sc[u] = s0 + s1;
+    }
 #pragma unroll
-      for (int off = G / 2; off > 0; off >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
+    for (int off = G / 2; off > 0; off >>= 1)
+#pragma unroll
+      for (int u = 0; u < U; ++u) sc[u] += __shfl_xor_sync(0xffffffffu, sc[u], off);
+    float mx = m;
+#pragma unroll
+    for (int u = 0; u < U; ++u)
+      if (vis[buf][u]) mx = fmaxf(mx, sc[u]);
+    if (mx > m) {
+      const float a = exp2f(m - mx);   // 0 when m is still -inf
+      l *= a;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) o[i] *= a;
+      m = mx;
+    }
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
       if (!vis[buf][u]) continue;
       float vv[8];
       unpack8(vr[buf][u], vv);
-      if (s > m) {
-        const float a = exp2f(m - s);   // 0 when m is still -inf
-        l *= a;
-#pragma unroll
-        for (int i = 0; i < 8; ++i) o[i] *= a;
-        m = s;
-      }
-      const float pr = exp2f(s - m);
+      const float pr = exp2f(sc[u] - m);
       l += pr;
 #pragma unroll
       for (int i = 0; i < 8; ++i) o[i] = fmaf(pr, vv[i], o[i]);
@@ -253,19 +274,42 @@ __global__ void __launch_bounds__(D) decode_combine_kernel(const DecodeParams p)
 
 int status() { return cudaGetLastError() == cudaSuccess ? SMAT_OK : SMAT_ERR_LAUNCH; }
 
-// splits per (b, h) and entries per split: about four waves of CTAs (four
-// resident per SM at 128 registers), so the last wave's tail is short; the
-// split count is then trimmed so that no split is empty
-int entries_per_split(int B, int H, int max_row) {
-  const int64_t bh = static_cast<int64_t>(B) * H;
-  int64_t s = (4 * 592 + bh - 1) / bh;
-  if (s > max_row) s = max_row;
-  if (s < 1) s = 1;
-  return static_cast<int>((max_row + s - 1) / s);
+// CTAs resident at once: four per SM (128 threads at 128 registers)
+int64_t resident_ctas() {
+  int dev = 0, sms = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess ||
+      cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms < 1)
+    sms = 148;
+  return 4LL * sms;
 }
-int n_splits(int B, int H, int max_row) {
-  const int bps = entries_per_split(B, H, max_row);
-  return max_row < 1 ? 1 : (max_row + bps - 1) / bps;
+// Steps per split (a step is 32 keys at D = 128, 64 at D = 64): the grid is
+// sized to the most whole waves of resident CTAs (up to four) whose splits
+// keep at least 8 steps, so a split's set-up is amortised and the last wave
+// is not left mostly empty; then the split count is trimmed so that no split
+// is empty.
+int steps_per_split(int B, int H, int D, int bs, int max_row) {
+  const int64_t bh = static_cast<int64_t>(B) * H, slots = resident_ctas();
+  const int step = D == 64 ? 64 : 32;
+  const int64_t row_steps = std::max<int64_t>(1, static_cast<int64_t>(max_row) * ((bs + step - 1) / step));
+  int64_t best = row_steps;
+  for (int w = 1; w <= 4; ++w) {
+    const int64_t ns = std::max<int64_t>(1, w * slots / bh);
+    const int64_t sps = (row_steps + ns - 1) / ns;
+    if (w == 1 || sps >= 8) best = sps;
+  }
+  return static_cast<int>(best);
+}
+int n_splits(int B, int H, int D, int bs, int max_row) {
+  const int64_t step = D == 64 ? 64 : 32;
+  const int64_t row_steps = std::max<int64_t>(1, static_cast<int64_t>(max_row) * ((bs + step - 1) / step));
+  const int sps = steps_per_split(B, H, D, bs, max_row);
+  return static_cast<int>((row_steps + sps - 1) / sps);
+}
+// an upper bound of n_splits over block sizes (the workspace query has none):
+// the grid never exceeds four waves, and a row has at least one split
+int max_splits(int B, int H) {
+  const int64_t bh = static_cast<int64_t>(B) * H;
+  return static_cast<int>(std::max<int64_t>(1, 4 * resident_ctas() / bh));
 }
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
@@ -277,7 +321,7 @@ extern "C" {
 int smat_decode_workspace(int B, int H, int D, int max_row, int64_t* floats_out) {
   if (B < 1 || H < 1 || max_row < 0 || (D != 64 && D != 128)) return SMAT_ERR_BAD_SHAPE;
   if (!floats_out) return SMAT_ERR_NULL_POINTER;
-  *floats_out = static_cast<int64_t>(B) * H * n_splits(B, H, max_row) * (D + 2);
+  *floats_out = static_cast<int64_t>(B) * H * max_splits(B, H) * (D + 2);
   return SMAT_OK;
 }
 
@@ -323,7 +367,7 @@ int smat_decode(int dtype, const void* q, const int64_t* q_stride, const void* k
     p.md = MdPattern{pt->row_bits, pt->col_bits, pt->family, pt->n,        pt->n_P,
                      pt->B,        pt->N0,       pt->row_words, pt->col_words};
   }
-  const int ns = n_splits(B, H, max_row);
+  const int ns = n_splits(B, H, D, block, max_row);
   if (workspace_floats < static_cast<int64_t>(B) * H * ns * (D + 2)) return SMAT_ERR_CAPACITY;
   p.q = static_cast<const __nv_bfloat16*>(q);
   p.k = static_cast<const __nv_bfloat16*>(k_cache);
@@ -352,7 +396,7 @@ int smat_decode(int dtype, const void* q, const int64_t* q_stride, const void* k
   p.nnzb = static_cast<int>(nnzb);
   p.bs = block;
   p.n_split = ns;
-  p.bps = entries_per_split(B, H, max_row);
+  p.sps = steps_per_split(B, H, D, block, max_row);
   p.scale_log2 = scale * 1.4426950408889634f;
   p.err = err_word;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
