@@ -6,8 +6,8 @@
 //
 //   partial  grid (B H, n_split), 128 threads.  The query's CSR row is a
 //            sequence of steps (STEP keys of one entry each); split s walks
-//            steps [s sps, (s + 1) sps), sps chosen so that the grid fills
-//            whole waves of resident CTAs.  A key is owned by
+//            steps [s sps, (s + 1) sps), the split count chosen for the
+//            most even work per SM.  A key is owned by
 //            a group of D / 8 lanes (16-byte vectors, a 256-byte row read by
 //            16 lanes at D = 128), each warp handling 4 x 32 / (D / 8) keys
 //            per step with all their loads issued first (values only for
@@ -80,12 +80,36 @@ __device__ __forceinline__ void merge_state(float& m, float& l, float* o, float 
 }
 
 template <int D>
-__global__ void __launch_bounds__(128) decode_partial_kernel(const DecodeParams p) {
-  constexpr int G = D / 8;        // lanes per key
-  constexpr int KPW = 32 / G;     // keys per warp and unrolled step
-  constexpr int U = 4;            // unrolled steps
-  __shared__ float red_m[4][KPW], red_l[4][KPW];
-  __shared__ float red_o[4][D];
+struct DecCfg {
+  static constexpr int G = D / 8;                // lanes per key
+  static constexpr int KPW = 32 / G;             // keys per warp and unrolled step
+  static constexpr int NW = 8;                   // compute warps
+  static constexpr int U = D == 64 ? 2 : 4;      // unrolled keys per lane group
+  static constexpr int STEP = NW * KPW * U;      // keys per step: 64
+  static constexpr int ROW = D * 2;              // bytes of one key row
+  static constexpr int STAGE = 2 * STEP * ROW;   // K rows, then V rows
+  static constexpr int NS = (96 * 1024) / STAGE; // ring stages (96 KB)
+  static constexpr int OFF_BAR = NS * STAGE;     // full[NS], empty[NS]
+  static constexpr int OFF_MISC = OFF_BAR + 2 * NS * 8;
+  static constexpr int SMEM_BYTES = OFF_MISC + 16;
+  static constexpr int THREADS = 32 * (NW + 1);  // compute warps + the producer warp
+  static constexpr int KPL = STEP / 32;          // keys per producer lane
+  static_assert(STEP == 64 && NS >= 2, "ring layout");
+  static_assert(SMEM_BYTES + 1024 + NW * (D + 2) * 4 <= 113 * 1024, "two CTAs per SM");
+};
+
+template <int D>
+__global__ void __launch_bounds__(DecCfg<D>::THREADS, 2)
+    decode_partial_kernel(const DecodeParams p) {
+  using C = DecCfg<D>;
+  constexpr int G = C::G, KPW = C::KPW, U = C::U, STEP = C::STEP, NW = C::NW;
+  extern __shared__ __align__(128) uint8_t smem[];
+  __shared__ float red_m[NW], red_l[NW];
+  __shared__ float red_o[NW][D];
+  const uint32_t sbase = smem_u32(smem);
+  auto full = [&](int i) { return sbase + C::OFF_BAR + 8u * i; };
+  auto empty = [&](int i) { return sbase + C::OFF_BAR + 8u * (C::NS + i); };
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + C::OFF_MISC);
   const int bh = blockIdx.x, split = blockIdx.y;
   const int b = bh / p.H, h = bh % p.H;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -93,10 +117,9 @@ __global__ void __launch_bounds__(128) decode_partial_kernel(const DecodeParams 
   float* out = p.part + (static_cast<int64_t>(bh) * p.n_split + split) * (D + 2);
 
   // The row's keys as one sequence of steps: step g covers entry e0 + g / spb,
-  // keys (g % spb) STEP + warp KPW U + u KPW + slot of it.  The loads of step
-  // k + 1 are issued before the arithmetic of step k (two register buffers),
-  // so every warp keeps loads in flight while it computes.
-  constexpr int STEP = 4 * KPW * U;             // keys per CTA step
+  // keys (g % spb) STEP .. + STEP - 1 of it.  The producer warp copies each
+  // step's K and V rows into a ring stage with bulk copies up to NS - 1
+  // steps ahead; compute warp w scores keys w KPW U + u KPW + slot of it.
   const int spb = (p.bs + STEP - 1) / STEP;     // steps per block
   const int t = __ldg(p.pos + b);
   int e0 = 0, s0 = 0, nsteps = 0;
@@ -113,131 +136,188 @@ __global__ void __launch_bounds__(128) decode_partial_kernel(const DecodeParams 
       nsteps = max(0, min((z - a) * spb - s0, p.sps));
     }
   }
-
-  float qv[8];
-  {
-    const V8 raw = *reinterpret_cast<const V8*>(p.q + b * p.q_sb + h * p.q_sh + part * 8);
-    unpack8(raw, qv);
-#pragma unroll
-    for (int i = 0; i < 8; ++i) qv[i] *= p.scale_log2;
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < C::NS; ++i) {
+      mbar_init(full(i), 1);
+      mbar_init(empty(i), NW);
+    }
+    fence_barrier_init();
+    *abort_flag = 0;
   }
+  __syncthreads();
+
+  // entry of step g: its first key, the keys in range, its kind (a bad entry
+  // is reported and read as empty)
+  auto entry = [&](int g, int& j0, int& jn, uint8_t& kd) {
+    const int e = e0 + g / spb;
+    const int kb = __ldg(p.indices + e);
+    kd = __ldg(p.kind + e);
+    const bool ok = kb >= 0 && kb < p.nblocks && kb * p.bs <= t;
+    if (!ok && lane == 0 && p.err) atomicOr(p.err, DEV_ERR_BAD_CSR);
+    j0 = ok ? kb * p.bs : 0;
+    jn = ok ? min(p.bs, p.T - j0) : 0;
+  };
   float m = -INFINITY, l = 0.f, o[8];
 #pragma unroll
   for (int i = 0; i < 8; ++i) o[i] = 0.f;
-  const __nv_bfloat16* kbase = p.k + b * p.k_sb + h * p.k_sh + part * 8;
-  const __nv_bfloat16* vbase = p.v + b * p.v_sb + h * p.v_sh + part * 8;
 
-  V8 kr[2][U], vr[2][U];
-  bool vis[2][U];
-  auto issue = [&](int k, int buf) {
-    const int g = s0 + k;
-    const int e = e0 + g / spb;
-    const int kb = __ldg(p.indices + e);
-    const uint8_t kd = __ldg(p.kind + e);
-    const bool ok = kb >= 0 && kb < p.nblocks && kb * p.bs <= t;
-    if (!ok && threadIdx.x == 0 && p.err) atomicOr(p.err, DEV_ERR_BAD_CSR);
-    const int j0 = ok ? kb * p.bs : 0;
-    const int jn = ok ? min(p.bs, p.T - j0) : 0;
-    const int base = (g % spb) * STEP + warp * KPW * U;
-#pragma unroll
-    for (int u = 0; u < U; ++u) {
-      const int jj = base + u * KPW + slot;
-      const bool in = jj < jn;
-      const int j = j0 + (in ? jj : 0);
-      bool vs = in;
-      if (kd == 1) {
-        vs = vs && j <= t;
-      } else if (kd == 2) {
-        if (p.md.row_bits) {
-          vs = vs && ((md_row_word(p.md, p.T, t, j & ~31) >> (j & 31)) & 1u);
+  if (warp == NW) {
+    // ------------------------------------------------------------ producer
+    const __nv_bfloat16* kb0 = p.k + b * p.k_sb + h * p.k_sh;
+    const __nv_bfloat16* vb0 = p.v + b * p.v_sb + h * p.v_sh;
+    const bool dense = p.k_st == D && p.v_st == D;   // a step's rows are one run
+    int issued = 0;
+    for (int k = 0; k < nsteps; ++k) {
+      const int st = k % C::NS;
+      bool ok = true;
+      if (lane == 0 && k >= C::NS)
+        ok = mbar_wait(empty(st), ((k / C::NS) - 1) & 1, abort_flag, p.err);
+      if (!__shfl_sync(0xffffffffu, ok, 0)) break;
+      const int g = s0 + k;
+      int j0, jn;
+      uint8_t kd;
+      entry(g, j0, jn, kd);
+      const int base = (g % spb) * STEP;
+      const int nv = max(0, min(jn - base, STEP));   // keys of the step in range
+      const uint32_t sk = sbase + st * C::STAGE, sv = sk + STEP * C::ROW;
+      if (lane == 0) mbar_expect_tx(full(st), 2u * nv * C::ROW);
+      __syncwarp();
+      if (nv > 0) {
+        const int64_t j = j0 + base;
+        if (dense) {
+          if (lane == 0) {
+            bulk_load(sk, kb0 + j * D, nv * C::ROW, full(st));
+            bulk_load(sv, vb0 + j * D, nv * C::ROW, full(st));
+          }
         } else {
-          vs = false;
-          if (part == 0 && p.err) atomicOr(p.err, DEV_ERR_BAD_CSR);
+#pragma unroll
+          for (int q = 0; q < C::KPL; ++q) {
+            const int kk = lane * C::KPL + q;
+            if (kk < nv) {
+              bulk_load(sk + kk * C::ROW, kb0 + (j + kk) * p.k_st, C::ROW, full(st));
+              bulk_load(sv + kk * C::ROW, vb0 + (j + kk) * p.v_st, C::ROW, full(st));
+            }
+          }
         }
       }
-      vis[buf][u] = vs;
-      kr[buf][u] = *reinterpret_cast<const V8*>(kbase + static_cast<int64_t>(j) * p.k_st);
-      if (vs) vr[buf][u] = *reinterpret_cast<const V8*>(vbase + static_cast<int64_t>(j) * p.v_st);
+      issued = k + 1;
     }
-  };
-  // A step's U keys are independent until the softmax update: their dot
-  // products and group reductions interleave, then one max, at most one
-  // rescale, and the U accumulations.
-  auto consume = [&](int buf) {
-    float sc[U];
+    // never exit with copies in flight
+    if (lane == 0 && *abort_flag)
+      for (int k = max(0, issued - C::NS); k < issued; ++k)
+        mbar_wait_drain(full(k % C::NS), (k / C::NS) & 1);
+  } else {
+    // ------------------------------------------------------------ compute
+    float qv[8];
+    {
+      const V8 raw = *reinterpret_cast<const V8*>(p.q + b * p.q_sb + h * p.q_sh + part * 8);
+      unpack8(raw, qv);
 #pragma unroll
-    for (int u = 0; u < U; ++u) {
-      float kv[8];
-      unpack8(kr[buf][u], kv);
-      float s0 = qv[0] * kv[0], s1 = qv[1] * kv[1];
+      for (int i = 0; i < 8; ++i) qv[i] *= p.scale_log2;
+    }
+    for (int k = 0; k < nsteps; ++k) {
+      const int st = k % C::NS;
+      const int g = s0 + k;
+      int j0, jn;
+      uint8_t kd;
+      entry(g, j0, jn, kd);
+      // visibility of this lane group's keys, before the wait
+      bool vis[U];
 #pragma unroll
-      for (int i = 2; i < 8; i += 2) {
-        s0 = fmaf(qv[i], kv[i], s0);
-        s1 = fmaf(qv[i + 1], kv[i + 1], s1);
+      for (int u = 0; u < U; ++u) {
+        const int jj = (g % spb) * STEP + warp * KPW * U + u * KPW + slot;
+        const int j = j0 + jj;
+        bool vs = jj < jn;
+        if (kd == 1) {
+          vs = vs && j <= t;
+        } else if (kd == 2) {
+          if (p.md.row_bits) {
+            vs = vs && ((md_row_word(p.md, p.T, t, j & ~31) >> (j & 31)) & 1u);
+          } else {
+            vs = false;
+            if (part == 0 && p.err) atomicOr(p.err, DEV_ERR_BAD_CSR);
+          }
+        }
+        vis[u] = vs;
       }
-      sc[u] = s0 + s1;
+      if (!__all_sync(0xffffffffu, mbar_wait(full(st), (k / C::NS) & 1, abort_flag, p.err)))
+        break;
+      const uint8_t* sk = smem + st * C::STAGE;
+      const uint8_t* sv = sk + STEP * C::ROW;
+      // the U keys are independent until the softmax update: dot products
+      // and group reductions interleave, then one max, at most one rescale,
+      // and the U accumulations (rows out of range were not copied: their
+      // scores are never used)
+      float sc[U];
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const int kk = warp * KPW * U + u * KPW + slot;
+        const V8 raw = *reinterpret_cast<const V8*>(sk + kk * C::ROW + part * 16);
+        float kv[8];
+        unpack8(raw, kv);
+        float a0 = qv[0] * kv[0], a1 = qv[1] * kv[1];
+#pragma unroll
+        for (int i = 2; i < 8; i += 2) {
+          a0 = fmaf(qv[i], kv[i], a0);
+          a1 = fmaf(qv[i + 1], kv[i + 1], a1);
+        }
+        sc[u] = a0 + a1;
+      }
+#pragma unroll
+      for (int off = G / 2; off > 0; off >>= 1)
+#pragma unroll
+        for (int u = 0; u < U; ++u) sc[u] += __shfl_xor_sync(0xffffffffu, sc[u], off);
+      float mx = m;
+#pragma unroll
+      for (int u = 0; u < U; ++u)
+        if (vis[u]) mx = fmaxf(mx, sc[u]);
+      if (mx > m) {
+        const float a = exp2f(m - mx);   // 0 when m is still -inf
+        l *= a;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) o[i] *= a;
+        m = mx;
+      }
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        if (!vis[u]) continue;
+        const int kk = warp * KPW * U + u * KPW + slot;
+        const V8 raw = *reinterpret_cast<const V8*>(sv + kk * C::ROW + part * 16);
+        float vv[8];
+        unpack8(raw, vv);
+        const float pr = exp2f(sc[u] - m);
+        l += pr;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) o[i] = fmaf(pr, vv[i], o[i]);
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(empty(st));
     }
+    // merge the KPW groups of the warp: lanes with the same part, xor over slot bits
 #pragma unroll
-    for (int off = G / 2; off > 0; off >>= 1)
+    for (int off = G; off < 32; off <<= 1) {
+      const float m2 = __shfl_xor_sync(0xffffffffu, m, off);
+      const float l2 = __shfl_xor_sync(0xffffffffu, l, off);
+      float o2[8];
 #pragma unroll
-      for (int u = 0; u < U; ++u) sc[u] += __shfl_xor_sync(0xffffffffu, sc[u], off);
-    float mx = m;
-#pragma unroll
-    for (int u = 0; u < U; ++u)
-      if (vis[buf][u]) mx = fmaxf(mx, sc[u]);
-    if (mx > m) {
-      const float a = exp2f(m - mx);   // 0 when m is still -inf
-      l *= a;
-#pragma unroll
-      for (int i = 0; i < 8; ++i) o[i] *= a;
-      m = mx;
+      for (int i = 0; i < 8; ++i) o2[i] = __shfl_xor_sync(0xffffffffu, o[i], off);
+      merge_state<8>(m, l, o, m2, l2, o2);
     }
+    if (slot == 0) {
 #pragma unroll
-    for (int u = 0; u < U; ++u) {
-      if (!vis[buf][u]) continue;
-      float vv[8];
-      unpack8(vr[buf][u], vv);
-      const float pr = exp2f(sc[u] - m);
-      l += pr;
-#pragma unroll
-      for (int i = 0; i < 8; ++i) o[i] = fmaf(pr, vv[i], o[i]);
-    }
-  };
-  // buffers are named by constants (a runtime index would move them to the stack)
-  if (nsteps > 0) issue(0, 0);
-  for (int k = 0; k < nsteps; k += 2) {
-    if (k + 1 < nsteps) issue(k + 1, 1);
-    consume(0);
-    if (k + 1 < nsteps) {
-      if (k + 2 < nsteps) issue(k + 2, 0);
-      consume(1);
-    }
-  }
-
-  // merge the KPW groups of the warp: lanes with the same part, xor over slot bits
-#pragma unroll
-  for (int off = G; off < 32; off <<= 1) {
-    const float m2 = __shfl_xor_sync(0xffffffffu, m, off);
-    const float l2 = __shfl_xor_sync(0xffffffffu, l, off);
-    float o2[8];
-#pragma unroll
-    for (int i = 0; i < 8; ++i) o2[i] = __shfl_xor_sync(0xffffffffu, o[i], off);
-    merge_state<8>(m, l, o, m2, l2, o2);
-  }
-  // merge the four warps
-  if (slot == 0) {
-#pragma unroll
-    for (int i = 0; i < 8; ++i) red_o[warp][part * 8 + i] = o[i];
-    if (part == 0) {
-      red_m[warp][0] = m;
-      red_l[warp][0] = l;
+      for (int i = 0; i < 8; ++i) red_o[warp][part * 8 + i] = o[i];
+      if (part == 0) {
+        red_m[warp] = m;
+        red_l[warp] = l;
+      }
     }
   }
   __syncthreads();
+  // merge the compute warps
   for (int d = threadIdx.x; d < D; d += blockDim.x) {
-    float M = red_m[0][0], L = red_l[0][0], O = red_o[0][d];
+    float M = red_m[0], L = red_l[0], O = red_o[0][d];
 #pragma unroll
-    for (int w = 1; w < 4; ++w) merge_state<1>(M, L, &O, red_m[w][0], red_l[w][0], &red_o[w][d]);
+    for (int w = 1; w < NW; ++w) merge_state<1>(M, L, &O, red_m[w], red_l[w], &red_o[w][d]);
     out[2 + d] = O;
     if (d == 0) {
       out[0] = M;
@@ -274,42 +354,41 @@ __global__ void __launch_bounds__(D) decode_combine_kernel(const DecodeParams p)
 
 int status() { return cudaGetLastError() == cudaSuccess ? SMAT_OK : SMAT_ERR_LAUNCH; }
 
-// CTAs resident at once: four per SM (128 threads at 128 registers)
-int64_t resident_ctas() {
+int sm_count() {
   int dev = 0, sms = 0;
   if (cudaGetDevice(&dev) != cudaSuccess ||
       cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms < 1)
     sms = 148;
-  return 4LL * sms;
+  return sms;
 }
-// Steps per split (a step is 32 keys at D = 128, 64 at D = 64): the grid is
-// sized to the most whole waves of resident CTAs (up to four) whose splits
-// keep at least 8 steps, so a split's set-up is amortised and the last wave
-// is not left mostly empty; then the split count is trimmed so that no split
-// is empty.
-int steps_per_split(int B, int H, int D, int bs, int max_row) {
-  const int64_t bh = static_cast<int64_t>(B) * H, slots = resident_ctas();
-  const int step = D == 64 ? 64 : 32;
-  const int64_t row_steps = std::max<int64_t>(1, static_cast<int64_t>(max_row) * ((bs + step - 1) / step));
-  int64_t best = row_steps;
-  for (int w = 1; w <= 4; ++w) {
-    const int64_t ns = std::max<int64_t>(1, w * slots / bh);
+constexpr int DEC_STEP = 64;       // keys per step (DecCfg<D>::STEP)
+constexpr int DEC_RESIDENT = 2;    // CTAs per SM (a 96 KB ring each)
+constexpr int DEC_MAX_SPLITS = 64;
+// Splits per row: the count whose busiest SM finishes first, with an SM's
+// time taken as the steps of the CTAs it runs plus a set-up of two steps per
+// round of resident CTAs.  (B H rows rarely divide evenly over the SMs.)
+int n_splits(int B, int H, int bs, int max_row) {
+  const int64_t bh = static_cast<int64_t>(B) * H, sms = sm_count();
+  const int64_t row_steps =
+      std::max<int64_t>(1, static_cast<int64_t>(max_row) * ((bs + DEC_STEP - 1) / DEC_STEP));
+  int best = 1;
+  int64_t best_cost = -1;
+  for (int64_t ns = 1; ns <= std::min<int64_t>(row_steps, DEC_MAX_SPLITS); ++ns) {
     const int64_t sps = (row_steps + ns - 1) / ns;
-    if (w == 1 || sps >= 8) best = sps;
+    const int64_t per_sm = (bh * ns + sms - 1) / sms;
+    const int64_t cost = per_sm * sps + 2 * ((per_sm + DEC_RESIDENT - 1) / DEC_RESIDENT);
+    if (best_cost < 0 || cost <= best_cost) {   // ties: more splits, more copies in flight
+      best_cost = cost;
+      best = static_cast<int>(ns);
+    }
   }
-  return static_cast<int>(best);
+  return best;
 }
-int n_splits(int B, int H, int D, int bs, int max_row) {
-  const int64_t step = D == 64 ? 64 : 32;
-  const int64_t row_steps = std::max<int64_t>(1, static_cast<int64_t>(max_row) * ((bs + step - 1) / step));
-  const int sps = steps_per_split(B, H, D, bs, max_row);
-  return static_cast<int>((row_steps + sps - 1) / sps);
-}
-// an upper bound of n_splits over block sizes (the workspace query has none):
-// the grid never exceeds four waves, and a row has at least one split
-int max_splits(int B, int H) {
-  const int64_t bh = static_cast<int64_t>(B) * H;
-  return static_cast<int>(std::max<int64_t>(1, 4 * resident_ctas() / bh));
+int steps_per_split(int B, int H, int bs, int max_row) {
+  const int64_t row_steps =
+      std::max<int64_t>(1, static_cast<int64_t>(max_row) * ((bs + DEC_STEP - 1) / DEC_STEP));
+  const int ns = n_splits(B, H, bs, max_row);
+  return static_cast<int>((row_steps + ns - 1) / ns);
 }
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
@@ -321,7 +400,7 @@ extern "C" {
 int smat_decode_workspace(int B, int H, int D, int max_row, int64_t* floats_out) {
   if (B < 1 || H < 1 || max_row < 0 || (D != 64 && D != 128)) return SMAT_ERR_BAD_SHAPE;
   if (!floats_out) return SMAT_ERR_NULL_POINTER;
-  *floats_out = static_cast<int64_t>(B) * H * max_splits(B, H) * (D + 2);
+  *floats_out = static_cast<int64_t>(B) * H * DEC_MAX_SPLITS * (D + 2);
   return SMAT_OK;
 }
 
@@ -367,7 +446,7 @@ int smat_decode(int dtype, const void* q, const int64_t* q_stride, const void* k
     p.md = MdPattern{pt->row_bits, pt->col_bits, pt->family, pt->n,        pt->n_P,
                      pt->B,        pt->N0,       pt->row_words, pt->col_words};
   }
-  const int ns = n_splits(B, H, D, block, max_row);
+  const int ns = n_splits(B, H, block, max_row);
   if (workspace_floats < static_cast<int64_t>(B) * H * ns * (D + 2)) return SMAT_ERR_CAPACITY;
   p.q = static_cast<const __nv_bfloat16*>(q);
   p.k = static_cast<const __nv_bfloat16*>(k_cache);
@@ -396,16 +475,23 @@ int smat_decode(int dtype, const void* q, const int64_t* q_stride, const void* k
   p.nnzb = static_cast<int>(nnzb);
   p.bs = block;
   p.n_split = ns;
-  p.sps = steps_per_split(B, H, D, block, max_row);
+  p.sps = steps_per_split(B, H, block, max_row);
   p.scale_log2 = scale * 1.4426950408889634f;
   p.err = err_word;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const dim3 grid(static_cast<unsigned>(B * H), static_cast<unsigned>(ns));
   if (D == 64) {
-    decode_partial_kernel<64><<<grid, 128, 0, s>>>(p);
+    if (cudaFuncSetAttribute(decode_partial_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             DecCfg<64>::SMEM_BYTES) != cudaSuccess)
+      return SMAT_ERR_LAUNCH;
+    decode_partial_kernel<64><<<grid, DecCfg<64>::THREADS, DecCfg<64>::SMEM_BYTES, s>>>(p);
     decode_combine_kernel<64><<<B * H, 64, 0, s>>>(p);
   } else {
-    decode_partial_kernel<128><<<grid, 128, 0, s>>>(p);
+    if (cudaFuncSetAttribute(decode_partial_kernel<128>,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             DecCfg<128>::SMEM_BYTES) != cudaSuccess)
+      return SMAT_ERR_LAUNCH;
+    decode_partial_kernel<128><<<grid, DecCfg<128>::THREADS, DecCfg<128>::SMEM_BYTES, s>>>(p);
     decode_combine_kernel<128><<<B * H, 128, 0, s>>>(p);
   }
   return status();

@@ -24,8 +24,11 @@ from smat_attention_b200.mask import build_block_mask, build_mask, materialise
 pytestmark = pytest.mark.gpu
 
 
-def _qkv(B, H, T, D, seed, device):
+def _qkv(B, H, T, D, seed, device, token_major=False):
     g = torch.Generator().manual_seed(seed)
+    if token_major:   # [B, T, H, D] memory seen as [B, H, T, D]: key rows H D apart
+        return [torch.randn(B, T, H, D, generator=g).to(device=device, dtype=torch.bfloat16)
+                .transpose(1, 2) for _ in range(3)]
     return [torch.randn(B, H, T, D, generator=g).to(device=device, dtype=torch.bfloat16)
             for _ in range(3)]
 
@@ -45,8 +48,8 @@ def _oracle_rows(q, k, v, rows_mask, pos, scale):
     return torch.stack(outs), torch.stack(lses)
 
 
-def _check(spec, rows_mask, B, H, T, D, positions, seed, device):
-    q, k, v = _qkv(B, H, T, D, seed, device)
+def _check(spec, rows_mask, B, H, T, D, positions, seed, device, token_major=False):
+    q, k, v = _qkv(B, H, T, D, seed, device, token_major)
     scale = 1.0 / math.sqrt(D)
     o_full, lse_full = fwd(q, k, v, spec, scale)
     pos = torch.tensor(positions, dtype=torch.int32, device=device)
@@ -89,6 +92,16 @@ def test_md_mask(cuda_device, T, d, chunk, D, positions):
     M = materialise(spec, np.uint8)
     _check(spec, lambda t: torch.from_numpy(M[t].astype(bool)), len(positions), 2, T, D,
            positions, seed=T + d, device=cuda_device)
+
+
+@pytest.mark.parametrize("D", [64, 128])
+def test_token_major_cache(cuda_device, D):
+    """Caches whose key rows are not contiguous (the copies go row by row)."""
+    T, lay = 2048, (128, 4, 4, 1)
+    spec = build_block_mask(T, *lay)
+    rows = OL.block_mask_rows(T, *lay)
+    dense = lambda t: rows(t, t + 1)[0].cpu()
+    _check(spec, dense, 2, 3, T, D, [2047, 1300], seed=D, device=cuda_device, token_major=True)
 
 
 def test_decoder_steps(cuda_device):
