@@ -838,7 +838,7 @@ def measure_decode(args, device, dist=None, rank=0, ws=1, K=None):
                      "traffic": None, "algorithmic_bytes": nbytes},
         "e2e": {"value": ws * B / (e2e_ms * 1e-3), "unit": "tokens/s", "ms_per_step": e2e_ms,
                 "h2d_bytes_per_step": B * H * D * 2, "d2h_bytes_per_step": B * H * D * 2},
-        "gpu_launches": 2 * K, "device_errors": dev_err, "clocks": clk,
+        "gpu_launches": K, "device_errors": dev_err, "clocks": clk,
     }
 
 

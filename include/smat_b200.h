@@ -404,8 +404,9 @@ SMAT_API int smat_bwd_pattern(int dtype,
  * element strides q_stride[2] / o_stride[2]; k_cache, v_cache: [B, H, T, D]
  * with (b, h, t) strides; pos: DEVICE int32 [B], each in [0, T) (else
  * SMAT_DEVERR_BAD_WORK and that row's output is 0).  bf16 only, D in {64,
- * 128}.  `workspace` holds the per-split partial results: at least
- * smat_decode_workspace(B, H, D, max_row) floats of device memory.
+ * 128}.  The splits of a row are combined inside the kernel (one thread-block
+ * cluster per row), so `workspace` is not used: it may be NULL, and
+ * smat_decode_workspace reports 0 floats (both kept for ABI compatibility).
  * The softmax counterpart of the reference's streaming decoder
  * (src/smat/attention.py:496-535, SmatDecoder.step). */
 SMAT_API int smat_decode_workspace(int B, int H, int D, int max_row, int64_t* floats_out);

@@ -4,19 +4,18 @@
 // One query row reads every visible key and value once, so decode is
 // HBM-bound (2 D bytes per key and value at bf16) and runs on CUDA cores:
 //
-//   partial  grid (B H, n_split), 128 threads.  The query's CSR row is a
-//            sequence of steps (STEP keys of one entry each); split s walks
-//            steps [s sps, (s + 1) sps), the split count chosen for the
-//            most even work per SM.  A key is owned by
-//            a group of D / 8 lanes (16-byte vectors, a 256-byte row read by
-//            16 lanes at D = 128), each warp handling 4 x 32 / (D / 8) keys
-//            per step with all their loads issued first (values only for
-//            visible keys); the dot product is reduced inside the group and each
-//            group keeps an online softmax (max, sum, D / 8 x 8 outputs).
-//            Groups and warps are merged at the end into one partial
-//            (m, l, o[D]) per split, in base-2 exponent units.
-//   combine  grid B H, D threads: rescales the partials to their common max
-//            and writes o (bf16) and the natural-log LSE.
+//   grid (B H, n_split), 288 threads, two CTAs per SM.  The query's CSR row
+//   is a sequence of steps (64 keys of one entry each); split s walks steps
+//   [s sps, (s + 1) sps), the split count chosen for the most even work per
+//   SM.  A producer warp copies each step's K and V rows into a shared-memory
+//   ring with bulk copies; eight compute warps score them: a key is owned by
+//   a group of D / 8 lanes (16-byte vectors), the dot product is reduced
+//   inside the group and each group keeps an online softmax (max, sum,
+//   8 outputs per lane).  Groups and warps are merged into one partial
+//   (m, l, o[D]) per split, in base-2 exponent units.  The splits of a row
+//   form one thread-block cluster: CTA rank 0 reads the others' partials from
+//   their shared memory, rescales them to the common max and writes o (bf16)
+//   and the natural-log LSE.
 //
 // Visibility of key j for query position t: FULL entries all keys, CAUSAL
 // entries j <= t, PATTERN entries the row word of pattern.cuh.
@@ -45,7 +44,6 @@ struct DecodeParams {
   const int32_t* indptr;
   const int32_t* indices;
   const uint8_t* kind;
-  float* part;               // [B H][n_split][D + 2]: m, l, o[D]
   int64_t q_sb, q_sh, k_sb, k_sh, k_st, v_sb, v_sh, v_st, o_sb, o_sh;
   int B, H, T, nblocks, nnzb, bs, n_split, sps;
   float scale_log2;
@@ -106,6 +104,7 @@ __global__ void __launch_bounds__(DecCfg<D>::THREADS, 2)
   extern __shared__ __align__(128) uint8_t smem[];
   __shared__ float red_m[NW], red_l[NW];
   __shared__ float red_o[NW][D];
+  __shared__ float fin[D + 2];   // this split's partial: m, l, o[D] (base-2 units)
   const uint32_t sbase = smem_u32(smem);
   auto full = [&](int i) { return sbase + C::OFF_BAR + 8u * i; };
   auto empty = [&](int i) { return sbase + C::OFF_BAR + 8u * (C::NS + i); };
@@ -114,7 +113,6 @@ __global__ void __launch_bounds__(DecCfg<D>::THREADS, 2)
   const int b = bh / p.H, h = bh % p.H;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int slot = lane / G, part = lane % G;
-  float* out = p.part + (static_cast<int64_t>(bh) * p.n_split + split) * (D + 2);
 
   // The row's keys as one sequence of steps: step g covers entry e0 + g / spb,
   // keys (g % spb) STEP .. + STEP - 1 of it.  The producer warp copies each
@@ -318,38 +316,35 @@ __global__ void __launch_bounds__(DecCfg<D>::THREADS, 2)
     float M = red_m[0], L = red_l[0], O = red_o[0][d];
 #pragma unroll
     for (int w = 1; w < NW; ++w) merge_state<1>(M, L, &O, red_m[w], red_l[w], &red_o[w][d]);
-    out[2 + d] = O;
+    fin[2 + d] = O;
     if (d == 0) {
-      out[0] = M;
-      out[1] = L;
+      fin[0] = M;
+      fin[1] = L;
     }
   }
-}
-
-template <int D>
-__global__ void __launch_bounds__(D) decode_combine_kernel(const DecodeParams p) {
-  const int bh = blockIdx.x, d = threadIdx.x;
-  const int b = bh / p.H, h = bh % p.H;
-  const float* in = p.part + static_cast<int64_t>(bh) * p.n_split * (D + 2);
-  // two passes with independent loads (the maxima, then the rescaled sums), so
-  // the loads of all splits are in flight together
-  float M = -INFINITY;
-#pragma unroll 8
-  for (int s = 0; s < p.n_split; ++s) M = fmaxf(M, in[s * (D + 2)]);
-  float L = 0.f, O = 0.f;
-  if (M != -INFINITY) {
-#pragma unroll 8
-    for (int s = 0; s < p.n_split; ++s) {
-      const float* ps = in + s * (D + 2);
-      const float w = exp2f(ps[0] - M);   // 0 for an empty split (m = -inf)
-      L = fmaf(ps[1], w, L);
-      O = fmaf(ps[2 + d], w, O);
+  // combine the row's splits: rank 0 reads every CTA's partial in place
+  cluster_sync();
+  if (cluster_ctarank() == 0) {
+    const uint32_t nr = gridDim.y;   // the cluster is the row's splits
+    const uint32_t fa = smem_u32(fin);
+    for (int d = threadIdx.x; d < D; d += blockDim.x) {
+      float M = -INFINITY;
+      for (uint32_t r = 0; r < nr; ++r) M = fmaxf(M, ld_cluster_f32(fa, r));
+      float L = 0.f, O = 0.f;
+      if (M != -INFINITY) {
+        for (uint32_t r = 0; r < nr; ++r) {
+          const float w = exp2f(ld_cluster_f32(fa, r) - M);   // 0 for an empty split
+          L = fmaf(ld_cluster_f32(fa + 4, r), w, L);
+          O = fmaf(ld_cluster_f32(fa + 4 * (2 + d), r), w, O);
+        }
+      }
+      const float res = L > 0.f ? O / L : 0.f;
+      p.o[b * p.o_sb + h * p.o_sh + d] = __float2bfloat16_rn(res);
+      if (d == 0 && p.lse)
+        p.lse[bh] = L > 0.f ? (M + log2f(L)) * 0.69314718055994531f : -INFINITY;
     }
   }
-  const float r = L > 0.f ? O / L : 0.f;
-  p.o[b * p.o_sb + h * p.o_sh + d] = __float2bfloat16_rn(r);
-  if (d == 0 && p.lse)
-    p.lse[bh] = L > 0.f ? (M + log2f(L)) * 0.69314718055994531f : -INFINITY;
+  cluster_sync();   // the partials stay in place until rank 0 has read them
 }
 
 int status() { return cudaGetLastError() == cudaSuccess ? SMAT_OK : SMAT_ERR_LAUNCH; }
@@ -363,7 +358,7 @@ int sm_count() {
 }
 constexpr int DEC_STEP = 64;       // keys per step (DecCfg<D>::STEP)
 constexpr int DEC_RESIDENT = 2;    // CTAs per SM (a 96 KB ring each)
-constexpr int DEC_MAX_SPLITS = 64;
+constexpr int DEC_MAX_SPLITS = 8;   // a row's splits are one (portable-size) cluster
 // Splits per row: the count whose busiest SM finishes first, with an SM's
 // time taken as the steps of the CTAs it runs plus a set-up of two steps per
 // round of resident CTAs.  (B H rows rarely divide evenly over the SMs.)
@@ -400,7 +395,7 @@ extern "C" {
 int smat_decode_workspace(int B, int H, int D, int max_row, int64_t* floats_out) {
   if (B < 1 || H < 1 || max_row < 0 || (D != 64 && D != 128)) return SMAT_ERR_BAD_SHAPE;
   if (!floats_out) return SMAT_ERR_NULL_POINTER;
-  *floats_out = static_cast<int64_t>(B) * H * DEC_MAX_SPLITS * (D + 2);
+  *floats_out = 0;   // the splits are combined in the kernel (kept for the ABI)
   return SMAT_OK;
 }
 
@@ -415,7 +410,9 @@ int smat_decode(int dtype, const void* q, const int64_t* q_stride, const void* k
   if (D != 64 && D != 128) return SMAT_ERR_UNSUPPORTED_D;
   if (B < 1 || H < 1 || T < 1 || block < 1 || nblocks != (T + block - 1) / block)
     return SMAT_ERR_BAD_SHAPE;
-  if (!q || !k_cache || !v_cache || !o || !pos || !indptr || !kind || !workspace ||
+  (void)workspace;   // unused: the splits are combined in the kernel
+  (void)workspace_floats;
+  if (!q || !k_cache || !v_cache || !o || !pos || !indptr || !kind ||
       !q_stride || !k_stride || !v_stride || !o_stride || (!indices && nnzb > 0))
     return SMAT_ERR_NULL_POINTER;
   if (nnzb < 0 || nnzb > 0x7FFFFFFF || max_row < 1) return SMAT_ERR_CSR_INVALID;
@@ -447,7 +444,6 @@ int smat_decode(int dtype, const void* q, const int64_t* q_stride, const void* k
                      pt->B,        pt->N0,       pt->row_words, pt->col_words};
   }
   const int ns = n_splits(B, H, block, max_row);
-  if (workspace_floats < static_cast<int64_t>(B) * H * ns * (D + 2)) return SMAT_ERR_CAPACITY;
   p.q = static_cast<const __nv_bfloat16*>(q);
   p.k = static_cast<const __nv_bfloat16*>(k_cache);
   p.v = static_cast<const __nv_bfloat16*>(v_cache);
@@ -457,7 +453,6 @@ int smat_decode(int dtype, const void* q, const int64_t* q_stride, const void* k
   p.indptr = indptr;
   p.indices = indices;
   p.kind = kind;
-  p.part = workspace;
   p.q_sb = q_stride[0];
   p.q_sh = q_stride[1];
   p.k_sb = k_stride[0];
@@ -479,20 +474,34 @@ int smat_decode(int dtype, const void* q, const int64_t* q_stride, const void* k
   p.scale_log2 = scale * 1.4426950408889634f;
   p.err = err_word;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  const dim3 grid(static_cast<unsigned>(B * H), static_cast<unsigned>(ns));
+  // one cluster per row: its ns splits (ns <= 8, the portable cluster size)
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(static_cast<unsigned>(B * H), static_cast<unsigned>(ns));
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 1;
+  attr[0].val.clusterDim.y = static_cast<unsigned>(ns);
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
   if (D == 64) {
     if (cudaFuncSetAttribute(decode_partial_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              DecCfg<64>::SMEM_BYTES) != cudaSuccess)
       return SMAT_ERR_LAUNCH;
-    decode_partial_kernel<64><<<grid, DecCfg<64>::THREADS, DecCfg<64>::SMEM_BYTES, s>>>(p);
-    decode_combine_kernel<64><<<B * H, 64, 0, s>>>(p);
+    cfg.blockDim = dim3(DecCfg<64>::THREADS);
+    cfg.dynamicSmemBytes = DecCfg<64>::SMEM_BYTES;
+    if (cudaLaunchKernelEx(&cfg, decode_partial_kernel<64>, p) != cudaSuccess)
+      return SMAT_ERR_LAUNCH;
   } else {
     if (cudaFuncSetAttribute(decode_partial_kernel<128>,
                              cudaFuncAttributeMaxDynamicSharedMemorySize,
                              DecCfg<128>::SMEM_BYTES) != cudaSuccess)
       return SMAT_ERR_LAUNCH;
-    decode_partial_kernel<128><<<grid, DecCfg<128>::THREADS, DecCfg<128>::SMEM_BYTES, s>>>(p);
-    decode_combine_kernel<128><<<B * H, 128, 0, s>>>(p);
+    cfg.blockDim = dim3(DecCfg<128>::THREADS);
+    cfg.dynamicSmemBytes = DecCfg<128>::SMEM_BYTES;
+    if (cudaLaunchKernelEx(&cfg, decode_partial_kernel<128>, p) != cudaSuccess)
+      return SMAT_ERR_LAUNCH;
   }
   return status();
 }
