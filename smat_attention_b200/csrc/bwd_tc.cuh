@@ -55,10 +55,16 @@ struct BwdParams {
   MdPattern md;            // tables of PATTERN tiles (null row_bits: the layout has none)
 };
 
-template <bool DKDV, int D>
+// CN_ chunk rows: 128, or 64 at D = 64 with 64-row blocks -- TMEM then needs
+// 256 columns and shared memory <= 113 KB, so two CTAs share an SM and one's
+// set-up, hand-off waits and epilogue overlap the other's chunks.
+template <bool DKDV, int D, int CN_ = 128>
 struct BwdCfg {
   static constexpr int BM = 128;     // tile rows
-  static constexpr int CN = 128;     // chunk rows (queries for dK/dV, keys for dQ)
+  static constexpr int CN = CN_;     // chunk rows (queries for dK/dV, keys for dQ)
+  static_assert(CN == 128 || (CN == 64 && D == 64), "chunk rows");
+  static constexpr int MIN_BLOCKS = CN == 64 ? 2 : 1;   // CTAs per SM
+  static constexpr int SMEM_CAP = (CN == 64 ? 113 : 227) * 1024;
   static constexpr int BOX = 64;     // TMA box rows of a chunk load
   static constexpr int ROW_BYTES = BM * D * 2;   // one resident operand
   static constexpr int CH_BYTES = CN * D * 2;    // one streamed operand chunk
@@ -67,7 +73,7 @@ struct BwdCfg {
   static constexpr int LD_BYTES = DKDV ? 2 * CN * 4 : 0;   // lse + delta per stage
   // as many stages as the shared memory holds (at most 8)
   static constexpr int FIXED = 2 * ROW_BYTES + 2048;  // + barriers, alignment
-  static constexpr int STAGES_FIT = (227 * 1024 - FIXED) / (2 * CH_BYTES + LD_BYTES);
+  static constexpr int STAGES_FIT = (SMEM_CAP - FIXED) / (2 * CH_BYTES + LD_BYTES);
   static constexpr int STAGES = STAGES_FIT > 8 ? 8 : STAGES_FIT;
   static constexpr int OFF_R0 = 0;                              // K (dK/dV) or Q (dQ)
   static constexpr int OFF_R1 = OFF_R0 + ROW_BYTES;             // V (dK/dV) or dO (dQ)
@@ -82,7 +88,7 @@ struct BwdCfg {
                        BAR_AD = BAR_DSR + 1, BAR_DRAIN = BAR_AD + 1, NBAR = BAR_DRAIN + 1;
   static constexpr int OFF_MISC = OFF_BAR + NBAR * 8;
   static constexpr int SMEM_BYTES = OFF_MISC + 16 + 1024;
-  static_assert(SMEM_BYTES <= 227 * 1024, "shared memory budget");
+  static_assert(SMEM_BYTES <= SMEM_CAP, "shared memory budget");
   static_assert(STAGES >= 2, "at least two stages");
   // the epilogue stages the output tile(s) in the chunk buffers of C0
   static_assert((DKDV ? 2 : 1) * ROW_BYTES <= STAGES * CH_BYTES, "epilogue staging");
@@ -90,11 +96,11 @@ struct BwdCfg {
   // memory: with N = 128 an MMA costs the same with A in shared memory or
   // in TMEM.
   static constexpr int COL_S = 0, COL_DP = CN, COL_ACC0 = 2 * CN, COL_ACC1 = COL_ACC0 + D;
-  static_assert(COL_ACC1 + D <= 512, "TMEM budget");
-  static constexpr int TMEM_COLS = 512;
-  // compute warps: 4 groups of 4; group g owns chunk columns [32 g, 32 g + 32)
-  static constexpr int NCW = 16, CW = CN / 4;
-  static_assert(CW == 32, "one 32-column block per warp");
+  static constexpr int TMEM_USED = COL_ACC0 + (DKDV ? 2 : 1) * D;
+  static constexpr int TMEM_COLS = TMEM_USED <= 256 ? 256 : 512;
+  static_assert(TMEM_USED <= TMEM_COLS && TMEM_COLS * MIN_BLOCKS <= 512, "TMEM budget");
+  // compute warps: CN / 32 groups of 4; group g owns chunk columns [32 g, 32 g + 32)
+  static constexpr int CW = 32, NCW = 4 * (CN / CW);
   static constexpr int PRODUCER_WARP = NCW, MMA_WARP = NCW + 1, THREADS = (NCW + 2) * 32;
   static constexpr uint32_t IDESC_SC = idesc_bf16(BM, CN, false, false);  // S, dP
   static constexpr uint32_t IDESC_ACC = idesc_bf16(BM, D, false, true);   // dV, dK, dQ
@@ -105,15 +111,15 @@ struct BwdCfg {
 // its first 16 columns
 __device__ __forceinline__ uint32_t a_col(int kk) { return 32u * (kk >> 1) + 8u * (kk & 1); }
 
-template <bool DKDV, int D>
-__global__ void __launch_bounds__(BwdCfg<DKDV, D>::THREADS, 1)
+template <bool DKDV, int D, int CN>
+__global__ void __launch_bounds__(BwdCfg<DKDV, D, CN>::THREADS, BwdCfg<DKDV, D, CN>::MIN_BLOCKS)
     smat_bwd_tc_kernel(const __grid_constant__ CUtensorMap tm_r0,
                        const __grid_constant__ CUtensorMap tm_r1,
                        const __grid_constant__ CUtensorMap tm_c0,
                        const __grid_constant__ CUtensorMap tm_c1,
                        const __grid_constant__ CUtensorMap tm_o0,
                        const __grid_constant__ CUtensorMap tm_o1, const BwdParams p) {
-  using C = BwdCfg<DKDV, D>;
+  using C = BwdCfg<DKDV, D, CN>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
@@ -196,7 +202,7 @@ __global__ void __launch_bounds__(BwdCfg<DKDV, D>::THREADS, 1)
       }
     }
     ChunkPair<2> it;
-    it.init(p.indptr, p.indices, p.kind, p.nblocks, p.nnzb, row0, sub, p.bs, p.err);
+    it.init(p.indptr, p.indices, p.kind, p.nblocks, p.nnzb, row0, sub, p.bs, p.err, C::CN);
     int issued = 0;
     uint32_t e[2];
     for (int j = 0; it.next(e, p.err); ++j) {
@@ -208,9 +214,9 @@ __global__ void __launch_bounds__(BwdCfg<DKDV, D>::THREADS, 1)
       __syncwarp();
       // first row of each 64-row half of the chunk; a missing half reads row
       // T onwards, which TMA fills with zeros
-      int prow[2];
+      int prow[2] = {p.T, p.T};
 #pragma unroll
-      for (int q = 0; q < 2; ++q) {
+      for (int q = 0; q < C::CN / 64; ++q) {
         const uint32_t eq = (p.bs == 64) ? e[q] : e[0];
         prow[q] = entry_present(eq) ? static_cast<int>(sched_block(eq)) * p.bs + (q * 64) % p.bs
                                     : p.T;
@@ -234,7 +240,7 @@ __global__ void __launch_bounds__(BwdCfg<DKDV, D>::THREADS, 1)
 #pragma unroll
         for (int pn = 0; pn < D / 64; ++pn)
 #pragma unroll
-          for (int q = 0; q < 2; ++q) {
+          for (int q = 0; q < C::CN / 64; ++q) {
             const uint32_t off = s * C::CH_BYTES + pn * C::PANEL_C + q * (C::BOX * 128);
             tma_load_4d(sbase + C::OFF_C0 + off, &tm_c0, bar(C::BAR_CF + s), pn * 64, prow[q], h,
                         b);
@@ -255,7 +261,7 @@ __global__ void __launch_bounds__(BwdCfg<DKDV, D>::THREADS, 1)
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
       ChunkPair<2> it;
-      it.init(p.indptr, p.indices, p.kind, p.nblocks, p.nnzb, row0, sub, p.bs, p.err);
+      it.init(p.indptr, p.indices, p.kind, p.nblocks, p.nnzb, row0, sub, p.bs, p.err, C::CN);
       // S (S^T) of chunk j:  R0 . C0_j^T;  dP (dP^T):  R1 . C1_j^T
       auto issue_sd = [&](int j, bool dp) {
         const int s = j % C::STAGES;
@@ -349,7 +355,7 @@ __global__ void __launch_bounds__(BwdCfg<DKDV, D>::THREADS, 1)
     bool alive = true;
     int n = 0;
     ChunkPair<2> it;
-    it.init(p.indptr, p.indices, p.kind, p.nblocks, p.nnzb, row0, sub, p.bs, p.err);
+    it.init(p.indptr, p.indices, p.kind, p.nblocks, p.nnzb, row0, sub, p.bs, p.err, C::CN);
     uint32_t e[2];
     for (int j = 0; alive && it.next(e, p.err); ++j) {
       n = j + 1;
@@ -480,7 +486,7 @@ __global__ void __launch_bounds__(BwdCfg<DKDV, D>::THREADS, 1)
       alive = false;
     if (alive) {
       tc_fence_after();
-      constexpr int EW = D / 4;   // accumulator columns per warp group
+      constexpr int EW = D / (C::NCW / 4);   // accumulator columns per warp group
 #pragma unroll
       for (int acc = 0; acc < (DKDV ? 2 : 1); ++acc) {
         const float mul = acc == 0 ? p.scale : 1.f;  // dK and dQ carry the softmax scale

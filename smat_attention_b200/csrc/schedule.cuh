@@ -112,18 +112,18 @@ struct MergeIter {
   }
 };
 
-// Chunks of 128 streamed rows: 128 / bs consecutive entries of the merged
-// list (one entry for bs = 128, two for bs = 64).  A missing second entry is
-// 0 (no row states).
+// Chunks of `cn` streamed rows (128, or 64 with bs = 64): cn / bs consecutive
+// entries of the merged list (one entry for bs = cn, two for bs = 64 and
+// cn = 128).  A missing second entry is 0 (no row states).
 template <int MAXROWS>
 struct ChunkPair {
   MergeIter<MAXROWS> it;
   int epc;
   __device__ __forceinline__ void init(const int32_t* indptr, const int32_t* indices,
                                        const uint8_t* kinds, int nblocks, int nnzb, int row0,
-                                       int nrows, int bs, int32_t* err) {
+                                       int nrows, int bs, int32_t* err, int cn = 128) {
     it.init(indptr, indices, kinds, nblocks, nnzb, row0, nrows, err);
-    epc = 128 / bs;
+    epc = cn / bs;
   }
   __device__ __forceinline__ bool next(uint32_t* e, int32_t* err) {
     if (!it.next(e[0], err)) return false;

@@ -290,13 +290,13 @@ struct DkdvSimt {
 };
 
 // ---------------------------------------------------------------- backward
-template <bool DKDV, int D>
-int bwd_tc(const TArg& r0, const TArg& r1, const TArg& c0, const TArg& c1, const float* lse,
-           const float* delta, const TArg& out0, const TArg* out1, int B, int H, int T,
-           const int32_t* indptr, const int32_t* indices, const uint8_t* kind, int nblocks,
-           int64_t nnzb, int block, float scale, const Work& work, const MdPattern& md,
-           int32_t* err, cudaStream_t s) {
-  using C = BwdCfg<DKDV, D>;
+template <bool DKDV, int D, int CN>
+int bwd_tc_cn(const TArg& r0, const TArg& r1, const TArg& c0, const TArg& c1, const float* lse,
+              const float* delta, const TArg& out0, const TArg* out1, int B, int H, int T,
+              const int32_t* indptr, const int32_t* indices, const uint8_t* kind, int nblocks,
+              int64_t nnzb, int block, float scale, const Work& work, const MdPattern& md,
+              int32_t* err, cudaStream_t s) {
+  using C = BwdCfg<DKDV, D, CN>;
   CUtensorMap m0, m1, mc0, mc1, mo0, mo1;
   int rc;
   if ((rc = make_map(&m0, r0, B, H, T, D, C::BM))) return rc;
@@ -334,13 +334,30 @@ int bwd_tc(const TArg& r0, const TArg& r1, const TArg& c0, const TArg& c1, const
   p.scale_log2 = scale * 1.4426950408889634f;
   p.err = err;
   p.md = md;
-  auto kern = smat_bwd_tc_kernel<DKDV, D>;
+  auto kern = smat_bwd_tc_kernel<DKDV, D, CN>;
   if ((rc = set_smem(kern, C::SMEM_BYTES))) return rc;
   const int64_t grid = static_cast<int64_t>(work.items ? work.n : p.n_tiles) * B * H;
   if (grid == 0) return SMAT_OK;
   kern<<<static_cast<unsigned>(grid), C::THREADS, C::SMEM_BYTES, s>>>(m0, m1, mc0, mc1, mo0, mo1,
                                                                        p);
   return launch_status();
+}
+// D = 64 with 64-row blocks: 64-row chunks, two CTAs per SM; otherwise
+// 128-row chunks.  The choice depends on (D, block) only, so launches with
+// and without a work list chunk alike.
+template <bool DKDV, int D>
+int bwd_tc(const TArg& r0, const TArg& r1, const TArg& c0, const TArg& c1, const float* lse,
+           const float* delta, const TArg& out0, const TArg* out1, int B, int H, int T,
+           const int32_t* indptr, const int32_t* indices, const uint8_t* kind, int nblocks,
+           int64_t nnzb, int block, float scale, const Work& work, const MdPattern& md,
+           int32_t* err, cudaStream_t s) {
+  if constexpr (D == 64) {
+    if (block == 64)
+      return bwd_tc_cn<DKDV, 64, 64>(r0, r1, c0, c1, lse, delta, out0, out1, B, H, T, indptr,
+                                     indices, kind, nblocks, nnzb, block, scale, work, md, err, s);
+  }
+  return bwd_tc_cn<DKDV, D, 128>(r0, r1, c0, c1, lse, delta, out0, out1, B, H, T, indptr, indices,
+                                 kind, nblocks, nnzb, block, scale, work, md, err, s);
 }
 
 }  // namespace
