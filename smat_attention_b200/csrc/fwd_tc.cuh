@@ -57,15 +57,20 @@ struct FwdParams {
 };
 
 // NT_ query tiles per CTA: 2 (one CTA per SM; its two softmax warpgroups
-// alternate on the tensor core) or 1 (D = 64 only: two CTAs per SM alternate,
-// and one CTA's set-up and epilogue overlap the other's chunks).
-template <int D, int NT_>
+// alternate on the tensor core) or 1 (D = 64 only: several CTAs per SM
+// alternate, and one CTA's set-up and epilogue overlap the others' chunks).
+// BN_ keys per chunk: 128, or 64 (D = 64 with 64-row blocks, one tile per
+// CTA): a tile then needs 128 TMEM columns and three CTAs share an SM.
+template <int D, int NT_, int BN_ = 128>
 struct FwdCfg {
-  static constexpr int BM = 128, NT = NT_, BN = 128, BOX = 64;
+  static constexpr int BM = 128, NT = NT_, BN = BN_, BOX = 64;
   static_assert(NT == 2 || (NT == 1 && D == 64), "tiles per CTA");
-  static constexpr int MIN_BLOCKS = 3 - NT;   // CTAs per SM
-  // per-CTA shared memory: 227 KB alone, 113 KB with two CTAs per SM
-  static constexpr int SMEM_CAP = (NT == 2 ? 227 : 113) * 1024;
+  static_assert(BN == 128 || (BN == 64 && D == 64 && NT == 1), "keys per chunk");
+  static constexpr int NH = BN / 64, NQ = BN / 32;   // 64-key halves, 32-key quarters
+  static constexpr int MIN_BLOCKS = BN == 64 ? 3 : 3 - NT;   // CTAs per SM
+  // per-CTA shared memory: the SM's 228 KB shared by MIN_BLOCKS CTAs (1 KB
+  // reserved each)
+  static constexpr int SMEM_CAP = (MIN_BLOCKS == 1 ? 227 : (MIN_BLOCKS == 2 ? 113 : 75)) * 1024;
   static constexpr int Q_BYTES = BM * D * 2;
   static constexpr int KV_BYTES = BN * D * 2;
   static constexpr int PANEL_Q = BM * 128, PANEL_KV = BN * 128;  // 64-column SW128 panels
@@ -89,15 +94,17 @@ struct FwdCfg {
   static constexpr int SMEM_BYTES = OFF_MISC + 16 + 1024;  // + alignment slack
   static_assert(SMEM_BYTES <= SMEM_CAP, "shared memory budget");
   static_assert(KS >= 2 && VS >= 2, "at least two slots per ring");
-  static constexpr int TILE_COLS = 256, COL_O = 128, TMEM_COLS = NT * TILE_COLS;
-  static_assert(COL_O + D <= TILE_COLS, "TMEM budget");
+  static constexpr int TILE_COLS = BN + D <= 128 ? 128 : 256, COL_O = BN;
+  static constexpr int TMEM_COLS = NT * TILE_COLS;
+  static_assert(COL_O + D <= TILE_COLS && TMEM_COLS * MIN_BLOCKS <= 512, "TMEM budget");
   // warpgroups 0 (and 1) softmax, the last warpgroup the producer and MMA
   // warps (and two idle ones, so that every warpgroup is whole for the
   // register split)
   static constexpr int PRODUCER_WARP = 4 * NT, MMA_WARP = 4 * NT + 1;
   static constexpr int THREADS = 128 * (NT + 1);
   static constexpr int REGS_LAUNCH = (65536 / (THREADS * MIN_BLOCKS)) & ~7;   // 168 / 128
-  static constexpr int REGS_SOFTMAX = NT == 2 ? 192 : 176, REGS_OTHER = NT == 2 ? 112 : 80;
+  static constexpr int REGS_SOFTMAX = NT == 2 ? 192 : (MIN_BLOCKS == 2 ? 176 : 112);
+  static constexpr int REGS_OTHER = NT == 2 ? 112 : (MIN_BLOCKS == 2 ? 80 : 48);
   static_assert(128 * (NT * REGS_SOFTMAX + REGS_OTHER) <= THREADS * REGS_LAUNCH,
                 "register split exceeds the launch allocation");
   static constexpr uint32_t IDESC_S = idesc_bf16(BM, BN, false, false);
@@ -108,13 +115,13 @@ struct FwdCfg {
 // of that half's S columns
 __device__ __forceinline__ uint32_t p_col(int kk) { return 64u * (kk >> 2) + 8u * (kk & 3); }
 
-template <int D, int NT>
-__global__ void __launch_bounds__(FwdCfg<D, NT>::THREADS, FwdCfg<D, NT>::MIN_BLOCKS)
+template <int D, int NT, int BN>
+__global__ void __launch_bounds__(FwdCfg<D, NT, BN>::THREADS, FwdCfg<D, NT, BN>::MIN_BLOCKS)
     smat_fwd_tc_kernel(const __grid_constant__ CUtensorMap tm_q,
                        const __grid_constant__ CUtensorMap tm_k,
                        const __grid_constant__ CUtensorMap tm_v,
                        const __grid_constant__ CUtensorMap tm_o, const FwdParams p) {
-  using C = FwdCfg<D, NT>;
+  using C = FwdCfg<D, NT, BN>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
@@ -219,8 +226,9 @@ __global__ void __launch_bounds__(FwdCfg<D, NT>::THREADS, FwdCfg<D, NT>::MIN_BLO
               tma_load_4d(sbase + C::OFF_Q + x * C::Q_BYTES + pn * C::PANEL_Q, &tm_q,
                           bar(C::BAR_Q), pn * 64, (tile0 + x) * C::BM, h, b);
         }
-        ChunkPair<4> it;
-        it.init(p.indptr, p.indices, p.kind, p.nblocks, p.nnzb, row0, ntile * sub, p.bs, p.err);
+        ChunkPair<2 * NT> it;
+        it.init(p.indptr, p.indices, p.kind, p.nblocks, p.nnzb, row0, ntile * sub, p.bs, p.err,
+                C::BN);
         int issued = 0;
         uint32_t e[2];
         for (int j = 0; it.next(e, p.err); ++j) {
@@ -228,9 +236,9 @@ __global__ void __launch_bounds__(FwdCfg<D, NT>::THREADS, FwdCfg<D, NT>::MIN_BLO
           if (j >= NS && !mbar_wait(bar(empty + s), ((j / NS) - 1) & 1, abort_flag, p.err)) break;
           // first key of each 64-key half; a missing half reads row T onwards,
           // which TMA fills with zeros
-          int krow[2];
+          int krow[2] = {p.T, p.T};
   #pragma unroll
-          for (int q = 0; q < 2; ++q) {
+          for (int q = 0; q < C::NH; ++q) {
             const uint32_t eq = (p.bs == 64) ? e[q] : e[0];
             krow[q] = entry_present(eq) ? static_cast<int>(sched_block(eq)) * p.bs + (q * 64) % p.bs
                                         : p.T;
@@ -239,7 +247,7 @@ __global__ void __launch_bounds__(FwdCfg<D, NT>::THREADS, FwdCfg<D, NT>::MIN_BLO
   #pragma unroll
           for (int pn = 0; pn < D / 64; ++pn)
   #pragma unroll
-            for (int q = 0; q < 2; ++q)
+            for (int q = 0; q < C::NH; ++q)
               tma_load_4d(ring + s * C::KV_BYTES + pn * C::PANEL_KV + q * (C::BOX * 128), tm,
                           bar(full + s), pn * 64, krow[q], h, b);
           issued = j + 1;
@@ -253,8 +261,9 @@ __global__ void __launch_bounds__(FwdCfg<D, NT>::THREADS, FwdCfg<D, NT>::MIN_BLO
     } else if (warp == C::MMA_WARP) {
       // ------------------------------------------------------------ MMA issuer
       if (lane == 0) {
-        ChunkPair<4> it;
-        it.init(p.indptr, p.indices, p.kind, p.nblocks, p.nnzb, row0, ntile * sub, p.bs, p.err);
+        ChunkPair<2 * NT> it;
+        it.init(p.indptr, p.indices, p.kind, p.nblocks, p.nnzb, row0, ntile * sub, p.bs, p.err,
+                C::BN);
         int cp[C::NT] = {};   // PVs issued per tile
         // S_x of chunk j (K slot j % KS)
         auto issue_s = [&](int j, int x) {
@@ -359,16 +368,17 @@ __global__ void __launch_bounds__(FwdCfg<D, NT>::THREADS, FwdCfg<D, NT>::MIN_BLO
     float m = -INFINITY, l = 0.f;
     int cnt = 0;
     bool alive = true;
-    ChunkPair<4> it;
-    it.init(p.indptr, p.indices, p.kind, p.nblocks, p.nnzb, row0, ntile * sub, p.bs, p.err);
+    ChunkPair<2 * NT> it;
+    it.init(p.indptr, p.indices, p.kind, p.nblocks, p.nnzb, row0, ntile * sub, p.bs, p.err,
+                C::BN);
     uint32_t e[2];
     while (alive && it.next(e, p.err)) {
       if (!active(e, x)) continue;
       // per 64-key half: state of this row (warp-uniform) and first key
-      uint32_t st[2];
-      int k0[2];
+      uint32_t st[2] = {ST_ABSENT, ST_ABSENT};
+      int k0[2] = {0, 0};
 #pragma unroll
-      for (int hf = 0; hf < 2; ++hf) {
+      for (int hf = 0; hf < C::NH; ++hf) {
         const uint32_t eh = (p.bs == 64) ? e[hf] : e[0];
         st[hf] = entry_present(eh) ? sched_state(eh, srow) : ST_ABSENT;
         k0[hf] = static_cast<int>(sched_block(eh)) * p.bs + (hf * 64) % p.bs;
@@ -384,7 +394,9 @@ __global__ void __launch_bounds__(FwdCfg<D, NT>::THREADS, FwdCfg<D, NT>::MIN_BLO
         if (sq == ST_PATTERN && p.err) atomicOr(p.err, DEV_ERR_BAD_CSR);
         return 0u;
       };
-      const uint32_t mw0 = qword(0), mw1 = qword(1), mw2 = qword(2), mw3 = qword(3);
+      uint32_t mw[C::NQ];
+#pragma unroll
+      for (int qq = 0; qq < C::NQ; ++qq) mw[qq] = qword(qq);
       if (!__all_sync(0xffffffffu,
                       mbar_wait(bar(C::BAR_SF + x), cnt & 1, abort_flag, p.err))) {
         alive = false;
@@ -392,24 +404,27 @@ __global__ void __launch_bounds__(FwdCfg<D, NT>::THREADS, FwdCfg<D, NT>::MIN_BLO
       }
       tc_fence_after();
       // the whole row of scores in one TMEM read
-      float s[128];
-      tmem_ld128(lane_base, s);
+      float s[C::BN];
+      if constexpr (C::BN == 128)
+        tmem_ld128(lane_base, s);
+      else
+        tmem_ld32x2(lane_base, lane_base + 32, s, s + 32);
       // quarter qq (32 keys, TMEM columns 32 qq ..): mask of this row
 #pragma unroll
-      for (int qq = 0; qq < 4; ++qq) {
+      for (int qq = 0; qq < C::NQ; ++qq) {
         const uint32_t sq = (qq >> 1) ? st[1] : st[0];
         if (sq != ST_FULL) {   // uniform per warp: its 32 rows share one CSR row
-          const uint32_t w = qq == 0 ? mw0 : (qq == 1 ? mw1 : (qq == 2 ? mw2 : mw3));
+          const uint32_t w = mw[qq];
 #pragma unroll
           for (int i = 0; i < 32; ++i)
             if (!((w >> i) & 1u)) s[32 * qq + i] = -INFINITY;
         }
       }
-      float mx[8];   // three-input max: 64 instructions per 128 scores
+      float mx[8];   // three-input max: BN / 2 instructions per BN scores
 #pragma unroll
       for (int a = 0; a < 8; ++a) mx[a] = s[a];
 #pragma unroll
-      for (int i = 8; i < 128; i += 2) mx[(i >> 1) & 7] = fmax3(mx[(i >> 1) & 7], s[i], s[i + 1]);
+      for (int i = 8; i < C::BN; i += 2) mx[(i >> 1) & 7] = fmax3(mx[(i >> 1) & 7], s[i], s[i + 1]);
       const float m_new = fmaxf(
           m, fmax3(fmax3(mx[0], mx[1], mx[2]), fmax3(mx[3], mx[4], mx[5]), fmaxf(mx[6], mx[7])) *
                  p.scale_log2);
@@ -428,7 +443,7 @@ __global__ void __launch_bounds__(FwdCfg<D, NT>::THREADS, FwdCfg<D, NT>::MIN_BLO
       // P of quarter qq packed into 16 columns at the start of its half's S
       // columns (64 h + 16 (qq % 2))
 #pragma unroll
-      for (int qq = 0; qq < 4; ++qq) {
+      for (int qq = 0; qq < C::NQ; ++qq) {
         uint32_t pw[16];
 #pragma unroll
         for (int i = 0; i < 16; ++i) {

@@ -173,12 +173,12 @@ int launch_status() {
 }
 
 // ---------------------------------------------------------------- forward
-template <int D, int NT>
+template <int D, int NT, int BN = 128>
 int fwd_tc(const TArg& q, const TArg& k, const TArg& v, const TArg& o, float* lse, int B, int H,
            int T, const int32_t* indptr, const int32_t* indices, const uint8_t* kind,
            int nblocks, int64_t nnzb, int block, float scale, const Work& work,
            const MdPattern& md, int32_t* err, cudaStream_t s) {
-  using C = FwdCfg<D, NT>;
+  using C = FwdCfg<D, NT, BN>;
   CUtensorMap mq, mk, mv, mo;
   int rc;
   if ((rc = make_map(&mq, q, B, H, T, D, C::BM))) return rc;
@@ -206,7 +206,7 @@ int fwd_tc(const TArg& q, const TArg& k, const TArg& v, const TArg& o, float* ls
   p.scale_log2 = scale * 1.4426950408889634f;
   p.err = err;
   p.md = md;
-  auto kern = smat_fwd_tc_kernel<D, NT>;
+  auto kern = smat_fwd_tc_kernel<D, NT, BN>;
   if ((rc = set_smem(kern, C::SMEM_BYTES))) return rc;
   const int64_t grid =
       static_cast<int64_t>(work.items ? work.n * (3 - NT) : (p.n_tiles + NT - 1) / NT) * B * H;
@@ -604,8 +604,12 @@ int fwd_impl(int dtype, const void* q, const int64_t* q_stride, const void* k,
   if (!std::isfinite(scale) || scale <= 0.f) return SMAT_ERR_BAD_SHAPE;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (dtype == SMAT_DTYPE_BF16) {
-    // D = 64: one tile per CTA, two CTAs per SM (with or without a work list,
-    // so that both launches group a tile's keys into the same chunks)
+    // D = 64: one tile per CTA; 64-key chunks and three CTAs per SM with
+    // 64-row blocks, else 128-key chunks and two (with or without a work
+    // list, so that both launches group a tile's keys into the same chunks)
+    if (D == 64 && block == 64)
+      return fwd_tc<64, 1, 64>(tq, tk, tv, to, lse, B, H, T, indptr, indices, kind, nblocks,
+                               nnzb, block, scale, work, md, err_word, s);
     if (D == 64)
       return fwd_tc<64, 1>(tq, tk, tv, to, lse, B, H, T, indptr, indices, kind, nblocks, nnzb,
                            block, scale, work, md, err_word, s);
