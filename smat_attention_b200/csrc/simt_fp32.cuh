@@ -277,7 +277,11 @@ __global__ void __launch_bounds__(128) smat_dkdv_simt_kernel(const SimtParams p)
 // delta[bh, t] = sum_d dO[b,h,t,d] * O[b,h,t,d] for t in [row_lo, row_lo + n_rows);
 // one warp per 32 / LPR rows, LPR lanes per row each reading 16-byte vectors;
 // rows = B * H * n_rows.
-template <typename T, int D>
+// delta[row] = sum_d O[row, d] dO[row, d] over rows (b, h, row_lo + t),
+// t < n_rows; LPR lanes per row, one 16-byte vector of O and dO each.  IDX is
+// the index type: 32-bit when rows * LPR fits (the divisions that locate a
+// row are then 32-bit), else 64-bit.
+template <typename T, int D, typename IDX>
 __global__ void __launch_bounds__(256) smat_bwd_pre_kernel(const T* __restrict__ o,
                                                            const T* __restrict__ dout,
                                                            float* __restrict__ delta,
@@ -289,14 +293,16 @@ __global__ void __launch_bounds__(256) smat_bwd_pre_kernel(const T* __restrict__
   constexpr int VEC = 16 / sizeof(T);
   constexpr int LPR = D / VEC;  // lanes per row
   static_assert(LPR <= 32 && 32 % LPR == 0, "unsupported D");
-  const int64_t gt = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-  const int64_t row = gt / LPR;
+  const IDX gt = static_cast<IDX>(blockIdx.x) * blockDim.x + threadIdx.x;
+  const IDX row = gt / LPR;
   const int part = static_cast<int>(gt % LPR);
+  const IDX nr = static_cast<IDX>(n_rows);
+  const int t = row_lo + static_cast<int>(row % nr);
+  const IDX bh = row / nr;
+  const bool in = static_cast<int64_t>(row) < rows;
   float acc = 0.f;
-  if (row < rows) {
-    const int t = row_lo + static_cast<int>(row % n_rows);
-    const int64_t bh = row / n_rows;
-    const int b = static_cast<int>(bh / H), h = static_cast<int>(bh % H);
+  if (in) {
+    const int b = static_cast<int>(bh / static_cast<IDX>(H)), h = static_cast<int>(bh % static_cast<IDX>(H));
     const T* op = o + b * o_sb + h * o_sh + t * o_st + part * VEC;
     const T* dp = dout + b * d_sb + h * d_sh + t * d_st + part * VEC;
     const uint4 ov = *reinterpret_cast<const uint4*>(op);
@@ -308,7 +314,7 @@ __global__ void __launch_bounds__(256) smat_bwd_pre_kernel(const T* __restrict__
   }
 #pragma unroll
   for (int off = 1; off < LPR; off <<= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
-  if (row < rows && part == 0) delta[(row / n_rows) * T_ + row_lo + row % n_rows] = acc;
+  if (in && part == 0) delta[static_cast<int64_t>(bh) * T_ + t] = acc;
 }
 
 }  // namespace smat

@@ -655,9 +655,16 @@ int pre_impl(int dtype, const void* o, const int64_t* o_stride, const void* dout
   const int64_t threads = rows * lpr;
   const unsigned grid = static_cast<unsigned>((threads + 255) / 256);
 #define SMAT_PRE(TY, DD)                                                                        \
-  smat_bwd_pre_kernel<TY, DD><<<grid, 256, 0, s>>>(                                            \
-      static_cast<const TY*>(o), static_cast<const TY*>(dout), delta, to.sb, to.sh, to.st, td.sb, \
-      td.sh, td.st, H, T, row_lo, n_rows, rows)
+  do {                                                                                          \
+    if (threads < (int64_t{1} << 31))                                                           \
+      smat_bwd_pre_kernel<TY, DD, uint32_t><<<grid, 256, 0, s>>>(                               \
+          static_cast<const TY*>(o), static_cast<const TY*>(dout), delta, to.sb, to.sh, to.st,  \
+          td.sb, td.sh, td.st, H, T, row_lo, n_rows, rows);                                     \
+    else                                                                                        \
+      smat_bwd_pre_kernel<TY, DD, int64_t><<<grid, 256, 0, s>>>(                                \
+          static_cast<const TY*>(o), static_cast<const TY*>(dout), delta, to.sb, to.sh, to.st,  \
+          td.sb, td.sh, td.st, H, T, row_lo, n_rows, rows);                                     \
+  } while (0)
   if (dtype == SMAT_DTYPE_BF16) {
     if (D == 64) SMAT_PRE(__nv_bfloat16, 64);
     else SMAT_PRE(__nv_bfloat16, 128);
