@@ -49,6 +49,7 @@ struct BwdParams {
   int64_t o0_sb, o0_sh, o0_st, o1_sb, o1_sh, o1_st;
   int B, H, T, nblocks, nnzb, bs, n_tiles;
   const int32_t* work;     // optional work list (one tile per CTA and (b, h)); null = all tiles
+  int head_group;          // without a work list: (b, h) per tile-interleaved group (>= 1)
   float scale;             // softmax scale
   float scale_log2;        // softmax scale * log2(e)
   int32_t* err;
@@ -143,12 +144,18 @@ __global__ void __launch_bounds__(BwdCfg<DKDV, D, CN>::THREADS, BwdCfg<DKDV, D, 
       return;
     }
   } else {
-    // all tiles of one (b, h) back to back, so the CTAs resident at a time
-    // share that head's streamed chunks in L2; heaviest first within a head
-    // (dQ: the latest query tiles; dK/dV: the earliest key tiles, since sinks
-    // and summaries are read by every later query)
-    bh = lin / p.n_tiles;
-    const int t = lin % p.n_tiles;
+    // (b, h) in groups of head_group: within a group the tiles run one tile
+    // index across the group's heads at a time (heaviest first: dQ the latest
+    // query tiles, dK/dV the earliest key tiles, since sinks and summaries are
+    // read by every later query), so a long tile of one head overlaps the
+    // tiles of the others; groups run one after another, so the resident
+    // CTAs share a few heads' streamed chunks in L2
+    const int G = p.head_group;
+    const int grp = lin / (G * p.n_tiles);
+    const int g0 = grp * G, gs = min(G, BH - g0);
+    const int r = lin - grp * G * p.n_tiles;
+    const int t = r / gs;
+    bh = g0 + r % gs;
     tile = DKDV ? t : p.n_tiles - 1 - t;
   }
   const int b = bh / p.H, h = bh % p.H;
