@@ -134,7 +134,7 @@ __global__ void __launch_bounds__(FwdCfg<D, NT, BN>::THREADS, FwdCfg<D, NT, BN>:
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int BH = p.B * p.H;
   const int lin = blockIdx.x;
-  const int bh = lin % BH;
+  int bh_sel = lin % BH;
   int tile0, ntile;
   if (p.work) {
     // caller-chosen tiles (a shard of the queries), in the caller's order.
@@ -156,10 +156,19 @@ __global__ void __launch_bounds__(FwdCfg<D, NT, BN>::THREADS, FwdCfg<D, NT, BN>:
       ntile = 1;
     }
   } else {
-    // heaviest (latest) tiles first
-    tile0 = NT * ((p.n_tiles + NT - 1) / NT - 1 - lin / BH);
+    // heaviest (latest) tiles first, one tile index across a group of 16
+    // (b, h) at a time (across all of them: c3 forward 2.32-2.35 ms against
+    // 2.28 -- the resident CTAs then span more heads' K / V than L2 holds)
+    const int np = (p.n_tiles + NT - 1) / NT;
+    constexpr int G = 16;
+    const int grp = lin / (G * np);
+    const int g0 = grp * G, gs = min(G, BH - g0);
+    const int rr = lin - grp * G * np;
+    bh_sel = g0 + rr % gs;
+    tile0 = NT * (np - 1 - rr / gs);
     ntile = min(NT, p.n_tiles - tile0);
   }
+  const int bh = bh_sel;
   const int b = bh / p.H, h = bh % p.H;
   const int sub = C::BM / p.bs;   // CSR rows per tile: 1 (bs 128) or 2 (bs 64)
   const int row0 = tile0 * sub;
