@@ -274,9 +274,6 @@ __global__ void __launch_bounds__(128) smat_dkdv_simt_kernel(const SimtParams p)
   }
 }
 
-// delta[bh, t] = sum_d dO[b,h,t,d] * O[b,h,t,d] for t in [row_lo, row_lo + n_rows);
-// one warp per 32 / LPR rows, LPR lanes per row each reading 16-byte vectors;
-// rows = B * H * n_rows.
 // delta[row] = sum_d O[row, d] dO[row, d] over rows (b, h, row_lo + t),
 // t < n_rows; LPR lanes per row, one 16-byte vector of O and dO each.  IDX is
 // the index type: 32-bit when rows * LPR fits (the divisions that locate a
