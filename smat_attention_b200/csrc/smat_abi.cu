@@ -255,36 +255,36 @@ int dispatch_simt_d(int D, SimtParams& p, int T, int n_work, int BH, cudaStream_
 template <int D>
 struct FwdSimt {
   static int run(SimtParams& p, int T, int n_work, int BH, cudaStream_t s) {
-    constexpr int RPC = 128 / (D / 32);
+    constexpr int RPC = SIMT_THREADS / (D / 32);
     const int64_t gx = p.work ? static_cast<int64_t>(n_work) * p.span_tiles * SIMT_TILE / RPC
                               : (T + RPC - 1) / RPC;
     if (gx == 0) return SMAT_OK;
     dim3 grid(static_cast<unsigned>(gx), BH);
-    smat_fwd_simt_kernel<D><<<grid, 128, 0, s>>>(p);
+    smat_fwd_simt_kernel<D><<<grid, SIMT_THREADS, 0, s>>>(p);
     return launch_status();
   }
 };
 template <int D>
 struct DqSimt {
   static int run(SimtParams& p, int T, int n_work, int BH, cudaStream_t s) {
-    constexpr int RPC = 128 / (D / 32);
+    constexpr int RPC = SIMT_THREADS / (D / 32);
     const int64_t gx = p.work ? static_cast<int64_t>(n_work) * p.span_tiles * SIMT_TILE / RPC
                               : (T + RPC - 1) / RPC;
     if (gx == 0) return SMAT_OK;
     dim3 grid(static_cast<unsigned>(gx), BH);
-    smat_dq_simt_kernel<D><<<grid, 128, 0, s>>>(p);
+    smat_dq_simt_kernel<D><<<grid, SIMT_THREADS, 0, s>>>(p);
     return launch_status();
   }
 };
 template <int D>
 struct DkdvSimt {
   static int run(SimtParams& p, int T, int n_work, int BH, cudaStream_t s) {
-    constexpr int RPC = 128 / (D / 32);
+    constexpr int RPC = SIMT_THREADS / (D / 32);
     const int64_t gx = p.work ? static_cast<int64_t>(n_work) * p.span_tiles * SIMT_TILE / RPC
                               : (T + RPC - 1) / RPC;
     if (gx == 0) return SMAT_OK;
     dim3 grid(static_cast<unsigned>(gx), BH);
-    smat_dkdv_simt_kernel<D><<<grid, 128, 0, s>>>(p);
+    smat_dkdv_simt_kernel<D><<<grid, SIMT_THREADS, 0, s>>>(p);
     return launch_status();
   }
 };
