@@ -103,6 +103,20 @@ __device__ __forceinline__ const float* row_ptr(const float* base, const int64_t
   return base + b * s[0] + h * s[1] + static_cast<int64_t>(t) * s[2];
 }
 
+// Rows of keys staged in shared memory for all rows of a CTA: SIMT_KB rows of
+// D floats at a stride of D + 4 (the TPR lanes of a row read different
+// 32-float parts of a key without bank conflicts).  Every thread of the CTA
+// takes part; consecutive threads read consecutive floats.
+constexpr int SIMT_KB = 32;
+template <int D>
+__device__ __forceinline__ void simt_stage(float* dst, const float* base, const int64_t* s, int b,
+                                           int h, int j0, int n) {
+  for (int idx = threadIdx.x; idx < n * D; idx += SIMT_THREADS) {
+    const int r = idx / D, c = idx % D;
+    dst[r * (D + 4) + c] = row_ptr(base, s, b, h, j0 + r)[c];
+  }
+}
+
 // grid: (ceil(T / rows_per_cta) or n_work * span_tiles * 128 / rows_per_cta, B * H);
 // block SIMT_THREADS threads.
 template <int D>
@@ -123,32 +137,64 @@ __global__ void __launch_bounds__(SIMT_THREADS) smat_fwd_simt_kernel(const SimtP
     acc[d] = 0.f;
   }
   float m = -INFINITY, l = 0.f;
-  const int qb = ii / p.bs;
-  const int e0 = p.indptr[qb], e1 = p.indptr[qb + 1];
-  for (int e = e0; e < e1; ++e) {
-    const int kb = p.indices[e];
-    const uint8_t kd = p.kind[e];
-    const int j0 = kb * p.bs, j1 = min(p.T, j0 + p.bs);
-    uint32_t w = 0u;
-    for (int j = j0; j < j1; ++j) {
-      const float* kr = row_ptr(p.k, p.k_s, b, h, j) + part * 32;
-      float s = 0.f;
+  // one key of the walk: score, visibility, online softmax update
+  auto step = [&](int j, int j0, uint8_t kd, uint32_t& w, const float* kr, const float* vr) {
+    float s = 0.f;
 #pragma unroll
-      for (int d = 0; d < 32; ++d) s = fmaf(q[d], kr[d], s);
-      s = group_sum<TPR>(s);
-      if (!simt_visible(p, kd, ii, j, false, j == j0, w)) continue;
-      const float* vr = row_ptr(p.v, p.v_s, b, h, j) + part * 32;
-      if (s > m) {
-        const float alpha = (m == -INFINITY) ? 0.f : expf(m - s);
-        l *= alpha;
+    for (int d = 0; d < 32; ++d) s = fmaf(q[d], kr[d], s);
+    s = group_sum<TPR>(s);
+    if (!simt_visible(p, kd, ii, j, false, j == j0, w)) return;
+    if (s > m) {
+      const float alpha = (m == -INFINITY) ? 0.f : expf(m - s);
+      l *= alpha;
 #pragma unroll
-        for (int d = 0; d < 32; ++d) acc[d] *= alpha;
-        m = s;
+      for (int d = 0; d < 32; ++d) acc[d] *= alpha;
+      m = s;
+    }
+    const float pr = expf(s - m);
+    l += pr;
+#pragma unroll
+    for (int d = 0; d < 32; ++d) acc[d] = fmaf(pr, vr[d], acc[d]);
+  };
+  // When every row of the CTA lies in one query block, the rows share a CSR
+  // row: its keys and values are staged in shared memory once for all of
+  // them, SIMT_KB at a time.  Otherwise each row walks its own CSR row
+  // reading K and V from global memory.
+  int first;
+  bool first_active;
+  simt_row<RPC>(p, 0, first, first_active);
+  const int last = min(first + RPC - 1, p.T - 1);
+  const bool shared = first < p.T && first / p.bs == last / p.bs;
+  if (shared) {
+    __shared__ float ks[SIMT_KB * (D + 4)], vs[SIMT_KB * (D + 4)];
+    const int qb = first / p.bs;
+    const int e0 = p.indptr[qb], e1 = p.indptr[qb + 1];
+    for (int e = e0; e < e1; ++e) {
+      const int kb = p.indices[e];
+      const uint8_t kd = p.kind[e];
+      const int j0 = kb * p.bs, j1 = min(p.T, j0 + p.bs);
+      uint32_t w = 0u;
+      for (int jb = j0; jb < j1; jb += SIMT_KB) {
+        const int n = min(SIMT_KB, j1 - jb);
+        __syncthreads();   // the previous keys are consumed
+        simt_stage<D>(ks, p.k, p.k_s, b, h, jb, n);
+        simt_stage<D>(vs, p.v, p.v_s, b, h, jb, n);
+        __syncthreads();
+        for (int jj = 0; jj < n; ++jj)
+          step(jb + jj, j0, kd, w, ks + jj * (D + 4) + part * 32, vs + jj * (D + 4) + part * 32);
       }
-      const float pr = expf(s - m);
-      l += pr;
-#pragma unroll
-      for (int d = 0; d < 32; ++d) acc[d] = fmaf(pr, vr[d], acc[d]);
+    }
+  } else {
+    const int qb = ii / p.bs;
+    const int e0 = p.indptr[qb], e1 = p.indptr[qb + 1];
+    for (int e = e0; e < e1; ++e) {
+      const int kb = p.indices[e];
+      const uint8_t kd = p.kind[e];
+      const int j0 = kb * p.bs, j1 = min(p.T, j0 + p.bs);
+      uint32_t w = 0u;
+      for (int j = j0; j < j1; ++j)
+        step(j, j0, kd, w, row_ptr(p.k, p.k_s, b, h, j) + part * 32,
+             row_ptr(p.v, p.v_s, b, h, j) + part * 32);
     }
   }
   if (!active) return;
@@ -182,28 +228,55 @@ __global__ void __launch_bounds__(SIMT_THREADS) smat_dq_simt_kernel(const SimtPa
   }
   const float lse = p.lse[static_cast<int64_t>(bh) * p.T + ii];
   const float dl = p.delta[static_cast<int64_t>(bh) * p.T + ii];
-  const int qb = ii / p.bs;
-  for (int e = p.indptr[qb]; e < p.indptr[qb + 1]; ++e) {
-    const int kb = p.indices[e];
-    const uint8_t kd = p.kind[e];
-    const int j0 = kb * p.bs, j1 = min(p.T, j0 + p.bs);
-    uint32_t w = 0u;
-    for (int j = j0; j < j1; ++j) {
-      const float* kr = row_ptr(p.k, p.k_s, b, h, j) + part * 32;
-      const float* vr = row_ptr(p.v, p.v_s, b, h, j) + part * 32;
-      float s = 0.f, dp = 0.f;
+  auto step = [&](int j, int j0, uint8_t kd, uint32_t& w, const float* kr, const float* vr) {
+    float s = 0.f, dp = 0.f;
 #pragma unroll
-      for (int d = 0; d < 32; ++d) {
-        s = fmaf(q[d], kr[d], s);
-        dp = fmaf(dor[d], vr[d], dp);
+    for (int d = 0; d < 32; ++d) {
+      s = fmaf(q[d], kr[d], s);
+      dp = fmaf(dor[d], vr[d], dp);
+    }
+    s = group_sum<TPR>(s);
+    dp = group_sum<TPR>(dp);
+    if (!simt_visible(p, kd, ii, j, false, j == j0, w)) return;
+    const float pr = expf(s - lse);
+    const float ds = pr * (dp - dl);
+#pragma unroll
+    for (int d = 0; d < 32; ++d) dq[d] = fmaf(ds, kr[d], dq[d]);
+  };
+  // rows of one query block share their CSR row: K and V staged once (as in
+  // the forward)
+  int first;
+  bool first_active;
+  simt_row<RPC>(p, 0, first, first_active);
+  const int last = min(first + RPC - 1, p.T - 1);
+  if (first < p.T && first / p.bs == last / p.bs) {
+    __shared__ float ks[SIMT_KB * (D + 4)], vs[SIMT_KB * (D + 4)];
+    const int qb = first / p.bs;
+    for (int e = p.indptr[qb]; e < p.indptr[qb + 1]; ++e) {
+      const int kb = p.indices[e];
+      const uint8_t kd = p.kind[e];
+      const int j0 = kb * p.bs, j1 = min(p.T, j0 + p.bs);
+      uint32_t w = 0u;
+      for (int jb = j0; jb < j1; jb += SIMT_KB) {
+        const int n = min(SIMT_KB, j1 - jb);
+        __syncthreads();
+        simt_stage<D>(ks, p.k, p.k_s, b, h, jb, n);
+        simt_stage<D>(vs, p.v, p.v_s, b, h, jb, n);
+        __syncthreads();
+        for (int jj = 0; jj < n; ++jj)
+          step(jb + jj, j0, kd, w, ks + jj * (D + 4) + part * 32, vs + jj * (D + 4) + part * 32);
       }
-      s = group_sum<TPR>(s);
-      dp = group_sum<TPR>(dp);
-      if (!simt_visible(p, kd, ii, j, false, j == j0, w)) continue;
-      const float pr = expf(s - lse);
-      const float ds = pr * (dp - dl);
-#pragma unroll
-      for (int d = 0; d < 32; ++d) dq[d] = fmaf(ds, kr[d], dq[d]);
+    }
+  } else {
+    const int qb = ii / p.bs;
+    for (int e = p.indptr[qb]; e < p.indptr[qb + 1]; ++e) {
+      const int kb = p.indices[e];
+      const uint8_t kd = p.kind[e];
+      const int j0 = kb * p.bs, j1 = min(p.T, j0 + p.bs);
+      uint32_t w = 0u;
+      for (int j = j0; j < j1; ++j)
+        step(j, j0, kd, w, row_ptr(p.k, p.k_s, b, h, j) + part * 32,
+             row_ptr(p.v, p.v_s, b, h, j) + part * 32);
     }
   }
   if (!active) return;
@@ -234,33 +307,66 @@ __global__ void __launch_bounds__(SIMT_THREADS) smat_dkdv_simt_kernel(const Simt
     dk[d] = 0.f;
     dv[d] = 0.f;
   }
-  const int kb = jj / p.bs;
-  for (int e = p.indptr[kb]; e < p.indptr[kb + 1]; ++e) {
-    const int qb = p.indices[e];
-    const uint8_t kd = p.kind[e];
-    const int i0 = qb * p.bs, i1 = min(p.T, i0 + p.bs);
-    uint32_t w = 0u;
-    for (int i = i0; i < i1; ++i) {
-      const float* qp = row_ptr(p.q, p.q_s, b, h, i) + part * 32;
-      const float* dp_ = row_ptr(p.dout, p.do_s, b, h, i) + part * 32;
-      float s = 0.f, dp = 0.f;
+  auto step = [&](int i, int i0, uint8_t kd, uint32_t& w, const float* qp, const float* dp_,
+                  float lse, float dl) {
+    float s = 0.f, dp = 0.f;
 #pragma unroll
-      for (int d = 0; d < 32; ++d) {
-        s = fmaf(qp[d], kr[d], s);
-        dp = fmaf(dp_[d], vr[d], dp);
-      }
-      s = group_sum<TPR>(s);
-      dp = group_sum<TPR>(dp);
-      if (!simt_visible(p, kd, i, jj, true, i == i0, w)) continue;
-      const float lse = p.lse[static_cast<int64_t>(bh) * p.T + i];
-      const float dl = p.delta[static_cast<int64_t>(bh) * p.T + i];
-      const float pr = expf(s - lse);
-      const float ds = pr * (dp - dl);
+    for (int d = 0; d < 32; ++d) {
+      s = fmaf(qp[d], kr[d], s);
+      dp = fmaf(dp_[d], vr[d], dp);
+    }
+    s = group_sum<TPR>(s);
+    dp = group_sum<TPR>(dp);
+    if (!simt_visible(p, kd, i, jj, true, i == i0, w)) return;
+    const float pr = expf(s - lse);
+    const float ds = pr * (dp - dl);
 #pragma unroll
-      for (int d = 0; d < 32; ++d) {
-        dv[d] = fmaf(pr, dp_[d], dv[d]);
-        dk[d] = fmaf(ds, qp[d], dk[d]);
+    for (int d = 0; d < 32; ++d) {
+      dv[d] = fmaf(pr, dp_[d], dv[d]);
+      dk[d] = fmaf(ds, qp[d], dk[d]);
+    }
+  };
+  const float* lse_bh = p.lse + static_cast<int64_t>(bh) * p.T;
+  const float* dl_bh = p.delta + static_cast<int64_t>(bh) * p.T;
+  // rows (keys) of one key block share their transposed CSR row: Q, dO and
+  // the queries' lse / delta staged once for all of them
+  int first;
+  bool first_active;
+  simt_row<RPC>(p, 0, first, first_active);
+  const int last = min(first + RPC - 1, p.T - 1);
+  if (first < p.T && first / p.bs == last / p.bs) {
+    __shared__ float qs[SIMT_KB * (D + 4)], ds_[SIMT_KB * (D + 4)], ls[SIMT_KB], dls[SIMT_KB];
+    const int kb = first / p.bs;
+    for (int e = p.indptr[kb]; e < p.indptr[kb + 1]; ++e) {
+      const int qb = p.indices[e];
+      const uint8_t kd = p.kind[e];
+      const int i0 = qb * p.bs, i1 = min(p.T, i0 + p.bs);
+      uint32_t w = 0u;
+      for (int ib = i0; ib < i1; ib += SIMT_KB) {
+        const int n = min(SIMT_KB, i1 - ib);
+        __syncthreads();
+        simt_stage<D>(qs, p.q, p.q_s, b, h, ib, n);
+        simt_stage<D>(ds_, p.dout, p.do_s, b, h, ib, n);
+        for (int r = threadIdx.x; r < n; r += SIMT_THREADS) {
+          ls[r] = lse_bh[ib + r];
+          dls[r] = dl_bh[ib + r];
+        }
+        __syncthreads();
+        for (int r = 0; r < n; ++r)
+          step(ib + r, i0, kd, w, qs + r * (D + 4) + part * 32, ds_ + r * (D + 4) + part * 32,
+               ls[r], dls[r]);
       }
+    }
+  } else {
+    const int kb = jj / p.bs;
+    for (int e = p.indptr[kb]; e < p.indptr[kb + 1]; ++e) {
+      const int qb = p.indices[e];
+      const uint8_t kd = p.kind[e];
+      const int i0 = qb * p.bs, i1 = min(p.T, i0 + p.bs);
+      uint32_t w = 0u;
+      for (int i = i0; i < i1; ++i)
+        step(i, i0, kd, w, row_ptr(p.q, p.q_s, b, h, i) + part * 32,
+             row_ptr(p.dout, p.do_s, b, h, i) + part * 32, lse_bh[i], dl_bh[i]);
     }
   }
   if (!active) return;
