@@ -25,9 +25,10 @@
 // word per row: the causal span on the diagonal, and for M^(d) PATTERN tiles
 // the row word (dQ) or column word (dK/dV) of pattern.cuh.
 //
-// Warp roles (576 threads): warps 0-15 compute -- warp w reads TMEM lanes
-// 32 (w % 4) .. +31 (its 32 tile rows) and chunk columns 32 (w / 4) .. +31;
-// warp 16 is the TMA producer; warp 17 allocates TMEM and issues the MMAs.
+// Warp roles (576 threads; 320 with 64-row chunks): warps 0 .. NCW-1 compute
+// -- warp w reads TMEM lanes 32 (w % 4) .. +31 (its 32 tile rows) and chunk
+// columns 32 (w / 4) .. +31; warp NCW is the TMA producer; warp NCW + 1
+// allocates TMEM and issues the MMAs.
 // P^T / dS^T / dS (bf16) are written back into the TMEM columns of the S / dP
 // they came from (each warp over columns it has already read) and feed the
 // tensor core as the A operand straight from TMEM.

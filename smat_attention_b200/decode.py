@@ -6,8 +6,9 @@ The reference decodes its kernelised arm in ``O(r p)`` per token from pooled
 state; softmax attention has no such summary, so each step reads the keys and
 values the new query sees -- its CSR row of the layout, at most ``max_row``
 blocks -- from a cache of the whole sequence.  :func:`decode_attention` is
-the op (``smat_decode`` of the C ABI: a split-row partial kernel and a
-combine kernel); :class:`SmatSoftmaxDecoder` keeps the cache and the
+the op (``smat_decode`` of the C ABI: one launch, each row's splits one
+thread-block cluster that combines them); :class:`SmatSoftmaxDecoder` keeps
+the cache and the
 positions and mirrors ``SmatDecoder``'s ``step`` / ``cache_words`` /
 ``kv_cache_words``.
 """
