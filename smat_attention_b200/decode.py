@@ -8,9 +8,8 @@ values the new query sees -- its CSR row of the layout, at most ``max_row``
 blocks -- from a cache of the whole sequence.  :func:`decode_attention` is
 the op (``smat_decode`` of the C ABI: one launch, each row's splits one
 thread-block cluster that combines them); :class:`SmatSoftmaxDecoder` keeps
-the cache and the
-positions and mirrors ``SmatDecoder``'s ``step`` / ``cache_words`` /
-``kv_cache_words``.
+the cache and the positions and mirrors ``SmatDecoder``'s ``step`` /
+``cache_words`` / ``kv_cache_words``.
 """
 
 from __future__ import annotations
