@@ -45,18 +45,6 @@ __device__ __forceinline__ void stage_rows(float* dst, const float* src, int row
               in ? 4u : 0u);
   }
 }
-// the same rows transposed: shared [WS][NS] (row i of the source in column i);
-// consecutive threads take consecutive rows, so the shared writes do not
-// collide on a bank (the strided global reads are served from L1)
-__device__ __forceinline__ void stage_rows_t(float* dst, const float* src, int row0, int nrows,
-                                             int T, int W, int WS, int NS) {
-  for (int e = threadIdx.x; e < nrows * WS; e += blockDim.x) {
-    const int i = e % nrows, c = e / nrows;
-    const bool in = c < W && row0 + i < T;
-    cp_async4(smem_u32(dst + c * NS + i),
-              in ? src + static_cast<int64_t>(row0 + i) * W + c : src, in ? 4u : 0u);
-  }
-}
 __device__ __forceinline__ void cp_async_wait_all() {
   asm volatile("cp.async.wait_all;" ::: "memory");
 }
@@ -177,10 +165,13 @@ __global__ void __launch_bounds__(256) kattn_seg_scan_kernel(float* __restrict__
 }
 
 // ---------------------------------------------------------------- chunk expand
-// For every chunk c: db_c += a_c dD_c ([C, R] x [R, P]) and
-// da_c += b_c dD_c^T ([C, P] x [P, R]).  Shared: a_c^T [RA][CS], b_c^T
-// [PB][CS], dD [R][PB], dD^T [P][RA] (zero-padded), so every 8 x 4 tile
-// reads two 16-byte words of rows and one of dD per 32 FMAs.
+// Chunk c of sequence s: db[rows] += a_c dD_c, da[rows] += b_c dD_c^T (the
+// backward of D = a_c^T b_c).  Shared, row-major: a rows [CS][RA] (16-byte
+// copies when R is a multiple of 4), b rows [CS][PB] (its chunk copied as one
+// run in 16-byte units, then re-laid -- P is odd in the reference), dD
+// [RA][PB] and dD^T [PB][RA] (the b run's staging reused); every copy reads
+// global memory in consecutive addresses.  A thread owns an 8-row x 4-column
+// tile of db or da and reads its 8 rows four k at a time.
 __global__ void __launch_bounds__(256) kattn_chunk_expand_kernel(
     const float* __restrict__ a, const float* __restrict__ b, const float* __restrict__ dD,
     float* __restrict__ da, float* __restrict__ db, int T, int C, int R, int P) {
@@ -188,13 +179,44 @@ __global__ void __launch_bounds__(256) kattn_chunk_expand_kernel(
   float* sm = reinterpret_cast<float*>(sm4);
   const int c = blockIdx.x, s = blockIdx.y, nc = gridDim.x;
   const int RA = round_up(R, 8), PB = round_up(P, 8), CS = round_up(C, 8);
-  float* saT = sm;                 // [RA][CS]
-  float* sbT = saT + RA * CS;      // [PB][CS]
-  float* sd = sbT + PB * CS;       // [RA][PB]  dD
+  float* sa = sm;                  // [CS][RA]
+  float* sb = sa + CS * RA;        // [CS][PB]
+  float* sd = sb + CS * PB;        // [RA][PB]  dD
   float* sdT = sd + RA * PB;       // [PB][RA]  dD^T
+  float* flat = sd;                // [C * P] staging of the b chunk (before sd / sdT)
   const int64_t row0 = static_cast<int64_t>(c) * C;
-  stage_rows_t(saT, a + static_cast<int64_t>(s) * T * R, c * C, C, T, R, RA, CS);
-  stage_rows_t(sbT, b + static_cast<int64_t>(s) * T * P, c * C, C, T, P, PB, CS);
+  const int rows = static_cast<int>(T - row0 < C ? T - row0 : C);
+  const float* as = a + static_cast<int64_t>(s) * T * R;
+  const float* bs = b + static_cast<int64_t>(s) * T * P;
+  if ((R & 3) == 0 && al16d(as)) {
+    for (int e = threadIdx.x; e < CS * (RA / 4); e += blockDim.x) {
+      const int i = e / (RA / 4), k = (e % (RA / 4)) * 4;
+      if (i < rows && k < R)
+        cp_async16(smem_u32(sa + i * RA + k), as + (row0 + i) * R + k);
+      else
+        *reinterpret_cast<float4*>(sa + i * RA + k) = make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+  } else {
+    stage_rows(sa, as, static_cast<int>(row0), CS, T, R, RA);
+  }
+  const float* bc = bs + row0 * P;
+  const int nflat = rows * P;
+  const bool flat16 = al16d(bc) && (nflat & 3) == 0 && C * P <= 2 * RA * PB;
+  if (flat16) {
+    for (int e = threadIdx.x * 4; e < nflat; e += blockDim.x * 4)
+      cp_async16(smem_u32(flat + e), bc + e);
+  } else {
+    stage_rows(sb, bs, static_cast<int>(row0), CS, T, P, PB);
+  }
+  cp_async_wait_all();
+  __syncthreads();
+  if (flat16) {   // [rows * P] -> [CS][PB], zero padding
+    for (int e = threadIdx.x; e < CS * PB; e += blockDim.x) {
+      const int i = e / PB, p = e % PB;
+      sb[e] = (i < rows && p < P) ? flat[i * P + p] : 0.f;
+    }
+    __syncthreads();   // the staging run is read before dD overwrites it
+  }
   const float* dd = dD + (static_cast<int64_t>(s) * nc + c) * R * P;
   for (int e = threadIdx.x; e < RA * PB; e += blockDim.x) {
     const int r = e / PB, p = e % PB;
@@ -202,23 +224,16 @@ __global__ void __launch_bounds__(256) kattn_chunk_expand_kernel(
     sd[e] = v;
     sdT[p * RA + r] = v;
   }
-  for (int e = threadIdx.x; e < (CS - C) * (RA + PB); e += blockDim.x) {
-    // rows past the chunk in the transposed tiles stay zero
-    const int w = e / (CS - C), i = C + e % (CS - C);
-    if (w < RA) saT[w * CS + i] = 0.f;
-    else sbT[(w - RA) * CS + i] = 0.f;
-  }
-  cp_async_wait_all();
   __syncthreads();
-  const int rows = static_cast<int>(T - row0 < C ? T - row0 : C);
-  // db tiles: 8 rows x 4 p, K = R; then da tiles: 8 rows x 4 r, K = P
+  // db tiles: 8 rows x 4 p, K = R (X = a rows, Y = dD); then da tiles: 8 rows
+  // x 4 r, K = P (X = b rows, Y = dD^T)
   const int tb = (CS / 8) * (PB / 4), ta = (CS / 8) * (RA / 4);
   for (int t = threadIdx.x; t < tb + ta; t += blockDim.x) {
     const bool is_b = t < tb;
     const int u = is_b ? t : t - tb;
     const int W = is_b ? PB : RA;          // output width (padded)
-    const int K = is_b ? RA : PB;          // contraction length (padded)
-    const float* X = is_b ? saT : sbT;     // [K][CS]
+    const int K = is_b ? RA : PB;          // contraction length (padded, multiple of 8)
+    const float* X = is_b ? sa : sb;       // [CS][K]
     const float* Y = is_b ? sd : sdT;      // [K][W]
     const int i0 = (u / (W / 4)) * 8, j0 = (u % (W / 4)) * 4;
     float acc[8][4];
@@ -226,17 +241,26 @@ __global__ void __launch_bounds__(256) kattn_chunk_expand_kernel(
     for (int i = 0; i < 8; ++i)
 #pragma unroll
       for (int j = 0; j < 4; ++j) acc[i][j] = 0.f;
-#pragma unroll 4
-    for (int k = 0; k < K; ++k) {
-      const float4 x0 = *reinterpret_cast<const float4*>(X + k * CS + i0);
-      const float4 x1 = *reinterpret_cast<const float4*>(X + k * CS + i0 + 4);
-      const float4 y = *reinterpret_cast<const float4*>(Y + k * W + j0);
-      const float xv[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
-      const float yv[4] = {y.x, y.y, y.z, y.w};
+#pragma unroll 2
+    for (int k = 0; k < K; k += 4) {
+      float xv[8][4];
 #pragma unroll
-      for (int i = 0; i < 8; ++i)
+      for (int i = 0; i < 8; ++i) {
+        const float4 x = *reinterpret_cast<const float4*>(X + (i0 + i) * K + k);
+        xv[i][0] = x.x;
+        xv[i][1] = x.y;
+        xv[i][2] = x.z;
+        xv[i][3] = x.w;
+      }
 #pragma unroll
-        for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(xv[i], yv[j], acc[i][j]);
+      for (int kk = 0; kk < 4; ++kk) {
+        const float4 y = *reinterpret_cast<const float4*>(Y + (k + kk) * W + j0);
+        const float yv[4] = {y.x, y.y, y.z, y.w};
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+#pragma unroll
+          for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(xv[i][kk], yv[j], acc[i][j]);
+      }
     }
     const int Wo = is_b ? P : R;
     float* dst = (is_b ? db + static_cast<int64_t>(s) * T * P : da + static_cast<int64_t>(s) * T * R) +

@@ -201,18 +201,26 @@ def _gather_sum(F, ptr, idx, n_out):
 
 
 class _Incidence(torch.autograd.Function):
+    """``U = C F`` as a CSR gather-sum; the backward is the same kernel over
+    the transposed table (given, or built on the device when needed)."""
+
     @staticmethod
-    def forward(ctx, F, ptr, idx, n_out):
-        ctx.save_for_backward(ptr, idx)
+    def forward(ctx, F, ptr, idx, n_out, t_ptr=None, t_idx=None):
+        if t_ptr is None:
+            ctx.save_for_backward(ptr, idx)
+        else:
+            ctx.save_for_backward(t_ptr, t_idx)
+        ctx.transposed = t_ptr is not None
         ctx.n_in = F.shape[1]
         ctx.dtype = F.dtype
         return _gather_sum(F, ptr, idx, n_out)
 
     @staticmethod
     def backward(ctx, dU):
-        ptr, idx = ctx.saved_tensors
-        t_ptr, t_idx = _transpose_csr(ptr, idx, ctx.n_in)
-        return _gather_sum(dU, t_ptr, t_idx, ctx.n_in).to(ctx.dtype), None, None, None
+        a, b = ctx.saved_tensors
+        t_ptr, t_idx = (a, b) if ctx.transposed else _transpose_csr(a, b, ctx.n_in)
+        return (_gather_sum(dU, t_ptr, t_idx, ctx.n_in).to(ctx.dtype),
+                None, None, None, None, None)
 
 
 def incidence(F, plane_pts, B: int):
@@ -222,13 +230,28 @@ def incidence(F, plane_pts, B: int):
     return _Incidence.apply(F, ptr, idx, int(B))
 
 
+def _transpose_csr_host(ptr, idx, n_cols):
+    """``_transpose_csr`` on the host (numpy): rows ascending per column."""
+    ptr = np.asarray(ptr, np.int64)
+    idx = np.asarray(idx, np.int64)
+    rows = np.repeat(np.arange(len(ptr) - 1, dtype=np.int64), np.diff(ptr))
+    order = np.argsort(idx * len(ptr) + rows, kind="stable")
+    t_ptr = np.zeros(n_cols + 1, np.int64)
+    t_ptr[1:] = np.cumsum(np.bincount(idx, minlength=n_cols))
+    return t_ptr, rows[order].astype(np.int32)
+
+
 def _incidence_csr(F, spec: MaskSpec):
+    """The op's incidence with the spec's table and its transpose staged on
+    the device once (the backward then reads the cached transpose)."""
     key = ("kattn_csr", str(F.device))
     if key not in spec.dev:
-        spec.dev[key] = (torch.from_numpy(np.ascontiguousarray(spec.C_indptr, np.int64)).to(F.device),
-                         torch.from_numpy(np.ascontiguousarray(spec.C_indices, np.int32)).to(F.device))
-    ptr, idx = spec.dev[key]
-    return _Incidence.apply(F, ptr, idx, int(spec.B))
+        as_t = lambda a, dt: torch.from_numpy(np.ascontiguousarray(a, dt)).to(F.device)
+        t_ptr, t_idx = _transpose_csr_host(spec.C_indptr, spec.C_indices, F.shape[1])
+        spec.dev[key] = (as_t(spec.C_indptr, np.int64), as_t(spec.C_indices, np.int32),
+                         as_t(t_ptr, np.int64), as_t(t_idx, np.int32))
+    ptr, idx, t_ptr, t_idx = spec.dev[key]
+    return _Incidence.apply(F, ptr, idx, int(spec.B), t_ptr, t_idx)
 
 
 # ---------------------------------------------------------------- normalisation
