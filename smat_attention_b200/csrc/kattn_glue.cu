@@ -167,11 +167,11 @@ __global__ void __launch_bounds__(256) kattn_seg_scan_kernel(float* __restrict__
 // ---------------------------------------------------------------- chunk expand
 // Chunk c of sequence s: db[rows] += a_c dD_c, da[rows] += b_c dD_c^T (the
 // backward of D = a_c^T b_c).  Shared, row-major: a rows [CS][RA] (16-byte
-// copies when R is a multiple of 4), b rows [CS][PB] (its chunk copied as one
-// run in 16-byte units, then re-laid -- P is odd in the reference), dD
-// [RA][PB] and dD^T [PB][RA] (the b run's staging reused); every copy reads
-// global memory in consecutive addresses.  A thread owns an 8-row x 4-column
-// tile of db or da and reads its 8 rows four k at a time.
+// copies when R is a multiple of 4), b rows [CS][PB], dD [RA][PB] and dD^T
+// [PB][RA] (4-byte copies -- P is odd in the reference); all copies are
+// issued before one wait and read global memory in consecutive addresses.  A
+// thread owns an 8-row x 4-column tile of db or da and reads its 8 rows four
+// k at a time.
 __global__ void __launch_bounds__(256) kattn_chunk_expand_kernel(
     const float* __restrict__ a, const float* __restrict__ b, const float* __restrict__ dD,
     float* __restrict__ da, float* __restrict__ db, int T, int C, int R, int P) {
@@ -183,7 +183,6 @@ __global__ void __launch_bounds__(256) kattn_chunk_expand_kernel(
   float* sb = sa + CS * RA;        // [CS][PB]
   float* sd = sb + CS * PB;        // [RA][PB]  dD
   float* sdT = sd + RA * PB;       // [PB][RA]  dD^T
-  float* flat = sd;                // [C * P] staging of the b chunk (before sd / sdT)
   const int64_t row0 = static_cast<int64_t>(c) * C;
   const int rows = static_cast<int>(T - row0 < C ? T - row0 : C);
   const float* as = a + static_cast<int64_t>(s) * T * R;
@@ -199,31 +198,16 @@ __global__ void __launch_bounds__(256) kattn_chunk_expand_kernel(
   } else {
     stage_rows(sa, as, static_cast<int>(row0), CS, T, R, RA);
   }
-  const float* bc = bs + row0 * P;
-  const int nflat = rows * P;
-  const bool flat16 = al16d(bc) && (nflat & 3) == 0 && C * P <= 2 * RA * PB;
-  if (flat16) {
-    for (int e = threadIdx.x * 4; e < nflat; e += blockDim.x * 4)
-      cp_async16(smem_u32(flat + e), bc + e);
-  } else {
-    stage_rows(sb, bs, static_cast<int>(row0), CS, T, P, PB);
-  }
-  cp_async_wait_all();
-  __syncthreads();
-  if (flat16) {   // [rows * P] -> [CS][PB], zero padding
-    for (int e = threadIdx.x; e < CS * PB; e += blockDim.x) {
-      const int i = e / PB, p = e % PB;
-      sb[e] = (i < rows && p < P) ? flat[i * P + p] : 0.f;
-    }
-    __syncthreads();   // the staging run is read before dD overwrites it
-  }
+  stage_rows(sb, bs, static_cast<int>(row0), CS, T, P, PB);
   const float* dd = dD + (static_cast<int64_t>(s) * nc + c) * R * P;
   for (int e = threadIdx.x; e < RA * PB; e += blockDim.x) {
     const int r = e / PB, p = e % PB;
-    const float v = (r < R && p < P) ? dd[r * P + p] : 0.f;
-    sd[e] = v;
-    sdT[p * RA + r] = v;
+    const bool in = r < R && p < P;
+    const float* src = in ? dd + r * P + p : dd;
+    cp_async4(smem_u32(sd + e), src, in ? 4u : 0u);
+    cp_async4(smem_u32(sdT + p * RA + r), src, in ? 4u : 0u);
   }
+  cp_async_wait_all();
   __syncthreads();
   // db tiles: 8 rows x 4 p, K = R (X = a rows, Y = dD); then da tiles: 8 rows
   // x 4 r, K = P (X = b rows, Y = dD^T)
