@@ -101,7 +101,9 @@ def _describe(w, H):
 
 def _flops(pairs, w, H):
     fwd = 4.0 * w["D"] * pairs * w["B"] * H
-    return {"fwd": fwd, "dkdv": 2.0 * fwd, "dq": 1.5 * fwd, "bwd": 2.5 * fwd, "step": 3.5 * fwd}
+    # dkdv_dq: the fused backward kernel (dK/dV plus the dQ accumulation)
+    return {"fwd": fwd, "dkdv": 2.0 * fwd, "dq": 1.5 * fwd, "dkdv_dq": 2.5 * fwd,
+            "bwd": 2.5 * fwd, "step": 3.5 * fwd}
 
 
 def _peaks():
@@ -470,6 +472,13 @@ class AttnCase:
         self.lse = torch.empty(B, H_, T, dtype=torch.float32, device=device)
         self.delta = torch.empty_like(self.lse)
         self.dq, self.dk, self.dv = (torch.empty_like(self.q) for _ in range(3))
+        # the opt-in fused backward: dQ accumulated by the dK/dV kernel in fp32
+        # (only with SMAT_FUSED_DQ=1, as in the library)
+        from smat_attention_b200 import attention as A
+        self.fused = (A.fused_dq_applies(self.dtype, D) and not w.get("fwd_only")
+                      and A.FUSED_DQ)
+        self.dq_acc = (torch.empty(B * H_ * T * D, dtype=torch.float32, device=device)
+                       if self.fused else None)
         self.err = torch.zeros(1, dtype=torch.int32, device=device)
         self.stream = torch.cuda.current_stream(device)
         self.L = _lib.lib()
@@ -511,6 +520,33 @@ class AttnCase:
                 lay["kind"].data_ptr(), lay["nblocks"], lay["nnzb"], lay["block"],
                 lay["max_row"], scale, err.data_ptr(), st))
 
+        def launch_dkdv_dq():
+            acc = self.dq_acc
+            _lib.check("smat_bwd_dkdv_dq", L.smat_bwd_dkdv_dq(
+                dt, q.data_ptr(), sp(q), k.data_ptr(), sp(k), v.data_ptr(), sp(v),
+                do.data_ptr(), sp(do), lse.data_ptr(), delta.data_ptr(), acc.data_ptr(),
+                acc.numel(), dk.data_ptr(), sp(dk), dv.data_ptr(), sp(dv), B, H, T, D,
+                lay["t_indptr"].data_ptr(), lay["t_indices"].data_ptr(),
+                lay["t_kind"].data_ptr(), lay["nblocks"], lay["nnzb"], lay["block"],
+                lay["t_max_row"], scale, err.data_ptr(), st))
+
+        def launch_dq_finish():
+            acc = self.dq_acc
+            _lib.check("smat_bwd_dq_finish", L.smat_bwd_dq_finish(
+                dt, acc.data_ptr(), acc.numel(), dq.data_ptr(), sp(dq), B, H, T, D, scale, st))
+
+        def launch_bwd_acc_pattern():
+            acc = self.dq_acc
+            _lib.check("smat_bwd_acc", L.smat_bwd_acc(
+                dt, q.data_ptr(), sp(q), k.data_ptr(), sp(k), v.data_ptr(), sp(v),
+                o.data_ptr(), sp(o), do.data_ptr(), sp(do), lse.data_ptr(), delta.data_ptr(),
+                dq.data_ptr(), sp(dq), dk.data_ptr(), sp(dk), dv.data_ptr(), sp(dv),
+                B, H, T, D, lay["indptr"].data_ptr(), lay["indices"].data_ptr(),
+                lay["kind"].data_ptr(), lay["t_indptr"].data_ptr(), lay["t_indices"].data_ptr(),
+                lay["t_kind"].data_ptr(), lay["nblocks"], lay["nnzb"], lay["block"],
+                lay["max_row"], lay["t_max_row"], lay["pattern"], acc.data_ptr(), acc.numel(),
+                scale, err.data_ptr(), st))
+
         def launch_fwd_pattern():
             _lib.check("smat_fwd_pattern", L.smat_fwd_pattern(
                 dt, q.data_ptr(), sp(q), k.data_ptr(), sp(k), v.data_ptr(), sp(v),
@@ -531,10 +567,17 @@ class AttnCase:
         if self.w.get("fwd_only"):
             # (name, launch, kernel launches it makes)
             return [("fwd", launch_fwd, 1)]
+        if lay["pattern"] is None and self.fused:
+            # the fused backward: dK/dV/dQ-accumulate (after zeroing the
+            # accumulator), then dQ's conversion
+            return [("fwd", launch_fwd, 1), ("bwd_pre", launch_pre, 1),
+                    ("dkdv_dq", launch_dkdv_dq, 1), ("dq_finish", launch_dq_finish, 1)]
         if lay["pattern"] is None:
             return [("fwd", launch_fwd, 1), ("bwd_pre", launch_pre, 1),
                     ("dkdv", launch_dkdv, 1), ("dq", launch_dq, 1)]
         # M^(d): the pattern entry points (the backward launches its three passes)
+        if self.fused:
+            return [("fwd", launch_fwd_pattern, 1), ("bwd", launch_bwd_acc_pattern, 3)]
         return [("fwd", launch_fwd_pattern, 1), ("bwd", launch_bwd_pattern, 3)]
 
     @property
@@ -573,7 +616,7 @@ class AttnCase:
         return start.elapsed_time(stop) / K, per_kernel, clk
 
     def free(self):
-        for name in ("q", "k", "v", "do", "o", "lse", "delta", "dq", "dk", "dv"):
+        for name in ("q", "k", "v", "do", "o", "lse", "delta", "dq", "dk", "dv", "dq_acc"):
             setattr(self, name, None)
         self.kernels = []
 
@@ -1212,7 +1255,8 @@ def run_gpu(args):
             tf = f / (t * 1e-3) / 1e12
             kern[name].update({"tflops": tf, "frac": tf / peaks["tflops"],
                                "frac_sustained": tf / peaks["tflops_sustained"]})
-    dom = max((n for n in per_kernel_max if n != "bwd_pre"), key=per_kernel_max.get)
+    dom = max((n for n in per_kernel_max if n not in ("bwd_pre", "dq_finish")),
+              key=per_kernel_max.get)
     achieved = case.fl[dom] / (per_kernel_max[dom] * 1e-3) / 1e12
     traffic = _traffic().get(dom)
     if traffic is not None and H_rank != WORKLOADS["c3"]["H"]:

@@ -358,6 +358,53 @@ SMAT_API int smat_bwd(int dtype,
              int nblocks, int64_t nnzb, int block, int max_row, int t_max_row,
              float scale, int32_t* err_word, void* stream);
 
+/* The fused backward (bf16, D = 128).  smat_bwd_dkdv_dq zeroes the caller's
+ * fp32 accumulator dq_acc ([B*H, T, D] contiguous, 16-byte aligned, at least
+ * B*H*T*D floats) and runs one kernel over the transposed CSR that writes dK
+ * and dV as smat_bwd_dkdv does and adds dS K (unscaled) for every block pair
+ * into dq_acc; smat_bwd_dq_finish then writes dq = bf16(scale * dq_acc) (D in
+ * {64, 128}).  dQ needs no second pass over the forward CSR, which would
+ * recompute S and dP: 5 block-pair MMAs per pair instead of 7.  The additions
+ * into dq_acc are fp32 reductions in L2 whose order varies between runs, so
+ * dQ may differ in its last bits from run to run (dK, dV are deterministic);
+ * smat_bwd stays the bitwise-deterministic backward.
+ * smat_bwd_acc: smat_bwd (pattern may be NULL) through these two passes where
+ * they apply (bf16, D = 128), else exactly smat_bwd (dq_acc unused, may be
+ * NULL).  The reference's autograd backward (src/smat/kernels/triton_bwd.py:
+ * 162-196) accumulates dQ per query block instead. */
+SMAT_API int smat_bwd_dkdv_dq(int dtype,
+                     const void* q, const int64_t* q_stride,
+                     const void* k, const int64_t* k_stride,
+                     const void* v, const int64_t* v_stride,
+                     const void* dout, const int64_t* do_stride,
+                     const float* lse, const float* delta,
+                     float* dq_acc, int64_t dq_acc_floats,
+                     void* dk, const int64_t* dk_stride,
+                     void* dv, const int64_t* dv_stride,
+                     int B, int H, int T, int D,
+                     const int32_t* t_indptr, const int32_t* t_indices, const uint8_t* t_kind,
+                     int nblocks, int64_t nnzb, int block, int t_max_row,
+                     float scale, int32_t* err_word, void* stream);
+SMAT_API int smat_bwd_dq_finish(int dtype, const float* dq_acc, int64_t dq_acc_floats,
+                       void* dq, const int64_t* dq_stride,
+                       int B, int H, int T, int D, float scale, void* stream);
+SMAT_API int smat_bwd_acc(int dtype,
+                 const void* q, const int64_t* q_stride,
+                 const void* k, const int64_t* k_stride,
+                 const void* v, const int64_t* v_stride,
+                 const void* o, const int64_t* o_stride,
+                 const void* dout, const int64_t* do_stride,
+                 const float* lse, float* delta,
+                 void* dq, const int64_t* dq_stride,
+                 void* dk, const int64_t* dk_stride,
+                 void* dv, const int64_t* dv_stride,
+                 int B, int H, int T, int D,
+                 const int32_t* indptr, const int32_t* indices, const uint8_t* kind,
+                 const int32_t* t_indptr, const int32_t* t_indices, const uint8_t* t_kind,
+                 int nblocks, int64_t nnzb, int block, int max_row, int t_max_row,
+                 const smat_pattern_t* pattern, float* dq_acc, int64_t dq_acc_floats,
+                 float scale, int32_t* err_word, void* stream);
+
 /* smat_fwd and smat_bwd for a layout with SMAT_TILE_PATTERN tiles (from
  * smat_layout_build_pattern) and the device bit tables of its M^(d) mask:
  * the reference's M^(d) masks (src/smat/mask.py:244-425) under softmax

@@ -87,6 +87,19 @@ SIGNATURES = {
                           _vp, _vp, _vp, _i64p, _vp, _i64p, _vp, _i64p,
                           _c_int, _c_int, _c_int, _c_int, _vp, _vp, _vp, _vp, _vp, _vp,
                           _c_int, _c_i64, _c_int, _c_int, _c_int, _c_f, _vp, _vp]),
+    # fused backward: dK/dV plus the fp32 dQ accumulator, the dQ finish, and
+    # smat_bwd with the pattern and the accumulator before scale
+    "smat_bwd_dkdv_dq": (_c_int, [_c_int, _vp, _i64p, _vp, _i64p, _vp, _i64p, _vp, _i64p,
+                                  _vp, _vp, _vp, _c_i64, _vp, _i64p, _vp, _i64p,
+                                  _c_int, _c_int, _c_int, _c_int, _vp, _vp, _vp,
+                                  _c_int, _c_i64, _c_int, _c_int, _c_f, _vp, _vp]),
+    "smat_bwd_dq_finish": (_c_int, [_c_int, _vp, _c_i64, _vp, _i64p,
+                                    _c_int, _c_int, _c_int, _c_int, _c_f, _vp]),
+    "smat_bwd_acc": (_c_int, [_c_int, _vp, _i64p, _vp, _i64p, _vp, _i64p, _vp, _i64p, _vp,
+                              _i64p, _vp, _vp, _vp, _i64p, _vp, _i64p, _vp, _i64p,
+                              _c_int, _c_int, _c_int, _c_int, _vp, _vp, _vp, _vp, _vp, _vp,
+                              _c_int, _c_i64, _c_int, _c_int, _c_int,
+                              ctypes.POINTER(Pattern), _vp, _c_i64, _c_f, _vp, _vp]),
     "smat_pattern_tables": (_c_int, [_c_int, _c_int, _vp, _vp, _vp, _c_int, _vp, _c_int]),
     "smat_layout_build_pattern": (_c_int, [_c_int, _c_int, _c_int, _c_int, _c_int, _c_int,
                                            _vp, _vp, _vp, _c_i64, _i64p]),

@@ -8,7 +8,13 @@ differentiable through :class:`SmatSoftmaxFn`:
 * forward: ``o = softmax(scale q k^T + mask) v`` and the fp32 natural-log
   normaliser ``lse`` (non-differentiable output);
 * backward: the ``delta = rowsum(dO * o)`` preprocess, then dK/dV over the
-  layout's transposed CSR and dQ over its forward CSR.
+  layout's transposed CSR and dQ over its forward CSR (bitwise
+  reproducible).  Optionally, for bf16 at D = 128, the dK/dV kernel also
+  accumulates dQ (fp32 reductions into a workspace, then one conversion
+  pass), which skips the second pass's recomputation of S and dP; that dQ
+  can differ in its last bits between runs.  ``FUSED_DQ = True`` (or the
+  environment variable ``SMAT_FUSED_DQ=1``) selects it; on B200 at config 3
+  it is not faster than the two passes.
 
 Tensors are ``[B, H, T, D]`` on a CUDA device, bf16 (tensor-core kernels,
 D in {64, 128}, block in {64, 128}) or fp32 (full-fp32 CUDA-core kernels,
@@ -32,6 +38,7 @@ from __future__ import annotations
 
 import ctypes
 import math
+import os
 from typing import Dict, Tuple
 
 import numpy as np
@@ -44,6 +51,16 @@ __all__ = ["smat_softmax_attention", "SmatSoftmaxFn", "layout_device_args",
            "kernel_layout", "check_device_errors", "fwd", "bwd"]
 
 _DTYPES = {torch.bfloat16: _lib.DTYPE_BF16, torch.float32: _lib.DTYPE_F32}
+
+# False: the backward's dQ comes from its own pass over the forward CSR
+# (bitwise reproducible); True: bf16 at D = 128 accumulates dQ inside the
+# dK/dV kernel (fewer MMAs, last bits vary between runs)
+FUSED_DQ = os.environ.get("SMAT_FUSED_DQ", "0") == "1"
+
+
+def fused_dq_applies(dtype, D: int) -> bool:
+    """Whether :func:`bwd` accumulates dQ inside the dK/dV kernel."""
+    return dtype == torch.bfloat16 and D == 128
 _ERR: Dict[str, torch.Tensor] = {}
 
 
@@ -170,8 +187,12 @@ def fwd(q, k, v, spec: MaskSpec, scale: float, o=None):
     return o, lse
 
 
-def bwd(q, k, v, o, lse, do, spec: MaskSpec, scale: float):
-    """Launch preprocess + dK/dV + dQ; returns ``(dq, dk, dv)``."""
+def bwd(q, k, v, o, lse, do, spec: MaskSpec, scale: float, fused_dq=None):
+    """Launch preprocess + dK/dV + dQ; returns ``(dq, dk, dv)``.
+
+    ``fused_dq`` (default: the module's ``FUSED_DQ``) accumulates dQ inside
+    the dK/dV kernel where that applies (bf16, D = 128).
+    """
     q, k, v, o, do = (_prep(x, n) for x, n in ((q, "q"), (k, "k"), (v, "v"), (o, "o"), (do, "do")))
     if do.dtype != q.dtype:
         do = do.to(q.dtype)
@@ -192,7 +213,13 @@ def bwd(q, k, v, o, lse, do, spec: MaskSpec, scale: float):
             lay["max_row"], lay["t_max_row"]]
     tail = [float(scale), _err_word(q.device).data_ptr(),
             torch.cuda.current_stream(q.device).cuda_stream]
-    if lay["pattern"] is None:
+    if fused_dq is None:
+        fused_dq = FUSED_DQ
+    if fused_dq and fused_dq_applies(q.dtype, D):
+        acc = torch.empty(B * H * T * D, dtype=torch.float32, device=q.device)
+        _lib.check("smat_bwd_acc", L.smat_bwd_acc(*args, lay["pattern"], acc.data_ptr(),
+                                                  acc.numel(), *tail))
+    elif lay["pattern"] is None:
         _lib.check("smat_bwd", L.smat_bwd(*args, *tail))
     else:
         _lib.check("smat_bwd_pattern", L.smat_bwd_pattern(*args, lay["pattern"], *tail))

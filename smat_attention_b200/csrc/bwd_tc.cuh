@@ -1,6 +1,7 @@
 // Block-sparse causal softmax attention, backward, bf16 on sm_100a tensor cores.
 //
-// Two kernels, no atomics (results are deterministic):
+// Two kernels, no atomics (results are deterministic), and an opt-in fused
+// variant of the first (FQ below) that also accumulates dQ:
 //
 // dK/dV  one CTA per 128-row key tile of one (batch, head); it walks the
 //        union of the tile's transposed-CSR rows (the query blocks that read
@@ -11,6 +12,9 @@
 // dQ     one CTA per 128-row query tile; it walks the forward CSR in chunks
 //        of 128 keys:
 //          S = Q K_c^T   dP = dO V_c^T   dS = P (dP - delta)   dQ += dS K_c
+//        Q and dO are copied into TMEM once per tile (S and dP take their A
+//        operand from there), after which their shared-memory tiles serve
+//        as one more slot of the K_c / V_c ring.
 //
 // Every tcgen05.mma is 128 x 128 (or 128 x D): on B200 an N = 64 MMA costs
 // nearly as many cycles as an N = 128 one, so the chunk is 128 wide.  TMEM
@@ -53,6 +57,7 @@ struct BwdParams {
   int head_group;          // without a work list: (b, h) per tile-interleaved group (>= 1)
   float scale;             // softmax scale
   float scale_log2;        // softmax scale * log2(e)
+  float* dq_acc;           // fused dQ (dK/dV kernel with FQ): fp32 [B*H, T, D], pre-zeroed
   int32_t* err;
   MdPattern md;            // tables of PATTERN tiles (null row_bits: the layout has none)
 };
@@ -60,11 +65,24 @@ struct BwdParams {
 // CN_ chunk rows: 128, or 64 at D = 64 with 64-row blocks -- TMEM then needs
 // 256 columns and shared memory <= 113 KB, so two CTAs share an SM and one's
 // set-up, hand-off waits and epilogue overlap the other's chunks.
-template <bool DKDV, int D, int CN_ = 128>
+// FQ_ (dK/dV only, D = 128): the same kernel also forms dQ_c = dS_c K for each
+// chunk and adds it into an fp32 dQ accumulator in global memory, so no
+// second kernel recomputes S and dP for dQ (5 MMAs per chunk instead of 4 + 3).
+// dS^T then goes to shared memory, over the chunk's dO once dV has read it,
+// where it is the A operand of dK (K-major) and the B operand of dQ_c^T =
+// K^T dS_c^T (MN-major); dQ_c^T lands in the TMEM columns of dP, which the
+// compute warps have already read.  Transposed, a TMEM lane holds one column
+// of D for the chunk's queries, so a warp's reduction instruction adds 32
+// consecutive floats of one dQ row (one 128-byte line) instead of 16 bytes
+// of 32 rows; the warps drain it before the next dP is issued.
+template <bool DKDV, int D, int CN_ = 128, bool FQ_ = false>
 struct BwdCfg {
   static constexpr int BM = 128;     // tile rows
   static constexpr int CN = CN_;     // chunk rows (queries for dK/dV, keys for dQ)
+  static constexpr bool FQ = FQ_;
   static_assert(CN == 128 || (CN == 64 && D == 64), "chunk rows");
+  // dS^T (CN x BM bf16) takes the place of a dO chunk (CN x D bf16)
+  static_assert(!FQ || (DKDV && D == BM && CN == 128), "fused dQ shape");
   static constexpr int MIN_BLOCKS = CN == 64 ? 2 : 1;   // CTAs per SM
   static constexpr int SMEM_CAP = (CN == 64 ? 113 : 227) * 1024;
   static constexpr int BOX = 64;     // TMA box rows of a chunk load
@@ -82,23 +100,46 @@ struct BwdCfg {
   static constexpr int OFF_C0 = OFF_R1 + ROW_BYTES;             // Q_c (dK/dV) or K_c (dQ)
   static constexpr int OFF_C1 = OFF_C0 + STAGES * CH_BYTES;     // dO_c (dK/dV) or V_c (dQ)
   static constexpr int OFF_LD = OFF_C1 + STAGES * CH_BYTES;     // per stage: lse [CN], delta [CN]
+  // dQ: once Q and dO sit in TMEM (below) their shared-memory tiles hold one
+  // more slot of the chunk ring (C0 over R0, C1 over R1)
+  static constexpr bool TA = !DKDV;
+  static constexpr int RING = TA ? STAGES + 1 : STAGES;
+  static_assert(!TA || CH_BYTES <= ROW_BYTES, "ring slot over the resident tiles");
+  __host__ __device__ static constexpr uint32_t c_off(int s, int which) {
+    return s < STAGES ? static_cast<uint32_t>((which ? OFF_C1 : OFF_C0) + s * CH_BYTES)
+                      : static_cast<uint32_t>(which ? OFF_R1 : OFF_R0);
+  }
   static constexpr int OFF_BAR = OFF_LD + STAGES * LD_BYTES;
   // barriers: r_full, c_full[S], c_empty[S], s_full, dp_full, p_ready, ds_ready,
   // acc_done, drain
-  static constexpr int BAR_R = 0, BAR_CF = 1, BAR_CE = 1 + STAGES, BAR_SF = 1 + 2 * STAGES,
+  // (+ with FQ: dv_done, dq_full, dq_empty)
+  // (+ with FQ: dv_done, dq_full, dq_empty; the dQ kernel: resident tiles in TMEM)
+  static constexpr int BAR_R = 0, BAR_CF = 1, BAR_CE = 1 + RING, BAR_SF = 1 + 2 * RING,
                        BAR_DPF = BAR_SF + 1, BAR_PR = BAR_DPF + 1, BAR_DSR = BAR_PR + 1,
-                       BAR_AD = BAR_DSR + 1, BAR_DRAIN = BAR_AD + 1, NBAR = BAR_DRAIN + 1;
+                       BAR_AD = BAR_DSR + 1, BAR_DRAIN = BAR_AD + 1, BAR_DVD = BAR_DRAIN + 1,
+                       BAR_DQF = BAR_DVD + 1, BAR_DQE = BAR_DQF + 1, BAR_RT = BAR_DQE + 1,
+                       NBAR = BAR_RT + 1;
   static constexpr int OFF_MISC = OFF_BAR + NBAR * 8;
   static constexpr int SMEM_BYTES = OFF_MISC + 16 + 1024;
   static_assert(SMEM_BYTES <= SMEM_CAP, "shared memory budget");
   static_assert(STAGES >= 2, "at least two stages");
   // the epilogue stages the output tile(s) in the chunk buffers of C0
   static_assert((DKDV ? 2 : 1) * ROW_BYTES <= STAGES * CH_BYTES, "epilogue staging");
-  // TMEM: S | dP | accumulators.  S and dP read both operands from shared
-  // memory: with N = 128 an MMA costs the same with A in shared memory or
-  // in TMEM.
+  // TMEM: S | dP | accumulators (| Q | dO for dQ).  A 128 x 128 x 16 MMA
+  // step with both operands in shared memory reads 8 KB in the 64 cycles it
+  // computes, the whole 128 B/cycle of the SM's shared-memory path, which
+  // TMA writes and the epilogue share; an operand read from TMEM halves it.
+  // The dQ kernel has the columns for its resident Q and dO tiles (bf16
+  // pairs, D / 2 columns each): its S and dP take A from TMEM.  The dK/dV
+  // kernel's accumulators leave no room, so its S^T and dP^T read K and V
+  // from shared memory.
   static constexpr int COL_S = 0, COL_DP = CN, COL_ACC0 = 2 * CN, COL_ACC1 = COL_ACC0 + D;
-  static constexpr int TMEM_USED = COL_ACC0 + (DKDV ? 2 : 1) * D;
+  static constexpr int COL_RA = COL_ACC0 + (DKDV ? 2 : 1) * D;   // TA: Q | dO
+  static constexpr int TMEM_USED = COL_RA + (TA ? D : 0);
+  // TA: warp (quad, grp) with grp < RA_GROUPS copies one 64-column panel of
+  // Q or dO for its 32 rows into TMEM
+  static constexpr int RA_GROUPS = 2 * D / 64;
+  static_assert(!TA || RA_GROUPS <= CN / 32, "resident-tile copy warps");
   static constexpr int TMEM_COLS = TMEM_USED <= 256 ? 256 : 512;
   static_assert(TMEM_USED <= TMEM_COLS && TMEM_COLS * MIN_BLOCKS <= 512, "TMEM budget");
   // compute warps: CN / 32 groups of 4; group g owns chunk columns [32 g, 32 g + 32)
@@ -106,6 +147,9 @@ struct BwdCfg {
   static constexpr int PRODUCER_WARP = NCW, MMA_WARP = NCW + 1, THREADS = (NCW + 2) * 32;
   static constexpr uint32_t IDESC_SC = idesc_bf16(BM, CN, false, false);  // S, dP
   static constexpr uint32_t IDESC_ACC = idesc_bf16(BM, D, false, true);   // dV, dK, dQ
+  // fused dQ_c^T = K^T dS_c^T: A = K^T (D x keys) read MN-major from the K
+  // tile, B = dS^T (keys x queries) MN-major
+  static constexpr uint32_t IDESC_DQ = idesc_bf16(D, CN, true, true);
 };
 
 // TMEM column (packed bf16 pairs) of the A operand's k-step kk (16 chunk
@@ -113,15 +157,16 @@ struct BwdCfg {
 // its first 16 columns
 __device__ __forceinline__ uint32_t a_col(int kk) { return 32u * (kk >> 1) + 8u * (kk & 1); }
 
-template <bool DKDV, int D, int CN>
-__global__ void __launch_bounds__(BwdCfg<DKDV, D, CN>::THREADS, BwdCfg<DKDV, D, CN>::MIN_BLOCKS)
+template <bool DKDV, int D, int CN, bool FQ = false>
+__global__ void __launch_bounds__(BwdCfg<DKDV, D, CN, FQ>::THREADS,
+                                  BwdCfg<DKDV, D, CN, FQ>::MIN_BLOCKS)
     smat_bwd_tc_kernel(const __grid_constant__ CUtensorMap tm_r0,
                        const __grid_constant__ CUtensorMap tm_r1,
                        const __grid_constant__ CUtensorMap tm_c0,
                        const __grid_constant__ CUtensorMap tm_c1,
                        const __grid_constant__ CUtensorMap tm_o0,
                        const __grid_constant__ CUtensorMap tm_o1, const BwdParams p) {
-  using C = BwdCfg<DKDV, D, CN>;
+  using C = BwdCfg<DKDV, D, CN, FQ>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
@@ -165,7 +210,7 @@ __global__ void __launch_bounds__(BwdCfg<DKDV, D, CN>::THREADS, BwdCfg<DKDV, D, 
 
   if (tid == 0) {
     mbar_init(bar(C::BAR_R), 1);
-    for (int s = 0; s < C::STAGES; ++s) {
+    for (int s = 0; s < C::RING; ++s) {
       mbar_init(bar(C::BAR_CF + s), 1);
       mbar_init(bar(C::BAR_CE + s), 1);
     }
@@ -175,6 +220,12 @@ __global__ void __launch_bounds__(BwdCfg<DKDV, D, CN>::THREADS, BwdCfg<DKDV, D, 
     mbar_init(bar(C::BAR_DSR), C::NCW);
     mbar_init(bar(C::BAR_AD), 1);
     mbar_init(bar(C::BAR_DRAIN), 1);
+    if constexpr (FQ) {
+      mbar_init(bar(C::BAR_DVD), 1);
+      mbar_init(bar(C::BAR_DQF), 1);
+      mbar_init(bar(C::BAR_DQE), C::NCW);
+    }
+    if constexpr (C::TA) mbar_init(bar(C::BAR_RT), 4 * C::RA_GROUPS);
     fence_barrier_init();
     misc[1] = 0;
   }
@@ -214,10 +265,13 @@ __global__ void __launch_bounds__(BwdCfg<DKDV, D, CN>::THREADS, BwdCfg<DKDV, D, 
     int issued = 0;
     uint32_t e[2];
     for (int j = 0; it.next(e, p.err); ++j) {
-      const int s = j % C::STAGES;
+      const int s = j % C::RING;
       bool ok = true;
-      if (lane == 0 && j >= C::STAGES)
-        ok = mbar_wait(bar(C::BAR_CE + s), ((j / C::STAGES) - 1) & 1, abort_flag, p.err);
+      if (lane == 0 && j >= C::RING)
+        ok = mbar_wait(bar(C::BAR_CE + s), ((j / C::RING) - 1) & 1, abort_flag, p.err);
+      // the ring slot over the resident tiles is free once they are in TMEM
+      if (C::TA && lane == 0 && j == C::STAGES && ok)
+        ok = mbar_wait(bar(C::BAR_RT), 0, abort_flag, p.err);
       if (!__shfl_sync(0xffffffffu, ok, 0)) break;
       __syncwarp();
       // first row of each 64-row half of the chunk; a missing half reads row
@@ -249,11 +303,11 @@ __global__ void __launch_bounds__(BwdCfg<DKDV, D, CN>::THREADS, BwdCfg<DKDV, D, 
         for (int pn = 0; pn < D / 64; ++pn)
 #pragma unroll
           for (int q = 0; q < C::CN / 64; ++q) {
-            const uint32_t off = s * C::CH_BYTES + pn * C::PANEL_C + q * (C::BOX * 128);
-            tma_load_4d(sbase + C::OFF_C0 + off, &tm_c0, bar(C::BAR_CF + s), pn * 64, prow[q], h,
-                        b);
-            tma_load_4d(sbase + C::OFF_C1 + off, &tm_c1, bar(C::BAR_CF + s), pn * 64, prow[q], h,
-                        b);
+            const uint32_t off = pn * C::PANEL_C + q * (C::BOX * 128);
+            tma_load_4d(sbase + C::c_off(s, 0) + off, &tm_c0, bar(C::BAR_CF + s), pn * 64,
+                        prow[q], h, b);
+            tma_load_4d(sbase + C::c_off(s, 1) + off, &tm_c1, bar(C::BAR_CF + s), pn * 64,
+                        prow[q], h, b);
           }
       }
       issued = j + 1;
@@ -261,8 +315,8 @@ __global__ void __launch_bounds__(BwdCfg<DKDV, D, CN>::THREADS, BwdCfg<DKDV, D, 
     if (lane == 0) {
       mbar_wait_drain(bar(C::BAR_R), 0);
       if (*abort_flag) {
-        for (int j = max(0, issued - C::STAGES); j < issued; ++j)
-          mbar_wait_drain(bar(C::BAR_CF + j % C::STAGES), (j / C::STAGES) & 1);
+        for (int j = max(0, issued - C::RING); j < issued; ++j)
+          mbar_wait_drain(bar(C::BAR_CF + j % C::RING), (j / C::RING) & 1);
       }
     }
   } else if (warp == C::MMA_WARP) {
@@ -272,16 +326,21 @@ __global__ void __launch_bounds__(BwdCfg<DKDV, D, CN>::THREADS, BwdCfg<DKDV, D, 
       it.init(p.indptr, p.indices, p.kind, p.nblocks, p.nnzb, row0, sub, p.bs, p.err, C::CN);
       // S (S^T) of chunk j:  R0 . C0_j^T;  dP (dP^T):  R1 . C1_j^T
       auto issue_sd = [&](int j, bool dp) {
-        const int s = j % C::STAGES;
+        const int s = j % C::RING;
         const uint32_t r = sbase + (dp ? C::OFF_R1 : C::OFF_R0);
-        const uint32_t c = sbase + (dp ? C::OFF_C1 : C::OFF_C0) + s * C::CH_BYTES;
+        const uint32_t c = sbase + C::c_off(s, dp ? 1 : 0);
         const uint32_t d = tbase + (dp ? C::COL_DP : C::COL_S);
         const uint64_t rd = sdesc_sw128(r, 16, 1024), cd = sdesc_sw128(c, 16, 1024);
+        // TA: A (Q or dO) from TMEM, k-step kk in columns 8 kk .. 8 kk + 7
+        const uint32_t ra = tbase + C::COL_RA + (dp ? D / 2 : 0);
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
           const uint32_t off = (kk >> 2) * C::PANEL_R + (kk & 3) * 32;
           const uint32_t offc = (kk >> 2) * C::PANEL_C + (kk & 3) * 32;
-          tc_mma(d, sdesc_add(rd, off), sdesc_add(cd, offc), C::IDESC_SC, kk > 0 ? 1u : 0u);
+          if constexpr (C::TA)
+            tc_mma_ts(d, ra + 8 * kk, sdesc_add(cd, offc), C::IDESC_SC, kk > 0 ? 1u : 0u);
+          else
+            tc_mma(d, sdesc_add(rd, off), sdesc_add(cd, offc), C::IDESC_SC, kk > 0 ? 1u : 0u);
         }
         tc_commit(bar(dp ? C::BAR_DPF : C::BAR_SF));
       };
@@ -295,7 +354,28 @@ __global__ void __launch_bounds__(BwdCfg<DKDV, D, CN>::THREADS, BwdCfg<DKDV, D, 
           tc_mma_ts(dt, at + a_col(kk), sdesc_add(cd, kk * 2048), C::IDESC_ACC,
                     (!first || kk > 0) ? 1u : 0u);
       };
+      // FQ: dQ_c^T = K^T dS_c^T into the dP columns (both operands MN-major,
+      // 16 keys per k-step), and dK += dS^T Q_c with the dS^T tile K-major
+      constexpr uint32_t PDS = C::BM * 128;   // one 64-query panel of the dS^T tile
+      auto issue_dq = [&](uint32_t dsb) {
+        const uint64_t kd = sdesc_sw128(sbase + C::OFF_R0, C::PANEL_R, 1024);
+        const uint64_t bd = sdesc_sw128(dsb, PDS, 1024);
+#pragma unroll
+        for (int kk = 0; kk < C::BM / 16; ++kk)
+          tc_mma(tbase + C::COL_DP, sdesc_add(kd, kk * 2048), sdesc_add(bd, kk * 2048),
+                 C::IDESC_DQ, kk > 0 ? 1u : 0u);
+      };
+      auto issue_dk = [&](uint32_t dsb, uint32_t cbase, bool first) {
+        const uint64_t ad = sdesc_sw128(dsb, 16, 1024);
+        const uint64_t cd = sdesc_sw128(cbase, C::PANEL_C, 1024);
+#pragma unroll
+        for (int kk = 0; kk < C::CN / 16; ++kk)
+          tc_mma(tbase + C::COL_ACC0, sdesc_add(ad, (kk >> 2) * PDS + (kk & 3) * 32),
+                 sdesc_add(cd, kk * 2048), C::IDESC_ACC, (!first || kk > 0) ? 1u : 0u);
+      };
       bool ok = mbar_wait(bar(C::BAR_R), 0, abort_flag, p.err);
+      // TA: the compute warps have put Q and dO into TMEM
+      if (C::TA && ok) ok = mbar_wait(bar(C::BAR_RT), 0, abort_flag, p.err);
       uint32_t e[2];
       bool has = ok && it.next(e, p.err);
       if (has) {
@@ -308,32 +388,42 @@ __global__ void __launch_bounds__(BwdCfg<DKDV, D, CN>::THREADS, BwdCfg<DKDV, D, 
       }
       for (int j = 0; ok && has; ++j) {
         const bool nxt = it.next(e, p.err);
-        const int s = j % C::STAGES;
-        const uint32_t c0 = sbase + C::OFF_C0 + s * C::CH_BYTES;
-        const uint32_t c1 = sbase + C::OFF_C1 + s * C::CH_BYTES;
+        const int s = j % C::RING;
+        const uint32_t c0 = sbase + C::c_off(s, 0);
+        const uint32_t c1 = sbase + C::c_off(s, 1);
         // P^T written (dK/dV) or S read (dQ)
         if (!mbar_wait(bar(C::BAR_PR), j & 1, abort_flag, p.err)) break;
         tc_fence_after();
         if (DKDV) issue_acc(C::COL_ACC1, C::COL_S, c1, j == 0);      // dV += P^T dO_c
+        if constexpr (FQ) tc_commit(bar(C::BAR_DVD));   // dO_c may take dS^T once dV is done
         // the next S goes in behind it if its operands already landed
         bool s_next = false;
-        if (nxt && mbar_try_wait(bar(C::BAR_CF + (j + 1) % C::STAGES), ((j + 1) / C::STAGES) & 1)) {
+        if (nxt && mbar_try_wait(bar(C::BAR_CF + (j + 1) % C::RING), ((j + 1) / C::RING) & 1)) {
           tc_fence_after();
           issue_sd(j + 1, false);
           s_next = true;
         }
         if (!mbar_wait(bar(C::BAR_DSR), j & 1, abort_flag, p.err)) break;
         tc_fence_after();
-        issue_acc(C::COL_ACC0, C::COL_DP, c0, j == 0);   // dK += dS^T Q_c  or  dQ += dS K_c
+        if constexpr (FQ) {
+          issue_dq(c1);                     // dQ_c^T = K^T dS_c^T
+          tc_commit(bar(C::BAR_DQF));
+          issue_dk(c1, c0, j == 0);         // dK += dS^T Q_c
+        } else {
+          issue_acc(C::COL_ACC0, C::COL_DP, c0, j == 0);   // dK += dS^T Q_c  or  dQ += dS K_c
+        }
         tc_commit(bar(C::BAR_CE + s));                    // chunk j's operands are consumed
         if (nxt) {
           if (!s_next) {
-            if (!mbar_wait(bar(C::BAR_CF + (j + 1) % C::STAGES), ((j + 1) / C::STAGES) & 1,
+            if (!mbar_wait(bar(C::BAR_CF + (j + 1) % C::RING), ((j + 1) / C::RING) & 1,
                            abort_flag, p.err))
               break;
             tc_fence_after();
             issue_sd(j + 1, false);
           }
+          // FQ: the next dP overwrites dQ_c once the compute warps have read it
+          if (FQ && !mbar_wait(bar(C::BAR_DQE), j & 1, abort_flag, p.err)) break;
+          tc_fence_after();
           issue_sd(j + 1, true);
         }
         has = nxt;
@@ -361,6 +451,34 @@ __global__ void __launch_bounds__(BwdCfg<DKDV, D, CN>::THREADS, BwdCfg<DKDV, D, 
       row_delta = in ? p.delta[static_cast<int64_t>(bh) * p.T + pos] : 0.f;
     }
     bool alive = true;
+    if constexpr (C::TA) {
+      // Q (grp < D / 64) or dO: one SW128 panel (64 columns of D) of this
+      // warp's 32 rows, unswizzled into 32 TMEM columns of bf16 pairs
+      if (grp < C::RA_GROUPS) {
+        if (!__all_sync(0xffffffffu, mbar_wait(bar(C::BAR_R), 0, abort_flag, p.err))) {
+          alive = false;
+        } else {
+          const int ten = grp / (D / 64), pn = grp % (D / 64);
+          const uint32_t src =
+              sbase + (ten ? C::OFF_R1 : C::OFF_R0) + pn * C::PANEL_R + r * 128;
+          uint32_t w[32];
+#pragma unroll
+          for (int u = 0; u < 8; ++u) {
+            const uint4 x = ld_shared_v4(src + ((u ^ (r & 7)) << 4));
+            w[4 * u] = x.x;
+            w[4 * u + 1] = x.y;
+            w[4 * u + 2] = x.z;
+            w[4 * u + 3] = x.w;
+          }
+          tmem_st32u(lane_base + C::COL_RA + ten * (D / 2) + pn * 32, w);
+          tmem_st_wait();
+          fence_proxy_async_smem();   // the tile's bytes are read before TMA refills them
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(bar(C::BAR_RT));
+        }
+      }
+    }
     int n = 0;
     ChunkPair<2> it;
     it.init(p.indptr, p.indices, p.kind, p.nblocks, p.nnzb, row0, sub, p.bs, p.err, C::CN);
@@ -385,10 +503,10 @@ __global__ void __launch_bounds__(BwdCfg<DKDV, D, CN>::THREADS, BwdCfg<DKDV, D, 
         else if (p.err)
           atomicOr(p.err, DEV_ERR_BAD_CSR);
       }
-      const float* ldj = ld + (j % C::STAGES) * (C::LD_BYTES / 4);
+      const float* ldj = ld + (j % C::RING) * (C::LD_BYTES / 4);
       // dK/dV reads the lse/delta the producer staged with this chunk
-      if (DKDV && !__all_sync(0xffffffffu, mbar_wait(bar(C::BAR_CF + j % C::STAGES),
-                                                     (j / C::STAGES) & 1, abort_flag, p.err))) {
+      if (DKDV && !__all_sync(0xffffffffu, mbar_wait(bar(C::BAR_CF + j % C::RING),
+                                                     (j / C::RING) & 1, abort_flag, p.err))) {
         alive = false;
         break;
       }
@@ -477,11 +595,59 @@ __global__ void __launch_bounds__(BwdCfg<DKDV, D, CN>::THREADS, BwdCfg<DKDV, D, 
           wd[k / 2 + 1] = pack_bf16(d[2], d[3]);
         }
       }
-      tmem_st16u(lane_base + C::COL_DP + col0, wd);
-      tmem_st_wait();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(bar(C::BAR_DSR));
+      if constexpr (FQ) {
+        // dS^T into this chunk's dO buffer (SW128, panels of 64 queries) once
+        // dV has read it: row r, chunk columns col0 .. col0 + 31
+        if (!__all_sync(0xffffffffu, mbar_wait(bar(C::BAR_DVD), j & 1, abort_flag, p.err))) {
+          alive = false;
+          break;
+        }
+        const uint32_t dsr = sbase + C::c_off(j % C::RING, 1) +
+                             (col0 >> 6) * (C::BM * 128) + r * 128;
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const uint32_t unit = static_cast<uint32_t>((col0 & 63) >> 3) + u;
+          st_shared_v4(dsr + ((unit ^ (r & 7u)) << 4),
+                       make_uint4(wd[4 * u], wd[4 * u + 1], wd[4 * u + 2], wd[4 * u + 3]));
+        }
+        fence_proxy_async_smem();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(bar(C::BAR_DSR));
+        // dQ_c^T: this lane's column quad * 32 + lane of D for the warp's
+        // chunk columns col0 .. col0 + 31 (queries cbase ..), read out of the
+        // dP columns, released, then added into dq_acc: each instruction adds
+        // 32 consecutive floats of one query's row
+        if (!__all_sync(0xffffffffu, mbar_wait(bar(C::BAR_DQF), j & 1, abort_flag, p.err))) {
+          alive = false;
+          break;
+        }
+        tc_fence_after();
+        float dq[32];
+        tmem_ld32(lane_base + C::COL_DP + col0, dq);
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(bar(C::BAR_DQE));
+        const int nq = min(C::CW, p.T - cbase);   // cbase = T for an absent half
+        if (nq > 0) {
+          float* dst =
+              p.dq_acc + (static_cast<int64_t>(bh) * p.T + cbase) * D + quad * 32 + lane;
+          if (nq == C::CW) {
+#pragma unroll
+            for (int i = 0; i < C::CW; ++i) red_add_f32(dst + i * D, dq[i]);
+          } else {
+#pragma unroll
+            for (int i = 0; i < C::CW; ++i)
+              if (i < nq) red_add_f32(dst + i * D, dq[i]);
+          }
+        }
+      } else {
+        tmem_st16u(lane_base + C::COL_DP + col0, wd);
+        tmem_st_wait();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(bar(C::BAR_DSR));
+      }
     }
     // ------------------------------------------------------------ epilogue
     // The accumulators leave through shared memory: each thread writes its

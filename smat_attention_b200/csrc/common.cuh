@@ -170,6 +170,14 @@ __device__ __forceinline__ void st_shared_v4(uint32_t addr, uint4 v) {
                "r"(v.z), "r"(v.w)
                : "memory");
 }
+__device__ __forceinline__ uint4 ld_shared_v4(uint32_t addr) {
+  uint4 v;
+  asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "r"(addr)
+               : "memory");
+  return v;
+}
 
 // ---------------------------------------------------------------- tcgen05
 __device__ __forceinline__ void tmem_alloc(uint32_t dst_smem, uint32_t ncols) {
@@ -536,6 +544,11 @@ __device__ __forceinline__ uint64_t fmul2(uint64_t a, uint64_t b) {
   uint64_t r;
   asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
   return r;
+}
+
+// *dst += a: a reduction in global memory (L2), no value returned
+__device__ __forceinline__ void red_add_f32(float* dst, float a) {
+  asm volatile("red.global.add.f32 [%0], %1;" ::"l"(dst), "f"(a) : "memory");
 }
 
 __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {

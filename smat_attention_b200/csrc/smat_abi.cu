@@ -290,13 +290,13 @@ struct DkdvSimt {
 };
 
 // ---------------------------------------------------------------- backward
-template <bool DKDV, int D, int CN>
+template <bool DKDV, int D, int CN, bool FQ = false>
 int bwd_tc_cn(const TArg& r0, const TArg& r1, const TArg& c0, const TArg& c1, const float* lse,
               const float* delta, const TArg& out0, const TArg* out1, int B, int H, int T,
               const int32_t* indptr, const int32_t* indices, const uint8_t* kind, int nblocks,
               int64_t nnzb, int block, float scale, const Work& work, const MdPattern& md,
-              int32_t* err, cudaStream_t s) {
-  using C = BwdCfg<DKDV, D, CN>;
+              int32_t* err, cudaStream_t s, float* dq_acc = nullptr) {
+  using C = BwdCfg<DKDV, D, CN, FQ>;
   CUtensorMap m0, m1, mc0, mc1, mo0, mo1;
   int rc;
   if ((rc = make_map(&m0, r0, B, H, T, D, C::BM))) return rc;
@@ -337,9 +337,10 @@ int bwd_tc_cn(const TArg& r0, const TArg& r1, const TArg& c0, const TArg& c1, co
   p.head_group = DKDV ? 16 : 1;
   p.scale = scale;
   p.scale_log2 = scale * 1.4426950408889634f;
+  p.dq_acc = dq_acc;
   p.err = err;
   p.md = md;
-  auto kern = smat_bwd_tc_kernel<DKDV, D, CN>;
+  auto kern = smat_bwd_tc_kernel<DKDV, D, CN, FQ>;
   if ((rc = set_smem(kern, C::SMEM_BYTES))) return rc;
   const int64_t grid = static_cast<int64_t>(work.items ? work.n : p.n_tiles) * B * H;
   if (grid == 0) return SMAT_OK;
@@ -347,6 +348,27 @@ int bwd_tc_cn(const TArg& r0, const TArg& r1, const TArg& c0, const TArg& c1, co
                                                                        p);
   return launch_status();
 }
+// dq = bf16(scale * acc), acc fp32 [B*H, T, D] contiguous; one thread per 8
+// elements (two 16-byte loads, one 16-byte store)
+template <int D>
+__global__ void __launch_bounds__(256) smat_dq_finish_kernel(const float* __restrict__ acc,
+                                                             __nv_bfloat16* __restrict__ dq,
+                                                             int64_t sb, int64_t sh, int64_t st,
+                                                             int H, int T, int64_t n8,
+                                                             float scale) {
+  const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i >= n8) return;
+  const int64_t row = i / (D / 8);
+  const int c = static_cast<int>(i % (D / 8)) * 8;
+  const int64_t bh = row / T;
+  const int t = static_cast<int>(row % T);
+  const float4* a = reinterpret_cast<const float4*>(acc + row * D + c);
+  const float4 x = __ldcs(a), y = __ldcs(a + 1);
+  *reinterpret_cast<uint4*>(dq + (bh / H) * sb + (bh % H) * sh + t * st + c) =
+      make_uint4(pack_bf16(x.x * scale, x.y * scale), pack_bf16(x.z * scale, x.w * scale),
+                 pack_bf16(y.x * scale, y.y * scale), pack_bf16(y.z * scale, y.w * scale));
+}
+
 // D = 64 with 64-row blocks: 64-row chunks, two CTAs per SM; otherwise
 // 128-row chunks.  The choice depends on (D, block) only, so launches with
 // and without a work list chunk alike.
@@ -370,7 +392,7 @@ int bwd_tc(const TArg& r0, const TArg& r1, const TArg& c0, const TArg& c1, const
 // ====================================================================== C ABI
 extern "C" {
 
-int smat_abi_version(void) { return 5; }
+int smat_abi_version(void) { return 6; }
 
 const char* smat_status_string(int status) {
   switch (status) {
@@ -804,6 +826,116 @@ int bwd_all(int dtype, const void* q, const int64_t* q_stride, const void* k,
   return SMAT_OK;
 }
 
+// The fused backward (bf16, D = 128): dK, dV and an fp32 dQ accumulator from
+// one kernel over the transposed CSR, then dQ = bf16(scale * acc).
+bool fused_dq_applies(int dtype, int D) { return dtype == SMAT_DTYPE_BF16 && D == 128; }
+
+int check_dq_acc(const float* dq_acc, int64_t dq_acc_floats, int B, int H, int T, int D) {
+  if (!dq_acc) return SMAT_ERR_NULL_POINTER;
+  if (reinterpret_cast<uintptr_t>(dq_acc) % 16) return SMAT_ERR_BAD_ALIGNMENT;
+  if (dq_acc_floats < static_cast<int64_t>(B) * H * T * D) return SMAT_ERR_BAD_SHAPE;
+  return SMAT_OK;
+}
+
+int dkdv_dq_impl(int dtype, const void* q, const int64_t* q_stride, const void* k,
+                 const int64_t* k_stride, const void* v, const int64_t* v_stride,
+                 const void* dout, const int64_t* do_stride, const float* lse, const float* delta,
+                 float* dq_acc, int64_t dq_acc_floats, void* dk, const int64_t* dk_stride,
+                 void* dv, const int64_t* dv_stride, int B, int H, int T, int D,
+                 const int32_t* t_indptr, const int32_t* t_indices, const uint8_t* t_kind,
+                 int nblocks, int64_t nnzb, int block, int t_max_row, float scale,
+                 const MdPattern& md, int32_t* err_word, void* stream, bool launch) {
+  int rc;
+  // the dK/dV checks cover every argument but the accumulator
+  if ((rc = dkdv_impl(dtype, q, q_stride, k, k_stride, v, v_stride, dout, do_stride, lse, delta,
+                      dk, dk_stride, dv, dv_stride, B, H, T, D, t_indptr, t_indices, t_kind,
+                      nblocks, nnzb, block, t_max_row, scale, kAllTiles, md, err_word, stream,
+                      false)))
+    return rc;
+  if (dtype != SMAT_DTYPE_BF16) return SMAT_ERR_UNSUPPORTED_DTYPE;
+  if (D != 128) return SMAT_ERR_UNSUPPORTED_D;
+  if ((rc = check_dq_acc(dq_acc, dq_acc_floats, B, H, T, D))) return rc;
+  if (!launch) return SMAT_OK;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (cudaMemsetAsync(dq_acc, 0, sizeof(float) * static_cast<size_t>(B) * H * T * D, s) !=
+      cudaSuccess)
+    return SMAT_ERR_LAUNCH;
+  const TArg tq = targ(q, q_stride), tk = targ(k, k_stride), tv = targ(v, v_stride),
+             td = targ(dout, do_stride), tdk = targ(dk, dk_stride), tdv = targ(dv, dv_stride);
+  return bwd_tc_cn<true, 128, 128, true>(tk, tv, tq, td, lse, delta, tdk, &tdv, B, H, T,
+                                         t_indptr, t_indices, t_kind, nblocks, nnzb, block, scale,
+                                         kAllTiles, md, err_word, s, dq_acc);
+}
+
+int dq_finish_impl(int dtype, const float* dq_acc, int64_t dq_acc_floats, void* dq,
+                   const int64_t* dq_stride, int B, int H, int T, int D, float scale,
+                   void* stream, bool launch) {
+  int rc;
+  if (!dq_stride) return SMAT_ERR_NULL_POINTER;
+  if ((rc = check_common(dtype, B, H, T, D, (T + 63) / 64, 64))) return rc;
+  if (dtype != SMAT_DTYPE_BF16) return SMAT_ERR_UNSUPPORTED_DTYPE;
+  if (D != 128 && D != 64) return SMAT_ERR_UNSUPPORTED_D;
+  const TArg tdq = targ(dq, dq_stride);
+  if ((rc = check_tensor(tdq, dtype))) return rc;
+  if ((rc = check_dq_acc(dq_acc, dq_acc_floats, B, H, T, D))) return rc;
+  if (!std::isfinite(scale) || scale <= 0.f) return SMAT_ERR_BAD_SHAPE;
+  if (!launch) return SMAT_OK;
+  const int64_t n8 = static_cast<int64_t>(B) * H * T * (D / 8);
+  if (n8 == 0) return SMAT_OK;
+  const unsigned grid = static_cast<unsigned>((n8 + 255) / 256);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  auto* out = static_cast<__nv_bfloat16*>(dq);
+  if (D == 128)
+    smat_dq_finish_kernel<128><<<grid, 256, 0, s>>>(dq_acc, out, tdq.sb, tdq.sh, tdq.st, H, T, n8,
+                                                    scale);
+  else
+    smat_dq_finish_kernel<64><<<grid, 256, 0, s>>>(dq_acc, out, tdq.sb, tdq.sh, tdq.st, H, T, n8,
+                                                   scale);
+  return launch_status();
+}
+
+// preprocess, fused dK/dV/dQ-accumulate, dQ finish; every pass is checked
+// before the first launches.  Layouts the fused kernel does not cover run the
+// two-kernel backward (dq_acc unused).
+int bwd_acc_all(int dtype, const void* q, const int64_t* q_stride, const void* k,
+                const int64_t* k_stride, const void* v, const int64_t* v_stride, const void* o,
+                const int64_t* o_stride, const void* dout, const int64_t* do_stride,
+                const float* lse, float* delta, void* dq, const int64_t* dq_stride, void* dk,
+                const int64_t* dk_stride, void* dv, const int64_t* dv_stride, int B, int H, int T,
+                int D, const int32_t* indptr, const int32_t* indices, const uint8_t* kind,
+                const int32_t* t_indptr, const int32_t* t_indices, const uint8_t* t_kind,
+                int nblocks, int64_t nnzb, int block, int max_row, int t_max_row,
+                const MdPattern& md, float* dq_acc, int64_t dq_acc_floats, float scale,
+                int32_t* err_word, void* stream) {
+  if (!fused_dq_applies(dtype, D))
+    return bwd_all(dtype, q, q_stride, k, k_stride, v, v_stride, o, o_stride, dout, do_stride, lse,
+                   delta, dq, dq_stride, dk, dk_stride, dv, dv_stride, B, H, T, D, indptr,
+                   indices, kind, t_indptr, t_indices, t_kind, nblocks, nnzb, block, max_row,
+                   t_max_row, scale, md, err_word, stream);
+  int rc;
+  for (int pass = 0; pass < 2; ++pass) {
+    const bool launch = pass == 1;
+    // the forward CSR is not read, but it is the caller's layout: check it too
+    if (!launch && (rc = dq_impl(dtype, q, q_stride, k, k_stride, v, v_stride, dout, do_stride,
+                                 lse, delta, dq, dq_stride, B, H, T, D, indptr, indices, kind,
+                                 nblocks, nnzb, block, max_row, scale, kAllTiles, md, err_word,
+                                 stream, false)))
+      return rc;
+    if (launch && (rc = pre_impl(dtype, o, o_stride, dout, do_stride, delta, B, H, T, D, 0, T,
+                                 stream)))
+      return rc;
+    if ((rc = dkdv_dq_impl(dtype, q, q_stride, k, k_stride, v, v_stride, dout, do_stride, lse,
+                           delta, dq_acc, dq_acc_floats, dk, dk_stride, dv, dv_stride, B, H, T, D,
+                           t_indptr, t_indices, t_kind, nblocks, nnzb, block, t_max_row, scale,
+                           md, err_word, stream, launch)))
+      return rc;
+    if ((rc = dq_finish_impl(dtype, dq_acc, dq_acc_floats, dq, dq_stride, B, H, T, D, scale,
+                             stream, launch)))
+      return rc;
+  }
+  return SMAT_OK;
+}
+
 }  // namespace
 
 extern "C" {
@@ -909,6 +1041,48 @@ int smat_bwd(int dtype, const void* q, const int64_t* q_stride, const void* k,
                  delta, dq, dq_stride, dk, dk_stride, dv, dv_stride, B, H, T, D, indptr, indices,
                  kind, t_indptr, t_indices, t_kind, nblocks, nnzb, block, max_row, t_max_row,
                  scale, kNoPattern, err_word, stream);
+}
+
+int smat_bwd_dkdv_dq(int dtype, const void* q, const int64_t* q_stride, const void* k,
+                     const int64_t* k_stride, const void* v, const int64_t* v_stride,
+                     const void* dout, const int64_t* do_stride, const float* lse,
+                     const float* delta, float* dq_acc, int64_t dq_acc_floats, void* dk,
+                     const int64_t* dk_stride, void* dv, const int64_t* dv_stride, int B, int H,
+                     int T, int D, const int32_t* t_indptr, const int32_t* t_indices,
+                     const uint8_t* t_kind, int nblocks, int64_t nnzb, int block, int t_max_row,
+                     float scale, int32_t* err_word, void* stream) {
+  return dkdv_dq_impl(dtype, q, q_stride, k, k_stride, v, v_stride, dout, do_stride, lse, delta,
+                      dq_acc, dq_acc_floats, dk, dk_stride, dv, dv_stride, B, H, T, D, t_indptr,
+                      t_indices, t_kind, nblocks, nnzb, block, t_max_row, scale, kNoPattern,
+                      err_word, stream, true);
+}
+
+int smat_bwd_dq_finish(int dtype, const float* dq_acc, int64_t dq_acc_floats, void* dq,
+                       const int64_t* dq_stride, int B, int H, int T, int D, float scale,
+                       void* stream) {
+  return dq_finish_impl(dtype, dq_acc, dq_acc_floats, dq, dq_stride, B, H, T, D, scale, stream,
+                        true);
+}
+
+int smat_bwd_acc(int dtype, const void* q, const int64_t* q_stride, const void* k,
+                 const int64_t* k_stride, const void* v, const int64_t* v_stride, const void* o,
+                 const int64_t* o_stride, const void* dout, const int64_t* do_stride,
+                 const float* lse, float* delta, void* dq, const int64_t* dq_stride, void* dk,
+                 const int64_t* dk_stride, void* dv, const int64_t* dv_stride, int B, int H,
+                 int T, int D, const int32_t* indptr, const int32_t* indices,
+                 const uint8_t* kind, const int32_t* t_indptr, const int32_t* t_indices,
+                 const uint8_t* t_kind, int nblocks, int64_t nnzb, int block, int max_row,
+                 int t_max_row, const smat_pattern_t* pattern, float* dq_acc,
+                 int64_t dq_acc_floats, float scale, int32_t* err_word, void* stream) {
+  MdPattern md = kNoPattern;
+  if (pattern) {
+    const int rc = check_pattern(pattern, T, true, &md);
+    if (rc) return rc;
+  }
+  return bwd_acc_all(dtype, q, q_stride, k, k_stride, v, v_stride, o, o_stride, dout, do_stride,
+                     lse, delta, dq, dq_stride, dk, dk_stride, dv, dv_stride, B, H, T, D, indptr,
+                     indices, kind, t_indptr, t_indices, t_kind, nblocks, nnzb, block, max_row,
+                     t_max_row, md, dq_acc, dq_acc_floats, scale, err_word, stream);
 }
 
 int smat_fwd_pattern(int dtype, const void* q, const int64_t* q_stride, const void* k,

@@ -21,7 +21,7 @@ def declared_symbols():
 
 def test_header_symbols_exported():
     syms = declared_symbols()
-    assert len(syms) == 29
+    assert len(syms) == 32
     L = _lib.lib()
     for s in syms:
         assert hasattr(L, s), s
@@ -30,7 +30,7 @@ def test_header_symbols_exported():
 
 def test_version_and_status_strings():
     L = _lib.lib()
-    assert L.smat_abi_version() == 5
+    assert L.smat_abi_version() == 6
     assert L.smat_status_string(0) == b"ok"
     assert b"CSR" in L.smat_status_string(7)
     assert L.smat_status_string(999) == b"unknown status"
