@@ -339,89 +339,155 @@ __global__ void __launch_bounds__(128) kattn_query_kernel(
 }
 
 // dphi[s, i] = dout[s, i] U_h^T and dU[s, h] = sum over rows i of type h of
-// phi[s, i]^T dout[s, i].  One CTA per (h, sequence); rows go QT_ROWS at a
-// time through shared memory (phi rows [QT_ROWS][RA], dout rows [QT_ROWS][PA]).
-// dU: thread = column p, 16 r at a time in registers, accumulated over the
-// row passes in shared memory [R][PA]; dphi: thread = r, walking U_h's row r.
-__global__ void __launch_bounds__(128) kattn_query_bwd_kernel(
+// phi[s, i]^T dout[s, i].  One CTA per (h, sequence), 128 threads per 384
+// dU blocks (below; 128 at r = 64, d_v = 64).  U_h goes
+// to shared memory [R][PU] once (PU = P rounded up to 4, plus 4 when that
+// makes an even count of 16-byte units, so rows 1 apart sit in different
+// bank groups); the rows of type h follow QT_ROWS at a time (phi [QT_ROWS][RA],
+// dout [QT_ROWS][PU]), all by asynchronous copies issued before one wait.
+// dU: a thread owns 4 x 4 blocks (4 r, 4 p; up to three blocks) accumulated
+// in registers over all passes, each row adding one 16-byte phi load and one
+// 16-byte dout load per 16 FMAs; at the end the blocks go through shared
+// memory (over U_h) and leave in row order.  dphi: a thread owns 2 rows x 4 r
+// (r = r0 + 16 k), each 16-byte step along p loading two dout and four U_h
+// vectors for 32 FMAs.
+constexpr int QB_MAXB = 3;         // dU blocks per thread
+constexpr int QB_MAXTHREADS = 512;  // (RA / 4) (PU / 4) <= QB_MAXB * 512
+
+__host__ __device__ inline int query_pu(int P) {
+  const int pu = round_up(P, 4);
+  return ((pu / 4) % 2 == 0) ? pu + 4 : pu;
+}
+
+__global__ void __launch_bounds__(QB_MAXTHREADS) kattn_query_bwd_kernel(
     const float* __restrict__ phi, int64_t phi_sb, const float* __restrict__ U,
     const float* __restrict__ dout, int64_t dout_sb, float* __restrict__ dphi, int64_t dphi_sb,
     float* __restrict__ dU, int T_R, int R, int P, int nU) {
   extern __shared__ float4 sm4[];
-  const int RA = round_up(R, 4), PA = round_up(P, 4);
-  float* sph = reinterpret_cast<float*>(sm4);   // [QT_ROWS][RA]
-  float* sdo = sph + QT_ROWS * RA;              // [QT_ROWS][PA]
-  float* sdu = sdo + QT_ROWS * PA;              // [R][PA]
-  const int h = blockIdx.x, s = blockIdx.y;
+  const int RA = round_up(R, 4), PU = query_pu(P);
+  float* su = reinterpret_cast<float*>(sm4);    // [RA][PU] = U_h (zero-padded)
+  float* sph = su + RA * PU;                    // [QT_ROWS][RA]
+  float* sdo = sph + QT_ROWS * RA;              // [QT_ROWS][PU]
+  const int h = blockIdx.x, s = blockIdx.y, tid = threadIdx.x;
   const float* Uh = U + (static_cast<int64_t>(s) * nU + h) * R * P;
   float* dUh = dU + (static_cast<int64_t>(s) * nU + h) * R * P;
+  const float* ph = phi + s * phi_sb;
+  const float* dos = dout + s * dout_sb;
+  for (int e = tid; e < RA * PU; e += blockDim.x) {
+    const int r = e / PU, c = e % PU;
+    const bool in = r < R && c < P;
+    cp_async4(smem_u32(su + e), in ? Uh + r * P + c : Uh, in ? 4u : 0u);
+  }
   const int n_rows = h < T_R ? (T_R - h + nU - 1) / nU : 0;
-  for (int e = threadIdx.x; e < R * PA; e += blockDim.x) sdu[e] = 0.f;
+  const int nbp = PU / 4, nblk = (RA / 4) * nbp;
+  float acc[QB_MAXB][4][4];
+#pragma unroll
+  for (int k = 0; k < QB_MAXB; ++k)
+#pragma unroll
+    for (int a = 0; a < 4; ++a)
+#pragma unroll
+      for (int c = 0; c < 4; ++c) acc[k][a][c] = 0.f;
+  const bool vec_phi = (R & 3) == 0 && al16d(ph) && ((nU * static_cast<int64_t>(R)) & 3) == 0;
   for (int g0 = 0; g0 < n_rows; g0 += QT_ROWS) {
     const int ng = min(QT_ROWS, n_rows - g0);
-    __syncthreads();
-    for (int e = threadIdx.x; e < QT_ROWS * RA; e += blockDim.x) {
-      const int i = e / RA, r = e % RA;
-      const int64_t row = h + (g0 + i) * static_cast<int64_t>(nU);
-      sph[e] = (i < ng && r < R) ? phi[s * phi_sb + row * R + r] : 0.f;
+    if (g0 > 0) __syncthreads();   // the previous pass has finished with sph / sdo
+    if (vec_phi) {
+      for (int e = tid * 4; e < QT_ROWS * RA; e += blockDim.x * 4) {
+        const int i = e / RA;
+        if (i < ng)
+          cp_async16(smem_u32(sph + e),
+                     ph + static_cast<int64_t>(h + (g0 + i) * static_cast<int64_t>(nU)) * R +
+                         e % RA);
+        else
+          *reinterpret_cast<float4*>(sph + e) = make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+    } else {
+      for (int e = tid; e < QT_ROWS * RA; e += blockDim.x) {
+        const int i = e / RA, r = e % RA;
+        const bool in = i < ng && r < R;
+        cp_async4(smem_u32(sph + e),
+                  in ? ph + static_cast<int64_t>(h + (g0 + i) * static_cast<int64_t>(nU)) * R + r
+                     : ph,
+                  in ? 4u : 0u);
+      }
     }
-    for (int e = threadIdx.x; e < QT_ROWS * PA; e += blockDim.x) {
-      const int i = e / PA, p = e % PA;
-      const int64_t row = h + (g0 + i) * static_cast<int64_t>(nU);
-      sdo[e] = (i < ng && p < P) ? dout[s * dout_sb + row * P + p] : 0.f;
+    for (int e = tid; e < QT_ROWS * PU; e += blockDim.x) {
+      const int i = e / PU, c = e % PU;
+      const bool in = i < ng && c < P;
+      cp_async4(smem_u32(sdo + e),
+                in ? dos + static_cast<int64_t>(h + (g0 + i) * static_cast<int64_t>(nU)) * P + c
+                   : dos,
+                in ? 4u : 0u);
     }
+    cp_async_wait_all();
     __syncthreads();
-    // dU: column p, 16 r per round
-    for (int p = threadIdx.x; p < P; p += blockDim.x) {
-      for (int r0 = 0; r0 < R; r0 += 16) {
-        float acc[16];
+    // dU blocks
 #pragma unroll
-        for (int j = 0; j < 16; ++j) acc[j] = 0.f;
+    for (int k = 0; k < QB_MAXB; ++k) {
+      const int bk = tid + k * blockDim.x;
+      if (bk < nblk) {
+        const int r0 = (bk / nbp) * 4, p0 = (bk % nbp) * 4;
         for (int i = 0; i < ng; ++i) {
-          const float d = sdo[i * PA + p];
+          const float4 a = *reinterpret_cast<const float4*>(sph + i * RA + r0);
+          const float4 v = *reinterpret_cast<const float4*>(sdo + i * PU + p0);
+          const float av[4] = {a.x, a.y, a.z, a.w}, vv[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
-          for (int j = 0; j < 16; j += 4) {
-            if (r0 + j < RA) {
-              const float4 x = *reinterpret_cast<const float4*>(sph + i * RA + r0 + j);
-              acc[j] = fmaf(x.x, d, acc[j]);
-              acc[j + 1] = fmaf(x.y, d, acc[j + 1]);
-              acc[j + 2] = fmaf(x.z, d, acc[j + 2]);
-              acc[j + 3] = fmaf(x.w, d, acc[j + 3]);
+          for (int aa = 0; aa < 4; ++aa)
+#pragma unroll
+            for (int c = 0; c < 4; ++c) acc[k][aa][c] = fmaf(av[aa], vv[c], acc[k][aa][c]);
+        }
+      }
+    }
+    // dphi: rows 2 ib, 2 ib + 1 of this pass, r = rl + 16 kk
+    const int rl = tid & 15;
+    for (int ib = tid >> 4; 2 * ib < ng; ib += blockDim.x >> 4) {
+      for (int rb = 0; rb < RA; rb += 64) {
+        float o[2][4] = {};
+        for (int q = 0; q < PU; q += 4) {
+          const float4 d0 = *reinterpret_cast<const float4*>(sdo + (2 * ib) * PU + q);
+          const float4 d1 = *reinterpret_cast<const float4*>(sdo + (2 * ib + 1) * PU + q);
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk) {
+            const int r = rb + rl + 16 * kk;
+            if (r < RA) {
+              const float4 u = *reinterpret_cast<const float4*>(su + r * PU + q);
+              o[0][kk] += d0.x * u.x + d0.y * u.y + d0.z * u.z + d0.w * u.w;
+              o[1][kk] += d1.x * u.x + d1.y * u.y + d1.z * u.z + d1.w * u.w;
             }
           }
         }
 #pragma unroll
-        for (int j = 0; j < 16; ++j)
-          if (r0 + j < R) sdu[(r0 + j) * PA + p] += acc[j];
-      }
-    }
-    // dphi: row r of U_h against each dout row
-    for (int r = threadIdx.x; r < R; r += blockDim.x) {
-      float acc[QT_ROWS];
+        for (int a = 0; a < 2; ++a) {
+          const int i = 2 * ib + a;
+          if (i < ng) {
+            float* drow = dphi + s * dphi_sb +
+                          static_cast<int64_t>(h + (g0 + i) * static_cast<int64_t>(nU)) * R;
 #pragma unroll
-      for (int i = 0; i < QT_ROWS; ++i) acc[i] = 0.f;
-      const float* ur = Uh + static_cast<int64_t>(r) * P;
-      for (int p0 = 0; p0 < PA; p0 += 4) {
-        float u[4];
-#pragma unroll
-        for (int j = 0; j < 4; ++j) u[j] = (p0 + j < P) ? __ldg(ur + p0 + j) : 0.f;
-#pragma unroll
-        for (int i = 0; i < QT_ROWS; ++i) {
-          const float4 d = *reinterpret_cast<const float4*>(sdo + i * PA + p0);
-          acc[i] = fmaf(d.x, u[0], acc[i]);
-          acc[i] = fmaf(d.y, u[1], acc[i]);
-          acc[i] = fmaf(d.z, u[2], acc[i]);
-          acc[i] = fmaf(d.w, u[3], acc[i]);
+            for (int kk = 0; kk < 4; ++kk) {
+              const int r = rb + rl + 16 * kk;
+              if (r < R) drow[r] = o[a][kk];
+            }
+          }
         }
       }
+    }
+  }
+  cp_async_wait_all();   // a type without rows still drains its U_h copy
+  __syncthreads();       // every thread is done reading su
+  // dU: the register blocks over U_h's shared memory, then out in row order
 #pragma unroll
-      for (int i = 0; i < QT_ROWS; ++i)
-        if (i < ng)
-          dphi[s * dphi_sb + (h + (g0 + i) * static_cast<int64_t>(nU)) * R + r] = acc[i];
+  for (int k = 0; k < QB_MAXB; ++k) {
+    const int bk = tid + k * blockDim.x;
+    if (bk < nblk) {
+      const int r0 = (bk / nbp) * 4, p0 = (bk % nbp) * 4;
+#pragma unroll
+      for (int aa = 0; aa < 4; ++aa)
+        *reinterpret_cast<float4*>(su + (r0 + aa) * PU + p0) =
+            make_float4(acc[k][aa][0], acc[k][aa][1], acc[k][aa][2], acc[k][aa][3]);
     }
   }
   __syncthreads();
-  for (int e = threadIdx.x; e < R * P; e += blockDim.x) dUh[e] = sdu[(e / P) * PA + e % P];
+  for (int e = tid; e < R * P; e += blockDim.x) dUh[e] = su[(e / P) * PU + e % P];
 }
 
 cudaStream_t st(void* s) { return static_cast<cudaStream_t>(s); }
@@ -505,13 +571,15 @@ int smat_kattn_query_by_type_bwd(const float* phi, int64_t phi_seq_stride, const
   if (nb < 1 || nb > 65535 || T_R < 0 || R < 1 || P < 1 || nU < 1 || phi_seq_stride < 0 ||
       dout_seq_stride < 0 || dphi_seq_stride < 0)
     return SMAT_ERR_BAD_SHAPE;
-  const int RA = round_up(R, 4), PA = round_up(P, 4);
-  const int smem = (QT_ROWS * (RA + PA) + R * PA) * 4;
-  if (smem > GLUE_SMEM_MAX) return SMAT_ERR_BAD_SHAPE;
+  const int RA = round_up(R, 4), PU = query_pu(P);
+  const int smem = (RA * PU + QT_ROWS * (RA + PU)) * 4;
+  const int nblk = (RA / 4) * (PU / 4);
+  if (smem > GLUE_SMEM_MAX || nblk > QB_MAXB * QB_MAXTHREADS) return SMAT_ERR_BAD_SHAPE;
+  const int threads = 128 * ((nblk + QB_MAXB * 128 - 1) / (QB_MAXB * 128));
   int rc = allow_smem(kattn_query_bwd_kernel, smem);
   if (rc) return rc;
   // every type gets a CTA: types without rows write dU_h = 0
-  kattn_query_bwd_kernel<<<dim3(nU, nb), 128, smem, st(stream)>>>(
+  kattn_query_bwd_kernel<<<dim3(nU, nb), threads, smem, st(stream)>>>(
       phi, phi_seq_stride, U, dout, dout_seq_stride, dphi, dphi_seq_stride, dU, T_R, R, P, nU);
   return launch_ok();
 }
