@@ -73,6 +73,35 @@ def test_bwd_rejects_on_host():
     assert L.smat_bwd_preprocess(1, 16, st, 16, st, None, 1, 1, 128, 64, None) == 8
 
 
+def test_fused_dq_entry_points_reject_on_host():
+    """smat_bwd_dkdv_dq / smat_bwd_dq_finish: bf16 at D = 128 only (finish: D
+    64 or 128), the accumulator non-null, 16-byte aligned and B*H*T*D floats
+    long; every check runs before the device is touched."""
+    L = _lib.lib()
+    st = (ctypes.c_int64 * 3)(0, 0, 128)
+    n = 128 * 128
+
+    def dkdv_dq(dtype=1, D=128, acc=16, n_acc=n):
+        return L.smat_bwd_dkdv_dq(dtype, 16, st, 16, st, 16, st, 16, st, 16, 16, acc, n_acc,
+                                  16, st, 16, st, 1, 1, 128, D, 16, 16, 16, 2, 3, 64, 2,
+                                  0.125, None, None)
+
+    assert dkdv_dq(acc=None) == 8                   # SMAT_ERR_NULL_POINTER
+    assert dkdv_dq(acc=24) == 6                     # SMAT_ERR_BAD_ALIGNMENT
+    assert dkdv_dq(n_acc=n - 1) == 1                # SMAT_ERR_BAD_SHAPE
+    assert dkdv_dq(dtype=0) == 4                    # fp32: SMAT_ERR_UNSUPPORTED_DTYPE
+    st64 = (ctypes.c_int64 * 3)(0, 0, 64)
+    assert L.smat_bwd_dkdv_dq(1, 16, st64, 16, st64, 16, st64, 16, st64, 16, 16, 16, n, 16,
+                              st64, 16, st64, 1, 1, 128, 64, 16, 16, 16, 2, 3, 64, 2, 0.125,
+                              None, None) == 2      # D = 64: SMAT_ERR_UNSUPPORTED_D
+    fin = lambda dtype=1, D=128, acc=16, stride=st: L.smat_bwd_dq_finish(
+        dtype, acc, n, 16, stride, 1, 1, 128, D, 0.125, None)
+    assert fin(dtype=0) == 4
+    assert fin(D=96) == 2
+    assert fin(acc=None) == 8
+    assert fin(stride=None) == 8
+
+
 def test_work_list_entry_points_reject_on_host():
     L = _lib.lib()
     st = (ctypes.c_int64 * 3)(4 * 1024 * 64, 1024 * 64, 64)
