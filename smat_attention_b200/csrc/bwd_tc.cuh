@@ -518,6 +518,12 @@ __global__ void __launch_bounds__(BwdCfg<DKDV, D, CN, FQ>::THREADS,
       // ---- P (P^T): 32 columns of S
       float pv[C::CW];
       tmem_ld32(lane_base + C::COL_S + col0, pv);
+      if (!DKDV) {
+        // dQ keeps P in registers: S's columns are free for the next S now
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(bar(C::BAR_PR));
+      }
       // warp-uniform: no element of this warp's 32 x 32 block is masked
       const bool all_valid = (st == ST_FULL) && (!DKDV || cbase + C::CW <= p.T);
       const float4* l4 = reinterpret_cast<const float4*>(ldj + col0);
@@ -553,10 +559,10 @@ __global__ void __launch_bounds__(BwdCfg<DKDV, D, CN, FQ>::THREADS,
         for (int i = 0; i < C::CW / 2; ++i) wp[i] = pack_bf16(pv[2 * i], pv[2 * i + 1]);
         tmem_st16u(lane_base + C::COL_S + col0, wp);
         tmem_st_wait();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(bar(C::BAR_PR));
       }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(bar(C::BAR_PR));
       // ---- dS (dS^T) = P (dP - delta)
       if (!__all_sync(0xffffffffu, mbar_wait(bar(C::BAR_DPF), j & 1, abort_flag, p.err))) {
         alive = false;
