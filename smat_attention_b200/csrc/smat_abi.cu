@@ -631,7 +631,7 @@ int fwd_impl(int dtype, const void* q, const int64_t* q_stride, const void* k,
   if (!std::isfinite(scale) || scale <= 0.f) return SMAT_ERR_BAD_SHAPE;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (dtype == SMAT_DTYPE_BF16) {
-    // D = 64: one tile per CTA; 64-key chunks and three CTAs per SM with
+    // D = 64: one tile per CTA; 64-key chunks and four CTAs per SM with
     // 64-row blocks, else 128-key chunks and two (with or without a work
     // list, so that both launches group a tile's keys into the same chunks)
     if (D == 64 && block == 64)
