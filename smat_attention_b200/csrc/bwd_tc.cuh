@@ -20,9 +20,10 @@
 // nearly as many cycles as an N = 128 one, so the chunk is 128 wide.  TMEM
 // (512 columns) then holds one S, one dP and the accumulators, so S and dP
 // are single-buffered and the hand-offs are split to keep the tensor core
-// fed: as soon as P (P^T) is ready the MMA warp issues dV and the next S;
-// as soon as dS is ready it issues dK (or dQ) and the next dP.  The compute
-// warps turn dP into dS while the tensor core runs dV and the next S.
+// fed: as soon as P^T is in TMEM (dK/dV), or S has been read (dQ, which
+// keeps P in registers), the MMA warp issues dV and the next S; as soon as
+// dS is ready it issues dK (or dQ) and the next dP.  The compute warps turn
+// dP into dS while the tensor core runs dV and the next S.
 // With bs = 64 a chunk is two 64-row blocks of the merged list (TMA loads
 // each half separately; a missing second half is loaded from row T, i.e.
 // zero-filled, and masked).  A warp's 32 x 32 block is masked by one 32-bit
