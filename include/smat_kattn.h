@@ -119,9 +119,7 @@ SMAT_API int smat_kattn_query_by_type(const float* phi, int64_t phi_seq_stride, 
 
 /* Its backward: dphi[s, i] = dout[s, i] U[s, i mod nU]^T (written) and
  * dU[s, h] = sum over the rows i of type h of phi[s, i]^T dout[s, i] (written,
- * zero for a type without rows); strides as above.  ceil(R / 4) times
- * ceil(P' / 4) <= 1536, P' = P rounded up to 4 (and up by 4 more when that
- * is a multiple of 8), else SMAT_ERR_BAD_SHAPE (R = P = 150 fits). */
+ * zero for a type without rows); strides as above. */
 SMAT_API int smat_kattn_query_by_type_bwd(const float* phi, int64_t phi_seq_stride,
                                           const float* U, const float* dout,
                                           int64_t dout_seq_stride, float* dphi,

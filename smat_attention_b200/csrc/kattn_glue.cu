@@ -339,27 +339,26 @@ __global__ void __launch_bounds__(128) kattn_query_kernel(
 }
 
 // dphi[s, i] = dout[s, i] U_h^T and dU[s, h] = sum over rows i of type h of
-// phi[s, i]^T dout[s, i].  One CTA per (h, sequence), 128 threads per 384
-// dU blocks (below; 128 at r = 64, d_v = 64).  U_h goes
-// to shared memory [R][PU] once (PU = P rounded up to 4, plus 4 when that
-// makes an even count of 16-byte units, so rows 1 apart sit in different
-// bank groups); the rows of type h follow QT_ROWS at a time (phi [QT_ROWS][RA],
-// dout [QT_ROWS][PU]), all by asynchronous copies issued before one wait.
-// dU: a thread owns 4 x 4 blocks (4 r, 4 p; up to three blocks) accumulated
-// in registers over all passes, each row adding one 16-byte phi load and one
-// 16-byte dout load per 16 FMAs; at the end the blocks go through shared
-// memory (over U_h) and leave in row order.  dphi: a thread owns 2 rows x 4 r
+// phi[s, i]^T dout[s, i].  One CTA of 128 threads per (h, sequence), at most
+// 64 registers a thread so that eight CTAs share an SM: a CTA loads U_h,
+// computes and stores in turn, and more resident CTAs keep more of those
+// loads in flight.  U_h goes to shared memory [RA][PU] once (PU = P rounded
+// up to 4, plus 4 when that makes an even count of 16-byte units, so rows 1
+// apart sit in different bank groups); the rows of type h follow QT_ROWS at
+// a time (phi [QT_ROWS][RA], dout [QT_ROWS][PU]), all by asynchronous copies
+// issued before one wait.  Per pass, dphi: a thread owns 2 rows x 4 r
 // (r = r0 + 16 k), each 16-byte step along p loading two dout and four U_h
-// vectors for 32 FMAs.
-constexpr int QB_MAXB = 3;         // dU blocks per thread
-constexpr int QB_MAXTHREADS = 512;  // (RA / 4) (PU / 4) <= QB_MAXB * 512
+// vectors for 32 FMAs; dU: 4 x 4 blocks (4 r, 4 p), one at a time per
+// thread, each row adding one 16-byte phi load and one 16-byte dout load per
+// 16 FMAs, the block then stored to dU (added on later passes: a block
+// belongs to one thread).
 
 __host__ __device__ inline int query_pu(int P) {
   const int pu = round_up(P, 4);
   return ((pu / 4) % 2 == 0) ? pu + 4 : pu;
 }
 
-__global__ void __launch_bounds__(QB_MAXTHREADS) kattn_query_bwd_kernel(
+__global__ void __launch_bounds__(128, 8) kattn_query_bwd_kernel(
     const float* __restrict__ phi, int64_t phi_sb, const float* __restrict__ U,
     const float* __restrict__ dout, int64_t dout_sb, float* __restrict__ dphi, int64_t dphi_sb,
     float* __restrict__ dU, int T_R, int R, int P, int nU) {
@@ -373,20 +372,17 @@ __global__ void __launch_bounds__(QB_MAXTHREADS) kattn_query_bwd_kernel(
   float* dUh = dU + (static_cast<int64_t>(s) * nU + h) * R * P;
   const float* ph = phi + s * phi_sb;
   const float* dos = dout + s * dout_sb;
+  const int n_rows = h < T_R ? (T_R - h + nU - 1) / nU : 0;
+  if (n_rows == 0) {   // a type without rows: dU_h = 0
+    for (int e = tid; e < R * P; e += blockDim.x) dUh[e] = 0.f;
+    return;
+  }
   for (int e = tid; e < RA * PU; e += blockDim.x) {
     const int r = e / PU, c = e % PU;
     const bool in = r < R && c < P;
     cp_async4(smem_u32(su + e), in ? Uh + r * P + c : Uh, in ? 4u : 0u);
   }
-  const int n_rows = h < T_R ? (T_R - h + nU - 1) / nU : 0;
   const int nbp = PU / 4, nblk = (RA / 4) * nbp;
-  float acc[QB_MAXB][4][4];
-#pragma unroll
-  for (int k = 0; k < QB_MAXB; ++k)
-#pragma unroll
-    for (int a = 0; a < 4; ++a)
-#pragma unroll
-      for (int c = 0; c < 4; ++c) acc[k][a][c] = 0.f;
   const bool vec_phi = (R & 3) == 0 && al16d(ph) && ((nU * static_cast<int64_t>(R)) & 3) == 0;
   for (int g0 = 0; g0 < n_rows; g0 += QT_ROWS) {
     const int ng = min(QT_ROWS, n_rows - g0);
@@ -421,24 +417,7 @@ __global__ void __launch_bounds__(QB_MAXTHREADS) kattn_query_bwd_kernel(
     }
     cp_async_wait_all();
     __syncthreads();
-    // dU blocks
-#pragma unroll
-    for (int k = 0; k < QB_MAXB; ++k) {
-      const int bk = tid + k * blockDim.x;
-      if (bk < nblk) {
-        const int r0 = (bk / nbp) * 4, p0 = (bk % nbp) * 4;
-        for (int i = 0; i < ng; ++i) {
-          const float4 a = *reinterpret_cast<const float4*>(sph + i * RA + r0);
-          const float4 v = *reinterpret_cast<const float4*>(sdo + i * PU + p0);
-          const float av[4] = {a.x, a.y, a.z, a.w}, vv[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-          for (int aa = 0; aa < 4; ++aa)
-#pragma unroll
-            for (int c = 0; c < 4; ++c) acc[k][aa][c] = fmaf(av[aa], vv[c], acc[k][aa][c]);
-        }
-      }
-    }
-    // dphi: rows 2 ib, 2 ib + 1 of this pass, r = rl + 16 kk
+    // dphi: rows 2 ib, 2 ib + 1 of this pass, r = rb + rl + 16 kk
     const int rl = tid & 15;
     for (int ib = tid >> 4; 2 * ib < ng; ib += blockDim.x >> 4) {
       for (int rb = 0; rb < RA; rb += 64) {
@@ -471,23 +450,30 @@ __global__ void __launch_bounds__(QB_MAXTHREADS) kattn_query_bwd_kernel(
         }
       }
     }
-  }
-  cp_async_wait_all();   // a type without rows still drains its U_h copy
-  __syncthreads();       // every thread is done reading su
-  // dU: the register blocks over U_h's shared memory, then out in row order
-#pragma unroll
-  for (int k = 0; k < QB_MAXB; ++k) {
-    const int bk = tid + k * blockDim.x;
-    if (bk < nblk) {
+    // dU blocks of this pass
+    for (int bk = tid; bk < nblk; bk += blockDim.x) {
       const int r0 = (bk / nbp) * 4, p0 = (bk % nbp) * 4;
+      float acc[4][4] = {};
+      for (int i = 0; i < ng; ++i) {
+        const float4 a = *reinterpret_cast<const float4*>(sph + i * RA + r0);
+        const float4 v = *reinterpret_cast<const float4*>(sdo + i * PU + p0);
+        const float av[4] = {a.x, a.y, a.z, a.w}, vv[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
-      for (int aa = 0; aa < 4; ++aa)
-        *reinterpret_cast<float4*>(su + (r0 + aa) * PU + p0) =
-            make_float4(acc[k][aa][0], acc[k][aa][1], acc[k][aa][2], acc[k][aa][3]);
+        for (int aa = 0; aa < 4; ++aa)
+#pragma unroll
+          for (int c = 0; c < 4; ++c) acc[aa][c] = fmaf(av[aa], vv[c], acc[aa][c]);
+      }
+#pragma unroll
+      for (int aa = 0; aa < 4; ++aa) {
+        if (r0 + aa < R) {
+          float* drow = dUh + (r0 + aa) * P;
+#pragma unroll
+          for (int c = 0; c < 4; ++c)
+            if (p0 + c < P) drow[p0 + c] = g0 == 0 ? acc[aa][c] : drow[p0 + c] + acc[aa][c];
+        }
+      }
     }
   }
-  __syncthreads();
-  for (int e = tid; e < R * P; e += blockDim.x) dUh[e] = su[(e / P) * PU + e % P];
 }
 
 cudaStream_t st(void* s) { return static_cast<cudaStream_t>(s); }
@@ -573,13 +559,11 @@ int smat_kattn_query_by_type_bwd(const float* phi, int64_t phi_seq_stride, const
     return SMAT_ERR_BAD_SHAPE;
   const int RA = round_up(R, 4), PU = query_pu(P);
   const int smem = (RA * PU + QT_ROWS * (RA + PU)) * 4;
-  const int nblk = (RA / 4) * (PU / 4);
-  if (smem > GLUE_SMEM_MAX || nblk > QB_MAXB * QB_MAXTHREADS) return SMAT_ERR_BAD_SHAPE;
-  const int threads = 128 * ((nblk + QB_MAXB * 128 - 1) / (QB_MAXB * 128));
+  if (smem > GLUE_SMEM_MAX) return SMAT_ERR_BAD_SHAPE;
   int rc = allow_smem(kattn_query_bwd_kernel, smem);
   if (rc) return rc;
   // every type gets a CTA: types without rows write dU_h = 0
-  kattn_query_bwd_kernel<<<dim3(nU, nb), threads, smem, st(stream)>>>(
+  kattn_query_bwd_kernel<<<dim3(nU, nb), 128, smem, st(stream)>>>(
       phi, phi_seq_stride, U, dout, dout_seq_stride, dphi, dphi_seq_stride, dU, T_R, R, P, nU);
   return launch_ok();
 }
