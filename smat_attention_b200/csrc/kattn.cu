@@ -390,14 +390,22 @@ __global__ void __launch_bounds__(192, (TileCfg<MODE, R, PN>::MIN_BLOCKS))
 
 // ---------------------------------------------------------------- pool
 // One CTA per (profile x, b).  The profile's columns (about n_X / N0, 16 at
-// c3 sizes) are staged in shared memory -- psi rows [POOL_MAXG][RR] and vb
-// rows [POOL_MAXG][SP], zero-padded to multiples of 4 -- and each thread
+// c3 sizes) are staged in shared memory -- psi rows [mg][RR] and vb rows
+// [mg][SP], mg = that count rounded up to 4 (at most POOL_MAXG), zero-padded
+// to multiples of 4 -- and each thread
 // accumulates 4 x 4 tiles of the R x P outer-product sum in registers (two
 // 16-byte shared loads per 16 FMAs, columns in order, so the sum is the same
 // sequence of fmaf as a scalar loop).  The tile goes back to global memory
 // through shared memory as one contiguous run of R P floats.
-constexpr int POOL_MAXG = 64;   // columns staged per round
+constexpr int POOL_MAXG = 64;   // columns staged per round at most
 constexpr int POOL_SMEM_MAX = 200 * 1024;
+
+// columns staged per round: a profile's column count, rounded up to 4, up to
+// POOL_MAXG (shared memory sized to it, so more CTAs share an SM)
+inline int pool_round(int n_P, int n, int N0) {
+  const int gmax = std::max(1, std::min(POOL_MAXG, (n - n_P + N0 - 1) / N0));
+  return (gmax + 3) & ~3;
+}
 
 // Row stride of a zero-padded shared row of P floats: a multiple of 4 whose
 // count of 16-byte units is odd, so 8 consecutive rows hit 8 distinct bank
@@ -411,14 +419,14 @@ __host__ __device__ inline int pool_stride(int P) {
 __global__ void __launch_bounds__(256) kattn_pool_kernel(const float* __restrict__ psi,
                                                          const float* __restrict__ vb,
                                                          float* __restrict__ F, int T, int R,
-                                                         int P, int n_P, int n, int N0) {
+                                                         int P, int n_P, int n, int N0, int mg) {
   extern __shared__ float4 stage4[];   // psi [MAXG][RR] | vb [MAXG][SP] | F_x [RR][SP]
   float* stage = reinterpret_cast<float*>(stage4);
   const int x = blockIdx.x, b = blockIdx.y;
   const int RR = (R + 3) & ~3, SP = pool_stride(P);
   float* sp = stage;
-  float* sv = sp + POOL_MAXG * RR;
-  float* so = sv + POOL_MAXG * SP;
+  float* sv = sp + mg * RR;
+  float* so = sv + mg * SP;
   const int RP = R * P;
   const int n_X = n - n_P;
   const int g = x < n_X ? (n_X - x + N0 - 1) / N0 : 0;   // columns of this profile
@@ -428,9 +436,10 @@ __global__ void __launch_bounds__(256) kattn_pool_kernel(const float* __restrict
   const int cg = SP >> 2;                 // 4-column groups per row
   const int ntile = (RR >> 2) * cg;
   for (int e = threadIdx.x; e < RR * SP; e += blockDim.x) so[e] = 0.f;
-  // rounds of up to POOL_MAXG staged columns (one round at the usual sizes)
-  for (int s0 = 0; s0 < g; s0 += POOL_MAXG) {
-    const int ns = min(POOL_MAXG, g - s0);
+  // rounds of up to mg staged columns (one round unless a profile has more
+  // than POOL_MAXG columns)
+  for (int s0 = 0; s0 < g; s0 += mg) {
+    const int ns = min(mg, g - s0);
     __syncthreads();
     // asynchronous 4-byte copies (zero-filled padding), all in flight at once
     for (int e = threadIdx.x; e < ns * RR; e += blockDim.x) {
@@ -487,14 +496,14 @@ __global__ void __launch_bounds__(256) kattn_pool_kernel(const float* __restrict
 __global__ void __launch_bounds__(256) kattn_pool_bwd_kernel(
     const float* __restrict__ psi, const float* __restrict__ vb, const float* __restrict__ dF,
     float* __restrict__ dpsi, float* __restrict__ dvb, int T, int R, int P, int n_P, int n,
-    int N0) {
+    int N0, int mg) {
   extern __shared__ float4 sm4[];   // dF [R][SP] | psi [MAXG][R] | vb [MAXG][SP]
   float* sm = reinterpret_cast<float*>(sm4);
   const int x = blockIdx.x, b = blockIdx.y;
   const int RP = R * P, SP = pool_stride(P), cg = SP >> 2;
   float* sdf = sm;
   float* sp = sm + R * SP;
-  float* sv = sp + POOL_MAXG * R;
+  float* sv = sp + mg * R;
   const float* df = dF + (static_cast<int64_t>(b) * N0 + x) * RP;
   const int n_X = n - n_P;
   const int g = x < n_X ? (n_X - x + N0 - 1) / N0 : 0;
@@ -505,8 +514,8 @@ __global__ void __launch_bounds__(256) kattn_pool_bwd_kernel(
     cp_async4(smem_u32(sdf + e), in ? df + rr * P + c : df, in ? 4u : 0u);
   }
   const int64_t row0 = static_cast<int64_t>(b) * T + n_P + x;
-  for (int s0 = 0; s0 < g; s0 += POOL_MAXG) {
-    const int ns = min(POOL_MAXG, g - s0);
+  for (int s0 = 0; s0 < g; s0 += mg) {
+    const int ns = min(mg, g - s0);
     const int nsb = (ns + 3) >> 2;   // blocks of four columns
     __syncthreads();
     for (int e = threadIdx.x; e < nsb * 4 * R; e += blockDim.x) {
@@ -832,13 +841,14 @@ int smat_kattn_pool_fwd(const float* psi, const float* vb, float* F, int nb, int
   if (nb < 1 || T < 1 || R < 1 || P < 1 || N0 < 1 || n_P < 0 || n < n_P || n > T)
     return SMAT_ERR_BAD_SHAPE;
   const int RR = (R + 3) & ~3, SP = pool_stride(P);
-  const int64_t bytes = (static_cast<int64_t>(POOL_MAXG) * (RR + SP) + RR * SP) * 4;
+  const int mg = pool_round(n_P, n, N0);
+  const int64_t bytes = (static_cast<int64_t>(mg) * (RR + SP) + RR * SP) * 4;
   if (bytes > POOL_SMEM_MAX) return SMAT_ERR_BAD_SHAPE;
   if (cudaFuncSetAttribute(kattn_pool_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                            POOL_SMEM_MAX) != cudaSuccess)
     return SMAT_ERR_LAUNCH;
   kattn_pool_kernel<<<dim3(N0, nb), 256, bytes, static_cast<cudaStream_t>(stream)>>>(
-      psi, vb, F, T, R, P, n_P, n, N0);
+      psi, vb, F, T, R, P, n_P, n, N0, mg);
   return cudaGetLastError() == cudaSuccess ? SMAT_OK : SMAT_ERR_LAUNCH;
 }
 
@@ -849,13 +859,14 @@ int smat_kattn_pool_bwd(const float* psi, const float* vb, const float* dF, floa
   if (nb < 1 || T < 1 || R < 1 || P < 1 || N0 < 1 || n_P < 0 || n < n_P || n > T)
     return SMAT_ERR_BAD_SHAPE;
   const int SP = pool_stride(P);
-  const int64_t bytes = (static_cast<int64_t>(R) * SP + POOL_MAXG * (R + SP)) * 4;
+  const int mg = pool_round(n_P, n, N0);
+  const int64_t bytes = (static_cast<int64_t>(R) * SP + static_cast<int64_t>(mg) * (R + SP)) * 4;
   if (bytes > POOL_SMEM_MAX) return SMAT_ERR_BAD_SHAPE;
   if (cudaFuncSetAttribute(kattn_pool_bwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                            POOL_SMEM_MAX) != cudaSuccess)
     return SMAT_ERR_LAUNCH;
   kattn_pool_bwd_kernel<<<dim3(N0, nb), 256, bytes, static_cast<cudaStream_t>(stream)>>>(
-      psi, vb, dF, dpsi, dvb, T, R, P, n_P, n, N0);
+      psi, vb, dF, dpsi, dvb, T, R, P, n_P, n, N0, mg);
   return cudaGetLastError() == cudaSuccess ? SMAT_OK : SMAT_ERR_LAUNCH;
 }
 
